@@ -1,0 +1,219 @@
+// extern "C" entry points of libzllm_cuda.so (declared in include/zllm.h).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "../../include/zllm.h"
+#include "capi_internal.h"
+#include "common.cuh"
+#include "internal.h"
+
+using namespace zllm;
+
+// ------------------------------------------------------------------------------------ helpers
+void zllm_set_error(zllm_ctx *c, const char *fmt, ...) {
+  if (!c) return;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(c->err, sizeof(c->err), fmt, ap);
+  va_end(ap);
+}
+
+int zllm_cuda_fail(zllm_ctx *c, cudaError_t e, const char *what) {
+  zllm_set_error(c, "%s: %s", what, cudaGetErrorString(e));
+  return e == cudaErrorMemoryAllocation ? ZLLM_E_OOM : ZLLM_E_CUDA;
+}
+
+// Grow-only device scratch buffer.
+int zllm_scratch(zllm_ctx *c, int slot, size_t bytes, void **out) {
+  if (slot < 0 || slot >= kScratchSlots) return ZLLM_E_ARG;
+  if (c->scratch_bytes[slot] < bytes) {
+    if (c->scratch[slot]) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(c->scratch[slot]);
+      c->scratch[slot] = nullptr;
+      c->scratch_bytes[slot] = 0;
+    }
+    size_t want = bytes < 4096 ? 4096 : bytes;
+    cudaError_t e = cudaMalloc(&c->scratch[slot], want);
+    if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMalloc(scratch)");
+    c->scratch_bytes[slot] = want;
+  }
+  *out = c->scratch[slot];
+  return ZLLM_OK;
+}
+
+static cudaStream_t pick(zllm_ctx *c, void *stream) { return stream ? (cudaStream_t)stream : c->stream; }
+
+// ------------------------------------------------------------------------------------ context
+extern "C" const char *zllm_version(void) { return "zllm-b200 0.1 (sm_100a)"; }
+
+extern "C" int zllm_init(int device, zllm_ctx **out) {
+  if (!out) return ZLLM_E_ARG;
+  *out = nullptr;
+  zllm_ctx *c = new (std::nothrow) zllm_ctx();
+  if (!c) return ZLLM_E_OOM;
+  c->device = device;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaHostAlloc((void **)&c->status_host, sizeof(unsigned), cudaHostAllocMapped);
+  if (e == cudaSuccess) {
+    *c->status_host = 0;
+    e = cudaHostGetDevicePointer((void **)&c->status_dev, c->status_host, 0);
+  }
+  if (e != cudaSuccess) {
+    fprintf(stderr, "zllm_init: %s\n", cudaGetErrorString(e));
+    int rc = e == cudaErrorMemoryAllocation ? ZLLM_E_OOM : ZLLM_E_CUDA;
+    zllm_destroy(c);
+    return rc;
+  }
+  *out = c;
+  return ZLLM_OK;
+}
+
+extern "C" void zllm_destroy(zllm_ctx *c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  for (int i = 0; i < kScratchSlots; i++)
+    if (c->scratch[i]) cudaFree(c->scratch[i]);
+  if (c->status_host) cudaFreeHost(c->status_host);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+extern "C" const char *zllm_last_error(const zllm_ctx *c) { return c ? c->err : "no context"; }
+extern "C" void *zllm_stream(zllm_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+int zllm_check_status(zllm_ctx *c) {
+  unsigned st = *(volatile unsigned *)c->status_host;
+  if (st) {
+    *(volatile unsigned *)c->status_host = 0;
+    zllm_set_error(c, "device wait timed out (status 0x%x): a bulk copy or stage hand-off did not complete within 2 s; "
+                      "the kernel drained its copies and returned", st);
+    return ZLLM_E_TIMEOUT;
+  }
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_sync(zllm_ctx *c) {
+  if (!c) return ZLLM_E_ARG;
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaStreamSynchronize");
+  return zllm_check_status(c);
+}
+
+// ------------------------------------------------------------------------------------ weights
+extern "C" int zllm_weight_upload(zllm_ctx *c, int type, int64_t rows, int64_t cols, const void *host, size_t nbytes,
+                                  zllm_weight **out) {
+  if (!c || !out || !host || rows <= 0 || cols <= 0) { zllm_set_error(c, "zllm_weight_upload: bad argument"); return ZLLM_E_ARG; }
+  *out = nullptr;
+  if (!type_supported(type)) {
+    zllm_set_error(c, "reference kernels: unsupported tensor type %d (supported: F32, F16, BF16, Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K)", type);
+    return ZLLM_E_UNSUPPORTED;
+  }
+  const int64_t rb = raw_row_bytes(type, cols);
+  if (rb < 0) { zllm_set_error(c, "row length %lld is not a multiple of the block size of type %d", (long long)cols, type); return ZLLM_E_ARG; }
+  if ((size_t)(rb * rows) != nbytes) {
+    zllm_set_error(c, "zllm_weight_upload: %zu bytes given, %lld expected", nbytes, (long long)(rb * rows));
+    return ZLLM_E_ARG;
+  }
+  zllm_weight *w = new (std::nothrow) zllm_weight();
+  if (!w) return ZLLM_E_OOM;
+  w->ctx = c;
+  w->m.type = type;
+  w->m.rows = rows;
+  w->m.cols = cols;
+  w->m.row_stride = dev_row_stride(type, cols);
+  w->bytes = (size_t)(w->m.row_stride * rows);
+  cudaSetDevice(c->device);
+  cudaError_t e = cudaMalloc((void **)&w->m.data, w->bytes);
+  if (e != cudaSuccess) { delete w; return zllm_cuda_fail(c, e, "cudaMalloc(weight)"); }
+  void *staging = nullptr;
+  const bool direct = w->m.row_stride == rb && (type == T_Q4_K || type == T_Q5_K || type == T_F16 || type == T_BF16 || type == T_F32);
+  if (direct) {
+    e = cudaMemcpyAsync(w->m.data, host, nbytes, cudaMemcpyHostToDevice, c->stream);
+  } else {
+    e = cudaMalloc(&staging, nbytes);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(staging, host, nbytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = repack_upload(w->m, staging, c->stream);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (staging) cudaFree(staging);
+  if (e != cudaSuccess) {
+    cudaFree(w->m.data);
+    delete w;
+    return zllm_cuda_fail(c, e, "zllm_weight_upload");
+  }
+  *out = w;
+  return ZLLM_OK;
+}
+
+extern "C" void zllm_weight_free(zllm_weight *w) {
+  if (!w) return;
+  if (w->m.data && w->owns) {
+    cudaSetDevice(w->ctx->device);
+    cudaStreamSynchronize(w->ctx->stream);
+    cudaFree(w->m.data);
+  }
+  delete w;
+}
+
+extern "C" int zllm_weight_info(const zllm_weight *w, int *type, int64_t *rows, int64_t *cols, size_t *bytes) {
+  if (!w) return ZLLM_E_ARG;
+  if (type) *type = w->m.type;
+  if (rows) *rows = w->m.rows;
+  if (cols) *cols = w->m.cols;
+  if (bytes) *bytes = w->bytes;
+  return ZLLM_OK;
+}
+
+// ------------------------------------------------------------------------------------ kernels
+extern "C" int zllm_quantize_act(zllm_ctx *c, const float *x, int64_t k, int ntok, int8_t *xq, float *xd, int32_t *xs,
+                                 void *stream) {
+  if (!c || !x || !xq || !xd || !xs || k <= 0 || k % 32 || ntok < 1) {
+    zllm_set_error(c, "zllm_quantize_act: bad argument (k must be a positive multiple of 32)");
+    return ZLLM_E_ARG;
+  }
+  cudaError_t e = launch_quantize(x, k, ntok, xq, xd, xs, c->status_dev, pick(c, stream));
+  return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "quantize_act launch");
+}
+
+extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, const float *xd, const int32_t *xs,
+                       const float *x, int ntok, float *y, int64_t y_stride, const float *y_add, void *stream) {
+  if (!c || !w || !y || ntok < 1) { zllm_set_error(c, "zllm_mm: bad argument"); return ZLLM_E_ARG; }
+  const bool q = type_quantized(w->m.type);
+  if (q ? (!xq || !xd || !xs) : !x) { zllm_set_error(c, "zllm_mm: missing activation for this weight type"); return ZLLM_E_ARG; }
+  if (ntok > 1 && y_stride < w->m.rows) { zllm_set_error(c, "zllm_mm: y_stride < rows"); return ZLLM_E_ARG; }
+  ActView a{xq, xd, xs, x, w->m.cols};
+  const char *why = "";
+  cudaError_t e = launch_gemv(w->m, a, ntok, y, y_stride, y_add, c->status_dev, c->num_sms, pick(c, stream), true, &why);
+  if (e == cudaErrorInvalidValue && why[0]) { zllm_set_error(c, "zllm_mm: %s", why); return ZLLM_E_UNSUPPORTED; }
+  return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "gemv launch");
+}
+
+extern "C" int zllm_matvec(zllm_ctx *c, const zllm_weight *w, const float *x_host, int ntok, float *y_host) {
+  if (!c || !w || !x_host || !y_host || ntok < 1) { zllm_set_error(c, "zllm_matvec: bad argument"); return ZLLM_E_ARG; }
+  cudaSetDevice(c->device);
+  const int64_t K = w->m.cols, R = w->m.rows;
+  void *xs_, *xq_, *xd_, *xsum_, *y_;
+  int rc;
+  if ((rc = zllm_scratch(c, 0, sizeof(float) * K * ntok, &xs_))) return rc;
+  if ((rc = zllm_scratch(c, 1, (size_t)K * ntok, &xq_))) return rc;
+  if ((rc = zllm_scratch(c, 2, sizeof(float) * (K / 32 + 1) * ntok, &xd_))) return rc;
+  if ((rc = zllm_scratch(c, 3, sizeof(int32_t) * (K / 32 + 1) * ntok, &xsum_))) return rc;
+  if ((rc = zllm_scratch(c, 4, sizeof(float) * R * ntok, &y_))) return rc;
+  cudaError_t e = cudaMemcpyAsync(xs_, x_host, sizeof(float) * K * ntok, cudaMemcpyHostToDevice, c->stream);
+  if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(x)");
+  const bool q = type_quantized(w->m.type);
+  if (q && (rc = zllm_quantize_act(c, (const float *)xs_, K, ntok, (int8_t *)xq_, (float *)xd_, (int32_t *)xsum_, c->stream)))
+    return rc;
+  if ((rc = zllm_mm(c, w, (const int8_t *)xq_, (const float *)xd_, (const int32_t *)xsum_, (const float *)xs_, ntok,
+                    (float *)y_, R, nullptr, c->stream)))
+    return rc;
+  e = cudaMemcpyAsync(y_host, y_, sizeof(float) * R * ntok, cudaMemcpyDeviceToHost, c->stream);
+  if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(y)");
+  return zllm_sync(c);
+}

@@ -1,0 +1,32 @@
+// Definitions of the opaque C-ABI handles (shared by the capi*.cu files).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+constexpr int kScratchSlots = 16;
+
+struct zllm_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  unsigned *status_host = nullptr;   // mapped pinned word the kernels report timeouts into
+  unsigned *status_dev = nullptr;
+  void *scratch[kScratchSlots] = {};
+  size_t scratch_bytes[kScratchSlots] = {};
+  char err[512] = {0};
+};
+
+struct zllm_weight {
+  zllm_ctx *ctx = nullptr;
+  zllm::DevMatrix m{};
+  size_t bytes = 0;
+  bool owns = true;
+};
+
+void zllm_set_error(zllm_ctx *c, const char *fmt, ...);
+int zllm_cuda_fail(zllm_ctx *c, cudaError_t e, const char *what);
+int zllm_scratch(zllm_ctx *c, int slot, size_t bytes, void **out);
+int zllm_check_status(zllm_ctx *c);

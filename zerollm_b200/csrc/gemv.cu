@@ -1,0 +1,562 @@
+// Decode GEMV (one activation vector x one weight matrix) for every hot-path ggml type, and the
+// load-time repack of raw GGUF rows into the layout these kernels read.
+//
+// Replaces the reference's per-type matvec kernels: src/compute/ref-kernels.js:127-302 (oracle)
+// and the WASM `matvec_*` exports (src/compute/wasm/kernels.js:30-114,
+// src/compute/wasm/kquant-kernels.js:337-504), dispatched by ggml type as in
+// src/compute/worker.js:184-197 / :251-270.
+//
+// Structure (one persistent CTA per SM):
+//   * a producer thread streams whole chunks of consecutive rows HBM -> shared memory with 1D bulk
+//     copies (cp.async.bulk, completion on an mbarrier), up to `ns` chunks in flight per SM; the
+//     copies are issued before griddepcontrol.wait, so under programmatic dependent launch the
+//     weights of this matrix stream while the previous kernel is still finishing;
+//   * consumer threads each own a fixed set of "units" of the row (64 values of a k-quant, one
+//     32-block of a legacy quant, 8 / 4 values of a float row) and keep that unit's activation in
+//     registers for the whole launch; every weight byte is read from shared memory exactly once;
+//   * integer block dots use dp4a (exact, like the reference's integer sums); the per-block
+//     scale arithmetic is done in IEEE double with the reference's operation order and no fused
+//     multiply-add (src/compute/ref-kernels.js:146, :235-236, :271), so each per-block term is
+//     bit-identical to the oracle's and only the order of the final double summation differs;
+//   * a row's partial sums are reduced across lanes (shuffles) and across the warps of its row
+//     group (shared memory) in a fixed order, so results are deterministic.
+#include "common.cuh"
+#include "internal.h"
+
+namespace zllm {
+
+// ============================================================================ helpers
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xffu; }
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+// 4 bits -> bit 0 of each of 4 bytes
+__device__ __forceinline__ uint32_t spread4(uint32_t t) { return (t * 0x00204081u) & 0x01010101u; }
+
+// ============================================================================ formats
+// Each format: Acc (partial sum type), units(K), Act (per-unit activation registers),
+// load(Act&, ActView, u) and dot(Act, row_in_smem, u, nb, Acc&) which adds the unit's terms.
+
+// ---- Q4_K / Q5_K: 256-value super-blocks, unit = (super-block sb, chunk c) = 64 values
+// ref-kernels.js:196-242.  Device layout = raw GGUF (144 / 176 byte blocks, 16-byte aligned).
+template <bool FIVE>
+struct FmtK45 {
+  using Acc = double;
+  static constexpr bool QACT = true;
+  static constexpr int BS = FIVE ? 176 : 144;
+  static constexpr int QS = FIVE ? 48 : 16;
+  struct Act { uint32_t lo[8], hi[8]; double xd0, xd1, xs0, xs1; };
+  static __host__ __device__ int units(int64_t k) { return (int)(k / 64); }
+  __device__ static void load(Act &a, const ActView &v, int u) {
+    const uint8_t *q = reinterpret_cast<const uint8_t *>(v.xq) + (int64_t)u * 64;
+    uint4 t0 = ldg128(q), t1 = ldg128(q + 16), t2 = ldg128(q + 32), t3 = ldg128(q + 48);
+    a.lo[0] = t0.x; a.lo[1] = t0.y; a.lo[2] = t0.z; a.lo[3] = t0.w;
+    a.lo[4] = t1.x; a.lo[5] = t1.y; a.lo[6] = t1.z; a.lo[7] = t1.w;
+    a.hi[0] = t2.x; a.hi[1] = t2.y; a.hi[2] = t2.z; a.hi[3] = t2.w;
+    a.hi[4] = t3.x; a.hi[5] = t3.y; a.hi[6] = t3.z; a.hi[7] = t3.w;
+    a.xd0 = (double)__ldg(v.xd + 2 * u);
+    a.xd1 = (double)__ldg(v.xd + 2 * u + 1);
+    a.xs0 = (double)__ldg(v.xs + 2 * u);
+    a.xs1 = (double)__ldg(v.xs + 2 * u + 1);
+  }
+  __device__ static void dot(const Act &a, const uint8_t *row, int u, int nb, Acc &acc) {
+    const int sb = u >> 2, c = u & 3;
+    const uint8_t *blk = row + sb * BS;
+    const uint4 h = lds128(blk);
+    const uint4 q0 = lds128(blk + QS + c * 32), q1 = lds128(blk + QS + c * 32 + 16);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    int lo = 0, hi = 0;
+    if (FIVE) {
+      const uint4 e0 = lds128(blk + 16), e1 = lds128(blk + 32);
+      const uint32_t e[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        uint32_t vl = (w[i] & 0x0f0f0f0fu) | (((e[i] >> (2 * c)) & 0x01010101u) << 4);
+        uint32_t vh = ((w[i] >> 4) & 0x0f0f0f0fu) | (((e[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+        lo = __dp4a((int)vl, (int)a.lo[i], lo);
+        hi = __dp4a((int)vh, (int)a.hi[i], hi);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        lo = __dp4a((int)(w[i] & 0x0f0f0f0fu), (int)a.lo[i], lo);
+        hi = __dp4a((int)((w[i] >> 4) & 0x0f0f0f0fu), (int)a.hi[i], hi);
+      }
+    }
+    // unpackScaleMinK4 (quant.js:109-118) for sub-blocks 2c and 2c+1
+    const int k0 = (2 * c) & 3, k1 = k0 + 1;
+    int sc0, mn0, sc1, mn1;
+    if (c < 2) {
+      sc0 = byte_of(h.y, k0) & 63; mn0 = byte_of(h.z, k0) & 63;
+      sc1 = byte_of(h.y, k1) & 63; mn1 = byte_of(h.z, k1) & 63;
+    } else {
+      sc0 = (byte_of(h.w, k0) & 15) | ((byte_of(h.y, k0) >> 6) << 4);
+      mn0 = (byte_of(h.w, k0) >> 4) | ((byte_of(h.z, k0) >> 6) << 4);
+      sc1 = (byte_of(h.w, k1) & 15) | ((byte_of(h.y, k1) >> 6) << 4);
+      mn1 = (byte_of(h.w, k1) >> 4) | ((byte_of(h.z, k1) >> 6) << 4);
+    }
+    const float d = h2f(h.x & 0xffffu), dmin = h2f(h.x >> 16);
+    // acc += xd * (d*sc*lo - dmin*mn*xs)   (d*sc and dmin*mn are exact in f32; the products by lo / xs are
+    // exact in double; the subtraction, the scaling by xd and the accumulation round like the JS)
+    const double a0 = __dmul_rn((double)__fmul_rn(d, (float)sc0), (double)lo);
+    const double b0 = __dmul_rn((double)__fmul_rn(dmin, (float)mn0), a.xs0);
+    acc = __dadd_rn(acc, __dmul_rn(a.xd0, __dsub_rn(a0, b0)));
+    const double a1 = __dmul_rn((double)__fmul_rn(d, (float)sc1), (double)hi);
+    const double b1 = __dmul_rn((double)__fmul_rn(dmin, (float)mn1), a.xs1);
+    acc = __dadd_rn(acc, __dmul_rn(a.xd1, __dsub_rn(a1, b1)));
+  }
+};
+
+// ---- Q6_K: unit = (sb, half h, lane group g) = 64 values in four 16-value scale groups
+// ref-kernels.js:243-277.  Device layout per row: ql[128*nb] | qh[64*nb] | scales[16*nb] | d[2*nb].
+struct FmtQ6K {
+  using Acc = double;
+  static constexpr bool QACT = true;
+  struct Act { uint32_t x[4][4]; int xsum[4]; double xd[4]; };
+  static __host__ __device__ int units(int64_t k) { return (int)(k / 64); }
+  __device__ static void load(Act &a, const ActView &v, int u) {
+    const int sb = u >> 2, h = (u >> 1) & 1, g = u & 1;
+    const uint8_t *q = reinterpret_cast<const uint8_t *>(v.xq) + (int64_t)sb * 256 + h * 128 + g * 16;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      uint4 t = ldg128(q + 32 * k);
+      a.x[k][0] = t.x; a.x[k][1] = t.y; a.x[k][2] = t.z; a.x[k][3] = t.w;
+      int s = 0;
+#pragma unroll
+      for (int i = 0; i < 4; i++) s = __dp4a((int)a.x[k][i], 0x01010101, s);
+      a.xsum[k] = s;
+      a.xd[k] = (double)__ldg(v.xd + sb * 8 + h * 4 + k);
+    }
+  }
+  __device__ static void dot(const Act &a, const uint8_t *row, int u, int nb, Acc &acc) {
+    const int sb = u >> 2, h = (u >> 1) & 1, g = u & 1;
+    const uint8_t *ql = row + sb * 128 + h * 64 + g * 16;
+    const uint4 A = lds128(ql), B = lds128(ql + 32);
+    const uint4 H = lds128(row + 128 * nb + sb * 64 + h * 32 + g * 16);
+    const uint2 S = *reinterpret_cast<const uint2 *>(row + 192 * nb + sb * 16 + h * 8);
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(row + 208 * nb + sb * 2));
+    const uint32_t aw[4] = {A.x, A.y, A.z, A.w}, bw[4] = {B.x, B.y, B.z, B.w}, hw[4] = {H.x, H.y, H.z, H.w};
+    int gs[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const uint32_t q1 = (aw[i] & 0x0f0f0f0fu) | ((hw[i] & 0x03030303u) << 4);
+      const uint32_t q2 = (bw[i] & 0x0f0f0f0fu) | ((hw[i] & 0x0c0c0c0cu) << 2);
+      const uint32_t q3 = ((aw[i] >> 4) & 0x0f0f0f0fu) | (hw[i] & 0x30303030u);
+      const uint32_t q4 = ((bw[i] >> 4) & 0x0f0f0f0fu) | ((hw[i] >> 2) & 0x30303030u);
+      gs[0] = __dp4a((int)q1, (int)a.x[0][i], gs[0]);
+      gs[1] = __dp4a((int)q2, (int)a.x[1][i], gs[1]);
+      gs[2] = __dp4a((int)q3, (int)a.x[2][i], gs[2]);
+      gs[3] = __dp4a((int)q4, (int)a.x[3][i], gs[3]);
+    }
+    const double dd = (double)d;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int gsum = gs[k] - 32 * a.xsum[k];                 // sum((q - 32) * x), exact
+      const uint32_t sw = k < 2 ? S.x : S.y;
+      const int scale = (int)(int8_t)byte_of(sw, (2 * k + g) & 3);
+      // acc += xd * d * scale * gsum  (left to right, each product rounded: ref-kernels.js:271)
+      double t = __dmul_rn(a.xd[k], dd);
+      t = __dmul_rn(t, (double)scale);
+      t = __dmul_rn(t, (double)gsum);
+      acc = __dadd_rn(acc, t);
+    }
+  }
+};
+
+// ---- Q8_0 / Q4_0 / Q5_0: unit = one 32-value block.  acc += s * d * xd  (ref-kernels.js:132-195)
+// Device layouts per row: Q8_0 qs[32*nb] | d[2*nb];  Q4_0 qs[16*nb] | d[2*nb];  Q5_0 qs[16*nb] | qh[4*nb] | d[2*nb].
+template <int T>
+struct FmtQ0 {
+  using Acc = double;
+  static constexpr bool QACT = true;
+  struct Act { uint32_t x[8]; double xd; int xs; };
+  static __host__ __device__ int units(int64_t k) { return (int)(k / 32); }
+  __device__ static void load(Act &a, const ActView &v, int u) {
+    const uint8_t *q = reinterpret_cast<const uint8_t *>(v.xq) + (int64_t)u * 32;
+    uint4 t0 = ldg128(q), t1 = ldg128(q + 16);
+    a.x[0] = t0.x; a.x[1] = t0.y; a.x[2] = t0.z; a.x[3] = t0.w;
+    a.x[4] = t1.x; a.x[5] = t1.y; a.x[6] = t1.z; a.x[7] = t1.w;
+    a.xd = (double)__ldg(v.xd + u);
+    a.xs = __ldg(v.xs + u);
+  }
+  __device__ static void dot(const Act &a, const uint8_t *row, int u, int nb, Acc &acc) {
+    int s = 0;
+    float d;
+    if (T == T_Q8_0) {
+      const uint4 q0 = lds128(row + u * 32), q1 = lds128(row + u * 32 + 16);
+      const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+      for (int i = 0; i < 8; i++) s = __dp4a((int)w[i], (int)a.x[i], s);
+      d = h2f(*reinterpret_cast<const uint16_t *>(row + 32 * nb + u * 2));
+    } else {
+      const uint4 q = lds128(row + u * 16);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      uint32_t qh = 0;
+      if (T == T_Q5_0) qh = *reinterpret_cast<const uint32_t *>(row + 16 * nb + u * 4);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        uint32_t vl = w[i] & 0x0f0f0f0fu, vh = (w[i] >> 4) & 0x0f0f0f0fu;
+        if (T == T_Q5_0) {
+          vl |= spread4((qh >> (4 * i)) & 15u) << 4;
+          vh |= spread4((qh >> (16 + 4 * i)) & 15u) << 4;
+        }
+        s = __dp4a((int)vl, (int)a.x[i], s);
+        s = __dp4a((int)vh, (int)a.x[4 + i], s);
+      }
+      s -= (T == T_Q5_0 ? 16 : 8) * a.xs;                    // sum((q - offset) * x), exact
+      d = h2f(*reinterpret_cast<const uint16_t *>(row + (T == T_Q5_0 ? 20 : 16) * nb + u * 2));
+    }
+    acc = __dadd_rn(acc, __dmul_rn(__dmul_rn((double)s, (double)d), a.xd));
+  }
+};
+
+// ---- F16 / BF16 / F32: unit = 16 bytes of weights; activations stay f32 (ref-kernels.js:278-299).
+// Partial sums accumulate in f32 with fused multiply-add (the reference accumulates in double;
+// the difference is at the 1e-7 relative level).
+template <int T>
+struct FmtFloat {
+  using Acc = float;
+  static constexpr bool QACT = false;
+  static constexpr int PER = T == T_F32 ? 4 : 8;
+  struct Act { float x[PER]; };
+  static __host__ __device__ int units(int64_t k) { return (int)(k / PER); }
+  __device__ static void load(Act &a, const ActView &v, int u) {
+    const float *p = v.x + (int64_t)u * PER;
+#pragma unroll
+    for (int i = 0; i < PER; i++) a.x[i] = __ldg(p + i);
+  }
+  __device__ static void dot(const Act &a, const uint8_t *row, int u, int nb, Acc &acc) {
+    const uint4 q = lds128(row + u * 16);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    if (T == T_F32) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc = __fmaf_rn(__uint_as_float(w[i]), a.x[i], acc);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float lo = T == T_F16 ? h2f(w[i] & 0xffffu) : bf2f(w[i] & 0xffffu);
+        const float hi = T == T_F16 ? h2f(w[i] >> 16) : bf2f(w[i] >> 16);
+        acc = __fmaf_rn(lo, a.x[2 * i], acc);
+        acc = __fmaf_rn(hi, a.x[2 * i + 1], acc);
+      }
+    }
+  }
+};
+
+__device__ __forceinline__ double warp_sum(double v) { return warp_sum_f64(v); }
+__device__ __forceinline__ float warp_sum(float v) { return warp_sum_f32(v); }
+__device__ __forceinline__ double acc_add(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ float acc_add(float a, float b) { return __fadd_rn(a, b); }
+
+// ============================================================================ kernel
+struct GemvArgs {
+  const uint8_t *w;
+  int64_t row_stride;
+  int64_t rows;
+  int nb;            // super-blocks (k-quants) or blocks (legacy quants) per row
+  ActView act;
+  float *y;
+  const float *y_add;
+  unsigned *status;
+  int units, tr, rg, cr, ns, stage_bytes;
+};
+
+constexpr int kConsumers = 256;             // max consumer threads per CTA
+constexpr int kThreads = kConsumers + 32;   // + one producer warp
+constexpr int kMaxStages = 32;
+
+template <class F, int UPT>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs p) {
+  using Acc = typename F::Acc;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x;
+  const int ncons = p.tr * p.rg;
+  const int wg = p.tr >> 5;                                     // warps per row group
+  uint8_t *stages = smem;
+  Acc *part = reinterpret_cast<Acc *>(smem + (size_t)p.ns * p.stage_bytes);
+  const size_t part_bytes = ((size_t)p.ns * p.cr * wg * sizeof(Acc) + 15) / 16 * 16;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)p.ns * p.stage_bytes + part_bytes);
+  uint64_t *empty = full + p.ns;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + p.ns);
+
+  const int64_t G = gridDim.x;
+  const int64_t r0 = (int64_t)blockIdx.x * p.rows / G, r1 = ((int64_t)blockIdx.x + 1) * p.rows / G;
+  const int nrows = (int)(r1 - r0);
+  const int nchunks = (nrows + p.cr - 1) / p.cr;
+
+  if (tid == 0) {
+    for (int i = 0; i < p.ns; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (tid >= kConsumers) {
+    // ------------------------------------------------------------------ producer
+    if (tid == kConsumers) {
+      const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
+      int issued = 0;
+      for (int i = 0; i < nchunks; i++) {
+        const int s = i % p.ns;
+        if (i >= p.ns && !mbar_wait_bounded(&empty[s], ((i / p.ns) - 1) & 1, deadline)) {
+          atomicOr(p.status, ST_EMPTY_TIMEOUT);
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        const int nr = min(p.cr, nrows - i * p.cr);
+        const uint32_t bytes = (uint32_t)(nr * p.row_stride);
+        mbar_arrive_expect_tx(&full[s], bytes);
+        bulk_g2s(stages + (size_t)s * p.stage_bytes, p.w + (r0 + (int64_t)i * p.cr) * p.row_stride, bytes, &full[s]);
+        issued = i + 1;
+      }
+      // every copy this CTA started must land before the CTA exits
+      const uint64_t drain_deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
+      for (int s = 0; s < p.ns && s < issued; s++) {
+        const int last = s + ((issued - 1 - s) / p.ns) * p.ns;
+        if (!mbar_wait_bounded(&full[s], (last / p.ns) & 1, drain_deadline)) atomicOr(p.status, ST_DRAIN_TIMEOUT);
+      }
+    }
+  } else if (tid < ncons) {
+    // ------------------------------------------------------------------ consumers
+    pdl_wait();                                                // activations come from the previous kernel
+    const int slot = tid / p.tr, lt = tid % p.tr;
+    typename F::Act act[UPT];
+#pragma unroll
+    for (int j = 0; j < UPT; j++) {
+      const int u = lt + j * p.tr;
+      if (u < p.units) F::load(act[j], p.act, u);
+    }
+    const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
+    for (int i = 0; i < nchunks; i++) {
+      const int s = i % p.ns;
+      const bool timed_out = !mbar_wait_bounded(&full[s], (i / p.ns) & 1, deadline);
+      // one uniform decision for all consumers (the producer may raise abort_flag at any time)
+      if (named_sync_or(1, ncons, timed_out || *abort_flag)) {
+        *abort_flag = 1;
+        if (tid == 0) atomicOr(p.status, ST_FULL_TIMEOUT);
+        break;
+      }
+      const uint8_t *st = stages + (size_t)s * p.stage_bytes;
+      const int nr = min(p.cr, nrows - i * p.cr);
+      for (int rr = slot; rr < nr; rr += p.rg) {
+        const uint8_t *row = st + (size_t)rr * p.row_stride;
+        Acc a = 0;
+#pragma unroll
+        for (int j = 0; j < UPT; j++) {
+          const int u = lt + j * p.tr;
+          if (u < p.units) F::dot(act[j], row, u, p.nb, a);
+        }
+        a = warp_sum(a);
+        if ((tid & 31) == 0) part[((size_t)s * p.cr + rr) * wg + (lt >> 5)] = a;
+      }
+      named_sync(1, ncons);
+      if (tid < nr) {
+        const Acc *pp = part + ((size_t)s * p.cr + tid) * wg;
+        Acc a = pp[0];
+        for (int w = 1; w < wg; w++) a = acc_add(a, pp[w]);
+        const int64_t r = r0 + (int64_t)i * p.cr + tid;
+        float out = (float)a;
+        if (p.y_add) out = __fadd_rn(p.y_add[r], out);
+        p.y[r] = out;
+      }
+      if (tid == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  __syncthreads();
+}
+
+// ============================================================================ repack (load time)
+__global__ void repack_kernel(int type, const uint8_t *raw, int64_t raw_row, uint8_t *dst, int64_t stride,
+                              int64_t rows, int nb) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint8_t *s = raw + r * raw_row;
+    uint8_t *d = dst + r * stride;
+    for (int64_t i = threadIdx.x; i < raw_row; i += blockDim.x) {
+      int64_t o = i;
+      if (type == T_Q6_K) {
+        const int b = (int)(i / 210), e = (int)(i % 210);
+        o = e < 128 ? b * 128 + e : e < 192 ? 128LL * nb + b * 64 + (e - 128)
+                                            : e < 208 ? 192LL * nb + b * 16 + (e - 192) : 208LL * nb + b * 2 + (e - 208);
+      } else if (type == T_Q8_0) {
+        const int b = (int)(i / 34), e = (int)(i % 34);
+        o = e < 2 ? 32LL * nb + b * 2 + e : b * 32 + (e - 2);
+      } else if (type == T_Q4_0) {
+        const int b = (int)(i / 18), e = (int)(i % 18);
+        o = e < 2 ? 16LL * nb + b * 2 + e : b * 16 + (e - 2);
+      } else if (type == T_Q5_0) {
+        const int b = (int)(i / 22), e = (int)(i % 22);
+        o = e < 2 ? 20LL * nb + b * 2 + e : e < 6 ? 16LL * nb + b * 4 + (e - 2) : b * 16 + (e - 6);
+      }
+      d[o] = s[i];
+    }
+    for (int64_t i = raw_row + threadIdx.x; i < stride; i += blockDim.x) d[i] = 0;
+  }
+}
+
+// ============================================================================ host side
+bool type_supported(int t) {
+  switch (t) {
+    case T_F32: case T_F16: case T_BF16: case T_Q4_0: case T_Q5_0: case T_Q8_0: case T_Q4_K: case T_Q5_K: case T_Q6_K:
+      return true;
+    default: return false;
+  }
+}
+bool type_quantized(int t) { return type_supported(t) && t != T_F32 && t != T_F16 && t != T_BF16; }
+
+int64_t raw_row_bytes(int t, int64_t cols) {
+  switch (t) {
+    case T_F32: return cols * 4;
+    case T_F16: case T_BF16: return cols * 2;
+    case T_Q8_0: return cols % 32 ? -1 : cols / 32 * 34;
+    case T_Q4_0: return cols % 32 ? -1 : cols / 32 * 18;
+    case T_Q5_0: return cols % 32 ? -1 : cols / 32 * 22;
+    case T_Q4_K: return cols % 256 ? -1 : cols / 256 * 144;
+    case T_Q5_K: return cols % 256 ? -1 : cols / 256 * 176;
+    case T_Q6_K: return cols % 256 ? -1 : cols / 256 * 210;
+    default: return -1;
+  }
+}
+
+int64_t dev_row_stride(int t, int64_t cols) {
+  const int64_t rb = raw_row_bytes(t, cols);
+  return rb < 0 ? -1 : (rb + 15) / 16 * 16;
+}
+
+cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s) {
+  const int64_t rb = raw_row_bytes(m.type, m.cols);
+  const int nb = (int)(m.type == T_Q4_K || m.type == T_Q5_K || m.type == T_Q6_K ? m.cols / 256 : m.cols / 32);
+  const int64_t grid = m.rows < 65535 ? m.rows : 65535;
+  repack_kernel<<<(unsigned)grid, 256, 0, s>>>(m.type, (const uint8_t *)raw_dev, rb, m.data, m.row_stride, m.rows, nb);
+  return cudaGetLastError();
+}
+
+static int units_of(int t, int64_t k) {
+  switch (t) {
+    case T_Q4_K: case T_Q5_K: case T_Q6_K: return (int)(k / 64);
+    case T_Q8_0: case T_Q4_0: case T_Q5_0: return (int)(k / 32);
+    case T_F16: case T_BF16: return (int)(k / 8);
+    case T_F32: return (int)(k / 4);
+  }
+  return 0;
+}
+
+static size_t acc_bytes(int t) { return type_quantized(t) ? 8 : 4; }
+
+bool plan_gemv(const DevMatrix &m, int num_sms, GemvPlan *p, const char **why) {
+  if (!type_supported(m.type)) { *why = "unsupported tensor type"; return false; }
+  if ((m.type == T_F16 || m.type == T_BF16) && m.cols % 8) { *why = "F16/BF16 rows must be a multiple of 8 values"; return false; }
+  if (m.type == T_F32 && m.cols % 4) { *why = "F32 rows must be a multiple of 4 values"; return false; }
+  const int U = units_of(m.type, m.cols);
+  if (U <= 0) { *why = "empty row"; return false; }
+  p->units = U;
+  p->tr = U <= kConsumers ? (U + 31) / 32 * 32 : kConsumers;
+  p->upt = (U + p->tr - 1) / p->tr;
+  if (p->upt > 4) { *why = "row too long for the decode GEMV (more than 4 units per thread)"; return false; }
+  if (p->upt == 3) p->upt = 4;
+  p->rg = kConsumers / p->tr;
+  if (p->rg < 1) p->rg = 1;
+  // ~8 KB chunks: small enough that the compute left after the last chunk lands is short,
+  // large enough that each bulk copy moves whole rows.
+  const int64_t target = 8192;
+  int64_t k = (target + (int64_t)p->rg * m.row_stride / 2) / ((int64_t)p->rg * m.row_stride);
+  if (k < 1) k = 1;
+  p->cr = (int)(k * p->rg);
+  if (p->cr > 64) p->cr = 64 / p->rg * p->rg;
+  if (p->cr < 1) p->cr = 1;
+  const int64_t stage = ((int64_t)p->cr * m.row_stride + 127) / 128 * 128;
+  if (stage > 100 * 1024) { *why = "row too long for a shared-memory stage"; return false; }
+  p->stage_bytes = (int)stage;
+  int64_t grid = (m.rows + p->cr - 1) / p->cr;
+  if (grid > num_sms) grid = num_sms;
+  if (grid < 1) grid = 1;
+  p->grid = (int)grid;
+  const int64_t rows_per_cta = (m.rows + grid - 1) / grid;
+  const int64_t chunks = (rows_per_cta + p->cr - 1) / p->cr;
+  const int64_t budget = 200 * 1024;
+  int64_t ns = budget / stage;
+  if (ns > kMaxStages) ns = kMaxStages;
+  if (ns > chunks) ns = chunks;
+  if (ns < 1) ns = 1;
+  p->ns = (int)ns;
+  const size_t part = (size_t)p->ns * p->cr * (p->tr / 32) * acc_bytes(m.type);
+  p->smem_bytes = (int)((size_t)p->ns * p->stage_bytes + (part + 15) / 16 * 16 + 2 * 8 * p->ns + 16);
+  return true;
+}
+
+template <class F, int UPT>
+static cudaError_t launch_one(const GemvArgs &a, const GemvPlan &pl, cudaStream_t s, bool pdl) {
+  auto kern = gemv_kernel<F, UPT>;
+  // the opt-in shared-memory size is a per-device function attribute: set it once per device
+  // (and only when it grows) so that launches inside stream capture make no attribute calls
+  static int granted[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (granted[dev] < pl.smem_bytes) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    granted[dev] = 227 * 1024;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = pl.smem_bytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <class F>
+static cudaError_t launch_fmt(const GemvArgs &a, const GemvPlan &pl, cudaStream_t s, bool pdl) {
+  switch (pl.upt) {
+    case 1: return launch_one<F, 1>(a, pl, s, pdl);
+    case 2: return launch_one<F, 2>(a, pl, s, pdl);
+    default: return launch_one<F, 4>(a, pl, s, pdl);
+  }
+}
+
+cudaError_t launch_gemv(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
+                        const float *y_add, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why) {
+  GemvPlan pl;
+  if (!plan_gemv(m, num_sms, &pl, why)) return cudaErrorInvalidValue;
+  const int64_t nbk = (m.type == T_Q4_K || m.type == T_Q5_K || m.type == T_Q6_K) ? m.cols / 256 : m.cols / 32;
+  for (int t = 0; t < ntok; t++) {
+    GemvArgs a;
+    a.w = m.data;
+    a.row_stride = m.row_stride;
+    a.rows = m.rows;
+    a.nb = (int)nbk;
+    a.act.k = act.k;
+    a.act.xq = act.xq ? act.xq + (int64_t)t * act.k : nullptr;
+    a.act.xd = act.xd ? act.xd + (int64_t)t * (act.k / 32) : nullptr;
+    a.act.xs = act.xs ? act.xs + (int64_t)t * (act.k / 32) : nullptr;
+    a.act.x = act.x ? act.x + (int64_t)t * act.k : nullptr;
+    a.y = y + (int64_t)t * y_stride;
+    a.y_add = y_add ? y_add + (int64_t)t * y_stride : nullptr;
+    a.status = status;
+    a.units = pl.units; a.tr = pl.tr; a.rg = pl.rg; a.cr = pl.cr; a.ns = pl.ns; a.stage_bytes = pl.stage_bytes;
+    cudaError_t e;
+    switch (m.type) {
+      case T_Q4_K: e = launch_fmt<FmtK45<false>>(a, pl, s, pdl); break;
+      case T_Q5_K: e = launch_fmt<FmtK45<true>>(a, pl, s, pdl); break;
+      case T_Q6_K: e = launch_fmt<FmtQ6K>(a, pl, s, pdl); break;
+      case T_Q8_0: e = launch_fmt<FmtQ0<T_Q8_0>>(a, pl, s, pdl); break;
+      case T_Q4_0: e = launch_fmt<FmtQ0<T_Q4_0>>(a, pl, s, pdl); break;
+      case T_Q5_0: e = launch_fmt<FmtQ0<T_Q5_0>>(a, pl, s, pdl); break;
+      case T_F16: e = launch_fmt<FmtFloat<T_F16>>(a, pl, s, pdl); break;
+      case T_BF16: e = launch_fmt<FmtFloat<T_BF16>>(a, pl, s, pdl); break;
+      case T_F32: e = launch_fmt<FmtFloat<T_F32>>(a, pl, s, pdl); break;
+      default: *why = "unsupported tensor type"; return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace zllm

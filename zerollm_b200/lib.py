@@ -1,0 +1,77 @@
+"""ctypes binding of libzllm_cuda.so (include/zllm.h).
+
+The library is the product: there is no CPU fallback.  Loading fails loudly when the shared
+object has not been built, and every call that returns a negative code raises ``ZllmError``
+with the library's message.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+LIB_PATH = os.path.join(PKG, "libzllm_cuda.so")
+HEADER = os.path.join(ROOT, "include", "zllm.h")
+
+OK, E_ARG, E_OOM, E_CUDA, E_CTX_FULL, E_TIMEOUT, E_STATE, E_UNSUPPORTED, E_TOKEN, E_BATCH = 0, -1, -2, -3, -4, -5, -6, -7, -8, -9
+
+
+class ZllmError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+vp, i32, i64, sz = C.c_void_p, C.c_int, C.c_int64, C.c_size_t
+PP = C.POINTER(C.c_void_p)
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "zllm_version": (C.c_char_p, []),
+    "zllm_init": (i32, [i32, PP]),
+    "zllm_destroy": (None, [vp]),
+    "zllm_last_error": (C.c_char_p, [vp]),
+    "zllm_stream": (vp, [vp]),
+    "zllm_sync": (i32, [vp]),
+    "zllm_weight_upload": (i32, [vp, i32, i64, i64, vp, sz, PP]),
+    "zllm_weight_free": (None, [vp]),
+    "zllm_weight_info": (i32, [vp, C.POINTER(i32), C.POINTER(i64), C.POINTER(i64), C.POINTER(sz)]),
+    "zllm_quantize_act": (i32, [vp, vp, i64, i32, vp, vp, vp, vp]),
+    "zllm_mm": (i32, [vp, vp, vp, vp, vp, vp, i32, vp, i64, vp, vp]),
+    "zllm_matvec": (i32, [vp, vp, vp, i32, vp]),
+}
+
+_lib = None
+
+
+def header_functions(path: str = HEADER) -> list[str]:
+    """Names of the functions include/zllm.h declares."""
+    text = open(path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(zllm_[a-z0-9_]+)\s*\(", text)))
+
+
+def load(path: str = LIB_PATH):
+    """Load libzllm_cuda.so (once).  Raises if it is missing: build it with
+    ``python -m zerollm_b200.build`` (or ``__graft_entry__.build()``)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ZllmError(E_STATE, f"{path} is not built: run `python -m zerollm_b200.build`")
+    L = C.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(rc: int, ctx=None, what: str = ""):
+    if rc != OK:
+        msg = load().zllm_last_error(ctx).decode() if ctx else ""
+        raise ZllmError(rc, f"{what}: {msg}" if what else msg)
+    return rc
