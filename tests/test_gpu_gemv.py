@@ -119,3 +119,12 @@ def test_rejects_bad_shapes(ctx):
         Weight(ctx, ggml.Q4_K, 4, 100, np.zeros(10, np.uint8))
     with pytest.raises(ZllmError):
         Weight(ctx, 3, 4, 256, np.zeros(4 * 160, np.uint8))       # Q4_1 is not a hot-path type
+
+
+def test_weight_outlives_context():
+    """Handles freed after their context is destroyed release only the handle (no crash, no leak)."""
+    c = Context(0)
+    wt = synth.tensor(ggml.Q4_K, 64, 256, np.random.default_rng(0), "bench")
+    w = Weight.from_tensor(c, wt)
+    c.close()
+    w.free()

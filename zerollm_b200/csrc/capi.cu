@@ -77,6 +77,14 @@ extern "C" void zllm_destroy(zllm_ctx *c) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  // weights may outlive their context: free their device memory now and detach them, so a later
+  // zllm_weight_free only releases the handle
+  for (zllm_weight *w : c->weights) {
+    if (w->m.data && w->owns) cudaFree(w->m.data);
+    w->m.data = nullptr;
+    w->ctx = nullptr;
+  }
+  c->weights.clear();
   for (int i = 0; i < kScratchSlots; i++)
     if (c->scratch[i]) cudaFree(c->scratch[i]);
   if (c->status_host) cudaFreeHost(c->status_host);
@@ -147,16 +155,18 @@ extern "C" int zllm_weight_upload(zllm_ctx *c, int type, int64_t rows, int64_t c
     delete w;
     return zllm_cuda_fail(c, e, "zllm_weight_upload");
   }
+  c->weights.insert(w);
   *out = w;
   return ZLLM_OK;
 }
 
 extern "C" void zllm_weight_free(zllm_weight *w) {
   if (!w) return;
-  if (w->m.data && w->owns) {
+  if (w->ctx) {
     cudaSetDevice(w->ctx->device);
     cudaStreamSynchronize(w->ctx->stream);
-    cudaFree(w->m.data);
+    if (w->m.data && w->owns) cudaFree(w->m.data);
+    w->ctx->weights.erase(w);
   }
   delete w;
 }
@@ -184,6 +194,7 @@ extern "C" int zllm_quantize_act(zllm_ctx *c, const float *x, int64_t k, int nto
 extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, const float *xd, const int32_t *xs,
                        const float *x, int ntok, float *y, int64_t y_stride, const float *y_add, void *stream) {
   if (!c || !w || !y || ntok < 1) { zllm_set_error(c, "zllm_mm: bad argument"); return ZLLM_E_ARG; }
+  if (!w->m.data) { zllm_set_error(c, "zllm_mm: the weight's context was destroyed"); return ZLLM_E_STATE; }
   const bool q = type_quantized(w->m.type);
   if (q ? (!xq || !xd || !xs) : !x) { zllm_set_error(c, "zllm_mm: missing activation for this weight type"); return ZLLM_E_ARG; }
   if (ntok > 1 && y_stride < w->m.rows) { zllm_set_error(c, "zllm_mm: y_stride < rows"); return ZLLM_E_ARG; }

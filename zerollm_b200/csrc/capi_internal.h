@@ -4,6 +4,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <set>
+
 #include "internal.h"
 
 constexpr int kScratchSlots = 16;
@@ -17,6 +19,7 @@ struct zllm_ctx {
   void *scratch[kScratchSlots] = {};
   size_t scratch_bytes[kScratchSlots] = {};
   char err[512] = {0};
+  std::set<struct zllm_weight *> weights;   // live uploads: zllm_destroy releases their device memory
 };
 
 struct zllm_weight {

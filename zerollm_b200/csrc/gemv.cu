@@ -248,6 +248,12 @@ __device__ __forceinline__ double acc_add(double a, double b) { return __dadd_rn
 __device__ __forceinline__ float acc_add(float a, float b) { return __fadd_rn(a, b); }
 
 // ============================================================================ kernel
+// One CTA = 8 warps split into row groups of G warps (G = 1, 2, 4 or 8).  A row group owns a
+// contiguous range of the CTA's rows and its own ring of shared-memory stages; each warp of the
+// group owns a contiguous slice of every row's units (with its activation in registers).  Lane 0
+// of the group's first warp issues the group's bulk copies.  Warps wait on mbarriers only: there
+// is no CTA-wide barrier until the very end, where rows with G > 1 add their G warp partials in
+// warp order.
 struct GemvArgs {
   const uint8_t *w;
   int64_t row_stride;
@@ -257,113 +263,139 @@ struct GemvArgs {
   float *y;
   const float *y_add;
   unsigned *status;
-  int units, tr, rg, cr, ns, stage_bytes;
+  int units;         // units per row
+  int g;             // warps per row group
+  int uw;            // units per warp (slice width)
+  int cr;            // rows per chunk (one bulk copy)
+  int nsg;           // stages per row group
+  int stage_bytes;
+  int max_rows;      // rows per CTA upper bound (sizes the partial-sum table)
 };
 
-constexpr int kConsumers = 256;             // max consumer threads per CTA
-constexpr int kThreads = kConsumers + 32;   // + one producer warp
-constexpr int kMaxStages = 32;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxStagesPerGroup = 16;
 
-template <class F, int UPT>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs p) {
+template <class F, int UPT, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) {
   using Acc = typename F::Acc;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int tid = threadIdx.x;
-  const int ncons = p.tr * p.rg;
-  const int wg = p.tr >> 5;                                     // warps per row group
-  uint8_t *stages = smem;
-  Acc *part = reinterpret_cast<Acc *>(smem + (size_t)p.ns * p.stage_bytes);
-  const size_t part_bytes = ((size_t)p.ns * p.cr * wg * sizeof(Acc) + 15) / 16 * 16;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)p.ns * p.stage_bytes + part_bytes);
-  uint64_t *empty = full + p.ns;
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + p.ns);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ngroups = kWarps / p.g;
+  const int gi = warp / p.g, wi = warp % p.g;
+  const bool leader = wi == 0 && lane == 0;
+
+  uint8_t *stages = smem + (size_t)gi * p.nsg * p.stage_bytes;
+  const size_t stage_area = (size_t)kWarps / p.g * p.nsg * p.stage_bytes;
+  Acc *part = reinterpret_cast<Acc *>(smem + stage_area);
+  const size_t part_bytes = ((size_t)p.max_rows * p.g * sizeof(Acc) + 15) / 16 * 16;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + stage_area + part_bytes);
+  uint64_t *full = bars + (size_t)gi * 2 * p.nsg;
+  uint64_t *empty = full + p.nsg;
 
   const int64_t G = gridDim.x;
-  const int64_t r0 = (int64_t)blockIdx.x * p.rows / G, r1 = ((int64_t)blockIdx.x + 1) * p.rows / G;
+  const int64_t c0 = (int64_t)blockIdx.x * p.rows / G, c1 = ((int64_t)blockIdx.x + 1) * p.rows / G;
+  const int64_t cta_rows = c1 - c0;
+  const int64_t r0 = c0 + (int64_t)gi * cta_rows / ngroups, r1 = c0 + ((int64_t)gi + 1) * cta_rows / ngroups;
   const int nrows = (int)(r1 - r0);
   const int nchunks = (nrows + p.cr - 1) / p.cr;
 
-  if (tid == 0) {
-    for (int i = 0; i < p.ns; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-    *abort_flag = 0;
+  // ---- set-up: the group leader initialises its barriers and starts its first copies at once
+  //      (weights never depend on the previous kernel, so this runs before griddepcontrol.wait)
+  int issued = min(nchunks, p.nsg);                 // tracked identically by every lane
+  if (leader) {
+    for (int i = 0; i < p.nsg; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], p.g); }
     fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-
-  if (tid >= kConsumers) {
-    // ------------------------------------------------------------------ producer
-    if (tid == kConsumers) {
-      const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
-      int issued = 0;
-      for (int i = 0; i < nchunks; i++) {
-        const int s = i % p.ns;
-        if (i >= p.ns && !mbar_wait_bounded(&empty[s], ((i / p.ns) - 1) & 1, deadline)) {
-          atomicOr(p.status, ST_EMPTY_TIMEOUT);
-          *abort_flag = 1;
-          break;
-        }
-        if (*abort_flag) break;
-        const int nr = min(p.cr, nrows - i * p.cr);
-        const uint32_t bytes = (uint32_t)(nr * p.row_stride);
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(stages + (size_t)s * p.stage_bytes, p.w + (r0 + (int64_t)i * p.cr) * p.row_stride, bytes, &full[s]);
-        issued = i + 1;
-      }
-      // every copy this CTA started must land before the CTA exits
-      const uint64_t drain_deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
-      for (int s = 0; s < p.ns && s < issued; s++) {
-        const int last = s + ((issued - 1 - s) / p.ns) * p.ns;
-        if (!mbar_wait_bounded(&full[s], (last / p.ns) & 1, drain_deadline)) atomicOr(p.status, ST_DRAIN_TIMEOUT);
-      }
-    }
-  } else if (tid < ncons) {
-    // ------------------------------------------------------------------ consumers
-    pdl_wait();                                                // activations come from the previous kernel
-    const int slot = tid / p.tr, lt = tid % p.tr;
-    typename F::Act act[UPT];
-#pragma unroll
-    for (int j = 0; j < UPT; j++) {
-      const int u = lt + j * p.tr;
-      if (u < p.units) F::load(act[j], p.act, u);
-    }
-    const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
-    for (int i = 0; i < nchunks; i++) {
-      const int s = i % p.ns;
-      const bool timed_out = !mbar_wait_bounded(&full[s], (i / p.ns) & 1, deadline);
-      // one uniform decision for all consumers (the producer may raise abort_flag at any time)
-      if (named_sync_or(1, ncons, timed_out || *abort_flag)) {
-        *abort_flag = 1;
-        if (tid == 0) atomicOr(p.status, ST_FULL_TIMEOUT);
-        break;
-      }
-      const uint8_t *st = stages + (size_t)s * p.stage_bytes;
+    for (int i = 0; i < issued; i++) {
       const int nr = min(p.cr, nrows - i * p.cr);
-      for (int rr = slot; rr < nr; rr += p.rg) {
-        const uint8_t *row = st + (size_t)rr * p.row_stride;
-        Acc a = 0;
-#pragma unroll
-        for (int j = 0; j < UPT; j++) {
-          const int u = lt + j * p.tr;
-          if (u < p.units) F::dot(act[j], row, u, p.nb, a);
-        }
-        a = warp_sum(a);
-        if ((tid & 31) == 0) part[((size_t)s * p.cr + rr) * wg + (lt >> 5)] = a;
-      }
-      named_sync(1, ncons);
-      if (tid < nr) {
-        const Acc *pp = part + ((size_t)s * p.cr + tid) * wg;
-        Acc a = pp[0];
-        for (int w = 1; w < wg; w++) a = acc_add(a, pp[w]);
-        const int64_t r = r0 + (int64_t)i * p.cr + tid;
-        float out = (float)a;
-        if (p.y_add) out = __fadd_rn(p.y_add[r], out);
-        p.y[r] = out;
-      }
-      if (tid == 0) mbar_arrive(&empty[s]);
+      const uint32_t bytes = (uint32_t)(nr * p.row_stride);
+      mbar_arrive_expect_tx(&full[i], bytes);
+      bulk_g2s(stages + (size_t)i * p.stage_bytes, p.w + (r0 + (int64_t)i * p.cr) * p.row_stride, bytes, &full[i]);
     }
   }
-  __syncthreads();
+  __syncthreads();                                   // barriers initialised before anyone waits on them
+  pdl_launch_dependents();
+  pdl_wait();                                        // the activation comes from the previous kernel
+
+  typename F::Act act[UPT];
+  const int u0 = wi * p.uw, u1 = min(p.units, u0 + p.uw);
+#pragma unroll
+  for (int j = 0; j < UPT; j++) {
+    const int u = u0 + lane + 32 * j;
+    if (u < u1) F::load(act[j], p.act, u);
+  }
+
+  const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
+  bool aborted = false;
+  for (int i = 0; i < nchunks; i++) {
+    const int s = i % p.nsg;
+    // warp-uniform decision: every lane waits (bounded), then the warp agrees
+    const bool ok = mbar_wait_bounded(&full[s], (i / p.nsg) & 1, deadline);
+    if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+    const uint8_t *st = stages + (size_t)s * p.stage_bytes;
+    const int nr = min(p.cr, nrows - i * p.cr);
+    for (int rr = 0; rr < nr; rr++) {
+      const uint8_t *row = st + (size_t)rr * p.row_stride;
+      Acc a = 0;
+#pragma unroll
+      for (int j = 0; j < UPT; j++) {
+        const int u = u0 + lane + 32 * j;
+        if (u < u1) F::dot(act[j], row, u, p.nb, a);
+      }
+      a = warp_sum(a);
+      const int lrow = (int)(r0 - c0) + i * p.cr + rr;
+      if (lane == 0) {
+        if (p.g == 1) {
+          const int64_t r = r0 + (int64_t)i * p.cr + rr;
+          float out = (float)a;
+          if (p.y_add) out = __fadd_rn(p.y_add[r], out);
+          p.y[r] = out;
+        } else {
+          part[(size_t)lrow * p.g + wi] = a;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    // refill stage s with chunk i + nsg once every warp of the group has released it
+    if (wi == 0 && issued < nchunks) {
+      bool fine = true;
+      if (lane == 0) {
+        fine = mbar_wait_bounded(&empty[s], (i / p.nsg) & 1, deadline);
+        if (fine) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          const int nr2 = min(p.cr, nrows - issued * p.cr);
+          const uint32_t bytes = (uint32_t)(nr2 * p.row_stride);
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(stages + (size_t)s * p.stage_bytes, p.w + (r0 + (int64_t)issued * p.cr) * p.row_stride, bytes,
+                   &full[s]);
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, fine, 0)) { aborted = true; break; }
+      issued++;
+    }
+  }
+  if (aborted && lane == 0) atomicOr(p.status, ST_FULL_TIMEOUT);
+  if (leader) {
+    // every copy this group started must land before the CTA exits (only pending after an abort)
+    const uint64_t drain_deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
+    for (int s = 0; s < p.nsg && s < issued; s++) {
+      const int last = s + ((issued - 1 - s) / p.nsg) * p.nsg;
+      if (!mbar_wait_bounded(&full[s], (last / p.nsg) & 1, drain_deadline)) atomicOr(p.status, ST_DRAIN_TIMEOUT);
+    }
+  }
+  if (p.g > 1) {
+    __syncthreads();
+    for (int lr = threadIdx.x; lr < cta_rows; lr += kThreads) {
+      const Acc *pp = part + (size_t)lr * p.g;
+      Acc a = pp[0];
+      for (int w = 1; w < p.g; w++) a = acc_add(a, pp[w]);
+      const int64_t r = c0 + lr;
+      float out = (float)a;
+      if (p.y_add) out = __fadd_rn(p.y_add[r], out);
+      p.y[r] = out;
+    }
+  }
 }
 
 // ============================================================================ repack (load time)
@@ -443,6 +475,10 @@ static int units_of(int t, int64_t k) {
 
 static size_t acc_bytes(int t) { return type_quantized(t) ? 8 : 4; }
 
+// Shared memory one CTA may use for stages: two CTAs fit per SM, so the next kernel of the stream
+// can become resident (and start its own weight copies) while this one finishes.
+constexpr int64_t kStageBudget = 96 * 1024;
+
 bool plan_gemv(const DevMatrix &m, int num_sms, GemvPlan *p, const char **why) {
   if (!type_supported(m.type)) { *why = "unsupported tensor type"; return false; }
   if ((m.type == T_F16 || m.type == T_BF16) && m.cols % 8) { *why = "F16/BF16 rows must be a multiple of 8 values"; return false; }
@@ -450,54 +486,57 @@ bool plan_gemv(const DevMatrix &m, int num_sms, GemvPlan *p, const char **why) {
   const int U = units_of(m.type, m.cols);
   if (U <= 0) { *why = "empty row"; return false; }
   p->units = U;
-  p->tr = U <= kConsumers ? (U + 31) / 32 * 32 : kConsumers;
-  p->upt = (U + p->tr - 1) / p->tr;
-  if (p->upt > 4) { *why = "row too long for the decode GEMV (more than 4 units per thread)"; return false; }
+  // warps per row group: as few as possible while each lane holds at most 2 units (else 4)
+  int g = 0;
+  for (int c = 1; c <= kWarps && !g; c *= 2) if ((U + c - 1) / c <= 64) g = c;
+  for (int c = 1; c <= kWarps && !g; c *= 2) if ((U + c - 1) / c <= 128) g = c;
+  if (!g) { *why = "row too long for the decode GEMV"; return false; }
+  p->g = g;
+  p->uw = (U + g - 1) / g;
+  p->upt = (p->uw + 31) / 32;
   if (p->upt == 3) p->upt = 4;
-  p->rg = kConsumers / p->tr;
-  if (p->rg < 1) p->rg = 1;
-  // ~8 KB chunks: small enough that the compute left after the last chunk lands is short,
-  // large enough that each bulk copy moves whole rows.
-  const int64_t target = 8192;
-  int64_t k = (target + (int64_t)p->rg * m.row_stride / 2) / ((int64_t)p->rg * m.row_stride);
-  if (k < 1) k = 1;
-  p->cr = (int)(k * p->rg);
-  if (p->cr > 64) p->cr = 64 / p->rg * p->rg;
-  if (p->cr < 1) p->cr = 1;
-  const int64_t stage = ((int64_t)p->cr * m.row_stride + 127) / 128 * 128;
-  if (stage > 100 * 1024) { *why = "row too long for a shared-memory stage"; return false; }
-  p->stage_bytes = (int)stage;
-  int64_t grid = (m.rows + p->cr - 1) / p->cr;
-  if (grid > num_sms) grid = num_sms;
+  const int ngroups = kWarps / g;
+  int64_t grid = m.rows < num_sms ? m.rows : num_sms;
   if (grid < 1) grid = 1;
   p->grid = (int)grid;
-  const int64_t rows_per_cta = (m.rows + grid - 1) / grid;
-  const int64_t chunks = (rows_per_cta + p->cr - 1) / p->cr;
-  const int64_t budget = 200 * 1024;
-  int64_t ns = budget / stage;
-  if (ns > kMaxStages) ns = kMaxStages;
-  if (ns > chunks) ns = chunks;
-  if (ns < 1) ns = 1;
-  p->ns = (int)ns;
-  const size_t part = (size_t)p->ns * p->cr * (p->tr / 32) * acc_bytes(m.type);
-  p->smem_bytes = (int)((size_t)p->ns * p->stage_bytes + (part + 15) / 16 * 16 + 2 * 8 * p->ns + 16);
+  const int64_t rows_cta = (m.rows + grid - 1) / grid;
+  const int64_t rows_grp = (rows_cta + ngroups - 1) / ngroups;
+  // ~8 KB chunks: the compute left after the last chunk lands stays short
+  int64_t cr = (8192 + m.row_stride / 2) / m.row_stride;
+  if (cr < 1) cr = 1;
+  if (cr > rows_grp) cr = rows_grp;
+  if (cr < 1) cr = 1;
+  p->cr = (int)cr;
+  const int64_t stage = (cr * m.row_stride + 127) / 128 * 128;
+  if (stage > 110 * 1024) { *why = "row too long for a shared-memory stage"; return false; }
+  p->stage_bytes = (int)stage;
+  const int64_t chunks = (rows_grp + cr - 1) / cr;
+  int64_t nsg = kStageBudget / ngroups / stage;
+  if (nsg > kMaxStagesPerGroup) nsg = kMaxStagesPerGroup;
+  if (nsg > chunks) nsg = chunks;
+  if (nsg < 1) nsg = 1;
+  p->nsg = (int)nsg;
+  p->max_rows = (int)rows_cta + 1;
+  const size_t part = g > 1 ? ((size_t)p->max_rows * g * acc_bytes(m.type) + 15) / 16 * 16 : 0;
+  p->smem_bytes = (int)((size_t)ngroups * nsg * stage + part + (size_t)ngroups * 2 * nsg * 8);
   return true;
 }
 
 template <class F, int UPT>
 static cudaError_t launch_one(const GemvArgs &a, const GemvPlan &pl, cudaStream_t s, bool pdl) {
-  auto kern = gemv_kernel<F, UPT>;
-  // the opt-in shared-memory size is a per-device function attribute: set it once per device
-  // (and only when it grows) so that launches inside stream capture make no attribute calls
-  static int granted[64] = {0};
+  constexpr int MINB = UPT <= 2 ? 2 : 1;
+  auto kern = gemv_kernel<F, UPT, MINB>;
+  // the opt-in shared-memory size is a per-device function attribute: set it once per device so
+  // that launches inside stream capture make no attribute calls
+  static bool granted[64] = {false};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (granted[dev] < pl.smem_bytes) {
+  if (!granted[dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
-    granted[dev] = 227 * 1024;
+    granted[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
@@ -540,7 +579,8 @@ cudaError_t launch_gemv(const DevMatrix &m, const ActView &act, int ntok, float 
     a.y = y + (int64_t)t * y_stride;
     a.y_add = y_add ? y_add + (int64_t)t * y_stride : nullptr;
     a.status = status;
-    a.units = pl.units; a.tr = pl.tr; a.rg = pl.rg; a.cr = pl.cr; a.ns = pl.ns; a.stage_bytes = pl.stage_bytes;
+    a.units = pl.units; a.g = pl.g; a.uw = pl.uw; a.cr = pl.cr; a.nsg = pl.nsg; a.stage_bytes = pl.stage_bytes;
+    a.max_rows = pl.max_rows;
     cudaError_t e;
     switch (m.type) {
       case T_Q4_K: e = launch_fmt<FmtK45<false>>(a, pl, s, pdl); break;

@@ -38,7 +38,7 @@ struct ActView {
 
 // Launch geometry of one GEMV (computed on the host, see plan_gemv).
 struct GemvPlan {
-  int units, tr, rg, upt, cr, ns, stage_bytes, grid, smem_bytes;
+  int units, g, uw, upt, cr, nsg, stage_bytes, grid, smem_bytes, max_rows;
 };
 
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s);
