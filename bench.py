@@ -245,6 +245,17 @@ def run_ours(args, world, rank, local):
             return float(t.item())
         return v
 
+    if args.profile:
+        # plain launches (no graph) for an ncu capture: warm-up then `steps` quantize + GEMV pairs
+        enqueue(args.warmup)
+        enqueue(args.steps)
+        torch.cuda.synchronize()
+        ctx.sync()
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "launches": 2 * (args.warmup + args.steps)}))
+        ctx.close()
+        return
+
     g_warm = graph(max(args.warmup, 1))
     g_main = graph(args.steps)
     g_kern = graph(args.steps, with_quant=False)
@@ -339,6 +350,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="plain launches without graphs or timing, for ncu")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args.gpus)

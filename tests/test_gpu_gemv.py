@@ -57,7 +57,10 @@ def test_matvec_matches_oracle(ctx, t, rows, cols):
     x = rng.standard_normal(cols).astype(np.float32)
     want = O.matvec(t, wt["data"], rows, cols, x, nthreads=8)
     w = Weight.from_tensor(ctx, wt)
-    got = matvec(w, Act(ctx, x)).cpu().numpy().ravel()
+    y = torch.full((1, rows), float("nan"), device="cuda")    # unwritten rows would stay NaN
+    got = matvec(w, Act(ctx, x), y=y).cpu().numpy().ravel()
+    ctx.sync()                                                # raises on a device-side timeout
+    assert np.isfinite(got).all(), np.argwhere(~np.isfinite(got))[:10]
     rel = _rel(got, want)
     assert rel <= 1e-3
     if t in ggml.QUANTIZED:

@@ -288,7 +288,8 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
   uint8_t *stages = smem + (size_t)gi * p.nsg * p.stage_bytes;
   const size_t stage_area = (size_t)kWarps / p.g * p.nsg * p.stage_bytes;
   Acc *part = reinterpret_cast<Acc *>(smem + stage_area);
-  const size_t part_bytes = ((size_t)p.max_rows * p.g * sizeof(Acc) + 15) / 16 * 16;
+  // the same layout plan_gemv sized: the partial table exists only for multi-warp row groups
+  const size_t part_bytes = p.g > 1 ? ((size_t)p.max_rows * p.g * sizeof(Acc) + 15) / 16 * 16 : 0;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + stage_area + part_bytes);
   uint64_t *full = bars + (size_t)gi * 2 * p.nsg;
   uint64_t *empty = full + p.nsg;
