@@ -73,8 +73,10 @@ void zllm_weight_free(zllm_weight *w);
 int zllm_weight_info(const zllm_weight *w, int *ggml_type, int64_t *rows, int64_t *cols, size_t *device_bytes);
 
 /* ------------------------------------------------------------------------------------ kernels
- * Device-pointer entry points, enqueued on `stream` (a cudaStream_t; NULL = the context stream).
- * They do not synchronise. */
+ * Device-pointer entry points, enqueued on `stream` (a cudaStream_t; NULL = the context stream,
+ * (void *)1 = cudaStreamLegacy, the legacy default stream).  They do not synchronise.  On a real
+ * stream consecutive kernels are chained with programmatic dependent launch (the next kernel starts
+ * streaming its weights while the previous one finishes); on the legacy stream they are not. */
 
 /* xq[t][k] int8, xd[t][k/32] f32 scales, xs[t][k/32] int32 block sums of x[t][k] for t < ntok;
  * bit-exact with quantizeAct (src/compute/ref-kernels.js:44-62; worker `prep` worker.js:238-249). */

@@ -45,6 +45,9 @@ int zllm_scratch(zllm_ctx *c, int slot, size_t bytes, void **out) {
 }
 
 static cudaStream_t pick(zllm_ctx *c, void *stream) { return stream ? (cudaStream_t)stream : c->stream; }
+// Programmatic dependent launch is used on real streams only: the legacy default stream (handle 0,
+// passed through `zllm_stream`-less callers) keeps plain stream ordering.
+static bool pdl_ok(cudaStream_t s) { return s != nullptr && s != cudaStreamLegacy && s != cudaStreamPerThread; }
 
 // ------------------------------------------------------------------------------------ context
 extern "C" const char *zllm_version(void) { return "zllm-b200 0.1 (sm_100a)"; }
@@ -58,11 +61,11 @@ extern "C" int zllm_init(int device, zllm_ctx **out) {
   cudaError_t e = cudaSetDevice(device);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
-  if (e == cudaSuccess) e = cudaHostAlloc((void **)&c->status_host, sizeof(unsigned), cudaHostAllocMapped);
-  if (e == cudaSuccess) {
-    *c->status_host = 0;
-    e = cudaHostGetDevicePointer((void **)&c->status_dev, c->status_host, 0);
-  }
+  // the status word lives in device memory: device atomics on mapped host memory are not atomic
+  // (and may be lost) on PCIe hosts
+  if (e == cudaSuccess) e = cudaMalloc((void **)&c->status_dev, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemsetAsync(c->status_dev, 0, sizeof(unsigned), c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) {
     fprintf(stderr, "zllm_init: %s\n", cudaGetErrorString(e));
     int rc = e == cudaErrorMemoryAllocation ? ZLLM_E_OOM : ZLLM_E_CUDA;
@@ -87,7 +90,7 @@ extern "C" void zllm_destroy(zllm_ctx *c) {
   c->weights.clear();
   for (int i = 0; i < kScratchSlots; i++)
     if (c->scratch[i]) cudaFree(c->scratch[i]);
-  if (c->status_host) cudaFreeHost(c->status_host);
+  if (c->status_dev) cudaFree(c->status_dev);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
 }
@@ -96,9 +99,11 @@ extern "C" const char *zllm_last_error(const zllm_ctx *c) { return c ? c->err : 
 extern "C" void *zllm_stream(zllm_ctx *c) { return c ? (void *)c->stream : nullptr; }
 
 int zllm_check_status(zllm_ctx *c) {
-  unsigned st = *(volatile unsigned *)c->status_host;
+  unsigned st = 0;
+  cudaError_t e = cudaMemcpy(&st, c->status_dev, sizeof(unsigned), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return zllm_cuda_fail(c, e, "reading the device status word");
   if (st) {
-    *(volatile unsigned *)c->status_host = 0;
+    cudaMemset(c->status_dev, 0, sizeof(unsigned));
     zllm_set_error(c, "device wait timed out (status 0x%x): a bulk copy or stage hand-off did not complete within 2 s; "
                       "the kernel drained its copies and returned", st);
     return ZLLM_E_TIMEOUT;
@@ -140,7 +145,7 @@ extern "C" int zllm_weight_upload(zllm_ctx *c, int type, int64_t rows, int64_t c
   cudaError_t e = cudaMalloc((void **)&w->m.data, w->bytes);
   if (e != cudaSuccess) { delete w; return zllm_cuda_fail(c, e, "cudaMalloc(weight)"); }
   void *staging = nullptr;
-  const bool direct = w->m.row_stride == rb && (type == T_Q4_K || type == T_Q5_K || type == T_F16 || type == T_BF16 || type == T_F32);
+  const bool direct = w->m.row_stride == rb && (type == T_F16 || type == T_BF16 || type == T_F32);
   if (direct) {
     e = cudaMemcpyAsync(w->m.data, host, nbytes, cudaMemcpyHostToDevice, c->stream);
   } else {
@@ -187,7 +192,8 @@ extern "C" int zllm_quantize_act(zllm_ctx *c, const float *x, int64_t k, int nto
     zllm_set_error(c, "zllm_quantize_act: bad argument (k must be a positive multiple of 32)");
     return ZLLM_E_ARG;
   }
-  cudaError_t e = launch_quantize(x, k, ntok, xq, xd, xs, c->status_dev, pick(c, stream));
+  cudaStream_t st = pick(c, stream);
+  cudaError_t e = launch_quantize(x, k, ntok, xq, xd, xs, c->status_dev, st, pdl_ok(st));
   return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "quantize_act launch");
 }
 
@@ -200,7 +206,8 @@ extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, cons
   if (ntok > 1 && y_stride < w->m.rows) { zllm_set_error(c, "zllm_mm: y_stride < rows"); return ZLLM_E_ARG; }
   ActView a{xq, xd, xs, x, w->m.cols};
   const char *why = "";
-  cudaError_t e = launch_gemv(w->m, a, ntok, y, y_stride, y_add, c->status_dev, c->num_sms, pick(c, stream), true, &why);
+  cudaStream_t st = pick(c, stream);
+  cudaError_t e = launch_gemv(w->m, a, ntok, y, y_stride, y_add, c->status_dev, c->num_sms, st, pdl_ok(st), &why);
   if (e == cudaErrorInvalidValue && why[0]) { zllm_set_error(c, "zllm_mm: %s", why); return ZLLM_E_UNSUPPORTED; }
   return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "gemv launch");
 }

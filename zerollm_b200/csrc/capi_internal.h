@@ -14,8 +14,7 @@ struct zllm_ctx {
   int device = 0;
   int num_sms = 148;
   cudaStream_t stream = nullptr;
-  unsigned *status_host = nullptr;   // mapped pinned word the kernels report timeouts into
-  unsigned *status_dev = nullptr;
+  unsigned *status_dev = nullptr;    // device word the kernels report timeouts into (atomicOr)
   void *scratch[kScratchSlots] = {};
   size_t scratch_bytes[kScratchSlots] = {};
   char err[512] = {0};

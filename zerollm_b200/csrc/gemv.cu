@@ -27,8 +27,40 @@ namespace zllm {
 
 // ============================================================================ helpers
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xffu; }
-__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+// shared-memory loads by 32-bit shared-window address (volatile: never hoisted above an mbarrier wait)
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
 __device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+// int32 -> double without the conversion pipe: (2^52 + 2^31 + v) - (2^52 + 2^31) is exact in double.
+// i2d_biased takes v + 2^31 (mod 2^32), which an integer multiply-add produces for free.
+__device__ __forceinline__ double i2d_biased(uint32_t v_plus_2p31) {
+  return __dsub_rn(__hiloint2double(0x43300000, (int)v_plus_2p31), 4503601774854144.0);
+}
+__device__ __forceinline__ double i2d_exact(int v) { return i2d_biased((uint32_t)v + 0x80000000u); }
+// sum of 4 (unsigned byte of a) x (signed byte of b) products plus c
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 // 4 bits -> bit 0 of each of 4 bytes
 __device__ __forceinline__ uint32_t spread4(uint32_t t) { return (t * 0x00204081u) & 0x01010101u; }
 
@@ -44,7 +76,8 @@ struct FmtK45 {
   static constexpr bool QACT = true;
   static constexpr int BS = FIVE ? 176 : 144;
   static constexpr int QS = FIVE ? 48 : 16;
-  struct Act { uint32_t lo[8], hi[8]; double xd0, xd1, xs0, xs1; };
+  // activation registers of one unit, plus the lane-constant pieces of its addressing
+  struct Act { uint32_t lo[8], hi[8]; double xd0, xd1; int xsi0, xsi1, off, c; };
   static __host__ __device__ int units(int64_t k) { return (int)(k / 64); }
   __device__ static void load(Act &a, const ActView &v, int u) {
     const uint8_t *q = reinterpret_cast<const uint8_t *>(v.xq) + (int64_t)u * 64;
@@ -55,54 +88,57 @@ struct FmtK45 {
     a.hi[4] = t3.x; a.hi[5] = t3.y; a.hi[6] = t3.z; a.hi[7] = t3.w;
     a.xd0 = (double)__ldg(v.xd + 2 * u);
     a.xd1 = (double)__ldg(v.xd + 2 * u + 1);
-    a.xs0 = (double)__ldg(v.xs + 2 * u);
-    a.xs1 = (double)__ldg(v.xs + 2 * u + 1);
+    a.xsi0 = __ldg(v.xs + 2 * u);
+    a.xsi1 = __ldg(v.xs + 2 * u + 1);
+    a.off = (u >> 2) * BS;
+    a.c = u & 3;
   }
-  __device__ static void dot(const Act &a, const uint8_t *row, int u, int nb, Acc &acc) {
-    const int sb = u >> 2, c = u & 3;
-    const uint8_t *blk = row + sb * BS;
+  __device__ static void dot(const Act &a, uint32_t row, int u, int nb, Acc &acc) {
+    const int c = a.c;
+    const uint32_t blk = row + a.off;
     const uint4 h = lds128(blk);
     const uint4 q0 = lds128(blk + QS + c * 32), q1 = lds128(blk + QS + c * 32 + 16);
     const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    int lo = 0, hi = 0;
+    int lo0 = 0, lo1 = 0, hi0 = 0, hi1 = 0;      // two chains each: shorter dependency paths
+    int hi;
     if (FIVE) {
       const uint4 e0 = lds128(blk + 16), e1 = lds128(blk + 32);
       const uint32_t e[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
 #pragma unroll
       for (int i = 0; i < 8; i++) {
-        uint32_t vl = (w[i] & 0x0f0f0f0fu) | (((e[i] >> (2 * c)) & 0x01010101u) << 4);
-        uint32_t vh = ((w[i] >> 4) & 0x0f0f0f0fu) | (((e[i] >> (2 * c + 1)) & 0x01010101u) << 4);
-        lo = __dp4a((int)vl, (int)a.lo[i], lo);
-        hi = __dp4a((int)vh, (int)a.hi[i], hi);
+        const uint32_t vl = (w[i] & 0x0f0f0f0fu) | (((e[i] >> (2 * c)) & 0x01010101u) << 4);
+        const uint32_t vh = ((w[i] >> 4) & 0x0f0f0f0fu) | (((e[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+        if (i & 1) { lo1 = __dp4a((int)vl, (int)a.lo[i], lo1); hi1 = __dp4a((int)vh, (int)a.hi[i], hi1); }
+        else { lo0 = __dp4a((int)vl, (int)a.lo[i], lo0); hi0 = __dp4a((int)vh, (int)a.hi[i], hi0); }
       }
+      hi = hi0 + hi1;
     } else {
+      // high nibbles are dotted in place (16 x the nibble, unsigned bytes x signed activations)
 #pragma unroll
       for (int i = 0; i < 8; i++) {
-        lo = __dp4a((int)(w[i] & 0x0f0f0f0fu), (int)a.lo[i], lo);
-        hi = __dp4a((int)((w[i] >> 4) & 0x0f0f0f0fu), (int)a.hi[i], hi);
+        if (i & 1) { lo1 = dp4a_us(w[i] & 0x0f0f0f0fu, a.lo[i], lo1); hi1 = dp4a_us(w[i] & 0xf0f0f0f0u, a.hi[i], hi1); }
+        else { lo0 = dp4a_us(w[i] & 0x0f0f0f0fu, a.lo[i], lo0); hi0 = dp4a_us(w[i] & 0xf0f0f0f0u, a.hi[i], hi0); }
       }
+      hi = (hi0 + hi1) >> 4;                     // exact: the sum is a multiple of 16
     }
-    // unpackScaleMinK4 (quant.js:109-118) for sub-blocks 2c and 2c+1
-    const int k0 = (2 * c) & 3, k1 = k0 + 1;
-    int sc0, mn0, sc1, mn1;
-    if (c < 2) {
-      sc0 = byte_of(h.y, k0) & 63; mn0 = byte_of(h.z, k0) & 63;
-      sc1 = byte_of(h.y, k1) & 63; mn1 = byte_of(h.z, k1) & 63;
-    } else {
-      sc0 = (byte_of(h.w, k0) & 15) | ((byte_of(h.y, k0) >> 6) << 4);
-      mn0 = (byte_of(h.w, k0) >> 4) | ((byte_of(h.z, k0) >> 6) << 4);
-      sc1 = (byte_of(h.w, k1) & 15) | ((byte_of(h.y, k1) >> 6) << 4);
-      mn1 = (byte_of(h.w, k1) >> 4) | ((byte_of(h.z, k1) >> 6) << 4);
-    }
-    const float d = h2f(h.x & 0xffffu), dmin = h2f(h.x >> 16);
-    // acc += xd * (d*sc*lo - dmin*mn*xs)   (d*sc and dmin*mn are exact in f32; the products by lo / xs are
-    // exact in double; the subtraction, the scaling by xd and the accumulation round like the JS)
-    const double a0 = __dmul_rn((double)__fmul_rn(d, (float)sc0), (double)lo);
-    const double b0 = __dmul_rn((double)__fmul_rn(dmin, (float)mn0), a.xs0);
-    acc = __dadd_rn(acc, __dmul_rn(a.xd0, __dsub_rn(a0, b0)));
-    const double a1 = __dmul_rn((double)__fmul_rn(d, (float)sc1), (double)hi);
-    const double b1 = __dmul_rn((double)__fmul_rn(dmin, (float)mn1), a.xs1);
-    acc = __dadd_rn(acc, __dmul_rn(a.xd1, __dsub_rn(a1, b1)));
+    const int lo = lo0 + lo1;
+    // scales and mins of sub-blocks 2c, 2c+1: the load-time repack stores them as one 24-bit field per
+    // chunk c at bit 24c of header bytes 4..15 (sc0 | sc1 << 6 | mn0 << 12 | mn1 << 18)
+    const uint32_t wlo = c < 2 ? h.y : (c == 2 ? h.z : h.w);
+    const uint32_t whi = c == 0 ? h.y : (c == 1 ? h.z : (c == 2 ? h.w : 0u));
+    const uint32_t F = __funnelshift_r(wlo, whi, (24 * c) & 31);
+    const int sc0 = F & 63, sc1 = (F >> 6) & 63, mn0 = (F >> 12) & 63, mn1 = (F >> 18) & 63;
+    const double d = (double)h2f(h.x & 0xffffu), dmin = (double)h2f(h.x >> 16);
+    // acc += xd * (d*sc*lo - dmin*mn*xs).  sc*lo and mn*xs are exact 32-bit integers, so d*(sc*lo) and
+    // dmin*(mn*xs) equal the JS products (d*sc)*lo and (dmin*mn)*xs exactly; the fused multiply-add
+    // rounds exactly once where the JS subtraction rounds, and the scaling by xd and the accumulation
+    // round like the JS.
+    const double p0 = i2d_biased((uint32_t)(sc0 * lo) + 0x80000000u), p1 = i2d_biased((uint32_t)(sc1 * hi) + 0x80000000u);
+    const double m0 = __dmul_rn(dmin, i2d_biased((uint32_t)(mn0 * a.xsi0) + 0x80000000u));
+    const double m1 = __dmul_rn(dmin, i2d_biased((uint32_t)(mn1 * a.xsi1) + 0x80000000u));
+    const double t0 = __dmul_rn(a.xd0, __fma_rn(d, p0, -m0));
+    const double t1 = __dmul_rn(a.xd1, __fma_rn(d, p1, -m1));
+    acc = __dadd_rn(__dadd_rn(acc, t0), t1);
   }
 };
 
@@ -127,13 +163,13 @@ struct FmtQ6K {
       a.xd[k] = (double)__ldg(v.xd + sb * 8 + h * 4 + k);
     }
   }
-  __device__ static void dot(const Act &a, const uint8_t *row, int u, int nb, Acc &acc) {
+  __device__ static void dot(const Act &a, uint32_t row, int u, int nb, Acc &acc) {
     const int sb = u >> 2, h = (u >> 1) & 1, g = u & 1;
-    const uint8_t *ql = row + sb * 128 + h * 64 + g * 16;
+    const uint32_t ql = row + sb * 128 + h * 64 + g * 16;
     const uint4 A = lds128(ql), B = lds128(ql + 32);
     const uint4 H = lds128(row + 128 * nb + sb * 64 + h * 32 + g * 16);
-    const uint2 S = *reinterpret_cast<const uint2 *>(row + 192 * nb + sb * 16 + h * 8);
-    const float d = h2f(*reinterpret_cast<const uint16_t *>(row + 208 * nb + sb * 2));
+    const uint2 S = lds64(row + 192 * nb + sb * 16 + h * 8);
+    const float d = h2f(lds16(row + 208 * nb + sb * 2));
     const uint32_t aw[4] = {A.x, A.y, A.z, A.w}, bw[4] = {B.x, B.y, B.z, B.w}, hw[4] = {H.x, H.y, H.z, H.w};
     int gs[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -153,10 +189,9 @@ struct FmtQ6K {
       const int gsum = gs[k] - 32 * a.xsum[k];                 // sum((q - 32) * x), exact
       const uint32_t sw = k < 2 ? S.x : S.y;
       const int scale = (int)(int8_t)byte_of(sw, (2 * k + g) & 3);
-      // acc += xd * d * scale * gsum  (left to right, each product rounded: ref-kernels.js:271)
-      double t = __dmul_rn(a.xd[k], dd);
-      t = __dmul_rn(t, (double)scale);
-      t = __dmul_rn(t, (double)gsum);
+      // acc += xd * d * scale * gsum (ref-kernels.js:271): xd*d (35 bits) and (xd*d)*scale (43 bits) are
+      // exact in double, so the JS left-to-right product equals (xd*d) * (scale*gsum) rounded once.
+      const double t = __dmul_rn(__dmul_rn(a.xd[k], dd), i2d_exact(scale * gsum));
       acc = __dadd_rn(acc, t);
     }
   }
@@ -178,7 +213,7 @@ struct FmtQ0 {
     a.xd = (double)__ldg(v.xd + u);
     a.xs = __ldg(v.xs + u);
   }
-  __device__ static void dot(const Act &a, const uint8_t *row, int u, int nb, Acc &acc) {
+  __device__ static void dot(const Act &a, uint32_t row, int u, int nb, Acc &acc) {
     int s = 0;
     float d;
     if (T == T_Q8_0) {
@@ -186,12 +221,12 @@ struct FmtQ0 {
       const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
       for (int i = 0; i < 8; i++) s = __dp4a((int)w[i], (int)a.x[i], s);
-      d = h2f(*reinterpret_cast<const uint16_t *>(row + 32 * nb + u * 2));
+      d = h2f(lds16(row + 32 * nb + u * 2));
     } else {
       const uint4 q = lds128(row + u * 16);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
       uint32_t qh = 0;
-      if (T == T_Q5_0) qh = *reinterpret_cast<const uint32_t *>(row + 16 * nb + u * 4);
+      if (T == T_Q5_0) qh = lds32(row + 16 * nb + u * 4);
 #pragma unroll
       for (int i = 0; i < 4; i++) {
         uint32_t vl = w[i] & 0x0f0f0f0fu, vh = (w[i] >> 4) & 0x0f0f0f0fu;
@@ -203,9 +238,10 @@ struct FmtQ0 {
         s = __dp4a((int)vh, (int)a.x[4 + i], s);
       }
       s -= (T == T_Q5_0 ? 16 : 8) * a.xs;                    // sum((q - offset) * x), exact
-      d = h2f(*reinterpret_cast<const uint16_t *>(row + (T == T_Q5_0 ? 20 : 16) * nb + u * 2));
+      d = h2f(lds16(row + (T == T_Q5_0 ? 20 : 16) * nb + u * 2));
     }
-    acc = __dadd_rn(acc, __dmul_rn(__dmul_rn((double)s, (double)d), a.xd));
+    // acc += s * d * xd (ref-kernels.js:146): s*d is exact in double, the product by xd rounds once
+    acc = __dadd_rn(acc, __dmul_rn(__dmul_rn(i2d_exact(s), (double)d), a.xd));
   }
 };
 
@@ -224,7 +260,7 @@ struct FmtFloat {
 #pragma unroll
     for (int i = 0; i < PER; i++) a.x[i] = __ldg(p + i);
   }
-  __device__ static void dot(const Act &a, const uint8_t *row, int u, int nb, Acc &acc) {
+  __device__ static void dot(const Act &a, uint32_t row, int u, int nb, Acc &acc) {
     const uint4 q = lds128(row + u * 16);
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
     if (T == T_F32) {
@@ -242,10 +278,46 @@ struct FmtFloat {
   }
 };
 
-__device__ __forceinline__ double warp_sum(double v) { return warp_sum_f64(v); }
-__device__ __forceinline__ float warp_sum(float v) { return warp_sum_f32(v); }
 __device__ __forceinline__ double acc_add(double a, double b) { return __dadd_rn(a, b); }
 __device__ __forceinline__ float acc_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ void warp_sum2(double &a, double &b) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a = __dadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+    b = __dadd_rn(b, __shfl_xor_sync(0xffffffffu, b, o));
+  }
+}
+__device__ __forceinline__ void warp_sum2(float &a, float &b) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+    b = __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, o));
+  }
+}
+// Butterfly reduction of RB per-lane partials (RB = 2 or 4) across the 32 lanes: the first log2(RB)
+// steps exchange half of the remaining values with the partner lane, the rest add one value; lane
+// k*32/RB ends with row k's total.  The order of additions is fixed, so results are deterministic.
+template <int RB, class T>
+__device__ __forceinline__ T reduce_rows(T (&v)[RB], int lane) {
+  if (RB == 4) {
+    const bool b4 = lane & 16;
+    T w0 = acc_add(b4 ? v[2] : v[0], __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[2], 16));
+    T w1 = acc_add(b4 ? v[3] : v[1], __shfl_xor_sync(0xffffffffu, b4 ? v[1] : v[3], 16));
+    const bool b3 = lane & 8;
+    T z = acc_add(b3 ? w1 : w0, __shfl_xor_sync(0xffffffffu, b3 ? w0 : w1, 8));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) z = acc_add(z, __shfl_xor_sync(0xffffffffu, z, o));
+    return z;
+  } else {
+    const bool b4 = lane & 16;
+    T z = acc_add(b4 ? v[1] : v[0], __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[1], 16));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) z = acc_add(z, __shfl_xor_sync(0xffffffffu, z, o));
+    return z;
+  }
+}
+__device__ __forceinline__ double warp_sum(double v) { return warp_sum_f64(v); }
+__device__ __forceinline__ float warp_sum(float v) { return warp_sum_f32(v); }
 
 // ============================================================================ kernel
 // One CTA = 8 warps split into row groups of G warps (G = 1, 2, 4 or 8).  A row group owns a
@@ -278,6 +350,7 @@ constexpr int kMaxStagesPerGroup = 16;
 
 template <class F, int UPT, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) {
+  constexpr int RB = UPT == 1 ? 4 : 2;           // rows per reduction batch
   using Acc = typename F::Acc;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -287,17 +360,18 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
 
   uint8_t *stages = smem + (size_t)gi * p.nsg * p.stage_bytes;
   const size_t stage_area = (size_t)kWarps / p.g * p.nsg * p.stage_bytes;
-  Acc *part = reinterpret_cast<Acc *>(smem + stage_area);
+  Acc *part_tab = reinterpret_cast<Acc *>(smem + stage_area);
   // the same layout plan_gemv sized: the partial table exists only for multi-warp row groups
   const size_t part_bytes = p.g > 1 ? ((size_t)p.max_rows * p.g * sizeof(Acc) + 15) / 16 * 16 : 0;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + stage_area + part_bytes);
   uint64_t *full = bars + (size_t)gi * 2 * p.nsg;
   uint64_t *empty = full + p.nsg;
 
-  const int64_t G = gridDim.x;
-  const int64_t c0 = (int64_t)blockIdx.x * p.rows / G, c1 = ((int64_t)blockIdx.x + 1) * p.rows / G;
-  const int64_t cta_rows = c1 - c0;
-  const int64_t r0 = c0 + (int64_t)gi * cta_rows / ngroups, r1 = c0 + ((int64_t)gi + 1) * cta_rows / ngroups;
+  // row partition (32-bit arithmetic: rows * grid < 2^31 is checked on the host)
+  const uint32_t G = gridDim.x, R = (uint32_t)p.rows;
+  const int64_t c0 = (blockIdx.x * R) / G, c1 = ((blockIdx.x + 1) * R) / G;
+  const uint32_t cta_rows = (uint32_t)(c1 - c0);
+  const int64_t r0 = c0 + (gi * cta_rows) / (uint32_t)ngroups, r1 = c0 + ((gi + 1) * cta_rows) / (uint32_t)ngroups;
   const int nrows = (int)(r1 - r0);
   const int nchunks = (nrows + p.cr - 1) / p.cr;
 
@@ -320,11 +394,16 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
 
   typename F::Act act[UPT];
   const int u0 = wi * p.uw, u1 = min(p.units, u0 + p.uw);
+  // lanes past the end of the slice load (and later compute) a duplicate unit whose result is
+  // discarded: the inner loop stays branch-free
+  bool valid[UPT];
 #pragma unroll
   for (int j = 0; j < UPT; j++) {
     const int u = u0 + lane + 32 * j;
-    if (u < u1) F::load(act[j], p.act, u);
+    valid[j] = u < u1;
+    F::load(act[j], p.act, valid[j] ? u : u1 - 1);
   }
+  const uint32_t stages_s = smem_u32(stages);
 
   const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
   bool aborted = false;
@@ -333,26 +412,40 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
     // warp-uniform decision: every lane waits (bounded), then the warp agrees
     const bool ok = mbar_wait_bounded(&full[s], (i / p.nsg) & 1, deadline);
     if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
-    const uint8_t *st = stages + (size_t)s * p.stage_bytes;
+    const uint32_t st = stages_s + (uint32_t)(s * p.stage_bytes);
     const int nr = min(p.cr, nrows - i * p.cr);
-    for (int rr = 0; rr < nr; rr++) {
-      const uint8_t *row = st + (size_t)rr * p.row_stride;
-      Acc a = 0;
+    // RB rows at a time, one accumulator per (row, unit): independent dependency chains for the
+    // scheduler; then one butterfly reduction across the warp leaves row k's total in lane k*32/RB
+    for (int rr = 0; rr < nr; rr += RB) {
+      Acc v[RB];
 #pragma unroll
-      for (int j = 0; j < UPT; j++) {
-        const int u = u0 + lane + 32 * j;
-        if (u < u1) F::dot(act[j], row, u, p.nb, a);
+      for (int k = 0; k < RB; k++) {
+        const int rk = min(rr + k, nr - 1);            // the tail repeats the last row (result unused)
+        const uint32_t row = st + (uint32_t)(rk * p.row_stride);
+        Acc part[UPT];
+#pragma unroll
+        for (int j = 0; j < UPT; j++) {
+          part[j] = 0;
+          const int u = valid[j] ? u0 + lane + 32 * j : u1 - 1;
+          F::dot(act[j], row, u, p.nb, part[j]);
+          part[j] = valid[j] ? part[j] : (Acc)0;
+        }
+        v[k] = part[0];
+#pragma unroll
+        for (int j = 1; j < UPT; j++) v[k] = acc_add(v[k], part[j]);
       }
-      a = warp_sum(a);
-      const int lrow = (int)(r0 - c0) + i * p.cr + rr;
-      if (lane == 0) {
+      const Acc tot = reduce_rows<RB>(v, lane);
+      constexpr int SPAN = 32 / RB;
+      const int k = lane / SPAN;
+      if (lane % SPAN == 0 && rr + k < nr) {
+        const int lrow = (int)(r0 - c0) + i * p.cr + rr + k;
         if (p.g == 1) {
-          const int64_t r = r0 + (int64_t)i * p.cr + rr;
-          float out = (float)a;
+          const int64_t r = r0 + (int64_t)i * p.cr + rr + k;
+          float out = (float)tot;
           if (p.y_add) out = __fadd_rn(p.y_add[r], out);
           p.y[r] = out;
         } else {
-          part[(size_t)lrow * p.g + wi] = a;
+          part_tab[(size_t)lrow * p.g + wi] = tot;
         }
       }
     }
@@ -388,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
   if (p.g > 1) {
     __syncthreads();
     for (int lr = threadIdx.x; lr < cta_rows; lr += kThreads) {
-      const Acc *pp = part + (size_t)lr * p.g;
+      const Acc *pp = part_tab + (size_t)lr * p.g;
       Acc a = pp[0];
       for (int w = 1; w < p.g; w++) a = acc_add(a, pp[w]);
       const int64_t r = c0 + lr;
@@ -407,7 +500,20 @@ __global__ void repack_kernel(int type, const uint8_t *raw, int64_t raw_row, uin
     uint8_t *d = dst + r * stride;
     for (int64_t i = threadIdx.x; i < raw_row; i += blockDim.x) {
       int64_t o = i;
-      if (type == T_Q6_K) {
+      if (type == T_Q4_K || type == T_Q5_K) {
+        const int bs = type == T_Q4_K ? 144 : 176;
+        const int e = (int)(i % bs);
+        if (e >= 4 && e < 16) {
+          // byte e of the 12-byte scale table: rebuilt from the whole table (quant.js:109-118)
+          const uint8_t *q = s + (i - e) + 4;
+          const int j = (e - 4) / 3, k = (e - 4) % 3;      // chunk j, byte k of its 24-bit field
+          auto scale = [&](int t) { return t < 4 ? q[t] & 63 : (q[t + 4] & 15) | ((q[t - 4] >> 6) << 4); };
+          auto minv = [&](int t) { return t < 4 ? q[t + 4] & 63 : (q[t + 4] >> 4) | ((q[t] >> 6) << 4); };
+          const uint32_t f = scale(2 * j) | (scale(2 * j + 1) << 6) | (minv(2 * j) << 12) | (minv(2 * j + 1) << 18);
+          d[i] = (uint8_t)(f >> (8 * k));
+          continue;
+        }
+      } else if (type == T_Q6_K) {
         const int b = (int)(i / 210), e = (int)(i % 210);
         o = e < 128 ? b * 128 + e : e < 192 ? 128LL * nb + b * 64 + (e - 128)
                                             : e < 208 ? 192LL * nb + b * 16 + (e - 192) : 208LL * nb + b * 2 + (e - 208);
@@ -488,7 +594,10 @@ bool plan_gemv(const DevMatrix &m, int num_sms, GemvPlan *p, const char **why) {
   if (U <= 0) { *why = "empty row"; return false; }
   p->units = U;
   // warps per row group: as few as possible while each lane holds at most 2 units (else 4)
+  // one unit per lane when the row splits evenly over whole warps (4-row batches fit in registers),
+  // else as few warps as keep each lane at <= 2 (then <= 4) units
   int g = 0;
+  for (int c = 1; c <= kWarps && !g; c *= 2) if ((U + c - 1) / c <= 32 && U >= 24 * c) g = c;
   for (int c = 1; c <= kWarps && !g; c *= 2) if ((U + c - 1) / c <= 64) g = c;
   for (int c = 1; c <= kWarps && !g; c *= 2) if ((U + c - 1) / c <= 128) g = c;
   if (!g) { *why = "row too long for the decode GEMV"; return false; }
@@ -499,6 +608,7 @@ bool plan_gemv(const DevMatrix &m, int num_sms, GemvPlan *p, const char **why) {
   const int ngroups = kWarps / g;
   int64_t grid = m.rows < num_sms ? m.rows : num_sms;
   if (grid < 1) grid = 1;
+  if ((m.rows + 1) * grid >= (1LL << 32)) { *why = "too many rows for the decode GEMV"; return false; }
   p->grid = (int)grid;
   const int64_t rows_cta = (m.rows + grid - 1) / grid;
   const int64_t rows_grp = (rows_cta + ngroups - 1) / ngroups;

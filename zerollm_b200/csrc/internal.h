@@ -43,7 +43,7 @@ struct GemvPlan {
 
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s);
 cudaError_t launch_quantize(const float *x, int64_t k, int ntok, int8_t *xq, float *xd, int32_t *xs, unsigned *status,
-                            cudaStream_t s);
+                            cudaStream_t s, bool pdl);
 // y[t*y_stride + r] = (y_add ? y_add[t*y_stride + r] : 0) + W[r] . act_t   for t < ntok
 cudaError_t launch_gemv(const DevMatrix &m, const ActView &a, int ntok, float *y, int64_t y_stride, const float *y_add,
                         unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why);

@@ -16,8 +16,10 @@ namespace zllm {
 // One warp per 32-value block, lane i owns value i.
 __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t nblocks, int8_t *__restrict__ xq,
                                     float *__restrict__ xd, int32_t *__restrict__ xs) {
-  pdl_wait();
+  // let the consumer GEMV launch now and start streaming its weights; it waits for this grid to
+  // finish before it reads xq / xd / xs
   pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < nblocks; b += warps) {
@@ -44,7 +46,7 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t nblocks
 }
 
 cudaError_t launch_quantize(const float *x, int64_t k, int ntok, int8_t *xq, float *xd, int32_t *xs, unsigned *status,
-                            cudaStream_t s) {
+                            cudaStream_t s, bool pdl) {
   (void)status;
   const int64_t nblocks = k / 32 * ntok;
   if (nblocks <= 0) return cudaSuccess;
@@ -59,7 +61,7 @@ cudaError_t launch_quantize(const float *x, int64_t k, int ntok, int8_t *xq, flo
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, quantize_act_kernel, x, nblocks, xq, xd, xs);
 }
 

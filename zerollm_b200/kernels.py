@@ -25,6 +25,16 @@ def _ptr(t):
     return None if t is None else C.c_void_p(t.data_ptr())
 
 
+# cudaStreamLegacy: the library reads a NULL stream as "the context's own stream", so torch's
+# default stream (handle 0) must be passed as the explicit legacy-stream handle.
+STREAM_LEGACY = 1
+
+
+def _stream(st) -> C.c_void_p:
+    st = int(st)
+    return C.c_void_p(st if st else STREAM_LEGACY)
+
+
 class Context:
     """One CUDA device, one stream, one status word (zllm_init)."""
 
@@ -120,7 +130,7 @@ class Act:
             self.s = torch.empty((self.ntok, self.k // 32), dtype=torch.int32, device=dev)
             st = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
             check(self.ctx.lib.zllm_quantize_act(self.ctx.h, _ptr(self.x), self.k, self.ntok, _ptr(self.q), _ptr(self.d),
-                                                 _ptr(self.s), C.c_void_p(st)), self.ctx.h, "zllm_quantize_act")
+                                                 _ptr(self.s), _stream(st)), self.ctx.h, "zllm_quantize_act")
         return self
 
 
@@ -137,7 +147,7 @@ def matvec(w: Weight, a: Act, y=None, y_add=None, stream=None):
         args = (_ptr(a.q), _ptr(a.d), _ptr(a.s), None)
     else:
         args = (None, None, None, _ptr(a.x))
-    check(w.ctx.lib.zllm_mm(w.ctx.h, w.h, *args, a.ntok, _ptr(y), y.stride(0), _ptr(y_add), C.c_void_p(st)),
+    check(w.ctx.lib.zllm_mm(w.ctx.h, w.h, *args, a.ntok, _ptr(y), y.stride(0), _ptr(y_add), _stream(st)),
           w.ctx.h, "zllm_mm")
     return y
 
