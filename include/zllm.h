@@ -95,6 +95,55 @@ int zllm_mm(zllm_ctx *ctx, const zllm_weight *w, const int8_t *xq, const float *
  * blocking.  The CUDA counterpart of `matvec(w, new Act(x), y)` (src/compute/ref-kernels.js:127). */
 int zllm_matvec(zllm_ctx *ctx, const zllm_weight *w, const float *x_host, int ntok, float *y_host);
 
+/* ------------------------------------------------------------------------------------ attention
+ * Geometry of one attention layer's KV cache.  A sequence's cache holds, per layer, K then V, each
+ * [n_head_kv][ctx][head_dim] (head-major, so one head's positions are contiguous); elements are f16
+ * (kv_f16 = 1, the reference's --kv f16) or f32.  seq_stride / head_stride are in elements between
+ * consecutive sequences / KV heads of the same K (or V) block. */
+typedef struct {
+  int n_head, n_head_kv, head_dim, n_rot;
+  int neox;          /* 1: rotate pairs (i, i + n_rot/2) (qwen2/qwen3); 0: (2i, 2i+1) (llama) */
+  int kv_f16;
+  int ctx;           /* positions per sequence */
+  double rms_eps;    /* as read from GGUF metadata (an f32 value) */
+  int64_t seq_stride, head_stride;
+} zllm_attn_geom;
+
+/* RoPE tables cos/sin [ctx_len][n_rot/2] computed on the host in double (Math.cos / Math.sin of
+ * p * base^(-2i/n_rot) / freq_factors[i]) and copied to device memory.  src/compute/ref-kernels.js:329-342.
+ * freq_factors_host may be NULL. */
+int zllm_rope_tables(zllm_ctx *ctx, int n_rot, double base, int ctx_len, const float *freq_factors_host,
+                     float *cos_dev, float *sin_dev);
+
+/* For ntok tokens: optional biases, per-head q-norm / k-norm, RoPE at pos[t], then the append of k and
+ * v at position pos[t] of sequence seq[t] (f32 -> f16 round-to-nearest-even when kv_f16); q_out gets the
+ * roped queries [ntok][n_head*head_dim].  Replaces src/compute/worker.js:290-309 and :313-315 (the
+ * append and the q preparation of the attention phase) and src/model/forward.js:113-121. */
+int zllm_qkv_append(zllm_ctx *ctx, const zllm_attn_geom *g, int ntok, const float *q, int64_t q_stride, const float *k,
+                    const float *v, int64_t kv_stride, const float *bq, const float *bk, const float *bv,
+                    const float *q_norm, const float *k_norm, const float *rope_cos, const float *rope_sin,
+                    const int32_t *pos, const int32_t *seq, float *q_out, void *kcache, void *vcache, void *stream);
+
+/* out[s][h][:] = softmax(q[s][h] . K[s][h/group][0..npos[s]) / sqrt(head_dim)) . V[...] for nseq
+ * sequences (npos device array, every value <= max_pos <= ctx).  Context-split ("flash decoding")
+ * with the merge done by the last CTA; scratch comes from the context.  Replaces the attention loop
+ * of src/compute/worker.js:310-337 (WASM attn_scores / attn_av, src/compute/wasm/attn-kernels.js:26-194)
+ * and src/model/forward.js:123-140. */
+int zllm_attn_decode(zllm_ctx *ctx, const zllm_attn_geom *g, const float *q, const void *kcache, const void *vcache,
+                     const int32_t *npos, int nseq, int max_pos, float *out, void *stream);
+
+/* kvSet: n positions of one layer's K or V block of one sequence from f32 [n][n_head_kv*head_dim]
+ * (device) -- cast to f16 when kv_f16.  kvGet: the reverse (f16 -> f32 exact).
+ * src/compute/worker.js:457-472, src/compute/pool.js:225-238. */
+int zllm_kv_import(zllm_ctx *ctx, const zllm_attn_geom *g, void *cache_block, int n, const float *stage, void *stream);
+int zllm_kv_export(zllm_ctx *ctx, const zllm_attn_geom *g, const void *cache_block, int n, float *stage, void *stream);
+
+/* Byte copy of positions [0, n) of every KV head between two K (or V) blocks with the given head
+ * strides (elements): a prefix-cache slot restore or save (src/model/prefix-cache.js:50-96 restores
+ * through kvSet; a device-resident slot makes it a copy).  Bit-exact by construction. */
+int zllm_kv_copy(zllm_ctx *ctx, const zllm_attn_geom *g, void *dst_block, int64_t dst_head_stride,
+                 const void *src_block, int64_t src_head_stride, int n, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

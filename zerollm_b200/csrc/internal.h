@@ -41,6 +41,42 @@ struct GemvPlan {
   int units, g, uw, upt, cr, nsg, stage_bytes, grid, smem_bytes, max_rows;
 };
 
+// q/k/v post-processing of `ntok` tokens (biases, q/k RMSNorm, RoPE) and the K/V append.
+struct QkvPostArgs {
+  const float *q, *k, *v;          // [ntok][q_stride] / [ntok][kv_stride] f32 projections
+  int64_t q_stride, kv_stride;
+  const float *bq, *bk, *bv;       // optional biases
+  const float *q_norm, *k_norm;    // optional per-head RMSNorm weights [head_dim]
+  const float *rope_cos, *rope_sin;  // [ctx][n_rot/2]
+  const int *pos, *seq;            // per token: position and sequence index
+  float *q_out;                    // [ntok][q_out_stride] roped queries
+  int64_t q_out_stride;
+  void *kcache, *vcache;           // caches, element f16 or f32
+  int64_t seq_stride, head_stride; // elements between sequences / KV heads (positions are head_dim apart)
+  int n_head, n_kv, head_dim, n_rot, neox, kv_f16, ntok;
+  double eps;
+};
+
+struct AttnArgs {
+  const float *q;                  // [nseq][n_head][head_dim]
+  const void *kcache, *vcache;
+  int64_t seq_stride, head_stride;
+  const int *npos;                 // positions to attend per sequence (device)
+  float *out;                      // [nseq][n_head][head_dim]
+  float *partial;                  // [nseq * n_kv][nsplit][group * (head_dim + 2)] scratch
+  int *counters;                   // [nseq * n_kv], zero between launches
+  unsigned *status;
+  float scale;
+  int n_head, n_kv, head_dim, nseq, nsplit;
+};
+
+cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t s, bool pdl);
+bool attn_supported(int head_dim, int group);
+size_t attn_smem_bytes(int head_dim, int group, bool f16);
+cudaError_t launch_attn(const AttnArgs &a, bool f16, cudaStream_t s, bool pdl);
+cudaError_t launch_kv_convert(float *stage, void *cache, int n, int n_kv, int hd, int64_t head_stride, bool f16, int dir,
+                              cudaStream_t s);
+
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s);
 cudaError_t launch_quantize(const float *x, int64_t k, int ntok, int8_t *xq, float *xd, int32_t *xs, unsigned *status,
                             cudaStream_t s, bool pdl);

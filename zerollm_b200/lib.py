@@ -41,7 +41,20 @@ SIGNATURES = {
     "zllm_quantize_act": (i32, [vp, vp, i64, i32, vp, vp, vp, vp]),
     "zllm_mm": (i32, [vp, vp, vp, vp, vp, vp, i32, vp, i64, vp, vp]),
     "zllm_matvec": (i32, [vp, vp, vp, i32, vp]),
+    "zllm_rope_tables": (i32, [vp, i32, C.c_double, i32, vp, vp, vp]),
+    "zllm_qkv_append": (i32, [vp, vp, i32, vp, i64, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "zllm_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, vp, vp]),
+    "zllm_kv_import": (i32, [vp, vp, vp, i32, vp, vp]),
+    "zllm_kv_export": (i32, [vp, vp, vp, i32, vp, vp]),
+    "zllm_kv_copy": (i32, [vp, vp, vp, i64, vp, i64, i32, vp]),
 }
+
+
+class AttnGeom(C.Structure):
+    """zllm_attn_geom (include/zllm.h)"""
+    _fields_ = [("n_head", C.c_int), ("n_head_kv", C.c_int), ("head_dim", C.c_int), ("n_rot", C.c_int),
+                ("neox", C.c_int), ("kv_f16", C.c_int), ("ctx", C.c_int), ("rms_eps", C.c_double),
+                ("seq_stride", C.c_int64), ("head_stride", C.c_int64)]
 
 _lib = None
 
