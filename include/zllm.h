@@ -144,6 +144,76 @@ int zllm_kv_export(zllm_ctx *ctx, const zllm_attn_geom *g, const void *cache_blo
 int zllm_kv_copy(zllm_ctx *ctx, const zllm_attn_geom *g, void *dst_block, int64_t dst_head_stride,
                  const void *src_block, int64_t src_head_stride, int n, void *stream);
 
+/* ------------------------------------------------------------------------------------ model
+ * A whole llama / qwen2 / qwen3 model on one GPU: the CUDA counterpart of the worker pool's model
+ * interface (PoolModel, src/compute/pool.js:24-317; RefModel, src/model/forward.js:10-168).  It holds
+ * n_seq independent sequences (1 = the reference's single-sequence model), each with its own KV
+ * cache of ctx positions. */
+typedef struct zllm_model zllm_model;
+
+typedef struct {
+  int n_embd, n_layer, n_ff, n_head, n_head_kv, head_dim, n_rot, vocab;   /* src/model/config.js:73-123 */
+  int neox;          /* RoPE pairing: 1 split-half (qwen2/qwen3), 0 adjacent (llama) */
+  int kv_f16;        /* --kv f16 (1) or f32 (0) */
+  int ctx;           /* positions per sequence */
+  int n_seq;         /* independent sequences */
+  int max_batch;     /* most tokens one call carries (the pool's maxBatch, <= 64; pool.js:63) */
+  int logits_batch;  /* most positions one call returns logits for with want = 2 (pool.js:65) */
+  double rms_eps, rope_base;
+} zllm_model_config;
+
+/* tensor kinds for zllm_model_set_matrix / zllm_model_set_vector (GGUF tensor names) */
+enum {
+  ZLLM_T_TOK_EMBD = 0,    /* token_embd.weight   [vocab][n_embd] */
+  ZLLM_T_OUTPUT = 1,      /* output.weight       [vocab][n_embd] (absent: tied to token_embd) */
+  ZLLM_T_OUTPUT_NORM = 2, /* output_norm.weight  [n_embd] */
+  ZLLM_T_ROPE_FREQS = 3,  /* rope_freqs.weight   [n_rot/2] */
+  ZLLM_T_ATTN_NORM = 10,  /* blk.L.attn_norm.weight */
+  ZLLM_T_WQ = 11, ZLLM_T_WK = 12, ZLLM_T_WV = 13, ZLLM_T_WO = 14,  /* blk.L.attn_{q,k,v,output}.weight */
+  ZLLM_T_BQ = 15, ZLLM_T_BK = 16, ZLLM_T_BV = 17,                  /* blk.L.attn_{q,k,v}.bias (qwen2) */
+  ZLLM_T_Q_NORM = 18, ZLLM_T_K_NORM = 19,                          /* blk.L.attn_{q,k}_norm.weight (qwen3) */
+  ZLLM_T_FFN_NORM = 20,
+  ZLLM_T_GATE = 21, ZLLM_T_UP = 22, ZLLM_T_DOWN = 23               /* blk.L.ffn_{gate,up,down}.weight */
+};
+
+int zllm_model_create(zllm_ctx *ctx, const zllm_model_config *cfg, zllm_model **out);
+/* Raw GGUF bytes of one matrix (the worker's weight plan, src/compute/worker.js:49-97). */
+int zllm_model_set_matrix(zllm_model *m, int kind, int layer, int ggml_type, int64_t rows, int64_t cols,
+                          const void *host_bytes, size_t nbytes);
+/* An f32 vector (norm weights, biases, RoPE frequency factors). */
+int zllm_model_set_vector(zllm_model *m, int kind, int layer, const float *host, int64_t n);
+/* Allocate the KV caches and activations once every tensor is set (called by the first pass). */
+int zllm_model_ready(zllm_model *m);
+/* n tokens of sequence `seq` at its next positions in one pass (forwardBatch, pool.js:145-160;
+ * forward = n 1).  want: 0 no logits, 1 the last token's, 2 every token's ([n][vocab], n <=
+ * logits_batch).  logits_host / argmax_host may be NULL.  Errors as the pool: ZLLM_E_CTX_FULL
+ * "context full (N tokens)", ZLLM_E_TOKEN "token id X out of range", ZLLM_E_BATCH "batch of B tokens
+ * (max M)"; a device failure latches and every later call returns ZLLM_E_STATE (pool.js:123-127). */
+int zllm_model_forward(zllm_model *m, int seq, const int32_t *tokens, int n, int want, float *logits_host,
+                       int32_t *argmax_host);
+/* One token for each of n distinct sequences (batched decode); logits [n][vocab]. */
+int zllm_model_decode(zllm_model *m, const int32_t *seqs, const int32_t *tokens, int n, float *logits_host,
+                      int32_t *argmax_host);
+/* Positions held by a sequence (PoolModel.pos). */
+int zllm_model_pos(const zllm_model *m, int seq);
+/* Roll back to n positions (truncate, pool.js:278-294: positional bookkeeping) / forget all. */
+int zllm_model_truncate(zllm_model *m, int seq, int n);
+int zllm_model_reset(zllm_model *m, int seq);
+/* kvGet / kvSet on host buffers f32 [n][n_head_kv*head_dim] (pool.js:225-238). */
+int zllm_model_kv_get(zllm_model *m, int seq, int layer, int is_v, int n, float *out);
+int zllm_model_kv_set(zllm_model *m, int seq, int layer, int is_v, int n, const float *in);
+/* After the KV regions were filled (kvSet): the sequence now holds n positions (restorePrefix, pool.js:244-247). */
+int zllm_model_restore_prefix(zllm_model *m, int seq, int n);
+/* Device-resident prefix slot: save the first n positions of a sequence's KV, restore them (a byte
+ * copy) into a sequence, which then holds those n positions. */
+int zllm_model_slot_save(zllm_model *m, int seq, int n);
+int zllm_model_slot_restore(zllm_model *m, int seq);
+/* Record passes into CUDA graphs (default on). */
+int zllm_model_set_graphs(zllm_model *m, int on);
+/* Device pointer of the logits of the last pass ([rows][vocab] f32). */
+void *zllm_model_logits(zllm_model *m);
+void zllm_model_destroy(zllm_model *m);
+
 #ifdef __cplusplus
 }
 #endif

@@ -6,6 +6,7 @@
 
 #include <set>
 
+#include "../../include/zllm.h"
 #include "internal.h"
 
 constexpr int kScratchSlots = 16;
@@ -32,3 +33,7 @@ void zllm_set_error(zllm_ctx *c, const char *fmt, ...);
 int zllm_cuda_fail(zllm_ctx *c, cudaError_t e, const char *what);
 int zllm_scratch(zllm_ctx *c, int slot, size_t bytes, void **out);
 int zllm_check_status(zllm_ctx *c);
+int zllm_attn_splits(const zllm_ctx *c, const zllm_attn_geom *g, int nseq, int max_pos);
+int zllm_attn_launch(zllm_ctx *c, const zllm_attn_geom *g, const float *q, const void *kcache, const void *vcache,
+                     const int32_t *npos, int nseq, int nsplit, float *out, float *partial, int32_t *counters,
+                     cudaStream_t s, const int32_t *seq);

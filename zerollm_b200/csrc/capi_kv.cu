@@ -80,8 +80,9 @@ int zllm_attn_splits(const zllm_ctx *c, const zllm_attn_geom *g, int nseq, int m
 
 int zllm_attn_launch(zllm_ctx *c, const zllm_attn_geom *g, const float *q, const void *kcache, const void *vcache,
                      const int32_t *npos, int nseq, int nsplit, float *out, float *partial, int32_t *counters,
-                     cudaStream_t s) {
+                     cudaStream_t s, const int32_t *seq) {
   AttnArgs a{};
+  a.seq = seq;
   a.q = q; a.kcache = kcache; a.vcache = vcache; a.seq_stride = g->seq_stride; a.head_stride = g->head_stride;
   a.npos = npos; a.out = out; a.partial = partial; a.counters = counters; a.status = c->status_dev;
   a.scale = (float)(1.0 / std::sqrt((double)g->head_dim));
@@ -120,7 +121,7 @@ extern "C" int zllm_attn_decode(zllm_ctx *c, const zllm_attn_geom *g, const floa
   }
   cnt = c->scratch[9];
   return zllm_attn_launch(c, g, q, kcache, vcache, npos, nseq, nsplit, out, (float *)part, (int32_t *)cnt,
-                          pick_stream(c, stream));
+                          pick_stream(c, stream), nullptr);
 }
 
 extern "C" int zllm_kv_import(zllm_ctx *c, const zllm_attn_geom *g, void *block, int n, const float *stage, void *stream) {

@@ -341,12 +341,14 @@ struct GemvArgs {
   int cr;            // rows per chunk (one bulk copy)
   int nsg;           // stages per row group
   int stage_bytes;
-  int max_rows;      // rows per CTA upper bound (sizes the partial-sum table)
+  int ntok;          // activations processed against each staged chunk (weights read once for all)
+  int64_t y_stride;  // floats between consecutive tokens' outputs (and y_add rows)
 };
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxStagesPerGroup = 16;
+constexpr int kMaxTok = 64;                  // tokens per launch (the reference's MAX_BATCH, src/compute/layout.js:23)
 
 template <class F, int UPT, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) {
@@ -360,9 +362,10 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
 
   uint8_t *stages = smem + (size_t)gi * p.nsg * p.stage_bytes;
   const size_t stage_area = (size_t)kWarps / p.g * p.nsg * p.stage_bytes;
-  Acc *part_tab = reinterpret_cast<Acc *>(smem + stage_area);
-  // the same layout plan_gemv sized: the partial table exists only for multi-warp row groups
-  const size_t part_bytes = p.g > 1 ? ((size_t)p.max_rows * p.g * sizeof(Acc) + 15) / 16 * 16 : 0;
+  // partial sums of multi-warp row groups: [group][stage][token][chunk row][warp of group]
+  const size_t part_per_group = (size_t)p.nsg * p.ntok * p.cr * p.g;
+  Acc *part_tab = reinterpret_cast<Acc *>(smem + stage_area) + (size_t)gi * part_per_group;
+  const size_t part_bytes = p.g > 1 ? ((size_t)ngroups * part_per_group * sizeof(Acc) + 15) / 16 * 16 : 0;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + stage_area + part_bytes);
   uint64_t *full = bars + (size_t)gi * 2 * p.nsg;
   uint64_t *empty = full + p.nsg;
@@ -414,49 +417,75 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
     if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
     const uint32_t st = stages_s + (uint32_t)(s * p.stage_bytes);
     const int nr = min(p.cr, nrows - i * p.cr);
-    // RB rows at a time, one accumulator per (row, unit): independent dependency chains for the
-    // scheduler; then one butterfly reduction across the warp leaves row k's total in lane k*32/RB
-    for (int rr = 0; rr < nr; rr += RB) {
-      Acc v[RB];
+    for (int t = 0; t < p.ntok; t++) {
+      if (p.ntok > 1) {
+        // the staged rows are reused for every token: reload this token's activation slice
+        ActView at = p.act;
+        if (at.xq) at.xq += (int64_t)t * at.k;
+        if (at.xd) at.xd += (int64_t)t * (at.k / 32);
+        if (at.xs) at.xs += (int64_t)t * (at.k / 32);
+        if (at.x) at.x += (int64_t)t * at.k;
 #pragma unroll
-      for (int k = 0; k < RB; k++) {
-        const int rk = min(rr + k, nr - 1);            // the tail repeats the last row (result unused)
-        const uint32_t row = st + (uint32_t)(rk * p.row_stride);
-        Acc part[UPT];
-#pragma unroll
-        for (int j = 0; j < UPT; j++) {
-          part[j] = 0;
-          const int u = valid[j] ? u0 + lane + 32 * j : u1 - 1;
-          F::dot(act[j], row, u, p.nb, part[j]);
-          part[j] = valid[j] ? part[j] : (Acc)0;
-        }
-        v[k] = part[0];
-#pragma unroll
-        for (int j = 1; j < UPT; j++) v[k] = acc_add(v[k], part[j]);
+        for (int j = 0; j < UPT; j++) F::load(act[j], at, valid[j] ? u0 + lane + 32 * j : u1 - 1);
       }
-      const Acc tot = reduce_rows<RB>(v, lane);
-      constexpr int SPAN = 32 / RB;
-      const int k = lane / SPAN;
-      if (lane % SPAN == 0 && rr + k < nr) {
-        const int lrow = (int)(r0 - c0) + i * p.cr + rr + k;
-        if (p.g == 1) {
-          const int64_t r = r0 + (int64_t)i * p.cr + rr + k;
-          float out = (float)tot;
-          if (p.y_add) out = __fadd_rn(p.y_add[r], out);
-          p.y[r] = out;
-        } else {
-          part_tab[(size_t)lrow * p.g + wi] = tot;
+      // RB rows at a time, one accumulator per (row, unit): independent dependency chains for the
+      // scheduler; then one butterfly reduction across the warp leaves row k's total in lane k*32/RB
+      for (int rr = 0; rr < nr; rr += RB) {
+        Acc v[RB];
+#pragma unroll
+        for (int k = 0; k < RB; k++) {
+          const int rk = min(rr + k, nr - 1);            // the tail repeats the last row (result unused)
+          const uint32_t row = st + (uint32_t)(rk * p.row_stride);
+          Acc part[UPT];
+#pragma unroll
+          for (int j = 0; j < UPT; j++) {
+            part[j] = 0;
+            const int u = valid[j] ? u0 + lane + 32 * j : u1 - 1;
+            F::dot(act[j], row, u, p.nb, part[j]);
+            part[j] = valid[j] ? part[j] : (Acc)0;
+          }
+          v[k] = part[0];
+#pragma unroll
+          for (int j = 1; j < UPT; j++) v[k] = acc_add(v[k], part[j]);
+        }
+        const Acc tot = reduce_rows<RB>(v, lane);
+        constexpr int SPAN = 32 / RB;
+        const int k = lane / SPAN;
+        if (lane % SPAN == 0 && rr + k < nr) {
+          if (p.g == 1) {
+            const int64_t r = r0 + (int64_t)i * p.cr + rr + k;
+            float out = (float)tot;
+            if (p.y_add) out = __fadd_rn(p.y_add[t * p.y_stride + r], out);
+            p.y[t * p.y_stride + r] = out;
+          } else {
+            part_tab[(((size_t)s * p.ntok + t) * p.cr + rr + k) * p.g + wi] = tot;
+          }
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    // refill stage s with chunk i + nsg once every warp of the group has released it
-    if (wi == 0 && issued < nchunks) {
+    // the group's first warp waits until every warp of the group released the stage, then adds the
+    // group's partial sums of this chunk in warp order and refills the stage with chunk i + nsg
+    if (wi == 0 && (p.g > 1 || issued < nchunks)) {
       bool fine = true;
-      if (lane == 0) {
-        fine = mbar_wait_bounded(&empty[s], (i / p.nsg) & 1, deadline);
-        if (fine) {
+      if (lane == 0) fine = mbar_wait_bounded(&empty[s], (i / p.nsg) & 1, deadline);
+      if (!__shfl_sync(0xffffffffu, fine, 0)) { aborted = true; break; }
+      if (p.g > 1) {
+        for (int e = lane; e < p.ntok * nr; e += 32) {
+          const int t = e / nr, rr = e % nr;
+          const Acc *pp = part_tab + (((size_t)s * p.ntok + t) * p.cr + rr) * p.g;
+          Acc acc = pp[0];
+          for (int w = 1; w < p.g; w++) acc = acc_add(acc, pp[w]);
+          const int64_t r = r0 + (int64_t)i * p.cr + rr;
+          float out = (float)acc;
+          if (p.y_add) out = __fadd_rn(p.y_add[t * p.y_stride + r], out);
+          p.y[t * p.y_stride + r] = out;
+        }
+        __syncwarp();
+      }
+      if (issued < nchunks) {
+        if (lane == 0) {
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           const int nr2 = min(p.cr, nrows - issued * p.cr);
           const uint32_t bytes = (uint32_t)(nr2 * p.row_stride);
@@ -464,9 +493,8 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
           bulk_g2s(stages + (size_t)s * p.stage_bytes, p.w + (r0 + (int64_t)issued * p.cr) * p.row_stride, bytes,
                    &full[s]);
         }
+        issued++;
       }
-      if (!__shfl_sync(0xffffffffu, fine, 0)) { aborted = true; break; }
-      issued++;
     }
   }
   if (aborted && lane == 0) atomicOr(p.status, ST_FULL_TIMEOUT);
@@ -476,18 +504,6 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
     for (int s = 0; s < p.nsg && s < issued; s++) {
       const int last = s + ((issued - 1 - s) / p.nsg) * p.nsg;
       if (!mbar_wait_bounded(&full[s], (last / p.nsg) & 1, drain_deadline)) atomicOr(p.status, ST_DRAIN_TIMEOUT);
-    }
-  }
-  if (p.g > 1) {
-    __syncthreads();
-    for (int lr = threadIdx.x; lr < cta_rows; lr += kThreads) {
-      const Acc *pp = part_tab + (size_t)lr * p.g;
-      Acc a = pp[0];
-      for (int w = 1; w < p.g; w++) a = acc_add(a, pp[w]);
-      const int64_t r = c0 + lr;
-      float out = (float)a;
-      if (p.y_add) out = __fadd_rn(p.y_add[r], out);
-      p.y[r] = out;
     }
   }
 }
@@ -628,9 +644,14 @@ bool plan_gemv(const DevMatrix &m, int num_sms, GemvPlan *p, const char **why) {
   if (nsg < 1) nsg = 1;
   p->nsg = (int)nsg;
   p->max_rows = (int)rows_cta + 1;
-  const size_t part = g > 1 ? ((size_t)p->max_rows * g * acc_bytes(m.type) + 15) / 16 * 16 : 0;
-  p->smem_bytes = (int)((size_t)ngroups * nsg * stage + part + (size_t)ngroups * 2 * nsg * 8);
   return true;
+}
+
+// shared memory of one launch over `ntok` tokens
+static size_t gemv_smem(const DevMatrix &m, const GemvPlan &pl, int ntok) {
+  const int ngroups = kWarps / pl.g;
+  const size_t part = pl.g > 1 ? ((size_t)ngroups * pl.nsg * ntok * pl.cr * pl.g * acc_bytes(m.type) + 15) / 16 * 16 : 0;
+  return (size_t)ngroups * pl.nsg * pl.stage_bytes + part + (size_t)ngroups * 2 * pl.nsg * 8;
 }
 
 template <class F, int UPT>
@@ -676,22 +697,26 @@ cudaError_t launch_gemv(const DevMatrix &m, const ActView &act, int ntok, float 
   GemvPlan pl;
   if (!plan_gemv(m, num_sms, &pl, why)) return cudaErrorInvalidValue;
   const int64_t nbk = (m.type == T_Q4_K || m.type == T_Q5_K || m.type == T_Q6_K) ? m.cols / 256 : m.cols / 32;
-  for (int t = 0; t < ntok; t++) {
+  // up to kMaxTok tokens share one pass over the weights
+  for (int t0 = 0; t0 < ntok; t0 += kMaxTok) {
+    const int nt = ntok - t0 < kMaxTok ? ntok - t0 : kMaxTok;
+    pl.smem_bytes = (int)gemv_smem(m, pl, nt);
     GemvArgs a;
     a.w = m.data;
     a.row_stride = m.row_stride;
     a.rows = m.rows;
     a.nb = (int)nbk;
     a.act.k = act.k;
-    a.act.xq = act.xq ? act.xq + (int64_t)t * act.k : nullptr;
-    a.act.xd = act.xd ? act.xd + (int64_t)t * (act.k / 32) : nullptr;
-    a.act.xs = act.xs ? act.xs + (int64_t)t * (act.k / 32) : nullptr;
-    a.act.x = act.x ? act.x + (int64_t)t * act.k : nullptr;
-    a.y = y + (int64_t)t * y_stride;
-    a.y_add = y_add ? y_add + (int64_t)t * y_stride : nullptr;
+    a.act.xq = act.xq ? act.xq + (int64_t)t0 * act.k : nullptr;
+    a.act.xd = act.xd ? act.xd + (int64_t)t0 * (act.k / 32) : nullptr;
+    a.act.xs = act.xs ? act.xs + (int64_t)t0 * (act.k / 32) : nullptr;
+    a.act.x = act.x ? act.x + (int64_t)t0 * act.k : nullptr;
+    a.y = y + (int64_t)t0 * y_stride;
+    a.y_add = y_add ? y_add + (int64_t)t0 * y_stride : nullptr;
+    a.ntok = nt;
+    a.y_stride = y_stride;
     a.status = status;
     a.units = pl.units; a.g = pl.g; a.uw = pl.uw; a.cr = pl.cr; a.nsg = pl.nsg; a.stage_bytes = pl.stage_bytes;
-    a.max_rows = pl.max_rows;
     cudaError_t e;
     switch (m.type) {
       case T_Q4_K: e = launch_fmt<FmtK45<false>>(a, pl, s, pdl); break;

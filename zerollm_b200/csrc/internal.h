@@ -59,6 +59,7 @@ struct QkvPostArgs {
 
 struct AttnArgs {
   const float *q;                  // [nseq][n_head][head_dim]
+  const int *seq;                  // cache sequence of query b (NULL: b)
   const void *kcache, *vcache;
   int64_t seq_stride, head_stride;
   const int *npos;                 // positions to attend per sequence (device)
@@ -76,6 +77,13 @@ size_t attn_smem_bytes(int head_dim, int group, bool f16);
 cudaError_t launch_attn(const AttnArgs &a, bool f16, cudaStream_t s, bool pdl);
 cudaError_t launch_kv_convert(float *stage, void *cache, int n, int n_kv, int hd, int64_t head_stride, bool f16, int dir,
                               cudaStream_t s);
+
+cudaError_t launch_rmsnorm_quant(const float *x, const float *w, int n, int ntok, double eps, float *xb, int8_t *xq, float *xd,
+                                 int32_t *xs, cudaStream_t s, bool pdl);
+cudaError_t launch_swiglu_quant(const float *gate, const float *up, int n, int ntok, int64_t stride, float *hb, int8_t *xq,
+                                float *xd, int32_t *xs, cudaStream_t s, bool pdl);
+cudaError_t launch_embed(const DevMatrix &m, const int32_t *tokens, int ntok, float *x, cudaStream_t s, bool pdl);
+cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, cudaStream_t s, bool pdl);
 
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s);
 cudaError_t launch_quantize(const float *x, int64_t k, int ntok, int8_t *xq, float *xd, int32_t *xs, unsigned *status,

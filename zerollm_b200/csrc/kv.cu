@@ -194,10 +194,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const A
   const int per = ((npos + a.nsplit - 1) / a.nsplit + kAttnTP - 1) / kAttnTP * kAttnTP;
   const int t0 = min(npos, split * per), t1 = min(npos, t0 + per);
   const int ntiles = (t1 - t0 + kAttnTP - 1) / kAttnTP;
+  const int64_t cs = a.seq ? a.seq[b] : b;            // cache sequence of this query
   const uint8_t *kbase = reinterpret_cast<const uint8_t *>(a.kcache) +
-                         ((int64_t)b * a.seq_stride + (int64_t)kh * a.head_stride + (int64_t)t0 * HD) * sizeof(T);
+                         (cs * a.seq_stride + (int64_t)kh * a.head_stride + (int64_t)t0 * HD) * sizeof(T);
   const uint8_t *vbase = reinterpret_cast<const uint8_t *>(a.vcache) +
-                         ((int64_t)b * a.seq_stride + (int64_t)kh * a.head_stride + (int64_t)t0 * HD) * sizeof(T);
+                         (cs * a.seq_stride + (int64_t)kh * a.head_stride + (int64_t)t0 * HD) * sizeof(T);
 
   // q of the group's heads: lane holds dims [dc*DPL, +DPL) for the score phase
   const int p_in = lane / C::LP, dc = lane % C::LP;

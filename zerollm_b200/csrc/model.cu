@@ -1,0 +1,524 @@
+// Model runtime: the whole forward pass of a llama / qwen2 / qwen3 model on one GPU, built from the
+// kernels of gemv.cu, quant.cu, kv.cu and ops.cu, behind the extern "C" model entry points of
+// include/zllm.h.
+//
+// One pass runs n tokens, each token t belonging to sequence seq[t] at position pos[t]: either B
+// consecutive tokens of one sequence (the reference's forwardBatch, src/compute/pool.js:145-160 /
+// the worker's runBatch, src/compute/worker.js:410-445) or one token of each of n independent
+// sequences (batched serving).  The phase order is the reference worker's: embedding; per layer
+// RMSNorm -> q,k,v -> norms/RoPE/KV append -> attention -> wo + residual -> RMSNorm -> gate, up ->
+// SwiGLU -> down + residual; output RMSNorm -> output head (src/compute/worker.js:278-348, :410-445;
+// src/model/forward.js:94-158).  Every matmul input is quantized per 32 values exactly like the
+// reference's quantizeAct, fused into the kernel that produces it.
+//
+// Steady-state decode passes of the same shape are recorded once into a CUDA graph and replayed
+// (kernels chained with programmatic dependent launch inside the graph).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/zllm.h"
+#include "capi_internal.h"
+#include "internal.h"
+
+using namespace zllm;
+
+namespace {
+
+struct Layer {
+  zllm_weight *w[7] = {};                 // wq wk wv wo gate up down
+  float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+};
+
+enum { WQ = 0, WK, WV, WO, GATE, UP, DOWN };
+
+template <typename T>
+cudaError_t dalloc(T **p, size_t n) { return cudaMalloc((void **)p, (n ? n : 1) * sizeof(T)); }
+
+}  // namespace
+
+struct zllm_model {
+  zllm_ctx *ctx = nullptr;
+  zllm_model_config c{};
+  cudaStream_t stream = nullptr;
+  std::vector<Layer> L;
+  zllm_weight *tok = nullptr, *out = nullptr;           // out == nullptr: tied to tok
+  float *out_norm = nullptr, *rope_freqs_host_dev = nullptr;
+  std::vector<float> rope_freqs_host;
+  bool ready = false, failed = false, closed = false;
+  // device state
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  void *kv = nullptr;                                    // [seq][layer][2][n_kv][ctx][hd]
+  size_t kv_bytes = 0;
+  void *slot = nullptr;                                  // prefix slot: [layer][2][n_kv][slot_n][hd]
+  int slot_cap = 0, slot_n = 0;
+  float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *att = nullptr;
+  float *g = nullptr, *u = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
+  int8_t *xq = nullptr;
+  float *xd = nullptr;
+  int32_t *xs = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_npos = nullptr, *d_arg = nullptr;
+  int32_t *counters = nullptr, *h_io = nullptr;          // h_io: pinned [4][max_batch] staging of the int arrays
+  int nsplit = 1;
+  std::vector<int> pos;                                   // positions held per sequence
+  // decode graph cache: one graph per token count
+  struct Graph { int n = 0; int want = 0; cudaGraphExec_t exec = nullptr; };
+  std::vector<Graph> graphs;
+  std::vector<std::pair<int, int>> eager_seen;           // shapes run once eagerly before being recorded
+  bool use_graphs = true;
+
+  int64_t qdim() const { return (int64_t)c.n_head * c.head_dim; }
+  int64_t kvdim() const { return (int64_t)c.n_head_kv * c.head_dim; }
+  int64_t seq_elems() const { return (int64_t)c.n_layer * 2 * kvdim() * c.ctx; }
+  size_t el() const { return c.kv_f16 ? 2 : 4; }
+  zllm_attn_geom geom() const {
+    zllm_attn_geom g{};
+    g.n_head = c.n_head; g.n_head_kv = c.n_head_kv; g.head_dim = c.head_dim; g.n_rot = c.n_rot; g.neox = c.neox;
+    g.kv_f16 = c.kv_f16; g.ctx = c.ctx; g.rms_eps = c.rms_eps;
+    g.seq_stride = seq_elems(); g.head_stride = (int64_t)c.ctx * c.head_dim;
+    return g;
+  }
+  uint8_t *kv_block(int seq, int layer, int is_v) const {
+    return (uint8_t *)kv + ((int64_t)seq * seq_elems() + ((int64_t)layer * 2 + is_v) * kvdim() * c.ctx) * el();
+  }
+};
+
+static int fail(zllm_model *m, int rc) {
+  if (rc == ZLLM_E_CUDA || rc == ZLLM_E_TIMEOUT || rc == ZLLM_E_OOM) m->failed = true;   // latched like pool.js:123-127
+  return rc;
+}
+
+#define CK(expr, what)                                                   \
+  do {                                                                   \
+    cudaError_t e_ = (expr);                                             \
+    if (e_ != cudaSuccess) return fail(m, zllm_cuda_fail(m->ctx, e_, what)); \
+  } while (0)
+
+extern "C" int zllm_model_create(zllm_ctx *ctx, const zllm_model_config *cfg, zllm_model **out) {
+  if (!ctx || !cfg || !out) return ZLLM_E_ARG;
+  *out = nullptr;
+  const zllm_model_config &c = *cfg;
+  if (c.n_embd <= 0 || c.n_layer <= 0 || c.n_ff <= 0 || c.n_head <= 0 || c.n_head_kv <= 0 || c.n_head % c.n_head_kv ||
+      c.head_dim <= 0 || c.vocab <= 0 || c.ctx <= 0 || c.n_seq <= 0 || c.max_batch <= 0 || c.max_batch > 64 ||
+      c.n_rot <= 0 || c.n_rot > c.head_dim || c.n_rot % 2 || c.n_embd % 32 || c.n_ff % 32 || (c.n_head * c.head_dim) % 32) {
+    zllm_set_error(ctx, "zllm_model_create: bad configuration");
+    return ZLLM_E_ARG;
+  }
+  if (!attn_supported(c.head_dim, c.n_head / c.n_head_kv)) {
+    zllm_set_error(ctx, "zllm_model_create: head_dim %d with %d query heads per KV head is not supported", c.head_dim,
+                   c.n_head / c.n_head_kv);
+    return ZLLM_E_UNSUPPORTED;
+  }
+  zllm_model *m = new (std::nothrow) zllm_model();
+  if (!m) return ZLLM_E_OOM;
+  m->ctx = ctx;
+  m->c = c;
+  if (m->c.logits_batch < 1) m->c.logits_batch = 1;
+  if (m->c.logits_batch > m->c.max_batch) m->c.logits_batch = m->c.max_batch;
+  m->L.resize(c.n_layer);
+  m->pos.assign(c.n_seq, 0);
+  cudaSetDevice(ctx->device);
+  if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) { delete m; return ZLLM_E_CUDA; }
+  *out = m;
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_set_matrix(zllm_model *m, int kind, int layer, int ggml_type, int64_t rows, int64_t cols,
+                                     const void *host, size_t nbytes) {
+  if (!m || m->ready) return ZLLM_E_STATE;
+  const zllm_model_config &c = m->c;
+  int64_t er = 0, ec = 0;
+  switch (kind) {
+    case ZLLM_T_TOK_EMBD: case ZLLM_T_OUTPUT: er = c.vocab; ec = c.n_embd; break;
+    case ZLLM_T_WQ: er = m->qdim(); ec = c.n_embd; break;
+    case ZLLM_T_WK: case ZLLM_T_WV: er = m->kvdim(); ec = c.n_embd; break;
+    case ZLLM_T_WO: er = c.n_embd; ec = m->qdim(); break;
+    case ZLLM_T_GATE: case ZLLM_T_UP: er = c.n_ff; ec = c.n_embd; break;
+    case ZLLM_T_DOWN: er = c.n_embd; ec = c.n_ff; break;
+    default: zllm_set_error(m->ctx, "zllm_model_set_matrix: unknown tensor kind %d", kind); return ZLLM_E_ARG;
+  }
+  const bool per_layer = kind >= ZLLM_T_WQ;
+  if (per_layer && (layer < 0 || layer >= c.n_layer)) { zllm_set_error(m->ctx, "layer %d out of range", layer); return ZLLM_E_ARG; }
+  if (rows != er || cols != ec) {
+    zllm_set_error(m->ctx, "tensor kind %d: shape %lld x %lld, expected %lld x %lld", kind, (long long)rows, (long long)cols,
+                   (long long)er, (long long)ec);
+    return ZLLM_E_ARG;
+  }
+  zllm_weight *w = nullptr;
+  int rc = zllm_weight_upload(m->ctx, ggml_type, rows, cols, host, nbytes, &w);
+  if (rc) return rc;
+  zllm_weight **slotp = nullptr;
+  switch (kind) {
+    case ZLLM_T_TOK_EMBD: slotp = &m->tok; break;
+    case ZLLM_T_OUTPUT: slotp = &m->out; break;
+    case ZLLM_T_WQ: slotp = &m->L[layer].w[WQ]; break;
+    case ZLLM_T_WK: slotp = &m->L[layer].w[WK]; break;
+    case ZLLM_T_WV: slotp = &m->L[layer].w[WV]; break;
+    case ZLLM_T_WO: slotp = &m->L[layer].w[WO]; break;
+    case ZLLM_T_GATE: slotp = &m->L[layer].w[GATE]; break;
+    case ZLLM_T_UP: slotp = &m->L[layer].w[UP]; break;
+    case ZLLM_T_DOWN: slotp = &m->L[layer].w[DOWN]; break;
+  }
+  if (*slotp) zllm_weight_free(*slotp);
+  *slotp = w;
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_set_vector(zllm_model *m, int kind, int layer, const float *host, int64_t n) {
+  if (!m || m->ready) return ZLLM_E_STATE;
+  const zllm_model_config &c = m->c;
+  int64_t en = 0;
+  float **dst = nullptr;
+  const bool per_layer = kind >= ZLLM_T_ATTN_NORM;
+  if (per_layer && (layer < 0 || layer >= c.n_layer)) { zllm_set_error(m->ctx, "layer %d out of range", layer); return ZLLM_E_ARG; }
+  switch (kind) {
+    case ZLLM_T_OUTPUT_NORM: en = c.n_embd; dst = &m->out_norm; break;
+    case ZLLM_T_ROPE_FREQS:
+      if (n != c.n_rot / 2 || !host) { zllm_set_error(m->ctx, "rope_freqs: %lld values, expected %d", (long long)n, c.n_rot / 2); return ZLLM_E_ARG; }
+      m->rope_freqs_host.assign(host, host + n);
+      return ZLLM_OK;
+    case ZLLM_T_ATTN_NORM: en = c.n_embd; dst = &m->L[layer].attn_norm; break;
+    case ZLLM_T_FFN_NORM: en = c.n_embd; dst = &m->L[layer].ffn_norm; break;
+    case ZLLM_T_Q_NORM: en = c.head_dim; dst = &m->L[layer].q_norm; break;
+    case ZLLM_T_K_NORM: en = c.head_dim; dst = &m->L[layer].k_norm; break;
+    case ZLLM_T_BQ: en = m->qdim(); dst = &m->L[layer].bq; break;
+    case ZLLM_T_BK: en = m->kvdim(); dst = &m->L[layer].bk; break;
+    case ZLLM_T_BV: en = m->kvdim(); dst = &m->L[layer].bv; break;
+    default: zllm_set_error(m->ctx, "zllm_model_set_vector: unknown tensor kind %d", kind); return ZLLM_E_ARG;
+  }
+  if (n != en || !host) { zllm_set_error(m->ctx, "vector kind %d: %lld values, expected %lld", kind, (long long)n, (long long)en); return ZLLM_E_ARG; }
+  if (!*dst) CK(dalloc(dst, (size_t)n), "cudaMalloc(vector)");
+  CK(cudaMemcpyAsync(*dst, host, sizeof(float) * n, cudaMemcpyHostToDevice, m->stream), "vector upload");
+  CK(cudaStreamSynchronize(m->stream), "vector upload");
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_ready(zllm_model *m) {
+  if (!m) return ZLLM_E_ARG;
+  if (m->ready) return ZLLM_OK;
+  const zllm_model_config &c = m->c;
+  if (!m->tok || !m->out_norm) { zllm_set_error(m->ctx, "model: token_embd / output_norm missing"); return ZLLM_E_ARG; }
+  for (int l = 0; l < c.n_layer; l++) {
+    for (int i = 0; i < 7; i++)
+      if (!m->L[l].w[i]) { zllm_set_error(m->ctx, "model: layer %d matrix %d missing", l, i); return ZLLM_E_ARG; }
+    if (!m->L[l].attn_norm || !m->L[l].ffn_norm) { zllm_set_error(m->ctx, "model: layer %d norms missing", l); return ZLLM_E_ARG; }
+  }
+  const int MB = c.max_batch;
+  const int64_t E = c.n_embd, F = c.n_ff, Q = m->qdim(), KV = m->kvdim();
+  const int64_t KX = std::max(E, std::max(F, Q));
+  const int LB = std::max(c.logits_batch, c.n_seq < MB ? c.n_seq : MB);
+  CK(dalloc(&m->rope_cos, (size_t)c.ctx * c.n_rot / 2), "rope");
+  CK(dalloc(&m->rope_sin, (size_t)c.ctx * c.n_rot / 2), "rope");
+  int rc = zllm_rope_tables(m->ctx, c.n_rot, c.rope_base, c.ctx, m->rope_freqs_host.empty() ? nullptr : m->rope_freqs_host.data(),
+                            m->rope_cos, m->rope_sin);
+  if (rc) return fail(m, rc);
+  m->kv_bytes = (size_t)c.n_seq * m->seq_elems() * m->el();
+  CK(cudaMalloc(&m->kv, m->kv_bytes), "cudaMalloc(KV cache)");
+  CK(cudaMemsetAsync(m->kv, 0, m->kv_bytes, m->stream), "KV clear");
+  CK(dalloc(&m->x, MB * E), "act");
+  CK(dalloc(&m->xb, MB * KX), "act");
+  CK(dalloc(&m->xq, MB * KX), "act");
+  CK(dalloc(&m->xd, MB * KX / 32), "act");
+  CK(dalloc(&m->xs, MB * KX / 32), "act");
+  CK(dalloc(&m->q, MB * Q), "act");
+  CK(dalloc(&m->k, MB * KV), "act");
+  CK(dalloc(&m->v, MB * KV), "act");
+  CK(dalloc(&m->qr, MB * Q), "act");
+  CK(dalloc(&m->att, MB * Q), "act");
+  CK(dalloc(&m->g, MB * F), "act");
+  CK(dalloc(&m->u, MB * F), "act");
+  CK(dalloc(&m->hb, MB * F), "act");
+  CK(dalloc(&m->logits, (size_t)LB * c.vocab), "logits");
+  CK(dalloc(&m->d_tok, MB), "ids");
+  CK(dalloc(&m->d_pos, MB), "ids");
+  CK(dalloc(&m->d_seq, MB), "ids");
+  CK(dalloc(&m->d_npos, MB), "ids");
+  CK(dalloc(&m->d_arg, MB), "ids");
+  CK(cudaHostAlloc((void **)&m->h_io, sizeof(int32_t) * 4 * MB, cudaHostAllocDefault), "pinned ids");
+  const zllm_attn_geom g = m->geom();
+  m->nsplit = zllm_attn_splits(m->ctx, &g, 1, c.ctx);     // the most splits any pass uses (one query)
+  const int group = c.n_head / c.n_head_kv;
+  CK(dalloc(&m->part, (size_t)MB * c.n_head_kv * m->nsplit * group * (c.head_dim + 2)), "attention scratch");
+  CK(dalloc(&m->counters, (size_t)MB * c.n_head_kv), "attention counters");
+  CK(cudaMemsetAsync(m->counters, 0, sizeof(int32_t) * MB * c.n_head_kv, m->stream), "counters");
+  CK(cudaStreamSynchronize(m->stream), "model ready");
+  m->ready = true;
+  return ZLLM_OK;
+}
+
+// ------------------------------------------------------------------------------------ the pass
+static cudaError_t gemv(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add, const float *xf,
+                        int64_t k) {
+  ActView a{m->xq, m->xd, m->xs, xf, k};
+  const char *why = "";
+  return launch_gemv(w->m, a, n, y, ys, y_add, m->ctx->status_dev, m->ctx->num_sms, m->stream, true, &why);
+}
+
+// Enqueue the pass for n tokens whose ids / positions / sequences are already in d_tok / d_pos /
+// d_seq / d_npos.  want: 0 no logits, 1 the last token's, 2 every token's.
+static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
+  const zllm_model_config &c = m->c;
+  const int64_t E = c.n_embd, F = c.n_ff, Q = m->qdim(), KV = m->kvdim();
+  cudaStream_t s = m->stream;
+  cudaError_t e;
+#define RUN(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
+  RUN(launch_embed(m->tok->m, m->d_tok, n, m->x, s, true));
+  const zllm_attn_geom g = m->geom();
+  for (int l = 0; l < c.n_layer; l++) {
+    const Layer &L = m->L[l];
+    RUN(launch_rmsnorm_quant(m->x, L.attn_norm, (int)E, n, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, true));
+    RUN(gemv(m, L.w[WQ], n, m->q, Q, nullptr, m->xb, E));
+    RUN(gemv(m, L.w[WK], n, m->k, KV, nullptr, m->xb, E));
+    RUN(gemv(m, L.w[WV], n, m->v, KV, nullptr, m->xb, E));
+    QkvPostArgs pa{};
+    pa.q = m->q; pa.k = m->k; pa.v = m->v; pa.q_stride = Q; pa.kv_stride = KV;
+    pa.bq = L.bq; pa.bk = L.bk; pa.bv = L.bv; pa.q_norm = L.q_norm; pa.k_norm = L.k_norm;
+    pa.rope_cos = m->rope_cos; pa.rope_sin = m->rope_sin; pa.pos = m->d_pos; pa.seq = m->d_seq;
+    pa.q_out = m->qr; pa.q_out_stride = Q;
+    pa.kcache = m->kv_block(0, l, 0); pa.vcache = m->kv_block(0, l, 1);
+    pa.seq_stride = g.seq_stride; pa.head_stride = g.head_stride;
+    pa.n_head = c.n_head; pa.n_kv = c.n_head_kv; pa.head_dim = c.head_dim; pa.n_rot = c.n_rot; pa.neox = c.neox;
+    pa.kv_f16 = c.kv_f16; pa.ntok = n; pa.eps = c.rms_eps;
+    RUN(launch_qkv_post(pa, s, true));
+    AttnArgs aa{};
+    aa.q = m->qr; aa.seq = m->d_seq; aa.kcache = m->kv_block(0, l, 0); aa.vcache = m->kv_block(0, l, 1);
+    aa.seq_stride = g.seq_stride; aa.head_stride = g.head_stride; aa.npos = m->d_npos; aa.out = m->att;
+    aa.partial = m->part; aa.counters = m->counters; aa.status = m->ctx->status_dev;
+    aa.scale = (float)(1.0 / std::sqrt((double)c.head_dim));
+    // one split count for every pass: a query's context partition (and so its rounding) does not
+    // depend on how many tokens share the pass, so batched passes equal token-by-token ones bit for bit
+    aa.n_head = c.n_head; aa.n_kv = c.n_head_kv; aa.head_dim = c.head_dim; aa.nseq = n; aa.nsplit = m->nsplit;
+    RUN(launch_attn(aa, c.kv_f16 != 0, s, true));
+    RUN(launch_quantize(m->att, Q, n, m->xq, m->xd, m->xs, m->ctx->status_dev, s, true));
+    RUN(gemv(m, L.w[WO], n, m->x, E, m->x, m->att, Q));                       // x += wo . att
+    RUN(launch_rmsnorm_quant(m->x, L.ffn_norm, (int)E, n, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, true));
+    RUN(gemv(m, L.w[GATE], n, m->g, F, nullptr, m->xb, E));
+    RUN(gemv(m, L.w[UP], n, m->u, F, nullptr, m->xb, E));
+    RUN(launch_swiglu_quant(m->g, m->u, (int)F, n, F, m->hb, m->xq, m->xd, m->xs, s, true));
+    RUN(gemv(m, L.w[DOWN], n, m->x, E, m->x, m->hb, F));                      // x += down . hb
+  }
+  if (want) {
+    const zllm_weight *ow = m->out ? m->out : m->tok;
+    const int nl = want == 2 ? n : 1;
+    const float *xl = want == 2 ? m->x : m->x + (int64_t)(n - 1) * E;
+    RUN(launch_rmsnorm_quant(xl, m->out_norm, (int)E, nl, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, true));
+    RUN(gemv(m, ow, nl, m->logits, c.vocab, nullptr, m->xb, E));
+    RUN(launch_argmax(m->logits, c.vocab, c.vocab, nl, m->d_arg, s, true));
+  }
+#undef RUN
+  return cudaSuccess;
+}
+
+// Validate, stage the int arrays, run the pass (replaying a recorded graph when possible), copy out.
+static int run(zllm_model *m, const int32_t *seqs, int single_seq, const int32_t *tokens, int n, int want, float *logits_host,
+               int32_t *argmax_host) {
+  if (!m) return ZLLM_E_ARG;
+  if (m->closed) { zllm_set_error(m->ctx, "model is closed"); return ZLLM_E_STATE; }
+  if (m->failed) return ZLLM_E_STATE;
+  if (!m->ready) { int rc = zllm_model_ready(m); if (rc) return rc; }
+  const zllm_model_config &c = m->c;
+  if (n < 1 || n > c.max_batch) { zllm_set_error(m->ctx, "batch of %d tokens (max %d)", n, c.max_batch); return ZLLM_E_BATCH; }
+  if (want == 2 && n > c.logits_batch && single_seq >= 0) {
+    zllm_set_error(m->ctx, "logits for all positions of a batch of %d tokens (this pool supports %d; raise the logitsBatch option)",
+                   n, c.logits_batch);
+    return ZLLM_E_BATCH;
+  }
+  for (int i = 0; i < n; i++)
+    if (!(tokens[i] >= 0 && tokens[i] < c.vocab)) { zllm_set_error(m->ctx, "token id %d out of range", tokens[i]); return ZLLM_E_TOKEN; }
+  int32_t *ht = m->h_io, *hp = m->h_io + c.max_batch, *hs = m->h_io + 2 * c.max_batch, *hn = m->h_io + 3 * c.max_batch;
+  std::vector<int> added(c.n_seq, 0);
+  for (int i = 0; i < n; i++) {
+    const int sq = single_seq >= 0 ? single_seq : seqs[i];
+    if (sq < 0 || sq >= c.n_seq) { zllm_set_error(m->ctx, "sequence %d out of range", sq); return ZLLM_E_ARG; }
+    const int p = m->pos[sq] + added[sq]++;
+    if (p >= c.ctx) { zllm_set_error(m->ctx, "context full (%d tokens)", c.ctx); return ZLLM_E_CTX_FULL; }
+    ht[i] = tokens[i]; hp[i] = p; hs[i] = sq; hn[i] = p + 1;
+  }
+  cudaStream_t s = m->stream;
+  CK(cudaMemcpyAsync(m->d_tok, ht, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
+  CK(cudaMemcpyAsync(m->d_pos, hp, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
+  CK(cudaMemcpyAsync(m->d_seq, hs, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
+  CK(cudaMemcpyAsync(m->d_npos, hn, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
+  cudaGraphExec_t exec = nullptr;
+  bool eager = !m->use_graphs;
+  if (!eager) {
+    for (auto &gr : m->graphs)
+      if (gr.n == n && gr.want == want) exec = gr.exec;
+    // the first pass of a shape runs eagerly (kernel attributes are set outside any capture)
+    if (!exec && std::find(m->eager_seen.begin(), m->eager_seen.end(), std::make_pair(n, want)) == m->eager_seen.end()) {
+      m->eager_seen.push_back({n, want});
+      eager = true;
+    }
+  }
+  if (!eager) {
+    if (!exec) {
+      cudaGraph_t graph = nullptr;
+      CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "graph capture");
+      cudaError_t e = enqueue_pass(m, n, want);
+      cudaError_t e2 = cudaStreamEndCapture(s, &graph);
+      if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        return fail(m, zllm_cuda_fail(m->ctx, e != cudaSuccess ? e : e2, "recording the pass"));
+      }
+      e = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (e != cudaSuccess) return fail(m, zllm_cuda_fail(m->ctx, e, "cudaGraphInstantiate"));
+      m->graphs.push_back({n, want, exec});
+    }
+    CK(cudaGraphLaunch(exec, s), "cudaGraphLaunch");
+  } else {
+    CK(enqueue_pass(m, n, want), "pass launch");
+  }
+  const int nl = want == 2 ? n : 1;
+  if (want && logits_host)
+    CK(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * nl * c.vocab, cudaMemcpyDeviceToHost, s), "logits");
+  if (want && argmax_host) CK(cudaMemcpyAsync(argmax_host, m->d_arg, sizeof(int32_t) * nl, cudaMemcpyDeviceToHost, s), "argmax");
+  CK(cudaStreamSynchronize(s), "pass");
+  int rc = zllm_check_status(m->ctx);
+  if (rc) return fail(m, rc);
+  for (int sq = 0; sq < c.n_seq; sq++) m->pos[sq] += added[sq];
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_forward(zllm_model *m, int seq, const int32_t *tokens, int n, int want, float *logits_host,
+                                  int32_t *argmax_host) {
+  if (!m || !tokens || want < 0 || want > 2) return ZLLM_E_ARG;
+  if (seq < 0 || seq >= m->c.n_seq) { zllm_set_error(m->ctx, "sequence %d out of range", seq); return ZLLM_E_ARG; }
+  return run(m, nullptr, seq, tokens, n, want, logits_host, argmax_host);
+}
+
+extern "C" int zllm_model_decode(zllm_model *m, const int32_t *seqs, const int32_t *tokens, int n, float *logits_host,
+                                 int32_t *argmax_host) {
+  if (!m || !tokens || !seqs) return ZLLM_E_ARG;
+  for (int i = 0; i < n; i++)
+    for (int j = 0; j < i; j++)
+      if (seqs[i] == seqs[j]) { zllm_set_error(m->ctx, "zllm_model_decode: sequence %d appears twice", seqs[i]); return ZLLM_E_ARG; }
+  return run(m, seqs, -1, tokens, n, 2, logits_host, argmax_host);
+}
+
+extern "C" int zllm_model_pos(const zllm_model *m, int seq) {
+  if (!m || seq < 0 || seq >= m->c.n_seq) return ZLLM_E_ARG;
+  return m->pos[seq];
+}
+
+extern "C" int zllm_model_truncate(zllm_model *m, int seq, int n) {
+  if (!m || seq < 0 || seq >= m->c.n_seq) return ZLLM_E_ARG;
+  if (n < 0) n = 0;
+  if (n < m->pos[seq]) m->pos[seq] = n;            // a KV cache is positional (src/compute/pool.js:278-281)
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_reset(zllm_model *m, int seq) { return zllm_model_truncate(m, seq, 0); }
+
+extern "C" int zllm_model_set_graphs(zllm_model *m, int on) {
+  if (!m) return ZLLM_E_ARG;
+  m->use_graphs = on != 0;
+  return ZLLM_OK;
+}
+
+extern "C" void *zllm_model_logits(zllm_model *m) { return m ? m->logits : nullptr; }
+
+static int kv_io(zllm_model *m, int seq, int layer, int is_v, int n, float *host, bool get) {
+  if (!m || !host || seq < 0 || seq >= m->c.n_seq || layer < 0 || layer >= m->c.n_layer || (is_v != 0 && is_v != 1) ||
+      n < 0 || n > m->c.ctx)
+    return ZLLM_E_ARG;
+  if (m->failed) return ZLLM_E_STATE;
+  if (!m->ready) { int rc = zllm_model_ready(m); if (rc) return rc; }
+  if (n == 0) return ZLLM_OK;
+  const zllm_attn_geom g = m->geom();
+  void *stage;
+  int rc = zllm_scratch(m->ctx, 12, sizeof(float) * n * m->kvdim(), &stage);
+  if (rc) return rc;
+  cudaStream_t s = m->stream;
+  if (get) {
+    rc = zllm_kv_export(m->ctx, &g, m->kv_block(seq, layer, is_v), n, (float *)stage, s);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(host, stage, sizeof(float) * n * m->kvdim(), cudaMemcpyDeviceToHost, s), "kvGet");
+  } else {
+    CK(cudaMemcpyAsync(stage, host, sizeof(float) * n * m->kvdim(), cudaMemcpyHostToDevice, s), "kvSet");
+    rc = zllm_kv_import(m->ctx, &g, m->kv_block(seq, layer, is_v), n, (const float *)stage, s);
+    if (rc) return rc;
+  }
+  CK(cudaStreamSynchronize(s), get ? "kvGet" : "kvSet");
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_kv_get(zllm_model *m, int seq, int layer, int is_v, int n, float *out) {
+  return kv_io(m, seq, layer, is_v, n, out, true);
+}
+extern "C" int zllm_model_kv_set(zllm_model *m, int seq, int layer, int is_v, int n, const float *in) {
+  return kv_io(m, seq, layer, is_v, n, const_cast<float *>(in), false);
+}
+
+extern "C" int zllm_model_restore_prefix(zllm_model *m, int seq, int n) {
+  if (!m || seq < 0 || seq >= m->c.n_seq || n < 0 || n > m->c.ctx) return ZLLM_E_ARG;
+  m->pos[seq] = n;                                  // src/compute/pool.js:244-247: the model now holds n positions
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_slot_save(zllm_model *m, int seq, int n) {
+  if (!m || seq < 0 || seq >= m->c.n_seq || n < 0 || n > m->pos[seq]) return ZLLM_E_ARG;
+  if (!m->ready) { int rc = zllm_model_ready(m); if (rc) return rc; }
+  if (n > m->slot_cap) {
+    if (m->slot) cudaFree(m->slot);
+    m->slot = nullptr;
+    m->slot_cap = 0;
+    CK(cudaMalloc(&m->slot, (size_t)m->c.n_layer * 2 * m->kvdim() * n * m->el()), "cudaMalloc(prefix slot)");
+    m->slot_cap = n;
+  }
+  const zllm_attn_geom g = m->geom();
+  const int64_t slot_hs = (int64_t)m->slot_cap * m->c.head_dim;
+  for (int l = 0; l < m->c.n_layer; l++)
+    for (int v = 0; v < 2; v++) {
+      uint8_t *dst = (uint8_t *)m->slot + ((int64_t)l * 2 + v) * m->kvdim() * m->slot_cap * m->el();
+      int rc = zllm_kv_copy(m->ctx, &g, dst, slot_hs, m->kv_block(seq, l, v), g.head_stride, n, m->stream);
+      if (rc) return rc;
+    }
+  CK(cudaStreamSynchronize(m->stream), "slot save");
+  m->slot_n = n;
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_slot_restore(zllm_model *m, int seq) {
+  if (!m || seq < 0 || seq >= m->c.n_seq) return ZLLM_E_ARG;
+  if (!m->slot || m->slot_n == 0) { zllm_set_error(m->ctx, "no prefix slot saved"); return ZLLM_E_STATE; }
+  const zllm_attn_geom g = m->geom();
+  const int64_t slot_hs = (int64_t)m->slot_cap * m->c.head_dim;
+  for (int l = 0; l < m->c.n_layer; l++)
+    for (int v = 0; v < 2; v++) {
+      const uint8_t *src = (const uint8_t *)m->slot + ((int64_t)l * 2 + v) * m->kvdim() * m->slot_cap * m->el();
+      int rc = zllm_kv_copy(m->ctx, &g, m->kv_block(seq, l, v), g.head_stride, src, slot_hs, m->slot_n, m->stream);
+      if (rc) return rc;
+    }
+  CK(cudaStreamSynchronize(m->stream), "slot restore");
+  m->pos[seq] = m->slot_n;
+  return ZLLM_OK;
+}
+
+extern "C" void zllm_model_destroy(zllm_model *m) {
+  if (!m) return;
+  m->closed = true;
+  cudaSetDevice(m->ctx->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (auto &gr : m->graphs)
+    if (gr.exec) cudaGraphExecDestroy(gr.exec);
+  for (auto &L : m->L) {
+    for (auto *w : L.w) zllm_weight_free(w);
+    for (float *p : {L.attn_norm, L.ffn_norm, L.q_norm, L.k_norm, L.bq, L.bk, L.bv}) cudaFree(p);
+  }
+  zllm_weight_free(m->tok);
+  zllm_weight_free(m->out);
+  for (void *p : {(void *)m->out_norm, (void *)m->rope_cos, (void *)m->rope_sin, m->kv, m->slot, (void *)m->x, (void *)m->xb,
+                  (void *)m->q, (void *)m->k, (void *)m->v, (void *)m->qr, (void *)m->att, (void *)m->g, (void *)m->u,
+                  (void *)m->hb, (void *)m->logits, (void *)m->part, (void *)m->xq, (void *)m->xd, (void *)m->xs,
+                  (void *)m->d_tok, (void *)m->d_pos, (void *)m->d_seq, (void *)m->d_npos, (void *)m->d_arg,
+                  (void *)m->counters})
+    if (p) cudaFree(p);
+  if (m->h_io) cudaFreeHost(m->h_io);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}

@@ -1,0 +1,235 @@
+// Per-token glue of the decode step, each fused with the activation quantization its consumer
+// needs: token embedding (dequantized row), RMSNorm + quantize, SwiGLU + quantize, greedy argmax.
+//
+// Arithmetic follows the reference: rmsnorm src/compute/ref-kernels.js:305-310 (double sum of
+// squares, s = 1/sqrt(ss/n + eps), f32(x * s * w)); silu :322 and the SwiGLU product
+// src/compute/worker.js:426 (double, stored f32); dequantRow :80-120 with quant.js:121-202;
+// quantizeAct :44-62 (see quant.cu); argmax src/model/generate.js:4-10 (first maximum wins).
+// The double sums of squares are reduced as a fixed tree rather than left to right, so a result can
+// differ from the reference's in the last bit of the double -- and only then, rarely, in the f32.
+#include "common.cuh"
+#include "internal.h"
+
+namespace zllm {
+
+// ---------------------------------------------------------------------------- block quantization
+// One warp quantizes one 32-value block held one value per lane (same arithmetic as quant.cu).
+__device__ __forceinline__ void quantize_block_warp(float v, int lane, int8_t *q, float *d, int32_t *s) {
+  float a = fabsf(v);
+  if (!(a == a)) a = 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  const double scale = __ddiv_rn((double)a, 127.0);
+  const double inv = scale != 0.0 ? __ddiv_rn(1.0, scale) : 0.0;
+  const double r = round(__dmul_rn((double)v, inv));
+  const bool nan = !(r == r);
+  q[lane] = nan ? (int8_t)0 : (int8_t)(int)r;
+  int sum = nan ? 0 : (int)r;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const bool any_nan = __any_sync(0xffffffffu, nan);
+  if (lane == 0) {
+    *d = __double2float_rn(scale);
+    *s = any_nan ? 0 : sum;
+  }
+}
+
+// ---------------------------------------------------------------------------- RMSNorm + quantize
+// One CTA per token.  xb (optional) receives the normalized f32 vector; xq/xd/xs (optional) its
+// quantization.  n must be a multiple of 32 when quantizing.
+__global__ void rmsnorm_quant_kernel(const float *__restrict__ x, const float *__restrict__ w, int n, double eps,
+                                     float *xb, int8_t *xq, float *xd, int32_t *xs) {
+  extern __shared__ double red[];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const float *xt = x + (int64_t)t * n;
+  double ss = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) ss = __dadd_rn(ss, __dmul_rn((double)xt[i], (double)xt[i]));
+  ss = warp_sum_f64(ss);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    double v = lane < nw ? red[lane] : 0.0;
+    v = warp_sum_f64(v);
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  const double s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(red[0], (double)n), eps)));
+  if (xq) {
+    for (int b = warp; b < n / 32; b += nw) {
+      const int i = b * 32 + lane;
+      const float v = __double2float_rn(__dmul_rn(__dmul_rn((double)xt[i], s), (double)w[i]));
+      if (xb) xb[(int64_t)t * n + i] = v;
+      quantize_block_warp(v, lane, xq + (int64_t)t * n + b * 32, xd + (int64_t)t * (n / 32) + b, xs + (int64_t)t * (n / 32) + b);
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      xb[(int64_t)t * n + i] = __double2float_rn(__dmul_rn(__dmul_rn((double)xt[i], s), (double)w[i]));
+  }
+}
+
+// ---------------------------------------------------------------------------- SwiGLU + quantize
+// hb = f32(silu(gate) * up) with silu(z) = z / (1 + exp(-z)) in double; then quantized per 32.
+__global__ void swiglu_quant_kernel(const float *__restrict__ gate, const float *__restrict__ up, int n, int ntok,
+                                    int64_t stride, float *hb, int8_t *xq, float *xd, int32_t *xs) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t nblk = (int64_t)ntok * (n / 32);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t gb = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); gb < nblk; gb += warps) {
+    const int t = (int)(gb / (n / 32)), b = (int)(gb % (n / 32));
+    const int64_t i = (int64_t)t * stride + b * 32 + lane;
+    const double z = gate[i];
+    const double sl = __ddiv_rn(z, __dadd_rn(1.0, exp(-z)));
+    const float v = __double2float_rn(__dmul_rn(sl, (double)up[i]));
+    if (hb) hb[(int64_t)t * n + b * 32 + lane] = v;
+    if (xq) quantize_block_warp(v, lane, xq + (int64_t)t * n + b * 32, xd + (int64_t)t * (n / 32) + b, xs + (int64_t)t * (n / 32) + b);
+  }
+}
+
+// ---------------------------------------------------------------------------- embedding
+// value i of row r of a device-layout matrix (the repacked layouts of gemv.cu), as f32
+__device__ float dequant_at(const DevMatrix &m, int64_t r, int64_t i) {
+  const uint8_t *row = m.data + r * m.row_stride;
+  switch (m.type) {
+    case T_F32: return reinterpret_cast<const float *>(row)[i];
+    case T_F16: return h2f(reinterpret_cast<const uint16_t *>(row)[i]);
+    case T_BF16: return bf2f(reinterpret_cast<const uint16_t *>(row)[i]);
+    case T_Q8_0: {
+      const int64_t nb = m.cols / 32, b = i / 32;
+      const double d = h2f(*reinterpret_cast<const uint16_t *>(row + 32 * nb + 2 * b));
+      return __double2float_rn(__dmul_rn(d, (double)(int8_t)row[b * 32 + i % 32]));
+    }
+    case T_Q4_0: case T_Q5_0: {
+      const int64_t nb = m.cols / 32, b = i / 32;
+      const int j = (int)(i % 32);
+      const uint8_t byte = row[b * 16 + (j & 15)];
+      int q = j < 16 ? (byte & 15) : (byte >> 4);
+      const bool five = m.type == T_Q5_0;
+      if (five) q |= (int)((*reinterpret_cast<const uint32_t *>(row + 16 * nb + 4 * b) >> j) & 1u) << 4;
+      const double d = h2f(*reinterpret_cast<const uint16_t *>(row + (five ? 20 : 16) * nb + 2 * b));
+      return __double2float_rn(__dmul_rn(d, (double)(q - (five ? 16 : 8))));
+    }
+    case T_Q4_K: case T_Q5_K: {
+      const bool five = m.type == T_Q5_K;
+      const int64_t sb = i / 256;
+      const int e = (int)(i % 256), s = e / 32, l = e % 32, c = s >> 1;
+      const uint8_t *blk = row + sb * (five ? 176 : 144);
+      const uint8_t byte = blk[(five ? 48 : 16) + c * 32 + l];
+      int v = (s & 1) ? byte >> 4 : byte & 15;
+      if (five) v |= ((blk[16 + l] >> s) & 1) << 4;
+      // the repacked scale field of chunk c: sc(2c) | sc(2c+1) << 6 | mn(2c) << 12 | mn(2c+1) << 18
+      const uint32_t F = (uint32_t)blk[4 + 3 * c] | ((uint32_t)blk[5 + 3 * c] << 8) | ((uint32_t)blk[6 + 3 * c] << 16);
+      const int sc = (s & 1) ? (F >> 6) & 63 : F & 63, mn = (s & 1) ? (F >> 18) & 63 : (F >> 12) & 63;
+      const double d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
+      // quant.js:150: d * sc * v - dmin * mn
+      return __double2float_rn(__dsub_rn(__dmul_rn(__dmul_rn(d, (double)sc), (double)v), __dmul_rn(dmin, (double)mn)));
+    }
+    case T_Q6_K: {
+      const int64_t nb = m.cols / 256, sb = i / 256;
+      const int e = (int)(i % 256), half = e / 128, k = (e % 128) / 32, l = e % 32;
+      const uint8_t ql = row[sb * 128 + half * 64 + (k & 1) * 32 + l];
+      const uint8_t qh = row[128 * nb + sb * 64 + half * 32 + l];
+      const int q = (int)(((k < 2 ? ql & 15 : ql >> 4)) | (((qh >> (2 * k)) & 3) << 4)) - 32;
+      const int scale = (int8_t)row[192 * nb + sb * 16 + half * 8 + (l >> 4) + 2 * k];
+      const double d = h2f(*reinterpret_cast<const uint16_t *>(row + 208 * nb + 2 * sb));
+      // quant.js:194-197: d * scale * q
+      return __double2float_rn(__dmul_rn(__dmul_rn(d, (double)scale), (double)q));
+    }
+  }
+  return 0.f;
+}
+
+__global__ void embed_kernel(const DevMatrix m, const int32_t *tokens, int ntok, float *x) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  if (t >= ntok) return;
+  const int64_t r = tokens[t];
+  for (int64_t i = threadIdx.x; i < m.cols; i += blockDim.x) x[(int64_t)t * m.cols + i] = dequant_at(m, r, i);
+}
+
+// ---------------------------------------------------------------------------- argmax
+__global__ void argmax_kernel(const float *logits, int64_t n, int64_t stride, int32_t *out) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const float *l = logits + (int64_t)blockIdx.x * stride;
+  float best = -INFINITY;
+  int idx = -1;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = l[i];
+    if (v > best || idx < 0) { best = v; idx = (int)i; }
+  }
+  // first maximum wins: on equal values keep the smaller index
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx) || (idx < 0 && oi >= 0)) { best = ob; idx = oi; }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? bv[lane] : -INFINITY;
+    idx = lane < nw ? bi[lane] : -1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ob > best || (ob == best && oi >= 0 && (idx < 0 || oi < idx))) { best = ob; idx = oi; }
+    }
+    if (lane == 0) out[blockIdx.x] = idx;
+  }
+}
+
+// ---------------------------------------------------------------------------- launchers
+static cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, cudaLaunchAttribute *attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cfg;
+}
+
+cudaError_t launch_rmsnorm_quant(const float *x, const float *w, int n, int ntok, double eps, float *xb, int8_t *xq, float *xd,
+                                 int32_t *xs, cudaStream_t s, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(dim3(ntok), dim3(512), 16 * sizeof(double), s, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, x, w, n, eps, xb, xq, xd, xs);
+}
+
+cudaError_t launch_swiglu_quant(const float *gate, const float *up, int n, int ntok, int64_t stride, float *hb, int8_t *xq,
+                                float *xd, int32_t *xs, cudaStream_t s, bool pdl) {
+  const int64_t blocks = (int64_t)ntok * (n / 32);
+  int64_t grid = (blocks + 7) / 8;
+  if (grid > 2048) grid = 2048;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(dim3((unsigned)grid), dim3(256), 0, s, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, gate, up, n, ntok, stride, hb, xq, xd, xs);
+}
+
+cudaError_t launch_embed(const DevMatrix &m, const int32_t *tokens, int ntok, float *x, cudaStream_t s, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(dim3(ntok), dim3(256), 0, s, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, embed_kernel, m, tokens, ntok, x);
+}
+
+cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, cudaStream_t s, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(dim3(ntok), dim3(1024), 0, s, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, argmax_kernel, logits, n, stride, out);
+}
+
+}  // namespace zllm

@@ -47,7 +47,36 @@ SIGNATURES = {
     "zllm_kv_import": (i32, [vp, vp, vp, i32, vp, vp]),
     "zllm_kv_export": (i32, [vp, vp, vp, i32, vp, vp]),
     "zllm_kv_copy": (i32, [vp, vp, vp, i64, vp, i64, i32, vp]),
+    "zllm_model_create": (i32, [vp, vp, PP]),
+    "zllm_model_set_matrix": (i32, [vp, i32, i32, i32, i64, i64, vp, sz]),
+    "zllm_model_set_vector": (i32, [vp, i32, i32, vp, i64]),
+    "zllm_model_ready": (i32, [vp]),
+    "zllm_model_forward": (i32, [vp, i32, vp, i32, i32, vp, vp]),
+    "zllm_model_decode": (i32, [vp, vp, vp, i32, vp, vp]),
+    "zllm_model_pos": (i32, [vp, i32]),
+    "zllm_model_truncate": (i32, [vp, i32, i32]),
+    "zllm_model_reset": (i32, [vp, i32]),
+    "zllm_model_kv_get": (i32, [vp, i32, i32, i32, i32, vp]),
+    "zllm_model_kv_set": (i32, [vp, i32, i32, i32, i32, vp]),
+    "zllm_model_restore_prefix": (i32, [vp, i32, i32]),
+    "zllm_model_slot_save": (i32, [vp, i32, i32]),
+    "zllm_model_slot_restore": (i32, [vp, i32]),
+    "zllm_model_set_graphs": (i32, [vp, i32]),
+    "zllm_model_logits": (vp, [vp]),
+    "zllm_model_destroy": (None, [vp]),
 }
+
+
+class ModelConfig(C.Structure):
+    """zllm_model_config (include/zllm.h)"""
+    _fields_ = [(n, C.c_int) for n in ("n_embd", "n_layer", "n_ff", "n_head", "n_head_kv", "head_dim", "n_rot", "vocab",
+                                      "neox", "kv_f16", "ctx", "n_seq", "max_batch", "logits_batch")] + \
+               [("rms_eps", C.c_double), ("rope_base", C.c_double)]
+
+
+# tensor kinds (include/zllm.h)
+T_TOK_EMBD, T_OUTPUT, T_OUTPUT_NORM, T_ROPE_FREQS = 0, 1, 2, 3
+T_ATTN_NORM, T_WQ, T_WK, T_WV, T_WO, T_BQ, T_BK, T_BV, T_Q_NORM, T_K_NORM, T_FFN_NORM, T_GATE, T_UP, T_DOWN = range(10, 24)
 
 
 class AttnGeom(C.Structure):
