@@ -44,6 +44,7 @@ SIGNATURES = {
     "zllm_rope_tables": (i32, [vp, i32, C.c_double, i32, vp, vp, vp]),
     "zllm_qkv_append": (i32, [vp, vp, i32, vp, i64, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "zllm_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, vp, vp]),
+    "zllm_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, vp, vp]),
     "zllm_kv_import": (i32, [vp, vp, vp, i32, vp, vp]),
     "zllm_kv_export": (i32, [vp, vp, vp, i32, vp, vp]),
     "zllm_kv_copy": (i32, [vp, vp, vp, i64, vp, i64, i32, vp]),
