@@ -4,7 +4,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 One step = one pass of the hot path over one activation: the activation quantization
-(quantizeAct) and the Q4_K GEMV of a 4096 x 4096 weight (config 0).  Weights rotate over 32
+(quantizeAct) and the Q4_K GEMV of a 4096 x 4096 weight (config 0), one kernel (the GEMV
+quantizes the f32 activation itself).  Weights rotate over 32
 seeded copies (302 MB, larger than the 126 MB L2), so every step streams its weight from HBM.
 `value` is the whole-job throughput in GB/s of algorithmic bytes (weight + x + y = 9,469,952 B
 per step) with everything resident in HBM; `e2e` is the same metric through the public host-
@@ -215,13 +216,16 @@ def run_ours(args, world, rank, local):
     stream = torch.cuda.Stream(device=dev)
 
     def enqueue(n, with_quant=True, offset=0):
+        """n steps; with_quant: f32 activation in (quantized inside the GEMV), else the pre-quantized one."""
         s = C.c_void_p(stream.cuda_stream)
         for i in range(n):
             j = (i + offset) % NCOPY
             if with_quant:
-                check(L.zllm_quantize_act(ctx.h, P(x), COLS, 1, P(xq), P(xd), P(xs), s), ctx.h)
-            check(L.zllm_mm(ctx.h, weights[j].h, P(xq), P(xd), P(xs), None, 1, C.c_void_p(y[j].data_ptr()), ROWS,
-                            None, s), ctx.h)
+                check(L.zllm_mm(ctx.h, weights[j].h, None, None, None, P(x), 1, C.c_void_p(y[j].data_ptr()), ROWS,
+                                None, s), ctx.h)
+            else:
+                check(L.zllm_mm(ctx.h, weights[j].h, P(xq), P(xd), P(xs), None, 1, C.c_void_p(y[j].data_ptr()), ROWS,
+                                None, s), ctx.h)
 
     def graph(n, with_quant=True):
         enqueue(2, with_quant)                      # set kernel attributes outside capture
@@ -245,14 +249,15 @@ def run_ours(args, world, rank, local):
             return float(t.item())
         return v
 
+    check(L.zllm_quantize_act(ctx.h, P(x), COLS, 1, P(xq), P(xd), P(xs), C.c_void_p(stream.cuda_stream)), ctx.h)
     if args.profile:
-        # plain launches (no graph) for an ncu capture: warm-up then `steps` quantize + GEMV pairs
+        # plain launches (no graph) for an ncu capture: warm-up then `steps` GEMV launches
         enqueue(args.warmup)
         enqueue(args.steps)
         torch.cuda.synchronize()
         ctx.sync()
         if rank == 0:
-            print(json.dumps({"profile_run": True, "launches": 2 * (args.warmup + args.steps)}))
+            print(json.dumps({"profile_run": True, "launches": args.warmup + args.steps}))
         ctx.close()
         return
 
@@ -276,7 +281,7 @@ def run_ours(args, world, rank, local):
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ctx.sync()
 
-    # ---------------------------------------------------------------- dominant kernel alone (roofline)
+    # ---------------------------------------------------------------- the same GEMV on a pre-quantized activation
     with torch.cuda.stream(stream):
         g_kern.replay()
         ev0.record(stream)
@@ -314,13 +319,15 @@ def run_ours(args, world, rank, local):
     if rank == 0:
         peak, peak_kind = measured_peaks()
         value = ALGO_BYTES * args.steps * world / (ms / 1e3) / 1e9
-        achieved = ALGO_BYTES / (kern_ms / 1e3) / 1e9
+        # every launch of the timed region is the one GEMV kernel: its average duration is ms / steps
+        achieved = ALGO_BYTES / (ms / args.steps / 1e3) / 1e9
         traffic = traffic_from_profile()
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8/f64", "data": "synthetic",
-            "config": {"workload": "config0: Q4_K GEMV 4096x4096, batch 1 (quantizeAct + matvec per step)", "rows": ROWS,
+            "config": {"workload": "config0: Q4_K GEMV 4096x4096, batch 1 (quantizeAct fused into the matvec kernel)",
+                       "rows": ROWS,
                        "cols": COLS, "weight_copies": NCOPY, "seed": SEED, "parallelism": f"replicas{world}",
                        "l2": f"inputs larger than L2: {NCOPY} rotating weight copies ({NCOPY * W_BYTES / 1e6:.0f} MB)",
                        "algorithmic_bytes_per_step": ALGO_BYTES, "graph": "CUDA graph of all timed steps, PDL edges"},
@@ -329,9 +336,11 @@ def run_ours(args, world, rank, local):
                     "steps": e_steps, "api": "zllm_matvec (host buffers, pinned)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "gemv_kernel<FmtK45<false>>", "kernel_us": round(kern_ms * 1e3, 3),
+                         "kernel": "kq_gemv_kernel<Q4_K, one token> (in-kernel activation quantization)",
+                         "kernel_us": round(ms / args.steps * 1e3, 3),
+                         "prequantized_kernel_us": round(kern_ms * 1e3, 3),
                          "algorithmic_bytes_per_launch": ALGO_BYTES},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": args.steps,
             "clocks": clocks.summary(),
             "parity": {"max_rel_err_vs_oracle": parity, "rows_checked": 256},
         }

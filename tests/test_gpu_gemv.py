@@ -105,15 +105,59 @@ def test_batched_equals_per_token_and_residual(ctx):
     assert np.array_equal(out.cpu().numpy(), want)
 
 
+KQ = [(ggml.Q4_K, 4096, 4096), (ggml.Q5_K, 520, 2048), (ggml.Q6_K, 700, 12288), (ggml.Q6_K, 40, 25600),
+      (ggml.Q4_K, 1000, 5120)]
+
+
+@pytest.mark.parametrize("t,rows,cols", KQ, ids=[f"{ggml.type_name(t)}-{r}x{c}" for t, r, c in KQ])
+def test_kquant_batches_bit_identical_to_single_tokens(ctx, t, rows, cols):
+    """The tensor-core GEMV adds each token's block terms in an order fixed by the matrix shape: a
+    token's outputs are the same bits alone (block-diagonal MMA) or in a batch of 2..8 (token MMA),
+    and batches above 8 run in groups."""
+    rng = np.random.default_rng(rows + cols + t)
+    wt = synth.tensor(t, rows, cols, rng, "bench")
+    w = Weight.from_tensor(ctx, wt)
+    X = rng.standard_normal((17, cols)).astype(np.float32)
+    X[3] *= 1e-3
+    singles = np.stack([matvec(w, Act(ctx, X[i])).cpu().numpy().ravel() for i in range(17)])
+    for n in (2, 5, 8, 17):
+        Y = matvec(w, Act(ctx, X[:n])).cpu().numpy()
+        ctx.sync()
+        assert np.array_equal(Y, singles[:n]), (n, np.argwhere(Y != singles[:n])[:5])
+    for i in (0, 3, 16):
+        want = O.matvec(t, wt["data"], rows, cols, X[i], nthreads=8)
+        assert _rel(singles[i], want) <= 1e-6
+
+
+@pytest.mark.parametrize("t", [ggml.Q4_K, ggml.Q5_K, ggml.Q6_K])
+def test_in_kernel_quantization_bit_identical(ctx, t):
+    """A one-token k-quant GEMV given the f32 activation quantizes it itself, bit-exactly."""
+    rng = np.random.default_rng(t)
+    rows, cols = 333, 4096
+    wt = synth.tensor(t, rows, cols, rng, "bench")
+    w = Weight.from_tensor(ctx, wt)
+    x = rng.standard_normal(cols).astype(np.float32)
+    x[:64] *= 1e-30
+    x[100] = np.nan
+    x[300] = np.inf
+    x[640:672] = 0
+    x[700:732] = np.float32(2.5)
+    a = matvec(w, Act(ctx, x)).cpu().numpy()
+    b = matvec(w, Act(ctx, x), fused_quant=True).cpu().numpy()
+    ctx.sync()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
 def test_host_entry_point_equals_device_path(ctx):
     rng = np.random.default_rng(6)
-    for t in (ggml.Q6_K, ggml.F16):
+    for t in (ggml.Q6_K, ggml.F16, ggml.Q4_K):
         wt = synth.tensor(t, 300, 1024, rng, "bench")
         w = Weight.from_tensor(ctx, wt)
-        X = rng.standard_normal((2, 1024)).astype(np.float32)
-        a = matvec_host(w, X)
-        b = matvec(w, Act(ctx, X)).cpu().numpy()
-        assert np.array_equal(a, b)
+        for n in (1, 2):
+            X = rng.standard_normal((n, 1024)).astype(np.float32)
+            a = matvec_host(w, X)
+            b = matvec(w, Act(ctx, X)).cpu().numpy()
+            assert np.array_equal(a, b)
 
 
 def test_rejects_bad_shapes(ctx):

@@ -202,9 +202,15 @@ extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, cons
   if (!c || !w || !y || ntok < 1) { zllm_set_error(c, "zllm_mm: bad argument"); return ZLLM_E_ARG; }
   if (!w->m.data) { zllm_set_error(c, "zllm_mm: the weight's context was destroyed"); return ZLLM_E_STATE; }
   const bool q = type_quantized(w->m.type);
-  if (q ? (!xq || !xd || !xs) : !x) { zllm_set_error(c, "zllm_mm: missing activation for this weight type"); return ZLLM_E_ARG; }
+  // quantized weights read (xq, xd, xs); a one-token k-quant product may pass x alone instead and
+  // the GEMV quantizes it
+  const bool fused = q && !xq && x && ntok == 1 && kq_type(w->m.type);
+  if (q ? (!fused && (!xq || !xd || !xs)) : !x) {
+    zllm_set_error(c, "zllm_mm: missing activation for this weight type");
+    return ZLLM_E_ARG;
+  }
   if (ntok > 1 && y_stride < w->m.rows) { zllm_set_error(c, "zllm_mm: y_stride < rows"); return ZLLM_E_ARG; }
-  ActView a{xq, xd, xs, x, w->m.cols};
+  ActView a{fused ? nullptr : xq, xd, xs, x, w->m.cols};
   const char *why = "";
   cudaStream_t st = pick(c, stream);
   cudaError_t e = launch_gemv(w->m, a, ntok, y, y_stride, y_add, c->status_dev, c->num_sms, st, pdl_ok(st), &why);
@@ -225,11 +231,13 @@ extern "C" int zllm_matvec(zllm_ctx *c, const zllm_weight *w, const float *x_hos
   if ((rc = zllm_scratch(c, 4, sizeof(float) * R * ntok, &y_))) return rc;
   cudaError_t e = cudaMemcpyAsync(xs_, x_host, sizeof(float) * K * ntok, cudaMemcpyHostToDevice, c->stream);
   if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(x)");
-  const bool q = type_quantized(w->m.type);
-  if (q && (rc = zllm_quantize_act(c, (const float *)xs_, K, ntok, (int8_t *)xq_, (float *)xd_, (int32_t *)xsum_, c->stream)))
+  // one token on a k-quant: the GEMV quantizes x itself
+  const bool q = type_quantized(w->m.type), fused = q && ntok == 1 && kq_type(w->m.type);
+  if (q && !fused &&
+      (rc = zllm_quantize_act(c, (const float *)xs_, K, ntok, (int8_t *)xq_, (float *)xd_, (int32_t *)xsum_, c->stream)))
     return rc;
-  if ((rc = zllm_mm(c, w, (const int8_t *)xq_, (const float *)xd_, (const int32_t *)xsum_, (const float *)xs_, ntok,
-                    (float *)y_, R, nullptr, c->stream)))
+  if ((rc = zllm_mm(c, w, fused ? nullptr : (const int8_t *)xq_, (const float *)xd_, (const int32_t *)xsum_,
+                    (const float *)xs_, ntok, (float *)y_, R, nullptr, c->stream)))
     return rc;
   e = cudaMemcpyAsync(y_host, y_, sizeof(float) * R * ntok, cudaMemcpyDeviceToHost, c->stream);
   if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(y)");

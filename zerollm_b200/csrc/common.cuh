@@ -63,6 +63,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   }
   return true;
 }
+// The same with the 2 s limit counted from the first unsuccessful try: the clock (a slow read) is
+// only consulted when the phase is not already complete.
+__device__ __forceinline__ bool mbar_wait_lazy(uint64_t *bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
+  return mbar_wait_bounded(bar, parity, deadline);
+}
 
 // ---------------------------------------------------------------------------- 1D bulk copy
 // global -> shared, completion counted on `bar` (bytes and both addresses 16-byte aligned).
@@ -94,6 +101,41 @@ __device__ __forceinline__ bool named_sync_or(uint32_t id, uint32_t nthreads, bo
       : "memory");
   return r != 0;
 }
+
+// ---------------------------------------------------------------------------- shared / global loads
+// shared-memory loads by 32-bit shared-window address (volatile: never hoisted above an mbarrier wait)
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_f(uint32_t a) { return __uint_as_float(lds32(a)); }
+__device__ __forceinline__ float2 lds_f2(uint32_t a) {
+  const uint2 v = lds64(a);
+  return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+}
+__device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+// int32 -> double without the conversion pipe: (2^52 + 2^31 + v) - (2^52 + 2^31) is exact in double.
+// i2d_biased takes v + 2^31 (mod 2^32), which an integer multiply-add produces for free.
+__device__ __forceinline__ double i2d_biased(uint32_t v_plus_2p31) {
+  return __dsub_rn(__hiloint2double(0x43300000, (int)v_plus_2p31), 4503601774854144.0);
+}
+__device__ __forceinline__ double i2d_exact(int v) { return i2d_biased((uint32_t)v + 0x80000000u); }
 
 // ---------------------------------------------------------------------------- numbers
 __device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }

@@ -1,10 +1,10 @@
-// Decode GEMV (one activation vector x one weight matrix) for every hot-path ggml type, and the
-// load-time repack of raw GGUF rows into the layout these kernels read.
+// Decode GEMV (one activation vector x one weight matrix) for the legacy quant and float ggml types
+// (Q8_0, Q4_0, Q5_0, F16, BF16, F32), the dispatch by type (k-quants go to gemv_kq.cu), and the
+// load-time repack of raw GGUF rows into the layout the kernels read.
 //
-// Replaces the reference's per-type matvec kernels: src/compute/ref-kernels.js:127-302 (oracle)
-// and the WASM `matvec_*` exports (src/compute/wasm/kernels.js:30-114,
-// src/compute/wasm/kquant-kernels.js:337-504), dispatched by ggml type as in
-// src/compute/worker.js:184-197 / :251-270.
+// Replaces the reference's per-type matvec kernels: src/compute/ref-kernels.js:127-195, :278-302
+// (oracle) and the WASM `matvec_*` exports (src/compute/wasm/kernels.js:30-114), dispatched by ggml
+// type as in src/compute/worker.js:184-197 / :251-270.
 //
 // Structure (one persistent CTA per SM):
 //   * a producer thread streams whole chunks of consecutive rows HBM -> shared memory with 1D bulk
@@ -22,180 +22,17 @@
 //     group (shared memory) in a fixed order, so results are deterministic.
 #include "common.cuh"
 #include "internal.h"
+#include "kq_layout.h"
 
 namespace zllm {
 
 // ============================================================================ helpers
-__device__ __forceinline__ uint32_t byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xffu; }
-// shared-memory loads by 32-bit shared-window address (volatile: never hoisted above an mbarrier wait)
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint2 lds64(uint32_t a) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-  unsigned short v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
-// int32 -> double without the conversion pipe: (2^52 + 2^31 + v) - (2^52 + 2^31) is exact in double.
-// i2d_biased takes v + 2^31 (mod 2^32), which an integer multiply-add produces for free.
-__device__ __forceinline__ double i2d_biased(uint32_t v_plus_2p31) {
-  return __dsub_rn(__hiloint2double(0x43300000, (int)v_plus_2p31), 4503601774854144.0);
-}
-__device__ __forceinline__ double i2d_exact(int v) { return i2d_biased((uint32_t)v + 0x80000000u); }
-// sum of 4 (unsigned byte of a) x (signed byte of b) products plus c
-__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
 // 4 bits -> bit 0 of each of 4 bytes
 __device__ __forceinline__ uint32_t spread4(uint32_t t) { return (t * 0x00204081u) & 0x01010101u; }
 
 // ============================================================================ formats
 // Each format: Acc (partial sum type), units(K), Act (per-unit activation registers),
 // load(Act&, ActView, u) and dot(Act, row_in_smem, u, nb, Acc&) which adds the unit's terms.
-
-// ---- Q4_K / Q5_K: 256-value super-blocks, unit = (super-block sb, chunk c) = 64 values
-// ref-kernels.js:196-242.  Device layout = raw GGUF (144 / 176 byte blocks, 16-byte aligned).
-template <bool FIVE>
-struct FmtK45 {
-  using Acc = double;
-  static constexpr bool QACT = true;
-  static constexpr int BS = FIVE ? 176 : 144;
-  static constexpr int QS = FIVE ? 48 : 16;
-  // activation registers of one unit, plus the lane-constant pieces of its addressing
-  struct Act { uint32_t lo[8], hi[8]; double xd0, xd1; int xsi0, xsi1, off, c; };
-  static __host__ __device__ int units(int64_t k) { return (int)(k / 64); }
-  __device__ static void load(Act &a, const ActView &v, int u) {
-    const uint8_t *q = reinterpret_cast<const uint8_t *>(v.xq) + (int64_t)u * 64;
-    uint4 t0 = ldg128(q), t1 = ldg128(q + 16), t2 = ldg128(q + 32), t3 = ldg128(q + 48);
-    a.lo[0] = t0.x; a.lo[1] = t0.y; a.lo[2] = t0.z; a.lo[3] = t0.w;
-    a.lo[4] = t1.x; a.lo[5] = t1.y; a.lo[6] = t1.z; a.lo[7] = t1.w;
-    a.hi[0] = t2.x; a.hi[1] = t2.y; a.hi[2] = t2.z; a.hi[3] = t2.w;
-    a.hi[4] = t3.x; a.hi[5] = t3.y; a.hi[6] = t3.z; a.hi[7] = t3.w;
-    a.xd0 = (double)__ldg(v.xd + 2 * u);
-    a.xd1 = (double)__ldg(v.xd + 2 * u + 1);
-    a.xsi0 = __ldg(v.xs + 2 * u);
-    a.xsi1 = __ldg(v.xs + 2 * u + 1);
-    a.off = (u >> 2) * BS;
-    a.c = u & 3;
-  }
-  __device__ static void dot(const Act &a, uint32_t row, int u, int nb, Acc &acc) {
-    const int c = a.c;
-    const uint32_t blk = row + a.off;
-    const uint4 h = lds128(blk);
-    const uint4 q0 = lds128(blk + QS + c * 32), q1 = lds128(blk + QS + c * 32 + 16);
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    int lo0 = 0, lo1 = 0, hi0 = 0, hi1 = 0;      // two chains each: shorter dependency paths
-    int hi;
-    if (FIVE) {
-      const uint4 e0 = lds128(blk + 16), e1 = lds128(blk + 32);
-      const uint32_t e[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const uint32_t vl = (w[i] & 0x0f0f0f0fu) | (((e[i] >> (2 * c)) & 0x01010101u) << 4);
-        const uint32_t vh = ((w[i] >> 4) & 0x0f0f0f0fu) | (((e[i] >> (2 * c + 1)) & 0x01010101u) << 4);
-        if (i & 1) { lo1 = __dp4a((int)vl, (int)a.lo[i], lo1); hi1 = __dp4a((int)vh, (int)a.hi[i], hi1); }
-        else { lo0 = __dp4a((int)vl, (int)a.lo[i], lo0); hi0 = __dp4a((int)vh, (int)a.hi[i], hi0); }
-      }
-      hi = hi0 + hi1;
-    } else {
-      // high nibbles are dotted in place (16 x the nibble, unsigned bytes x signed activations)
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        if (i & 1) { lo1 = dp4a_us(w[i] & 0x0f0f0f0fu, a.lo[i], lo1); hi1 = dp4a_us(w[i] & 0xf0f0f0f0u, a.hi[i], hi1); }
-        else { lo0 = dp4a_us(w[i] & 0x0f0f0f0fu, a.lo[i], lo0); hi0 = dp4a_us(w[i] & 0xf0f0f0f0u, a.hi[i], hi0); }
-      }
-      hi = (hi0 + hi1) >> 4;                     // exact: the sum is a multiple of 16
-    }
-    const int lo = lo0 + lo1;
-    // scales and mins of sub-blocks 2c, 2c+1: the load-time repack stores them as one 24-bit field per
-    // chunk c at bit 24c of header bytes 4..15 (sc0 | sc1 << 6 | mn0 << 12 | mn1 << 18)
-    const uint32_t wlo = c < 2 ? h.y : (c == 2 ? h.z : h.w);
-    const uint32_t whi = c == 0 ? h.y : (c == 1 ? h.z : (c == 2 ? h.w : 0u));
-    const uint32_t F = __funnelshift_r(wlo, whi, (24 * c) & 31);
-    const int sc0 = F & 63, sc1 = (F >> 6) & 63, mn0 = (F >> 12) & 63, mn1 = (F >> 18) & 63;
-    const double d = (double)h2f(h.x & 0xffffu), dmin = (double)h2f(h.x >> 16);
-    // acc += xd * (d*sc*lo - dmin*mn*xs).  sc*lo and mn*xs are exact 32-bit integers, so d*(sc*lo) and
-    // dmin*(mn*xs) equal the JS products (d*sc)*lo and (dmin*mn)*xs exactly; the fused multiply-add
-    // rounds exactly once where the JS subtraction rounds, and the scaling by xd and the accumulation
-    // round like the JS.
-    const double p0 = i2d_biased((uint32_t)(sc0 * lo) + 0x80000000u), p1 = i2d_biased((uint32_t)(sc1 * hi) + 0x80000000u);
-    const double m0 = __dmul_rn(dmin, i2d_biased((uint32_t)(mn0 * a.xsi0) + 0x80000000u));
-    const double m1 = __dmul_rn(dmin, i2d_biased((uint32_t)(mn1 * a.xsi1) + 0x80000000u));
-    const double t0 = __dmul_rn(a.xd0, __fma_rn(d, p0, -m0));
-    const double t1 = __dmul_rn(a.xd1, __fma_rn(d, p1, -m1));
-    acc = __dadd_rn(__dadd_rn(acc, t0), t1);
-  }
-};
-
-// ---- Q6_K: unit = (sb, half h, lane group g) = 64 values in four 16-value scale groups
-// ref-kernels.js:243-277.  Device layout per row: ql[128*nb] | qh[64*nb] | scales[16*nb] | d[2*nb].
-struct FmtQ6K {
-  using Acc = double;
-  static constexpr bool QACT = true;
-  struct Act { uint32_t x[4][4]; int xsum[4]; double xd[4]; };
-  static __host__ __device__ int units(int64_t k) { return (int)(k / 64); }
-  __device__ static void load(Act &a, const ActView &v, int u) {
-    const int sb = u >> 2, h = (u >> 1) & 1, g = u & 1;
-    const uint8_t *q = reinterpret_cast<const uint8_t *>(v.xq) + (int64_t)sb * 256 + h * 128 + g * 16;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      uint4 t = ldg128(q + 32 * k);
-      a.x[k][0] = t.x; a.x[k][1] = t.y; a.x[k][2] = t.z; a.x[k][3] = t.w;
-      int s = 0;
-#pragma unroll
-      for (int i = 0; i < 4; i++) s = __dp4a((int)a.x[k][i], 0x01010101, s);
-      a.xsum[k] = s;
-      a.xd[k] = (double)__ldg(v.xd + sb * 8 + h * 4 + k);
-    }
-  }
-  __device__ static void dot(const Act &a, uint32_t row, int u, int nb, Acc &acc) {
-    const int sb = u >> 2, h = (u >> 1) & 1, g = u & 1;
-    const uint32_t ql = row + sb * 128 + h * 64 + g * 16;
-    const uint4 A = lds128(ql), B = lds128(ql + 32);
-    const uint4 H = lds128(row + 128 * nb + sb * 64 + h * 32 + g * 16);
-    const uint2 S = lds64(row + 192 * nb + sb * 16 + h * 8);
-    const float d = h2f(lds16(row + 208 * nb + sb * 2));
-    const uint32_t aw[4] = {A.x, A.y, A.z, A.w}, bw[4] = {B.x, B.y, B.z, B.w}, hw[4] = {H.x, H.y, H.z, H.w};
-    int gs[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const uint32_t q1 = (aw[i] & 0x0f0f0f0fu) | ((hw[i] & 0x03030303u) << 4);
-      const uint32_t q2 = (bw[i] & 0x0f0f0f0fu) | ((hw[i] & 0x0c0c0c0cu) << 2);
-      const uint32_t q3 = ((aw[i] >> 4) & 0x0f0f0f0fu) | (hw[i] & 0x30303030u);
-      const uint32_t q4 = ((bw[i] >> 4) & 0x0f0f0f0fu) | ((hw[i] >> 2) & 0x30303030u);
-      gs[0] = __dp4a((int)q1, (int)a.x[0][i], gs[0]);
-      gs[1] = __dp4a((int)q2, (int)a.x[1][i], gs[1]);
-      gs[2] = __dp4a((int)q3, (int)a.x[2][i], gs[2]);
-      gs[3] = __dp4a((int)q4, (int)a.x[3][i], gs[3]);
-    }
-    const double dd = (double)d;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int gsum = gs[k] - 32 * a.xsum[k];                 // sum((q - 32) * x), exact
-      const uint32_t sw = k < 2 ? S.x : S.y;
-      const int scale = (int)(int8_t)byte_of(sw, (2 * k + g) & 3);
-      // acc += xd * d * scale * gsum (ref-kernels.js:271): xd*d (35 bits) and (xd*d)*scale (43 bits) are
-      // exact in double, so the JS left-to-right product equals (xd*d) * (scale*gsum) rounded once.
-      const double t = __dmul_rn(__dmul_rn(a.xd[k], dd), i2d_exact(scale * gsum));
-      acc = __dadd_rn(acc, t);
-    }
-  }
-};
 
 // ---- Q8_0 / Q4_0 / Q5_0: unit = one 32-value block.  acc += s * d * xd  (ref-kernels.js:132-195)
 // Device layouts per row: Q8_0 qs[32*nb] | d[2*nb];  Q4_0 qs[16*nb] | d[2*nb];  Q5_0 qs[16*nb] | qh[4*nb] | d[2*nb].
@@ -529,10 +366,9 @@ __global__ void repack_kernel(int type, const uint8_t *raw, int64_t raw_row, uin
           d[i] = (uint8_t)(f >> (8 * k));
           continue;
         }
+        o = kq_dev_offset(type, i, nb);
       } else if (type == T_Q6_K) {
-        const int b = (int)(i / 210), e = (int)(i % 210);
-        o = e < 128 ? b * 128 + e : e < 192 ? 128LL * nb + b * 64 + (e - 128)
-                                            : e < 208 ? 192LL * nb + b * 16 + (e - 192) : 208LL * nb + b * 2 + (e - 208);
+        o = kq_dev_offset(type, i, nb);
       } else if (type == T_Q8_0) {
         const int b = (int)(i / 34), e = (int)(i % 34);
         o = e < 2 ? 32LL * nb + b * 2 + e : b * 32 + (e - 2);
@@ -694,6 +530,7 @@ static cudaError_t launch_fmt(const GemvArgs &a, const GemvPlan &pl, cudaStream_
 
 cudaError_t launch_gemv(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
                         const float *y_add, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why) {
+  if (kq_type(m.type)) return launch_gemv_kq(m, act, ntok, y, y_stride, y_add, status, num_sms, s, pdl, why);
   GemvPlan pl;
   if (!plan_gemv(m, num_sms, &pl, why)) return cudaErrorInvalidValue;
   const int64_t nbk = (m.type == T_Q4_K || m.type == T_Q5_K || m.type == T_Q6_K) ? m.cols / 256 : m.cols / 32;
@@ -719,9 +556,6 @@ cudaError_t launch_gemv(const DevMatrix &m, const ActView &act, int ntok, float 
     a.units = pl.units; a.g = pl.g; a.uw = pl.uw; a.cr = pl.cr; a.nsg = pl.nsg; a.stage_bytes = pl.stage_bytes;
     cudaError_t e;
     switch (m.type) {
-      case T_Q4_K: e = launch_fmt<FmtK45<false>>(a, pl, s, pdl); break;
-      case T_Q5_K: e = launch_fmt<FmtK45<true>>(a, pl, s, pdl); break;
-      case T_Q6_K: e = launch_fmt<FmtQ6K>(a, pl, s, pdl); break;
       case T_Q8_0: e = launch_fmt<FmtQ0<T_Q8_0>>(a, pl, s, pdl); break;
       case T_Q4_0: e = launch_fmt<FmtQ0<T_Q4_0>>(a, pl, s, pdl); break;
       case T_Q5_0: e = launch_fmt<FmtQ0<T_Q5_0>>(a, pl, s, pdl); break;

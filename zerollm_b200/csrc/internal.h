@@ -92,5 +92,10 @@ cudaError_t launch_quantize(const float *x, int64_t k, int ntok, int8_t *xq, flo
 cudaError_t launch_gemv(const DevMatrix &m, const ActView &a, int ntok, float *y, int64_t y_stride, const float *y_add,
                         unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why);
 bool plan_gemv(const DevMatrix &m, int num_sms, GemvPlan *p, const char **why);
+// k-quant (Q4_K / Q5_K / Q6_K) GEMV on the tensor cores (gemv_kq.cu).  With one token, act.xq may be
+// NULL and act.x the f32 activation: the kernel quantizes it itself.
+bool kq_type(int type);
+cudaError_t launch_gemv_kq(const DevMatrix &m, const ActView &a, int ntok, float *y, int64_t y_stride,
+                           const float *y_add, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why);
 
 }  // namespace zllm

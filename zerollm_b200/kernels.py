@@ -134,15 +134,20 @@ class Act:
         return self
 
 
-def matvec(w: Weight, a: Act, y=None, y_add=None, stream=None):
-    """y[t, r] = (y_add[t, r] +) dot(W[r], x[t]) on the device; returns y [ntok, rows]."""
+def matvec(w: Weight, a: Act, y=None, y_add=None, stream=None, fused_quant: bool = False):
+    """y[t, r] = (y_add[t, r] +) dot(W[r], x[t]) on the device; returns y [ntok, rows].
+
+    ``fused_quant`` (one token, k-quant weight) passes the f32 activation alone and lets the GEMV
+    quantize it."""
     torch = _torch()
     if a.k != w.cols:
         raise ValueError(f"activation length {a.k} != weight cols {w.cols}")
     if y is None:
         y = torch.empty((a.ntok, w.rows), dtype=torch.float32, device=a.x.device)
     st = stream if stream is not None else torch.cuda.current_stream(a.x.device).cuda_stream
-    if w.type in ggml.QUANTIZED:
+    if w.type in ggml.QUANTIZED and fused_quant:
+        args = (None, None, None, _ptr(a.x))
+    elif w.type in ggml.QUANTIZED:
         a.quant(st)
         args = (_ptr(a.q), _ptr(a.d), _ptr(a.s), None)
     else:
