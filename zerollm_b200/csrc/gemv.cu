@@ -1,10 +1,10 @@
-// Decode GEMV (one activation vector x one weight matrix) for the legacy quant and float ggml types
-// (Q8_0, Q4_0, Q5_0, F16, BF16, F32), the dispatch by type (k-quants go to gemv_kq.cu), and the
-// load-time repack of raw GGUF rows into the layout the kernels read.
+// Decode GEMV (one activation vector x one weight matrix) for the legacy quant types (Q8_0, Q4_0,
+// Q5_0), the dispatch by ggml type (k-quants go to gemv_kq.cu, float types to gemv_float.cu), and
+// the load-time repack of raw GGUF rows into the layout the kernels read.
 //
-// Replaces the reference's per-type matvec kernels: src/compute/ref-kernels.js:127-195, :278-302
-// (oracle) and the WASM `matvec_*` exports (src/compute/wasm/kernels.js:30-114), dispatched by ggml
-// type as in src/compute/worker.js:184-197 / :251-270.
+// Replaces the reference's per-type matvec kernels: src/compute/ref-kernels.js:127-195 (oracle)
+// and the WASM `matvec_*` exports (src/compute/wasm/kernels.js:30-114), dispatched by ggml type as
+// in src/compute/worker.js:184-197 / :251-270.
 //
 // Structure (one persistent CTA per SM):
 //   * a producer thread streams whole chunks of consecutive rows HBM -> shared memory with 1D bulk
@@ -79,39 +79,6 @@ struct FmtQ0 {
     }
     // acc += s * d * xd (ref-kernels.js:146): s*d is exact in double, the product by xd rounds once
     acc = __dadd_rn(acc, __dmul_rn(__dmul_rn(i2d_exact(s), (double)d), a.xd));
-  }
-};
-
-// ---- F16 / BF16 / F32: unit = 16 bytes of weights; activations stay f32 (ref-kernels.js:278-299).
-// Partial sums accumulate in f32 with fused multiply-add (the reference accumulates in double;
-// the difference is at the 1e-7 relative level).
-template <int T>
-struct FmtFloat {
-  using Acc = float;
-  static constexpr bool QACT = false;
-  static constexpr int PER = T == T_F32 ? 4 : 8;
-  struct Act { float x[PER]; };
-  static __host__ __device__ int units(int64_t k) { return (int)(k / PER); }
-  __device__ static void load(Act &a, const ActView &v, int u) {
-    const float *p = v.x + (int64_t)u * PER;
-#pragma unroll
-    for (int i = 0; i < PER; i++) a.x[i] = __ldg(p + i);
-  }
-  __device__ static void dot(const Act &a, uint32_t row, int u, int nb, Acc &acc) {
-    const uint4 q = lds128(row + u * 16);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    if (T == T_F32) {
-#pragma unroll
-      for (int i = 0; i < 4; i++) acc = __fmaf_rn(__uint_as_float(w[i]), a.x[i], acc);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const float lo = T == T_F16 ? h2f(w[i] & 0xffffu) : bf2f(w[i] & 0xffffu);
-        const float hi = T == T_F16 ? h2f(w[i] >> 16) : bf2f(w[i] >> 16);
-        acc = __fmaf_rn(lo, a.x[2 * i], acc);
-        acc = __fmaf_rn(hi, a.x[2 * i + 1], acc);
-      }
-    }
   }
 };
 
@@ -531,6 +498,7 @@ static cudaError_t launch_fmt(const GemvArgs &a, const GemvPlan &pl, cudaStream_
 cudaError_t launch_gemv(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
                         const float *y_add, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why) {
   if (kq_type(m.type)) return launch_gemv_kq(m, act, ntok, y, y_stride, y_add, status, num_sms, s, pdl, why);
+  if (float_type(m.type)) return launch_gemv_float(m, act, ntok, y, y_stride, y_add, num_sms, s, pdl, why);
   GemvPlan pl;
   if (!plan_gemv(m, num_sms, &pl, why)) return cudaErrorInvalidValue;
   const int64_t nbk = (m.type == T_Q4_K || m.type == T_Q5_K || m.type == T_Q6_K) ? m.cols / 256 : m.cols / 32;
@@ -559,9 +527,6 @@ cudaError_t launch_gemv(const DevMatrix &m, const ActView &act, int ntok, float 
       case T_Q8_0: e = launch_fmt<FmtQ0<T_Q8_0>>(a, pl, s, pdl); break;
       case T_Q4_0: e = launch_fmt<FmtQ0<T_Q4_0>>(a, pl, s, pdl); break;
       case T_Q5_0: e = launch_fmt<FmtQ0<T_Q5_0>>(a, pl, s, pdl); break;
-      case T_F16: e = launch_fmt<FmtFloat<T_F16>>(a, pl, s, pdl); break;
-      case T_BF16: e = launch_fmt<FmtFloat<T_BF16>>(a, pl, s, pdl); break;
-      case T_F32: e = launch_fmt<FmtFloat<T_F32>>(a, pl, s, pdl); break;
       default: *why = "unsupported tensor type"; return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;

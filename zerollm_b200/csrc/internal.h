@@ -95,6 +95,10 @@ bool plan_gemv(const DevMatrix &m, int num_sms, GemvPlan *p, const char **why);
 // k-quant (Q4_K / Q5_K / Q6_K) GEMV on the tensor cores (gemv_kq.cu).  With one token, act.xq may be
 // NULL and act.x the f32 activation: the kernel quantizes it itself.
 bool kq_type(int type);
+// F16 / BF16 / F32 GEMV (gemv_float.cu)
+bool float_type(int type);
+cudaError_t launch_gemv_float(const DevMatrix &m, const ActView &a, int ntok, float *y, int64_t y_stride,
+                              const float *y_add, int num_sms, cudaStream_t s, bool pdl, const char **why);
 cudaError_t launch_gemv_kq(const DevMatrix &m, const ActView &a, int ntok, float *y, int64_t y_stride,
                            const float *y_add, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why);
 
