@@ -207,6 +207,14 @@ int zllm_model_forward(zllm_model *m, int seq, const int32_t *tokens, int n, int
 /* One token for each of n distinct sequences (batched decode); logits [n][vocab]. */
 int zllm_model_decode(zllm_model *m, const int32_t *seqs, const int32_t *tokens, int n, float *logits_host,
                       int32_t *argmax_host);
+/* Greedy generation on the device: `steps` passes, the first on `tokens`, each later one on the
+ * argmax of the previous pass's logits (src/model/generate.js:4-10 with greedy sampling), with no
+ * host round trip between passes.  seqs == NULL: one token (n == 1) continuing sequence `seq`;
+ * else one token for each of n distinct sequences.  out_host[steps][n] receives each pass's argmax
+ * (the next input).  The reference's generate() loop (src/model/generate.js:55-96) does the same
+ * with a host round trip per token. */
+int zllm_model_generate(zllm_model *m, int seq, const int32_t *seqs, const int32_t *tokens, int n, int steps,
+                        int32_t *out_host);
 /* Positions held by a sequence (PoolModel.pos). */
 int zllm_model_pos(const zllm_model *m, int seq);
 /* Roll back to n positions (truncate, pool.js:278-294: positional bookkeeping) / forget all. */

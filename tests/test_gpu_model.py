@@ -145,3 +145,35 @@ def test_pool_errors():
     m.close()
     with pytest.raises(ZllmError, match="model is closed"):
         m.forward(1)
+
+
+def test_generate_on_device_equals_host_loop():
+    """Greedy generation fed back on the device (zllm_model_generate) picks the same tokens as the
+    host loop of generate.js (forward, argmax, forward ...), alone and for several sequences."""
+    cfg, w = tiny("q4_k_m", seed=8)
+    a = CudaModel.create(cfg, w, ctx=64, kv="f16")
+    b = CudaModel.create(cfg, w, ctx=64, kv="f16")
+    for m in (a, b):
+        m.forwardBatch([1, 2, 3, 4], logits=False)
+    got = a.generate([5], 10)[:, 0]
+    tok, want = 5, []
+    for _ in range(10):
+        tok = int(np.argmax(b.forward(tok)))
+        want.append(tok)
+    assert [int(v) for v in got] == want
+    assert a.pos == b.pos == 14
+    multi = CudaModel.create(cfg, w, ctx=64, kv="f16", n_seq=3)
+    single = [CudaModel.create(cfg, w, ctx=64, kv="f16") for _ in range(3)]
+    prompts = [[1, 2, 3], [40, 41], [7, 8, 9, 10]]
+    for s, p in enumerate(prompts):
+        multi.forwardBatch(p, logits=False, seq=s)
+        single[s].forwardBatch(p, logits=False)
+    got = multi.generate([11, 12, 13], 6, seqs=[0, 1, 2])
+    for s, t0 in enumerate([11, 12, 13]):
+        tok, want = t0, []
+        for _ in range(6):
+            tok = int(np.argmax(single[s].forward(tok)))
+            want.append(tok)
+        assert [int(v) for v in got[:, s]] == want
+    with pytest.raises(ZllmError):
+        a.generate([1], 64)                                   # context full

@@ -67,15 +67,11 @@ extern "C" int zllm_qkv_append(zllm_ctx *c, const zllm_attn_geom *g, int ntok, c
   return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "qkv_append launch");
 }
 
-// context splits for a decode attention launch: about two CTAs per SM, at least one 64-row tile each
+// context splits of a decode attention launch: one per kAttnSplit positions of the longest sequence
 int zllm_attn_splits(const zllm_ctx *c, const zllm_attn_geom *g, int nseq, int max_pos) {
-  const int tiles = (max_pos + 63) / 64;
-  const int groups = nseq * g->n_head_kv;
-  int ns = (2 * c->num_sms + groups - 1) / groups;
-  if (ns > tiles) ns = tiles;
-  if (ns > 256) ns = 256;
-  if (ns < 1) ns = 1;
-  return ns;
+  (void)c; (void)g; (void)nseq;
+  const int ns = (max_pos + kAttnSplit - 1) / kAttnSplit;
+  return ns < 1 ? 1 : ns;
 }
 
 int zllm_attn_launch(zllm_ctx *c, const zllm_attn_geom *g, const float *q, const void *kcache, const void *vcache,

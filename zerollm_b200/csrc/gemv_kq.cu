@@ -370,6 +370,9 @@ struct KqArgs {
   const float *xd;
   const int32_t *xs;
   const float *x;       // f32 activation, quantized in the kernel when xq is NULL
+  const float *norm_w;  // with x: RMSNorm x with these weights before quantizing (NULL: none)
+  double norm_eps;
+  int swiglu;           // rows are (gate, up) pairs: y gets silu(gate) * up, one value per pair
   int64_t k;
   float *y;
   const float *y_add;
@@ -378,11 +381,34 @@ struct KqArgs {
   int x_off, part_off, bar_off;   // shared-memory regions
 };
 
+// RMSNorm scale 1 / sqrt(mean(x^2) + eps) of one token, with exactly the reduction of
+// rmsnorm_quant_kernel (ops.cu): 256 partial sums, sum i = t (mod 256) for thread t, then a
+// butterfly within each of 8 warps and one over the 8 warp sums -- so both give the same bits.
+template <int NT>
+__device__ double rms_scale(const float *x, int64_t n, double eps, int warp, int lane) {
+  static_assert(NT >= 256, "rms_scale needs 256 threads");
+  __shared__ double red[8];
+  double ss = 0.0;
+  if (threadIdx.x < 256)
+    for (int64_t i = threadIdx.x; i < n; i += 256) ss = __dadd_rn(ss, __dmul_rn((double)x[i], (double)x[i]));
+  if (warp < 8) {
+    ss = warp_sum_f64(ss);
+    if (lane == 0) red[warp] = ss;
+  }
+  __syncthreads();
+  double tot = lane < 8 ? red[lane] : 0.0;
+  tot = warp_sum_f64(tot);
+  return __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(tot, (double)n), eps)));
+}
+
 // Quantize one token's f32 activation into shared memory; bit-exact with quantize_act_kernel
 // (quantizeAct, src/compute/ref-kernels.js:44-62).  Lane pairs own a 32-value block, 16 values each.
+// With norm_w the values are first f32(x * s * w) with s the RMSNorm scale (ref-kernels.js:305-310),
+// as rmsnorm_quant_kernel writes them.
 template <int NT>
-__device__ void quantize_to_smem(const float *x, int64_t k, uint8_t *sxq, double *sxd, int32_t *sxs, int32_t *sxs16,
-                                 int warp, int lane) {
+__device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w, double eps, uint8_t *sxq, double *sxd,
+                                 int32_t *sxs, int32_t *sxs16, int warp, int lane) {
+  const double rs = norm_w ? rms_scale<NT>(x, k, eps, warp, lane) : 0.0;
   const int nhb = (int)(k / 16);
   for (int base = warp * 32; base < nhb; base += NT) {
     const int hb = base + lane;
@@ -394,6 +420,16 @@ __device__ void quantize_to_smem(const float *x, int64_t k, uint8_t *sxq, double
       for (int i = 0; i < 4; i++) {
         const float4 f = __ldg(p + i);
         v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+      }
+      if (norm_w) {
+        const float4 *wp = reinterpret_cast<const float4 *>(norm_w + (int64_t)hb * 16);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float4 f = __ldg(wp + i);
+          const float wv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+          for (int j = 0; j < 4; j++) v[4 * i + j] = __double2float_rn(__dmul_rn(__dmul_rn((double)v[4 * i + j], rs), (double)wv[j]));
+        }
       }
     } else {
 #pragma unroll
@@ -455,7 +491,9 @@ __global__ void __launch_bounds__(groups_of<TOK>() * kGroupWarps * 32, 2) kq_gem
   uint8_t *stages = smem + (size_t)grp * nst * kTile * p.pitch;
   double *part = reinterpret_cast<double *>(smem + p.part_off) + (size_t)grp * 2 * kSlots * kTile * NTP;  // [2][slot][row][NTP]
 
-  const int64_t r0 = (int64_t)blockIdx.x * p.rows / gridDim.x, r1 = (int64_t)(blockIdx.x + 1) * p.rows / gridDim.x;
+  // row range of this CTA (whole (gate, up) pairs with swiglu)
+  const int64_t pr = p.swiglu ? p.rows / 2 : p.rows, rm = p.swiglu ? 2 : 1;
+  const int64_t r0 = rm * ((int64_t)blockIdx.x * pr / gridDim.x), r1 = rm * ((int64_t)(blockIdx.x + 1) * pr / gridDim.x);
   const int ntile = (int)((r1 - r0 + kTile - 1) / kTile);
   const int gtiles = (ntile - grp + NG - 1) / NG;   // tiles grp, grp + NG, ...
   const int nunit = gtiles * p.nchunk;              // this group's units: (its k-th tile, chunk)
@@ -497,7 +535,7 @@ __global__ void __launch_bounds__(groups_of<TOK>() * kGroupWarps * 32, 2) kq_gem
     int32_t *sxs = reinterpret_cast<int32_t *>(sxd + p.k / 32);
     int32_t *sxs16 = FMT == T_Q6_K ? sxs + p.k / 32 : nullptr;
     if (p.xq == nullptr) {
-      quantize_to_smem<NT>(p.x, p.k, sxq, sxd, sxs, sxs16, warp, lane);
+      quantize_to_smem<NT>(p.x, p.k, p.norm_w, p.norm_eps, sxq, sxd, sxs, sxs16, warp, lane);
     } else {
       const uint4 *q4 = reinterpret_cast<const uint4 *>(p.xq);
       for (int i = threadIdx.x; i < p.k / 16; i += NT) {
@@ -588,9 +626,18 @@ __global__ void __launch_bounds__(groups_of<TOK>() * kGroupWarps * 32, 2) kq_gem
       if (c == p.nchunk - 1) {
         const int row = gtid / NTP, tok = gtid % NTP;
         const int64_t r = r0 + (int64_t)tile * kTile + row;
-        if (tok < p.ntok && r < r1) {
+        float out = __double2float_rn(tot);
+        if (p.swiglu) {
+          // rows r (gate) and r + 1 (up) are the adders gtid and gtid + NTP, in the same warp:
+          // silu in double, the product rounded to f32 (src/compute/worker.js:426, ref-kernels.js:322)
+          const float up = __shfl_xor_sync(TOK ? 0xffffffffu : 0x0000ffffu, out, NTP);
+          if ((row & 1) == 0 && tok < p.ntok && r < r1) {
+            const double z = out;
+            const double sl = __ddiv_rn(z, __dadd_rn(1.0, exp(-z)));
+            p.y[(int64_t)tok * p.y_stride + r / 2] = __double2float_rn(__dmul_rn(sl, (double)up));
+          }
+        } else if (tok < p.ntok && r < r1) {
           const int64_t o = (int64_t)tok * p.y_stride + r;
-          float out = __double2float_rn(tot);
           if (p.y_add) out = __fadd_rn(p.y_add[o], out);
           p.y[o] = out;
         }
@@ -678,6 +725,14 @@ bool kq_type(int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K; }
 
 cudaError_t launch_gemv_kq(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
                            const float *y_add, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why) {
+  return launch_gemv_kq_ex(m, act, ntok, y, y_stride, y_add, GemvFuse{}, status, num_sms, s, pdl, why);
+}
+
+cudaError_t launch_gemv_kq_ex(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
+                              const float *y_add, const GemvFuse &fz, unsigned *status, int num_sms, cudaStream_t s,
+                              bool pdl, const char **why) {
+  if (fz.norm_w && (act.xq || !act.x || ntok != 1)) { *why = "the fused RMSNorm takes one f32 token"; return cudaErrorInvalidValue; }
+  if (fz.swiglu && (m.rows % 2 || y_add)) { *why = "the SwiGLU epilogue takes (gate, up) row pairs and no residual"; return cudaErrorInvalidValue; }
   KqPlan pl1, plt;
   if (!plan_kq(m, num_sms, false, &pl1, why)) return cudaErrorInvalidValue;
   if (ntok > 1 && !plan_kq(m, num_sms, true, &plt, why)) return cudaErrorInvalidValue;
@@ -700,6 +755,7 @@ cudaError_t launch_gemv_kq(const DevMatrix &m, const ActView &act, int ntok, flo
     a.y = y + (int64_t)t0 * y_stride;
     a.y_add = y_add ? y_add + (int64_t)t0 * y_stride : nullptr;
     a.y_stride = y_stride;
+    a.norm_w = fz.norm_w; a.norm_eps = fz.eps; a.swiglu = fz.swiglu ? 1 : 0;
     a.status = status;
     a.x_off = pl.x_off; a.part_off = pl.part_off; a.bar_off = pl.bar_off;
     cudaError_t e;

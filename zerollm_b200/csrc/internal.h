@@ -57,6 +57,10 @@ struct QkvPostArgs {
   double eps;
 };
 
+// decode attention: positions per context split (fixed, so a query's partition depends on its own
+// length only); a launch needs ceil(max_pos / kAttnSplit) splits
+constexpr int kAttnSplit = 256;
+
 struct AttnArgs {
   const float *q;                  // [nseq][n_head][head_dim]
   const int *seq;                  // cache sequence of query b (NULL: b)
@@ -64,7 +68,7 @@ struct AttnArgs {
   int64_t seq_stride, head_stride;
   const int *npos;                 // positions to attend per sequence (device)
   float *out;                      // [nseq][n_head][head_dim]
-  float *partial;                  // [nseq * n_kv][nsplit][group * (head_dim + 2)] scratch
+  float *partial;                  // [nseq * n_kv][nsplit][group * (head_dim + 2)] scratch (nsplit >= ceil(npos / kAttnSplit))
   int *counters;                   // [nseq * n_kv], zero between launches
   unsigned *status;
   float scale;
@@ -84,6 +88,8 @@ cudaError_t launch_swiglu_quant(const float *gate, const float *up, int n, int n
                                 float *xd, int32_t *xs, cudaStream_t s, bool pdl);
 cudaError_t launch_embed(const DevMatrix &m, const int32_t *tokens, int ntok, float *x, cudaStream_t s, bool pdl);
 cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, cudaStream_t s, bool pdl);
+cudaError_t launch_advance(const int32_t *arg, int n, int32_t *tok, int32_t *pos, int32_t *npos, int32_t *out,
+                           int32_t *step, cudaStream_t s, bool pdl);
 
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s);
 cudaError_t launch_quantize(const float *x, int64_t k, int ntok, int8_t *xq, float *xd, int32_t *xs, unsigned *status,
@@ -101,5 +107,16 @@ cudaError_t launch_gemv_float(const DevMatrix &m, const ActView &a, int ntok, fl
                               const float *y_add, int num_sms, cudaStream_t s, bool pdl, const char **why);
 cudaError_t launch_gemv_kq(const DevMatrix &m, const ActView &a, int ntok, float *y, int64_t y_stride,
                            const float *y_add, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why);
+// Work fused into a k-quant GEMV: norm_w -- RMSNorm of the f32 activation before the in-kernel
+// quantization (one token); swiglu -- rows are interleaved (gate, up) pairs and y receives
+// f32(silu(gate) * up) per pair.
+struct GemvFuse {
+  const float *norm_w = nullptr;
+  double eps = 0.0;
+  bool swiglu = false;
+};
+cudaError_t launch_gemv_kq_ex(const DevMatrix &m, const ActView &a, int ntok, float *y, int64_t y_stride,
+                              const float *y_add, const GemvFuse &fz, unsigned *status, int num_sms, cudaStream_t s,
+                              bool pdl, const char **why);
 
 }  // namespace zllm

@@ -190,9 +190,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const A
   pdl_launch_dependents();
   pdl_wait();                                         // q and the newest K/V row come from the previous kernel
 
+  // split s covers positions [s * kAttnSplit, (s + 1) * kAttnSplit): the partition depends on the
+  // sequence's own length only, so a query gets the same bits alone or in any batch
   const int npos = a.npos[b];
-  const int per = ((npos + a.nsplit - 1) / a.nsplit + kAttnTP - 1) / kAttnTP * kAttnTP;
-  const int t0 = min(npos, split * per), t1 = min(npos, t0 + per);
+  const int active = npos > 0 ? (npos + kAttnSplit - 1) / kAttnSplit : 1;
+  if (split >= active) return;                        // nothing of this sequence here (no partial, no count)
+  const int t0 = min(npos, split * kAttnSplit), t1 = min(npos, t0 + kAttnSplit);
   const int ntiles = (t1 - t0 + kAttnTP - 1) / kAttnTP;
   const int64_t cs = a.seq ? a.seq[b] : b;            // cache sequence of this query
   const uint8_t *kbase = reinterpret_cast<const uint8_t *>(a.kcache) +
@@ -351,7 +354,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const A
   }
   __syncthreads();
   const int64_t grp = (int64_t)b * a.n_kv + kh;
-  if (a.nsplit == 1) {
+  if (active == 1) {
     for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
       const int g = e / HD;
       const float l = stat[2 * G + g];
@@ -367,18 +370,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const A
   __syncthreads();
   if (threadIdx.x == 0) {
     const int done = atomicAdd(a.counters + grp, 1);
-    *last_flag = done == a.nsplit - 1;
+    *last_flag = done == active - 1;
   }
   __syncthreads();
   if (!*last_flag) return;
   __threadfence();
-  // merge all splits in split order (deterministic)
+  // merge the active splits in split order (deterministic)
   for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
     const int g = e / HD;
     float M = -INFINITY;
-    for (int j = 0; j < a.nsplit; j++) M = fmaxf(M, __ldcg(a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2)) + g));
+#pragma unroll 8
+    for (int j = 0; j < active; j++) M = fmaxf(M, __ldcg(a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2)) + g));
     float L = 0.f, O = 0.f;
-    for (int j = 0; j < a.nsplit; j++) {
+#pragma unroll 8
+    for (int j = 0; j < active; j++) {
       const float *pj = a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2));
       const float mj = __ldcg(pj + g);
       if (mj == -INFINITY) continue;

@@ -14,6 +14,7 @@
 // Steady-state decode passes of the same shape are recorded once into a CUDA graph and replayed
 // (kernels chained with programmatic dependent launch inside the graph).
 #include <algorithm>
+#include <initializer_list>
 #include <cmath>
 #include <cstring>
 #include <new>
@@ -30,6 +31,7 @@ namespace {
 
 struct Layer {
   zllm_weight *w[7] = {};                 // wq wk wv wo gate up down
+  zllm_weight *qkv = nullptr, *gu = nullptr;   // [wq; wk; wv] and [gate; up] row-concatenated (when types agree)
   float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   float *bq = nullptr, *bk = nullptr, *bv = nullptr;
 };
@@ -58,6 +60,7 @@ struct zllm_model {
   int slot_cap = 0, slot_n = 0;
   float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *att = nullptr;
   float *g = nullptr, *u = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
+  float *qkv = nullptr, *gu = nullptr;                   // outputs of the row-concatenated projections
   int8_t *xq = nullptr;
   float *xd = nullptr;
   int32_t *xs = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_npos = nullptr, *d_arg = nullptr;
@@ -65,9 +68,11 @@ struct zllm_model {
   int nsplit = 1;
   std::vector<int> pos;                                   // positions held per sequence
   // decode graph cache: one graph per token count
-  struct Graph { int n = 0; int want = 0; cudaGraphExec_t exec = nullptr; };
+  struct Graph { int n = 0; int want = 0; int adv = 0; cudaGraphExec_t exec = nullptr; };
   std::vector<Graph> graphs;
-  std::vector<std::pair<int, int>> eager_seen;           // shapes run once eagerly before being recorded
+  std::vector<std::pair<int, int>> eager_seen;           // shapes (n, want | adv << 2) run once eagerly before being recorded
+  int32_t *d_gen = nullptr, *d_step = nullptr;           // greedy generation: tokens [steps][n], step counter
+  int64_t gen_cap = 0;
   bool use_graphs = true;
 
   int64_t qdim() const { return (int64_t)c.n_head * c.head_dim; }
@@ -196,6 +201,47 @@ extern "C" int zllm_model_set_vector(zllm_model *m, int kind, int layer, const f
   return ZLLM_OK;
 }
 
+// The rows of several matrices of one type and row length as one weight (the projections that read
+// the same activation: q, k, v; gate, up), so one GEMV launch streams them all.  The device rows
+// are independent (each row's layout depends on the row alone), so a byte copy of each matrix in
+// turn is the concatenation, and every output row keeps its bits.  NULL when types or widths differ.
+// With `interleave` (equal row counts) row i of matrix j lands at row i * count + j instead: the
+// gate / up pairs of the SwiGLU epilogue.
+static zllm_weight *concat_rows(zllm_model *m, std::initializer_list<zllm_weight *> ws, bool interleave = false) {
+  const zllm_weight *w0 = *ws.begin();
+  int64_t rows = 0;
+  for (const zllm_weight *w : ws) {
+    if (!w || w->m.type != w0->m.type || w->m.cols != w0->m.cols || w->m.row_stride != w0->m.row_stride) return nullptr;
+    if (interleave && w->m.rows != w0->m.rows) return nullptr;
+    rows += w->m.rows;
+  }
+  zllm_weight *f = new (std::nothrow) zllm_weight();
+  if (!f) return nullptr;
+  f->ctx = m->ctx;
+  f->m = w0->m;
+  f->m.rows = rows;
+  f->bytes = (size_t)(f->m.row_stride * rows);
+  if (cudaMalloc((void **)&f->m.data, f->bytes) != cudaSuccess) { delete f; cudaGetLastError(); return nullptr; }
+  size_t off = 0;
+  cudaError_t e = cudaSuccess;
+  const size_t rs = (size_t)w0->m.row_stride, count = ws.size();
+  int j = 0;
+  for (const zllm_weight *w : ws) {
+    if (e != cudaSuccess) break;
+    if (interleave)
+      e = cudaMemcpy2DAsync(f->m.data + j * rs, count * rs, w->m.data, rs, rs, (size_t)w->m.rows, cudaMemcpyDeviceToDevice,
+                            m->stream);
+    else
+      e = cudaMemcpyAsync(f->m.data + off, w->m.data, w->bytes, cudaMemcpyDeviceToDevice, m->stream);
+    off += w->bytes;
+    j++;
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  if (e != cudaSuccess) { cudaFree(f->m.data); delete f; cudaGetLastError(); return nullptr; }
+  m->ctx->weights.insert(f);
+  return f;
+}
+
 extern "C" int zllm_model_ready(zllm_model *m) {
   if (!m) return ZLLM_E_ARG;
   if (m->ready) return ZLLM_OK;
@@ -205,6 +251,14 @@ extern "C" int zllm_model_ready(zllm_model *m) {
     for (int i = 0; i < 7; i++)
       if (!m->L[l].w[i]) { zllm_set_error(m->ctx, "model: layer %d matrix %d missing", l, i); return ZLLM_E_ARG; }
     if (!m->L[l].attn_norm || !m->L[l].ffn_norm) { zllm_set_error(m->ctx, "model: layer %d norms missing", l); return ZLLM_E_ARG; }
+  }
+  // one launch per group of projections that read the same activation
+  for (auto &L : m->L) {
+    if ((L.qkv = concat_rows(m, {L.w[WQ], L.w[WK], L.w[WV]})))
+      for (int i : {WQ, WK, WV}) { zllm_weight_free(L.w[i]); L.w[i] = nullptr; }
+    // gate / up interleaved for the SwiGLU epilogue, which only the k-quant GEMV has
+    if (kq_type(L.w[GATE]->m.type) && (L.gu = concat_rows(m, {L.w[GATE], L.w[UP]}, true)))
+      for (int i : {GATE, UP}) { zllm_weight_free(L.w[i]); L.w[i] = nullptr; }
   }
   const int MB = c.max_batch;
   const int64_t E = c.n_embd, F = c.n_ff, Q = m->qdim(), KV = m->kvdim();
@@ -224,6 +278,8 @@ extern "C" int zllm_model_ready(zllm_model *m) {
   CK(dalloc(&m->xd, MB * KX / 32), "act");
   CK(dalloc(&m->xs, MB * KX / 32), "act");
   CK(dalloc(&m->q, MB * Q), "act");
+  CK(dalloc(&m->qkv, MB * (Q + 2 * KV)), "act");
+  CK(dalloc(&m->gu, MB * 2 * F), "act");
   CK(dalloc(&m->k, MB * KV), "act");
   CK(dalloc(&m->v, MB * KV), "act");
   CK(dalloc(&m->qr, MB * Q), "act");
@@ -251,10 +307,17 @@ extern "C" int zllm_model_ready(zllm_model *m) {
 
 // ------------------------------------------------------------------------------------ the pass
 static cudaError_t gemv(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add, const float *xf,
-                        int64_t k) {
+                        int64_t k, bool pdl = false) {
   ActView a{m->xq, m->xd, m->xs, xf, k};
   const char *why = "";
-  return launch_gemv(w->m, a, n, y, ys, y_add, m->ctx->status_dev, m->ctx->num_sms, m->stream, true, &why);
+  return launch_gemv(w->m, a, n, y, ys, y_add, m->ctx->status_dev, m->ctx->num_sms, m->stream, pdl, &why);
+}
+
+// A k-quant GEMV with fused work: `act` may carry the f32 activation alone (one token).
+static cudaError_t gemv_ex(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add,
+                           const ActView &act, const GemvFuse &fz, bool pdl = false) {
+  const char *why = "";
+  return launch_gemv_kq_ex(w->m, act, n, y, ys, y_add, fz, m->ctx->status_dev, m->ctx->num_sms, m->stream, pdl, &why);
 }
 
 // Enqueue the pass for n tokens whose ids / positions / sequences are already in d_tok / d_pos /
@@ -264,17 +327,36 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
   const int64_t E = c.n_embd, F = c.n_ff, Q = m->qdim(), KV = m->kvdim();
   cudaStream_t s = m->stream;
   cudaError_t e;
+  // Programmatic dependent launch only where a GEMV follows a GEMV (the next matrix streams in while
+  // the previous one finishes); ahead of the other kernels the early-resident CTAs cost more than
+  // they save (measured on the decode pass).
 #define RUN(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
-  RUN(launch_embed(m->tok->m, m->d_tok, n, m->x, s, true));
+  RUN(launch_embed(m->tok->m, m->d_tok, n, m->x, s, false));
   const zllm_attn_geom g = m->geom();
   for (int l = 0; l < c.n_layer; l++) {
     const Layer &L = m->L[l];
-    RUN(launch_rmsnorm_quant(m->x, L.attn_norm, (int)E, n, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, true));
-    RUN(gemv(m, L.w[WQ], n, m->q, Q, nullptr, m->xb, E));
-    RUN(gemv(m, L.w[WK], n, m->k, KV, nullptr, m->xb, E));
-    RUN(gemv(m, L.w[WV], n, m->v, KV, nullptr, m->xb, E));
+    // a single-token pass folds the norms, the activation quantization and SwiGLU into the k-quant
+    // GEMVs (the same arithmetic as the separate kernels, so the same bits)
+    const bool one = n == 1;
+    const bool fuse_qkv = one && L.qkv && kq_type(L.qkv->m.type);
+    if (!fuse_qkv) RUN(launch_rmsnorm_quant(m->x, L.attn_norm, (int)E, n, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, false));
     QkvPostArgs pa{};
-    pa.q = m->q; pa.k = m->k; pa.v = m->v; pa.q_stride = Q; pa.kv_stride = KV;
+    if (L.qkv) {
+      if (fuse_qkv) {
+        GemvFuse fz;
+        fz.norm_w = L.attn_norm;
+        fz.eps = c.rms_eps;
+        RUN(gemv_ex(m, L.qkv, 1, m->qkv, Q + 2 * KV, nullptr, ActView{nullptr, nullptr, nullptr, m->x, E}, fz, l > 0));
+      } else {
+        RUN(gemv(m, L.qkv, n, m->qkv, Q + 2 * KV, nullptr, m->xb, E));
+      }
+      pa.q = m->qkv; pa.k = m->qkv + Q; pa.v = m->qkv + Q + KV; pa.q_stride = Q + 2 * KV; pa.kv_stride = Q + 2 * KV;
+    } else {
+      RUN(gemv(m, L.w[WQ], n, m->q, Q, nullptr, m->xb, E));
+      RUN(gemv(m, L.w[WK], n, m->k, KV, nullptr, m->xb, E));
+      RUN(gemv(m, L.w[WV], n, m->v, KV, nullptr, m->xb, E));
+      pa.q = m->q; pa.k = m->k; pa.v = m->v; pa.q_stride = Q; pa.kv_stride = KV;
+    }
     pa.bq = L.bq; pa.bk = L.bk; pa.bv = L.bv; pa.q_norm = L.q_norm; pa.k_norm = L.k_norm;
     pa.rope_cos = m->rope_cos; pa.rope_sin = m->rope_sin; pa.pos = m->d_pos; pa.seq = m->d_seq;
     pa.q_out = m->qr; pa.q_out_stride = Q;
@@ -282,7 +364,7 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
     pa.seq_stride = g.seq_stride; pa.head_stride = g.head_stride;
     pa.n_head = c.n_head; pa.n_kv = c.n_head_kv; pa.head_dim = c.head_dim; pa.n_rot = c.n_rot; pa.neox = c.neox;
     pa.kv_f16 = c.kv_f16; pa.ntok = n; pa.eps = c.rms_eps;
-    RUN(launch_qkv_post(pa, s, true));
+    RUN(launch_qkv_post(pa, s, false));
     AttnArgs aa{};
     aa.q = m->qr; aa.seq = m->d_seq; aa.kcache = m->kv_block(0, l, 0); aa.vcache = m->kv_block(0, l, 1);
     aa.seq_stride = g.seq_stride; aa.head_stride = g.head_stride; aa.npos = m->d_npos; aa.out = m->att;
@@ -291,28 +373,96 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
     // one split count for every pass: a query's context partition (and so its rounding) does not
     // depend on how many tokens share the pass, so batched passes equal token-by-token ones bit for bit
     aa.n_head = c.n_head; aa.n_kv = c.n_head_kv; aa.head_dim = c.head_dim; aa.nseq = n; aa.nsplit = m->nsplit;
-    RUN(launch_attn(aa, c.kv_f16 != 0, s, true));
-    RUN(launch_quantize(m->att, Q, n, m->xq, m->xd, m->xs, m->ctx->status_dev, s, true));
-    RUN(gemv(m, L.w[WO], n, m->x, E, m->x, m->att, Q));                       // x += wo . att
-    RUN(launch_rmsnorm_quant(m->x, L.ffn_norm, (int)E, n, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, true));
-    RUN(gemv(m, L.w[GATE], n, m->g, F, nullptr, m->xb, E));
-    RUN(gemv(m, L.w[UP], n, m->u, F, nullptr, m->xb, E));
-    RUN(launch_swiglu_quant(m->g, m->u, (int)F, n, F, m->hb, m->xq, m->xd, m->xs, s, true));
-    RUN(gemv(m, L.w[DOWN], n, m->x, E, m->x, m->hb, F));                      // x += down . hb
+    RUN(launch_attn(aa, c.kv_f16 != 0, s, false));
+    if (one && kq_type(L.w[WO]->m.type)) {
+      RUN(gemv_ex(m, L.w[WO], 1, m->x, E, m->x, ActView{nullptr, nullptr, nullptr, m->att, Q}, GemvFuse{}));
+    } else {
+      RUN(launch_quantize(m->att, Q, n, m->xq, m->xd, m->xs, m->ctx->status_dev, s, false));
+      RUN(gemv(m, L.w[WO], n, m->x, E, m->x, m->att, Q));                     // x += wo . att
+    }
+    if (L.gu) {
+      // interleaved (gate, up) rows; the GEMV writes hb = silu(gate) * up
+      GemvFuse fz;
+      fz.swiglu = true;
+      if (one) {
+        fz.norm_w = L.ffn_norm;
+        fz.eps = c.rms_eps;
+        RUN(gemv_ex(m, L.gu, 1, m->hb, F, nullptr, ActView{nullptr, nullptr, nullptr, m->x, E}, fz, true));
+      } else {
+        RUN(launch_rmsnorm_quant(m->x, L.ffn_norm, (int)E, n, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, false));
+        RUN(gemv_ex(m, L.gu, n, m->hb, F, nullptr, ActView{m->xq, m->xd, m->xs, m->xb, E}, fz));
+      }
+      if (one && kq_type(L.w[DOWN]->m.type)) {
+        RUN(gemv_ex(m, L.w[DOWN], 1, m->x, E, m->x, ActView{nullptr, nullptr, nullptr, m->hb, F}, GemvFuse{}, true));
+      } else {
+        RUN(launch_quantize(m->hb, F, n, m->xq, m->xd, m->xs, m->ctx->status_dev, s, false));
+        RUN(gemv(m, L.w[DOWN], n, m->x, E, m->x, m->hb, F));                  // x += down . hb
+      }
+    } else {
+      RUN(launch_rmsnorm_quant(m->x, L.ffn_norm, (int)E, n, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, false));
+      RUN(gemv(m, L.w[GATE], n, m->g, F, nullptr, m->xb, E));
+      RUN(gemv(m, L.w[UP], n, m->u, F, nullptr, m->xb, E));
+      RUN(launch_swiglu_quant(m->g, m->u, (int)F, n, F, m->hb, m->xq, m->xd, m->xs, s, false));
+      RUN(gemv(m, L.w[DOWN], n, m->x, E, m->x, m->hb, F));                    // x += down . hb
+    }
   }
   if (want) {
     const zllm_weight *ow = m->out ? m->out : m->tok;
     const int nl = want == 2 ? n : 1;
     const float *xl = want == 2 ? m->x : m->x + (int64_t)(n - 1) * E;
-    RUN(launch_rmsnorm_quant(xl, m->out_norm, (int)E, nl, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, true));
+    RUN(launch_rmsnorm_quant(xl, m->out_norm, (int)E, nl, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, false));
     RUN(gemv(m, ow, nl, m->logits, c.vocab, nullptr, m->xb, E));
-    RUN(launch_argmax(m->logits, c.vocab, c.vocab, nl, m->d_arg, s, true));
+    RUN(launch_argmax(m->logits, c.vocab, c.vocab, nl, m->d_arg, s, false));
   }
 #undef RUN
   return cudaSuccess;
 }
 
 // Validate, stage the int arrays, run the pass (replaying a recorded graph when possible), copy out.
+// One pass of n tokens (with `adv`: followed by the greedy advance of generate), replayed from a
+// recorded graph when the shape was seen before.
+static int launch_shape(zllm_model *m, int n, int want, bool adv) {
+  cudaStream_t s = m->stream;
+  const int key = want | (adv ? 4 : 0);
+  auto enqueue = [&]() -> cudaError_t {
+    cudaError_t e = enqueue_pass(m, n, want);
+    if (e == cudaSuccess && adv) e = launch_advance(m->d_arg, n, m->d_tok, m->d_pos, m->d_npos, m->d_gen, m->d_step, s, false);
+    return e;
+  };
+  cudaGraphExec_t exec = nullptr;
+  bool eager = !m->use_graphs;
+  if (!eager) {
+    for (auto &gr : m->graphs)
+      if (gr.n == n && gr.want == want && gr.adv == (adv ? 1 : 0)) exec = gr.exec;
+    // the first pass of a shape runs eagerly (kernel attributes are set outside any capture)
+    if (!exec && std::find(m->eager_seen.begin(), m->eager_seen.end(), std::make_pair(n, key)) == m->eager_seen.end()) {
+      m->eager_seen.push_back({n, key});
+      eager = true;
+    }
+  }
+  if (!eager) {
+    if (!exec) {
+      cudaGraph_t graph = nullptr;
+      CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "graph capture");
+      cudaError_t e = enqueue();
+      cudaError_t e2 = cudaStreamEndCapture(s, &graph);
+      if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        return fail(m, zllm_cuda_fail(m->ctx, e != cudaSuccess ? e : e2, "recording the pass"));
+      }
+      e = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (e != cudaSuccess) return fail(m, zllm_cuda_fail(m->ctx, e, "cudaGraphInstantiate"));
+      m->graphs.push_back({n, want, adv ? 1 : 0, exec});
+    }
+    CK(cudaGraphLaunch(exec, s), "cudaGraphLaunch");
+  } else {
+    CK(enqueue(), "pass launch");
+  }
+  return ZLLM_OK;
+}
+
 static int run(zllm_model *m, const int32_t *seqs, int single_seq, const int32_t *tokens, int n, int want, float *logits_host,
                int32_t *argmax_host) {
   if (!m) return ZLLM_E_ARG;
@@ -342,37 +492,8 @@ static int run(zllm_model *m, const int32_t *seqs, int single_seq, const int32_t
   CK(cudaMemcpyAsync(m->d_pos, hp, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
   CK(cudaMemcpyAsync(m->d_seq, hs, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
   CK(cudaMemcpyAsync(m->d_npos, hn, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
-  cudaGraphExec_t exec = nullptr;
-  bool eager = !m->use_graphs;
-  if (!eager) {
-    for (auto &gr : m->graphs)
-      if (gr.n == n && gr.want == want) exec = gr.exec;
-    // the first pass of a shape runs eagerly (kernel attributes are set outside any capture)
-    if (!exec && std::find(m->eager_seen.begin(), m->eager_seen.end(), std::make_pair(n, want)) == m->eager_seen.end()) {
-      m->eager_seen.push_back({n, want});
-      eager = true;
-    }
-  }
-  if (!eager) {
-    if (!exec) {
-      cudaGraph_t graph = nullptr;
-      CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "graph capture");
-      cudaError_t e = enqueue_pass(m, n, want);
-      cudaError_t e2 = cudaStreamEndCapture(s, &graph);
-      if (e != cudaSuccess || e2 != cudaSuccess) {
-        if (graph) cudaGraphDestroy(graph);
-        cudaGetLastError();
-        return fail(m, zllm_cuda_fail(m->ctx, e != cudaSuccess ? e : e2, "recording the pass"));
-      }
-      e = cudaGraphInstantiate(&exec, graph, 0);
-      cudaGraphDestroy(graph);
-      if (e != cudaSuccess) return fail(m, zllm_cuda_fail(m->ctx, e, "cudaGraphInstantiate"));
-      m->graphs.push_back({n, want, exec});
-    }
-    CK(cudaGraphLaunch(exec, s), "cudaGraphLaunch");
-  } else {
-    CK(enqueue_pass(m, n, want), "pass launch");
-  }
+  int rc0 = launch_shape(m, n, want, false);
+  if (rc0) return rc0;
   const int nl = want == 2 ? n : 1;
   if (want && logits_host)
     CK(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * nl * c.vocab, cudaMemcpyDeviceToHost, s), "logits");
@@ -398,6 +519,59 @@ extern "C" int zllm_model_decode(zllm_model *m, const int32_t *seqs, const int32
     for (int j = 0; j < i; j++)
       if (seqs[i] == seqs[j]) { zllm_set_error(m->ctx, "zllm_model_decode: sequence %d appears twice", seqs[i]); return ZLLM_E_ARG; }
   return run(m, seqs, -1, tokens, n, 2, logits_host, argmax_host);
+}
+
+// Greedy generation on the device: `steps` passes, the first on `tokens`, each later one on the
+// argmax of the previous pass's logits (generate.js:4-10 with greedy sampling), with no host work
+// between passes.  n == 1 with seqs == NULL continues sequence `seq`; otherwise one token for each
+// of the n distinct sequences.  out_host[steps][n] receives every pass's argmax.
+extern "C" int zllm_model_generate(zllm_model *m, int seq, const int32_t *seqs, const int32_t *tokens, int n, int steps,
+                                   int32_t *out_host) {
+  if (!m || !tokens || !out_host || steps < 1 || (!seqs && n != 1)) return ZLLM_E_ARG;
+  if (m->closed) { zllm_set_error(m->ctx, "model is closed"); return ZLLM_E_STATE; }
+  if (m->failed) return ZLLM_E_STATE;
+  if (!m->ready) { int rc = zllm_model_ready(m); if (rc) return rc; }
+  const zllm_model_config &c = m->c;
+  if (n < 1 || n > c.max_batch) { zllm_set_error(m->ctx, "batch of %d tokens (max %d)", n, c.max_batch); return ZLLM_E_BATCH; }
+  int32_t *ht = m->h_io, *hp = m->h_io + c.max_batch, *hs = m->h_io + 2 * c.max_batch, *hn = m->h_io + 3 * c.max_batch;
+  for (int i = 0; i < n; i++) {
+    const int sq = seqs ? seqs[i] : seq;
+    if (sq < 0 || sq >= c.n_seq) { zllm_set_error(m->ctx, "sequence %d out of range", sq); return ZLLM_E_ARG; }
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == sq) { zllm_set_error(m->ctx, "zllm_model_generate: sequence %d appears twice", sq); return ZLLM_E_ARG; }
+    if (!(tokens[i] >= 0 && tokens[i] < c.vocab)) { zllm_set_error(m->ctx, "token id %d out of range", tokens[i]); return ZLLM_E_TOKEN; }
+    if (m->pos[sq] + steps > c.ctx) { zllm_set_error(m->ctx, "context full (%d tokens)", c.ctx); return ZLLM_E_CTX_FULL; }
+    ht[i] = tokens[i]; hp[i] = m->pos[sq]; hs[i] = sq; hn[i] = m->pos[sq] + 1;
+  }
+  cudaStream_t s = m->stream;
+  if ((int64_t)steps * n > m->gen_cap) {
+    CK(cudaStreamSynchronize(s), "generate");
+    if (m->d_gen) cudaFree(m->d_gen);
+    m->d_gen = nullptr;
+    m->gen_cap = 0;
+    CK(cudaMalloc(&m->d_gen, sizeof(int32_t) * (size_t)steps * n), "cudaMalloc(generated tokens)");
+    m->gen_cap = (int64_t)steps * n;
+    // recorded advance graphs hold the old buffer
+    for (auto it = m->graphs.begin(); it != m->graphs.end();)
+      if (it->adv) { cudaGraphExecDestroy(it->exec); it = m->graphs.erase(it); } else ++it;
+  }
+  if (!m->d_step) CK(cudaMalloc(&m->d_step, sizeof(int32_t)), "cudaMalloc(step)");
+  CK(cudaMemsetAsync(m->d_step, 0, sizeof(int32_t), s), "step");
+  CK(cudaMemcpyAsync(m->d_tok, ht, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
+  CK(cudaMemcpyAsync(m->d_pos, hp, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
+  CK(cudaMemcpyAsync(m->d_seq, hs, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
+  CK(cudaMemcpyAsync(m->d_npos, hn, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
+  const int want = n == 1 ? 1 : 2;
+  for (int i = 0; i < steps; i++) {
+    int rc = launch_shape(m, n, want, true);
+    if (rc) return rc;
+  }
+  CK(cudaMemcpyAsync(out_host, m->d_gen, sizeof(int32_t) * (size_t)steps * n, cudaMemcpyDeviceToHost, s), "tokens");
+  CK(cudaStreamSynchronize(s), "generate");
+  int rc = zllm_check_status(m->ctx);
+  if (rc) return fail(m, rc);
+  for (int i = 0; i < n; i++) m->pos[seqs ? seqs[i] : seq] += steps;
+  return ZLLM_OK;
 }
 
 extern "C" int zllm_model_pos(const zllm_model *m, int seq) {
@@ -508,15 +682,17 @@ extern "C" void zllm_model_destroy(zllm_model *m) {
     if (gr.exec) cudaGraphExecDestroy(gr.exec);
   for (auto &L : m->L) {
     for (auto *w : L.w) zllm_weight_free(w);
+    zllm_weight_free(L.qkv);
+    zllm_weight_free(L.gu);
     for (float *p : {L.attn_norm, L.ffn_norm, L.q_norm, L.k_norm, L.bq, L.bk, L.bv}) cudaFree(p);
   }
   zllm_weight_free(m->tok);
   zllm_weight_free(m->out);
   for (void *p : {(void *)m->out_norm, (void *)m->rope_cos, (void *)m->rope_sin, m->kv, m->slot, (void *)m->x, (void *)m->xb,
                   (void *)m->q, (void *)m->k, (void *)m->v, (void *)m->qr, (void *)m->att, (void *)m->g, (void *)m->u,
-                  (void *)m->hb, (void *)m->logits, (void *)m->part, (void *)m->xq, (void *)m->xd, (void *)m->xs,
+                  (void *)m->hb, (void *)m->qkv, (void *)m->gu, (void *)m->logits, (void *)m->part, (void *)m->xq, (void *)m->xd, (void *)m->xs,
                   (void *)m->d_tok, (void *)m->d_pos, (void *)m->d_seq, (void *)m->d_npos, (void *)m->d_arg,
-                  (void *)m->counters})
+                  (void *)m->counters, (void *)m->d_gen, (void *)m->d_step})
     if (p) cudaFree(p);
   if (m->h_io) cudaFreeHost(m->h_io);
   if (m->stream) cudaStreamDestroy(m->stream);

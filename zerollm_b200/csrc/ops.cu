@@ -36,11 +36,13 @@ __device__ __forceinline__ void quantize_block_warp(float v, int lane, int8_t *q
 }
 
 // ---------------------------------------------------------------------------- RMSNorm + quantize
-// One CTA per token.  xb (optional) receives the normalized f32 vector; xq/xd/xs (optional) its
-// quantization.  n must be a multiple of 32 when quantizing.
+// grid (ntok, nsplit): every CTA of a token computes the token's sum of squares (the same reduction
+// in the same order, so the same bits) and then normalizes / quantizes its own share of the 32-value
+// blocks.  xb (optional) receives the normalized f32 vector; xq/xd/xs (optional) its quantization.
+// n must be a multiple of 32 when quantizing.
 __global__ void rmsnorm_quant_kernel(const float *__restrict__ x, const float *__restrict__ w, int n, double eps,
                                      float *xb, int8_t *xq, float *xd, int32_t *xs) {
-  extern __shared__ double red[];
+  __shared__ double red[32];
   pdl_launch_dependents();
   pdl_wait();
   const int t = blockIdx.x;
@@ -51,22 +53,21 @@ __global__ void rmsnorm_quant_kernel(const float *__restrict__ x, const float *_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   if (lane == 0) red[warp] = ss;
   __syncthreads();
-  if (warp == 0) {
-    double v = lane < nw ? red[lane] : 0.0;
-    v = warp_sum_f64(v);
-    if (lane == 0) red[0] = v;
-  }
-  __syncthreads();
-  const double s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(red[0], (double)n), eps)));
+  double tot = lane < nw ? red[lane] : 0.0;
+  tot = warp_sum_f64(tot);                      // every warp reduces the same values in the same order
+  const double s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(tot, (double)n), eps)));
+  const int nblk = n / 32, per = (nblk + gridDim.y - 1) / gridDim.y;
+  const int b0 = blockIdx.y * per, b1 = min(nblk, b0 + per);
   if (xq) {
-    for (int b = warp; b < n / 32; b += nw) {
+    for (int b = b0 + warp; b < b1; b += nw) {
       const int i = b * 32 + lane;
       const float v = __double2float_rn(__dmul_rn(__dmul_rn((double)xt[i], s), (double)w[i]));
       if (xb) xb[(int64_t)t * n + i] = v;
       quantize_block_warp(v, lane, xq + (int64_t)t * n + b * 32, xd + (int64_t)t * (n / 32) + b, xs + (int64_t)t * (n / 32) + b);
     }
   } else {
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
+    const int i0 = blockIdx.y == 0 ? 0 : b0 * 32, i1 = blockIdx.y == gridDim.y - 1 ? n : b1 * 32;
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x)
       xb[(int64_t)t * n + i] = __double2float_rn(__dmul_rn(__dmul_rn((double)xt[i], s), (double)w[i]));
   }
 }
@@ -210,7 +211,12 @@ static cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, size_t smem, cudaStream_
 cudaError_t launch_rmsnorm_quant(const float *x, const float *w, int n, int ntok, double eps, float *xb, int8_t *xq, float *xd,
                                  int32_t *xs, cudaStream_t s, bool pdl) {
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = cfg_of(dim3(ntok), dim3(512), 16 * sizeof(double), s, pdl, attr);
+  // split each token's blocks over CTAs so that about 128 CTAs run (each re-reads the token to get
+  // the same sum of squares)
+  const int nblk = n / 32 > 0 ? n / 32 : 1;
+  int split = (128 + ntok - 1) / ntok;
+  if (split > nblk / 8) split = nblk / 8 > 0 ? nblk / 8 : 1;
+  cudaLaunchConfig_t cfg = cfg_of(dim3(ntok, split), dim3(256), 0, s, pdl, attr);
   return cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, x, w, n, eps, xb, xq, xd, xs);
 }
 
@@ -228,6 +234,33 @@ cudaError_t launch_embed(const DevMatrix &m, const int32_t *tokens, int ntok, fl
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = cfg_of(dim3(ntok), dim3(256), 0, s, pdl, attr);
   return cudaLaunchKernelEx(&cfg, embed_kernel, m, tokens, ntok, x);
+}
+
+// Greedy feedback between decode passes on the device: each sequence's next input is the argmax of
+// its logits (src/model/generate.js:4-10 picks the first maximum), at the next position; the token
+// is also recorded as output `step` (a device counter advanced here).
+__global__ void advance_kernel(const int32_t *arg, int n, int32_t *tok, int32_t *pos, int32_t *npos, int32_t *out,
+                               int32_t *step) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int i = threadIdx.x;
+  const int st = *step;
+  if (i < n) {
+    const int32_t a = arg[i];
+    tok[i] = a;
+    pos[i] += 1;
+    npos[i] += 1;
+    out[(int64_t)st * n + i] = a;
+  }
+  __syncthreads();
+  if (i == 0) *step = st + 1;
+}
+
+cudaError_t launch_advance(const int32_t *arg, int n, int32_t *tok, int32_t *pos, int32_t *npos, int32_t *out,
+                           int32_t *step, cudaStream_t s, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(dim3(1), dim3(64), 0, s, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, advance_kernel, arg, n, tok, pos, npos, out, step);
 }
 
 cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, cudaStream_t s, bool pdl) {

@@ -54,6 +54,7 @@ SIGNATURES = {
     "zllm_model_ready": (i32, [vp]),
     "zllm_model_forward": (i32, [vp, i32, vp, i32, i32, vp, vp]),
     "zllm_model_decode": (i32, [vp, vp, vp, i32, vp, vp]),
+    "zllm_model_generate": (i32, [vp, i32, vp, vp, i32, i32, vp]),
     "zllm_model_pos": (i32, [vp, i32]),
     "zllm_model_truncate": (i32, [vp, i32, i32]),
     "zllm_model_reset": (i32, [vp, i32]),

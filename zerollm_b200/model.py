@@ -157,6 +157,24 @@ class CudaModel:
             self._tokens[int(sq)].append(int(tk))
         return self._logits[:t.size], self._argmax[:t.size]
 
+    def generate(self, tokens, steps: int, seqs=None) -> np.ndarray:
+        """Greedy decoding on the device: ``steps`` passes starting from ``tokens`` (one per sequence
+        of ``seqs``, or one token of sequence 0), each pass fed the previous pass's argmax.  Returns
+        the argmax tokens [steps][n]."""
+        self._guard()
+        t = np.ascontiguousarray(np.atleast_1d(tokens), np.int32)
+        n = t.size
+        out = np.zeros((steps, n), np.int32)
+        s = None if seqs is None else np.ascontiguousarray(seqs, np.int32)
+        rc = self.lib.zllm_model_generate(self.h, 0, None if s is None else s.ctypes.data_as(C.c_void_p),
+                                          t.ctypes.data_as(C.c_void_p), n, int(steps), out.ctypes.data_as(C.c_void_p))
+        self._run(rc, "generate")
+        for i in range(n):
+            sq = 0 if s is None else int(s[i])
+            self._tokens[sq].append(int(t[i]))
+            self._tokens[sq].extend(int(v) for v in out[:-1, i])
+        return out
+
     def kvGet(self, layer: int, isV: int, n: int, seq: int = 0) -> np.ndarray:
         self._guard()
         out = np.empty(n * self.kv_dim, np.float32)
