@@ -190,6 +190,197 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------ 8B decode
+DEC_PROMPT, DEC_STEPS, DEC_CTX = 512, 128, 4096
+DEC_WEIGHT_BYTES = 5_618_794_496            # Qwen3-8B Q4_K/Q6_K mix + f16 head: bytes read per decode step
+DEC_KV_BYTES_PER_POS = 36 * 2 * 8 * 128 * 2  # f16 K and V of every layer, per cached position
+
+
+def _gen_kquant(t, rows, cols, g):
+    """Raw GGUF bytes of a seeded k-quant matrix (config 0/1 distribution: random nibbles / 6-bit
+    scales / high bits, d and dmin = f16(|N(0,1)| * 0.01); Q6_K int8 scales U[-32, 31]), drawn on
+    the GPU and returned as host bytes, as a GGUF reader would hand them over."""
+    import torch
+    from zerollm_b200 import ggml
+    _, bs, ts = ggml.TYPE_INFO[t]
+    nblk = rows * (cols // bs)
+    raw = torch.randint(0, 256, (nblk, ts), dtype=torch.uint8, device="cuda", generator=g)
+    d = (torch.randn(nblk, device="cuda", generator=g).abs() * 0.01).half().view(torch.uint8).view(nblk, 2)
+    if t == ggml.Q6_K:
+        raw[:, 192:208] = torch.randint(-32, 32, (nblk, 16), device="cuda", generator=g).to(torch.int8).view(torch.uint8)
+        raw[:, 208:210] = d
+    else:
+        raw[:, 0:2] = d
+        raw[:, 2:4] = (torch.randn(nblk, device="cuda", generator=g).abs() * 0.01).half().view(torch.uint8).view(nblk, 2)
+    return raw.cpu().numpy().reshape(-1)
+
+
+def decode_bench(n_seq: int, device: int, profile: bool = False):
+    """Config 3: random-init Qwen3-8B shapes (36 layers, hidden 4096, FFN 12288, 32/8 heads,
+    head_dim 128, vocab 151936), Q4_K everywhere but Q6_K ffn_down, f16 output head, norms
+    1 + N(0, 0.02), f16 KV cache of 4096 positions.  Prefill 512 seeded token ids per sequence, then
+    128 greedy decode steps (the argmax fed back on the device) through zllm_model_generate."""
+    import ctypes as C
+
+    import torch
+
+    from zerollm_b200 import ggml, synth
+    from zerollm_b200.kernels import Context
+    from zerollm_b200.lib import (T_ATTN_NORM, T_DOWN, T_FFN_NORM, T_GATE, T_K_NORM, T_OUTPUT, T_OUTPUT_NORM, T_Q_NORM,
+                                  T_TOK_EMBD, T_UP, T_WK, T_WO, T_WQ, T_WV, ModelConfig, check)
+    cfg = synth.qwen3_8b()
+    ctx = Context(device)
+    L = ctx.lib
+    E, F, V, NL = cfg["n_embd"], cfg["n_ff"], cfg["vocab"], cfg["n_layer"]
+    mc = ModelConfig(n_embd=E, n_layer=NL, n_ff=F, n_head=32, n_head_kv=8, head_dim=128, n_rot=128, vocab=V, neox=1,
+                     kv_f16=1, ctx=DEC_CTX, n_seq=n_seq, max_batch=64, logits_batch=16, rms_eps=cfg["rms_eps"],
+                     rope_base=1e6)
+    h = C.c_void_p()
+    check(L.zllm_model_create(ctx.h, C.byref(mc), C.byref(h)), ctx.h)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED)
+    rng = np.random.default_rng(SEED)
+
+    def mat(kind, layer, t, rows, cols):
+        buf = _gen_kquant(t, rows, cols, g) if t != ggml.F16 else \
+            (torch.randn(rows, cols, device="cuda", generator=g) * 0.02).half().view(torch.uint8).cpu().numpy().reshape(-1)
+        check(L.zllm_model_set_matrix(h, kind, layer, t, rows, cols, buf.ctypes.data_as(C.c_void_p), buf.nbytes), ctx.h)
+
+    def vec(kind, layer, n):
+        a = (1 + rng.standard_normal(n) * 0.02).astype(np.float32)
+        check(L.zllm_model_set_vector(h, kind, layer, a.ctypes.data_as(C.c_void_p), a.size), ctx.h)
+
+    mat(T_TOK_EMBD, 0, ggml.Q4_K, V, E)
+    mat(T_OUTPUT, 0, ggml.F16, V, E)
+    vec(T_OUTPUT_NORM, 0, E)
+    for l in range(NL):
+        for k_, n_ in ((T_ATTN_NORM, E), (T_FFN_NORM, E), (T_Q_NORM, 128), (T_K_NORM, 128)):
+            vec(k_, l, n_)
+        for k_, t_, r_, c_ in ((T_WQ, ggml.Q4_K, 4096, E), (T_WK, ggml.Q4_K, 1024, E), (T_WV, ggml.Q4_K, 1024, E),
+                               (T_WO, ggml.Q4_K, E, 4096), (T_GATE, ggml.Q4_K, F, E), (T_UP, ggml.Q4_K, F, E),
+                               (T_DOWN, ggml.Q6_K, E, F)):
+            mat(k_, l, t_, r_, c_)
+    check(L.zllm_model_ready(h), ctx.h)
+    P = lambda a: a.ctypes.data_as(C.c_void_p)
+    arg = np.zeros(64, np.int32)
+    first = np.zeros(n_seq, np.int32)
+    t0 = time.perf_counter()
+    for s in range(n_seq):
+        toks = rng.integers(0, V, DEC_PROMPT).astype(np.int32)
+        for i in range(0, DEC_PROMPT, 64):
+            chunk = np.ascontiguousarray(toks[i:i + 64])
+            want = 1 if i + 64 >= DEC_PROMPT else 0
+            check(L.zllm_model_forward(h, s, P(chunk), chunk.size, want, None, P(arg) if want else None), ctx.h)
+        first[s] = arg[0]
+    prefill_s = time.perf_counter() - t0
+    seqs = np.arange(n_seq, dtype=np.int32)
+    seqp = None if n_seq == 1 else P(seqs)
+    out = np.zeros((DEC_STEPS, n_seq), np.int32)
+    check(L.zllm_model_generate(h, 0, seqp, P(first), n_seq, 3, P(out)), ctx.h)      # warm-up: record the graphs
+    cur = np.ascontiguousarray(out[2])
+    steps = 2 if profile else DEC_STEPS
+    if profile:
+        torch.cuda.nvtx.range_push("decode")        # ncu --nvtx --nvtx-include "decode/" captures these steps
+    t0 = time.perf_counter()
+    check(L.zllm_model_generate(h, 0, seqp, P(cur), n_seq, steps, P(out)), ctx.h)
+    dt = time.perf_counter() - t0
+    if profile:
+        torch.cuda.nvtx.range_pop()
+    L.zllm_model_destroy(h)
+    ctx.close()
+    avg_pos = DEC_PROMPT + 3 + DEC_STEPS / 2
+    step_bytes = DEC_WEIGHT_BYTES + n_seq * avg_pos * DEC_KV_BYTES_PER_POS
+    return {"tok_s": round(n_seq * steps / dt, 1), "ms_per_step": round(dt / steps * 1e3, 3), "seconds": dt,
+            "prefill_tok_s": round(n_seq * DEC_PROMPT / prefill_s, 1), "step_bytes": int(step_bytes),
+            "hbm_gbs": round(step_bytes / (dt / steps) / 1e9, 1)}
+
+
+# ------------------------------------------------------------------------------------------ attention (config 2)
+def attn_bench(device: int, reps: int = 20):
+    """Config 2: GQA decode attention, 32 query / 8 KV heads, head_dim 128, f16 K/V caches filled
+    with N(0,1) at 2048 / 8192 / 32768 positions, batch 1 and 64 sequences.  A step appends one
+    token's K/V (f32 -> f16, q/k RMSNorm, RoPE theta 1e6) and attends over the cache; timed as a
+    graph of `reps` steps.  Also the restore of a 1024-position prefix slot (a byte copy of f16
+    K and V) into every sequence of one layer."""
+    import torch
+
+    from zerollm_b200.attention import KVCache, attn_decode, kv_copy, qkv_append, rope_tables
+    from zerollm_b200.kernels import Context
+    ctx = Context(device)
+    dev = torch.device(f"cuda:{device}")
+    stream = torch.cuda.Stream(device=dev)
+    nh, nkv, hd = 32, 8, 128
+    out = {}
+    for L in (2048, 8192, 32768):
+        for nseq in (1, 64):
+            cache = KVCache(ctx, 1, nkv, hd, L + 8, True, nseq)
+            torch.manual_seed(L + nseq)
+            cache.t.copy_(torch.randn(cache.t.shape, device=dev).half().view(torch.int16))
+            g = cache.geom(nh, eps=float(np.float32(1e-6)))
+            rope = rope_tables(ctx, hd, 1e6, L + 8)
+            q = torch.randn(nseq, nh * hd, device=dev)
+            k = torch.randn(nseq, nkv * hd, device=dev)
+            v = torch.randn(nseq, nkv * hd, device=dev)
+            qn = torch.ones(hd, device=dev)
+            pos = torch.full((nseq,), L - 1, dtype=torch.int32, device=dev)
+            seq = torch.arange(nseq, dtype=torch.int32, device=dev)
+            npos = torch.full((nseq,), L, dtype=torch.int32, device=dev)
+            qo = torch.empty_like(q)
+            o = torch.empty_like(q)
+            sid = stream.cuda_stream
+
+            def step():
+                qkv_append(ctx, g, cache, 0, q, k, v, pos, seq, rope, qn, qn, q_out=qo, stream=sid)
+                attn_decode(ctx, g, cache, 0, qo, npos, L, out=o, stream=sid)
+            with torch.cuda.stream(stream):
+                step()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for _ in range(reps):
+                    step()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                gr.replay()
+                e0.record(stream)
+                gr.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            ctx.sync()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            kv_bytes = nseq * 2 * nkv * L * hd * 2
+            out[f"ctx{L}_b{nseq}"] = {"us_per_layer_step": round(us, 2), "kv_bytes": kv_bytes,
+                                      "hbm_gbs": round(kv_bytes / us / 1e3, 1)}
+            del gr, cache
+            torch.cuda.empty_cache()
+    # prefix-slot restore: 1024 positions of f16 K and V into each of 64 sequences, one layer
+    nseq, n = 64, 1024
+    slot = KVCache(ctx, 1, nkv, hd, n, True)
+    slot.t.copy_(torch.randn(slot.t.shape, device=dev).half().view(torch.int16))
+    dst = KVCache(ctx, 1, nkv, hd, 2048, True, nseq)
+    g = dst.geom(nh)
+    sid = stream.cuda_stream
+
+    def restore():
+        for sq in range(nseq):
+            for isv in (0, 1):
+                kv_copy(ctx, g, dst.block(sq, 0, isv), dst.head_stride, slot.block(0, 0, isv), slot.head_stride, n, stream=sid)
+    with torch.cuda.stream(stream):
+        restore()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        restore()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    assert torch.equal(dst.t[5, 0, :, :, :n], slot.t[0, 0])
+    us = e0.elapsed_time(e1) * 1e3
+    moved = nseq * 2 * nkv * n * hd * 2
+    out["prefix_restore_1024x64"] = {"us_per_layer": round(us, 1), "bytes_copied": moved,
+                                     "hbm_gbs_read_plus_write": round(2 * moved / us / 1e3, 1)}
+    ctx.close()
+    return out
+
+
 def run_ours(args, world, rank, local):
     import ctypes as C
 
@@ -316,6 +507,22 @@ def run_ours(args, world, rank, local):
     e_ms = max_over_ranks(e0.elapsed_time(e1))
     barrier()
 
+    attn = {}
+    if not args.no_decode:
+        barrier()
+        attn = attn_bench(local)
+    decode = {}
+    if not args.no_decode:
+        del weights
+        torch.cuda.empty_cache()
+        for nseq in (1, 32):
+            barrier()
+            r = decode_bench(nseq, local)
+            slowest = max_over_ranks(r["seconds"])
+            decode[f"b{nseq}"] = {"tok_s": round(world * nseq * DEC_STEPS / slowest, 1), "ms_per_step": r["ms_per_step"],
+                                  "prefill_tok_s_per_gpu": r["prefill_tok_s"], "hbm_gbs_per_gpu": r["hbm_gbs"],
+                                  "step_bytes_per_gpu": r["step_bytes"]}
+
     if rank == 0:
         peak, peak_kind = measured_peaks()
         value = ALGO_BYTES * args.steps * world / (ms / 1e3) / 1e9
@@ -344,6 +551,15 @@ def run_ours(args, world, rank, local):
             "clocks": clocks.summary(),
             "parity": {"max_rel_err_vs_oracle": parity, "rows_checked": 256},
         }
+        if attn:
+            line["attention"] = {"config": "config2: 32 q / 8 KV heads, hd 128, f16 KV, RoPE 1e6; per step append + attend, one layer",
+                                 "api": "zllm_qkv_append + zllm_attn_decode (device buffers)", "peak_gbs": peak, **attn}
+        if decode:
+            line["decode"] = {"metric": "8B Q4_K_M decode tok/s (config 3)", "unit": "tok/s",
+                              "model": "Qwen3-8B shapes, random init: Q4_K + Q6_K ffn_down, f16 output head",
+                              "kv": f"f16, ctx {DEC_CTX}", "prompt": DEC_PROMPT, "steps": DEC_STEPS,
+                              "api": "zllm_model_generate (greedy, argmax fed back on the device)",
+                              "scaling": "weak (one model replica and its sequences per GPU)", **decode}
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds, os.cpu_count() or 1)
         print(json.dumps(line), flush=True)
@@ -360,9 +576,17 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="plain launches without graphs or timing, for ncu")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
+    ap.add_argument("--profile-decode", type=int, default=0, metavar="NSEQ",
+                    help="only the 8B decode at NSEQ sequences, 2 steps inside an NVTX range 'decode' (for ncu)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args.gpus)
+    if args.profile_decode:
+        import torch
+        torch.cuda.set_device(local)
+        print(json.dumps({"profile_decode": decode_bench(args.profile_decode, local, profile=True)}))
+        return
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)

@@ -84,7 +84,9 @@ int zllm_quantize_act(zllm_ctx *ctx, const float *x, int64_t k, int ntok, int8_t
                       void *stream);
 
 /* y[t*y_stride + r] = (y_add ? y_add[t*y_stride + r] : 0) + dot(W[r], act_t) for r < rows, t < ntok.
- * Quantized W reads the quantized activation (xq, xd, xs); F16/BF16/F32 W reads x.
+ * Quantized W reads the quantized activation (xq, xd, xs); F16/BF16/F32 W reads x.  A one-token
+ * product on a k-quant W (Q4_K, Q5_K, Q6_K) may pass xq = NULL and the f32 x: the GEMV quantizes it
+ * itself, bit-exactly as zllm_quantize_act.
  * Replaces the per-type kernels matvec_* / mm_* (src/compute/wasm/kernels.js:30-240,
  * src/compute/wasm/kquant-kernels.js:337-504) and the dispatch in src/compute/worker.js:251-270.
  * y_add == y gives the in-place residual add of worker.js:346 / :432. */
