@@ -301,7 +301,7 @@ def attn_bench(device: int, reps: int = 20):
     with N(0,1) at 2048 / 8192 / 32768 positions, batch 1 and 64 sequences.  A step appends one
     token's K/V (f32 -> f16, q/k RMSNorm, RoPE theta 1e6) and attends over the cache; timed as a
     graph of `reps` steps.  Also the restore of a 1024-position prefix slot (a byte copy of f16
-    K and V) into every sequence of one layer."""
+    K and V) into every sequence of one layer: 128 zllm_kv_copy calls recorded in a graph."""
     import torch
 
     from zerollm_b200.attention import KVCache, attn_decode, kv_copy, qkv_append, rope_tables
@@ -367,11 +367,18 @@ def attn_bench(device: int, reps: int = 20):
                 kv_copy(ctx, g, dst.block(sq, 0, isv), dst.head_stride, slot.block(0, 0, isv), slot.head_stride, n, stream=sid)
     with torch.cuda.stream(stream):
         restore()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        restore()
+    with torch.cuda.stream(stream):
+        gr.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        restore()
+        gr.replay()
         e1.record(stream)
     torch.cuda.synchronize()
+    del gr
     assert torch.equal(dst.t[5, 0, :, :, :n], slot.t[0, 0])
     us = e0.elapsed_time(e1) * 1e3
     moved = nseq * 2 * nkv * n * hd * 2

@@ -67,16 +67,23 @@ extern "C" int zllm_qkv_append(zllm_ctx *c, const zllm_attn_geom *g, int ntok, c
   return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "qkv_append launch");
 }
 
-// context splits of a decode attention launch: one per kAttnSplit positions of the longest sequence
+// context splits of a decode attention launch: those of the longest sequence (attn_nsplit is
+// non-decreasing in the length)
 int zllm_attn_splits(const zllm_ctx *c, const zllm_attn_geom *g, int nseq, int max_pos) {
   (void)c; (void)g; (void)nseq;
-  const int ns = (max_pos + kAttnSplit - 1) / kAttnSplit;
-  return ns < 1 ? 1 : ns;
+  return attn_nsplit(max_pos);
 }
 
 int zllm_attn_launch(zllm_ctx *c, const zllm_attn_geom *g, const float *q, const void *kcache, const void *vcache,
                      const int32_t *npos, int nseq, int nsplit, float *out, float *partial, int32_t *counters,
                      cudaStream_t s, const int32_t *seq) {
+  // each lane reads head_dim / 32 elements of a row as one vector load: the caches and the
+  // strides must keep that vector aligned
+  const int64_t elt = g->kv_f16 ? 2 : 4, vec = (g->head_dim / 32) * elt;
+  if ((uintptr_t)kcache % vec || (uintptr_t)vcache % vec || (g->seq_stride * elt) % vec || (g->head_stride * elt) % vec) {
+    zllm_set_error(c, "zllm_attn_decode: caches and strides must be %lld-byte aligned", (long long)vec);
+    return ZLLM_E_ARG;
+  }
   AttnArgs a{};
   a.seq = seq;
   a.q = q; a.kcache = kcache; a.vcache = vcache; a.seq_stride = g->seq_stride; a.head_stride = g->head_stride;
@@ -151,7 +158,12 @@ extern "C" int zllm_kv_copy(zllm_ctx *c, const zllm_attn_geom *g, void *dst, int
   }
   if (n == 0) return ZLLM_OK;
   const size_t el = g->kv_f16 ? 2 : 4;
-  cudaError_t e = cudaMemcpy2DAsync(dst, dst_hs * el, src, src_hs * el, (size_t)n * g->head_dim * el, g->n_head_kv,
-                                    cudaMemcpyDeviceToDevice, pick_stream(c, stream));
+  if (((uintptr_t)dst | (uintptr_t)src | (uintptr_t)(dst_hs * el) | (uintptr_t)(src_hs * el) |
+       (uintptr_t)((size_t)n * g->head_dim * el)) % 16) {
+    zllm_set_error(c, "zllm_kv_copy: blocks, head strides and the copied rows must be multiples of 16 bytes");
+    return ZLLM_E_ARG;
+  }
+  cudaError_t e = launch_kv_block_copy(dst, dst_hs * el, 0, src, src_hs * el, 0, (int64_t)n * g->head_dim * el,
+                                       g->n_head_kv, 1, c->num_sms, pick_stream(c, stream));
   return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "zllm_kv_copy");
 }

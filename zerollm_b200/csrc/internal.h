@@ -57,9 +57,25 @@ struct QkvPostArgs {
   double eps;
 };
 
-// decode attention: positions per context split (fixed, so a query's partition depends on its own
-// length only); a launch needs ceil(max_pos / kAttnSplit) splits
-constexpr int kAttnSplit = 256;
+// decode attention: a sequence of n positions is cut into context splits whose number and length
+// depend on n alone (so a query's partition, and its bits, do not depend on the batch around it).
+// At least kAttnMinSplit positions per split, at most kAttnSplitCap splits until the splits reach
+// kAttnMaxSplit positions: 37 splits x 8 KV heads = 296 CTAs = two per SM of the 148.
+// attn_nsplit is non-decreasing in n, so a launch sized for the longest sequence fits every other.
+constexpr int kAttnWarps = 8, kAttnMinSplit = 128, kAttnMaxSplit = 1024, kAttnSplitCap = 37;
+__host__ __device__ inline int attn_nsplit(int n) {
+  int ns = (n + kAttnMinSplit - 1) / kAttnMinSplit;
+  if (ns > kAttnSplitCap) ns = kAttnSplitCap;
+  const int big = (n + kAttnMaxSplit - 1) / kAttnMaxSplit;
+  if (ns < big) ns = big;
+  return ns < 1 ? 1 : ns;
+}
+// positions per warp of a split (the split is kAttnWarps times that)
+__host__ __device__ inline int attn_warp_len(int n) {
+  const int ns = attn_nsplit(n);
+  const int per = (n + ns - 1) / ns;
+  return (per + kAttnWarps - 1) / kAttnWarps;
+}
 
 struct AttnArgs {
   const float *q;                  // [nseq][n_head][head_dim]
@@ -68,7 +84,7 @@ struct AttnArgs {
   int64_t seq_stride, head_stride;
   const int *npos;                 // positions to attend per sequence (device)
   float *out;                      // [nseq][n_head][head_dim]
-  float *partial;                  // [nseq * n_kv][nsplit][group * (head_dim + 2)] scratch (nsplit >= ceil(npos / kAttnSplit))
+  float *partial;                  // [nseq * n_kv][nsplit][group * (head_dim + 2)] scratch (nsplit >= attn_nsplit(npos))
   int *counters;                   // [nseq * n_kv], zero between launches
   unsigned *status;
   float scale;
@@ -79,6 +95,8 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t s, bool pdl);
 bool attn_supported(int head_dim, int group);
 size_t attn_smem_bytes(int head_dim, int group, bool f16);
 cudaError_t launch_attn(const AttnArgs &a, bool f16, cudaStream_t s, bool pdl);
+cudaError_t launch_kv_block_copy(void *dst, int64_t dst_row, int64_t dst_blk, const void *src, int64_t src_row,
+                                 int64_t src_blk, int64_t row_bytes, int rows, int nblk, int num_sms, cudaStream_t s);
 cudaError_t launch_kv_convert(float *stage, void *cache, int n, int n_kv, int hd, int64_t head_stride, bool f16, int dir,
                               cudaStream_t s);
 

@@ -122,258 +122,201 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t s, bool pdl) {
 }
 
 // ============================================================================ decode attention
-// CTA = 8 warps, one (sequence, KV head, context split).  Tiles of TP positions of K and V are bulk
-// copied into a ring of shared-memory stages.  Per tile: (1) scores -- LP lanes share one position,
-// each dotting HD/LP dims for all G query heads of the group, reduced across the LP lanes; (2) an
-// online-softmax update of the running max / sum per head; (3) P.V -- each lane owns HD/32 dims of
-// every head of the group and accumulates over the warp's positions.  At the end the 8 warps'
-// accumulators are added, and the CTA either writes the final output (one split) or a partial
-// (max, sum, acc) that the last CTA of the (sequence, KV head) merges in split order.
-constexpr int kAttnWarps = 8;
-constexpr int kAttnTP = 64;                          // positions per tile
+// CTA = 8 warps, one (sequence, KV head, context split); the splits of a sequence of n positions
+// are attn_nsplit(n) runs of 8 x attn_warp_len(n) positions, and each warp streams its own
+// attn_warp_len(n) positions with no CTA barrier until the end.  Lane l holds dims
+// [l*DPL, (l+1)*DPL) of the G query heads and of their output accumulators.  Positions go in
+// batches of NB: K and V rows are read straight from HBM (coalesced, the next batch in flight
+// while the current one is used); a batch's NI = NB x G partial dot products are added across the
+// lanes by a butterfly reduce-scatter (lane l ends with index l / R, R = 32 / NI lanes holding each
+// score); an online softmax per head follows (the reference's softmax, ref-kernels.js:313-320,
+// computed with a running maximum); the batch's probabilities go through shared memory to every
+// lane for P.V.  At the end the 8 warps' (max, sum, acc) are merged in warp order, and a CTA
+// either writes the output (one split) or a partial that the last CTA of the (sequence, KV head)
+// merges in split order.  Every order is fixed by the sequence's length alone.
 
-template <typename T, int HD, int G>
-struct AttnCfg {
-  static constexpr int LP = G >= 8 ? 16 : (G >= 4 ? 8 : 4);   // lanes per position in the score phase
-  static constexpr int DPL = HD / LP;                        // dims per lane in the score phase
-  static constexpr int PPW = kAttnTP / kAttnWarps;           // positions per warp per tile
-  static constexpr int DPV = HD / 32;                        // dims per lane in the P.V phase
-  static constexpr int ROW = HD * (int)sizeof(T);            // bytes per cached position
-  static constexpr int TILE = kAttnTP * ROW;                 // bytes of one K (or V) tile
-  static constexpr int NS = sizeof(T) == 2 ? 3 : 2;          // stages (shared memory budget)
+template <typename T, int HD>
+struct KvRow {
+  static constexpr int DPL = HD / 32;                  // dims per lane
+  static constexpr int WORDS = DPL * (int)sizeof(T) / 4;  // 32-bit words per lane per row
+  uint32_t w[WORDS > 0 ? WORDS : 1];
+  __device__ __forceinline__ void load(const T *row, int lane) {
+    const uint8_t *p = reinterpret_cast<const uint8_t *>(row) + lane * DPL * sizeof(T);
+    if constexpr (WORDS == 4) { const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p)); w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w; }
+    else if constexpr (WORDS == 2) { const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p)); w[0] = v.x; w[1] = v.y; }
+    else { w[0] = __ldg(reinterpret_cast<const uint32_t *>(p)); }
+  }
+  __device__ __forceinline__ float get(int i) const {
+    if constexpr (sizeof(T) == 2) return h2f((w[i >> 1] >> (16 * (i & 1))) & 0xffffu);
+    else return __uint_as_float(w[i]);
+  }
 };
 
-__device__ __forceinline__ void load_row(const uint8_t *p, float *out, int n, bool f16) {
-  if (f16 && n % 8) {
-    for (int i = 0; i < n; i += 4) {
-      const uint2 v = *reinterpret_cast<const uint2 *>(p + 2 * i);
-      out[i] = h2f(v.x & 0xffffu); out[i + 1] = h2f(v.x >> 16); out[i + 2] = h2f(v.y & 0xffffu); out[i + 3] = h2f(v.y >> 16);
-    }
-  } else if (f16) {
-    for (int i = 0; i < n; i += 8) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(p + 2 * i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        out[i + 2 * j] = h2f(w[j] & 0xffffu);
-        out[i + 2 * j + 1] = h2f(w[j] >> 16);
-      }
-    }
-  } else {
-    for (int i = 0; i < n; i += 4) {
-      const float4 v = *reinterpret_cast<const float4 *>(p + 4 * i);
-      out[i] = v.x; out[i + 1] = v.y; out[i + 2] = v.z; out[i + 3] = v.w;
-    }
-  }
-}
-
 template <typename T, int HD, int G>
-__global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const AttnArgs a) {
-  using C = AttnCfg<T, HD, G>;
-  constexpr bool F16 = sizeof(T) == 2;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t *stage = smem;                                                     // [stages][K tile | V tile]
-  float *sc = reinterpret_cast<float *>(smem + C::NS * 2 * C::TILE);   // scores / probs [G][TP]
-  float *stat = sc + G * kAttnTP;                                            // m_new[G], alpha[G], l[G], m[G]
-  float *red = stat + 4 * G;                                                 // [warps][G][HD] accumulators
-  uint64_t *full = reinterpret_cast<uint64_t *>(red + kAttnWarps * G * HD);
-  uint64_t *empty = full + C::NS;
-  int *last_flag = reinterpret_cast<int *>(empty + C::NS);
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const AttnArgs a) {
+  constexpr int DPL = HD / 32;
+  // batch: 32 / G positions, fewer where K and V of two batches would not fit in registers
+  constexpr int NBMAX = 16 / KvRow<T, HD>::WORDS;
+  constexpr int NB = 32 / G < NBMAX ? 32 / G : NBMAX;
+  constexpr int NI = NB * G, R = 32 / NI;
+  __shared__ float sp[kAttnWarps][NB][G];               // a batch's probabilities
+  __shared__ float sa[kAttnWarps][G];                   // a batch's rescale factors
+  __shared__ float sm[kAttnWarps][G], sl[kAttnWarps][G];
+  __shared__ float sacc[kAttnWarps][G][HD];
+  __shared__ int last_flag;
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < C::NS; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], kAttnWarps); }
-    fence_mbar_init();
-  }
-  __syncthreads();
   pdl_launch_dependents();
   pdl_wait();                                         // q and the newest K/V row come from the previous kernel
-
-  // split s covers positions [s * kAttnSplit, (s + 1) * kAttnSplit): the partition depends on the
-  // sequence's own length only, so a query gets the same bits alone or in any batch
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  // the partition depends on the sequence's own length only, so a query gets the same bits alone
+  // or in any batch
   const int npos = a.npos[b];
-  const int active = npos > 0 ? (npos + kAttnSplit - 1) / kAttnSplit : 1;
+  const int ppw = attn_warp_len(npos), slen = ppw * kAttnWarps;
+  const int active = npos > 0 ? (npos + slen - 1) / slen : 1;
   if (split >= active) return;                        // nothing of this sequence here (no partial, no count)
-  const int t0 = min(npos, split * kAttnSplit), t1 = min(npos, t0 + kAttnSplit);
-  const int ntiles = (t1 - t0 + kAttnTP - 1) / kAttnTP;
+  const int t0 = min(npos, split * slen), t1 = min(npos, t0 + slen);
+  const int w0 = min(t1, t0 + warp * ppw), w1 = min(t1, w0 + ppw);
   const int64_t cs = a.seq ? a.seq[b] : b;            // cache sequence of this query
-  const uint8_t *kbase = reinterpret_cast<const uint8_t *>(a.kcache) +
-                         (cs * a.seq_stride + (int64_t)kh * a.head_stride + (int64_t)t0 * HD) * sizeof(T);
-  const uint8_t *vbase = reinterpret_cast<const uint8_t *>(a.vcache) +
-                         (cs * a.seq_stride + (int64_t)kh * a.head_stride + (int64_t)t0 * HD) * sizeof(T);
+  const T *kbase = reinterpret_cast<const T *>(a.kcache) + cs * a.seq_stride + (int64_t)kh * a.head_stride;
+  const T *vbase = reinterpret_cast<const T *>(a.vcache) + cs * a.seq_stride + (int64_t)kh * a.head_stride;
 
-  // q of the group's heads: lane holds dims [dc*DPL, +DPL) for the score phase
-  const int p_in = lane / C::LP, dc = lane % C::LP;
-  float q[G][C::DPL];
+  float q[G][DPL], acc[G][DPL];
 #pragma unroll
   for (int g = 0; g < G; g++) {
-    const float *qs = a.q + ((int64_t)b * a.n_head + kh * G + g) * HD + dc * C::DPL;
+    const float *qs = a.q + ((int64_t)b * a.n_head + kh * G + g) * HD + lane * DPL;
 #pragma unroll
-    for (int i = 0; i < C::DPL; i++) q[g][i] = qs[i];
+    for (int i = 0; i < DPL; i++) { q[g][i] = qs[i]; acc[g][i] = 0.f; }
   }
-  float acc[G][C::DPV];
-#pragma unroll
-  for (int g = 0; g < G; g++)
-#pragma unroll
-    for (int i = 0; i < C::DPV; i++) acc[g][i] = 0.f;
-  if (threadIdx.x < G) { stat[3 * G + threadIdx.x] = -INFINITY; stat[2 * G + threadIdx.x] = 0.f; }
+  // running max / sum of head (lane % G), kept identically by every lane of that head
+  float m_run = -INFINITY, l_run = 0.f;
+  const int my_i = lane / R, my_h = my_i % G, my_p = my_i / G;
 
-  int issued = 0;
-  auto issue = [&](int i) {                            // thread 0 only
-    const int s = i % C::NS;
-    const int rows = min(kAttnTP, t1 - t0 - i * kAttnTP);
-    const uint32_t bytes = (uint32_t)(rows * C::ROW);
-    mbar_arrive_expect_tx(&full[s], 2 * bytes);
-    bulk_g2s(stage + (size_t)s * 2 * C::TILE, kbase + (int64_t)i * C::TILE, bytes, &full[s]);
-    bulk_g2s(stage + (size_t)s * 2 * C::TILE + C::TILE, vbase + (int64_t)i * C::TILE, bytes, &full[s]);
+  KvRow<T, HD> kr[NB], vr[NB];
+  auto load_batch = [&](int p0, KvRow<T, HD> (&k)[NB], KvRow<T, HD> (&v)[NB]) {
+#pragma unroll
+    for (int j = 0; j < NB; j++) {
+      const int p = min(p0 + j, w1 - 1);               // past the end: repeat the last row (masked below)
+      k[j].load(kbase + (int64_t)p * HD, lane);
+      v[j].load(vbase + (int64_t)p * HD, lane);
+    }
   };
-  if (threadIdx.x == 0)
-    for (; issued < ntiles && issued < C::NS; issued++) issue(issued);
-  issued = min(ntiles, C::NS);
-  __syncthreads();
-
-  const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
-  bool aborted = false;
-  for (int i = 0; i < ntiles; i++) {
-    const int s = i % C::NS;
-    const bool ok = mbar_wait_bounded(&full[s], (i / C::NS) & 1, deadline);
-    if (!__syncthreads_and(ok)) { aborted = true; break; }   // uniform across the CTA
-    const uint8_t *kt = stage + (size_t)s * 2 * C::TILE, *vt = kt + C::TILE;
-    const int rows = min(kAttnTP, t1 - t0 - i * kAttnTP);
-    // (1) scores
+  if (w0 < w1) load_batch(w0, kr, vr);
+  for (int p0 = w0; p0 < w1; p0 += NB) {
+    KvRow<T, HD> kc[NB], vc[NB];
 #pragma unroll
-    for (int pass = 0; pass < C::PPW * C::LP / 32; pass++) {
-      const int tp = warp * C::PPW + pass * (32 / C::LP) + p_in;
-      float kv[C::DPL];
-      load_row(kt + (size_t)min(tp, rows - 1) * C::ROW + dc * C::DPL * sizeof(T), kv, C::DPL, F16);
-      float d[G];
+    for (int j = 0; j < NB; j++) { kc[j] = kr[j]; vc[j] = vr[j]; }
+    if (p0 + NB < w1) load_batch(p0 + NB, kr, vr);    // the next batch streams while this one is used
+    // partial scores, index j * G + g
+    float v32[NI];
+#pragma unroll
+    for (int j = 0; j < NB; j++)
 #pragma unroll
       for (int g = 0; g < G; g++) {
-        float s0 = 0.f;
+        float d = 0.f;
 #pragma unroll
-        for (int j = 0; j < C::DPL; j++) s0 = __fmaf_rn(q[g][j], kv[j], s0);
-        d[g] = s0;
+        for (int i = 0; i < DPL; i++) d = __fmaf_rn(q[g][i], kc[j].get(i), d);
+        v32[j * G + g] = d;
       }
+    // butterfly reduce-scatter: lane l ends with the full sum of index l / R (the R lanes of an
+    // index add the same two values at each step, so they hold the same bits)
 #pragma unroll
-      for (int o = C::LP / 2; o > 0; o >>= 1)
+    for (int o = 16, n = NI; o > 0; o >>= 1, n >>= 1) {
+      if (n > 1) {
+        const bool up = lane & o;
 #pragma unroll
-        for (int g = 0; g < G; g++) d[g] = __fadd_rn(d[g], __shfl_xor_sync(0xffffffffu, d[g], o));
-      if (dc == 0)
-#pragma unroll
-        for (int g = 0; g < G; g++) sc[g * kAttnTP + tp] = tp < rows ? d[g] * a.scale : -INFINITY;
-    }
-    __syncthreads();
-    // (2) online softmax: warp g < G owns head g
-    if (warp < G) {
-      const float v0 = sc[warp * kAttnTP + lane], v1 = sc[warp * kAttnTP + lane + 32];
-      float mx = fmaxf(v0, v1);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_old = stat[3 * G + warp];
-      const float m_new = fmaxf(m_old, mx);
-      const float p0 = expf(v0 - m_new), p1 = expf(v1 - m_new);
-      sc[warp * kAttnTP + lane] = p0;
-      sc[warp * kAttnTP + lane + 32] = p1;
-      float ps = p0 + p1;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      if (lane == 0) {
-        const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-        stat[G + warp] = alpha;
-        stat[2 * G + warp] = stat[2 * G + warp] * alpha + ps;
-        stat[3 * G + warp] = m_new;
-      }
-    }
-    __syncthreads();
-    // (3) P.V over this warp's positions
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-      const float al = stat[G + g];
-#pragma unroll
-      for (int i2 = 0; i2 < C::DPV; i2++) acc[g][i2] *= al;
-    }
-    for (int j = 0; j < C::PPW; j++) {
-      const int tp = warp * C::PPW + j;
-      if (tp >= rows) break;
-      float vv[C::DPV];
-      const uint8_t *vr = vt + (size_t)tp * C::ROW + lane * C::DPV * sizeof(T);
-      if (F16) {
-        if (C::DPV == 4) {
-          const uint2 w = *reinterpret_cast<const uint2 *>(vr);
-          vv[0] = h2f(w.x & 0xffffu); vv[1] = h2f(w.x >> 16); vv[2] = h2f(w.y & 0xffffu); vv[3] = h2f(w.y >> 16);
-        } else {
-          const uint32_t w = *reinterpret_cast<const uint32_t *>(vr);
-          vv[0] = h2f(w & 0xffffu); vv[C::DPV - 1] = h2f(w >> 16);
+        for (int i = 0; i < n / 2; i++) {
+          const float send = up ? v32[i] : v32[i + n / 2];
+          const float keep = up ? v32[i + n / 2] : v32[i];
+          v32[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
         }
       } else {
-#pragma unroll
-        for (int i2 = 0; i2 < C::DPV; i2++) vv[i2] = reinterpret_cast<const float *>(vr)[i2];
+        v32[0] = __fadd_rn(v32[0], __shfl_xor_sync(0xffffffffu, v32[0], o));
       }
+    }
+    const bool valid = p0 + my_p < w1;
+    const float sc = valid ? v32[0] * a.scale : -INFINITY;
+    // online softmax per head over the batch (the positions of one head differ in the lane bits
+    // >= log2(R * G); the R copies of a score are not added twice)
+    float mx = sc;
 #pragma unroll
-      for (int g = 0; g < G; g++) {
-        const float pg = sc[g * kAttnTP + tp];
+    for (int o = R * G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float m_new = fmaxf(m_run, mx);
+    const float pr = valid ? expf(sc - m_new) : 0.f;
+    float ps = pr;
 #pragma unroll
-        for (int i2 = 0; i2 < C::DPV; i2++) acc[g][i2] = __fmaf_rn(pg, vv[i2], acc[g][i2]);
-      }
+    for (int o = R * G; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+    l_run = __fmaf_rn(l_run, alpha, ps);
+    m_run = m_new;
+    if (lane % R == 0) {
+      sp[warp][my_p][my_h] = pr;
+      if (my_i < G) sa[warp][my_i] = alpha;
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    if (threadIdx.x == 0 && issued < ntiles) {
-      if (mbar_wait_bounded(&empty[s], (i / C::NS) & 1, deadline)) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        issue(issued);
-      } else {
-        atomicOr(a.status, ST_EMPTY_TIMEOUT);
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      const float al = sa[warp][g];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) acc[g][i] *= al;
+    }
+#pragma unroll
+    for (int j = 0; j < NB; j++) {
+      float pj[G];
+#pragma unroll
+      for (int g = 0; g < G; g++) pj[g] = sp[warp][j][g];
+#pragma unroll
+      for (int i = 0; i < DPL; i++) {
+        const float vv = vc[j].get(i);
+#pragma unroll
+        for (int g = 0; g < G; g++) acc[g][i] = __fmaf_rn(pj[g], vv, acc[g][i]);
       }
     }
-    issued = min(issued + (issued < ntiles ? 1 : 0), ntiles);
-    __syncthreads();                                  // scores are rewritten by the next tile
+    __syncwarp();                                      // sp / sa are rewritten by the next batch
   }
-  if (aborted) {
-    if (threadIdx.x == 0) atomicOr(a.status, ST_FULL_TIMEOUT);
+  // merge the 8 warps in warp order (lane g * R holds head g's running max and sum)
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    const float lg = __shfl_sync(0xffffffffu, l_run, g * R);
+    const float mg = __shfl_sync(0xffffffffu, m_run, g * R);
+    if (lane == 0) { sl[warp][g] = lg; sm[warp][g] = mg; }
   }
-  if (threadIdx.x == 0) {
-    // copies still in flight (only after an abort) must land before the CTA exits
-    const uint64_t dd = globaltimer_ns() + WAIT_DEADLINE_NS;
-    for (int s = 0; s < C::NS && s < issued; s++) {
-      const int last = s + ((issued - 1 - s) / C::NS) * C::NS;
-      if (!mbar_wait_bounded(&full[s], (last / C::NS) & 1, dd)) atomicOr(a.status, ST_DRAIN_TIMEOUT);
-    }
-  }
-  // add the warps' accumulators
 #pragma unroll
   for (int g = 0; g < G; g++)
 #pragma unroll
-    for (int i2 = 0; i2 < C::DPV; i2++) red[((size_t)warp * G + g) * HD + lane * C::DPV + i2] = acc[g][i2];
-  __syncthreads();
-  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
-    float sum = 0.f;
-    for (int w = 0; w < kAttnWarps; w++) sum += red[(size_t)w * G * HD + e];
-    red[e] = sum;                                       // warp 0's slot now holds the CTA total
-  }
+    for (int i = 0; i < DPL; i++) sacc[warp][g][lane * DPL + i] = acc[g][i];
   __syncthreads();
   const int64_t grp = (int64_t)b * a.n_kv + kh;
-  if (active == 1) {
-    for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
-      const int g = e / HD;
-      const float l = stat[2 * G + g];
-      a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = l > 0.f ? red[e] / l : 0.f;
-    }
-    return;
-  }
-  // partial: [grp][split] -> m[G], l[G], acc[G][HD]
   float *part = a.partial + (grp * a.nsplit + split) * (size_t)(G * (HD + 2));
-  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) part[2 * G + e] = red[e];
-  if (threadIdx.x < G) { part[threadIdx.x] = stat[3 * G + threadIdx.x]; part[G + threadIdx.x] = stat[2 * G + threadIdx.x]; }
+  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+    const int g = e / HD, d = e % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm[w][g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) {
+      if (sm[w][g] == -INFINITY) continue;
+      const float f = expf(sm[w][g] - M);
+      L = __fmaf_rn(sl[w][g], f, L);
+      O = __fmaf_rn(sacc[w][g][d], f, O);
+    }
+    if (active == 1) {
+      a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
+    } else {
+      part[2 * G + e] = O;
+      if (d == 0) { part[g] = M; part[G + g] = L; }
+    }
+  }
+  if (active == 1) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const int done = atomicAdd(a.counters + grp, 1);
-    *last_flag = done == active - 1;
+    last_flag = done == active - 1;
   }
   __syncthreads();
-  if (!*last_flag) return;
+  if (!last_flag) return;
   __threadfence();
   // merge the active splits in split order (deterministic)
   for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
@@ -396,27 +339,41 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_decode_kernel(const A
   if (threadIdx.x == 0) a.counters[grp] = 0;            // ready for the next launch
 }
 
+// ============================================================================ KV block copy
+// nblk blocks of `rows` rows of row_bytes (a multiple of 16) each, between arbitrary row / block
+// strides: the prefix-slot save and restore (every layer's K and V of a sequence in one launch) and
+// zllm_kv_copy.  16-byte loads and stores, grid-stride; a byte copy, so bit-exact by construction.
+__global__ void kv_block_copy_kernel(uint8_t *__restrict__ dst, int64_t dst_row, int64_t dst_blk,
+                                     const uint8_t *__restrict__ src, int64_t src_row, int64_t src_blk, int64_t row_bytes,
+                                     int rows, int nblk) {
+  const int64_t per_row = row_bytes / 16, per_blk = per_row * rows, total = per_blk * nblk;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / per_blk, rem = i % per_blk, r = rem / per_row, c = rem % per_row;
+    const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src + b * src_blk + r * src_row) + c);
+    reinterpret_cast<uint4 *>(dst + b * dst_blk + r * dst_row)[c] = v;
+  }
+}
+
+cudaError_t launch_kv_block_copy(void *dst, int64_t dst_row, int64_t dst_blk, const void *src, int64_t src_row,
+                                 int64_t src_blk, int64_t row_bytes, int rows, int nblk, int num_sms, cudaStream_t s) {
+  const int64_t chunks = row_bytes / 16 * rows * nblk;
+  if (chunks <= 0) return cudaSuccess;
+  int64_t grid = (chunks + 255) / 256;
+  if (grid > (int64_t)num_sms * 8) grid = (int64_t)num_sms * 8;
+  kv_block_copy_kernel<<<(unsigned)grid, 256, 0, s>>>((uint8_t *)dst, dst_row, dst_blk, (const uint8_t *)src, src_row,
+                                                       src_blk, row_bytes, rows, nblk);
+  return cudaGetLastError();
+}
+
 size_t attn_smem_bytes(int head_dim, int group, bool f16) {
-  const size_t tile = (size_t)kAttnTP * head_dim * (f16 ? 2 : 4);
-  const int ns = f16 ? 3 : 2;
-  return ns * 2 * tile + sizeof(float) * (group * kAttnTP + 4 * group + (size_t)kAttnWarps * group * head_dim) +
-         2 * ns * 8 + 16;
+  (void)head_dim; (void)group; (void)f16;
+  return 0;                                           // static shared memory only
 }
 
 template <typename T, int HD, int G>
 static cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s, bool pdl) {
   auto kern = attn_decode_kernel<T, HD, G>;
-  const size_t smem = attn_smem_bytes(HD, G, sizeof(T) == 2);
-  static bool granted[64] = {false};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!granted[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    granted[dev] = true;
-  }
+  const size_t smem = 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nsplit, a.n_kv, a.nseq);
   cfg.blockDim = dim3(kAttnWarps * 32);

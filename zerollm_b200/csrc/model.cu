@@ -644,14 +644,11 @@ extern "C" int zllm_model_slot_save(zllm_model *m, int seq, int n) {
     CK(cudaMalloc(&m->slot, (size_t)m->c.n_layer * 2 * m->kvdim() * n * m->el()), "cudaMalloc(prefix slot)");
     m->slot_cap = n;
   }
-  const zllm_attn_geom g = m->geom();
-  const int64_t slot_hs = (int64_t)m->slot_cap * m->c.head_dim;
-  for (int l = 0; l < m->c.n_layer; l++)
-    for (int v = 0; v < 2; v++) {
-      uint8_t *dst = (uint8_t *)m->slot + ((int64_t)l * 2 + v) * m->kvdim() * m->slot_cap * m->el();
-      int rc = zllm_kv_copy(m->ctx, &g, dst, slot_hs, m->kv_block(seq, l, v), g.head_stride, n, m->stream);
-      if (rc) return rc;
-    }
+  // every layer's K and V blocks in one launch: [layer][k|v][n_kv][n][hd] out of the cache
+  const int64_t el = (int64_t)m->el(), hd = m->c.head_dim, KV = m->kvdim();
+  CK(launch_kv_block_copy(m->slot, (int64_t)m->slot_cap * hd * el, KV * m->slot_cap * el, m->kv_block(seq, 0, 0),
+                          (int64_t)m->c.ctx * hd * el, KV * m->c.ctx * el, (int64_t)n * hd * el, m->c.n_head_kv,
+                          m->c.n_layer * 2, m->ctx->num_sms, m->stream), "slot save");
   CK(cudaStreamSynchronize(m->stream), "slot save");
   m->slot_n = n;
   return ZLLM_OK;
@@ -660,14 +657,10 @@ extern "C" int zllm_model_slot_save(zllm_model *m, int seq, int n) {
 extern "C" int zllm_model_slot_restore(zllm_model *m, int seq) {
   if (!m || seq < 0 || seq >= m->c.n_seq) return ZLLM_E_ARG;
   if (!m->slot || m->slot_n == 0) { zllm_set_error(m->ctx, "no prefix slot saved"); return ZLLM_E_STATE; }
-  const zllm_attn_geom g = m->geom();
-  const int64_t slot_hs = (int64_t)m->slot_cap * m->c.head_dim;
-  for (int l = 0; l < m->c.n_layer; l++)
-    for (int v = 0; v < 2; v++) {
-      const uint8_t *src = (const uint8_t *)m->slot + ((int64_t)l * 2 + v) * m->kvdim() * m->slot_cap * m->el();
-      int rc = zllm_kv_copy(m->ctx, &g, m->kv_block(seq, l, v), g.head_stride, src, slot_hs, m->slot_n, m->stream);
-      if (rc) return rc;
-    }
+  const int64_t el = (int64_t)m->el(), hd = m->c.head_dim, KV = m->kvdim();
+  CK(launch_kv_block_copy(m->kv_block(seq, 0, 0), (int64_t)m->c.ctx * hd * el, KV * m->c.ctx * el, m->slot,
+                          (int64_t)m->slot_cap * hd * el, KV * m->slot_cap * el, (int64_t)m->slot_n * hd * el,
+                          m->c.n_head_kv, m->c.n_layer * 2, m->ctx->num_sms, m->stream), "slot restore");
   CK(cudaStreamSynchronize(m->stream), "slot restore");
   m->pos[seq] = m->slot_n;
   return ZLLM_OK;
