@@ -140,7 +140,7 @@ extern "C" int zllm_weight_upload(zllm_ctx *c, int type, int64_t rows, int64_t c
   w->m.rows = rows;
   w->m.cols = cols;
   w->m.row_stride = dev_row_stride(type, cols);
-  w->bytes = (size_t)(w->m.row_stride * rows);
+  w->bytes = (size_t)dev_matrix_bytes(type, rows, cols);
   cudaSetDevice(c->device);
   cudaError_t e = cudaMalloc((void **)&w->m.data, w->bytes);
   if (e != cudaSuccess) { delete w; return zllm_cuda_fail(c, e, "cudaMalloc(weight)"); }

@@ -315,28 +315,34 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs p) 
 // ============================================================================ repack (load time)
 __global__ void repack_kernel(int type, const uint8_t *raw, int64_t raw_row, uint8_t *dst, int64_t stride,
                               int64_t rows, int nb) {
+  const bool kq = type == T_Q4_K || type == T_Q5_K || type == T_Q6_K;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const uint8_t *s = raw + r * raw_row;
+    if (kq) {
+      // the k-quants: each byte to its place in the (tile, super-block) units (kq_layout.h)
+      for (int64_t i = threadIdx.x; i < raw_row; i += blockDim.x) {
+        uint8_t v = s[i];
+        if (type != T_Q6_K) {
+          const int bs = type == T_Q4_K ? 144 : 176;
+          const int e = (int)(i % bs);
+          if (e >= 4 && e < 16) {
+            // byte e of the 12-byte scale table: rebuilt from the whole table (quant.js:109-118)
+            const uint8_t *q = s + (i - e) + 4;
+            const int j = (e - 4) / 3, k = (e - 4) % 3;      // chunk j, byte k of its 24-bit field
+            auto scale = [&](int t) { return t < 4 ? q[t] & 63 : (q[t + 4] & 15) | ((q[t - 4] >> 6) << 4); };
+            auto minv = [&](int t) { return t < 4 ? q[t + 4] & 63 : (q[t + 4] >> 4) | ((q[t] >> 6) << 4); };
+            const uint32_t f = scale(2 * j) | (scale(2 * j + 1) << 6) | (minv(2 * j) << 12) | (minv(2 * j + 1) << 18);
+            v = (uint8_t)(f >> (8 * k));
+          }
+        }
+        dst[kq_dev_pos(type, r, i, nb)] = v;
+      }
+      continue;
+    }
     uint8_t *d = dst + r * stride;
     for (int64_t i = threadIdx.x; i < raw_row; i += blockDim.x) {
       int64_t o = i;
-      if (type == T_Q4_K || type == T_Q5_K) {
-        const int bs = type == T_Q4_K ? 144 : 176;
-        const int e = (int)(i % bs);
-        if (e >= 4 && e < 16) {
-          // byte e of the 12-byte scale table: rebuilt from the whole table (quant.js:109-118)
-          const uint8_t *q = s + (i - e) + 4;
-          const int j = (e - 4) / 3, k = (e - 4) % 3;      // chunk j, byte k of its 24-bit field
-          auto scale = [&](int t) { return t < 4 ? q[t] & 63 : (q[t + 4] & 15) | ((q[t - 4] >> 6) << 4); };
-          auto minv = [&](int t) { return t < 4 ? q[t + 4] & 63 : (q[t + 4] >> 4) | ((q[t] >> 6) << 4); };
-          const uint32_t f = scale(2 * j) | (scale(2 * j + 1) << 6) | (minv(2 * j) << 12) | (minv(2 * j + 1) << 18);
-          d[i] = (uint8_t)(f >> (8 * k));
-          continue;
-        }
-        o = kq_dev_offset(type, i, nb);
-      } else if (type == T_Q6_K) {
-        o = kq_dev_offset(type, i, nb);
-      } else if (type == T_Q8_0) {
+      if (type == T_Q8_0) {
         const int b = (int)(i / 34), e = (int)(i % 34);
         o = e < 2 ? 32LL * nb + b * 2 + e : b * 32 + (e - 2);
       } else if (type == T_Q4_0) {
@@ -349,6 +355,17 @@ __global__ void repack_kernel(int type, const uint8_t *raw, int64_t raw_row, uin
       d[o] = s[i];
     }
     for (int64_t i = raw_row + threadIdx.x; i < stride; i += blockDim.x) d[i] = 0;
+  }
+}
+
+// Rows src[0 .. nrows) of a k-quant matrix to rows dst_row0 + i * dst_step of another of the same
+// type and width (both in the unit layout): the concatenations of model.cu.
+__global__ void kq_copy_rows_kernel(int type, int nb, uint8_t *dst, int64_t dst_row0, int64_t dst_step,
+                                    const uint8_t *src, int64_t nrows) {
+  const int64_t rb = (int64_t)nb * kq_block_bytes(type);
+  for (int64_t r = blockIdx.x; r < nrows; r += gridDim.x) {
+    const int64_t rd = dst_row0 + r * dst_step;
+    for (int64_t i = threadIdx.x; i < rb; i += blockDim.x) dst[kq_dev_pos(type, rd, i, nb)] = src[kq_dev_pos(type, r, i, nb)];
   }
 }
 
@@ -381,11 +398,32 @@ int64_t dev_row_stride(int t, int64_t cols) {
   return rb < 0 ? -1 : (rb + 15) / 16 * 16;
 }
 
+int64_t dev_matrix_bytes(int t, int64_t rows, int64_t cols) {
+  if (t == T_Q4_K || t == T_Q5_K || t == T_Q6_K) return cols % 256 ? -1 : kq_matrix_bytes(t, rows, cols / 256);
+  const int64_t rs = dev_row_stride(t, cols);
+  return rs < 0 ? -1 : rs * rows;
+}
+
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s) {
   const int64_t rb = raw_row_bytes(m.type, m.cols);
-  const int nb = (int)(m.type == T_Q4_K || m.type == T_Q5_K || m.type == T_Q6_K ? m.cols / 256 : m.cols / 32);
+  const bool kq = m.type == T_Q4_K || m.type == T_Q5_K || m.type == T_Q6_K;
+  const int nb = (int)(kq ? m.cols / 256 : m.cols / 32);
+  if (kq && m.rows % kKqTile) {
+    // the rows that pad the last tile read as zeros
+    const cudaError_t e = cudaMemsetAsync(m.data, 0, (size_t)kq_matrix_bytes(m.type, m.rows, nb), s);
+    if (e != cudaSuccess) return e;
+  }
   const int64_t grid = m.rows < 65535 ? m.rows : 65535;
   repack_kernel<<<(unsigned)grid, 256, 0, s>>>(m.type, (const uint8_t *)raw_dev, rb, m.data, m.row_stride, m.rows, nb);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_kq_copy_rows(const DevMatrix &dst, int64_t dst_row0, int64_t dst_step, const DevMatrix &src,
+                                cudaStream_t s) {
+  if (dst.type != src.type || dst.cols != src.cols || !kq_type(src.type)) return cudaErrorInvalidValue;
+  const int64_t grid = src.rows < 65535 ? src.rows : 65535;
+  kq_copy_rows_kernel<<<(unsigned)grid, 256, 0, s>>>(src.type, (int)(src.cols / 256), dst.data, dst_row0, dst_step,
+                                                     src.data, src.rows);
   return cudaGetLastError();
 }
 

@@ -6,22 +6,22 @@
 // (src/compute/wasm/kquant-kernels.js:337-504), dispatched by ggml type as in
 // src/compute/worker.js:184-197 / :251-270.
 //
-// What one launch computes, for up to 8 tokens:  y[t][r] = (y_add) + sum over blocks of
+// What a launch computes, for 1..8 tokens:  y[t][r] = (y_add) + sum over blocks of
 //   Q4_K / Q5_K:  xd * (d*sc*lo - dmin*mn*xs)       per 32-value sub-block (ref-kernels.js:235-236)
 //   Q6_K:         xd * d * scale * gsum             per 16-value group     (ref-kernels.js:271)
 // where lo / gsum are exact integer dot products of the weight quants with the int8 activation.
 //
-// Structure.  A CTA owns a contiguous range of rows (the same count for every CTA, within one) and
-// walks it in tiles of 16 rows; a tile's rows are streamed HBM -> shared memory in chunks of 16
-// (Q6_K: 8) super-blocks by 1D bulk copies (one per row, each issued by its own lane of warp 0,
-// completion on an mbarrier), `nst` chunks in flight.  The copies of the first chunks are issued
-// before griddepcontrol.wait, so under programmatic dependent launch a matrix streams in while the
-// kernel before it is still computing.  Warp w takes super-blocks w and w + 8 of every chunk and
-// runs warp-level integer MMAs on them (mma.sync m16n8k32 / m16n8k16, int8 x uint8 -> int32, exact):
-//   * one token: the B operand is block-diagonal -- column j carries the activation of sub-block
-//     (group) j and is zero elsewhere -- so the 8 MMAs of a super-block leave the 16 rows x 8
-//     sub-blocks of integer dots in one accumulator, one value per lane and row pair;
-//   * 2..8 tokens: B column j carries token j, one MMA per sub-block (group).
+// The weights are stored as units of (16-row tile, super-block) (kq_layout.h); a CTA owns a
+// contiguous range of tiles, i.e. one contiguous range of HBM.  The integer dots are warp-level
+// MMAs (mma.sync m16n8k32 / m16n8k16, uint8 or int8 x int8 -> int32, exact) on a unit:
+//   * one token (kq_stream_kernel): the B operand is block-diagonal -- column j carries the
+//     activation of sub-block (group) j and is zero elsewhere -- so the 8 MMAs of a unit leave the
+//     16 rows x 8 sub-blocks of integer dots in one accumulator, one value per lane and row pair.
+//     Every warp streams its share of the CTA's units straight from HBM into registers (coalesced
+//     16-byte loads, a few units in flight), with no shared-memory staging of the weights;
+//   * 2..8 tokens (kq_tok_kernel): B column j carries token j, one MMA per sub-block (group); runs
+//     of units are staged in shared memory by 1D bulk copies (one per stage, completion on an
+//     mbarrier) and shared by the 8 warps.
 // Each integer dot becomes its block term in IEEE double with the reference's operations and
 // rounding (no fused multiply-add where the JS rounds twice), so every block term is bit-identical
 // to the oracle's.  Only the order of the final double additions differs from the reference, and
@@ -29,12 +29,8 @@
 // ((T0 + T1) + (T2 + T3)) + ((T4 + T5) + (T6 + T7)); Q6_K: the same over groups 0..7 plus the same
 // over 8..15) and the super-block sums are added in super-block order.  That order depends on
 // nothing but the row, so a token gets the same bits alone, in a batch, or in any launch shape.
-//
-// After each chunk one CTA barrier (which also carries the bounded waits' give-up flag to every
-// warp) publishes the chunk's super-block sums; one thread per output then adds them in order, and
-// warp 0 refills the freed stage.  A one-token launch may take the f32
-// activation and quantize it itself (bit-exact with quantize_act_kernel), so a lone matvec is one
-// kernel.
+// A one-token launch may take the f32 activation (optionally RMSNorm-ed first) and quantize it
+// itself, bit-exact with quantize_act_kernel, so a lone matvec is one kernel.
 #include "common.cuh"
 #include "internal.h"
 #include "kq_layout.h"
@@ -43,14 +39,14 @@ namespace zllm {
 
 namespace {
 
-constexpr int kTile = 16;                    // rows per tile (the MMA's M)
-// super-blocks per staged chunk: two per warp for Q4_K / Q5_K (processed together), one per warp for
-// Q6_K (its Q6_K SoA groups of 8, and twice the MMAs per super-block)
-template <int FMT> constexpr int chunk_sb() { return FMT == T_Q6_K ? 8 : 16; }
-__host__ __device__ constexpr int chunk_sb_of(int type) { return type == T_Q6_K ? 8 : 16; }
-constexpr int kMaxStages = 8;
-constexpr int kMaxTok = 8;                   // tokens per launch (the MMA's N)
-constexpr int64_t kSmemBudget = 110 * 1024;  // two CTAs per SM
+constexpr int kTile = kKqTile;               // rows per unit (the MMA's M)
+constexpr int kMaxTok = 8;                   // tokens per launch of the token kernel (the MMA's N)
+
+// unit regions (kq_layout.h)
+template <int FMT> constexpr int unit_bytes() { return FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360; }
+template <int FMT> constexpr int hdr_off() { return FMT == T_Q4_K ? 2048 : 2560; }   // Q4_K / Q5_K header region
+constexpr int kE5 = 2048;                                  // Q5_K high bits
+constexpr int kQ6H = 2048, kQ6S = 3072, kQ6D = 3328;        // Q6_K qh, scales, d
 
 // ---------------------------------------------------------------------------- tensor-core dots
 // C += A . B with A 16 x K uint8 (weights), B K x 8 int8 (activations), exact int32 accumulation.
@@ -136,111 +132,7 @@ struct SAct {
   uint32_t xq, xd, xs, xs16;    // shared-window addresses
   uint32_t sel[8];
 };
-
-// ---------------------------------------------------------------------------- per super-block, one token
-// One warp turns a staged super-block into its sum per row: lane (g, t) holds sub-blocks 2t, 2t+1
-// (Q6_K: groups 8h+2t, 8h+2t+1 of half h) of rows g and g+8, forms the pair sum T(2t) + T(2t+1),
-// and the quad tree over t gives ((p_0 + p_1) + (p_2 + p_3)) -- the super-block sum (Q6_K: the
-// half's tree; super-block = half 0 + half 1).  The token-mode routines build the same trees
-// within one lane.
-template <bool FIVE>
-__device__ __forceinline__ void sb_k45_one(uint32_t blk, int pitch, int g, int t, const SAct &x, int sb, double &p0,
-                                           double &p1) {
-  constexpr int QS = FIVE ? 48 : 16;
-  const uint32_t rg = blk + (uint32_t)(g * pitch), rh = blk + (uint32_t)((g + 8) * pitch);
-  uint2 eg = make_uint2(0, 0), eh = make_uint2(0, 0);
-  if (FIVE) { eg = lds64(rg + 16 + 8 * t); eh = lds64(rh + 16 + 8 * t); }
-  // this lane's activation column: sub-block g, values 4t.. and 16+4t..
-  const uint32_t xa = lds32(x.xq + sb * 256 + 32 * g + 4 * t), xb = lds32(x.xq + sb * 256 + 32 * g + 16 + 4 * t);
-  int C0[4] = {0, 0, 0, 0}, C1[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int cp = 0; cp < 2; cp++) {
-    // chunks 2cp, 2cp+1: words (half 0, half 1) of each, rows g and g+8
-    const uint4 wq = lds128(rg + QS + 32 * t + 16 * cp), vq = lds128(rh + QS + 32 * t + 16 * cp);
-    const uint32_t wg[4] = {wq.x, wq.y, wq.z, wq.w}, wh[4] = {vq.x, vq.y, vq.z, vq.w};
-#pragma unroll
-    for (int ci = 0; ci < 2; ci++) {
-      const int c = 2 * cp + ci;
-      uint32_t lg0 = wg[2 * ci] & 0x0f0f0f0fu, lg1 = wg[2 * ci + 1] & 0x0f0f0f0fu;
-      uint32_t lh0 = wh[2 * ci] & 0x0f0f0f0fu, lh1 = wh[2 * ci + 1] & 0x0f0f0f0fu;
-      uint32_t ug0, ug1, uh0, uh1;
-      if (FIVE) {
-        lg0 |= ((eg.x >> (2 * c)) & 0x01010101u) << 4; lg1 |= ((eg.y >> (2 * c)) & 0x01010101u) << 4;
-        lh0 |= ((eh.x >> (2 * c)) & 0x01010101u) << 4; lh1 |= ((eh.y >> (2 * c)) & 0x01010101u) << 4;
-        ug0 = ((wg[2 * ci] >> 4) & 0x0f0f0f0fu) | (((eg.x >> (2 * c + 1)) & 0x01010101u) << 4);
-        ug1 = ((wg[2 * ci + 1] >> 4) & 0x0f0f0f0fu) | (((eg.y >> (2 * c + 1)) & 0x01010101u) << 4);
-        uh0 = ((wh[2 * ci] >> 4) & 0x0f0f0f0fu) | (((eh.x >> (2 * c + 1)) & 0x01010101u) << 4);
-        uh1 = ((wh[2 * ci + 1] >> 4) & 0x0f0f0f0fu) | (((eh.y >> (2 * c + 1)) & 0x01010101u) << 4);
-      } else {
-        // high nibbles in place (16 x the quant, still an exact uint8): the word minus its low nibbles
-        ug0 = wg[2 * ci] - lg0; ug1 = wg[2 * ci + 1] - lg1;
-        uh0 = wh[2 * ci] - lh0; uh1 = wh[2 * ci + 1] - lh1;
-      }
-      int(&C)[4] = (c & 1) ? C1 : C0;
-      mma_k32(C, lg0, lh0, lg1, lh1, xa * x.sel[2 * c], xb * x.sel[2 * c]);
-      mma_k32(C, ug0, uh0, ug1, uh1, xa * x.sel[2 * c + 1], xb * x.sel[2 * c + 1]);
-    }
-  }
-  // lane (g, t): sub-blocks 2t and 2t+1 of rows g and g+8
-  int v0 = C0[0] + C1[0], v1 = C0[1] + C1[1], v2 = C0[2] + C1[2], v3 = C0[3] + C1[3];
-  if (!FIVE) { v1 >>= 4; v3 >>= 4; }
-  const uint4 xdw = lds128(x.xd + 8 * (sb * 8 + 2 * t));
-  const double xd0 = __hiloint2double((int)xdw.y, (int)xdw.x), xd1 = __hiloint2double((int)xdw.w, (int)xdw.z);
-  const uint2 xs = lds64(x.xs + 4 * (sb * 8 + 2 * t));
-  // d, dmin and this lane's 24-bit scale field (chunk t, bytes 4+3t .. 6+3t of the block)
-  const uint32_t fo = 4 + 3 * t, fw = fo & ~3u, fs = (fo & 3) * 8;
-#pragma unroll
-  for (int r = 0; r < 2; r++) {
-    const uint32_t row = r ? rh : rg;
-    const uint32_t dw = lds32(row), F = __funnelshift_r(lds32(row + fw), lds32(row + fw + 4), fs);
-    const double d = h2d(dw & 0xffffu), dmin = h2d(dw >> 16);
-    const double pr = __dadd_rn(k45_term(d, dmin, F & 63, (F >> 12) & 63, r ? v2 : v0, (int)xs.x, xd0),
-                                k45_term(d, dmin, (F >> 6) & 63, (F >> 18) & 63, r ? v3 : v1, (int)xs.y, xd1));
-    if (r) p1 = quad_tree(pr); else p0 = quad_tree(pr);
-  }
-}
-
-// Q6_K, half h of super-block j of a staged chunk (group of n super-blocks).
-__device__ __forceinline__ void sb_q6_one(uint32_t blk, int pitch, int n, int j, int h, int g, int t, const SAct &x,
-                                          int sb, double &p0, double &p1) {
-  const uint32_t rg = blk + (uint32_t)(g * pitch), rh = blk + (uint32_t)((g + 8) * pitch);
-  const uint32_t qlo = 128 * j + 32 * t + 16 * h, qho = 128 * n + 64 * j + 16 * t + 8 * h,
-                 sco = 192 * n + 16 * j + 4 * t + 2 * h, dof = 208 * n + 2 * j;
-  // ql words [u][p], qh words [u] of half h
-  const uint4 lg = lds128(rg + qlo), lh = lds128(rh + qlo);
-  const uint2 qg = lds64(rg + qho), qh = lds64(rh + qho);
-  const uint32_t lgw[4] = {lg.x, lg.y, lg.z, lg.w}, lhw[4] = {lh.x, lh.y, lh.z, lh.w};
-  const uint32_t qgw[2] = {qg.x, qg.y}, qhw[2] = {qh.x, qh.y};
-  // this lane's activation column: group 8h + g, values 4t..4t+3
-  const uint32_t xa = lds32(x.xq + sb * 256 + 16 * (8 * h + g) + 4 * t);
-  int C[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int u = 0; u < 2; u++) {
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const uint32_t a0 = q6_unpack(lgw[u * 2], lgw[u * 2 + 1], qgw[u], k);
-      const uint32_t a1 = q6_unpack(lhw[u * 2], lhw[u * 2 + 1], qhw[u], k);
-      mma_k16(C, a0, a1, xa * x.sel[2 * k + u]);
-    }
-  }
-  // lane (g, t): groups 8h+2t, 8h+2t+1 of rows g and g+8
-  const uint2 s2 = lds64(x.xs16 + 4 * (sb * 16 + 8 * h + 2 * t));
-  const uint2 xdw = lds64(x.xd + 8 * (sb * 8 + 4 * h + t));
-  const double xdv = __hiloint2double((int)xdw.y, (int)xdw.x);
-#pragma unroll
-  for (int r = 0; r < 2; r++) {
-    const uint32_t row = r ? rh : rg;
-    const uint32_t scw = lds16(row + sco);
-    const double xdd = __dmul_rn(xdv, h2d(lds16(row + dof)));
-    const double pr = __dadd_rn(q6_term(xdd, (int)(int8_t)(scw & 0xff), C[2 * r] - 32 * (int)s2.x),
-                                q6_term(xdd, (int)(int8_t)(scw >> 8), C[2 * r + 1] - 32 * (int)s2.y));
-    if (r) p1 = quad_tree(pr); else p0 = quad_tree(pr);
-  }
-}
-
-// ---------------------------------------------------------------------------- per super-block, 2..8 tokens
-// Lane (g, t) supplies token g's activation and owns outputs e = 2*ri + ti: row g + 8*ri, token
-// 2t + ti.  It builds the same per-super-block trees as the one-token path from all sub-blocks.
+// 2..8 tokens, read from global memory
 struct GAct {
   const int8_t *xq;     // [ntok][k]
   const float *xd;      // [ntok][k/32]
@@ -249,122 +141,12 @@ struct GAct {
   int ntok;
 };
 
-template <bool FIVE>
-__device__ __forceinline__ void sb_k45_tok(uint32_t blk, int pitch, int g, int t, const GAct &x, int sb, double (&S)[4]) {
-  constexpr int QS = FIVE ? 48 : 16;
-  const uint32_t rg = blk + (uint32_t)(g * pitch), rh = blk + (uint32_t)((g + 8) * pitch);
-  const uint4 hdr[2] = {lds128(rg), lds128(rh)};
-  const bool live = g < x.ntok;
-  const uint32_t *xw = reinterpret_cast<const uint32_t *>(x.xq + (live ? g : 0) * x.k + (int64_t)sb * 256);
-  const int t0 = 2 * t < x.ntok ? 2 * t : 0, t1 = 2 * t + 1 < x.ntok ? 2 * t + 1 : 0;   // padding tokens read token 0
-  const float *xd0 = x.xd + t0 * (x.k / 32) + sb * 8, *xd1 = x.xd + t1 * (x.k / 32) + sb * 8;
-  const int32_t *xs0 = x.xs + t0 * (x.k / 32) + sb * 8, *xs1 = x.xs + t1 * (x.k / 32) + sb * 8;
-  double dd[2], dm[2];
-#pragma unroll
-  for (int ri = 0; ri < 2; ri++) { dd[ri] = h2d(hdr[ri].x & 0xffffu); dm[ri] = h2d(hdr[ri].x >> 16); }
-  double q01[4];
-#pragma unroll
-  for (int c = 0; c < 4; c++) {
-    const uint2 wgc = lds64(rg + QS + 32 * t + 8 * c), whc = lds64(rh + QS + 32 * t + 8 * c);
-    uint32_t lg0 = wgc.x & 0x0f0f0f0fu, lg1 = wgc.y & 0x0f0f0f0fu, lh0 = whc.x & 0x0f0f0f0fu, lh1 = whc.y & 0x0f0f0f0fu;
-    uint32_t ug0, ug1, uh0, uh1;
-    if (FIVE) {
-      const uint2 eg = lds64(rg + 16 + 8 * t), eh = lds64(rh + 16 + 8 * t);
-      lg0 |= ((eg.x >> (2 * c)) & 0x01010101u) << 4; lg1 |= ((eg.y >> (2 * c)) & 0x01010101u) << 4;
-      lh0 |= ((eh.x >> (2 * c)) & 0x01010101u) << 4; lh1 |= ((eh.y >> (2 * c)) & 0x01010101u) << 4;
-      ug0 = ((wgc.x >> 4) & 0x0f0f0f0fu) | (((eg.x >> (2 * c + 1)) & 0x01010101u) << 4);
-      ug1 = ((wgc.y >> 4) & 0x0f0f0f0fu) | (((eg.y >> (2 * c + 1)) & 0x01010101u) << 4);
-      uh0 = ((whc.x >> 4) & 0x0f0f0f0fu) | (((eh.x >> (2 * c + 1)) & 0x01010101u) << 4);
-      uh1 = ((whc.y >> 4) & 0x0f0f0f0fu) | (((eh.y >> (2 * c + 1)) & 0x01010101u) << 4);
-    } else {
-      ug0 = wgc.x & 0xf0f0f0f0u; ug1 = wgc.y & 0xf0f0f0f0u; uh0 = whc.x & 0xf0f0f0f0u; uh1 = whc.y & 0xf0f0f0f0u;
-    }
-    // token g's activation of sub-blocks 2c (lo) and 2c+1 (hi)
-    const uint32_t xla = live ? __ldg(xw + 16 * c + t) : 0u, xlb = live ? __ldg(xw + 16 * c + 4 + t) : 0u;
-    const uint32_t xua = live ? __ldg(xw + 16 * c + 8 + t) : 0u, xub = live ? __ldg(xw + 16 * c + 12 + t) : 0u;
-    int L[4] = {0, 0, 0, 0}, U[4] = {0, 0, 0, 0};
-    mma_k32(L, lg0, lh0, lg1, lh1, xla, xlb);
-    mma_k32(U, ug0, uh0, ug1, uh1, xua, xub);
-    const float2 d0 = __ldg(reinterpret_cast<const float2 *>(xd0 + 2 * c)), d1 = __ldg(reinterpret_cast<const float2 *>(xd1 + 2 * c));
-    const int2 s0 = __ldg(reinterpret_cast<const int2 *>(xs0 + 2 * c)), s1 = __ldg(reinterpret_cast<const int2 *>(xs1 + 2 * c));
-    const uint32_t F[2] = {k45_field(hdr[0], c), k45_field(hdr[1], c)};
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const int ri = e >> 1, ti = e & 1;
-      const int hi = FIVE ? U[e] : U[e] >> 4;
-      const double xdl = (double)(ti ? d1.x : d0.x), xdu = (double)(ti ? d1.y : d0.y);
-      const int xsl = ti ? s1.x : s0.x, xsu = ti ? s1.y : s0.y;
-      const double P = __dadd_rn(k45_term(dd[ri], dm[ri], F[ri] & 63, (F[ri] >> 12) & 63, L[e], xsl, xdl),
-                                 k45_term(dd[ri], dm[ri], (F[ri] >> 6) & 63, (F[ri] >> 18) & 63, hi, xsu, xdu));
-      // pairwise tree over the four pairs: ((P0 + P1) + (P2 + P3))
-      if (c == 0 || c == 2) q01[e] = P;
-      else if (c == 1) S[e] = __dadd_rn(q01[e], P);
-      else S[e] = __dadd_rn(S[e], __dadd_rn(q01[e], P));
-    }
-  }
-}
-
-// Q6_K, 2..8 tokens: Sh[e][h] = tree8 of half h, ((P0 + P1) + (P2 + P3)) with P_k the pair of
-// groups 8h + 2k, 8h + 2k + 1 (the pair lane k holds in the one-token path).
-__device__ __forceinline__ void sb_q6_tok(uint32_t blk, int pitch, int n, int j, int g, int t, const GAct &x, int sb,
-                                          double (&Sh)[4][2]) {
-  const uint32_t rg = blk + (uint32_t)(g * pitch), rh = blk + (uint32_t)((g + 8) * pitch);
-  const double d[2] = {h2d(lds16(rg + 208 * n + 2 * j)), h2d(lds16(rh + 208 * n + 2 * j))};
-  const bool live = g < x.ntok;
-  const uint32_t *xw = reinterpret_cast<const uint32_t *>(x.xq + (live ? g : 0) * x.k + (int64_t)sb * 256);
-  const int t0 = 2 * t < x.ntok ? 2 * t : 0, t1 = 2 * t + 1 < x.ntok ? 2 * t + 1 : 0;
-  const float *xd0 = x.xd + t0 * (x.k / 32) + sb * 8, *xd1 = x.xd + t1 * (x.k / 32) + sb * 8;
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    // this lane's quants of half h: ql words [u][p], qh words [u] (values 4t..4t+3 of each group)
-    const uint32_t qlo = 128 * j + 32 * t + 16 * h, qho = 128 * n + 64 * j + 16 * t + 8 * h;
-    const uint4 lg = lds128(rg + qlo), lh = lds128(rh + qlo);
-    const uint2 qg = lds64(rg + qho), qh = lds64(rh + qho);
-    const uint32_t gw[4] = {lg.x, lg.y, lg.z, lg.w}, hw[4] = {lh.x, lh.y, lh.z, lh.w};
-    const uint32_t gq[2] = {qg.x, qg.y}, hq[2] = {qh.x, qh.y};
-    double q[4][2];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      // scales of groups 8h + 2k + u (reordered table: byte 4k + 2h + u) and their 32-block's xd
-      const uint32_t sw[2] = {lds16(rg + 192 * n + 16 * j + 4 * k + 2 * h), lds16(rh + 192 * n + 16 * j + 4 * k + 2 * h)};
-      const double xdv[2] = {(double)__ldg(xd0 + 4 * h + k), (double)__ldg(xd1 + 4 * h + k)};
-      double P[4];
-#pragma unroll
-      for (int u = 0; u < 2; u++) {
-        // signed quants q - 32 (bytes in [0, 63]: + 96 never carries, then flip the top bit)
-        const uint32_t a0 = (q6_unpack(gw[u * 2], gw[u * 2 + 1], gq[u], k) + 0x60606060u) ^ 0x80808080u;
-        const uint32_t a1 = (q6_unpack(hw[u * 2], hw[u * 2 + 1], hq[u], k) + 0x60606060u) ^ 0x80808080u;
-        const uint32_t xa = live ? __ldg(xw + 4 * (8 * h + 2 * k + u) + t) : 0u;
-        int Cm[4] = {0, 0, 0, 0};
-        mma_k16s(Cm, a0, a1, xa);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const int ri = e >> 1, ti = e & 1;
-          const int scale = (int)(int8_t)((sw[ri] >> (8 * u)) & 0xffu);
-          const double T = q6_term(__dmul_rn(xdv[ti], d[ri]), scale, Cm[e]);
-          P[e] = u == 0 ? T : __dadd_rn(P[e], T);
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        if (k == 0 || k == 2) q[e][k >> 1] = P[e];
-        else q[e][k >> 1] = __dadd_rn(q[e][k >> 1], P[e]);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 4; e++) Sh[e][h] = __dadd_rn(q[e][0], q[e][1]);
-  }
-}
-
-// ---------------------------------------------------------------------------- kernel
 struct KqArgs {
-  const uint8_t *w;
-  int64_t row_stride;
-  int64_t rows;
+  const uint8_t *w;     // first unit of the launch's first tile
+  int64_t rows;         // rows of the launch (the last tile may be partial)
   int nb;               // super-blocks per row
-  int nchunk;           // chunks per row
-  int pitch;            // shared-memory bytes per staged row
-  int nst;              // stages in the ring
+  int nchunk;           // token kernel: chunks of super-blocks per tile
+  int nst;              // token kernel: stages in the ring
   int ntok;             // tokens in this launch (1..8)
   const int8_t *xq;     // quantized activation [ntok][k] (one token: may be NULL with x set)
   const float *xd;
@@ -380,6 +162,28 @@ struct KqArgs {
   unsigned *status;
   int x_off, part_off, bar_off;   // shared-memory regions
 };
+
+// tiles [T0, T1) of a CTA: an even split of the launch's tiles
+__device__ __forceinline__ void cta_tiles(int64_t rows, int &T0, int &T1) {
+  const int64_t nt = (rows + kTile - 1) / kTile;
+  T0 = (int)((int64_t)blockIdx.x * nt / gridDim.x);
+  T1 = (int)((int64_t)(blockIdx.x + 1) * nt / gridDim.x);
+}
+
+// y for output row r (launch-relative) from its f64 total; with swiglu the (gate, up) pair
+// r, r + 1 is written once, by r (src/compute/worker.js:426, ref-kernels.js:322: silu in double,
+// the product rounded to f32)
+__device__ __forceinline__ void store_row(const KqArgs &p, int tok, int64_t r, float out, float up) {
+  if (p.swiglu) {
+    const double z = out;
+    const double sl = __ddiv_rn(z, __dadd_rn(1.0, exp(-z)));
+    p.y[(int64_t)tok * p.y_stride + r / 2] = __double2float_rn(__dmul_rn(sl, (double)up));
+  } else {
+    const int64_t o = (int64_t)tok * p.y_stride + r;
+    if (p.y_add) out = __fadd_rn(p.y_add[o], out);
+    p.y[o] = out;
+  }
+}
 
 // RMSNorm scale 1 / sqrt(mean(x^2) + eps) of one token, with exactly the reduction of
 // rmsnorm_quant_kernel (ops.cu): 256 partial sums, sum i = t (mod 256) for thread t, then a
@@ -469,145 +273,210 @@ __device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w,
   }
 }
 
-// warps per CTA: 16 for one token (latency hiding), 8 for 2..8 tokens (registers)
-// A CTA runs NG independent groups of 8 warps.  One token: 2 groups, each taking alternate 16-row
-// tiles with its own stage ring, barrier and adder, so one group's waits and barriers overlap the
-// other's arithmetic.  2..8 tokens: 1 group (their registers allow no more).
-constexpr int kGroupWarps = 8;
-template <bool TOK> constexpr int groups_of() { return TOK ? 1 : 2; }
+// ---------------------------------------------------------------------------- 2..8 tokens
+// One unit in shared memory at `u` (kq_layout.h): lane (g, t) computes rows g and g + 8 for tokens
+// 2t and 2t + 1.  S[e] (e = 2 * row half + token parity) = the super-block sum in the canonical
+// tree order.
+template <bool FIVE>
+__device__ __forceinline__ void sb_k45_tok(uint32_t u, int lane, int g, int t, const GAct &x, int sb, double (&S)[4]) {
+  constexpr int HO = FIVE ? 2560 : 2048;
+  const uint4 hdr[2] = {lds128(u + HO + 16 * g), lds128(u + HO + 16 * (g + 8))};
+  const bool live = g < x.ntok;
+  const uint32_t *xw = reinterpret_cast<const uint32_t *>(x.xq + (live ? g : 0) * x.k + (int64_t)sb * 256);
+  const int t0 = 2 * t < x.ntok ? 2 * t : 0, t1 = 2 * t + 1 < x.ntok ? 2 * t + 1 : 0;   // padding tokens read token 0
+  const float *xd0 = x.xd + t0 * (x.k / 32) + sb * 8, *xd1 = x.xd + t1 * (x.k / 32) + sb * 8;
+  const int32_t *xs0 = x.xs + t0 * (x.k / 32) + sb * 8, *xs1 = x.xs + t1 * (x.k / 32) + sb * 8;
+  double dd[2], dm[2];
+#pragma unroll
+  for (int ri = 0; ri < 2; ri++) { dd[ri] = h2d(hdr[ri].x & 0xffffu); dm[ri] = h2d(hdr[ri].x >> 16); }
+  uint2 eg = make_uint2(0, 0), eh = make_uint2(0, 0);
+  if (FIVE) { eg = lds64(u + kE5 + 8 * lane); eh = lds64(u + kE5 + 256 + 8 * lane); }
+  double q01[4];
+#pragma unroll
+  for (int cp = 0; cp < 2; cp++) {
+    const uint4 wq = lds128(u + (cp * 32 + lane) * 16), vq = lds128(u + ((2 + cp) * 32 + lane) * 16);
+#pragma unroll
+    for (int ci = 0; ci < 2; ci++) {
+      const int c = 2 * cp + ci;
+      const uint32_t wx = ci ? wq.z : wq.x, wy = ci ? wq.w : wq.y, vx = ci ? vq.z : vq.x, vy = ci ? vq.w : vq.y;
+      uint32_t lg0 = wx & 0x0f0f0f0fu, lg1 = wy & 0x0f0f0f0fu, lh0 = vx & 0x0f0f0f0fu, lh1 = vy & 0x0f0f0f0fu;
+      uint32_t ug0, ug1, uh0, uh1;
+      if (FIVE) {
+        lg0 |= ((eg.x >> (2 * c)) & 0x01010101u) << 4; lg1 |= ((eg.y >> (2 * c)) & 0x01010101u) << 4;
+        lh0 |= ((eh.x >> (2 * c)) & 0x01010101u) << 4; lh1 |= ((eh.y >> (2 * c)) & 0x01010101u) << 4;
+        ug0 = ((wx >> 4) & 0x0f0f0f0fu) | (((eg.x >> (2 * c + 1)) & 0x01010101u) << 4);
+        ug1 = ((wy >> 4) & 0x0f0f0f0fu) | (((eg.y >> (2 * c + 1)) & 0x01010101u) << 4);
+        uh0 = ((vx >> 4) & 0x0f0f0f0fu) | (((eh.x >> (2 * c + 1)) & 0x01010101u) << 4);
+        uh1 = ((vy >> 4) & 0x0f0f0f0fu) | (((eh.y >> (2 * c + 1)) & 0x01010101u) << 4);
+      } else {
+        ug0 = wx & 0xf0f0f0f0u; ug1 = wy & 0xf0f0f0f0u; uh0 = vx & 0xf0f0f0f0u; uh1 = vy & 0xf0f0f0f0u;
+      }
+      // token g's activation of sub-blocks 2c (lo) and 2c+1 (hi)
+      const uint32_t xla = live ? __ldg(xw + 16 * c + t) : 0u, xlb = live ? __ldg(xw + 16 * c + 4 + t) : 0u;
+      const uint32_t xua = live ? __ldg(xw + 16 * c + 8 + t) : 0u, xub = live ? __ldg(xw + 16 * c + 12 + t) : 0u;
+      int L[4] = {0, 0, 0, 0}, U[4] = {0, 0, 0, 0};
+      mma_k32(L, lg0, lh0, lg1, lh1, xla, xlb);
+      mma_k32(U, ug0, uh0, ug1, uh1, xua, xub);
+      const float2 d0 = __ldg(reinterpret_cast<const float2 *>(xd0 + 2 * c)), d1 = __ldg(reinterpret_cast<const float2 *>(xd1 + 2 * c));
+      const int2 s0 = __ldg(reinterpret_cast<const int2 *>(xs0 + 2 * c)), s1 = __ldg(reinterpret_cast<const int2 *>(xs1 + 2 * c));
+      const uint32_t F[2] = {k45_field(hdr[0], c), k45_field(hdr[1], c)};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int ri = e >> 1, ti = e & 1;
+        const int hi = FIVE ? U[e] : U[e] >> 4;
+        const double xdl = (double)(ti ? d1.x : d0.x), xdu = (double)(ti ? d1.y : d0.y);
+        const int xsl = ti ? s1.x : s0.x, xsu = ti ? s1.y : s0.y;
+        const double P = __dadd_rn(k45_term(dd[ri], dm[ri], F[ri] & 63, (F[ri] >> 12) & 63, L[e], xsl, xdl),
+                                   k45_term(dd[ri], dm[ri], (F[ri] >> 6) & 63, (F[ri] >> 18) & 63, hi, xsu, xdu));
+        // pairwise tree over the four pairs: ((P0 + P1) + (P2 + P3))
+        if (c == 0 || c == 2) q01[e] = P;
+        else if (c == 1) S[e] = __dadd_rn(q01[e], P);
+        else S[e] = __dadd_rn(S[e], __dadd_rn(q01[e], P));
+      }
+    }
+  }
+}
 
-template <int FMT, bool TOK>
-__global__ void __launch_bounds__(groups_of<TOK>() * kGroupWarps * 32, 2) kq_gemv_kernel(const KqArgs p) {
-  constexpr int BS = FMT == T_Q4_K ? 144 : FMT == T_Q5_K ? 176 : 210;
-  constexpr int NTP = TOK ? kMaxTok : 1;
-  constexpr int NG = groups_of<TOK>(), NT = NG * kGroupWarps * 32, GT = kGroupWarps * 32;
+// Q6_K, 2..8 tokens: Sh[e][h] = tree8 of half h, ((P0 + P1) + (P2 + P3)) with P_k the pair of
+// groups 8h + 2k, 8h + 2k + 1 (the pair lane k holds in the one-token path).
+__device__ __forceinline__ void sb_q6_tok(uint32_t u, int lane, int g, int t, const GAct &x, int sb,
+                                          double (&Sh)[4][2]) {
+  const double d[2] = {h2d(lds16(u + kQ6D + 2 * g)), h2d(lds16(u + kQ6D + 2 * (g + 8)))};
+  const uint4 scw[2] = {lds128(u + kQ6S + 16 * g), lds128(u + kQ6S + 16 * (g + 8))};   // the rows' 16 scales
+  const uint4 qhw[2] = {lds128(u + kQ6H + 16 * lane), lds128(u + kQ6H + 512 + 16 * lane)};
+  const bool live = g < x.ntok;
+  const uint32_t *xw = reinterpret_cast<const uint32_t *>(x.xq + (live ? g : 0) * x.k + (int64_t)sb * 256);
+  const int t0 = 2 * t < x.ntok ? 2 * t : 0, t1 = 2 * t + 1 < x.ntok ? 2 * t + 1 : 0;
+  const float *xd0 = x.xd + t0 * (x.k / 32) + sb * 8, *xd1 = x.xd + t1 * (x.k / 32) + sb * 8;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    // this lane's quants of half h: ql words [u][p], qh words [u] (values 4t..4t+3 of each group)
+    const uint4 lg = lds128(u + (h * 32 + lane) * 16), lh = lds128(u + ((2 + h) * 32 + lane) * 16);
+    const uint32_t gw[4] = {lg.x, lg.y, lg.z, lg.w}, hw[4] = {lh.x, lh.y, lh.z, lh.w};
+    const uint32_t gq[2] = {h ? qhw[0].z : qhw[0].x, h ? qhw[0].w : qhw[0].y};
+    const uint32_t hq[2] = {h ? qhw[1].z : qhw[1].x, h ? qhw[1].w : qhw[1].y};
+    double q[4][2];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      // scales of groups 8h + 2k + uu (reordered table: byte 4k + 2h + uu) and their 32-block's xd
+      const uint32_t swd[2] = {k == 0 ? scw[0].x : k == 1 ? scw[0].y : k == 2 ? scw[0].z : scw[0].w,
+                               k == 0 ? scw[1].x : k == 1 ? scw[1].y : k == 2 ? scw[1].z : scw[1].w};
+      const uint32_t sw[2] = {(swd[0] >> (16 * h)) & 0xffffu, (swd[1] >> (16 * h)) & 0xffffu};
+      const double xdv[2] = {(double)__ldg(xd0 + 4 * h + k), (double)__ldg(xd1 + 4 * h + k)};
+      double P[4];
+#pragma unroll
+      for (int uu = 0; uu < 2; uu++) {
+        // signed quants q - 32 (bytes in [0, 63]: + 96 never carries, then flip the top bit)
+        const uint32_t a0 = (q6_unpack(gw[uu * 2], gw[uu * 2 + 1], gq[uu], k) + 0x60606060u) ^ 0x80808080u;
+        const uint32_t a1 = (q6_unpack(hw[uu * 2], hw[uu * 2 + 1], hq[uu], k) + 0x60606060u) ^ 0x80808080u;
+        const uint32_t xa = live ? __ldg(xw + 4 * (8 * h + 2 * k + uu) + t) : 0u;
+        int Cm[4] = {0, 0, 0, 0};
+        mma_k16s(Cm, a0, a1, xa);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int ri = e >> 1, ti = e & 1;
+          const int scale = (int)(int8_t)((sw[ri] >> (8 * uu)) & 0xffu);
+          const double T = q6_term(__dmul_rn(xdv[ti], d[ri]), scale, Cm[e]);
+          P[e] = uu == 0 ? T : __dadd_rn(P[e], T);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        if (k == 0 || k == 2) q[e][k >> 1] = P[e];
+        else q[e][k >> 1] = __dadd_rn(q[e][k >> 1], P[e]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; e++) Sh[e][h] = __dadd_rn(q[e][0], q[e][1]);
+  }
+}
+
+// super-blocks per staged chunk (Q6_K: more bytes and twice the MMAs per super-block)
+template <int FMT> constexpr int chunk_sb() { return FMT == T_Q6_K ? 8 : 16; }
+constexpr int chunk_sb_of(int type) { return type == T_Q6_K ? 8 : 16; }
+constexpr int kTokWarps = 8;
+constexpr int kMaxStages = 8;
+constexpr int64_t kTokBudget = 200 * 1024;   // one CTA per SM (the grid is at most one per SM)
+
+// 2..8 tokens.  A CTA owns tiles [T0, T1) and walks them in chunks of up to kChunk super-blocks:
+// stage s of the ring holds one chunk (one bulk copy of its contiguous units, issued by lane 0 of
+// warp 0, completion on full[s]).  Warp w takes super-blocks w and w + 8 of every chunk; each
+// lane writes its super-block sums to a per-chunk slot array, one CTA barrier (which also carries
+// the bounded waits' give-up flag to every warp) publishes them, and one thread per (row, token)
+// adds them in super-block order while warp 0 refills the freed stage.
+template <int FMT>
+__global__ void __launch_bounds__(kTokWarps * 32, 1) kq_tok_kernel(const KqArgs p) {
+  constexpr int US = unit_bytes<FMT>();
+  constexpr int NTP = kMaxTok, NT = kTokWarps * 32;
   constexpr int kChunk = chunk_sb<FMT>();
   constexpr int kSlots = 16;                    // per-chunk slots of super-block sums (Q6_K: 8 x 2 halves)
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int grp = warp / kGroupWarps, gw = warp % kGroupWarps;     // group, warp within the group
-  const int nst = p.nst;                        // stages per group
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.bar_off) + grp * nst;
-  uint8_t *stages = smem + (size_t)grp * nst * kTile * p.pitch;
-  double *part = reinterpret_cast<double *>(smem + p.part_off) + (size_t)grp * 2 * kSlots * kTile * NTP;  // [2][slot][row][NTP]
+  const int nst = p.nst;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.bar_off);
+  uint8_t *stages = smem;
+  double *part = reinterpret_cast<double *>(smem + p.part_off);    // [2][slot][row][NTP]
+  int T0, T1;
+  cta_tiles(p.rows, T0, T1);
+  const int nunit = (T1 - T0) * p.nchunk;       // this CTA's (tile, chunk) units of work
+  const int stage_bytes = kChunk * US;
 
-  // row range of this CTA (whole (gate, up) pairs with swiglu)
-  const int64_t pr = p.swiglu ? p.rows / 2 : p.rows, rm = p.swiglu ? 2 : 1;
-  const int64_t r0 = rm * ((int64_t)blockIdx.x * pr / gridDim.x), r1 = rm * ((int64_t)(blockIdx.x + 1) * pr / gridDim.x);
-  const int ntile = (int)((r1 - r0 + kTile - 1) / kTile);
-  const int gtiles = (ntile - grp + NG - 1) / NG;   // tiles grp, grp + NG, ...
-  const int nunit = gtiles * p.nchunk;              // this group's units: (its k-th tile, chunk)
-  const int stage_bytes = kTile * p.pitch;
-
-  // Warp 0 of the group fills stage u % nst with the group's unit u, one bulk copy per row issued
-  // by its own lane.
-  auto issue = [&](int u) {
-    const int s = u % nst, tile = (u / p.nchunk) * NG + grp, c = u % p.nchunk;
-    const int64_t row0 = r0 + (int64_t)tile * kTile;
-    const int nr = (int)min((int64_t)kTile, r1 - row0);
+  auto issue = [&](int u) {                     // lane 0 of warp 0
+    const int s = u % nst, tile = u / p.nchunk, c = u % p.nchunk;
     const int sb0 = c * kChunk, nsb = min(kChunk, p.nb - sb0);
-    const uint32_t bytes = (uint32_t)((nsb * BS + 15) & ~15);
-    if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)nr * bytes);
-    __syncwarp();
-    if (lane < nr)
-      bulk_g2s(stages + (size_t)s * stage_bytes + lane * p.pitch, p.w + (row0 + lane) * p.row_stride + (int64_t)sb0 * BS,
-               bytes, &full[s]);
+    const uint32_t bytes = (uint32_t)(nsb * US);
+    mbar_arrive_expect_tx(&full[s], bytes);
+    bulk_g2s(stages + (size_t)s * stage_bytes, p.w + ((int64_t)(T0 + tile) * p.nb + sb0) * US, bytes, &full[s]);
   };
 
-  int issued = 0;                               // units issued so far (tracked by warp 0 of the group)
-  if (gw == 0) {
-    if (lane == 0) {
-      for (int s = 0; s < nst; s++) mbar_init(&full[s], 1);
-      fence_mbar_init();
-    }
-    __syncwarp();
+  int issued = 0;                               // units issued so far (tracked by lane 0 of warp 0)
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < nst; s++) mbar_init(&full[s], 1);
+    fence_mbar_init();
     for (; issued < nunit && issued < nst; issued++) issue(issued);
   }
   pdl_launch_dependents();
   __syncthreads();                              // barriers initialised before anyone waits on them
   pdl_wait();                                   // the activation comes from the previous kernel
 
-  SAct sa{};
   GAct ga{};
-  if constexpr (!TOK) {
-    uint8_t *sxq = smem + p.x_off;
-    double *sxd = reinterpret_cast<double *>(sxq + p.k);
-    int32_t *sxs = reinterpret_cast<int32_t *>(sxd + p.k / 32);
-    int32_t *sxs16 = FMT == T_Q6_K ? sxs + p.k / 32 : nullptr;
-    if (p.xq == nullptr) {
-      quantize_to_smem<NT>(p.x, p.k, p.norm_w, p.norm_eps, sxq, sxd, sxs, sxs16, warp, lane);
-    } else {
-      const uint4 *q4 = reinterpret_cast<const uint4 *>(p.xq);
-      for (int i = threadIdx.x; i < p.k / 16; i += NT) {
-        const uint4 v = __ldg(q4 + i);
-        reinterpret_cast<uint4 *>(sxq)[i] = v;
-        if (sxs16) sxs16[i] = __dp4a((int)v.x, 0x01010101, __dp4a((int)v.y, 0x01010101,
-                                     __dp4a((int)v.z, 0x01010101, __dp4a((int)v.w, 0x01010101, 0))));
-      }
-      for (int i = threadIdx.x; i < p.k / 32; i += NT) { sxd[i] = (double)__ldg(p.xd + i); sxs[i] = __ldg(p.xs + i); }
-    }
-    __syncthreads();
-    sa.xq = smem_u32(sxq); sa.xd = smem_u32(sxd); sa.xs = smem_u32(sxs); sa.xs16 = sxs16 ? smem_u32(sxs16) : 0u;
-#pragma unroll
-    for (int i = 0; i < 8; i++) sa.sel[i] = g == i ? 1u : 0u;
-  } else {
-    ga.xq = p.xq; ga.xd = p.xd; ga.xs = p.xs; ga.k = p.k; ga.ntok = p.ntok;
-  }
-
+  ga.xq = p.xq; ga.xd = p.xd; ga.xs = p.xs; ga.k = p.k; ga.ntok = p.ntok;
   const uint32_t sbase = smem_u32(stages);
-  // One thread per output (row, token) of the group's current tile adds the chunk's super-block
-  // sums in super-block order: lanes of the group's warp 0 (and 1..3 for 8 tokens).
-  const int gtid = threadIdx.x - grp * GT;
-  const bool adder = gtid < kTile * NTP;
+  const bool adder = threadIdx.x < kTile * NTP;
   double tot = 0.0;
   bool aborted = false;
   for (int u = 0; u < nunit; u++) {
-    const int s = u % nst, tile = (u / p.nchunk) * NG + grp, c = u % p.nchunk;
+    const int s = u % nst, tile = u / p.nchunk, c = u % p.nchunk;
     // after one give-up the warp waits no more: it only passes the barriers until all stop together
     const bool ok = !aborted && mbar_wait_warp(&full[s], (uint32_t)(u / nst) & 1u, lane);
     const int sb0 = c * kChunk, nsb = min(kChunk, p.nb - sb0);
     double *pu = part + (size_t)(u & 1) * kSlots * kTile * NTP;
     if (ok) {
       const uint32_t st = sbase + (uint32_t)(s * stage_bytes);
-      if constexpr (!TOK) {
-        // warp w of the group: super-blocks w and w + 8 (Q6_K: super-block w, both halves)
-#pragma unroll 1
-        for (int i = 0; i < 2; i++) {
-          const int j = FMT == T_Q6_K ? gw : gw + 8 * i, h = FMT == T_Q6_K ? i : 0;
-          const int slot = FMT == T_Q6_K ? gw + 8 * i : j;
-          if (j < nsb) {
-            double S0, S1;
-            if constexpr (FMT == T_Q6_K) sb_q6_one(st, p.pitch, nsb, j, h, g, t, sa, sb0 + j, S0, S1);
-            else sb_k45_one<FMT == T_Q5_K>(st + (uint32_t)(j * BS), p.pitch, g, t, sa, sb0 + j, S0, S1);
-            if (t == 0) { pu[slot * kTile + g] = S0; pu[slot * kTile + g + 8] = S1; }
-          }
-        }
-      } else {
 #pragma unroll
-        for (int jj = 0; jj < kChunk / kGroupWarps; jj++) {
-          const int j = gw + kGroupWarps * jj;
-          if (j >= nsb) break;
-          if constexpr (FMT == T_Q6_K) {
-            double Sh[4][2];
-            sb_q6_tok(st, p.pitch, nsb, j, g, t, ga, sb0 + j, Sh);
+      for (int jj = 0; jj < kChunk / kTokWarps; jj++) {
+        const int j = warp + kTokWarps * jj;
+        if (j >= nsb) break;
+        const uint32_t un = st + (uint32_t)(j * US);
+        if constexpr (FMT == T_Q6_K) {
+          double Sh[4][2];
+          sb_q6_tok(un, lane, g, t, ga, sb0 + j, Sh);
 #pragma unroll
-            for (int e = 0; e < 4; e++)
+          for (int e = 0; e < 4; e++)
 #pragma unroll
-              for (int h = 0; h < 2; h++)
-                pu[((j + 8 * h) * kTile + g + 8 * (e >> 1)) * NTP + 2 * t + (e & 1)] = Sh[e][h];
-          } else {
-            double S[4];
-            sb_k45_tok<FMT == T_Q5_K>(st + (uint32_t)(j * BS), p.pitch, g, t, ga, sb0 + j, S);
+            for (int h = 0; h < 2; h++)
+              pu[((j + 8 * h) * kTile + g + 8 * (e >> 1)) * NTP + 2 * t + (e & 1)] = Sh[e][h];
+        } else {
+          double S[4];
+          sb_k45_tok<FMT == T_Q5_K>(un, lane, g, t, ga, sb0 + j, S);
 #pragma unroll
-            for (int e = 0; e < 4; e++) pu[(j * kTile + g + 8 * (e >> 1)) * NTP + 2 * t + (e & 1)] = S[e];
-          }
+          for (int e = 0; e < 4; e++) pu[(j * kTile + g + 8 * (e >> 1)) * NTP + 2 * t + (e & 1)] = S[e];
         }
       }
     }
-    // every warp of the group is done with stage s and has published its sums: one group barrier,
-    // which also tells every warp of the group whether any of them gave up waiting
-    if (named_sync_or(1 + grp, GT, aborted || !ok)) { aborted = true; break; }
-    if (u + nst < nunit && gw == 0) {
+    // every warp is done with stage s and has published its sums
+    if (named_sync_or(1, NT, aborted || !ok)) { aborted = true; break; }
+    if (u + nst < nunit && warp == 0 && lane == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(u + nst);
       issued = u + nst + 1;
@@ -619,35 +488,25 @@ __global__ void __launch_bounds__(groups_of<TOK>() * kGroupWarps * 32, 2) kq_gem
 #pragma unroll
       for (int j = 0; j < NJ; j++)
         if (j < nsb)
-          v[j] = FMT == T_Q6_K ? __dadd_rn(pu[j * kTile * NTP + gtid], pu[(j + 8) * kTile * NTP + gtid]) : pu[j * kTile * NTP + gtid];
+          v[j] = FMT == T_Q6_K ? __dadd_rn(pu[j * kTile * NTP + threadIdx.x], pu[(j + 8) * kTile * NTP + threadIdx.x])
+                               : pu[j * kTile * NTP + threadIdx.x];
 #pragma unroll
       for (int j = 0; j < NJ; j++)
         if (j < nsb) tot = __dadd_rn(tot, v[j]);
       if (c == p.nchunk - 1) {
-        const int row = gtid / NTP, tok = gtid % NTP;
-        const int64_t r = r0 + (int64_t)tile * kTile + row;
-        float out = __double2float_rn(tot);
-        if (p.swiglu) {
-          // rows r (gate) and r + 1 (up) are the adders gtid and gtid + NTP, in the same warp:
-          // silu in double, the product rounded to f32 (src/compute/worker.js:426, ref-kernels.js:322)
-          const float up = __shfl_xor_sync(TOK ? 0xffffffffu : 0x0000ffffu, out, NTP);
-          if ((row & 1) == 0 && tok < p.ntok && r < r1) {
-            const double z = out;
-            const double sl = __ddiv_rn(z, __dadd_rn(1.0, exp(-z)));
-            p.y[(int64_t)tok * p.y_stride + r / 2] = __double2float_rn(__dmul_rn(sl, (double)up));
-          }
-        } else if (tok < p.ntok && r < r1) {
-          const int64_t o = (int64_t)tok * p.y_stride + r;
-          if (p.y_add) out = __fadd_rn(p.y_add[o], out);
-          p.y[o] = out;
-        }
+        const int row = threadIdx.x / NTP, tk = threadIdx.x % NTP;
+        const int64_t r = (int64_t)(T0 + tile) * kTile + row;
+        const float out = __double2float_rn(tot);
+        // rows r (gate) and r + 1 (up) are the adders threadIdx.x and threadIdx.x + NTP, in one warp
+        const float up = __shfl_xor_sync(0xffffffffu, out, NTP);
+        if (tk < p.ntok && r < p.rows && (!p.swiglu || (row & 1) == 0)) store_row(p, tk, r, out, up);
         tot = 0.0;
       }
     }
   }
   if (aborted) {
     if (lane == 0) atomicOr(p.status, ST_FULL_TIMEOUT);
-    if (gw == 0 && lane == 0) {
+    if (warp == 0 && lane == 0) {
       // copies still in flight must land before the CTA's shared memory is released
       const uint64_t drain_deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
       for (int v = issued - nst > 0 ? issued - nst : 0; v < issued; v++)
@@ -657,59 +516,235 @@ __global__ void __launch_bounds__(groups_of<TOK>() * kGroupWarps * 32, 2) kq_gem
   }
 }
 
-struct KqPlan {
-  int nchunk, pitch, nst, grid, smem, x_off, part_off, bar_off;
-};
+// ---------------------------------------------------------------------------- one token, register streaming
+// A unit as lane (g, t) needs it: its pieces of rows g and g + 8, loaded straight from HBM; every
+// load but the headers and d reads 512 (Q5_K high bits: 256; Q6_K scales: 128) contiguous bytes
+// across the warp.
+template <int FMT> struct PairRegs;
+template <> struct PairRegs<T_Q4_K> { uint4 q[2][2]; uint4 h[2]; };             // quants [row][half], header [row]
+template <> struct PairRegs<T_Q5_K> { uint4 q[2][2]; uint4 h[2]; uint2 e[2]; }; // + high bits [row]
+template <> struct PairRegs<T_Q6_K> { uint4 l[2][2]; uint4 qh[2]; uint32_t sc[2]; uint32_t d[2]; };
 
-bool plan_kq(const DevMatrix &m, int num_sms, bool tok, KqPlan *p, const char **why) {
-  const int bs = m.type == T_Q4_K ? 144 : m.type == T_Q5_K ? 176 : 210;
-  const int64_t nb = m.cols / 256;
-  if (nb < 1 || m.cols % 256) { *why = "k-quant rows must be a whole number of 256-value super-blocks"; return false; }
-  if (nb > (1 << 24)) { *why = "k-quant rows too long"; return false; }
-  const int kChunk = chunk_sb_of(m.type);
-  p->nchunk = (int)((nb + kChunk - 1) / kChunk);
-  const int chunk = (int)(((nb < kChunk ? nb : kChunk) * bs + 15) / 16 * 16);
-  int pitch = chunk;
-  while ((pitch / 4) % 8 != 4) pitch += 16;    // rows g = 0..7 of a tile land on distinct bank groups
-  p->pitch = pitch;
-  const int64_t grid = m.rows < num_sms ? m.rows : num_sms;
-  p->grid = (int)(grid < 1 ? 1 : grid);
-  const int64_t rows_cta = (m.rows + p->grid - 1) / p->grid;
-  const int ng = tok ? 1 : 2;
-  const int64_t units = ((rows_cta + kTile - 1) / kTile + ng - 1) / ng * p->nchunk;   // per group
-  const int64_t x_bytes = tok ? 0 : (m.cols + 12 * (m.cols / 32) + (m.type == T_Q6_K ? 4 * (m.cols / 16) : 0) + 127) / 128 * 128;
-  const int64_t stage = (int64_t)kTile * pitch;
-  const int64_t part_bytes = (int64_t)ng * 2 * 16 * kTile * (tok ? kMaxTok : 1) * 8;
-  const int64_t avail = kSmemBudget - x_bytes - part_bytes - 8 * ng * kMaxStages;
-  int64_t nst = avail / (stage * ng);
-  if (nst > kMaxStages) nst = kMaxStages;
-  if (nst > units) nst = units;
-  if (nst < 1) { *why = "k-quant rows too long for the shared-memory stages"; return false; }
-  p->nst = (int)nst;
-  p->x_off = (int)(ng * nst * stage);
-  p->part_off = (int)(p->x_off + x_bytes);
-  p->bar_off = (int)(p->part_off + part_bytes);
-  p->smem = p->bar_off + 8 * ng * p->nst;
-  return true;
+template <int FMT>
+__device__ __forceinline__ void load_unit(PairRegs<FMT> &R, const uint8_t *u, int lane, int g) {
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    if constexpr (FMT == T_Q6_K) {
+      R.l[r][0] = ldg128(u + ((2 * r) * 32 + lane) * 16);
+      R.l[r][1] = ldg128(u + ((2 * r + 1) * 32 + lane) * 16);
+      R.qh[r] = ldg128(u + kQ6H + (r * 32 + lane) * 16);
+      R.sc[r] = __ldg(reinterpret_cast<const uint32_t *>(u + kQ6S + (r * 32 + lane) * 4));
+      R.d[r] = __ldg(reinterpret_cast<const unsigned short *>(u + kQ6D + 2 * (8 * r + g)));
+    } else {
+      R.q[r][0] = ldg128(u + ((2 * r) * 32 + lane) * 16);
+      R.q[r][1] = ldg128(u + ((2 * r + 1) * 32 + lane) * 16);
+      R.h[r] = ldg128(u + hdr_off<FMT>() + 16 * (8 * r + g));
+      if constexpr (FMT == T_Q5_K) R.e[r] = __ldg(reinterpret_cast<const uint2 *>(u + kE5 + (r * 32 + lane) * 8));
+    }
+  }
 }
 
-template <int FMT, bool TOK>
-cudaError_t launch_kq_t(const KqArgs &a, const KqPlan &pl, cudaStream_t s, bool pdl) {
-  auto kern = kq_gemv_kernel<FMT, TOK>;
+// The super-block sums of rows g (p0) and g + 8 (p1) of one unit from registers, in the canonical
+// order: the quad tree over lanes t of (T(2t) + T(2t+1)) (Q6_K: half 0's tree plus half 1's tree,
+// each over the pairs of groups 8h + 2t, 8h + 2t + 1).
+template <int FMT>
+__device__ __forceinline__ void pair_sums(const PairRegs<FMT> &R, int g, int t, const SAct &x, int sb, double &p0,
+                                          double &p1) {
+  if constexpr (FMT == T_Q6_K) {
+    double ph[2][2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint32_t lgw[4] = {R.l[0][h].x, R.l[0][h].y, R.l[0][h].z, R.l[0][h].w};
+      const uint32_t lhw[4] = {R.l[1][h].x, R.l[1][h].y, R.l[1][h].z, R.l[1][h].w};
+      const uint32_t qgw[2] = {h ? R.qh[0].z : R.qh[0].x, h ? R.qh[0].w : R.qh[0].y};
+      const uint32_t qhw[2] = {h ? R.qh[1].z : R.qh[1].x, h ? R.qh[1].w : R.qh[1].y};
+      const uint32_t xa = lds32(x.xq + sb * 256 + 16 * (8 * h + g) + 4 * t);
+      int C[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const uint32_t a0 = q6_unpack(lgw[u * 2], lgw[u * 2 + 1], qgw[u], k);
+          const uint32_t a1 = q6_unpack(lhw[u * 2], lhw[u * 2 + 1], qhw[u], k);
+          mma_k16(C, a0, a1, xa * x.sel[2 * k + u]);
+        }
+      }
+      const uint2 s2 = lds64(x.xs16 + 4 * (sb * 16 + 8 * h + 2 * t));
+      const uint2 xdw = lds64(x.xd + 8 * (sb * 8 + 4 * h + t));
+      const double xdv = __hiloint2double((int)xdw.y, (int)xdw.x);
+#pragma unroll
+      for (int r = 0; r < 2; r++) {
+        const uint32_t scw = (R.sc[r] >> (16 * h)) & 0xffffu;
+        const double xdd = __dmul_rn(xdv, h2d(R.d[r]));
+        const double pr = __dadd_rn(q6_term(xdd, (int)(int8_t)(scw & 0xff), C[2 * r] - 32 * (int)s2.x),
+                                    q6_term(xdd, (int)(int8_t)(scw >> 8), C[2 * r + 1] - 32 * (int)s2.y));
+        ph[h][r] = quad_tree(pr);
+      }
+    }
+    p0 = __dadd_rn(ph[0][0], ph[1][0]);
+    p1 = __dadd_rn(ph[0][1], ph[1][1]);
+  } else {
+    constexpr bool FIVE = FMT == T_Q5_K;
+    uint2 eg = make_uint2(0, 0), eh = make_uint2(0, 0);
+    if constexpr (FIVE) { eg = R.e[0]; eh = R.e[1]; }
+    const uint32_t xa = lds32(x.xq + sb * 256 + 32 * g + 4 * t), xb = lds32(x.xq + sb * 256 + 32 * g + 16 + 4 * t);
+    int C0[4] = {0, 0, 0, 0}, C1[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int cp = 0; cp < 2; cp++) {
+      const uint4 wq = R.q[0][cp], vq = R.q[1][cp];
+      const uint32_t wg[4] = {wq.x, wq.y, wq.z, wq.w}, wh[4] = {vq.x, vq.y, vq.z, vq.w};
+#pragma unroll
+      for (int ci = 0; ci < 2; ci++) {
+        const int c = 2 * cp + ci;
+        uint32_t lg0 = wg[2 * ci] & 0x0f0f0f0fu, lg1 = wg[2 * ci + 1] & 0x0f0f0f0fu;
+        uint32_t lh0 = wh[2 * ci] & 0x0f0f0f0fu, lh1 = wh[2 * ci + 1] & 0x0f0f0f0fu;
+        uint32_t ug0, ug1, uh0, uh1;
+        if constexpr (FIVE) {
+          lg0 |= ((eg.x >> (2 * c)) & 0x01010101u) << 4; lg1 |= ((eg.y >> (2 * c)) & 0x01010101u) << 4;
+          lh0 |= ((eh.x >> (2 * c)) & 0x01010101u) << 4; lh1 |= ((eh.y >> (2 * c)) & 0x01010101u) << 4;
+          ug0 = ((wg[2 * ci] >> 4) & 0x0f0f0f0fu) | (((eg.x >> (2 * c + 1)) & 0x01010101u) << 4);
+          ug1 = ((wg[2 * ci + 1] >> 4) & 0x0f0f0f0fu) | (((eg.y >> (2 * c + 1)) & 0x01010101u) << 4);
+          uh0 = ((wh[2 * ci] >> 4) & 0x0f0f0f0fu) | (((eh.x >> (2 * c + 1)) & 0x01010101u) << 4);
+          uh1 = ((wh[2 * ci + 1] >> 4) & 0x0f0f0f0fu) | (((eh.y >> (2 * c + 1)) & 0x01010101u) << 4);
+        } else {
+          ug0 = wg[2 * ci] - lg0; ug1 = wg[2 * ci + 1] - lg1;
+          uh0 = wh[2 * ci] - lh0; uh1 = wh[2 * ci + 1] - lh1;
+        }
+        int(&C)[4] = (c & 1) ? C1 : C0;
+        mma_k32(C, lg0, lh0, lg1, lh1, xa * x.sel[2 * c], xb * x.sel[2 * c]);
+        mma_k32(C, ug0, uh0, ug1, uh1, xa * x.sel[2 * c + 1], xb * x.sel[2 * c + 1]);
+      }
+    }
+    int v0 = C0[0] + C1[0], v1 = C0[1] + C1[1], v2 = C0[2] + C1[2], v3 = C0[3] + C1[3];
+    if (!FIVE) { v1 >>= 4; v3 >>= 4; }
+    const uint4 xdw = lds128(x.xd + 8 * (sb * 8 + 2 * t));
+    const double xd0 = __hiloint2double((int)xdw.y, (int)xdw.x), xd1 = __hiloint2double((int)xdw.w, (int)xdw.z);
+    const uint2 xs = lds64(x.xs + 4 * (sb * 8 + 2 * t));
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const uint4 hd = R.h[r];
+      const uint32_t F = k45_field(hd, t);
+      const double d = h2d(hd.x & 0xffffu), dmin = h2d(hd.x >> 16);
+      const double pr = __dadd_rn(k45_term(d, dmin, F & 63, (F >> 12) & 63, r ? v2 : v0, (int)xs.x, xd0),
+                                  k45_term(d, dmin, (F >> 6) & 63, (F >> 18) & 63, r ? v3 : v1, (int)xs.y, xd1));
+      if (r) p1 = quad_tree(pr); else p0 = quad_tree(pr);
+    }
+  }
+}
+
+// Stage one token's activation in shared memory (quantized here from f32, or copied when the
+// caller quantized it) and return its view.
+template <int FMT, int NT>
+__device__ __forceinline__ SAct stage_token(const KqArgs &p, uint8_t *base, int warp, int lane, int g) {
+  uint8_t *sxq = base;
+  double *sxd = reinterpret_cast<double *>(sxq + p.k);
+  int32_t *sxs = reinterpret_cast<int32_t *>(sxd + p.k / 32);
+  int32_t *sxs16 = FMT == T_Q6_K ? sxs + p.k / 32 : nullptr;
+  if (p.xq == nullptr) {
+    quantize_to_smem<NT>(p.x, p.k, p.norm_w, p.norm_eps, sxq, sxd, sxs, sxs16, warp, lane);
+  } else {
+    const uint4 *q4 = reinterpret_cast<const uint4 *>(p.xq);
+    for (int i = threadIdx.x; i < p.k / 16; i += NT) {
+      const uint4 v = __ldg(q4 + i);
+      reinterpret_cast<uint4 *>(sxq)[i] = v;
+      if (sxs16) sxs16[i] = __dp4a((int)v.x, 0x01010101, __dp4a((int)v.y, 0x01010101,
+                                   __dp4a((int)v.z, 0x01010101, __dp4a((int)v.w, 0x01010101, 0))));
+    }
+    for (int i = threadIdx.x; i < p.k / 32; i += NT) { sxd[i] = (double)__ldg(p.xd + i); sxs[i] = __ldg(p.xs + i); }
+  }
+  SAct sa{};
+  sa.xq = smem_u32(sxq); sa.xd = smem_u32(sxd); sa.xs = smem_u32(sxs); sa.xs16 = sxs16 ? smem_u32(sxs16) : 0u;
+#pragma unroll
+  for (int i = 0; i < 8; i++) sa.sel[i] = g == i ? 1u : 0u;
+  return sa;
+}
+
+// One token.  A CTA owns tiles [T0, T1); their units, (tile, super-block) in order, are one
+// contiguous range, cut into 16 equal runs, one per warp.  A warp keeps D units of loads in flight
+// in registers -- the first ones issued before griddepcontrol.wait -- and writes each unit's two
+// super-block sums to shared memory.  After one CTA barrier a thread per row adds its super-block
+// sums in super-block order and applies the epilogue.  No waits on other warps or copies: nothing
+// to bound.
+constexpr int kStreamWarps = 16;
+constexpr int kStreamDepth = 2;
+
+template <int FMT>
+__global__ void __launch_bounds__(kStreamWarps * 32, 1) kq_stream_kernel(const KqArgs p) {
+  constexpr int NT = kStreamWarps * 32, D = kStreamDepth, US = unit_bytes<FMT>();
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  int T0, T1;
+  cta_tiles(p.rows, T0, T1);
+  const int nb = p.nb;
+  const int npair = (T1 - T0) * nb;
+  const int i0 = (int)((int64_t)warp * npair / kStreamWarps), i1 = (int)((int64_t)(warp + 1) * npair / kStreamWarps);
+  const int64_t row0 = (int64_t)T0 * kTile;
+  const int nrows = (int)(min((int64_t)T1 * kTile, p.rows) - row0);
+  double *sums = reinterpret_cast<double *>(smem + p.part_off);    // [pair][16 rows]
+  const uint8_t *base = p.w + (int64_t)T0 * nb * US;
+
+  PairRegs<FMT> R[D];
+#pragma unroll
+  for (int d = 0; d < D; d++)
+    if (i0 + d < i1) load_unit<FMT>(R[d], base + (int64_t)(i0 + d) * US, lane, g);   // not the previous kernel's output
+  pdl_launch_dependents();
+  pdl_wait();                                   // the activation is
+  const SAct sa = stage_token<FMT, NT>(p, smem + p.x_off, warp, lane, g);
+  __syncthreads();
+
+  int sb = nb > 0 ? i0 % nb : 0;                // super-block of unit i
+  for (int i = i0; i < i1; i += D) {
+#pragma unroll
+    for (int d = 0; d < D; d++) {
+      const int ii = i + d;
+      if (ii < i1) {
+        double S0, S1;
+        pair_sums<FMT>(R[d], g, t, sa, sb, S0, S1);
+        if (ii + D < i1) load_unit<FMT>(R[d], base + (int64_t)(ii + D) * US, lane, g);
+        if (t == 0) { sums[ii * kTile + g] = S0; sums[ii * kTile + g + 8] = S1; }
+        if (++sb == nb) sb = 0;
+      }
+    }
+  }
+  __syncthreads();
+
+  // one thread per row (per (gate, up) pair with swiglu): the super-block sums in order
+  const int step = p.swiglu ? 2 : 1;
+  for (int row = step * threadIdx.x; row < nrows; row += step * NT) {
+    float o[2] = {0.f, 0.f};
+    for (int e = 0; e < step; e++) {
+      const int rr = row + e;
+      const double *sr = sums + (int64_t)(rr / kTile) * nb * kTile + rr % kTile;
+      double tot = 0.0;
+      for (int s = 0; s < nb; s++) tot = __dadd_rn(tot, sr[s * kTile]);
+      o[e] = __double2float_rn(tot);
+    }
+    store_row(p, 0, row0 + row, o[0], o[1]);
+  }
+}
+
+// ---------------------------------------------------------------------------- host side
+int kq_x_bytes(const DevMatrix &m) {
+  return (int)((m.cols + 12 * (m.cols / 32) + (m.type == T_Q6_K ? 4 * (m.cols / 16) : 0) + 127) / 128 * 128);
+}
+
+// one shared-memory grant per kernel (the template parameter) and device
+template <void (*kern)(KqArgs)>
+cudaError_t launch_ex(int64_t max_smem, const KqArgs &a, int grid, int block, int smem, cudaStream_t s, bool pdl) {
   static bool granted[64] = {false};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!granted[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget + 1024);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_smem);
     if (e != cudaSuccess) return e;
     granted[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.grid);
-  cfg.blockDim = dim3(groups_of<TOK>() * kGroupWarps * 32);
-  cfg.dynamicSmemBytes = pl.smem;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -717,6 +752,90 @@ cudaError_t launch_kq_t(const KqArgs &a, const KqPlan &pl, cudaStream_t s, bool 
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// The one-token launches over a matrix: each takes whole tiles, at most as many per CTA as leave
+// the CTA's super-block sums room in shared memory next to the staged activation.
+constexpr int64_t kStreamBudget = 200 * 1024;
+
+cudaError_t launch_stream(const DevMatrix &m, const ActView &act, float *y, const float *y_add, const GemvFuse &fz,
+                          unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why) {
+  const int64_t nb = m.cols / 256;
+  const int64_t x_bytes = kq_x_bytes(m);
+  const int64_t cap = (kStreamBudget - x_bytes) / (nb * kTile * 8);       // tiles per CTA
+  if (cap < 1) { *why = "k-quant rows too long for the one-token GEMV"; return cudaErrorInvalidValue; }
+  const int64_t tiles_all = (m.rows + kTile - 1) / kTile, per_launch = cap * num_sms;
+  const int us = kq_unit_bytes(m.type);
+  for (int64_t tb = 0; tb < tiles_all; tb += per_launch) {
+    const int64_t nt = tiles_all - tb < per_launch ? tiles_all - tb : per_launch;
+    const int64_t rb = tb * kTile;
+    const int grid = (int)(nt < num_sms ? nt : num_sms);
+    const int64_t tiles_cta = (nt + grid - 1) / grid;
+    KqArgs a{};
+    a.w = m.data + tb * nb * us;
+    a.rows = m.rows - rb < nt * kTile ? m.rows - rb : nt * kTile;
+    a.nb = (int)nb; a.ntok = 1; a.k = m.cols;
+    a.xq = act.xq; a.xd = act.xd; a.xs = act.xs; a.x = act.x;
+    a.y = y + (fz.swiglu ? rb / 2 : rb);
+    a.y_add = y_add ? y_add + rb : nullptr;
+    a.norm_w = fz.norm_w; a.norm_eps = fz.eps; a.swiglu = fz.swiglu ? 1 : 0;
+    a.status = status;
+    a.x_off = 0; a.part_off = (int)x_bytes;
+    const int smem = (int)(x_bytes + tiles_cta * nb * kTile * 8);
+    const int block = kStreamWarps * 32;
+    cudaError_t e;
+    switch (m.type) {
+      case T_Q4_K: e = launch_ex<kq_stream_kernel<T_Q4_K>>(kStreamBudget, a, grid, block, smem, s, pdl); break;
+      case T_Q5_K: e = launch_ex<kq_stream_kernel<T_Q5_K>>(kStreamBudget, a, grid, block, smem, s, pdl); break;
+      default: e = launch_ex<kq_stream_kernel<T_Q6_K>>(kStreamBudget, a, grid, block, smem, s, pdl); break;
+    }
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// 2..8 tokens per launch, tokens in groups of 8.
+cudaError_t launch_tok(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride, const float *y_add,
+                       const GemvFuse &fz, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why) {
+  if (!act.xq) { *why = "the in-kernel activation quantization takes one token"; return cudaErrorInvalidValue; }
+  const int64_t nb = m.cols / 256;
+  const int kChunk = chunk_sb_of(m.type), us = kq_unit_bytes(m.type);
+  const int nchunk = (int)((nb + kChunk - 1) / kChunk);
+  const int64_t tiles_all = (m.rows + kTile - 1) / kTile;
+  const int grid = (int)(tiles_all < num_sms ? tiles_all : num_sms);
+  const int64_t units = (tiles_all + grid - 1) / grid * nchunk;           // per CTA, at most
+  const int64_t stage = (int64_t)kChunk * us;
+  const int64_t part_bytes = 2LL * 16 * kTile * kMaxTok * 8;
+  int64_t nst = (kTokBudget - part_bytes - 8 * kMaxStages) / stage;
+  if (nst > kMaxStages) nst = kMaxStages;
+  if (nst > units) nst = units;
+  if (nst < 1) { *why = "k-quant rows too long for the shared-memory stages"; return cudaErrorInvalidValue; }
+  const int part_off = (int)(nst * stage), bar_off = (int)(part_off + part_bytes);
+  const int smem = bar_off + 8 * (int)nst;
+  for (int t0 = 0; t0 < ntok; t0 += kMaxTok) {
+    const int nt = ntok - t0 < kMaxTok ? ntok - t0 : kMaxTok;
+    KqArgs a{};
+    a.w = m.data; a.rows = m.rows; a.nb = (int)nb; a.nchunk = nchunk; a.nst = (int)nst;
+    a.ntok = nt; a.k = m.cols;
+    a.xq = act.xq + (int64_t)t0 * m.cols;
+    a.xd = act.xd + (int64_t)t0 * (m.cols / 32);
+    a.xs = act.xs + (int64_t)t0 * (m.cols / 32);
+    a.y = y + (int64_t)t0 * y_stride;
+    a.y_add = y_add ? y_add + (int64_t)t0 * y_stride : nullptr;
+    a.y_stride = y_stride;
+    a.swiglu = fz.swiglu ? 1 : 0;
+    a.status = status;
+    a.part_off = part_off; a.bar_off = bar_off;
+    const int block = kTokWarps * 32;
+    cudaError_t e;
+    switch (m.type) {
+      case T_Q4_K: e = launch_ex<kq_tok_kernel<T_Q4_K>>(kTokBudget + 1024, a, grid, block, smem, s, pdl); break;
+      case T_Q5_K: e = launch_ex<kq_tok_kernel<T_Q5_K>>(kTokBudget + 1024, a, grid, block, smem, s, pdl); break;
+      default: e = launch_ex<kq_tok_kernel<T_Q6_K>>(kTokBudget + 1024, a, grid, block, smem, s, pdl); break;
+    }
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -731,43 +850,15 @@ cudaError_t launch_gemv_kq(const DevMatrix &m, const ActView &act, int ntok, flo
 cudaError_t launch_gemv_kq_ex(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
                               const float *y_add, const GemvFuse &fz, unsigned *status, int num_sms, cudaStream_t s,
                               bool pdl, const char **why) {
+  if (m.cols % 256 || m.cols < 256) { *why = "k-quant rows must be a whole number of 256-value super-blocks"; return cudaErrorInvalidValue; }
   if (fz.norm_w && (act.xq || !act.x || ntok != 1)) { *why = "the fused RMSNorm takes one f32 token"; return cudaErrorInvalidValue; }
   if (fz.swiglu && (m.rows % 2 || y_add)) { *why = "the SwiGLU epilogue takes (gate, up) row pairs and no residual"; return cudaErrorInvalidValue; }
-  KqPlan pl1, plt;
-  if (!plan_kq(m, num_sms, false, &pl1, why)) return cudaErrorInvalidValue;
-  if (ntok > 1 && !plan_kq(m, num_sms, true, &plt, why)) return cudaErrorInvalidValue;
   if (act.xq == nullptr && (ntok != 1 || act.x == nullptr)) {
     *why = "the in-kernel activation quantization takes one token";
     return cudaErrorInvalidValue;
   }
-  for (int t0 = 0; t0 < ntok; t0 += kMaxTok) {
-    const int nt = ntok - t0 < kMaxTok ? ntok - t0 : kMaxTok;
-    const KqPlan &pl = nt == 1 ? pl1 : plt;
-    KqArgs a{};
-    a.w = m.data; a.row_stride = m.row_stride; a.rows = m.rows; a.nb = (int)(m.cols / 256);
-    a.nchunk = pl.nchunk; a.pitch = pl.pitch; a.nst = pl.nst;
-    a.ntok = nt;
-    a.k = m.cols;
-    a.xq = act.xq ? act.xq + (int64_t)t0 * m.cols : nullptr;
-    a.xd = act.xd ? act.xd + (int64_t)t0 * (m.cols / 32) : nullptr;
-    a.xs = act.xs ? act.xs + (int64_t)t0 * (m.cols / 32) : nullptr;
-    a.x = act.x ? act.x + (int64_t)t0 * m.cols : nullptr;
-    a.y = y + (int64_t)t0 * y_stride;
-    a.y_add = y_add ? y_add + (int64_t)t0 * y_stride : nullptr;
-    a.y_stride = y_stride;
-    a.norm_w = fz.norm_w; a.norm_eps = fz.eps; a.swiglu = fz.swiglu ? 1 : 0;
-    a.status = status;
-    a.x_off = pl.x_off; a.part_off = pl.part_off; a.bar_off = pl.bar_off;
-    cudaError_t e;
-    const bool tok = nt > 1;
-    switch (m.type) {
-      case T_Q4_K: e = tok ? launch_kq_t<T_Q4_K, true>(a, pl, s, pdl) : launch_kq_t<T_Q4_K, false>(a, pl, s, pdl); break;
-      case T_Q5_K: e = tok ? launch_kq_t<T_Q5_K, true>(a, pl, s, pdl) : launch_kq_t<T_Q5_K, false>(a, pl, s, pdl); break;
-      default: e = tok ? launch_kq_t<T_Q6_K, true>(a, pl, s, pdl) : launch_kq_t<T_Q6_K, false>(a, pl, s, pdl); break;
-    }
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  if (ntok == 1) return launch_stream(m, act, y, y_add, fz, status, num_sms, s, pdl, why);
+  return launch_tok(m, act, ntok, y, y_stride, y_add, fz, status, num_sms, s, pdl, why);
 }
 
 }  // namespace zllm

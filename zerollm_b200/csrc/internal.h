@@ -15,8 +15,11 @@ bool type_supported(int type);
 bool type_quantized(int type);
 // bytes of one raw GGUF row; -1 when cols is not a whole number of blocks
 int64_t raw_row_bytes(int type, int64_t cols);
-// bytes of one device row (repacked layout, padded to 16)
+// bytes of one device row (repacked layout, padded to 16); for the k-quants, whose rows are
+// interleaved in units of 16 (kq_layout.h), the raw row length rounded up to 16
 int64_t dev_row_stride(int type, int64_t cols);
+// device bytes of a whole matrix
+int64_t dev_matrix_bytes(int type, int64_t rows, int64_t cols);
 
 // A device-resident matrix in the kernels' layout (see repack in gemv.cu).
 struct DevMatrix {
@@ -110,6 +113,9 @@ cudaError_t launch_advance(const int32_t *arg, int n, int32_t *tok, int32_t *pos
                            int32_t *step, cudaStream_t s, bool pdl);
 
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s);
+// k-quant rows src[i] -> dst row dst_row0 + i * dst_step (same type and width)
+cudaError_t launch_kq_copy_rows(const DevMatrix &dst, int64_t dst_row0, int64_t dst_step, const DevMatrix &src,
+                                cudaStream_t s);
 cudaError_t launch_quantize(const float *x, int64_t k, int ntok, int8_t *xq, float *xd, int32_t *xs, unsigned *status,
                             cudaStream_t s, bool pdl);
 // y[t*y_stride + r] = (y_add ? y_add[t*y_stride + r] : 0) + W[r] . act_t   for t < ntok

@@ -202,11 +202,11 @@ extern "C" int zllm_model_set_vector(zllm_model *m, int kind, int layer, const f
 }
 
 // The rows of several matrices of one type and row length as one weight (the projections that read
-// the same activation: q, k, v; gate, up), so one GEMV launch streams them all.  The device rows
-// are independent (each row's layout depends on the row alone), so a byte copy of each matrix in
-// turn is the concatenation, and every output row keeps its bits.  NULL when types or widths differ.
-// With `interleave` (equal row counts) row i of matrix j lands at row i * count + j instead: the
-// gate / up pairs of the SwiGLU epilogue.
+// the same activation: q, k, v; gate, up), so one GEMV launch streams them all.  Every row's
+// bytes are copied unchanged (for the k-quants to their place in the 16-row units), so every
+// output row keeps its bits.  NULL when types or widths differ.  With `interleave` (equal row
+// counts) row i of matrix j lands at row i * count + j instead: the gate / up pairs of the SwiGLU
+// epilogue.
 static zllm_weight *concat_rows(zllm_model *m, std::initializer_list<zllm_weight *> ws, bool interleave = false) {
   const zllm_weight *w0 = *ws.begin();
   int64_t rows = 0;
@@ -220,15 +220,22 @@ static zllm_weight *concat_rows(zllm_model *m, std::initializer_list<zllm_weight
   f->ctx = m->ctx;
   f->m = w0->m;
   f->m.rows = rows;
-  f->bytes = (size_t)(f->m.row_stride * rows);
+  f->bytes = (size_t)dev_matrix_bytes(f->m.type, rows, f->m.cols);
   if (cudaMalloc((void **)&f->m.data, f->bytes) != cudaSuccess) { delete f; cudaGetLastError(); return nullptr; }
   size_t off = 0;
   cudaError_t e = cudaSuccess;
   const size_t rs = (size_t)w0->m.row_stride, count = ws.size();
   int j = 0;
+  const bool kq = kq_type(w0->m.type);
+  if (kq && rows % 16) e = cudaMemsetAsync(f->m.data, 0, f->bytes, m->stream);   // padding rows
+  int64_t row0 = 0;
   for (const zllm_weight *w : ws) {
     if (e != cudaSuccess) break;
-    if (interleave)
+    if (kq) {
+      e = interleave ? launch_kq_copy_rows(f->m, j, (int64_t)count, w->m, m->stream)
+                     : launch_kq_copy_rows(f->m, row0, 1, w->m, m->stream);
+      row0 += w->m.rows;
+    } else if (interleave)
       e = cudaMemcpy2DAsync(f->m.data + j * rs, count * rs, w->m.data, rs, rs, (size_t)w->m.rows, cudaMemcpyDeviceToDevice,
                             m->stream);
     else

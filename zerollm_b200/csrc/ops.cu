@@ -120,27 +120,27 @@ __device__ float dequant_at(const DevMatrix &m, int64_t r, int64_t i) {
       const int bs = five ? 176 : 144;
       const int64_t nb = m.cols / 256, sb = i / 256;
       const int e = (int)(i % 256), s = e / 32, l = e % 32, c = s >> 1;
-      const uint8_t *blk = row + sb * bs;
       // raw GGUF byte positions, mapped to the device layout (kq_layout.h)
-      const uint8_t byte = row[kq_dev_offset(m.type, sb * bs + (five ? 48 : 16) + c * 32 + l, nb)];
+      auto at = [&](int64_t raw) { return m.data[kq_dev_pos(m.type, r, sb * bs + raw, nb)]; };
+      const uint8_t byte = at((five ? 48 : 16) + c * 32 + l);
       int v = (s & 1) ? byte >> 4 : byte & 15;
-      if (five) v |= ((row[kq_dev_offset(m.type, sb * bs + 16 + l, nb)] >> s) & 1) << 4;
+      if (five) v |= ((at(16 + l) >> s) & 1) << 4;
       // the repacked scale field of chunk c: sc(2c) | sc(2c+1) << 6 | mn(2c) << 12 | mn(2c+1) << 18
-      const uint32_t F = (uint32_t)blk[4 + 3 * c] | ((uint32_t)blk[5 + 3 * c] << 8) | ((uint32_t)blk[6 + 3 * c] << 16);
+      const uint32_t F = (uint32_t)at(4 + 3 * c) | ((uint32_t)at(5 + 3 * c) << 8) | ((uint32_t)at(6 + 3 * c) << 16);
       const int sc = (s & 1) ? (F >> 6) & 63 : F & 63, mn = (s & 1) ? (F >> 18) & 63 : (F >> 12) & 63;
-      const double d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
+      const double d = h2f(at(0) | (at(1) << 8)), dmin = h2f(at(2) | (at(3) << 8));
       // quant.js:150: d * sc * v - dmin * mn
       return __double2float_rn(__dsub_rn(__dmul_rn(__dmul_rn(d, (double)sc), (double)v), __dmul_rn(dmin, (double)mn)));
     }
     case T_Q6_K: {
       const int64_t nb = m.cols / 256, sb = i / 256, rb = sb * 210;
       const int e = (int)(i % 256), half = e / 128, k = (e % 128) / 32, l = e % 32;
-      const uint8_t ql = row[kq_dev_offset(T_Q6_K, rb + half * 64 + (k & 1) * 32 + l, nb)];
-      const uint8_t qh = row[kq_dev_offset(T_Q6_K, rb + 128 + half * 32 + l, nb)];
+      auto at = [&](int64_t raw) { return m.data[kq_dev_pos(T_Q6_K, r, rb + raw, nb)]; };
+      const uint8_t ql = at(half * 64 + (k & 1) * 32 + l);
+      const uint8_t qh = at(128 + half * 32 + l);
       const int q = (int)(((k < 2 ? ql & 15 : ql >> 4)) | (((qh >> (2 * k)) & 3) << 4)) - 32;
-      const int scale = (int8_t)row[kq_dev_offset(T_Q6_K, rb + 192 + half * 8 + (l >> 4) + 2 * k, nb)];
-      const int64_t dof = kq_dev_offset(T_Q6_K, rb + 208, nb);
-      const double d = h2f(row[dof] | (row[dof + 1] << 8));
+      const int scale = (int8_t)at(192 + half * 8 + (l >> 4) + 2 * k);
+      const double d = h2f(at(208) | (at(209) << 8));
       // quant.js:194-197: d * scale * q
       return __double2float_rn(__dmul_rn(__dmul_rn(d, (double)scale), (double)q));
     }
