@@ -550,7 +550,7 @@ def run_ours(args, world, rank, local):
                     "steps": e_steps, "api": "zllm_matvec (host buffers, pinned)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "kq_gemv_kernel<Q4_K, one token> (in-kernel activation quantization)",
+                         "kernel": "kq_stream_kernel<Q4_K> (one token, in-kernel activation quantization)",
                          "kernel_us": round(ms / args.steps * 1e3, 3),
                          "prequantized_kernel_us": round(kern_ms * 1e3, 3),
                          "algorithmic_bytes_per_launch": ALGO_BYTES},
