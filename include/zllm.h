@@ -89,9 +89,21 @@ int zllm_quantize_act(zllm_ctx *ctx, const float *x, int64_t k, int ntok, int8_t
  * itself, bit-exactly as zllm_quantize_act.
  * Replaces the per-type kernels matvec_* / mm_* (src/compute/wasm/kernels.js:30-240,
  * src/compute/wasm/kquant-kernels.js:337-504) and the dispatch in src/compute/worker.js:251-270.
- * y_add == y gives the in-place residual add of worker.js:346 / :432. */
+ * y_add == y gives the in-place residual add of worker.js:346 / :432.
+ * 16 or more tokens on a k-quant W run the tensor-core GEMM (weights and the quantized activation
+ * each rounded once to f16, f32 accumulation: within 1e-3 of the reference, not bit-identical to
+ * the per-token path); 1..15 tokens keep the exact per-token arithmetic, so batches below 16
+ * reproduce single tokens bit for bit (test/kquant-kernels.test.js:65-97).  The GEMM's activation
+ * tiles live in a context scratch buffer that grows on demand (a cudaMalloc on first use). */
 int zllm_mm(zllm_ctx *ctx, const zllm_weight *w, const int8_t *xq, const float *xd, const int32_t *xs, const float *x,
             int ntok, float *y, int64_t y_stride, const float *y_add, void *stream);
+
+/* D[j*m + i] = sum_k A[i*k + kk] * B[j*k + kk] for i < m, j < n: f16 A [m][k] and B [n][k] (row-major,
+ * 16-byte aligned, k a multiple of 64), f32 D [n][m], on the same tcgen05 kernel as the k-quant GEMM
+ * (the reference has no f16 GEMM entry; this one exposes the dense core of its batched mm_* path,
+ * src/compute/worker.js:251-270, for tests and f16 callers).  Scratch for the tiled operands is a
+ * context buffer that grows on demand. */
+int zllm_gemm_f16(zllm_ctx *ctx, const void *A, const void *B, int64_t m, int64_t n, int64_t k, float *D, void *stream);
 
 /* Host-buffer convenience: y_host[t][rows] = W . x_host[t][cols] (quantizing x on the device first),
  * blocking.  The CUDA counterpart of `matvec(w, new Act(x), y)` (src/compute/ref-kernels.js:127). */

@@ -113,14 +113,15 @@ KQ = [(ggml.Q4_K, 4096, 4096), (ggml.Q5_K, 520, 2048), (ggml.Q6_K, 700, 12288), 
 def test_kquant_batches_bit_identical_to_single_tokens(ctx, t, rows, cols):
     """The tensor-core GEMV adds each token's block terms in an order fixed by the matrix shape: a
     token's outputs are the same bits alone (block-diagonal MMA) or in a batch of 2..8 (token MMA),
-    and batches above 8 run in groups."""
+    and batches of 9..15 run in groups of 8.  From 16 tokens the f16 tensor-core GEMM takes over
+    (within 1e-3, tests/test_gpu_gemm.py)."""
     rng = np.random.default_rng(rows + cols + t)
     wt = synth.tensor(t, rows, cols, rng, "bench")
     w = Weight.from_tensor(ctx, wt)
     X = rng.standard_normal((17, cols)).astype(np.float32)
     X[3] *= 1e-3
     singles = np.stack([matvec(w, Act(ctx, X[i])).cpu().numpy().ravel() for i in range(17)])
-    for n in (2, 5, 8, 17):
+    for n in (2, 5, 8, 15):
         Y = matvec(w, Act(ctx, X[:n])).cpu().numpy()
         ctx.sync()
         assert np.array_equal(Y, singles[:n]), (n, np.argwhere(Y != singles[:n])[:5])

@@ -197,6 +197,22 @@ extern "C" int zllm_quantize_act(zllm_ctx *c, const float *x, int64_t k, int nto
   return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "quantize_act launch");
 }
 
+int zllm_weight_gemm_ok(zllm_ctx *c, zllm_weight *w) {
+  if (w->gemm_ok >= 0) return w->gemm_ok;
+  if (!gemm_kq_supported(w->m)) return w->gemm_ok = 0;
+  void *buf = nullptr;
+  if (zllm_scratch(c, 13, 4, &buf)) return 0;
+  unsigned bits = 0;
+  cudaError_t e = launch_kq_bound(w->m, reinterpret_cast<unsigned *>(buf), c->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&bits, buf, 4, cudaMemcpyDeviceToHost, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) { cudaGetLastError(); return 0; }
+  float bound;
+  memcpy(&bound, &bits, 4);
+  w->gemm_wscale = gemm_weight_scale(bound);
+  return w->gemm_ok = bound < 3.0e38f ? 1 : 0;          // NaN or infinite scales: the exact kernel
+}
+
 extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, const float *xd, const int32_t *xs,
                        const float *x, int ntok, float *y, int64_t y_stride, const float *y_add, void *stream) {
   if (!c || !w || !y || ntok < 1) { zllm_set_error(c, "zllm_mm: bad argument"); return ZLLM_E_ARG; }
@@ -213,9 +229,34 @@ extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, cons
   ActView a{fused ? nullptr : xq, xd, xs, x, w->m.cols};
   const char *why = "";
   cudaStream_t st = pick(c, stream);
+  if (ntok >= kGemmMinTokens && xq && (uintptr_t)xq % 8 == 0 && kq_type(w->m.type) &&
+      zllm_weight_gemm_ok(c, const_cast<zllm_weight *>(w))) {
+    // 16 or more tokens: the tensor-core GEMM on f16 tiles of the activation
+    void *bbuf = nullptr;
+    int rc = zllm_scratch(c, 14, gemm_b_bytes(w->m.cols, ntok), &bbuf);
+    if (rc) return rc;
+    cudaError_t e = launch_gemm_prep(a, ntok, bbuf, st);
+    if (e == cudaSuccess) e = launch_gemm_kq(w->m, bbuf, ntok, y, y_stride, y_add, w->gemm_wscale, c->status_dev, st);
+    return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "gemm launch");
+  }
   cudaError_t e = launch_gemv(w->m, a, ntok, y, y_stride, y_add, c->status_dev, c->num_sms, st, pdl_ok(st), &why);
   if (e == cudaErrorInvalidValue && why[0]) { zllm_set_error(c, "zllm_mm: %s", why); return ZLLM_E_UNSUPPORTED; }
   return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "gemv launch");
+}
+
+extern "C" int zllm_gemm_f16(zllm_ctx *c, const void *A, const void *B, int64_t m, int64_t n, int64_t k, float *D,
+                             void *stream) {
+  if (!c || !A || !B || !D || m < 1 || n < 1 || k < 64 || k % 64) {
+    zllm_set_error(c, "zllm_gemm_f16: bad argument (k must be a positive multiple of 64)");
+    return ZLLM_E_ARG;
+  }
+  if (((uintptr_t)A | (uintptr_t)B) % 16) { zllm_set_error(c, "zllm_gemm_f16: A and B must be 16-byte aligned"); return ZLLM_E_ARG; }
+  void *scr = nullptr;
+  int rc = zllm_scratch(c, 15, gemm_f16_scratch_bytes(m, n, k), &scr);
+  if (rc) return rc;
+  cudaError_t e = launch_gemm_f16(reinterpret_cast<const uint16_t *>(A), reinterpret_cast<const uint16_t *>(B), m, n, k, D, scr,
+                                  c->status_dev, pick(c, stream));
+  return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "gemm_f16 launch");
 }
 
 extern "C" int zllm_matvec(zllm_ctx *c, const zllm_weight *w, const float *x_host, int ntok, float *y_host) {

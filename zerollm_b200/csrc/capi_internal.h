@@ -27,7 +27,12 @@ struct zllm_weight {
   zllm::DevMatrix m{};
   size_t bytes = 0;
   bool owns = true;
+  int gemm_ok = -1;      // k-quant: the tensor-core GEMM may take it (1), not (0), not yet known (-1)
+  float gemm_wscale = 1.f;   // power of two applied to its dequantized values in f16
 };
+
+// Whether the tensor-core GEMM may take this k-quant weight (computed once, synchronously).
+int zllm_weight_gemm_ok(zllm_ctx *c, zllm_weight *w);
 
 void zllm_set_error(zllm_ctx *c, const char *fmt, ...);
 int zllm_cuda_fail(zllm_ctx *c, cudaError_t e, const char *what);

@@ -113,6 +113,25 @@ cudaError_t launch_advance(const int32_t *arg, int n, int32_t *tok, int32_t *pos
                            int32_t *step, cudaStream_t s, bool pdl);
 
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s);
+
+// Tensor-core GEMM for k-quant matrices and 16 or more tokens (gemm_kq.cu).  The activation is
+// first turned into f16 tiles (launch_gemm_prep, gemm_b_bytes of scratch), then launch_gemm_kq
+// computes y[t][r] (+ y_add) for all tokens.  launch_kq_bound writes an upper bound of the
+// matrix's |dequantized value| (as f32 bits); a finite bound qualifies the matrix, and
+// gemm_weight_scale(bound) is the power of two that brings its values just under 2^15 in f16.
+constexpr int kGemmMinTokens = 16;
+float gemm_weight_scale(float bound);
+int64_t gemm_tokens_pad(int ntok);
+size_t gemm_b_bytes(int64_t k, int ntok);
+bool gemm_kq_supported(const DevMatrix &m);
+cudaError_t launch_kq_bound(const DevMatrix &m, unsigned *out, cudaStream_t s);
+cudaError_t launch_gemm_prep(const ActView &act, int ntok, void *bbuf, cudaStream_t s);
+cudaError_t launch_gemm_kq(const DevMatrix &m, const void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
+                           float wscale, unsigned *status, cudaStream_t s, bool swiglu = false);
+// f16 x f16 -> f32 on the same kernel: D[j][i] = sum_k A[i][k] B[j][k] (row-major, k % 64 == 0)
+size_t gemm_f16_scratch_bytes(int64_t m, int64_t n, int64_t k);
+cudaError_t launch_gemm_f16(const uint16_t *A, const uint16_t *B, int64_t m, int64_t n, int64_t k, float *D, void *scratch,
+                            unsigned *status, cudaStream_t s);
 // k-quant rows src[i] -> dst row dst_row0 + i * dst_step (same type and width)
 cudaError_t launch_kq_copy_rows(const DevMatrix &dst, int64_t dst_row0, int64_t dst_step, const DevMatrix &src,
                                 cudaStream_t s);

@@ -61,6 +61,7 @@ struct zllm_model {
   float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *att = nullptr;
   float *g = nullptr, *u = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
   float *qkv = nullptr, *gu = nullptr;                   // outputs of the row-concatenated projections
+  void *gemm_b = nullptr;                                // f16 activation tiles of the tensor-core GEMM (max_batch >= 16)
   int8_t *xq = nullptr;
   float *xd = nullptr;
   int32_t *xs = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_npos = nullptr, *d_arg = nullptr;
@@ -294,6 +295,13 @@ extern "C" int zllm_model_ready(zllm_model *m) {
   CK(dalloc(&m->g, MB * F), "act");
   CK(dalloc(&m->u, MB * F), "act");
   CK(dalloc(&m->hb, MB * F), "act");
+  if (MB >= kGemmMinTokens) {
+    // passes of 16 or more tokens run the k-quant projections as tensor-core GEMMs
+    CK(cudaMalloc(&m->gemm_b, gemm_b_bytes(KX, MB)), "GEMM activation tiles");
+    for (auto &L : m->L)
+      for (zllm_weight *w : {L.w[0], L.w[1], L.w[2], L.w[3], L.w[4], L.w[5], L.w[6], L.qkv, L.gu})
+        if (w && kq_type(w->m.type)) zllm_weight_gemm_ok(m->ctx, w);
+  }
   CK(dalloc(&m->logits, (size_t)LB * c.vocab), "logits");
   CK(dalloc(&m->d_tok, MB), "ids");
   CK(dalloc(&m->d_pos, MB), "ids");
@@ -313,8 +321,22 @@ extern "C" int zllm_model_ready(zllm_model *m) {
 }
 
 // ------------------------------------------------------------------------------------ the pass
+// 16 or more tokens on a k-quant weight that qualifies: the tensor-core GEMM on f16 tiles of the
+// quantized activation (within the 1e-3 contract; not bit-identical to the per-token arithmetic).
+static bool use_gemm(const zllm_model *m, const zllm_weight *w, int n) {
+  return n >= kGemmMinTokens && m->gemm_b && w->gemm_ok == 1;
+}
+static cudaError_t gemm(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add, int64_t k,
+                        bool swiglu) {
+  const ActView a{m->xq, m->xd, m->xs, nullptr, k};
+  cudaError_t e = launch_gemm_prep(a, n, m->gemm_b, m->stream);
+  if (e != cudaSuccess) return e;
+  return launch_gemm_kq(w->m, m->gemm_b, n, y, ys, y_add, w->gemm_wscale, m->ctx->status_dev, m->stream, swiglu);
+}
+
 static cudaError_t gemv(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add, const float *xf,
                         int64_t k, bool pdl = false) {
+  if (use_gemm(m, w, n)) return gemm(m, w, n, y, ys, y_add, k, false);
   ActView a{m->xq, m->xd, m->xs, xf, k};
   const char *why = "";
   return launch_gemv(w->m, a, n, y, ys, y_add, m->ctx->status_dev, m->ctx->num_sms, m->stream, pdl, &why);
@@ -323,6 +345,7 @@ static cudaError_t gemv(zllm_model *m, const zllm_weight *w, int n, float *y, in
 // A k-quant GEMV with fused work: `act` may carry the f32 activation alone (one token).
 static cudaError_t gemv_ex(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add,
                            const ActView &act, const GemvFuse &fz, bool pdl = false) {
+  if (act.xq && !fz.norm_w && use_gemm(m, w, n)) return gemm(m, w, n, y, ys, y_add, act.k, fz.swiglu);
   const char *why = "";
   return launch_gemv_kq_ex(w->m, act, n, y, ys, y_add, fz, m->ctx->status_dev, m->ctx->num_sms, m->stream, pdl, &why);
 }
@@ -692,7 +715,7 @@ extern "C" void zllm_model_destroy(zllm_model *m) {
                   (void *)m->q, (void *)m->k, (void *)m->v, (void *)m->qr, (void *)m->att, (void *)m->g, (void *)m->u,
                   (void *)m->hb, (void *)m->qkv, (void *)m->gu, (void *)m->logits, (void *)m->part, (void *)m->xq, (void *)m->xd, (void *)m->xs,
                   (void *)m->d_tok, (void *)m->d_pos, (void *)m->d_seq, (void *)m->d_npos, (void *)m->d_arg,
-                  (void *)m->counters, (void *)m->d_gen, (void *)m->d_step})
+                  (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b})
     if (p) cudaFree(p);
   if (m->h_io) cudaFreeHost(m->h_io);
   if (m->stream) cudaStreamDestroy(m->stream);
