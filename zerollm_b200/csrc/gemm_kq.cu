@@ -39,14 +39,15 @@ namespace {
 constexpr int GM = 128;            // rows per CTA (MMA M)
 constexpr int GN = 128;            // tokens per CTA (MMA N)
 constexpr int GK = 64;             // K per stage: one 128-byte swizzle row of f16
-constexpr int kStages = 3;
+constexpr int kAStages = 2;        // dequantized weight tiles (hi, lo): filled from registers, no latency to hide
+constexpr int kBStages = 5;        // activation tiles (hi, lo): ~2 us of loaded memory latency to cover
 constexpr int kProdWarps = 4;
 constexpr int kMmaWarp = kProdWarps;
 constexpr int kDqWarp0 = kProdWarps + 1;
 constexpr int kDqWarps = 8;
 constexpr int kThreads = (kDqWarp0 + kDqWarps) * 32;
 constexpr int kTileBytes = GM * GK * 2;   // one 128 x 64 f16 tile: 16 KB (B tiles are the same with GN = GM)
-constexpr int kStageBytes = 4 * kTileBytes;   // A hi, A lo, B hi, B lo
+constexpr int kPairBytes = 2 * kTileBytes;   // a hi tile and its lo tile
 constexpr int kQ6HOff = 2048, kQ6SOff = 3072, kQ6DOff = 3328;   // Q6_K unit regions (kq_layout.h)
 static_assert(GM == GN, "A and B tiles share one size");
 
@@ -330,13 +331,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
   constexpr int US = FMT == 0 ? 0 : FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);   // swizzle atoms need 1024
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
-  uint64_t *full_a = bars, *full_b = bars + kStages, *empty = bars + 2 * kStages, *acc_full = bars + 3 * kStages;
+  uint8_t *a_ring = smem, *b_ring = smem + kAStages * kPairBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(b_ring + kBStages * kPairBytes);
+  uint64_t *full_a = bars, *empty_a = bars + kAStages, *full_b = bars + 2 * kAStages, *empty_b = full_b + kBStages;
+  uint64_t *acc_full = empty_b + kBStages;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  auto a_hi = [&](int s) { return smem + (size_t)s * kStageBytes; };
-  auto a_lo = [&](int s) { return smem + (size_t)s * kStageBytes + kTileBytes; };
-  auto b_hi = [&](int s) { return smem + (size_t)s * kStageBytes + 2 * kTileBytes; };
+  auto a_hi = [&](int s) { return a_ring + (size_t)s * kPairBytes; };
+  auto a_lo = [&](int s) { return a_ring + (size_t)s * kPairBytes + kTileBytes; };
+  auto b_hi = [&](int s) { return b_ring + (size_t)s * kPairBytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tile = blockIdx.x, n_tile = blockIdx.y;
@@ -351,10 +354,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
   const int koff = FMT == 0 ? (m_tile * 28) % nks : 4 * koff_sb;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; s++) {
+    for (int s = 0; s < kAStages; s++) {
       mbar_init(&full_a[s], FMT == 0 ? kProdWarps * 32 : kDqWarps);
+      mbar_init(&empty_a[s], 1);
+    }
+    for (int s = 0; s < kBStages; s++) {
       mbar_init(&full_b[s], kProdWarps * 32);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty_b[s], 1);
     }
     mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -371,8 +377,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
     // of the A tile) with 16-byte cp.async; the stage's barrier counts every lane's completion
     const int pw = warp;
     for (int k = 0; k < nks; k++) {
-      const int s = k % kStages;
-      if (k >= kStages && !waitw(&empty[s], (uint32_t)(k / kStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
+      const int s = k % kBStages;
+      if (k >= kBStages && !waitw(&empty_b[s], (uint32_t)(k / kBStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
       const int kd = (k + koff) % nks;
       constexpr int QB = 2 * kTileBytes / kProdWarps;   // bytes of B hi + lo per producer warp
       const uint8_t *src = p.b + ((int64_t)n_tile * nks + kd) * 2 * kTileBytes + pw * QB;
@@ -381,12 +387,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
       for (int q = lane; q < QB / 16; q += 32) cp_async16(dst + q * 16, src + q * 16);
       cp_async_arrive(&full_b[s]);
       if constexpr (FMT == 0) {
+        // the A tile rides with the B stage: FMT 0 keeps k % kAStages == k % kBStages by waiting
+        // on the A ring's own barrier first
+        const int sa = k % kAStages;
+        if (k >= kAStages && !waitw(&empty_a[sa], (uint32_t)(k / kAStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
         constexpr int QA = kTileBytes / kProdWarps;
         const uint8_t *asrc = p.w + ((int64_t)m_tile * nks + kd) * kTileBytes + pw * QA;
-        const uint32_t adst = smem_u32(a_hi(s)) + pw * QA;
+        const uint32_t adst = smem_u32(a_hi(sa)) + pw * QA;
 #pragma unroll 4
         for (int q = lane; q < QA / 16; q += 32) cp_async16(adst + q * 16, asrc + q * 16);
-        cp_async_arrive(&full_a[s]);
+        cp_async_arrive(&full_a[sa]);
       }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");   // this warp's copies land before it leaves
@@ -395,12 +405,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
     if (lane == 0) {
       int issued = 0;
       for (int k = 0; k < nks; k++) {
-        const int s = k % kStages;
-        const uint32_t ph = (uint32_t)(k / kStages) & 1u;
-        if (!wait1(&full_b[s], ph, ctl, ST_FULL_TIMEOUT) || !wait1(&full_a[s], ph, ctl, ST_FULL_TIMEOUT)) break;
+        const int sb = k % kBStages, sa = k % kAStages;
+        if (!wait1(&full_b[sb], (uint32_t)(k / kBStages) & 1u, ctl, ST_FULL_TIMEOUT) ||
+            !wait1(&full_a[sa], (uint32_t)(k / kAStages) & 1u, ctl, ST_FULL_TIMEOUT))
+          break;
         fence_async_smem();                             // the generic-proxy stores / cp.async data -> the MMA's reads
         tc_fence_after();
-        const uint32_t ah = smem_u32(a_hi(s)), al = ah + kTileBytes, bh = ah + 2 * kTileBytes, bl = ah + 3 * kTileBytes;
+        const uint32_t ah = smem_u32(a_hi(sa)), al = ah + kTileBytes, bh = smem_u32(b_hi(sb)), bl = bh + kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < GK / 16; kk++) {
           const uint32_t o = kk * 32;
@@ -410,7 +421,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
             mma_f16(tmem, sw128_desc(al + o), sw128_desc(bh + o), kIdesc, 1u);
           }
         }
-        mma_commit(&empty[s]);                          // the stage is free once these MMAs finish
+        mma_commit(&empty_a[sa]);                       // the stages are free once these MMAs finish
+        mma_commit(&empty_b[sb]);
         issued++;
       }
       mma_commit(acc_full);                             // every MMA issued has finished
@@ -433,12 +445,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
       if (present) nxt.load(ubase + (int64_t)(koff_sb % p.nb) * US, m, tp);
       bool live = true;
       for (int k = 0; k < nks && live; k++) {
-        const int s = k % kStages, sbi = k >> 2, c = k & 3;
+        const int s = k % kAStages, sbi = k >> 2, c = k & 3;
         if (c == 0 && present) {
           cur.set(nxt, p.wscale);
           if (sbi + 1 < p.nb) nxt.load(ubase + (int64_t)((sbi + 1 + koff_sb) % p.nb) * US, m, tp);
         }
-        if (k >= kStages) live = waitw(&empty[s], (uint32_t)(k / kStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane);
+        if (k >= kAStages) live = waitw(&empty_a[s], (uint32_t)(k / kAStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane);
         if (!live) break;
         uint4 hi[4], lo[4];
         if (present) {
@@ -588,7 +600,8 @@ cudaError_t launch_t(const GemmArgs &a, dim3 grid, size_t smem, cudaStream_t s) 
   return cudaGetLastError();
 }
 
-constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + (3 * kStages + 1) * 8 + 16;
+constexpr size_t kSmem = 1024 + (size_t)(kAStages + kBStages) * kPairBytes + (2 * kAStages + 2 * kBStages + 1) * 8 + 16;
+static_assert(kSmem <= 227 * 1024, "shared memory");
 
 // An upper bound of |dequantized value| over a k-quant matrix, as the bits of a non-negative f32
 // (atomicMax on the bits orders them); a NaN or infinite scale makes it +inf.
