@@ -209,6 +209,18 @@ int zllm_model_set_matrix(zllm_model *m, int kind, int layer, int ggml_type, int
                           const void *host_bytes, size_t nbytes);
 /* An f32 vector (norm weights, biases, RoPE frequency factors). */
 int zllm_model_set_vector(zllm_model *m, int kind, int layer, const float *host, int64_t n);
+/* ------------------------------------------------------------------------ tensor parallelism
+ * A model too large for one GPU runs with its weights sharded over `size` GPUs, one process (one
+ * context, one model) per GPU: each rank's model is created with its local configuration (its
+ * query / KV heads and its slice of the FFN; the host cuts the shards) and joins the group before
+ * its first pass.  attn_output and ffn_down are row-parallel: after each, the ranks' partial sums
+ * are added with an NCCL all-reduce over NVLink (the reference has one process and no such step;
+ * BASELINE config 4).  NCCL is opened at run time (libnccl.so.2).
+ * zllm_tp_unique_id: rank 0 creates the group's id (out: NCCL_UNIQUE_ID_BYTES = 128 bytes), which the
+ * host hands to every rank; zllm_model_set_tp blocks until all `size` ranks have joined. */
+int zllm_tp_unique_id(zllm_ctx *ctx, void *out, size_t bytes);
+int zllm_model_set_tp(zllm_model *m, int rank, int size, const void *unique_id);
+
 /* Allocate the KV caches and activations once every tensor is set (called by the first pass). */
 int zllm_model_ready(zllm_model *m);
 /* n tokens of sequence `seq` at its next positions in one pass (forwardBatch, pool.js:145-160;

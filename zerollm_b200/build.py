@@ -22,8 +22,25 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libzllm_cuda.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+def _nccl_include() -> list[str]:
+    """The NCCL header (declarations only: the library is opened at run time by tp.cu)."""
+    cands = []
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia")
+        for base in (spec.submodule_search_locations or []) if spec else []:
+            cands.append(os.path.join(base, "nccl", "include"))
+    except Exception:
+        pass
+    cands += ["/usr/include", "/usr/local/cuda/include"]
+    for c in cands:
+        if os.path.exists(os.path.join(c, "nccl.h")):
+            return [f"-I{c}"]
+    raise RuntimeError("nccl.h not found")
+
+
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
-              "-Xptxas", "-warn-spills", f"-I{os.path.join(ROOT, 'include')}", f"-I{CSRC}"]
+              "-Xptxas", "-warn-spills", f"-I{os.path.join(ROOT, 'include')}", f"-I{CSRC}", *_nccl_include()]
 
 
 def nvcc() -> str:

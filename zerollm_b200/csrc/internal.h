@@ -128,6 +128,13 @@ cudaError_t launch_kq_bound(const DevMatrix &m, unsigned *out, cudaStream_t s);
 cudaError_t launch_gemm_prep(const ActView &act, int ntok, void *bbuf, cudaStream_t s);
 cudaError_t launch_gemm_kq(const DevMatrix &m, const void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
                            float wscale, unsigned *status, cudaStream_t s, bool swiglu = false);
+// Tensor-parallel collectives (tp.cu): NCCL opened at run time.  Return 0 / cudaSuccess, else set *why.
+size_t tp_unique_id_bytes();
+int tp_unique_id(void *out, size_t bytes, const char **why);
+int tp_comm_init(void **comm, int rank, int size, const void *unique_id, const char **why);
+void tp_comm_destroy(void *comm);
+cudaError_t tp_allreduce_sum(void *comm, float *buf, size_t count, cudaStream_t s, const char **why);
+
 // f16 x f16 -> f32 on the same kernel: D[j][i] = sum_k A[i][k] B[j][k] (row-major, k % 64 == 0)
 size_t gemm_f16_scratch_bytes(int64_t m, int64_t n, int64_t k);
 cudaError_t launch_gemm_f16(const uint16_t *A, const uint16_t *B, int64_t m, int64_t n, int64_t k, float *D, void *scratch,

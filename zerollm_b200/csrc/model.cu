@@ -62,6 +62,8 @@ struct zllm_model {
   float *g = nullptr, *u = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
   float *qkv = nullptr, *gu = nullptr;                   // outputs of the row-concatenated projections
   void *gemm_b = nullptr;                                // f16 activation tiles of the tensor-core GEMM (max_batch >= 16)
+  void *tp_comm = nullptr;                               // NCCL communicator when the weights are sharded
+  int tp_rank = 0, tp_size = 1;
   int8_t *xq = nullptr;
   float *xd = nullptr;
   int32_t *xs = nullptr, *d_tok = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_npos = nullptr, *d_arg = nullptr;
@@ -250,6 +252,28 @@ static zllm_weight *concat_rows(zllm_model *m, std::initializer_list<zllm_weight
   return f;
 }
 
+extern "C" int zllm_tp_unique_id(zllm_ctx *ctx, void *out, size_t bytes) {
+  if (!ctx || !out) return ZLLM_E_ARG;
+  const char *why = "";
+  if (tp_unique_id(out, bytes, &why)) { zllm_set_error(ctx, "zllm_tp_unique_id: %s", why); return ZLLM_E_UNSUPPORTED; }
+  return ZLLM_OK;
+}
+
+extern "C" int zllm_model_set_tp(zllm_model *m, int rank, int size, const void *unique_id) {
+  if (!m || !unique_id || size < 1 || rank < 0 || rank >= size) return ZLLM_E_ARG;
+  if (m->ready || m->tp_comm) { zllm_set_error(m->ctx, "zllm_model_set_tp: call it once, before the first pass"); return ZLLM_E_STATE; }
+  if (size == 1) return ZLLM_OK;
+  cudaSetDevice(m->ctx->device);
+  const char *why = "";
+  if (tp_comm_init(&m->tp_comm, rank, size, unique_id, &why)) {
+    zllm_set_error(m->ctx, "zllm_model_set_tp: %s", why);
+    return ZLLM_E_CUDA;
+  }
+  m->tp_rank = rank;
+  m->tp_size = size;
+  return ZLLM_OK;
+}
+
 extern "C" int zllm_model_ready(zllm_model *m) {
   if (!m) return ZLLM_E_ARG;
   if (m->ready) return ZLLM_OK;
@@ -350,6 +374,13 @@ static cudaError_t gemv_ex(zllm_model *m, const zllm_weight *w, int n, float *y,
   return launch_gemv_kq_ex(w->m, act, n, y, ys, y_add, fz, m->ctx->status_dev, m->ctx->num_sms, m->stream, pdl, &why);
 }
 
+// Sum the ranks' x (n tokens x n_embd) in place: the all-reduce after a row-parallel projection.
+static cudaError_t tp_reduce(zllm_model *m, int n) {
+  if (m->tp_size <= 1) return cudaSuccess;
+  const char *why = "";
+  return tp_allreduce_sum(m->tp_comm, m->x, (size_t)n * m->c.n_embd, m->stream, &why);
+}
+
 // Enqueue the pass for n tokens whose ids / positions / sequences are already in d_tok / d_pos /
 // d_seq / d_npos.  want: 0 no logits, 1 the last token's, 2 every token's.
 static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
@@ -404,12 +435,17 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
     // depend on how many tokens share the pass, so batched passes equal token-by-token ones bit for bit
     aa.n_head = c.n_head; aa.n_kv = c.n_head_kv; aa.head_dim = c.head_dim; aa.nseq = n; aa.nsplit = m->nsplit;
     RUN(launch_attn(aa, c.kv_f16 != 0, s, false));
+    // tensor parallel: attn_output and ffn_down are row-parallel, so each rank holds a partial sum;
+    // rank 0 adds the residual, the others overwrite x, and one all-reduce gives every rank
+    // x + sum of the partials
+    const float *res = m->tp_size > 1 && m->tp_rank != 0 ? nullptr : m->x;
     if (one && kq_type(L.w[WO]->m.type)) {
-      RUN(gemv_ex(m, L.w[WO], 1, m->x, E, m->x, ActView{nullptr, nullptr, nullptr, m->att, Q}, GemvFuse{}));
+      RUN(gemv_ex(m, L.w[WO], 1, m->x, E, res, ActView{nullptr, nullptr, nullptr, m->att, Q}, GemvFuse{}));
     } else {
       RUN(launch_quantize(m->att, Q, n, m->xq, m->xd, m->xs, m->ctx->status_dev, s, false));
-      RUN(gemv(m, L.w[WO], n, m->x, E, m->x, m->att, Q));                     // x += wo . att
+      RUN(gemv(m, L.w[WO], n, m->x, E, res, m->att, Q));                      // x += wo . att
     }
+    RUN(tp_reduce(m, n));
     if (L.gu) {
       // interleaved (gate, up) rows; the GEMV writes hb = silu(gate) * up
       GemvFuse fz;
@@ -423,17 +459,19 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
         RUN(gemv_ex(m, L.gu, n, m->hb, F, nullptr, ActView{m->xq, m->xd, m->xs, m->xb, E}, fz));
       }
       if (one && kq_type(L.w[DOWN]->m.type)) {
-        RUN(gemv_ex(m, L.w[DOWN], 1, m->x, E, m->x, ActView{nullptr, nullptr, nullptr, m->hb, F}, GemvFuse{}, true));
+        RUN(gemv_ex(m, L.w[DOWN], 1, m->x, E, res, ActView{nullptr, nullptr, nullptr, m->hb, F}, GemvFuse{}, true));
       } else {
         RUN(launch_quantize(m->hb, F, n, m->xq, m->xd, m->xs, m->ctx->status_dev, s, false));
-        RUN(gemv(m, L.w[DOWN], n, m->x, E, m->x, m->hb, F));                  // x += down . hb
+        RUN(gemv(m, L.w[DOWN], n, m->x, E, res, m->hb, F));                   // x += down . hb
       }
+      RUN(tp_reduce(m, n));
     } else {
       RUN(launch_rmsnorm_quant(m->x, L.ffn_norm, (int)E, n, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, false));
       RUN(gemv(m, L.w[GATE], n, m->g, F, nullptr, m->xb, E));
       RUN(gemv(m, L.w[UP], n, m->u, F, nullptr, m->xb, E));
       RUN(launch_swiglu_quant(m->g, m->u, (int)F, n, F, m->hb, m->xq, m->xd, m->xs, s, false));
-      RUN(gemv(m, L.w[DOWN], n, m->x, E, m->x, m->hb, F));                    // x += down . hb
+      RUN(gemv(m, L.w[DOWN], n, m->x, E, res, m->hb, F));                     // x += down . hb
+      RUN(tp_reduce(m, n));
     }
   }
   if (want) {
@@ -718,6 +756,7 @@ extern "C" void zllm_model_destroy(zllm_model *m) {
                   (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b})
     if (p) cudaFree(p);
   if (m->h_io) cudaFreeHost(m->h_io);
+  if (m->tp_comm) tp_comm_destroy(m->tp_comm);          // after the graphs that hold its collectives
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }

@@ -39,10 +39,15 @@ class CudaModel:
 
     @classmethod
     def create(cls, cfg: dict, weights: dict, ctx: int = 2048, kv: str = "f32", max_batch: int = 16,
-               logits_batch: int | None = None, device: int = 0, n_seq: int = 1, context: Context | None = None):
-        return cls(cfg, weights, ctx, kv, max_batch, logits_batch, device, n_seq, context)
+               logits_batch: int | None = None, device: int = 0, n_seq: int = 1, context: Context | None = None,
+               tp: tuple | None = None):
+        return cls(cfg, weights, ctx, kv, max_batch, logits_batch, device, n_seq, context, tp)
 
-    def __init__(self, cfg, weights, ctx=2048, kv="f32", max_batch=16, logits_batch=None, device=0, n_seq=1, context=None):
+    def __init__(self, cfg, weights, ctx=2048, kv="f32", max_batch=16, logits_batch=None, device=0, n_seq=1, context=None,
+                 tp=None):
+        """``tp = (rank, size, unique_id)`` joins a tensor-parallel group: ``cfg`` / ``weights`` are
+        then this rank's shard (zerollm_b200.tp.shard_model) and ``unique_id`` the group's id from
+        rank 0's ``tp_unique_id``."""
         if kv not in ("f32", "f16"):
             raise ValueError(f'kv must be f32 or f16 (got "{kv}")')
         self.cfg = dict(cfg)
@@ -68,6 +73,10 @@ class CudaModel:
         h = C.c_void_p()
         self._check(self.lib.zllm_model_create(self.context.h, C.byref(mc), C.byref(h)), "zllm_model_create")
         self.h = h
+        if tp is not None:
+            rank, size, uid = tp
+            buf = C.create_string_buffer(bytes(uid), len(uid))
+            self._check(self.lib.zllm_model_set_tp(self.h, int(rank), int(size), buf), "zllm_model_set_tp")
         self._load(weights)
         self._check(self.lib.zllm_model_ready(self.h), "zllm_model_ready")
         self._logits = np.zeros((self.logitsBatch if self.n_seq == 1 else max(self.logitsBatch, self.n_seq), self.vocab),
@@ -232,3 +241,13 @@ class CudaModel:
             self.close()
         except Exception:
             pass
+
+
+def tp_unique_id(context: Context) -> bytes:
+    """A new tensor-parallel group id (rank 0 creates it; every rank passes it to CudaModel(tp=...))."""
+    lib = load()
+    buf = C.create_string_buffer(128)
+    rc = lib.zllm_tp_unique_id(context.h, buf, 128)
+    if rc:
+        raise ZllmError(rc, lib.zllm_last_error(context.h).decode())
+    return buf.raw
