@@ -295,6 +295,106 @@ def decode_bench(n_seq: int, device: int, profile: bool = False):
             "hbm_gbs": round(step_bytes / (dt / steps) / 1e9, 1)}
 
 
+# ------------------------------------------------------------------------------------------ TP decode (config 4)
+TP_PROMPT, TP_STEPS, TP_CTX = 512, 128, 8192
+TP_SHAPE = dict(n_embd=5120, n_layer=64, n_ff=25600, n_head=64, n_head_kv=8, head_dim=128, vocab=151936)
+
+
+def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
+    """Config 4: random-init Qwen3-32B shapes (64 layers, hidden 5120, FFN 25600, 64 query / 8 KV
+    heads, head_dim 128, vocab 151936), Q4_K everywhere but Q6_K ffn_down, f16 output head, f16 KV
+    cache of 8192 positions, tensor-parallel over the `world` GPUs: each rank draws its own shard
+    (its 64/world query and 8/world KV heads, its 1/world of the FFN at 256-value blocks), the
+    replicated tensors (embedding, norms, output head) from one shared seed; an NCCL all-reduce
+    follows attn_output and ffn_down.  Prefill TP_PROMPT seeded ids per sequence, then TP_STEPS
+    greedy steps through zllm_model_generate, timed with CUDA events on the model's stream."""
+    import ctypes as C
+
+    import torch
+
+    from zerollm_b200 import ggml
+    from zerollm_b200.kernels import Context
+    from zerollm_b200.lib import (T_ATTN_NORM, T_DOWN, T_FFN_NORM, T_GATE, T_K_NORM, T_OUTPUT, T_OUTPUT_NORM, T_Q_NORM,
+                                  T_TOK_EMBD, T_UP, T_WK, T_WO, T_WQ, T_WV, ModelConfig, check)
+    from zerollm_b200.model import tp_unique_id
+    from zerollm_b200.tp import ranges
+    c = TP_SHAPE
+    E, F, V, NL, hd = c["n_embd"], c["n_ff"], c["vocab"], c["n_layer"], c["head_dim"]
+    Hl, KVl = c["n_head"] // world, c["n_head_kv"] // world
+    f0, f1 = [(a * 256, b * 256) for a, b in ranges(F // 256, world)][rank]
+    Fl = f1 - f0
+    ctx = Context(device)
+    L = ctx.lib
+    uid = b"\0" * 128
+    if world > 1:
+        import torch.distributed as dist
+        obj = [tp_unique_id(ctx) if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    mc = ModelConfig(n_embd=E, n_layer=NL, n_ff=Fl, n_head=Hl, n_head_kv=KVl, head_dim=hd, n_rot=hd, vocab=V, neox=1,
+                     kv_f16=1, ctx=TP_CTX, n_seq=n_seq, max_batch=64, logits_batch=16, rms_eps=float(np.float32(1e-6)),
+                     rope_base=1e6)
+    h = C.c_void_p()
+    check(L.zllm_model_create(ctx.h, C.byref(mc), C.byref(h)), ctx.h)
+    if world > 1:
+        ub = C.create_string_buffer(uid, 128)
+        check(L.zllm_model_set_tp(h, rank, world, ub), ctx.h)
+    g_local = torch.Generator(device="cuda")
+    g_local.manual_seed(SEED + 1000 * (rank + 1))          # this rank's shards
+    g_shared = torch.Generator(device="cuda")
+    g_shared.manual_seed(SEED)                            # replicated tensors: the same on every rank
+    rng = np.random.default_rng(SEED)
+
+    def mat(kind, layer, t, rows, cols, g):
+        buf = _gen_kquant(t, rows, cols, g) if t != ggml.F16 else \
+            (torch.randn(rows, cols, device="cuda", generator=g) * 0.02).half().view(torch.uint8).cpu().numpy().reshape(-1)
+        check(L.zllm_model_set_matrix(h, kind, layer, t, rows, cols, buf.ctypes.data_as(C.c_void_p), buf.nbytes), ctx.h)
+
+    def vec(kind, layer, n):
+        a = (1 + rng.standard_normal(n) * 0.02).astype(np.float32)
+        check(L.zllm_model_set_vector(h, kind, layer, a.ctypes.data_as(C.c_void_p), a.size), ctx.h)
+
+    mat(T_TOK_EMBD, 0, ggml.Q4_K, V, E, g_shared)
+    mat(T_OUTPUT, 0, ggml.F16, V, E, g_shared)
+    vec(T_OUTPUT_NORM, 0, E)
+    for l in range(NL):
+        for k_, n_ in ((T_ATTN_NORM, E), (T_FFN_NORM, E), (T_Q_NORM, hd), (T_K_NORM, hd)):
+            vec(k_, l, n_)
+        for k_, t_, r_, c_ in ((T_WQ, ggml.Q4_K, Hl * hd, E), (T_WK, ggml.Q4_K, KVl * hd, E), (T_WV, ggml.Q4_K, KVl * hd, E),
+                               (T_WO, ggml.Q4_K, E, Hl * hd), (T_GATE, ggml.Q4_K, Fl, E), (T_UP, ggml.Q4_K, Fl, E),
+                               (T_DOWN, ggml.Q6_K, E, Fl)):
+            mat(k_, l, t_, r_, c_, g_local)
+    check(L.zllm_model_ready(h), ctx.h)
+    P = lambda a: a.ctypes.data_as(C.c_void_p)
+    arg = np.zeros(64, np.int32)
+    first = np.zeros(n_seq, np.int32)
+    for s_ in range(n_seq):
+        toks = rng.integers(0, V, TP_PROMPT).astype(np.int32)
+        for i in range(0, TP_PROMPT, 64):
+            chunk = np.ascontiguousarray(toks[i:i + 64])
+            want = 1 if i + 64 >= TP_PROMPT else 0
+            check(L.zllm_model_forward(h, s_, P(chunk), chunk.size, want, None, P(arg) if want else None), ctx.h)
+        first[s_] = arg[0]
+    seqs = np.arange(n_seq, dtype=np.int32)
+    seqp = None if n_seq == 1 else P(seqs)
+    out = np.zeros((TP_STEPS, n_seq), np.int32)
+    check(L.zllm_model_generate(h, 0, seqp, P(first), n_seq, 3, P(out)), ctx.h)      # warm-up: record the graphs
+    cur = np.ascontiguousarray(out[2])
+    st = torch.cuda.ExternalStream(L.zllm_model_stream(h), device=f"cuda:{device}")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    check(L.zllm_model_generate(h, 0, seqp, P(cur), n_seq, TP_STEPS, P(out)), ctx.h)
+    e1.record(st)
+    e1.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3
+    same = out[-1].copy()
+    L.zllm_model_destroy(h)                               # releases the graphs before the communicator
+    ctx.close()
+    wbytes = NL * (2.25 * (Hl * hd * E + 2 * KVl * hd * E + E * Hl * hd + 2 * Fl * E) / 4 + 210 / 256 * E * Fl) + V * E * 2
+    return {"seconds": dt, "ms_per_step": round(dt / TP_STEPS * 1e3, 3), "weight_bytes_per_rank": int(wbytes),
+            "last_tokens": same.tolist()}
+
+
 # ------------------------------------------------------------------------------------------ attention (config 2)
 def attn_bench(device: int, reps: int = 20):
     """Config 2: GQA decode attention, 32 query / 8 KV heads, head_dim 128, f16 K/V caches filled
@@ -530,6 +630,17 @@ def run_ours(args, world, rank, local):
                                   "prefill_tok_s_per_gpu": r["prefill_tok_s"], "hbm_gbs_per_gpu": r["hbm_gbs"],
                                   "step_bytes_per_gpu": r["step_bytes"]}
 
+    tp = {}
+    if not args.no_decode and not args.no_tp:
+        torch.cuda.empty_cache()
+        for nseq in (1, 16):
+            barrier()
+            r = tp_decode_bench(nseq, world, rank, local)
+            slowest = max_over_ranks(r["seconds"])
+            tp[f"b{nseq}"] = {"tok_s": round(nseq * TP_STEPS / slowest, 1), "ms_per_step": round(slowest / TP_STEPS * 1e3, 3),
+                              "weight_bytes_per_rank": r["weight_bytes_per_rank"],
+                              "hbm_gbs_per_rank_weights": round(r["weight_bytes_per_rank"] / (slowest / TP_STEPS) / 1e9, 1)}
+
     if rank == 0:
         peak, peak_kind = measured_peaks()
         value = ALGO_BYTES * args.steps * world / (ms / 1e3) / 1e9
@@ -567,6 +678,13 @@ def run_ours(args, world, rank, local):
                               "kv": f"f16, ctx {DEC_CTX}", "prompt": DEC_PROMPT, "steps": DEC_STEPS,
                               "api": "zllm_model_generate (greedy, argmax fed back on the device)",
                               "scaling": "weak (one model replica and its sequences per GPU)", **decode}
+        if tp:
+            line["tp_decode"] = {"metric": "32B Q4_K_M tensor-parallel decode tok/s (config 4)", "unit": "tok/s",
+                                 "model": "Qwen3-32B shapes, random init: Q4_K + Q6_K ffn_down, f16 output head (replicated)",
+                                 "tp": world, "kv": f"f16, ctx {TP_CTX}", "prompt": TP_PROMPT, "steps": TP_STEPS,
+                                 "collective": "NCCL all-reduce after attn_output and ffn_down, inside the captured pass",
+                                 "timing": "CUDA events on the model stream, max over ranks",
+                                 "scaling": "strong (one model over all GPUs)", **tp}
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds, os.cpu_count() or 1)
         print(json.dumps(line), flush=True)
@@ -583,7 +701,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="plain launches without graphs or timing, for ncu")
-    ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode, attention and 32B TP measurements")
+    ap.add_argument("--no-tp", action="store_true", help="skip the 32B tensor-parallel decode measurement")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="NSEQ",
                     help="only the 8B decode at NSEQ sequences, 2 steps inside an NVTX range 'decode' (for ncu)")
     args = ap.parse_args()

@@ -219,6 +219,9 @@ int zllm_model_set_vector(zllm_model *m, int kind, int layer, const float *host,
  * zllm_tp_unique_id: rank 0 creates the group's id (out: NCCL_UNIQUE_ID_BYTES = 128 bytes), which the
  * host hands to every rank; zllm_model_set_tp blocks until all `size` ranks have joined. */
 int zllm_tp_unique_id(zllm_ctx *ctx, void *out, size_t bytes);
+/* The model's own stream (a cudaStream_t): every pass runs on it; a caller may record CUDA events
+ * on it to time passes on the device (no reference counterpart). */
+void *zllm_model_stream(zllm_model *m);
 int zllm_model_set_tp(zllm_model *m, int rank, int size, const void *unique_id);
 
 /* Allocate the KV caches and activations once every tensor is set (called by the first pass). */

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 TOKS = [3, 17, 42, 5, 88, 1, 250, 7]
-BATCH = [(5 * i + 2) % 320 for i in range(20)]     # 20 tokens: the tensor-core GEMM plus the all-reduce
+BATCH = [(5 * i + 2) % 320 for i in range(64)]     # 64 tokens: the tensor-core GEMM plus the all-reduce
 
 
 def _model():
@@ -40,7 +40,7 @@ def _rank(rank, size, uid_q, out_q):
         uid = uid_q.get(timeout=120)
     cfg, w = _model()
     lc, lw = shard_model(cfg, w, rank, size)
-    m = CudaModel.create(lc, lw, ctx=64, kv="f16", max_batch=32, device=rank, context=ctx, tp=(rank, size, uid))
+    m = CudaModel.create(lc, lw, ctx=96, kv="f16", max_batch=64, device=rank, context=ctx, tp=(rank, size, uid))
     step = [m.forward(t).copy() for t in TOKS]
     last = m.forwardBatch(BATCH, logits="last").copy()
     m.close()
@@ -70,7 +70,7 @@ def test_tp2_matches_single_gpu():
     assert sorted(res) == [0, 1], "a rank did not finish"
     assert np.array_equal(res[0][0], res[1][0]) and np.array_equal(res[0][1], res[1][1])
     cfg, w = _model()
-    one = CudaModel.create(cfg, w, ctx=64, kv="f16", max_batch=32)
+    one = CudaModel.create(cfg, w, ctx=96, kv="f16", max_batch=64)
     want = [one.forward(t).copy() for t in TOKS] + [one.forwardBatch(BATCH, logits="last").copy()]
     got = list(res[0][0]) + [res[0][1]]
     for g, ww in zip(got, want):

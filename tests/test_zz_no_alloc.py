@@ -4,6 +4,7 @@ the results agree well inside the attention tolerance) on two calls in a row wit
 lengths, with no change in the device's free memory across those calls; oversized requests are
 refused before anything runs."""
 import ctypes as C
+import gc
 
 import numpy as np
 import pytest
@@ -48,13 +49,14 @@ def test_noalloc_matches_allocating_entry_point():
         assert _call(ctx, L.zllm_attn_decode_noalloc, g, q, cache, npos0, lens[0].max(), warm) == 0
         outs = [torch.empty_like(q) for _ in lens]
         npos = [torch.as_tensor(n).cuda() for n in lens]
+        gc.collect()                                                # earlier tests' handles are freed now, not mid-check
         torch.cuda.synchronize()
         free0 = torch.cuda.mem_get_info()[0]
         for n, t, o in zip(lens, npos, outs):                       # two calls in a row, different lengths
             assert _call(ctx, L.zllm_attn_decode_noalloc, g, q, cache, t, n.max(), o) == 0, \
                 L.zllm_last_error(ctx.h).decode()
         torch.cuda.synchronize()
-        assert torch.cuda.mem_get_info()[0] == free0
+        assert torch.cuda.mem_get_info()[0] >= free0                # nothing allocated (a late free elsewhere may add)
         assert ctx.lib.zllm_sync(ctx.h) == 0
         for got, ref in zip(outs, want):
             rel = float((got - ref).abs().max() / ref.abs().max())

@@ -119,7 +119,8 @@ cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t 
 // computes y[t][r] (+ y_add) for all tokens.  launch_kq_bound writes an upper bound of the
 // matrix's |dequantized value| (as f32 bits); a finite bound qualifies the matrix, and
 // gemm_weight_scale(bound) is the power of two that brings its values just under 2^15 in f16.
-constexpr int kGemmMinTokens = 16;
+constexpr int kGemmMinTokens = 16;        // zllm_mm
+constexpr int kModelGemmMinTokens = 64;   // model passes: below this the per-token kernel streams the weights faster
 float gemm_weight_scale(float bound);
 int64_t gemm_tokens_pad(int ntok);
 size_t gemm_b_bytes(int64_t k, int ntok);

@@ -252,6 +252,8 @@ static zllm_weight *concat_rows(zllm_model *m, std::initializer_list<zllm_weight
   return f;
 }
 
+extern "C" void *zllm_model_stream(zllm_model *m) { return m ? (void *)m->stream : nullptr; }
+
 extern "C" int zllm_tp_unique_id(zllm_ctx *ctx, void *out, size_t bytes) {
   if (!ctx || !out) return ZLLM_E_ARG;
   const char *why = "";
@@ -319,7 +321,7 @@ extern "C" int zllm_model_ready(zllm_model *m) {
   CK(dalloc(&m->g, MB * F), "act");
   CK(dalloc(&m->u, MB * F), "act");
   CK(dalloc(&m->hb, MB * F), "act");
-  if (MB >= kGemmMinTokens) {
+  if (MB >= kModelGemmMinTokens) {
     // passes of 16 or more tokens run the k-quant projections as tensor-core GEMMs
     CK(cudaMalloc(&m->gemm_b, gemm_b_bytes(KX, MB)), "GEMM activation tiles");
     for (auto &L : m->L)
@@ -345,10 +347,12 @@ extern "C" int zllm_model_ready(zllm_model *m) {
 }
 
 // ------------------------------------------------------------------------------------ the pass
-// 16 or more tokens on a k-quant weight that qualifies: the tensor-core GEMM on f16 tiles of the
-// quantized activation (within the 1e-3 contract; not bit-identical to the per-token arithmetic).
+// 64 or more tokens (a prefill chunk) on a k-quant weight that qualifies: the tensor-core GEMM on
+// f16 hi / lo tiles of the quantized activation (~1e-5 of the largest output from the exact
+// per-token arithmetic).  Smaller batches (batched decode) keep the per-token kernel, which streams
+// the weights faster at that size and stays bit-identical to single-token passes.
 static bool use_gemm(const zllm_model *m, const zllm_weight *w, int n) {
-  return n >= kGemmMinTokens && m->gemm_b && w->gemm_ok == 1;
+  return n >= kModelGemmMinTokens && m->gemm_b && w->gemm_ok == 1;
 }
 static cudaError_t gemm(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add, int64_t k,
                         bool swiglu) {
