@@ -56,6 +56,17 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def measured_tensor_peak():
+    """Dense f16/bf16 tensor peak for a kernel timed alone (the burst figure), TFLOP/s."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        for k in ("bf16_tflops", "bf16_tflops_burst"):
+            if k in j:
+                return float(j[k]), "measured (MEASURED_PEAKS.json bf16_tflops, burst; f16 runs at the same rate)"
+    return 1590.0, "fallback (1.59 PFLOP/s burst)"
+
+
 def traffic_from_profile():
     """dram bytes (read + write) per launch from the committed ncu summary of this kernel, if any."""
     p = os.path.join(ROOT, "profiles", "gemv_q4k_4096x4096.md")
@@ -293,6 +304,130 @@ def decode_bench(n_seq: int, device: int, profile: bool = False):
     return {"tok_s": round(n_seq * steps / dt, 1), "ms_per_step": round(dt / steps * 1e3, 3), "seconds": dt,
             "prefill_tok_s": round(n_seq * DEC_PROMPT / prefill_s, 1), "step_bytes": int(step_bytes),
             "hbm_gbs": round(step_bytes / (dt / steps) / 1e9, 1)}
+
+
+# ------------------------------------------------------------------------------------------ prefill GEMM (config 1)
+GEMM_TOKENS = 512
+GEMM_MIX = (("attn_q", "Q4_K", 4096, 4096), ("attn_k", "Q4_K", 1024, 4096), ("attn_v", "Q4_K", 1024, 4096),
+            ("attn_output", "Q4_K", 4096, 4096), ("ffn_gate", "Q4_K", 12288, 4096), ("ffn_up", "Q4_K", 12288, 4096),
+            ("ffn_down", "Q6_K", 4096, 12288))
+
+
+def gemm_bench(device: int, reps: int = 20):
+    """Config 1: the prefill GEMM mix of one Qwen3-8B layer (Q4_K q / k / v / o / gate / up, Q6_K
+    down, seeded config-0 distributions) against 512 tokens of N(0,1) activations, quantized once.
+    One step per matrix = zllm_mm on 512 tokens (the f16 hi / lo activation tiles are prepared inside
+    the call, then the tcgen05 GEMM); `reps` steps per matrix in a CUDA graph (replayed once untimed),
+    CUDA events on the launching stream."""
+    import ctypes as C
+
+    import torch
+
+    from zerollm_b200 import ggml
+    from zerollm_b200.kernels import Context, Weight
+    from zerollm_b200.lib import check
+    ctx = Context(device)
+    L = ctx.lib
+    P = lambda t: C.c_void_p(t.data_ptr())
+    stream = torch.cuda.Stream(device=device)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 7)
+    T = GEMM_TOKENS
+    out, tot_fl, tot_us = {}, 0.0, 0.0
+    for name, tname, rows, cols in GEMM_MIX:
+        t = ggml.NAMES[tname]
+        w = Weight(ctx, t, rows, cols, _gen_kquant(t, rows, cols, g))
+        x = torch.randn(T, cols, device="cuda", generator=g)
+        xq = torch.empty(T, cols, dtype=torch.int8, device="cuda")
+        xd = torch.empty(T, cols // 32, device="cuda")
+        xs = torch.empty(T, cols // 32, dtype=torch.int32, device="cuda")
+        y = torch.empty(T, rows, device="cuda")
+        s = C.c_void_p(stream.cuda_stream)
+        check(L.zllm_quantize_act(ctx.h, P(x), cols, T, P(xq), P(xd), P(xs), s), ctx.h)
+
+        def run():
+            check(L.zllm_mm(ctx.h, w.h, P(xq), P(xd), P(xs), None, T, P(y), rows, None, s), ctx.h)
+        with torch.cuda.stream(stream):
+            run()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for _ in range(reps):
+                run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            gr.replay()
+            e0.record(stream)
+            gr.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ctx.sync()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        fl = 2.0 * rows * cols * T
+        tot_fl += fl
+        tot_us += us
+        out[name] = {"type": tname, "rows": rows, "cols": cols, "us": round(us, 2), "tflops": round(fl / us / 1e6, 1)}
+        del gr, w
+    ctx.close()
+    return out, tot_fl, tot_us
+
+
+def profile_run(args, device: int):
+    """Plain launches without graphs or timing, for ncu: --profile-gemm (config 1's attn_q at 512
+    tokens: gemm_bscale / gemm_bfill / gemm_kq_kernel per step) or --profile-attn CTX NSEQ (config 2:
+    qkv_post_kernel + attn_decode_kernel per step); args.warmup + args.steps steps."""
+    import ctypes as C
+
+    import torch
+
+    from zerollm_b200 import ggml
+    from zerollm_b200.kernels import Context, Weight
+    from zerollm_b200.lib import check
+    ctx = Context(device)
+    L = ctx.lib
+    P = lambda t: C.c_void_p(t.data_ptr())
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED + 7)
+    n = args.warmup + args.steps
+    if args.profile_gemm:
+        _, tname, rows, cols = GEMM_MIX[0]
+        t = ggml.NAMES[tname]
+        w = Weight(ctx, t, rows, cols, _gen_kquant(t, rows, cols, g))
+        T = GEMM_TOKENS
+        x = torch.randn(T, cols, device="cuda", generator=g)
+        xq = torch.empty(T, cols, dtype=torch.int8, device="cuda")
+        xd = torch.empty(T, cols // 32, device="cuda")
+        xs = torch.empty(T, cols // 32, dtype=torch.int32, device="cuda")
+        y = torch.empty(T, rows, device="cuda")
+        check(L.zllm_quantize_act(ctx.h, P(x), cols, T, P(xq), P(xd), P(xs), None), ctx.h)
+        for _ in range(n):
+            check(L.zllm_mm(ctx.h, w.h, P(xq), P(xd), P(xs), None, T, P(y), rows, None, None), ctx.h)
+        torch.cuda.synchronize()
+        ctx.sync()
+        ctx.close()
+        return {"profile_gemm": True, "launches": n, "rows": rows, "cols": cols, "tokens": T}
+    from zerollm_b200.attention import KVCache, attn_decode, qkv_append, rope_tables
+    Lc, nseq = args.profile_attn
+    nh, nkv, hd = 32, 8, 128
+    cache = KVCache(ctx, 1, nkv, hd, Lc + 8, True, nseq)
+    cache.t.copy_(torch.randn(cache.t.shape, device="cuda", generator=g).half().view(torch.int16))
+    geo = cache.geom(nh, eps=float(np.float32(1e-6)))
+    rope = rope_tables(ctx, hd, 1e6, Lc + 8)
+    q = torch.randn(nseq, nh * hd, device="cuda", generator=g)
+    k = torch.randn(nseq, nkv * hd, device="cuda", generator=g)
+    v = torch.randn(nseq, nkv * hd, device="cuda", generator=g)
+    qn = torch.ones(hd, device="cuda")
+    pos = torch.full((nseq,), Lc - 1, dtype=torch.int32, device="cuda")
+    seq = torch.arange(nseq, dtype=torch.int32, device="cuda")
+    npos = torch.full((nseq,), Lc, dtype=torch.int32, device="cuda")
+    qo, o = torch.empty_like(q), torch.empty_like(q)
+    for _ in range(n):
+        qkv_append(ctx, geo, cache, 0, q, k, v, pos, seq, rope, qn, qn, q_out=qo)
+        attn_decode(ctx, geo, cache, 0, qo, npos, Lc, out=o)
+    torch.cuda.synchronize()
+    ctx.sync()
+    ctx.close()
+    return {"profile_attn": True, "launches": n, "ctx": Lc, "nseq": nseq}
 
 
 # ------------------------------------------------------------------------------------------ TP decode (config 4)
@@ -569,6 +704,9 @@ def run_ours(args, world, rank, local):
         for _ in range(3):
             g_warm.replay()
     barrier()
+    with torch.cuda.stream(stream):
+        g_main.replay()                             # first replay of a graph uploads it: untimed
+    barrier()
     clocks = Clocks(local)
     with clocks:
         with torch.cuda.stream(stream):
@@ -630,6 +768,10 @@ def run_ours(args, world, rank, local):
                                   "prefill_tok_s_per_gpu": r["prefill_tok_s"], "hbm_gbs_per_gpu": r["hbm_gbs"],
                                   "step_bytes_per_gpu": r["step_bytes"]}
 
+    gemm = None
+    if not args.no_decode:
+        barrier()
+        gemm = gemm_bench(local)
     tp = {}
     if not args.no_decode and not args.no_tp:
         torch.cuda.empty_cache()
@@ -655,7 +797,7 @@ def run_ours(args, world, rank, local):
                        "rows": ROWS,
                        "cols": COLS, "weight_copies": NCOPY, "seed": SEED, "parallelism": f"replicas{world}",
                        "l2": f"inputs larger than L2: {NCOPY} rotating weight copies ({NCOPY * W_BYTES / 1e6:.0f} MB)",
-                       "algorithmic_bytes_per_step": ALGO_BYTES, "graph": "CUDA graph of all timed steps, PDL edges"},
+                       "algorithmic_bytes_per_step": ALGO_BYTES, "graph": "CUDA graph of all timed steps, PDL edges, replayed once untimed before the timed replay"},
             "e2e": {"value": round(ALGO_BYTES * e_steps * world / (e_ms / 1e3) / 1e9, 2), "unit": UNIT,
                     "h2d_bytes_per_step": COLS * 4, "d2h_bytes_per_step": ROWS * 4,
                     "steps": e_steps, "api": "zllm_matvec (host buffers, pinned)"},
@@ -678,6 +820,21 @@ def run_ours(args, world, rank, local):
                               "kv": f"f16, ctx {DEC_CTX}", "prompt": DEC_PROMPT, "steps": DEC_STEPS,
                               "api": "zllm_model_generate (greedy, argmax fed back on the device)",
                               "scaling": "weak (one model replica and its sequences per GPU)", **decode}
+        if gemm:
+            parts, fl, us = gemm
+            useful = fl / us / 1e6
+            pk, pk_kind = measured_tensor_peak()
+            line["prefill_gemm"] = {
+                "metric": "prefill GEMM mix TFLOP/s (config 1)", "unit": "TFLOP/s", "tokens": GEMM_TOKENS,
+                "model": "one Qwen3-8B layer: Q4_K q/k/v/o/gate/up, Q6_K down", "api": "zllm_mm (512 tokens)",
+                "kernel": "gemm_kq_kernel: tcgen05.mma kind::f16, f32 accumulation in TMEM, weights dequantized into "
+                          "f16 hi/lo tiles in shared memory, activations as f16 hi/lo tiles",
+                "value": round(useful, 1),
+                "roofline": {"bound": "tensor", "achieved": round(useful, 1), "peak": pk, "unit": "TFLOP/s",
+                             "frac": round(useful / pk, 4), "peak_source": pk_kind,
+                             "executed_tflops": round(3 * useful, 1),
+                             "note": "three MMAs (hi.hi, hi.lo, lo.hi) per useful one keep ~1e-5 of the exact result"},
+                "mix_us": round(us, 1), "per_matrix": parts}
         if tp:
             line["tp_decode"] = {"metric": "32B Q4_K_M tensor-parallel decode tok/s (config 4)", "unit": "tok/s",
                                  "model": "Qwen3-32B shapes, random init: Q4_K + Q6_K ffn_down, f16 output head (replicated)",
@@ -703,6 +860,10 @@ def main():
     ap.add_argument("--profile", action="store_true", help="plain launches without graphs or timing, for ncu")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode, attention and 32B TP measurements")
     ap.add_argument("--no-tp", action="store_true", help="skip the 32B tensor-parallel decode measurement")
+    ap.add_argument("--profile-gemm", action="store_true",
+                    help="plain launches (for ncu): prep + GEMM of the config-1 attn_q matrix, 512 tokens, warm-up + steps")
+    ap.add_argument("--profile-attn", type=int, nargs=2, default=None, metavar=("CTX", "NSEQ"),
+                    help="plain launches (for ncu): config-2 append + attention at CTX positions and NSEQ sequences")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="NSEQ",
                     help="only the 8B decode at NSEQ sequences, 2 steps inside an NVTX range 'decode' (for ncu)")
     args = ap.parse_args()
@@ -712,6 +873,11 @@ def main():
         import torch
         torch.cuda.set_device(local)
         print(json.dumps({"profile_decode": decode_bench(args.profile_decode, local, profile=True)}))
+        return
+    if args.profile_gemm or args.profile_attn:
+        import torch
+        torch.cuda.set_device(local)
+        print(json.dumps(profile_run(args, local)))
         return
     try:
         if args.impl == "reference":
