@@ -90,11 +90,12 @@ int zllm_quantize_act(zllm_ctx *ctx, const float *x, int64_t k, int ntok, int8_t
  * Replaces the per-type kernels matvec_* / mm_* (src/compute/wasm/kernels.js:30-240,
  * src/compute/wasm/kquant-kernels.js:337-504) and the dispatch in src/compute/worker.js:251-270.
  * y_add == y gives the in-place residual add of worker.js:346 / :432.
- * 16 or more tokens on a k-quant W run the tensor-core GEMM (weights and the quantized activation
- * each rounded once to f16, f32 accumulation: within 1e-3 of the reference, not bit-identical to
- * the per-token path); 1..15 tokens keep the exact per-token arithmetic, so batches below 16
- * reproduce single tokens bit for bit (test/kquant-kernels.test.js:65-97).  The GEMM's activation
- * tiles live in a context scratch buffer that grows on demand (a cudaMalloc on first use). */
+ * 64 or more tokens on a k-quant W run the tensor-core GEMM (weights and the quantized activation
+ * each split into an f16 hi/lo pair, three MMAs, f32 accumulation: within ~1e-5 of the largest
+ * output of the per-token arithmetic, not bit-identical to it); 1..63 tokens keep the per-token
+ * arithmetic, so batches below 64 reproduce single tokens bit for bit
+ * (test/kquant-kernels.test.js:65-97).  The GEMM's activation tiles live in a context scratch
+ * buffer that grows on demand (a cudaMalloc on first use). */
 int zllm_mm(zllm_ctx *ctx, const zllm_weight *w, const int8_t *xq, const float *xd, const int32_t *xs, const float *x,
             int ntok, float *y, int64_t y_stride, const float *y_add, void *stream);
 

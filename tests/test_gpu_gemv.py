@@ -1,8 +1,9 @@
 """GPU parity of activation quantization and the decode GEMVs against the CPU oracle.
 
-Contract: every matmul output within max|d| / max|ref| <= 1e-3 of the oracle.  The quantized
-types compute each per-block term with the oracle's own double arithmetic, so they are held to
-a much tighter bar here (1e-6, and >= 99% of outputs bit-identical); quantization is bit-exact.
+Contract: every matmul output within max|d| / max|ref| <= 1e-3 of the oracle.  The k-quant
+GEMVs compute their block terms in f32 on exact integer dots and are held to a much tighter bar
+here (5e-6); the legacy quants Q8_0 / Q4_0 / Q5_0 keep the oracle's double arithmetic (1e-6, and
+>= 99% of outputs bit-identical); quantization is bit-exact.
 """
 import numpy as np
 import pytest
@@ -63,7 +64,9 @@ def test_matvec_matches_oracle(ctx, t, rows, cols):
     assert np.isfinite(got).all(), np.argwhere(~np.isfinite(got))[:10]
     rel = _rel(got, want)
     assert rel <= 1e-3
-    if t in ggml.QUANTIZED:
+    if t in (ggml.Q4_K, ggml.Q5_K, ggml.Q6_K):
+        assert rel <= 5e-6, rel
+    elif t in ggml.QUANTIZED:
         assert rel <= 1e-6, rel
         assert np.mean(got == want) >= 0.99
     else:
@@ -86,7 +89,7 @@ def test_extreme_blocks_match_oracle(ctx, name):
     fin = np.isfinite(want)
     assert np.array_equal(np.isinf(got), np.isinf(want))
     if fin.any():
-        assert _rel(got[fin], want[fin]) <= (1e-6 if t in ggml.QUANTIZED else 1e-5)
+        assert _rel(got[fin], want[fin]) <= (5e-6 if t in ggml.QUANTIZED else 1e-5)
 
 
 def test_batched_equals_per_token_and_residual(ctx):
@@ -111,23 +114,23 @@ KQ = [(ggml.Q4_K, 4096, 4096), (ggml.Q5_K, 520, 2048), (ggml.Q6_K, 700, 12288), 
 
 @pytest.mark.parametrize("t,rows,cols", KQ, ids=[f"{ggml.type_name(t)}-{r}x{c}" for t, r, c in KQ])
 def test_kquant_batches_bit_identical_to_single_tokens(ctx, t, rows, cols):
-    """The tensor-core GEMV adds each token's block terms in an order fixed by the matrix shape: a
-    token's outputs are the same bits alone (block-diagonal MMA) or in a batch of 2..8 (token MMA),
-    and batches of 9..15 run in groups of 8.  From 16 tokens the f16 tensor-core GEMM takes over
-    (within 1e-3, tests/test_gpu_gemm.py)."""
+    """The tensor-core GEMVs add each token's block terms with one formula in an order fixed by the
+    matrix shape: a token's outputs are the same bits alone (block-diagonal MMA) or in a batch
+    (token MMA, 8 or 16 tokens per launch, more in launches of 16).  From 64 tokens the tcgen05
+    GEMM takes over (within 1e-3, tests/test_gpu_gemm.py)."""
     rng = np.random.default_rng(rows + cols + t)
     wt = synth.tensor(t, rows, cols, rng, "bench")
     w = Weight.from_tensor(ctx, wt)
-    X = rng.standard_normal((17, cols)).astype(np.float32)
+    X = rng.standard_normal((40, cols)).astype(np.float32)
     X[3] *= 1e-3
-    singles = np.stack([matvec(w, Act(ctx, X[i])).cpu().numpy().ravel() for i in range(17)])
-    for n in (2, 5, 8, 15):
+    singles = np.stack([matvec(w, Act(ctx, X[i])).cpu().numpy().ravel() for i in range(40)])
+    for n in (2, 5, 8, 9, 15, 16, 17, 33, 40):
         Y = matvec(w, Act(ctx, X[:n])).cpu().numpy()
         ctx.sync()
         assert np.array_equal(Y, singles[:n]), (n, np.argwhere(Y != singles[:n])[:5])
-    for i in (0, 3, 16):
+    for i in (0, 3, 16, 39):
         want = O.matvec(t, wt["data"], rows, cols, X[i], nthreads=8)
-        assert _rel(singles[i], want) <= 1e-6
+        assert _rel(singles[i], want) <= 5e-6
 
 
 @pytest.mark.parametrize("t", [ggml.Q4_K, ggml.Q5_K, ggml.Q6_K])

@@ -195,3 +195,23 @@ def test_long_prefill_gemm_tracks_oracle():
         _close(allrows[i], ref.forward(t))
     _close(gpu.forward(5).copy(), ref.forward(5))
     gpu.close()
+
+
+def test_batched_logits_head_gemm_matches_single_tokens():
+    """With 16 or more logit rows the F16 output head runs on the tensor-core GEMM (f32 hidden
+    state split into f16 hi / lo, f32 accumulation).  Below 64 tokens the layers keep the
+    per-token arithmetic, so the rows of a 20-token pass differ from token-by-token logits only
+    by the head's rounding: within 1e-5 of the largest logit, same argmax where the margin is clear."""
+    cfg, w = tiny("q4_k_m", seed=12)
+    toks = [(11 * i + 5) % cfg["vocab"] for i in range(20)]
+    a = CudaModel.create(cfg, w, ctx=64, kv="f16", max_batch=32, logits_batch=32)
+    b = CudaModel.create(cfg, w, ctx=64, kv="f16")
+    rows = a.forwardBatch(toks, logits="all").copy()
+    for i, t in enumerate(toks):
+        want = b.forward(t).copy()
+        assert float(np.abs(rows[i] - want).max()) <= 1e-5 * float(np.abs(want).max())
+        s = np.sort(want)
+        if s[-1] - s[-2] > 1e-4 * abs(s[-1]):
+            assert int(np.argmax(rows[i])) == int(np.argmax(want))
+    a.close()
+    b.close()

@@ -231,7 +231,7 @@ extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, cons
   cudaStream_t st = pick(c, stream);
   if (ntok >= kGemmMinTokens && xq && (uintptr_t)xq % 8 == 0 && kq_type(w->m.type) &&
       zllm_weight_gemm_ok(c, const_cast<zllm_weight *>(w))) {
-    // 16 or more tokens: the tensor-core GEMM on f16 tiles of the activation
+    // kGemmMinTokens or more tokens: the tensor-core GEMM on f16 tiles of the activation
     void *bbuf = nullptr;
     int rc = zllm_scratch(c, 14, gemm_b_bytes(w->m.cols, ntok), &bbuf);
     if (rc) return rc;

@@ -2,7 +2,7 @@
 //
 // Replaces the reference's batched k-quant kernels mm_q4_k / mm_q5_k / mm_q6_k
 // (src/compute/wasm/kquant-kernels.js:337-504, dispatched by src/compute/worker.js:251-270) for
-// passes of 16 or more tokens.  y[t][r] = (y_add) + sum_k W[r][k] * X[t][k], where W is the k-quant
+// passes of 64 or more tokens.  y[t][r] = (y_add) + sum_k W[r][k] * X[t][k], where W is the k-quant
 // matrix and X the quantized activation (quantizeAct, ref-kernels.js:44-62).  Expanding the
 // reference's block terms, xd * (d*sc*lo - dmin*mn*xs) summed over a row's sub-blocks is exactly
 // sum_k (d*sc*q_k - dmin*mn) * (xd * xq_k): the dequantized weight (quant.js:150, :194-197) times the
@@ -113,7 +113,10 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          | ((uint64_t)2 << 61);                  // 128-byte swizzle
 }
 // Instruction descriptor of kind::f16: f16 A and B, f32 D, both K-major, M x N.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(GN >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
+// instruction descriptor of kind::f16 with f32 accumulation, M = GM; N (a multiple of 16, at most
+// GN) goes in bits 17..22 as N / 8
+constexpr uint32_t kIdescM = (1u << 4) | ((uint32_t)(GM >> 4) << 24);
+__device__ __forceinline__ uint32_t idesc_n(int n) { return kIdescM | ((uint32_t)(n >> 3) << 17); }
 
 // byte offset of element (row, k) of a [rows][64] f16 tile in the 128-byte-swizzled layout
 __host__ __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
@@ -311,8 +314,13 @@ template <> struct Dq<T_Q6_K> {
   }
 };
 
+// FMT: a k-quant type (units dequantized in the kernel, three MMAs per slice: hi*hi, hi*lo, lo*hi);
+// 0 -- A already tiled f16, one MMA (A * B hi); T_F16 (1) -- A already tiled f16 against an f32
+// activation split into B hi / lo, two MMAs.
+template <int FMT> constexpr bool a_tiled() { return FMT == 0 || FMT == T_F16; }
+
 struct GemmArgs {
-  const uint8_t *w;       // k-quant units of the matrix; or (FMT 0) A tiles [m_tile][K/64][128][64] f16
+  const uint8_t *w;       // k-quant units of the matrix; or (a_tiled) A tiles [m_tile][K/64][128][64] f16
   const uint8_t *b;       // activation tiles [n_tile][K/64][hi, lo][128][64] f16, 128-byte swizzled
   const float *bscale;    // [n_tiles * 128] per-token multiplier of the accumulators
   float wscale, wscale_inv;   // power of two applied to the dequantized weights, and its inverse
@@ -325,10 +333,11 @@ struct GemmArgs {
   unsigned *status;
 };
 
-// FMT 0: A already tiled f16 (the f16 x f16 entry point, one MMA per slice); else a k-quant type.
+// A CTA computes a 128-row x 128-token tile; its MMAs use N = the tile's tokens rounded up to 16,
+// and the producers copy only those rows of the activation tiles.
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) {
-  constexpr int US = FMT == 0 ? 0 : FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360;
+  constexpr int US = a_tiled<FMT>() ? 0 : FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);   // swizzle atoms need 1024
   uint8_t *a_ring = smem, *b_ring = smem + kAStages * kPairBytes;
@@ -351,11 +360,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
   // each M tile walks K from its own starting super-block, so the CTAs of one token tile do not all
   // ask for the same activation tile at once (the per-output order depends on the tile only)
   const int koff_sb = p.nb > 0 ? (m_tile * 7) % p.nb : 0;
-  const int koff = FMT == 0 ? (m_tile * 28) % nks : 4 * koff_sb;
+  const int koff = a_tiled<FMT>() ? (m_tile * 28) % nks : 4 * koff_sb;
+  const int ntok_tile = min(GN, p.ntok - n_tile * GN);
+  const int nmma = (ntok_tile + 15) / 16 * 16;          // MMA N: the tile's tokens, rounded up to 16
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAStages; s++) {
-      mbar_init(&full_a[s], FMT == 0 ? kProdWarps * 32 : kDqWarps);
+      mbar_init(&full_a[s], a_tiled<FMT>() ? kProdWarps * 32 : kDqWarps);
       mbar_init(&empty_a[s], 1);
     }
     for (int s = 0; s < kBStages; s++) {
@@ -373,20 +384,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
   const uint32_t tmem = *tmem_slot;
 
   if (warp < kProdWarps) {
-    // ---- activation producers: warp pw copies quarter pw of each stage's B hi / lo (and, FMT 0,
-    // of the A tile) with 16-byte cp.async; the stage's barrier counts every lane's completion
+    // ---- activation producers: the 128 producer threads copy the stage's first nmma rows of B hi
+    // and lo (and, a_tiled, a quarter of the A tile per warp) with 16-byte cp.async; the stage's
+    // barrier counts every lane's completion
     const int pw = warp;
+    const int bchunks = nmma * 128 / 16;                // 16-byte chunks of one part's rows [0, nmma)
     for (int k = 0; k < nks; k++) {
       const int s = k % kBStages;
       if (k >= kBStages && !waitw(&empty_b[s], (uint32_t)(k / kBStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
       const int kd = (k + koff) % nks;
-      constexpr int QB = 2 * kTileBytes / kProdWarps;   // bytes of B hi + lo per producer warp
-      const uint8_t *src = p.b + ((int64_t)n_tile * nks + kd) * 2 * kTileBytes + pw * QB;
-      const uint32_t dst = smem_u32(b_hi(s)) + pw * QB;
+      const uint8_t *src = p.b + ((int64_t)n_tile * nks + kd) * 2 * kTileBytes;
+      const uint32_t dst = smem_u32(b_hi(s));
+#pragma unroll
+      for (int part = 0; part < 2; part++) {          // bchunks is a multiple of the 128 producer threads
 #pragma unroll 4
-      for (int q = lane; q < QB / 16; q += 32) cp_async16(dst + q * 16, src + q * 16);
+        for (int q = threadIdx.x; q < bchunks; q += kProdWarps * 32)
+          cp_async16(dst + part * kTileBytes + q * 16, src + part * kTileBytes + q * 16);
+      }
       cp_async_arrive(&full_b[s]);
-      if constexpr (FMT == 0) {
+      if constexpr (a_tiled<FMT>()) {
         // the A tile rides with the B stage: FMT 0 keeps k % kAStages == k % kBStages by waiting
         // on the A ring's own barrier first
         const int sa = k % kAStages;
@@ -403,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
   } else if (warp == kMmaWarp) {
     // ---- MMA issuer
     if (lane == 0) {
+      const uint32_t idesc = idesc_n(nmma);
       int issued = 0;
       for (int k = 0; k < nks; k++) {
         const int sb = k % kBStages, sa = k % kAStages;
@@ -415,11 +432,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
 #pragma unroll
         for (int kk = 0; kk < GK / 16; kk++) {
           const uint32_t o = kk * 32;
-          mma_f16(tmem, sw128_desc(ah + o), sw128_desc(bh + o), kIdesc, (k | kk) != 0);
-          if constexpr (FMT != 0) {
-            mma_f16(tmem, sw128_desc(ah + o), sw128_desc(bl + o), kIdesc, 1u);
-            mma_f16(tmem, sw128_desc(al + o), sw128_desc(bh + o), kIdesc, 1u);
-          }
+          mma_f16(tmem, sw128_desc(ah + o), sw128_desc(bh + o), idesc, (k | kk) != 0);
+          if constexpr (FMT != 0) mma_f16(tmem, sw128_desc(ah + o), sw128_desc(bl + o), idesc, 1u);
+          if constexpr (!a_tiled<FMT>()) mma_f16(tmem, sw128_desc(al + o), sw128_desc(bh + o), idesc, 1u);
         }
         mma_commit(&empty_a[sa]);                       // the stages are free once these MMAs finish
         mma_commit(&empty_b[sb]);
@@ -433,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
   } else {
     // ---- dequantizing warps (FMT != 0), then the epilogue
     const int dw = warp - kDqWarp0;
-    if constexpr (FMT != 0) {
+    if constexpr (!a_tiled<FMT>()) {
       // warp dw owns unit dw of the tile (rows 16 dw ..): lane -> row m = (lane & 7) + 8 (lane >> 4)
       // and half tp = (lane >> 3) & 1, so each 8-lane quarter stores 8 rows' runs of one column of
       // 16-byte chunks -- 8 distinct swizzled chunks, no bank conflict
@@ -487,6 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
 #pragma unroll 1
       for (int cc = 0; cc < GN / 64; cc++) {
         const int col0 = half * (GN / 2) + cc * 32;
+        if (col0 >= ntok_tile) break;                  // uniform: no token in these columns
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0, v);
         if (p.swiglu) {
@@ -565,14 +581,52 @@ __global__ void gemm_bfill_kernel(const int8_t *xq, const float *xd, int64_t k, 
     *reinterpret_cast<uint4 *>(base + kTileBytes) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
-// Tiles of a plain f16 matrix [rows][k] (row-major), rows past the end 0: `parts` 1 gives A tiles
-// [m_tile][K/64][128][64]; 2 gives B tiles [n_tile][K/64][hi, lo][128][64] with lo = 0.
-__global__ void gemm_tile_f16_kernel(const uint16_t *a, int64_t rows, int64_t k, int64_t mpad, int parts, uint8_t *at) {
+// f32 activations x [ntok][ldx] (the output head's normalized hidden state): per token the power of
+// two with every |x| * 2^-e below 2^15, then tiles of hi = f16(x * 2^-e), lo = f16(x * 2^-e - hi).
+__global__ void gemm_bscale_f32_kernel(const float *x, int64_t ldx, int64_t k, int ntok, int npad, float *bscale) {
+  const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (warp >= npad) return;
+  float amax = 0.f;
+  if (warp < ntok)
+    for (int64_t i = lane; i < k; i += 32) amax = fmaxf(amax, fabsf(x[(int64_t)warp * ldx + i]));
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  float s = 1.f;
+  if (amax > 0.f && amax < 3.0e38f) s = exp2f((float)(ilogbf(amax) - 14));
+  if (lane == 0) bscale[warp] = s;
+}
+__global__ void gemm_bfill_f32_kernel(const float *x, int64_t ldx, int64_t k, int ntok, int npad, const float *bscale,
+                                      uint8_t *bt) {
+  const int64_t groups = k / 8, total = (int64_t)npad * groups;
+  const int kc = (int)(k / 64);
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int n = (int)(e / groups);
+    const int64_t k0 = (e % groups) * 8;
+    uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+    if (n < ntok) {
+      const float inv = 1.f / bscale[n];                 // exact: a power of two
+      const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)n * ldx + k0);
+      const float4 a = src[0], b = src[1];
+      split2(a.x * inv, a.y * inv, h[0], l[0]);
+      split2(a.z * inv, a.w * inv, h[1], l[1]);
+      split2(b.x * inv, b.y * inv, h[2], l[2]);
+      split2(b.z * inv, b.w * inv, h[3], l[3]);
+    }
+    const int nt = n / GN, nr = n % GN, c = (int)(k0 / 64), kk = (int)(k0 % 64);
+    uint8_t *base = bt + ((int64_t)nt * kc + c) * 2 * kTileBytes + sw128_off(nr, kk);
+    *reinterpret_cast<uint4 *>(base) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4 *>(base + kTileBytes) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+// Tiles of a plain f16 matrix [rows][k] (row-major, lda elements between rows), rows past the end 0:
+// `parts` 1 gives A tiles [m_tile][K/64][128][64]; 2 gives B tiles [n_tile][K/64][hi, lo][128][64]
+// with lo = 0.
+__global__ void gemm_tile_f16_kernel(const uint16_t *a, int64_t lda, int64_t rows, int64_t k, int64_t mpad, int parts,
+                                     uint8_t *at) {
   const int64_t groups = k / 8, total = mpad * groups;
   const int kc = (int)(k / 64);
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = e / groups, k0 = (e % groups) * 8;
-    const uint4 v = r < rows ? *reinterpret_cast<const uint4 *>(a + r * k + k0) : make_uint4(0, 0, 0, 0);
+    const uint4 v = r < rows ? *reinterpret_cast<const uint4 *>(a + r * lda + k0) : make_uint4(0, 0, 0, 0);
     const int64_t mt = r / GM;
     uint8_t *base = at + (mt * kc + k0 / 64) * parts * kTileBytes + sw128_off((int)(r % GM), (int)(k0 % 64));
     *reinterpret_cast<uint4 *>(base) = v;
@@ -702,10 +756,10 @@ cudaError_t launch_gemm_f16(const uint16_t *A, const uint16_t *B, int64_t m, int
   const int threads = 256;
   int64_t tot = mpad * (k / 8);
   gemm_tile_f16_kernel<<<(unsigned)((tot + threads - 1) / threads < 4096 ? (tot + threads - 1) / threads : 4096), threads, 0, s>>>(
-      A, m, k, mpad, 1, at);
+      A, k, m, k, mpad, 1, at);
   tot = npad * (k / 8);
   gemm_tile_f16_kernel<<<(unsigned)((tot + threads - 1) / threads < 4096 ? (tot + threads - 1) / threads : 4096), threads, 0, s>>>(
-      B, n, k, npad, 2, bt);
+      B, k, n, k, npad, 2, bt);
   fill_f32_kernel<<<(unsigned)((npad + 255) / 256), 256, 0, s>>>(bscale, npad, 1.f);   // unit scales
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -714,6 +768,47 @@ cudaError_t launch_gemm_f16(const uint16_t *A, const uint16_t *B, int64_t m, int
   a.wscale = 1.f; a.wscale_inv = 1.f;
   a.nb = (int)(k / 256); a.kc = (int)(k / 64); a.status = status;
   return launch_t<0>(a, dim3((unsigned)(mpad / GM), (unsigned)(npad / GN)), kSmem, s);
+}
+
+
+size_t gemm_f16_tiles_bytes(int64_t rows, int64_t k) { return (size_t)((rows + GM - 1) / GM * GM) * (size_t)k * 2; }
+
+cudaError_t launch_gemm_tile_f16(const DevMatrix &m, void *tiles, cudaStream_t s) {
+  if (m.type != T_F16 || m.cols % 64 || m.row_stride % 2) return cudaErrorInvalidValue;
+  const int64_t mpad = (m.rows + GM - 1) / GM * GM, tot = mpad * (m.cols / 8);
+  const int threads = 256;
+  gemm_tile_f16_kernel<<<(unsigned)((tot + threads - 1) / threads < 8192 ? (tot + threads - 1) / threads : 8192), threads, 0, s>>>(
+      reinterpret_cast<const uint16_t *>(m.data), m.row_stride / 2, m.rows, m.cols, mpad, 1, reinterpret_cast<uint8_t *>(tiles));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_prep_f32(const float *x, int64_t ldx, int64_t k, int ntok, void *bbuf, cudaStream_t s) {
+  if (k % 64 || ldx % 4 || (uintptr_t)x % 16) return cudaErrorInvalidValue;
+  const int64_t npad = gemm_tokens_pad(ntok);
+  uint8_t *bt = reinterpret_cast<uint8_t *>(bbuf);
+  float *bscale = reinterpret_cast<float *>(bt + npad * k * 4);
+  const int threads = 256;
+  gemm_bscale_f32_kernel<<<(unsigned)((npad * 32 + threads - 1) / threads), threads, 0, s>>>(x, ldx, k, ntok, (int)npad, bscale);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int64_t total = npad * (k / 8);
+  const int64_t grid = (total + threads - 1) / threads < 148 * 16 ? (total + threads - 1) / threads : 148 * 16;
+  gemm_bfill_f32_kernel<<<(unsigned)grid, threads, 0, s>>>(x, ldx, k, ntok, (int)npad, bscale, bt);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_f16_tiled(const void *tiles, int64_t rows, int64_t k, const void *bbuf, int ntok, float *y,
+                                  int64_t y_stride, unsigned *status, cudaStream_t s) {
+  if (k % 64 || ntok < 1) return cudaErrorInvalidValue;
+  const int64_t mpad = (rows + GM - 1) / GM * GM, npad = gemm_tokens_pad(ntok);
+  GemmArgs a{};
+  a.w = reinterpret_cast<const uint8_t *>(tiles);
+  a.b = reinterpret_cast<const uint8_t *>(bbuf);
+  a.bscale = reinterpret_cast<const float *>(a.b + npad * k * 4);
+  a.y = y; a.y_stride = y_stride; a.rows = rows; a.ntok = ntok;
+  a.wscale = 1.f; a.wscale_inv = 1.f;
+  a.nb = (int)(k / 256); a.kc = (int)(k / 64); a.status = status;
+  return launch_t<T_F16>(a, dim3((unsigned)(mpad / GM), (unsigned)(npad / GN)), kSmem, s);
 }
 
 }  // namespace zllm

@@ -6,29 +6,30 @@
 // (src/compute/wasm/kquant-kernels.js:337-504), dispatched by ggml type as in
 // src/compute/worker.js:184-197 / :251-270.
 //
-// What a launch computes, for 1..8 tokens:  y[t][r] = (y_add) + sum over blocks of
+// What a launch computes, for each token t and row r:  y[t][r] = (y_add) + sum over blocks of
 //   Q4_K / Q5_K:  xd * (d*sc*lo - dmin*mn*xs)       per 32-value sub-block (ref-kernels.js:235-236)
 //   Q6_K:         xd * d * scale * gsum             per 16-value group     (ref-kernels.js:271)
 // where lo / gsum are exact integer dot products of the weight quants with the int8 activation.
 //
 // The weights are stored as units of (16-row tile, super-block) (kq_layout.h); a CTA owns a
-// contiguous range of tiles, i.e. one contiguous range of HBM.  The integer dots are warp-level
-// MMAs (mma.sync m16n8k32 / m16n8k16, uint8 or int8 x int8 -> int32, exact) on a unit:
+// contiguous range of tiles.  The integer dots are warp-level MMAs (mma.sync m16n8k32 / m16n8k16,
+// uint8 or int8 x int8 -> int32, exact) on a unit, whose A operand is the unit itself:
 //   * one token (kq_stream_kernel): the B operand is block-diagonal -- column j carries the
 //     activation of sub-block (group) j and is zero elsewhere -- so the 8 MMAs of a unit leave the
-//     16 rows x 8 sub-blocks of integer dots in one accumulator, one value per lane and row pair.
-//     Every warp streams its share of the CTA's units straight from HBM into registers (coalesced
-//     16-byte loads, a few units in flight), with no shared-memory staging of the weights;
-//   * 2..8 tokens (kq_tok_kernel): B column j carries token j, one MMA per sub-block (group); runs
-//     of units are staged in shared memory by 1D bulk copies (one per stage, completion on an
-//     mbarrier) and shared by the 8 warps.
-// Each integer dot becomes its block term in IEEE double with the reference's operations and
-// rounding (no fused multiply-add where the JS rounds twice), so every block term is bit-identical
-// to the oracle's.  Only the order of the final double additions differs from the reference, and
-// it is fixed: each super-block's terms are added as a pairwise tree (Q4_K / Q5_K:
-// ((T0 + T1) + (T2 + T3)) + ((T4 + T5) + (T6 + T7)); Q6_K: the same over groups 0..7 plus the same
-// over 8..15) and the super-block sums are added in super-block order.  That order depends on
-// nothing but the row, so a token gets the same bits alone, in a batch, or in any launch shape.
+//     16 rows x 8 sub-blocks of integer dots in one accumulator.  Every warp streams its share of
+//     the CTA's units straight from HBM into registers (coalesced 16-byte loads, a few units in
+//     flight), with no shared-memory staging of the weights;
+//   * 2..16 tokens per launch (kq_batch_kernel): B column j carries token j, one MMA per sub-block
+//     (group) and group of 8 tokens.  The CTA's units are walked super-block by super-block, so a
+//     warp loads a super-block's activation fragments once and reuses them for every tile.
+// Block terms are f32 with a fixed formula shared by both kernels (k45_pair / q6_pair below); an
+// integer dot leaves the MMA already biased by 1.5 * 2^23 (the accumulator starts there), so one
+// subtraction turns it into the exact float.  The order of the additions is fixed as well: each
+// super-block's terms are added as a pairwise tree (Q4_K / Q5_K: ((P0 + P1) + (P2 + P3)) over the
+// sub-block pairs; Q6_K: the same over the group pairs of each 128-value half, then half 0 + half
+// 1), and the super-block sums are added in super-block order.  That order depends on nothing but
+// the row, so a token gets the same bits alone, in a batch, or in any launch shape.  Against the
+// oracle's double arithmetic the outputs differ by f32 rounding only (max|d| / max|y| ~ 1e-6).
 // A one-token launch may take the f32 activation (optionally RMSNorm-ed first) and quantize it
 // itself, bit-exact with quantize_act_kernel, so a lone matvec is one kernel.
 #include "common.cuh"
@@ -40,7 +41,7 @@ namespace zllm {
 namespace {
 
 constexpr int kTile = kKqTile;               // rows per unit (the MMA's M)
-constexpr int kMaxTok = 8;                   // tokens per launch of the token kernel (the MMA's N)
+constexpr int kBatchTok = 16;                // tokens per launch of the batch kernel (two MMA N groups)
 
 // unit regions (kq_layout.h)
 template <int FMT> constexpr int unit_bytes() { return FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360; }
@@ -61,7 +62,6 @@ __device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, u
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(b0));
 }
-
 // C += A . B, both int8 (the signed Q6_K quants q - 32 against the activation)
 __device__ __forceinline__ void mma_k16s(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
   asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
@@ -69,43 +69,46 @@ __device__ __forceinline__ void mma_k16s(int (&c)[4], uint32_t a0, uint32_t a1, 
       : "r"(a0), "r"(a1), "r"(b0));
 }
 
-// f16 bits -> double (exact)
-__device__ __forceinline__ double h2d(uint32_t bits16) {
-  double d;
-  asm("cvt.f64.f16 %0, %1;" : "=d"(d) : "h"((unsigned short)bits16));
-  return d;
-}
+// ---------------------------------------------------------------------------- exact int -> f32
+// An int32 accumulator that started at kBias holds kBias + v; for |v| < 2^22 its bits are the float
+// 1.5 * 2^23 + v exactly (a float with unit spacing), so one subtraction yields v.  Every integer dot
+// here is below 2^22 in magnitude (Q5_K: 32 * 31 * 127 = 125,984).
+constexpr int kBias = 0x4B400000;
+constexpr float kBiasF = 12582912.0f;
+__device__ __forceinline__ float biased_f(int acc) { return __fsub_rn(__int_as_float(acc), kBiasF); }
+// small ints (|v| < 2^22) to float on the integer + FMA pipes instead of the conversion pipe
+__device__ __forceinline__ float small_f(int v) { return biased_f(v + kBias); }
 
-// Bounded wait on an mbarrier phase by lane 0 alone (the other lanes would only queue on the same
-// word); the result is broadcast and __syncwarp orders the stage's data for the whole warp.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, int lane) {
-  bool ok = true;
-  if (lane == 0) ok = mbar_wait_lazy(bar, parity);
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok;
-}
-
-__device__ __forceinline__ double dshfl_xor(double v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+__device__ __forceinline__ float fshfl_xor(float v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
 // Sum over the 4 lanes t of a lane quad: ((v0 + v1) + (v2 + v3)) in every lane of the quad.
-__device__ __forceinline__ double quad_tree(double v) {
-  v = __dadd_rn(v, dshfl_xor(v, 1));
-  return __dadd_rn(v, dshfl_xor(v, 2));
+__device__ __forceinline__ float quad_tree(float v) {
+  v = __fadd_rn(v, fshfl_xor(v, 1));
+  return __fadd_rn(v, fshfl_xor(v, 2));
 }
 
 // ---------------------------------------------------------------------------- block terms
-// Q4_K / Q5_K sub-block term xd * (d*sc*lo - dmin*mn*xs).  sc*lo and mn*xs are exact int32, so
-// d*(sc*lo) and dmin*(mn*xs) are the JS products (d*sc)*lo and (dmin*mn)*xs exactly; the fused
-// multiply-add rounds once where the JS subtraction rounds; the product by xd rounds like the JS.
-__device__ __forceinline__ double k45_term(double d, double dmin, int sc, int mn, int lo, int xs, double xd) {
-  const double p = i2d_biased((uint32_t)(sc * lo) + 0x80000000u);
-  const double m = __dmul_rn(dmin, i2d_biased((uint32_t)(mn * xs) + 0x80000000u));
-  return __dmul_rn(xd, __fma_rn(d, p, -m));
+// Scales of one Q4_K / Q5_K row for a sub-block pair (2c, 2c + 1): d*sc and dmin*mn, exact in f32
+// (an f16 times a 6-bit integer).
+struct K45Sc { float ds0, ds1, dm0, dm1; };
+__device__ __forceinline__ K45Sc k45_sc(float d, float dmin, uint32_t F) {
+  K45Sc s;
+  s.ds0 = __fmul_rn(d, small_f((int)(F & 63)));
+  s.ds1 = __fmul_rn(d, small_f((int)((F >> 6) & 63)));
+  s.dm0 = __fmul_rn(dmin, small_f((int)((F >> 12) & 63)));
+  s.dm1 = __fmul_rn(dmin, small_f((int)((F >> 18) & 63)));
+  return s;
 }
-// Q6_K group term xd * d * scale * gsum: xd*d (35 bits) and (xd*d)*scale are exact in double, so the
-// JS left-to-right product equals (xd*d) * (scale*gsum) rounded once.
-__device__ __forceinline__ double q6_term(double xdd, int scale, int gsum) {
-  return __dmul_rn(xdd, i2d_exact(scale * gsum));
+// The pair term T(2c) + T(2c + 1) of one (row, token): with xdm = (xd0, xd1, xd0*xs0, xd1*xs1) of the
+// token's two 32-blocks, xd * (d*sc*lo - dmin*mn*xs) summed over the pair as
+//   fma(xd1*ds1, lo1, fma(xd0*ds0, lo0, -(fma(dm1, xm1, dm0*xm0)))).
+__device__ __forceinline__ float k45_pair(const K45Sc &s, float lo0, float lo1, const float4 &xdm) {
+  const float m = __fmaf_rn(s.dm1, xdm.w, __fmul_rn(s.dm0, xdm.z));
+  return __fmaf_rn(__fmul_rn(xdm.y, s.ds1), lo1, __fmaf_rn(__fmul_rn(xdm.x, s.ds0), lo0, -m));
+}
+// The Q6_K pair term of groups (G, G + 1), which share the 32-block b: (xd_b * d) * (sc_G * g_G +
+// sc_G+1 * g_G+1); the integer combination is exact in f32 (|.| < 2^24).
+__device__ __forceinline__ float q6_pair(float xd, float d, float sc0, float g0, float sc1, float g1) {
+  return __fmul_rn(__fmul_rn(xd, d), __fmaf_rn(sc1, g1, __fmul_rn(sc0, g0)));
 }
 // the 24-bit scale/min field of chunk c from header words 1..3 of a Q4_K / Q5_K block
 __device__ __forceinline__ uint32_t k45_field(const uint4 &h, int c) {
@@ -122,32 +125,15 @@ __device__ __forceinline__ uint32_t q6_unpack(uint32_t w0, uint32_t w1, uint32_t
     default: return ((w1 >> 4) & 0x0f0f0f0fu) | ((h >> 2) & 0x30303030u);
   }
 }
+// int8 scale byte i of a word as float
+__device__ __forceinline__ float sbyte_f(uint32_t w, int i) { return small_f((int)(int8_t)((w >> (8 * i)) & 0xffu)); }
 
-// ---------------------------------------------------------------------------- activation views
-// One-token activation staged in shared memory: xq [K] int8, xd [K/32] f64 (the f32 scales,
-// widened once), xs [K/32] i32, and for Q6_K xs16 [K/16] i32 (sums of the stored int8 per
-// 16-value group).  sel[s] = 1 when the lane's MMA column is s, else 0: the block-diagonal B
-// operand is x * sel[s], a multiply on the FMA pipe instead of a select on the integer pipe.
-struct SAct {
-  uint32_t xq, xd, xs, xs16;    // shared-window addresses
-  uint32_t sel[8];
-};
-// 2..8 tokens, read from global memory
-struct GAct {
-  const int8_t *xq;     // [ntok][k]
-  const float *xd;      // [ntok][k/32]
-  const int32_t *xs;    // [ntok][k/32]
-  int64_t k;
-  int ntok;
-};
-
+// ---------------------------------------------------------------------------- launch arguments
 struct KqArgs {
   const uint8_t *w;     // first unit of the launch's first tile
   int64_t rows;         // rows of the launch (the last tile may be partial)
   int nb;               // super-blocks per row
-  int nchunk;           // token kernel: chunks of super-blocks per tile
-  int nst;              // token kernel: stages in the ring
-  int ntok;             // tokens in this launch (1..8)
+  int ntok;             // tokens in this launch
   const int8_t *xq;     // quantized activation [ntok][k] (one token: may be NULL with x set)
   const float *xd;
   const int32_t *xs;
@@ -159,8 +145,7 @@ struct KqArgs {
   float *y;
   const float *y_add;
   int64_t y_stride;
-  unsigned *status;
-  int x_off, part_off, bar_off;   // shared-memory regions
+  int x_off, part_off;  // shared-memory regions
 };
 
 // tiles [T0, T1) of a CTA: an even split of the launch's tiles
@@ -170,7 +155,7 @@ __device__ __forceinline__ void cta_tiles(int64_t rows, int &T0, int &T1) {
   T1 = (int)((int64_t)(blockIdx.x + 1) * nt / gridDim.x);
 }
 
-// y for output row r (launch-relative) from its f64 total; with swiglu the (gate, up) pair
+// y for output row r (launch-relative) from its f32 total; with swiglu the (gate, up) pair
 // r, r + 1 is written once, by r (src/compute/worker.js:426, ref-kernels.js:322: silu in double,
 // the product rounded to f32)
 __device__ __forceinline__ void store_row(const KqArgs &p, int tok, int64_t r, float out, float up) {
@@ -183,6 +168,34 @@ __device__ __forceinline__ void store_row(const KqArgs &p, int tok, int64_t r, f
     if (p.y_add) out = __fadd_rn(p.y_add[o], out);
     p.y[o] = out;
   }
+}
+
+// ---------------------------------------------------------------------------- one-token activation
+// One token's activation staged in shared memory:
+//   xq   [K] int8;
+//   Q4_K / Q5_K: xdm [K/64] float4 = (xd of 32-blocks 2p, 2p + 1, then xd * xs of the same);
+//   Q6_K:        xd6 [K/256][4] float2 = (xd of 32-blocks t, 4 + t of the super-block) and
+//                moff [K/256][4] float4 = kBiasF + 32 * (sum of the int8 of groups 2t, 2t + 1,
+//                8 + 2t, 9 + 2t): the unsigned-quant dot minus moff is the signed group dot.
+// sel[s] = 1 when the lane's MMA column is s, else 0: the block-diagonal B operand is x * sel[s].
+struct SAct {
+  uint32_t xq, sc0, sc1;    // shared-window addresses: xq, xdm / xd6, moff
+  uint32_t sel[8];
+};
+
+template <int FMT>
+__device__ __forceinline__ void put_block_scales(float *ssc0, int b, float xd, int xs) {
+  if constexpr (FMT == T_Q6_K) {
+    ssc0[((b >> 3) * 4 + (b & 3)) * 2 + ((b >> 2) & 1)] = xd;
+  } else {
+    ssc0[(b >> 1) * 4 + (b & 1)] = xd;
+    ssc0[(b >> 1) * 4 + 2 + (b & 1)] = __fmul_rn(xd, __int2float_rn(xs));
+  }
+}
+// moff of 16-value group G (global index) from the sum of its int8
+__device__ __forceinline__ void put_group_off(float *ssc1, int G, int s16) {
+  const int gg = G & 15;
+  ssc1[((G >> 4) * 4 + ((gg >> 1) & 3)) * 4 + 2 * (gg >> 3) + (gg & 1)] = __fadd_rn(kBiasF, __int2float_rn(32 * s16));
 }
 
 // RMSNorm scale 1 / sqrt(mean(x^2) + eps) of one token, with exactly the reduction of
@@ -209,9 +222,9 @@ __device__ double rms_scale(const float *x, int64_t n, double eps, int warp, int
 // (quantizeAct, src/compute/ref-kernels.js:44-62).  Lane pairs own a 32-value block, 16 values each.
 // With norm_w the values are first f32(x * s * w) with s the RMSNorm scale (ref-kernels.js:305-310),
 // as rmsnorm_quant_kernel writes them.
-template <int NT>
-__device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w, double eps, uint8_t *sxq, double *sxd,
-                                 int32_t *sxs, int32_t *sxs16, int warp, int lane) {
+template <int FMT, int NT>
+__device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w, double eps, uint8_t *sxq, float *ssc0,
+                                 float *ssc1, int warp, int lane) {
   const double rs = norm_w ? rms_scale<NT>(x, k, eps, warp, lane) : 0.0;
   const int nhb = (int)(k / 16);
   for (int base = warp * 32; base < nhb; base += NT) {
@@ -264,268 +277,50 @@ __device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w,
     const bool onan = __shfl_xor_sync(0xffffffffu, (int)nan, 1) != 0;
     if (act) {
       reinterpret_cast<uint4 *>(sxq)[hb] = make_uint4(words[0], words[1], words[2], words[3]);
-      if (sxs16) sxs16[hb] = sum;
-      if ((lane & 1) == 0) {
-        sxd[hb >> 1] = (double)__double2float_rn(scale);
-        sxs[hb >> 1] = (nan || onan) ? 0 : sum + osum;
-      }
+      if constexpr (FMT == T_Q6_K) put_group_off(ssc1, hb, sum);
+      if ((lane & 1) == 0) put_block_scales<FMT>(ssc0, hb >> 1, __double2float_rn(scale), (nan || onan) ? 0 : sum + osum);
     }
   }
 }
 
-// ---------------------------------------------------------------------------- 2..8 tokens
-// One unit in shared memory at `u` (kq_layout.h): lane (g, t) computes rows g and g + 8 for tokens
-// 2t and 2t + 1.  S[e] (e = 2 * row half + token parity) = the super-block sum in the canonical
-// tree order.
-template <bool FIVE>
-__device__ __forceinline__ void sb_k45_tok(uint32_t u, int lane, int g, int t, const GAct &x, int sb, double (&S)[4]) {
-  constexpr int HO = FIVE ? 2560 : 2048;
-  const uint4 hdr[2] = {lds128(u + HO + 16 * g), lds128(u + HO + 16 * (g + 8))};
-  const bool live = g < x.ntok;
-  const uint32_t *xw = reinterpret_cast<const uint32_t *>(x.xq + (live ? g : 0) * x.k + (int64_t)sb * 256);
-  const int t0 = 2 * t < x.ntok ? 2 * t : 0, t1 = 2 * t + 1 < x.ntok ? 2 * t + 1 : 0;   // padding tokens read token 0
-  const float *xd0 = x.xd + t0 * (x.k / 32) + sb * 8, *xd1 = x.xd + t1 * (x.k / 32) + sb * 8;
-  const int32_t *xs0 = x.xs + t0 * (x.k / 32) + sb * 8, *xs1 = x.xs + t1 * (x.k / 32) + sb * 8;
-  double dd[2], dm[2];
-#pragma unroll
-  for (int ri = 0; ri < 2; ri++) { dd[ri] = h2d(hdr[ri].x & 0xffffu); dm[ri] = h2d(hdr[ri].x >> 16); }
-  uint2 eg = make_uint2(0, 0), eh = make_uint2(0, 0);
-  if (FIVE) { eg = lds64(u + kE5 + 8 * lane); eh = lds64(u + kE5 + 256 + 8 * lane); }
-  double q01[4];
-#pragma unroll
-  for (int cp = 0; cp < 2; cp++) {
-    const uint4 wq = lds128(u + (cp * 32 + lane) * 16), vq = lds128(u + ((2 + cp) * 32 + lane) * 16);
-#pragma unroll
-    for (int ci = 0; ci < 2; ci++) {
-      const int c = 2 * cp + ci;
-      const uint32_t wx = ci ? wq.z : wq.x, wy = ci ? wq.w : wq.y, vx = ci ? vq.z : vq.x, vy = ci ? vq.w : vq.y;
-      uint32_t lg0 = wx & 0x0f0f0f0fu, lg1 = wy & 0x0f0f0f0fu, lh0 = vx & 0x0f0f0f0fu, lh1 = vy & 0x0f0f0f0fu;
-      uint32_t ug0, ug1, uh0, uh1;
-      if (FIVE) {
-        lg0 |= ((eg.x >> (2 * c)) & 0x01010101u) << 4; lg1 |= ((eg.y >> (2 * c)) & 0x01010101u) << 4;
-        lh0 |= ((eh.x >> (2 * c)) & 0x01010101u) << 4; lh1 |= ((eh.y >> (2 * c)) & 0x01010101u) << 4;
-        ug0 = ((wx >> 4) & 0x0f0f0f0fu) | (((eg.x >> (2 * c + 1)) & 0x01010101u) << 4);
-        ug1 = ((wy >> 4) & 0x0f0f0f0fu) | (((eg.y >> (2 * c + 1)) & 0x01010101u) << 4);
-        uh0 = ((vx >> 4) & 0x0f0f0f0fu) | (((eh.x >> (2 * c + 1)) & 0x01010101u) << 4);
-        uh1 = ((vy >> 4) & 0x0f0f0f0fu) | (((eh.y >> (2 * c + 1)) & 0x01010101u) << 4);
-      } else {
-        ug0 = wx & 0xf0f0f0f0u; ug1 = wy & 0xf0f0f0f0u; uh0 = vx & 0xf0f0f0f0u; uh1 = vy & 0xf0f0f0f0u;
-      }
-      // token g's activation of sub-blocks 2c (lo) and 2c+1 (hi)
-      const uint32_t xla = live ? __ldg(xw + 16 * c + t) : 0u, xlb = live ? __ldg(xw + 16 * c + 4 + t) : 0u;
-      const uint32_t xua = live ? __ldg(xw + 16 * c + 8 + t) : 0u, xub = live ? __ldg(xw + 16 * c + 12 + t) : 0u;
-      int L[4] = {0, 0, 0, 0}, U[4] = {0, 0, 0, 0};
-      mma_k32(L, lg0, lh0, lg1, lh1, xla, xlb);
-      mma_k32(U, ug0, uh0, ug1, uh1, xua, xub);
-      const float2 d0 = __ldg(reinterpret_cast<const float2 *>(xd0 + 2 * c)), d1 = __ldg(reinterpret_cast<const float2 *>(xd1 + 2 * c));
-      const int2 s0 = __ldg(reinterpret_cast<const int2 *>(xs0 + 2 * c)), s1 = __ldg(reinterpret_cast<const int2 *>(xs1 + 2 * c));
-      const uint32_t F[2] = {k45_field(hdr[0], c), k45_field(hdr[1], c)};
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const int ri = e >> 1, ti = e & 1;
-        const int hi = FIVE ? U[e] : U[e] >> 4;
-        const double xdl = (double)(ti ? d1.x : d0.x), xdu = (double)(ti ? d1.y : d0.y);
-        const int xsl = ti ? s1.x : s0.x, xsu = ti ? s1.y : s0.y;
-        const double P = __dadd_rn(k45_term(dd[ri], dm[ri], F[ri] & 63, (F[ri] >> 12) & 63, L[e], xsl, xdl),
-                                   k45_term(dd[ri], dm[ri], (F[ri] >> 6) & 63, (F[ri] >> 18) & 63, hi, xsu, xdu));
-        // pairwise tree over the four pairs: ((P0 + P1) + (P2 + P3))
-        if (c == 0 || c == 2) q01[e] = P;
-        else if (c == 1) S[e] = __dadd_rn(q01[e], P);
-        else S[e] = __dadd_rn(S[e], __dadd_rn(q01[e], P));
-      }
+// Stage one token's activation in shared memory (quantized here from f32, or copied when the
+// caller quantized it) and return its view.
+template <int FMT, int NT>
+__device__ __forceinline__ SAct stage_token(const KqArgs &p, uint8_t *base, int warp, int lane, int g) {
+  uint8_t *sxq = base;
+  float *ssc0 = reinterpret_cast<float *>(sxq + p.k);
+  float *ssc1 = FMT == T_Q6_K ? ssc0 + p.k / 32 : nullptr;
+  if (p.xq == nullptr) {
+    quantize_to_smem<FMT, NT>(p.x, p.k, p.norm_w, p.norm_eps, sxq, ssc0, ssc1, warp, lane);
+  } else {
+    const uint4 *q4 = reinterpret_cast<const uint4 *>(p.xq);
+    for (int i = threadIdx.x; i < p.k / 16; i += NT) {
+      const uint4 v = __ldg(q4 + i);
+      reinterpret_cast<uint4 *>(sxq)[i] = v;
+      if constexpr (FMT == T_Q6_K)
+        put_group_off(ssc1, i, __dp4a((int)v.x, 0x01010101, __dp4a((int)v.y, 0x01010101,
+                                      __dp4a((int)v.z, 0x01010101, __dp4a((int)v.w, 0x01010101, 0)))));
     }
+    for (int i = threadIdx.x; i < p.k / 32; i += NT) put_block_scales<FMT>(ssc0, i, __ldg(p.xd + i), __ldg(p.xs + i));
   }
+  SAct sa{};
+  sa.xq = smem_u32(sxq); sa.sc0 = smem_u32(ssc0); sa.sc1 = ssc1 ? smem_u32(ssc1) : 0u;
+#pragma unroll
+  for (int i = 0; i < 8; i++) sa.sel[i] = g == i ? 1u : 0u;
+  return sa;
 }
 
-// Q6_K, 2..8 tokens: Sh[e][h] = tree8 of half h, ((P0 + P1) + (P2 + P3)) with P_k the pair of
-// groups 8h + 2k, 8h + 2k + 1 (the pair lane k holds in the one-token path).
-__device__ __forceinline__ void sb_q6_tok(uint32_t u, int lane, int g, int t, const GAct &x, int sb,
-                                          double (&Sh)[4][2]) {
-  const double d[2] = {h2d(lds16(u + kQ6D + 2 * g)), h2d(lds16(u + kQ6D + 2 * (g + 8)))};
-  const uint4 scw[2] = {lds128(u + kQ6S + 16 * g), lds128(u + kQ6S + 16 * (g + 8))};   // the rows' 16 scales
-  const uint4 qhw[2] = {lds128(u + kQ6H + 16 * lane), lds128(u + kQ6H + 512 + 16 * lane)};
-  const bool live = g < x.ntok;
-  const uint32_t *xw = reinterpret_cast<const uint32_t *>(x.xq + (live ? g : 0) * x.k + (int64_t)sb * 256);
-  const int t0 = 2 * t < x.ntok ? 2 * t : 0, t1 = 2 * t + 1 < x.ntok ? 2 * t + 1 : 0;
-  const float *xd0 = x.xd + t0 * (x.k / 32) + sb * 8, *xd1 = x.xd + t1 * (x.k / 32) + sb * 8;
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    // this lane's quants of half h: ql words [u][p], qh words [u] (values 4t..4t+3 of each group)
-    const uint4 lg = lds128(u + (h * 32 + lane) * 16), lh = lds128(u + ((2 + h) * 32 + lane) * 16);
-    const uint32_t gw[4] = {lg.x, lg.y, lg.z, lg.w}, hw[4] = {lh.x, lh.y, lh.z, lh.w};
-    const uint32_t gq[2] = {h ? qhw[0].z : qhw[0].x, h ? qhw[0].w : qhw[0].y};
-    const uint32_t hq[2] = {h ? qhw[1].z : qhw[1].x, h ? qhw[1].w : qhw[1].y};
-    double q[4][2];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      // scales of groups 8h + 2k + uu (reordered table: byte 4k + 2h + uu) and their 32-block's xd
-      const uint32_t swd[2] = {k == 0 ? scw[0].x : k == 1 ? scw[0].y : k == 2 ? scw[0].z : scw[0].w,
-                               k == 0 ? scw[1].x : k == 1 ? scw[1].y : k == 2 ? scw[1].z : scw[1].w};
-      const uint32_t sw[2] = {(swd[0] >> (16 * h)) & 0xffffu, (swd[1] >> (16 * h)) & 0xffffu};
-      const double xdv[2] = {(double)__ldg(xd0 + 4 * h + k), (double)__ldg(xd1 + 4 * h + k)};
-      double P[4];
-#pragma unroll
-      for (int uu = 0; uu < 2; uu++) {
-        // signed quants q - 32 (bytes in [0, 63]: + 96 never carries, then flip the top bit)
-        const uint32_t a0 = (q6_unpack(gw[uu * 2], gw[uu * 2 + 1], gq[uu], k) + 0x60606060u) ^ 0x80808080u;
-        const uint32_t a1 = (q6_unpack(hw[uu * 2], hw[uu * 2 + 1], hq[uu], k) + 0x60606060u) ^ 0x80808080u;
-        const uint32_t xa = live ? __ldg(xw + 4 * (8 * h + 2 * k + uu) + t) : 0u;
-        int Cm[4] = {0, 0, 0, 0};
-        mma_k16s(Cm, a0, a1, xa);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const int ri = e >> 1, ti = e & 1;
-          const int scale = (int)(int8_t)((sw[ri] >> (8 * uu)) & 0xffu);
-          const double T = q6_term(__dmul_rn(xdv[ti], d[ri]), scale, Cm[e]);
-          P[e] = uu == 0 ? T : __dadd_rn(P[e], T);
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        if (k == 0 || k == 2) q[e][k >> 1] = P[e];
-        else q[e][k >> 1] = __dadd_rn(q[e][k >> 1], P[e]);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 4; e++) Sh[e][h] = __dadd_rn(q[e][0], q[e][1]);
-  }
-}
-
-// super-blocks per staged chunk (Q6_K: more bytes and twice the MMAs per super-block)
-template <int FMT> constexpr int chunk_sb() { return FMT == T_Q6_K ? 8 : 16; }
-constexpr int chunk_sb_of(int type) { return type == T_Q6_K ? 8 : 16; }
-constexpr int kTokWarps = 8;
-constexpr int kMaxStages = 8;
-constexpr int64_t kTokBudget = 200 * 1024;   // one CTA per SM (the grid is at most one per SM)
-
-// 2..8 tokens.  A CTA owns tiles [T0, T1) and walks them in chunks of up to kChunk super-blocks:
-// stage s of the ring holds one chunk (one bulk copy of its contiguous units, issued by lane 0 of
-// warp 0, completion on full[s]).  Warp w takes super-blocks w and w + 8 of every chunk; each
-// lane writes its super-block sums to a per-chunk slot array, one CTA barrier (which also carries
-// the bounded waits' give-up flag to every warp) publishes them, and one thread per (row, token)
-// adds them in super-block order while warp 0 refills the freed stage.
-template <int FMT>
-__global__ void __launch_bounds__(kTokWarps * 32, 1) kq_tok_kernel(const KqArgs p) {
-  constexpr int US = unit_bytes<FMT>();
-  constexpr int NTP = kMaxTok, NT = kTokWarps * 32;
-  constexpr int kChunk = chunk_sb<FMT>();
-  constexpr int kSlots = 16;                    // per-chunk slots of super-block sums (Q6_K: 8 x 2 halves)
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int nst = p.nst;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.bar_off);
-  uint8_t *stages = smem;
-  double *part = reinterpret_cast<double *>(smem + p.part_off);    // [2][slot][row][NTP]
-  int T0, T1;
-  cta_tiles(p.rows, T0, T1);
-  const int nunit = (T1 - T0) * p.nchunk;       // this CTA's (tile, chunk) units of work
-  const int stage_bytes = kChunk * US;
-
-  auto issue = [&](int u) {                     // lane 0 of warp 0
-    const int s = u % nst, tile = u / p.nchunk, c = u % p.nchunk;
-    const int sb0 = c * kChunk, nsb = min(kChunk, p.nb - sb0);
-    const uint32_t bytes = (uint32_t)(nsb * US);
-    mbar_arrive_expect_tx(&full[s], bytes);
-    bulk_g2s(stages + (size_t)s * stage_bytes, p.w + ((int64_t)(T0 + tile) * p.nb + sb0) * US, bytes, &full[s]);
-  };
-
-  int issued = 0;                               // units issued so far (tracked by lane 0 of warp 0)
-  if (warp == 0 && lane == 0) {
-    for (int s = 0; s < nst; s++) mbar_init(&full[s], 1);
-    fence_mbar_init();
-    for (; issued < nunit && issued < nst; issued++) issue(issued);
-  }
-  pdl_launch_dependents();
-  __syncthreads();                              // barriers initialised before anyone waits on them
-  pdl_wait();                                   // the activation comes from the previous kernel
-
-  GAct ga{};
-  ga.xq = p.xq; ga.xd = p.xd; ga.xs = p.xs; ga.k = p.k; ga.ntok = p.ntok;
-  const uint32_t sbase = smem_u32(stages);
-  const bool adder = threadIdx.x < kTile * NTP;
-  double tot = 0.0;
-  bool aborted = false;
-  for (int u = 0; u < nunit; u++) {
-    const int s = u % nst, tile = u / p.nchunk, c = u % p.nchunk;
-    // after one give-up the warp waits no more: it only passes the barriers until all stop together
-    const bool ok = !aborted && mbar_wait_warp(&full[s], (uint32_t)(u / nst) & 1u, lane);
-    const int sb0 = c * kChunk, nsb = min(kChunk, p.nb - sb0);
-    double *pu = part + (size_t)(u & 1) * kSlots * kTile * NTP;
-    if (ok) {
-      const uint32_t st = sbase + (uint32_t)(s * stage_bytes);
-#pragma unroll
-      for (int jj = 0; jj < kChunk / kTokWarps; jj++) {
-        const int j = warp + kTokWarps * jj;
-        if (j >= nsb) break;
-        const uint32_t un = st + (uint32_t)(j * US);
-        if constexpr (FMT == T_Q6_K) {
-          double Sh[4][2];
-          sb_q6_tok(un, lane, g, t, ga, sb0 + j, Sh);
-#pragma unroll
-          for (int e = 0; e < 4; e++)
-#pragma unroll
-            for (int h = 0; h < 2; h++)
-              pu[((j + 8 * h) * kTile + g + 8 * (e >> 1)) * NTP + 2 * t + (e & 1)] = Sh[e][h];
-        } else {
-          double S[4];
-          sb_k45_tok<FMT == T_Q5_K>(un, lane, g, t, ga, sb0 + j, S);
-#pragma unroll
-          for (int e = 0; e < 4; e++) pu[(j * kTile + g + 8 * (e >> 1)) * NTP + 2 * t + (e & 1)] = S[e];
-        }
-      }
-    }
-    // every warp is done with stage s and has published its sums
-    if (named_sync_or(1, NT, aborted || !ok)) { aborted = true; break; }
-    if (u + nst < nunit && warp == 0 && lane == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(u + nst);
-      issued = u + nst + 1;
-    }
-    if (adder) {
-      // the chunk's super-block sums in super-block order (Q6_K: half 0 + half 1 first)
-      constexpr int NJ = FMT == T_Q6_K ? 8 : 16;
-      double v[NJ];
-#pragma unroll
-      for (int j = 0; j < NJ; j++)
-        if (j < nsb)
-          v[j] = FMT == T_Q6_K ? __dadd_rn(pu[j * kTile * NTP + threadIdx.x], pu[(j + 8) * kTile * NTP + threadIdx.x])
-                               : pu[j * kTile * NTP + threadIdx.x];
-#pragma unroll
-      for (int j = 0; j < NJ; j++)
-        if (j < nsb) tot = __dadd_rn(tot, v[j]);
-      if (c == p.nchunk - 1) {
-        const int row = threadIdx.x / NTP, tk = threadIdx.x % NTP;
-        const int64_t r = (int64_t)(T0 + tile) * kTile + row;
-        const float out = __double2float_rn(tot);
-        // rows r (gate) and r + 1 (up) are the adders threadIdx.x and threadIdx.x + NTP, in one warp
-        const float up = __shfl_xor_sync(0xffffffffu, out, NTP);
-        if (tk < p.ntok && r < p.rows && (!p.swiglu || (row & 1) == 0)) store_row(p, tk, r, out, up);
-        tot = 0.0;
-      }
-    }
-  }
-  if (aborted) {
-    if (lane == 0) atomicOr(p.status, ST_FULL_TIMEOUT);
-    if (warp == 0 && lane == 0) {
-      // copies still in flight must land before the CTA's shared memory is released
-      const uint64_t drain_deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
-      for (int v = issued - nst > 0 ? issued - nst : 0; v < issued; v++)
-        if (!mbar_wait_bounded(&full[v % nst], (uint32_t)(v / nst) & 1u, drain_deadline))
-          atomicOr(p.status, ST_DRAIN_TIMEOUT);
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------- one token, register streaming
+// ---------------------------------------------------------------------------- unit registers
 // A unit as lane (g, t) needs it: its pieces of rows g and g + 8, loaded straight from HBM; every
 // load but the headers and d reads 512 (Q5_K high bits: 256; Q6_K scales: 128) contiguous bytes
-// across the warp.
+// across the warp.  The batch kernel takes the two rows' whole Q6_K scale records (sc16) instead
+// of the lane's four scales (sc).
 template <int FMT> struct PairRegs;
 template <> struct PairRegs<T_Q4_K> { uint4 q[2][2]; uint4 h[2]; };             // quants [row][half], header [row]
 template <> struct PairRegs<T_Q5_K> { uint4 q[2][2]; uint4 h[2]; uint2 e[2]; }; // + high bits [row]
-template <> struct PairRegs<T_Q6_K> { uint4 l[2][2]; uint4 qh[2]; uint32_t sc[2]; uint32_t d[2]; };
+template <> struct PairRegs<T_Q6_K> { uint4 l[2][2]; uint4 qh[2]; uint32_t sc[2]; uint4 sc16[2]; uint32_t d[2]; };
 
-template <int FMT>
+template <int FMT, bool ALL_SC = false>
 __device__ __forceinline__ void load_unit(PairRegs<FMT> &R, const uint8_t *u, int lane, int g) {
 #pragma unroll
   for (int r = 0; r < 2; r++) {
@@ -533,7 +328,8 @@ __device__ __forceinline__ void load_unit(PairRegs<FMT> &R, const uint8_t *u, in
       R.l[r][0] = ldg128(u + ((2 * r) * 32 + lane) * 16);
       R.l[r][1] = ldg128(u + ((2 * r + 1) * 32 + lane) * 16);
       R.qh[r] = ldg128(u + kQ6H + (r * 32 + lane) * 16);
-      R.sc[r] = __ldg(reinterpret_cast<const uint32_t *>(u + kQ6S + (r * 32 + lane) * 4));
+      if constexpr (ALL_SC) R.sc16[r] = ldg128(u + kQ6S + 16 * (8 * r + g));
+      else R.sc[r] = __ldg(reinterpret_cast<const uint32_t *>(u + kQ6S + (r * 32 + lane) * 4));
       R.d[r] = __ldg(reinterpret_cast<const unsigned short *>(u + kQ6D + 2 * (8 * r + g)));
     } else {
       R.q[r][0] = ldg128(u + ((2 * r) * 32 + lane) * 16);
@@ -544,14 +340,37 @@ __device__ __forceinline__ void load_unit(PairRegs<FMT> &R, const uint8_t *u, in
   }
 }
 
+// The A operands of chunk c (sub-blocks 2c and 2c + 1) of a Q4_K / Q5_K unit: lo = {row g k 0-3,
+// row g+8 k 0-3, row g k 16-19, row g+8 k 16-19} of sub-block 2c, hi the same of sub-block 2c + 1.
+template <bool FIVE>
+__device__ __forceinline__ void k45_operands(const uint4 (&q)[2][2], uint2 eg, uint2 eh, int c, uint32_t (&lo)[4],
+                                             uint32_t (&hi)[4]) {
+  const int cp = c >> 1, ci = c & 1;
+  const uint4 wq = q[0][cp], vq = q[1][cp];
+  const uint32_t wx = ci ? wq.z : wq.x, wy = ci ? wq.w : wq.y, vx = ci ? vq.z : vq.x, vy = ci ? vq.w : vq.y;
+  lo[0] = wx & 0x0f0f0f0fu; lo[2] = wy & 0x0f0f0f0fu; lo[1] = vx & 0x0f0f0f0fu; lo[3] = vy & 0x0f0f0f0fu;
+  hi[0] = (wx >> 4) & 0x0f0f0f0fu; hi[2] = (wy >> 4) & 0x0f0f0f0fu;
+  hi[1] = (vx >> 4) & 0x0f0f0f0fu; hi[3] = (vy >> 4) & 0x0f0f0f0fu;
+  if constexpr (FIVE) {
+    lo[0] |= ((eg.x >> (2 * c)) & 0x01010101u) << 4; lo[2] |= ((eg.y >> (2 * c)) & 0x01010101u) << 4;
+    lo[1] |= ((eh.x >> (2 * c)) & 0x01010101u) << 4; lo[3] |= ((eh.y >> (2 * c)) & 0x01010101u) << 4;
+    hi[0] |= ((eg.x >> (2 * c + 1)) & 0x01010101u) << 4; hi[2] |= ((eg.y >> (2 * c + 1)) & 0x01010101u) << 4;
+    hi[1] |= ((eh.x >> (2 * c + 1)) & 0x01010101u) << 4; hi[3] |= ((eh.y >> (2 * c + 1)) & 0x01010101u) << 4;
+  }
+}
+
+// ---------------------------------------------------------------------------- one token, register streaming
 // The super-block sums of rows g (p0) and g + 8 (p1) of one unit from registers, in the canonical
-// order: the quad tree over lanes t of (T(2t) + T(2t+1)) (Q6_K: half 0's tree plus half 1's tree,
-// each over the pairs of groups 8h + 2t, 8h + 2t + 1).
+// order: the quad tree over lanes t of the pair term of sub-blocks (2t, 2t + 1) (Q6_K: half 0's
+// tree plus half 1's tree, each over the pairs of groups 8h + 2t, 8h + 2t + 1).
 template <int FMT>
-__device__ __forceinline__ void pair_sums(const PairRegs<FMT> &R, int g, int t, const SAct &x, int sb, double &p0,
-                                          double &p1) {
+__device__ __forceinline__ void pair_sums(const PairRegs<FMT> &R, int g, int t, const SAct &x, int sb, float &p0,
+                                          float &p1) {
   if constexpr (FMT == T_Q6_K) {
-    double ph[2][2];
+    float ph[2][2];
+    const float2 xd = lds_f2(x.sc0 + 8 * (sb * 4 + t));               // 32-blocks t, 4 + t
+    const uint4 mo = lds128(x.sc1 + 16 * (sb * 4 + t));               // groups 2t, 2t+1, 8+2t, 9+2t
+    const float moff[4] = {__uint_as_float(mo.x), __uint_as_float(mo.y), __uint_as_float(mo.z), __uint_as_float(mo.w)};
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       const uint32_t lgw[4] = {R.l[0][h].x, R.l[0][h].y, R.l[0][h].z, R.l[0][h].w};
@@ -559,7 +378,7 @@ __device__ __forceinline__ void pair_sums(const PairRegs<FMT> &R, int g, int t, 
       const uint32_t qgw[2] = {h ? R.qh[0].z : R.qh[0].x, h ? R.qh[0].w : R.qh[0].y};
       const uint32_t qhw[2] = {h ? R.qh[1].z : R.qh[1].x, h ? R.qh[1].w : R.qh[1].y};
       const uint32_t xa = lds32(x.xq + sb * 256 + 16 * (8 * h + g) + 4 * t);
-      int C[4] = {0, 0, 0, 0};
+      int C[4] = {kBias, kBias, kBias, kBias};
 #pragma unroll
       for (int u = 0; u < 2; u++) {
 #pragma unroll
@@ -569,94 +388,41 @@ __device__ __forceinline__ void pair_sums(const PairRegs<FMT> &R, int g, int t, 
           mma_k16(C, a0, a1, xa * x.sel[2 * k + u]);
         }
       }
-      const uint2 s2 = lds64(x.xs16 + 4 * (sb * 16 + 8 * h + 2 * t));
-      const uint2 xdw = lds64(x.xd + 8 * (sb * 8 + 4 * h + t));
-      const double xdv = __hiloint2double((int)xdw.y, (int)xdw.x);
+      const float xdv = h ? xd.y : xd.x;
 #pragma unroll
       for (int r = 0; r < 2; r++) {
-        const uint32_t scw = (R.sc[r] >> (16 * h)) & 0xffffu;
-        const double xdd = __dmul_rn(xdv, h2d(R.d[r]));
-        const double pr = __dadd_rn(q6_term(xdd, (int)(int8_t)(scw & 0xff), C[2 * r] - 32 * (int)s2.x),
-                                    q6_term(xdd, (int)(int8_t)(scw >> 8), C[2 * r + 1] - 32 * (int)s2.y));
-        ph[h][r] = quad_tree(pr);
+        const uint32_t scw = R.sc[r] >> (16 * h);
+        const float g0 = __fsub_rn(__int_as_float(C[2 * r]), moff[2 * h]);
+        const float g1 = __fsub_rn(__int_as_float(C[2 * r + 1]), moff[2 * h + 1]);
+        ph[h][r] = quad_tree(q6_pair(xdv, h2f(R.d[r]), sbyte_f(scw, 0), g0, sbyte_f(scw, 1), g1));
       }
     }
-    p0 = __dadd_rn(ph[0][0], ph[1][0]);
-    p1 = __dadd_rn(ph[0][1], ph[1][1]);
+    p0 = __fadd_rn(ph[0][0], ph[1][0]);
+    p1 = __fadd_rn(ph[0][1], ph[1][1]);
   } else {
     constexpr bool FIVE = FMT == T_Q5_K;
     uint2 eg = make_uint2(0, 0), eh = make_uint2(0, 0);
     if constexpr (FIVE) { eg = R.e[0]; eh = R.e[1]; }
     const uint32_t xa = lds32(x.xq + sb * 256 + 32 * g + 4 * t), xb = lds32(x.xq + sb * 256 + 32 * g + 16 + 4 * t);
-    int C0[4] = {0, 0, 0, 0}, C1[4] = {0, 0, 0, 0};
+    int C0[4] = {kBias, kBias, kBias, kBias}, C1[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int cp = 0; cp < 2; cp++) {
-      const uint4 wq = R.q[0][cp], vq = R.q[1][cp];
-      const uint32_t wg[4] = {wq.x, wq.y, wq.z, wq.w}, wh[4] = {vq.x, vq.y, vq.z, vq.w};
-#pragma unroll
-      for (int ci = 0; ci < 2; ci++) {
-        const int c = 2 * cp + ci;
-        uint32_t lg0 = wg[2 * ci] & 0x0f0f0f0fu, lg1 = wg[2 * ci + 1] & 0x0f0f0f0fu;
-        uint32_t lh0 = wh[2 * ci] & 0x0f0f0f0fu, lh1 = wh[2 * ci + 1] & 0x0f0f0f0fu;
-        uint32_t ug0, ug1, uh0, uh1;
-        if constexpr (FIVE) {
-          lg0 |= ((eg.x >> (2 * c)) & 0x01010101u) << 4; lg1 |= ((eg.y >> (2 * c)) & 0x01010101u) << 4;
-          lh0 |= ((eh.x >> (2 * c)) & 0x01010101u) << 4; lh1 |= ((eh.y >> (2 * c)) & 0x01010101u) << 4;
-          ug0 = ((wg[2 * ci] >> 4) & 0x0f0f0f0fu) | (((eg.x >> (2 * c + 1)) & 0x01010101u) << 4);
-          ug1 = ((wg[2 * ci + 1] >> 4) & 0x0f0f0f0fu) | (((eg.y >> (2 * c + 1)) & 0x01010101u) << 4);
-          uh0 = ((wh[2 * ci] >> 4) & 0x0f0f0f0fu) | (((eh.x >> (2 * c + 1)) & 0x01010101u) << 4);
-          uh1 = ((wh[2 * ci + 1] >> 4) & 0x0f0f0f0fu) | (((eh.y >> (2 * c + 1)) & 0x01010101u) << 4);
-        } else {
-          ug0 = wg[2 * ci] - lg0; ug1 = wg[2 * ci + 1] - lg1;
-          uh0 = wh[2 * ci] - lh0; uh1 = wh[2 * ci + 1] - lh1;
-        }
-        int(&C)[4] = (c & 1) ? C1 : C0;
-        mma_k32(C, lg0, lh0, lg1, lh1, xa * x.sel[2 * c], xb * x.sel[2 * c]);
-        mma_k32(C, ug0, uh0, ug1, uh1, xa * x.sel[2 * c + 1], xb * x.sel[2 * c + 1]);
-      }
+    for (int c = 0; c < 4; c++) {
+      uint32_t lo[4], hi[4];
+      k45_operands<FIVE>(R.q, eg, eh, c, lo, hi);
+      int(&C)[4] = (c & 1) ? C1 : C0;
+      mma_k32(C, lo[0], lo[1], lo[2], lo[3], xa * x.sel[2 * c], xb * x.sel[2 * c]);
+      mma_k32(C, hi[0], hi[1], hi[2], hi[3], xa * x.sel[2 * c + 1], xb * x.sel[2 * c + 1]);
     }
-    int v0 = C0[0] + C1[0], v1 = C0[1] + C1[1], v2 = C0[2] + C1[2], v3 = C0[3] + C1[3];
-    if (!FIVE) { v1 >>= 4; v3 >>= 4; }
-    const uint4 xdw = lds128(x.xd + 8 * (sb * 8 + 2 * t));
-    const double xd0 = __hiloint2double((int)xdw.y, (int)xdw.x), xd1 = __hiloint2double((int)xdw.w, (int)xdw.z);
-    const uint2 xs = lds64(x.xs + 4 * (sb * 8 + 2 * t));
+    const uint4 xw = lds128(x.sc0 + 16 * (sb * 4 + t));
+    const float4 xdm = make_float4(__uint_as_float(xw.x), __uint_as_float(xw.y), __uint_as_float(xw.z), __uint_as_float(xw.w));
 #pragma unroll
     for (int r = 0; r < 2; r++) {
       const uint4 hd = R.h[r];
-      const uint32_t F = k45_field(hd, t);
-      const double d = h2d(hd.x & 0xffffu), dmin = h2d(hd.x >> 16);
-      const double pr = __dadd_rn(k45_term(d, dmin, F & 63, (F >> 12) & 63, r ? v2 : v0, (int)xs.x, xd0),
-                                  k45_term(d, dmin, (F >> 6) & 63, (F >> 18) & 63, r ? v3 : v1, (int)xs.y, xd1));
+      const K45Sc s = k45_sc(h2f(hd.x & 0xffffu), h2f(hd.x >> 16), k45_field(hd, t));
+      const float pr = k45_pair(s, biased_f(C0[2 * r] + C1[2 * r]), biased_f(C0[2 * r + 1] + C1[2 * r + 1]), xdm);
       if (r) p1 = quad_tree(pr); else p0 = quad_tree(pr);
     }
   }
-}
-
-// Stage one token's activation in shared memory (quantized here from f32, or copied when the
-// caller quantized it) and return its view.
-template <int FMT, int NT>
-__device__ __forceinline__ SAct stage_token(const KqArgs &p, uint8_t *base, int warp, int lane, int g) {
-  uint8_t *sxq = base;
-  double *sxd = reinterpret_cast<double *>(sxq + p.k);
-  int32_t *sxs = reinterpret_cast<int32_t *>(sxd + p.k / 32);
-  int32_t *sxs16 = FMT == T_Q6_K ? sxs + p.k / 32 : nullptr;
-  if (p.xq == nullptr) {
-    quantize_to_smem<NT>(p.x, p.k, p.norm_w, p.norm_eps, sxq, sxd, sxs, sxs16, warp, lane);
-  } else {
-    const uint4 *q4 = reinterpret_cast<const uint4 *>(p.xq);
-    for (int i = threadIdx.x; i < p.k / 16; i += NT) {
-      const uint4 v = __ldg(q4 + i);
-      reinterpret_cast<uint4 *>(sxq)[i] = v;
-      if (sxs16) sxs16[i] = __dp4a((int)v.x, 0x01010101, __dp4a((int)v.y, 0x01010101,
-                                   __dp4a((int)v.z, 0x01010101, __dp4a((int)v.w, 0x01010101, 0))));
-    }
-    for (int i = threadIdx.x; i < p.k / 32; i += NT) { sxd[i] = (double)__ldg(p.xd + i); sxs[i] = __ldg(p.xs + i); }
-  }
-  SAct sa{};
-  sa.xq = smem_u32(sxq); sa.xd = smem_u32(sxd); sa.xs = smem_u32(sxs); sa.xs16 = sxs16 ? smem_u32(sxs16) : 0u;
-#pragma unroll
-  for (int i = 0; i < 8; i++) sa.sel[i] = g == i ? 1u : 0u;
-  return sa;
 }
 
 // One token.  A CTA owns tiles [T0, T1); their units, (tile, super-block) in order, are one
@@ -680,7 +446,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) kq_stream_kernel(const K
   const int i0 = (int)((int64_t)warp * npair / kStreamWarps), i1 = (int)((int64_t)(warp + 1) * npair / kStreamWarps);
   const int64_t row0 = (int64_t)T0 * kTile;
   const int nrows = (int)(min((int64_t)T1 * kTile, p.rows) - row0);
-  double *sums = reinterpret_cast<double *>(smem + p.part_off);    // [pair][16 rows]
+  float *sums = reinterpret_cast<float *>(smem + p.part_off);      // [pair][16 rows]
   const uint8_t *base = p.w + (int64_t)T0 * nb * US;
 
   PairRegs<FMT> R[D];
@@ -698,7 +464,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) kq_stream_kernel(const K
     for (int d = 0; d < D; d++) {
       const int ii = i + d;
       if (ii < i1) {
-        double S0, S1;
+        float S0, S1;
         pair_sums<FMT>(R[d], g, t, sa, sb, S0, S1);
         if (ii + D < i1) load_unit<FMT>(R[d], base + (int64_t)(ii + D) * US, lane, g);
         if (t == 0) { sums[ii * kTile + g] = S0; sums[ii * kTile + g + 8] = S1; }
@@ -714,18 +480,241 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) kq_stream_kernel(const K
     float o[2] = {0.f, 0.f};
     for (int e = 0; e < step; e++) {
       const int rr = row + e;
-      const double *sr = sums + (int64_t)(rr / kTile) * nb * kTile + rr % kTile;
-      double tot = 0.0;
-      for (int s = 0; s < nb; s++) tot = __dadd_rn(tot, sr[s * kTile]);
-      o[e] = __double2float_rn(tot);
+      const float *sr = sums + (int64_t)(rr / kTile) * nb * kTile + rr % kTile;
+      float tot = 0.f;
+      for (int s = 0; s < nb; s++) tot = __fadd_rn(tot, sr[s * kTile]);
+      o[e] = tot;
     }
     store_row(p, 0, row0 + row, o[0], o[1]);
   }
 }
 
+// ---------------------------------------------------------------------------- 2..16 tokens
+// Per-warp scale staging of one super-block for the batch kernel:
+//   Q4_K / Q5_K: [token][pair c] float4 (xd, xd, xd*xs, xd*xs of 32-blocks 2c, 2c + 1);
+//   Q6_K:        [token][32-block] float xd.
+template <int FMT, int NTOK> constexpr int batch_sc_bytes() { return FMT == T_Q6_K ? NTOK * 8 * 4 : NTOK * 4 * 16; }
+
+template <int FMT, int NTOK>
+__device__ __forceinline__ void stage_batch_scales(const KqArgs &p, int sb, uint8_t *wsc, int lane) {
+  const int64_t kb = p.k / 32;
+  if constexpr (FMT == T_Q6_K) {
+    float *o = reinterpret_cast<float *>(wsc);
+#pragma unroll
+    for (int e = lane; e < NTOK * 8; e += 32) {
+      const int tok = e >> 3, b = e & 7;
+      o[e] = tok < p.ntok ? __ldg(p.xd + tok * kb + sb * 8 + b) : 0.f;
+    }
+  } else {
+    float4 *o = reinterpret_cast<float4 *>(wsc);
+#pragma unroll
+    for (int e = lane; e < NTOK * 4; e += 32) {
+      const int tok = e >> 2, c = e & 3;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (tok < p.ntok) {
+        const float2 xd = __ldg(reinterpret_cast<const float2 *>(p.xd + tok * kb + sb * 8 + 2 * c));
+        const int2 xs = __ldg(reinterpret_cast<const int2 *>(p.xs + tok * kb + sb * 8 + 2 * c));
+        v = make_float4(xd.x, xd.y, __fmul_rn(xd.x, __int2float_rn(xs.x)), __fmul_rn(xd.y, __int2float_rn(xs.y)));
+      }
+      o[e] = v;
+    }
+  }
+}
+
+// B fragments of super-block sb for NG groups of 8 tokens: token 8G + g, words 4m + t (m = 0..15:
+// Q4_K / Q5_K sub-block m >> 1, bytes 16 (m & 1) + 4t..; Q6_K group m, bytes 4t..).  Padding tokens
+// read zeros.
+template <int NG>
+__device__ __forceinline__ void load_batch_b(const KqArgs &p, int sb, int g, int t, uint32_t (&B)[NG][16]) {
+#pragma unroll
+  for (int G = 0; G < NG; G++) {
+    const int tok = 8 * G + g;
+    const bool live = tok < p.ntok;
+    const uint32_t *xw = reinterpret_cast<const uint32_t *>(p.xq + (int64_t)(live ? tok : 0) * p.k + (int64_t)sb * 256);
+#pragma unroll
+    for (int m = 0; m < 16; m++) B[G][m] = live ? __ldg(xw + 4 * m + t) : 0u;
+  }
+}
+
+// One Q4_K / Q5_K unit for NG token groups: S[G][e] = the super-block sum of row g + 8 (e >> 1),
+// token 8G + 2t + (e & 1), in the canonical order.
+template <int FMT, int NG>
+__device__ __forceinline__ void unit_k45_batch(const PairRegs<FMT> &R, const uint32_t (&B)[NG][16], uint32_t wsc, int t,
+                                               float (&S)[NG][4]) {
+  constexpr bool FIVE = FMT == T_Q5_K;
+  uint2 eg = make_uint2(0, 0), eh = make_uint2(0, 0);
+  if constexpr (FIVE) { eg = R.e[0]; eh = R.e[1]; }
+  const float d[2] = {h2f(R.h[0].x & 0xffffu), h2f(R.h[1].x & 0xffffu)};
+  const float dm[2] = {h2f(R.h[0].x >> 16), h2f(R.h[1].x >> 16)};
+  float q01[NG][4];
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    uint32_t lo[4], hi[4];
+    k45_operands<FIVE>(R.q, eg, eh, c, lo, hi);
+    const K45Sc s[2] = {k45_sc(d[0], dm[0], k45_field(R.h[0], c)), k45_sc(d[1], dm[1], k45_field(R.h[1], c))};
+#pragma unroll
+    for (int G = 0; G < NG; G++) {
+      int L[4] = {kBias, kBias, kBias, kBias}, U[4] = {kBias, kBias, kBias, kBias};
+      mma_k32(L, lo[0], lo[1], lo[2], lo[3], B[G][4 * c], B[G][4 * c + 1]);
+      mma_k32(U, hi[0], hi[1], hi[2], hi[3], B[G][4 * c + 2], B[G][4 * c + 3]);
+      const uint4 w0 = lds128(wsc + 16 * ((8 * G + 2 * t) * 4 + c)), w1 = lds128(wsc + 16 * ((8 * G + 2 * t + 1) * 4 + c));
+      const float4 xdm[2] = {make_float4(__uint_as_float(w0.x), __uint_as_float(w0.y), __uint_as_float(w0.z), __uint_as_float(w0.w)),
+                             make_float4(__uint_as_float(w1.x), __uint_as_float(w1.y), __uint_as_float(w1.z), __uint_as_float(w1.w))};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float P = k45_pair(s[e >> 1], biased_f(L[e]), biased_f(U[e]), xdm[e & 1]);
+        if (c == 0 || c == 2) q01[G][e] = P;
+        else if (c == 1) S[G][e] = __fadd_rn(q01[G][e], P);
+        else S[G][e] = __fadd_rn(S[G][e], __fadd_rn(q01[G][e], P));
+      }
+    }
+  }
+}
+
+// One Q6_K unit for NG token groups (same output convention).
+template <int NG>
+__device__ __forceinline__ void unit_q6_batch(const PairRegs<T_Q6_K> &R, const uint32_t (&B)[NG][16], uint32_t wsc,
+                                              int t, float (&S)[NG][4]) {
+  const float d[2] = {h2f(R.d[0]), h2f(R.d[1])};
+  float H0[NG][4], part[NG][4];                 // half 0's tree; the running (P0 + P1) of a half
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const uint32_t lgw[4] = {R.l[0][h].x, R.l[0][h].y, R.l[0][h].z, R.l[0][h].w};
+    const uint32_t lhw[4] = {R.l[1][h].x, R.l[1][h].y, R.l[1][h].z, R.l[1][h].w};
+    const uint32_t qgw[2] = {h ? R.qh[0].z : R.qh[0].x, h ? R.qh[0].w : R.qh[0].y};
+    const uint32_t qhw[2] = {h ? R.qh[1].z : R.qh[1].x, h ? R.qh[1].w : R.qh[1].y};
+    float q[NG][4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      // scales of groups 8h + 2k, 8h + 2k + 1 (word k of the row's record, bytes 2h, 2h + 1)
+      const uint32_t w0 = k == 0 ? R.sc16[0].x : k == 1 ? R.sc16[0].y : k == 2 ? R.sc16[0].z : R.sc16[0].w;
+      const uint32_t w1 = k == 0 ? R.sc16[1].x : k == 1 ? R.sc16[1].y : k == 2 ? R.sc16[1].z : R.sc16[1].w;
+      const float sc[2][2] = {{sbyte_f(w0, 2 * h), sbyte_f(w0, 2 * h + 1)}, {sbyte_f(w1, 2 * h), sbyte_f(w1, 2 * h + 1)}};
+      int C[NG][2][4];
+#pragma unroll
+      for (int uu = 0; uu < 2; uu++) {
+        // signed quants q - 32 (bytes in [0, 63]: + 96 never carries, then flip the top bit)
+        const uint32_t a0 = (q6_unpack(lgw[uu * 2], lgw[uu * 2 + 1], qgw[uu], k) + 0x60606060u) ^ 0x80808080u;
+        const uint32_t a1 = (q6_unpack(lhw[uu * 2], lhw[uu * 2 + 1], qhw[uu], k) + 0x60606060u) ^ 0x80808080u;
+#pragma unroll
+        for (int G = 0; G < NG; G++) {
+#pragma unroll
+          for (int e = 0; e < 4; e++) C[G][uu][e] = kBias;
+          mma_k16s(C[G][uu], a0, a1, B[G][8 * h + 2 * k + uu]);
+        }
+      }
+#pragma unroll
+      for (int G = 0; G < NG; G++) {
+        const float xd[2] = {lds_f(wsc + 4 * ((8 * G + 2 * t) * 8 + 4 * h + k)),
+                             lds_f(wsc + 4 * ((8 * G + 2 * t + 1) * 8 + 4 * h + k))};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int ri = e >> 1;
+          const float P = q6_pair(xd[e & 1], d[ri], sc[ri][0], biased_f(C[G][0][e]), sc[ri][1], biased_f(C[G][1][e]));
+          if (k == 0 || k == 2) q[G][e] = P;
+          else if (k == 1) part[G][e] = __fadd_rn(q[G][e], P);
+          else {
+            const float hh = __fadd_rn(part[G][e], __fadd_rn(q[G][e], P));
+            if (h == 0) H0[G][e] = hh; else S[G][e] = __fadd_rn(H0[G][e], hh);
+          }
+        }
+      }
+    }
+  }
+}
+
+// 2..16 tokens.  A CTA owns tiles [T0, T1); its units are taken super-block-major (unit i = tile
+// i % nt of super-block i / nt) and cut into equal runs, one per warp, so a warp loads the
+// activation fragments of a super-block once for all the tiles it takes of it.  Weights stream
+// from HBM into registers (D units in flight, the first before griddepcontrol.wait); each unit's
+// super-block sums go to shared memory [tile][super-block][row][token], and after one CTA barrier
+// a thread per (row, token) adds them in super-block order.  No waits: nothing to bound.
+// Two token groups hold twice the activation fragments: 12 warps leave each thread 168 registers.
+template <int NG> constexpr int batch_warps() { return NG == 2 ? 12 : 16; }
+constexpr int kBatchDepth = 2;
+constexpr int64_t kBatchBudget = 210 * 1024;
+
+template <int FMT, int NG>
+__global__ void __launch_bounds__(batch_warps<NG>() * 32, 1) kq_batch_kernel(const KqArgs p) {
+  constexpr int NW = batch_warps<NG>();
+  constexpr int NT = NW * 32, NTOK = 8 * NG, D = kBatchDepth, US = unit_bytes<FMT>();
+  constexpr int SCB = batch_sc_bytes<FMT, NTOK>();
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  int T0, T1;
+  cta_tiles(p.rows, T0, T1);
+  const int nb = p.nb, nt = T1 - T0, N = nt * nb;
+  const int i0 = (int)((int64_t)warp * N / NW), i1 = (int)((int64_t)(warp + 1) * N / NW);
+  float *sums = reinterpret_cast<float *>(smem + p.part_off);      // [tile][sb][16 rows][NTOK]
+  uint8_t *wsc = smem + warp * SCB;
+  const uint32_t wsc_a = smem_u32(wsc);
+  const uint8_t *base = p.w + (int64_t)T0 * nb * US;
+  auto unit_ptr = [&](int i) {
+    const int sb = i / nt, tl = i - sb * nt;
+    return base + ((int64_t)tl * nb + sb) * US;
+  };
+
+  PairRegs<FMT> R[D];
+#pragma unroll
+  for (int d = 0; d < D; d++)
+    if (i0 + d < i1) load_unit<FMT, true>(R[d], unit_ptr(i0 + d), lane, g);   // not the previous kernel's output
+  pdl_launch_dependents();
+  pdl_wait();                                   // the activation is
+
+  uint32_t B[NG][16];
+  int cur = -1;
+  for (int i = i0; i < i1; i += D) {
+#pragma unroll
+    for (int d = 0; d < D; d++) {
+      const int ii = i + d;
+      if (ii < i1) {
+        const int sb = ii / nt, tl = ii - sb * nt;
+        if (sb != cur) {
+          load_batch_b<NG>(p, sb, g, t, B);
+          __syncwarp();
+          stage_batch_scales<FMT, NTOK>(p, sb, wsc, lane);
+          __syncwarp();
+          cur = sb;
+        }
+        float S[NG][4];
+        if constexpr (FMT == T_Q6_K) unit_q6_batch<NG>(R[d], B, wsc_a, t, S);
+        else unit_k45_batch<FMT, NG>(R[d], B, wsc_a, t, S);
+        if (ii + D < i1) load_unit<FMT, true>(R[d], unit_ptr(ii + D), lane, g);
+        float *su = sums + ((int64_t)tl * nb + sb) * kTile * NTOK;
+#pragma unroll
+        for (int G = 0; G < NG; G++)
+#pragma unroll
+          for (int ri = 0; ri < 2; ri++)
+            *reinterpret_cast<float2 *>(su + (g + 8 * ri) * NTOK + 8 * G + 2 * t) = make_float2(S[G][2 * ri], S[G][2 * ri + 1]);
+      }
+    }
+  }
+  __syncthreads();
+
+  // one thread per (row, token) (per (gate, up) pair and token with swiglu): sums in super-block order
+  const int step = p.swiglu ? 2 : 1;
+  const int64_t row0 = (int64_t)T0 * kTile;
+  const int nrows = (int)(min((int64_t)T1 * kTile, p.rows) - row0);
+  const int npos = (nrows + step - 1) / step * NTOK;
+  for (int idx = threadIdx.x; idx < npos; idx += NT) {
+    const int tok = idx % NTOK, row = (idx / NTOK) * step;
+    if (tok >= p.ntok) continue;
+    float o[2] = {0.f, 0.f};
+    for (int e = 0; e < step; e++) {
+      const int rr = row + e;
+      const float *sr = sums + (int64_t)(rr / kTile) * nb * kTile * NTOK + (rr % kTile) * NTOK + tok;
+      float tot = 0.f;
+      for (int s = 0; s < nb; s++) tot = __fadd_rn(tot, sr[(int64_t)s * kTile * NTOK]);
+      o[e] = tot;
+    }
+    store_row(p, tok, row0 + row, o[0], o[1]);
+  }
+}
+
 // ---------------------------------------------------------------------------- host side
 int kq_x_bytes(const DevMatrix &m) {
-  return (int)((m.cols + 12 * (m.cols / 32) + (m.type == T_Q6_K ? 4 * (m.cols / 16) : 0) + 127) / 128 * 128);
+  const int64_t k = m.cols;
+  return (int)((k + (m.type == T_Q6_K ? k / 8 + k / 4 : k / 4) + 127) / 128 * 128);
 }
 
 // one shared-memory grant per kernel (the template parameter) and device
@@ -759,10 +748,10 @@ cudaError_t launch_ex(int64_t max_smem, const KqArgs &a, int grid, int block, in
 constexpr int64_t kStreamBudget = 200 * 1024;
 
 cudaError_t launch_stream(const DevMatrix &m, const ActView &act, float *y, const float *y_add, const GemvFuse &fz,
-                          unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why) {
+                          int num_sms, cudaStream_t s, bool pdl, const char **why) {
   const int64_t nb = m.cols / 256;
   const int64_t x_bytes = kq_x_bytes(m);
-  const int64_t cap = (kStreamBudget - x_bytes) / (nb * kTile * 8);       // tiles per CTA
+  const int64_t cap = (kStreamBudget - x_bytes) / (nb * kTile * 4);       // tiles per CTA
   if (cap < 1) { *why = "k-quant rows too long for the one-token GEMV"; return cudaErrorInvalidValue; }
   const int64_t tiles_all = (m.rows + kTile - 1) / kTile, per_launch = cap * num_sms;
   const int us = kq_unit_bytes(m.type);
@@ -779,9 +768,8 @@ cudaError_t launch_stream(const DevMatrix &m, const ActView &act, float *y, cons
     a.y = y + (fz.swiglu ? rb / 2 : rb);
     a.y_add = y_add ? y_add + rb : nullptr;
     a.norm_w = fz.norm_w; a.norm_eps = fz.eps; a.swiglu = fz.swiglu ? 1 : 0;
-    a.status = status;
     a.x_off = 0; a.part_off = (int)x_bytes;
-    const int smem = (int)(x_bytes + tiles_cta * nb * kTile * 8);
+    const int smem = (int)(x_bytes + tiles_cta * nb * kTile * 4);
     const int block = kStreamWarps * 32;
     cudaError_t e;
     switch (m.type) {
@@ -794,46 +782,57 @@ cudaError_t launch_stream(const DevMatrix &m, const ActView &act, float *y, cons
   return cudaSuccess;
 }
 
-// 2..8 tokens per launch, tokens in groups of 8.
-cudaError_t launch_tok(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride, const float *y_add,
-                       const GemvFuse &fz, unsigned *status, int num_sms, cudaStream_t s, bool pdl, const char **why) {
+template <int NG>
+cudaError_t launch_batch_ng(const KqArgs &a, int type, int grid, int smem, cudaStream_t s, bool pdl) {
+  const int block = batch_warps<NG>() * 32;
+  switch (type) {
+    case T_Q4_K: return launch_ex<kq_batch_kernel<T_Q4_K, NG>>(kBatchBudget, a, grid, block, smem, s, pdl);
+    case T_Q5_K: return launch_ex<kq_batch_kernel<T_Q5_K, NG>>(kBatchBudget, a, grid, block, smem, s, pdl);
+    default: return launch_ex<kq_batch_kernel<T_Q6_K, NG>>(kBatchBudget, a, grid, block, smem, s, pdl);
+  }
+}
+
+// 2..n tokens: launches of up to 16 tokens (8 with one MMA group), each over as many tiles per CTA
+// as leave the super-block sums room in shared memory.
+cudaError_t launch_batch(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
+                         const float *y_add, const GemvFuse &fz, int num_sms, cudaStream_t s, bool pdl,
+                         const char **why) {
   if (!act.xq) { *why = "the in-kernel activation quantization takes one token"; return cudaErrorInvalidValue; }
   const int64_t nb = m.cols / 256;
-  const int kChunk = chunk_sb_of(m.type), us = kq_unit_bytes(m.type);
-  const int nchunk = (int)((nb + kChunk - 1) / kChunk);
   const int64_t tiles_all = (m.rows + kTile - 1) / kTile;
-  const int grid = (int)(tiles_all < num_sms ? tiles_all : num_sms);
-  const int64_t units = (tiles_all + grid - 1) / grid * nchunk;           // per CTA, at most
-  const int64_t stage = (int64_t)kChunk * us;
-  const int64_t part_bytes = 2LL * 16 * kTile * kMaxTok * 8;
-  int64_t nst = (kTokBudget - part_bytes - 8 * kMaxStages) / stage;
-  if (nst > kMaxStages) nst = kMaxStages;
-  if (nst > units) nst = units;
-  if (nst < 1) { *why = "k-quant rows too long for the shared-memory stages"; return cudaErrorInvalidValue; }
-  const int part_off = (int)(nst * stage), bar_off = (int)(part_off + part_bytes);
-  const int smem = bar_off + 8 * (int)nst;
-  for (int t0 = 0; t0 < ntok; t0 += kMaxTok) {
-    const int nt = ntok - t0 < kMaxTok ? ntok - t0 : kMaxTok;
-    KqArgs a{};
-    a.w = m.data; a.rows = m.rows; a.nb = (int)nb; a.nchunk = nchunk; a.nst = (int)nst;
-    a.ntok = nt; a.k = m.cols;
-    a.xq = act.xq + (int64_t)t0 * m.cols;
-    a.xd = act.xd + (int64_t)t0 * (m.cols / 32);
-    a.xs = act.xs + (int64_t)t0 * (m.cols / 32);
-    a.y = y + (int64_t)t0 * y_stride;
-    a.y_add = y_add ? y_add + (int64_t)t0 * y_stride : nullptr;
-    a.y_stride = y_stride;
-    a.swiglu = fz.swiglu ? 1 : 0;
-    a.status = status;
-    a.part_off = part_off; a.bar_off = bar_off;
-    const int block = kTokWarps * 32;
-    cudaError_t e;
-    switch (m.type) {
-      case T_Q4_K: e = launch_ex<kq_tok_kernel<T_Q4_K>>(kTokBudget + 1024, a, grid, block, smem, s, pdl); break;
-      case T_Q5_K: e = launch_ex<kq_tok_kernel<T_Q5_K>>(kTokBudget + 1024, a, grid, block, smem, s, pdl); break;
-      default: e = launch_ex<kq_tok_kernel<T_Q6_K>>(kTokBudget + 1024, a, grid, block, smem, s, pdl); break;
+  const int us = kq_unit_bytes(m.type);
+  for (int t0 = 0; t0 < ntok; t0 += kBatchTok) {
+    const int nt_tok = ntok - t0 < kBatchTok ? ntok - t0 : kBatchTok;
+    const int ng = nt_tok > 8 ? 2 : 1;
+    const int ntokp = 8 * ng;
+    const int64_t sc_bytes = (int64_t)(ng == 2 ? batch_warps<2>() : batch_warps<1>()) *
+                             (m.type == T_Q6_K ? ntokp * 8 * 4 : ntokp * 4 * 16);
+    const int64_t per_tile = nb * kTile * ntokp * 4;
+    const int64_t cap = (kBatchBudget - sc_bytes) / per_tile;              // tiles per CTA
+    if (cap < 1) { *why = "k-quant rows too long for the batched GEMV"; return cudaErrorInvalidValue; }
+    const int64_t per_launch = cap * num_sms;
+    for (int64_t tb = 0; tb < tiles_all; tb += per_launch) {
+      const int64_t nt = tiles_all - tb < per_launch ? tiles_all - tb : per_launch;
+      const int64_t rb = tb * kTile;
+      const int grid = (int)(nt < num_sms ? nt : num_sms);
+      const int64_t tiles_cta = (nt + grid - 1) / grid;
+      KqArgs a{};
+      a.w = m.data + tb * nb * us;
+      a.rows = m.rows - rb < nt * kTile ? m.rows - rb : nt * kTile;
+      a.nb = (int)nb; a.ntok = nt_tok; a.k = m.cols;
+      a.xq = act.xq + (int64_t)t0 * m.cols;
+      a.xd = act.xd + (int64_t)t0 * (m.cols / 32);
+      a.xs = act.xs + (int64_t)t0 * (m.cols / 32);
+      a.y = y + (int64_t)t0 * y_stride + (fz.swiglu ? rb / 2 : rb);
+      a.y_add = y_add ? y_add + (int64_t)t0 * y_stride + rb : nullptr;
+      a.y_stride = y_stride;
+      a.swiglu = fz.swiglu ? 1 : 0;
+      a.part_off = (int)sc_bytes;
+      const int smem = (int)(sc_bytes + tiles_cta * per_tile);
+      const cudaError_t e = ng == 2 ? launch_batch_ng<2>(a, m.type, grid, smem, s, pdl)
+                                    : launch_batch_ng<1>(a, m.type, grid, smem, s, pdl);
+      if (e != cudaSuccess) return e;
     }
-    if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
@@ -850,6 +849,7 @@ cudaError_t launch_gemv_kq(const DevMatrix &m, const ActView &act, int ntok, flo
 cudaError_t launch_gemv_kq_ex(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
                               const float *y_add, const GemvFuse &fz, unsigned *status, int num_sms, cudaStream_t s,
                               bool pdl, const char **why) {
+  (void)status;                                 // these kernels never wait, so they report no timeouts
   if (m.cols % 256 || m.cols < 256) { *why = "k-quant rows must be a whole number of 256-value super-blocks"; return cudaErrorInvalidValue; }
   if (fz.norm_w && (act.xq || !act.x || ntok != 1)) { *why = "the fused RMSNorm takes one f32 token"; return cudaErrorInvalidValue; }
   if (fz.swiglu && (m.rows % 2 || y_add)) { *why = "the SwiGLU epilogue takes (gate, up) row pairs and no residual"; return cudaErrorInvalidValue; }
@@ -857,8 +857,8 @@ cudaError_t launch_gemv_kq_ex(const DevMatrix &m, const ActView &act, int ntok, 
     *why = "the in-kernel activation quantization takes one token";
     return cudaErrorInvalidValue;
   }
-  if (ntok == 1) return launch_stream(m, act, y, y_add, fz, status, num_sms, s, pdl, why);
-  return launch_tok(m, act, ntok, y, y_stride, y_add, fz, status, num_sms, s, pdl, why);
+  if (ntok == 1) return launch_stream(m, act, y, y_add, fz, num_sms, s, pdl, why);
+  return launch_batch(m, act, ntok, y, y_stride, y_add, fz, num_sms, s, pdl, why);
 }
 
 }  // namespace zllm

@@ -114,13 +114,17 @@ cudaError_t launch_advance(const int32_t *arg, int n, int32_t *tok, int32_t *pos
 
 cudaError_t repack_upload(const DevMatrix &m, const void *raw_dev, cudaStream_t s);
 
-// Tensor-core GEMM for k-quant matrices and 16 or more tokens (gemm_kq.cu).  The activation is
+// Tensor-core GEMM for k-quant matrices and 64 or more tokens (gemm_kq.cu).  The activation is
 // first turned into f16 tiles (launch_gemm_prep, gemm_b_bytes of scratch), then launch_gemm_kq
 // computes y[t][r] (+ y_add) for all tokens.  launch_kq_bound writes an upper bound of the
 // matrix's |dequantized value| (as f32 bits); a finite bound qualifies the matrix, and
 // gemm_weight_scale(bound) is the power of two that brings its values just under 2^15 in f16.
-constexpr int kGemmMinTokens = 16;        // zllm_mm
-constexpr int kModelGemmMinTokens = 64;   // model passes: below this the per-token kernel streams the weights faster
+// Below kGemmMinTokens (zllm_mm and model passes alike) the batched GEMV streams the weights faster
+// and keeps every token's bits equal to a single-token pass.
+constexpr int kGemmMinTokens = 64;
+// An F16 output head of 16 or more logit rows runs on the tensor-core GEMM (f32 activation as f16
+// hi / lo, ~1e-6 of the largest logit from the CUDA-core GEMV, whose f32 FMA chain it replaces).
+constexpr int kHeadGemmMinRows = 16;
 float gemm_weight_scale(float bound);
 int64_t gemm_tokens_pad(int ntok);
 size_t gemm_b_bytes(int64_t k, int ntok);
@@ -136,6 +140,13 @@ int tp_comm_init(void **comm, int rank, int size, const void *unique_id, const c
 void tp_comm_destroy(void *comm);
 cudaError_t tp_allreduce_sum(void *comm, float *buf, size_t count, cudaStream_t s, const char **why);
 
+// An F16 matrix (the output head) pre-tiled once for the same kernel, against f32 activations
+// x [ntok][ldx] split into f16 hi / lo tiles (two MMAs, f32 accumulation): y[t][r] = W[r] . x_t.
+size_t gemm_f16_tiles_bytes(int64_t rows, int64_t k);
+cudaError_t launch_gemm_tile_f16(const DevMatrix &m, void *tiles, cudaStream_t s);
+cudaError_t launch_gemm_prep_f32(const float *x, int64_t ldx, int64_t k, int ntok, void *bbuf, cudaStream_t s);
+cudaError_t launch_gemm_f16_tiled(const void *tiles, int64_t rows, int64_t k, const void *bbuf, int ntok, float *y,
+                                  int64_t y_stride, unsigned *status, cudaStream_t s);
 // f16 x f16 -> f32 on the same kernel: D[j][i] = sum_k A[i][k] B[j][k] (row-major, k % 64 == 0)
 size_t gemm_f16_scratch_bytes(int64_t m, int64_t n, int64_t k);
 cudaError_t launch_gemm_f16(const uint16_t *A, const uint16_t *B, int64_t m, int64_t n, int64_t k, float *D, void *scratch,

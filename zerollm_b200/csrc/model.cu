@@ -61,7 +61,8 @@ struct zllm_model {
   float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *att = nullptr;
   float *g = nullptr, *u = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
   float *qkv = nullptr, *gu = nullptr;                   // outputs of the row-concatenated projections
-  void *gemm_b = nullptr;                                // f16 activation tiles of the tensor-core GEMM (max_batch >= 16)
+  void *gemm_b = nullptr;                                // f16 activation tiles of the tensor-core GEMM (max_batch >= 64)
+  void *head_tiles = nullptr, *head_b = nullptr;         // F16 output head tiled for the GEMM, and its activation tiles
   void *tp_comm = nullptr;                               // NCCL communicator when the weights are sharded
   int tp_rank = 0, tp_size = 1;
   int8_t *xq = nullptr;
@@ -321,14 +322,24 @@ extern "C" int zllm_model_ready(zllm_model *m) {
   CK(dalloc(&m->g, MB * F), "act");
   CK(dalloc(&m->u, MB * F), "act");
   CK(dalloc(&m->hb, MB * F), "act");
-  if (MB >= kModelGemmMinTokens) {
-    // passes of 16 or more tokens run the k-quant projections as tensor-core GEMMs
+  if (MB >= kGemmMinTokens) {
+    // passes of kGemmMinTokens or more tokens run the k-quant projections as tensor-core GEMMs
     CK(cudaMalloc(&m->gemm_b, gemm_b_bytes(KX, MB)), "GEMM activation tiles");
     for (auto &L : m->L)
       for (zllm_weight *w : {L.w[0], L.w[1], L.w[2], L.w[3], L.w[4], L.w[5], L.w[6], L.qkv, L.gu})
         if (w && kq_type(w->m.type)) zllm_weight_gemm_ok(m->ctx, w);
   }
   CK(dalloc(&m->logits, (size_t)LB * c.vocab), "logits");
+  {
+    // an F16 output head that passes of kHeadGemmMinRows or more logit rows will use (batched decode,
+    // all-position logits) is also kept tiled for the tensor-core GEMM
+    const zllm_weight *ow = m->out ? m->out : m->tok;
+    if (LB >= kHeadGemmMinRows && ow->m.type == T_F16 && E % 64 == 0) {
+      CK(cudaMalloc(&m->head_tiles, gemm_f16_tiles_bytes(ow->m.rows, E)), "output head tiles");
+      CK(launch_gemm_tile_f16(ow->m, m->head_tiles, m->stream), "output head tiling");
+      CK(cudaMalloc(&m->head_b, gemm_b_bytes(E, LB)), "output head activation tiles");
+    }
+  }
   CK(dalloc(&m->d_tok, MB), "ids");
   CK(dalloc(&m->d_pos, MB), "ids");
   CK(dalloc(&m->d_seq, MB), "ids");
@@ -352,7 +363,7 @@ extern "C" int zllm_model_ready(zllm_model *m) {
 // per-token arithmetic).  Smaller batches (batched decode) keep the per-token kernel, which streams
 // the weights faster at that size and stays bit-identical to single-token passes.
 static bool use_gemm(const zllm_model *m, const zllm_weight *w, int n) {
-  return n >= kModelGemmMinTokens && m->gemm_b && w->gemm_ok == 1;
+  return n >= kGemmMinTokens && m->gemm_b && w->gemm_ok == 1;
 }
 static cudaError_t gemm(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add, int64_t k,
                         bool swiglu) {
@@ -483,7 +494,12 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
     const int nl = want == 2 ? n : 1;
     const float *xl = want == 2 ? m->x : m->x + (int64_t)(n - 1) * E;
     RUN(launch_rmsnorm_quant(xl, m->out_norm, (int)E, nl, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, false));
-    RUN(gemv(m, ow, nl, m->logits, c.vocab, nullptr, m->xb, E));
+    if (nl >= kHeadGemmMinRows && m->head_tiles) {
+      RUN(launch_gemm_prep_f32(m->xb, E, E, nl, m->head_b, s));
+      RUN(launch_gemm_f16_tiled(m->head_tiles, ow->m.rows, E, m->head_b, nl, m->logits, c.vocab, m->ctx->status_dev, s));
+    } else {
+      RUN(gemv(m, ow, nl, m->logits, c.vocab, nullptr, m->xb, E));
+    }
     RUN(launch_argmax(m->logits, c.vocab, c.vocab, nl, m->d_arg, s, false));
   }
 #undef RUN
@@ -757,7 +773,7 @@ extern "C" void zllm_model_destroy(zllm_model *m) {
                   (void *)m->q, (void *)m->k, (void *)m->v, (void *)m->qr, (void *)m->att, (void *)m->g, (void *)m->u,
                   (void *)m->hb, (void *)m->qkv, (void *)m->gu, (void *)m->logits, (void *)m->part, (void *)m->xq, (void *)m->xd, (void *)m->xs,
                   (void *)m->d_tok, (void *)m->d_pos, (void *)m->d_seq, (void *)m->d_npos, (void *)m->d_arg,
-                  (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b})
+                  (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b, m->head_tiles, m->head_b})
     if (p) cudaFree(p);
   if (m->h_io) cudaFreeHost(m->h_io);
   if (m->tp_comm) tp_comm_destroy(m->tp_comm);          // after the graphs that hold its collectives
