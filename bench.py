@@ -374,8 +374,10 @@ def gemm_bench(device: int, reps: int = 20):
 
 def profile_run(args, device: int):
     """Plain launches without graphs or timing, for ncu: --profile-gemm (config 1's attn_q at 512
-    tokens: gemm_bscale / gemm_bfill / gemm_kq_kernel per step) or --profile-attn CTX NSEQ (config 2:
-    qkv_post_kernel + attn_decode_kernel per step); args.warmup + args.steps steps."""
+    tokens: gemm_bscale / gemm_bfill / gemm_kq_kernel per step), --profile-batch NTOK (config 3's
+    interleaved gate/up, Q4_K 24576 x 4096, at NTOK tokens: kq_batch_kernel launches) or
+    --profile-attn CTX NSEQ (config 2: qkv_post_kernel + attn_decode_kernel per step);
+    args.warmup + args.steps steps."""
     import ctypes as C
 
     import torch
@@ -389,11 +391,13 @@ def profile_run(args, device: int):
     g = torch.Generator(device="cuda")
     g.manual_seed(SEED + 7)
     n = args.warmup + args.steps
-    if args.profile_gemm:
+    if args.profile_gemm or args.profile_batch:
         _, tname, rows, cols = GEMM_MIX[0]
+        if args.profile_batch:
+            rows = 2 * 12288
         t = ggml.NAMES[tname]
         w = Weight(ctx, t, rows, cols, _gen_kquant(t, rows, cols, g))
-        T = GEMM_TOKENS
+        T = args.profile_batch or GEMM_TOKENS
         x = torch.randn(T, cols, device="cuda", generator=g)
         xq = torch.empty(T, cols, dtype=torch.int8, device="cuda")
         xd = torch.empty(T, cols // 32, device="cuda")
@@ -405,7 +409,8 @@ def profile_run(args, device: int):
         torch.cuda.synchronize()
         ctx.sync()
         ctx.close()
-        return {"profile_gemm": True, "launches": n, "rows": rows, "cols": cols, "tokens": T}
+        return {"profile_gemm" if args.profile_gemm else "profile_batch": True, "launches": n, "rows": rows, "cols": cols,
+                "tokens": T}
     from zerollm_b200.attention import KVCache, attn_decode, qkv_append, rope_tables
     Lc, nseq = args.profile_attn
     nh, nkv, hd = 32, 8, 128
@@ -862,6 +867,8 @@ def main():
     ap.add_argument("--no-tp", action="store_true", help="skip the 32B tensor-parallel decode measurement")
     ap.add_argument("--profile-gemm", action="store_true",
                     help="plain launches (for ncu): prep + GEMM of the config-1 attn_q matrix, 512 tokens, warm-up + steps")
+    ap.add_argument("--profile-batch", type=int, default=0, metavar="NTOK",
+                    help="plain launches (for ncu): batched GEMV of the Q4_K 24576 x 4096 gate/up matrix at NTOK tokens")
     ap.add_argument("--profile-attn", type=int, nargs=2, default=None, metavar=("CTX", "NSEQ"),
                     help="plain launches (for ncu): config-2 append + attention at CTX positions and NSEQ sequences")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="NSEQ",
@@ -874,7 +881,7 @@ def main():
         torch.cuda.set_device(local)
         print(json.dumps({"profile_decode": decode_bench(args.profile_decode, local, profile=True)}))
         return
-    if args.profile_gemm or args.profile_attn:
+    if args.profile_gemm or args.profile_attn or args.profile_batch:
         import torch
         torch.cuda.set_device(local)
         print(json.dumps(profile_run(args, local)))
