@@ -63,9 +63,12 @@ struct QkvPostArgs {
 // decode attention: a sequence of n positions is cut into context splits whose number and length
 // depend on n alone (so a query's partition, and its bits, do not depend on the batch around it).
 // At least kAttnMinSplit positions per split, at most kAttnSplitCap splits until the splits reach
-// kAttnMaxSplit positions: 37 splits x 8 KV heads = 296 CTAs = two per SM of the 148.
+// kAttnMaxSplit positions: 37 splits x 8 KV heads = 296 CTAs = two per SM of the 148.  Measured on
+// B200 (config 2 and the 8B decode), 256 positions per split beat 128 (more work per warp, fewer
+// partials to merge: +30 % at 2048 x 64 sequences and 8192 x 1, +5 % at 32-sequence decode) and
+// 512 (which starves one short sequence of CTAs: -26 % at 2048 x 1).
 // attn_nsplit is non-decreasing in n, so a launch sized for the longest sequence fits every other.
-constexpr int kAttnWarps = 8, kAttnMinSplit = 128, kAttnMaxSplit = 1024, kAttnSplitCap = 37;
+constexpr int kAttnWarps = 8, kAttnMinSplit = 256, kAttnMaxSplit = 1024, kAttnSplitCap = 37;
 __host__ __device__ inline int attn_nsplit(int n) {
   int ns = (n + kAttnMinSplit - 1) / kAttnMinSplit;
   if (ns > kAttnSplitCap) ns = kAttnSplitCap;
