@@ -318,6 +318,15 @@ template <> struct Dq<T_Q6_K> {
 // 0 -- A already tiled f16, one MMA (A * B hi); T_F16 (1) -- A already tiled f16 against an f32
 // activation split into B hi / lo, two MMAs.
 template <int FMT> constexpr bool a_tiled() { return FMT == 0 || FMT == T_F16; }
+// Ring geometry: dequantized A tiles (hi, lo) come from registers and need little depth; tiled A
+// tiles (hi only) stream from HBM like B and get the same depth.
+template <int FMT> constexpr int a_stages() { return a_tiled<FMT>() ? 4 : kAStages; }
+template <int FMT> constexpr int b_stages() { return a_tiled<FMT>() ? 4 : kBStages; }
+template <int FMT> constexpr int a_slot() { return a_tiled<FMT>() ? kTileBytes : kPairBytes; }
+template <int FMT> constexpr size_t smem_bytes() {
+  return 1024 + (size_t)a_stages<FMT>() * a_slot<FMT>() + (size_t)b_stages<FMT>() * kPairBytes +
+         (2 * a_stages<FMT>() + 2 * b_stages<FMT>() + 1) * 8 + 16;
+}
 
 struct GemmArgs {
   const uint8_t *w;       // k-quant units of the matrix; or (a_tiled) A tiles [m_tile][K/64][128][64] f16
@@ -338,16 +347,17 @@ struct GemmArgs {
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) {
   constexpr int US = a_tiled<FMT>() ? 0 : FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360;
+  constexpr int AS = a_stages<FMT>(), BS = b_stages<FMT>(), ASLOT = a_slot<FMT>();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);   // swizzle atoms need 1024
-  uint8_t *a_ring = smem, *b_ring = smem + kAStages * kPairBytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(b_ring + kBStages * kPairBytes);
-  uint64_t *full_a = bars, *empty_a = bars + kAStages, *full_b = bars + 2 * kAStages, *empty_b = full_b + kBStages;
-  uint64_t *acc_full = empty_b + kBStages;
+  uint8_t *a_ring = smem, *b_ring = smem + AS * ASLOT;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(b_ring + BS * kPairBytes);
+  uint64_t *full_a = bars, *empty_a = bars + AS, *full_b = bars + 2 * AS, *empty_b = full_b + BS;
+  uint64_t *acc_full = empty_b + BS;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  auto a_hi = [&](int s) { return a_ring + (size_t)s * kPairBytes; };
-  auto a_lo = [&](int s) { return a_ring + (size_t)s * kPairBytes + kTileBytes; };
+  auto a_hi = [&](int s) { return a_ring + (size_t)s * ASLOT; };
+  auto a_lo = [&](int s) { return a_ring + (size_t)s * ASLOT + kTileBytes; };   // k-quant A only
   auto b_hi = [&](int s) { return b_ring + (size_t)s * kPairBytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -365,11 +375,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
   const int nmma = (ntok_tile + 15) / 16 * 16;          // MMA N: the tile's tokens, rounded up to 16
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kAStages; s++) {
+    for (int s = 0; s < AS; s++) {
       mbar_init(&full_a[s], a_tiled<FMT>() ? kProdWarps * 32 : kDqWarps);
       mbar_init(&empty_a[s], 1);
     }
-    for (int s = 0; s < kBStages; s++) {
+    for (int s = 0; s < BS; s++) {
       mbar_init(&full_b[s], kProdWarps * 32);
       mbar_init(&empty_b[s], 1);
     }
@@ -390,8 +400,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
     const int pw = warp;
     const int bchunks = nmma * 128 / 16;                // 16-byte chunks of one part's rows [0, nmma)
     for (int k = 0; k < nks; k++) {
-      const int s = k % kBStages;
-      if (k >= kBStages && !waitw(&empty_b[s], (uint32_t)(k / kBStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
+      const int s = k % BS;
+      if (k >= BS && !waitw(&empty_b[s], (uint32_t)(k / BS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
       const int kd = (k + koff) % nks;
       const uint8_t *src = p.b + ((int64_t)n_tile * nks + kd) * 2 * kTileBytes;
       const uint32_t dst = smem_u32(b_hi(s));
@@ -403,10 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
       }
       cp_async_arrive(&full_b[s]);
       if constexpr (a_tiled<FMT>()) {
-        // the A tile rides with the B stage: FMT 0 keeps k % kAStages == k % kBStages by waiting
-        // on the A ring's own barrier first
-        const int sa = k % kAStages;
-        if (k >= kAStages && !waitw(&empty_a[sa], (uint32_t)(k / kAStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
+        // the A tile of the same K step goes into its own ring (stage k % AS, after that stage's
+        // previous MMAs have released it)
+        const int sa = k % AS;
+        if (k >= AS && !waitw(&empty_a[sa], (uint32_t)(k / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
         constexpr int QA = kTileBytes / kProdWarps;
         const uint8_t *asrc = p.w + ((int64_t)m_tile * nks + kd) * kTileBytes + pw * QA;
         const uint32_t adst = smem_u32(a_hi(sa)) + pw * QA;
@@ -422,9 +432,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
       const uint32_t idesc = idesc_n(nmma);
       int issued = 0;
       for (int k = 0; k < nks; k++) {
-        const int sb = k % kBStages, sa = k % kAStages;
-        if (!wait1(&full_b[sb], (uint32_t)(k / kBStages) & 1u, ctl, ST_FULL_TIMEOUT) ||
-            !wait1(&full_a[sa], (uint32_t)(k / kAStages) & 1u, ctl, ST_FULL_TIMEOUT))
+        const int sb = k % BS, sa = k % AS;
+        if (!wait1(&full_b[sb], (uint32_t)(k / BS) & 1u, ctl, ST_FULL_TIMEOUT) ||
+            !wait1(&full_a[sa], (uint32_t)(k / AS) & 1u, ctl, ST_FULL_TIMEOUT))
           break;
         fence_async_smem();                             // the generic-proxy stores / cp.async data -> the MMA's reads
         tc_fence_after();
@@ -460,12 +470,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
       if (present) nxt.load(ubase + (int64_t)(koff_sb % p.nb) * US, m, tp);
       bool live = true;
       for (int k = 0; k < nks && live; k++) {
-        const int s = k % kAStages, sbi = k >> 2, c = k & 3;
+        const int s = k % AS, sbi = k >> 2, c = k & 3;
         if (c == 0 && present) {
           cur.set(nxt, p.wscale);
           if (sbi + 1 < p.nb) nxt.load(ubase + (int64_t)((sbi + 1 + koff_sb) % p.nb) * US, m, tp);
         }
-        if (k >= kAStages) live = waitw(&empty_a[s], (uint32_t)(k / kAStages - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane);
+        if (k >= AS) live = waitw(&empty_a[s], (uint32_t)(k / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane);
         if (!live) break;
         uint4 hi[4], lo[4];
         if (present) {
@@ -654,8 +664,7 @@ cudaError_t launch_t(const GemmArgs &a, dim3 grid, size_t smem, cudaStream_t s) 
   return cudaGetLastError();
 }
 
-constexpr size_t kSmem = 1024 + (size_t)(kAStages + kBStages) * kPairBytes + (2 * kAStages + 2 * kBStages + 1) * 8 + 16;
-static_assert(kSmem <= 227 * 1024, "shared memory");
+static_assert(smem_bytes<T_Q4_K>() <= 227 * 1024 && smem_bytes<T_F16>() <= 227 * 1024, "shared memory");
 
 // An upper bound of |dequantized value| over a k-quant matrix, as the bits of a non-negative f32
 // (atomicMax on the bits orders them); a NaN or infinite scale makes it +inf.
@@ -737,9 +746,9 @@ cudaError_t launch_gemm_kq(const DevMatrix &m, const void *bbuf, int ntok, float
   a.status = status;
   const dim3 grid((unsigned)((m.rows + GM - 1) / GM), (unsigned)(npad / GN));
   switch (m.type) {
-    case T_Q4_K: return launch_t<T_Q4_K>(a, grid, kSmem, s);
-    case T_Q5_K: return launch_t<T_Q5_K>(a, grid, kSmem, s);
-    default: return launch_t<T_Q6_K>(a, grid, kSmem, s);
+    case T_Q4_K: return launch_t<T_Q4_K>(a, grid, smem_bytes<T_Q4_K>(), s);
+    case T_Q5_K: return launch_t<T_Q5_K>(a, grid, smem_bytes<T_Q5_K>(), s);
+    default: return launch_t<T_Q6_K>(a, grid, smem_bytes<T_Q6_K>(), s);
   }
 }
 
@@ -767,7 +776,7 @@ cudaError_t launch_gemm_f16(const uint16_t *A, const uint16_t *B, int64_t m, int
   a.w = at; a.b = bt; a.bscale = bscale; a.y = D; a.y_stride = m; a.rows = m; a.ntok = (int)n;
   a.wscale = 1.f; a.wscale_inv = 1.f;
   a.nb = (int)(k / 256); a.kc = (int)(k / 64); a.status = status;
-  return launch_t<0>(a, dim3((unsigned)(mpad / GM), (unsigned)(npad / GN)), kSmem, s);
+  return launch_t<0>(a, dim3((unsigned)(mpad / GM), (unsigned)(npad / GN)), smem_bytes<0>(), s);
 }
 
 
@@ -808,7 +817,7 @@ cudaError_t launch_gemm_f16_tiled(const void *tiles, int64_t rows, int64_t k, co
   a.y = y; a.y_stride = y_stride; a.rows = rows; a.ntok = ntok;
   a.wscale = 1.f; a.wscale_inv = 1.f;
   a.nb = (int)(k / 256); a.kc = (int)(k / 64); a.status = status;
-  return launch_t<T_F16>(a, dim3((unsigned)(mpad / GM), (unsigned)(npad / GN)), kSmem, s);
+  return launch_t<T_F16>(a, dim3((unsigned)(mpad / GM), (unsigned)(npad / GN)), smem_bytes<T_F16>(), s);
 }
 
 }  // namespace zllm
