@@ -576,7 +576,7 @@ template <int NG>
 __device__ __forceinline__ void unit_q6_batch(const PairRegs<T_Q6_K> &R, const uint32_t (&B)[NG][16], uint32_t wsc,
                                               int t, float (&S)[NG][4]) {
   const float d[2] = {h2f(R.d[0]), h2f(R.d[1])};
-  float H0[NG][4], part[NG][4];                 // half 0's tree; the running (P0 + P1) of a half
+  float part[NG][4];                            // the running (P0 + P1) of a half; S holds half 0's tree
 #pragma unroll
   for (int h = 0; h < 2; h++) {
     const uint32_t lgw[4] = {R.l[0][h].x, R.l[0][h].y, R.l[0][h].z, R.l[0][h].w};
@@ -590,32 +590,30 @@ __device__ __forceinline__ void unit_q6_batch(const PairRegs<T_Q6_K> &R, const u
       const uint32_t w0 = k == 0 ? R.sc16[0].x : k == 1 ? R.sc16[0].y : k == 2 ? R.sc16[0].z : R.sc16[0].w;
       const uint32_t w1 = k == 0 ? R.sc16[1].x : k == 1 ? R.sc16[1].y : k == 2 ? R.sc16[1].z : R.sc16[1].w;
       const float sc[2][2] = {{sbyte_f(w0, 2 * h), sbyte_f(w0, 2 * h + 1)}, {sbyte_f(w1, 2 * h), sbyte_f(w1, 2 * h + 1)}};
-      int C[NG][2][4];
+      // signed quants q - 32 of groups 8h + 2k + uu (bytes in [0, 63]: + 96 never carries, then flip
+      // the top bit), rows g and g + 8
+      uint32_t A[2][2];
 #pragma unroll
       for (int uu = 0; uu < 2; uu++) {
-        // signed quants q - 32 (bytes in [0, 63]: + 96 never carries, then flip the top bit)
-        const uint32_t a0 = (q6_unpack(lgw[uu * 2], lgw[uu * 2 + 1], qgw[uu], k) + 0x60606060u) ^ 0x80808080u;
-        const uint32_t a1 = (q6_unpack(lhw[uu * 2], lhw[uu * 2 + 1], qhw[uu], k) + 0x60606060u) ^ 0x80808080u;
-#pragma unroll
-        for (int G = 0; G < NG; G++) {
-#pragma unroll
-          for (int e = 0; e < 4; e++) C[G][uu][e] = kBias;
-          mma_k16s(C[G][uu], a0, a1, B[G][8 * h + 2 * k + uu]);
-        }
+        A[uu][0] = (q6_unpack(lgw[uu * 2], lgw[uu * 2 + 1], qgw[uu], k) + 0x60606060u) ^ 0x80808080u;
+        A[uu][1] = (q6_unpack(lhw[uu * 2], lhw[uu * 2 + 1], qhw[uu], k) + 0x60606060u) ^ 0x80808080u;
       }
 #pragma unroll
       for (int G = 0; G < NG; G++) {
+        int C0[4] = {kBias, kBias, kBias, kBias}, C1[4] = {kBias, kBias, kBias, kBias};
+        mma_k16s(C0, A[0][0], A[0][1], B[G][8 * h + 2 * k]);
+        mma_k16s(C1, A[1][0], A[1][1], B[G][8 * h + 2 * k + 1]);
         const float xd[2] = {lds_f(wsc + 4 * ((8 * G + 2 * t) * 8 + 4 * h + k)),
                              lds_f(wsc + 4 * ((8 * G + 2 * t + 1) * 8 + 4 * h + k))};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
           const int ri = e >> 1;
-          const float P = q6_pair(xd[e & 1], d[ri], sc[ri][0], biased_f(C[G][0][e]), sc[ri][1], biased_f(C[G][1][e]));
+          const float P = q6_pair(xd[e & 1], d[ri], sc[ri][0], biased_f(C0[e]), sc[ri][1], biased_f(C1[e]));
           if (k == 0 || k == 2) q[G][e] = P;
           else if (k == 1) part[G][e] = __fadd_rn(q[G][e], P);
           else {
             const float hh = __fadd_rn(part[G][e], __fadd_rn(q[G][e], P));
-            if (h == 0) H0[G][e] = hh; else S[G][e] = __fadd_rn(H0[G][e], hh);
+            S[G][e] = h == 0 ? hh : __fadd_rn(S[G][e], hh);
           }
         }
       }
@@ -637,7 +635,8 @@ constexpr int64_t kBatchBudget = 210 * 1024;
 template <int FMT, int NG>
 __global__ void __launch_bounds__(batch_warps<NG>() * 32, 1) kq_batch_kernel(const KqArgs p) {
   constexpr int NW = batch_warps<NG>();
-  constexpr int NT = NW * 32, NTOK = 8 * NG, D = kBatchDepth, US = unit_bytes<FMT>();
+  // Q6_K units (34 registers a lane) keep one in flight with two token groups
+  constexpr int NT = NW * 32, NTOK = 8 * NG, D = FMT == T_Q6_K && NG == 2 ? 1 : kBatchDepth, US = unit_bytes<FMT>();
   constexpr int SCB = batch_sc_bytes<FMT, NTOK>();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
