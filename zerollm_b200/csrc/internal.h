@@ -95,6 +95,11 @@ struct AttnArgs {
   unsigned *status;
   float scale;
   int n_head, n_kv, head_dim, nseq, nsplit;
+  // fused decode (every query a different sequence, at its position npos - 1): the kernel does the
+  // q/k/v post-processing of `post` itself (q is then unused) -- the roped queries stay in shared
+  // memory and the last context split appends the key / value row before reading it
+  int fused;
+  QkvPostArgs post;
 };
 
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t s, bool pdl);

@@ -27,20 +27,13 @@ __device__ __forceinline__ uint16_t f32_to_f16_bits(float x) {
 }
 
 // ============================================================================ q/k/v post-processing + append
-// One warp per head: heads [0, n_head) are query heads, [n_head, n_head + n_kv) key heads (whose
-// value head is appended alongside).  Token t of the batch is at position pos[t] of sequence seq[t].
-__global__ void qkv_post_kernel(const QkvPostArgs a) {
-  extern __shared__ float sh[];                     // one head_dim row per warp
-  pdl_launch_dependents();
-  pdl_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int heads = a.n_head + a.n_kv;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (gw >= heads * a.ntok) return;
-  const int t = gw / heads, h = gw % heads;
+// Head h of token t, by one warp with a head_dim row of shared memory: heads [0, n_head) are query
+// heads (the roped query is left in `row`, and copied to q_out unless it is NULL), [n_head, n_head
+// + n_kv) key heads (k is normalized, roped and appended with its value head).  Token t of the
+// batch is at position pos[t] of sequence seq[t].
+__device__ void post_head(const QkvPostArgs &a, int t, int h, float *row, float *q_out, int lane) {
   const bool isq = h < a.n_head;
   const int hd = a.head_dim;
-  float *row = sh + warp * hd;
   const float *src = isq ? a.q + (int64_t)t * a.q_stride + h * hd : a.k + (int64_t)t * a.kv_stride + (h - a.n_head) * hd;
   const float *bias = isq ? (a.bq ? a.bq + h * hd : nullptr) : (a.bk ? a.bk + (h - a.n_head) * hd : nullptr);
   const float *norm = isq ? a.q_norm : a.k_norm;
@@ -76,8 +69,8 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
   }
   __syncwarp();
   if (isq) {
-    float *dst = a.q_out + (int64_t)t * a.q_out_stride + h * hd;
-    for (int i = lane; i < hd; i += 32) dst[i] = row[i];
+    if (q_out)
+      for (int i = lane; i < hd; i += 32) q_out[i] = row[i];
     return;
   }
   // append k and v at `pos` of this sequence's cache (worker.js:303-308)
@@ -102,6 +95,20 @@ __global__ void qkv_post_kernel(const QkvPostArgs a) {
       vc[i] = v;
     }
   }
+}
+
+// One warp per head of every token.
+__global__ void qkv_post_kernel(const QkvPostArgs a) {
+  extern __shared__ float sh[];                     // one head_dim row per warp
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = a.n_head + a.n_kv;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (gw >= heads * a.ntok) return;
+  const int t = gw / heads, h = gw % heads;
+  post_head(a, t, h, sh + warp * a.head_dim, h < a.n_head ? a.q_out + (int64_t)t * a.q_out_stride + h * a.head_dim : nullptr,
+            lane);
 }
 
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t s, bool pdl) {
@@ -140,8 +147,15 @@ struct KvRow {
   static constexpr int DPL = HD / 32;                  // dims per lane
   static constexpr int WORDS = DPL * (int)sizeof(T) / 4;  // 32-bit words per lane per row
   uint32_t w[WORDS > 0 ? WORDS : 1];
-  __device__ __forceinline__ void load(const T *row, int lane) {
+  // `fresh`: a row this launch wrote (the fused append) -- read through L2, not the read-only path
+  __device__ __forceinline__ void load(const T *row, int lane, bool fresh = false) {
     const uint8_t *p = reinterpret_cast<const uint8_t *>(row) + lane * DPL * sizeof(T);
+    if (fresh) {
+      if constexpr (WORDS == 4) { const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p)); w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w; }
+      else if constexpr (WORDS == 2) { const uint2 v = __ldcg(reinterpret_cast<const uint2 *>(p)); w[0] = v.x; w[1] = v.y; }
+      else { w[0] = __ldcg(reinterpret_cast<const uint32_t *>(p)); }
+      return;
+    }
     if constexpr (WORDS == 4) { const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p)); w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w; }
     else if constexpr (WORDS == 2) { const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p)); w[0] = v.x; w[1] = v.y; }
     else { w[0] = __ldg(reinterpret_cast<const uint32_t *>(p)); }
@@ -163,6 +177,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
   __shared__ float sa[kAttnWarps][G];                   // a batch's rescale factors
   __shared__ float sm[kAttnWarps][G], sl[kAttnWarps][G];
   __shared__ float sacc[kAttnWarps][G][HD];
+  __shared__ float sq[G][HD];                           // fused: this KV head's roped queries
   __shared__ int last_flag;
 
   pdl_launch_dependents();
@@ -180,28 +195,42 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
   const int64_t cs = a.seq ? a.seq[b] : b;            // cache sequence of this query
   const T *kbase = reinterpret_cast<const T *>(a.kcache) + cs * a.seq_stride + (int64_t)kh * a.head_stride;
   const T *vbase = reinterpret_cast<const T *>(a.vcache) + cs * a.seq_stride + (int64_t)kh * a.head_stride;
-
-  float q[G][DPL], acc[G][DPL];
-#pragma unroll
-  for (int g = 0; g < G; g++) {
-    const float *qs = a.q + ((int64_t)b * a.n_head + kh * G + g) * HD + lane * DPL;
-#pragma unroll
-    for (int i = 0; i < DPL; i++) { q[g][i] = qs[i]; acc[g][i] = 0.f; }
-  }
-  // running max / sum of head (lane % G), kept identically by every lane of that head
-  float m_run = -INFINITY, l_run = 0.f;
-  const int my_i = lane / R, my_h = my_i % G, my_p = my_i / G;
+  // fused decode: this launch appends the query's own position npos - 1 (the last split's CTA does)
+  const int newp = a.fused ? npos - 1 : -1;
 
   KvRow<T, HD> kr[NB], vr[NB];
   auto load_batch = [&](int p0, KvRow<T, HD> (&k)[NB], KvRow<T, HD> (&v)[NB]) {
 #pragma unroll
     for (int j = 0; j < NB; j++) {
       const int p = min(p0 + j, w1 - 1);               // past the end: repeat the last row (masked below)
-      k[j].load(kbase + (int64_t)p * HD, lane);
-      v[j].load(vbase + (int64_t)p * HD, lane);
+      k[j].load(kbase + (int64_t)p * HD, lane, p == newp);
+      v[j].load(vbase + (int64_t)p * HD, lane, p == newp);
     }
   };
-  if (w0 < w1) load_batch(w0, kr, vr);
+  // the first batch streams in during the fused prologue unless it holds the row being appended
+  const bool early = !(w0 <= newp && newp < w0 + NB);
+  if (w0 < w1 && early) load_batch(w0, kr, vr);
+  if (a.fused) {
+    // q/k/v post-processing of this query (qkv_post_kernel's arithmetic): warps take the KV head's
+    // G query heads, and in the last split also the key / value head, which is appended before any
+    // warp reads the row
+    const int nh = G + (split == active - 1 ? 1 : 0);
+    for (int hh = warp; hh < nh; hh += kAttnWarps)
+      post_head(a.post, b, hh < G ? kh * G + hh : a.n_head + kh, hh < G ? &sq[hh][0] : &sacc[warp][0][0], nullptr, lane);
+    __syncthreads();
+  }
+  if (w0 < w1 && !early) load_batch(w0, kr, vr);
+
+  float q[G][DPL], acc[G][DPL];
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    const float *qs = a.fused ? &sq[g][lane * DPL] : a.q + ((int64_t)b * a.n_head + kh * G + g) * HD + lane * DPL;
+#pragma unroll
+    for (int i = 0; i < DPL; i++) { q[g][i] = qs[i]; acc[g][i] = 0.f; }
+  }
+  // running max / sum of head (lane % G), kept identically by every lane of that head
+  float m_run = -INFINITY, l_run = 0.f;
+  const int my_i = lane / R, my_h = my_i % G, my_p = my_i / G;
   for (int p0 = w0; p0 < w1; p0 += NB) {
     KvRow<T, HD> kc[NB], vc[NB];
 #pragma unroll

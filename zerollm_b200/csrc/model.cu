@@ -72,7 +72,7 @@ struct zllm_model {
   int nsplit = 1;
   std::vector<int> pos;                                   // positions held per sequence
   // decode graph cache: one graph per token count
-  struct Graph { int n = 0; int want = 0; int adv = 0; cudaGraphExec_t exec = nullptr; };
+  struct Graph { int n = 0; int want = 0; int adv = 0; int distinct = 0; cudaGraphExec_t exec = nullptr; };
   std::vector<Graph> graphs;
   std::vector<std::pair<int, int>> eager_seen;           // shapes (n, want | adv << 2) run once eagerly before being recorded
   int32_t *d_gen = nullptr, *d_step = nullptr;           // greedy generation: tokens [steps][n], step counter
@@ -397,8 +397,10 @@ static cudaError_t tp_reduce(zllm_model *m, int n) {
 }
 
 // Enqueue the pass for n tokens whose ids / positions / sequences are already in d_tok / d_pos /
-// d_seq / d_npos.  want: 0 no logits, 1 the last token's, 2 every token's.
-static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
+// d_seq / d_npos.  want: 0 no logits, 1 the last token's, 2 every token's.  distinct: every token
+// belongs to a different sequence (decode), so the attention kernel can do the q/k/v
+// post-processing and the KV append of its own query (no token reads another token's new row).
+static cudaError_t enqueue_pass(zllm_model *m, int n, int want, bool distinct) {
   const zllm_model_config &c = m->c;
   const int64_t E = c.n_embd, F = c.n_ff, Q = m->qdim(), KV = m->kvdim();
   cudaStream_t s = m->stream;
@@ -440,8 +442,10 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
     pa.seq_stride = g.seq_stride; pa.head_stride = g.head_stride;
     pa.n_head = c.n_head; pa.n_kv = c.n_head_kv; pa.head_dim = c.head_dim; pa.n_rot = c.n_rot; pa.neox = c.neox;
     pa.kv_f16 = c.kv_f16; pa.ntok = n; pa.eps = c.rms_eps;
-    RUN(launch_qkv_post(pa, s, false));
+    if (!distinct) RUN(launch_qkv_post(pa, s, false));
     AttnArgs aa{};
+    aa.fused = distinct ? 1 : 0;
+    aa.post = pa;
     aa.q = m->qr; aa.seq = m->d_seq; aa.kcache = m->kv_block(0, l, 0); aa.vcache = m->kv_block(0, l, 1);
     aa.seq_stride = g.seq_stride; aa.head_stride = g.head_stride; aa.npos = m->d_npos; aa.out = m->att;
     aa.partial = m->part; aa.counters = m->counters; aa.status = m->ctx->status_dev;
@@ -509,11 +513,11 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want) {
 // Validate, stage the int arrays, run the pass (replaying a recorded graph when possible), copy out.
 // One pass of n tokens (with `adv`: followed by the greedy advance of generate), replayed from a
 // recorded graph when the shape was seen before.
-static int launch_shape(zllm_model *m, int n, int want, bool adv) {
+static int launch_shape(zllm_model *m, int n, int want, bool adv, bool distinct) {
   cudaStream_t s = m->stream;
-  const int key = want | (adv ? 4 : 0);
+  const int key = want | (adv ? 4 : 0) | (distinct ? 8 : 0);
   auto enqueue = [&]() -> cudaError_t {
-    cudaError_t e = enqueue_pass(m, n, want);
+    cudaError_t e = enqueue_pass(m, n, want, distinct);
     if (e == cudaSuccess && adv) e = launch_advance(m->d_arg, n, m->d_tok, m->d_pos, m->d_npos, m->d_gen, m->d_step, s, false);
     return e;
   };
@@ -521,7 +525,7 @@ static int launch_shape(zllm_model *m, int n, int want, bool adv) {
   bool eager = !m->use_graphs;
   if (!eager) {
     for (auto &gr : m->graphs)
-      if (gr.n == n && gr.want == want && gr.adv == (adv ? 1 : 0)) exec = gr.exec;
+      if (gr.n == n && gr.want == want && gr.adv == (adv ? 1 : 0) && gr.distinct == (distinct ? 1 : 0)) exec = gr.exec;
     // the first pass of a shape runs eagerly (kernel attributes are set outside any capture)
     if (!exec && std::find(m->eager_seen.begin(), m->eager_seen.end(), std::make_pair(n, key)) == m->eager_seen.end()) {
       m->eager_seen.push_back({n, key});
@@ -542,7 +546,7 @@ static int launch_shape(zllm_model *m, int n, int want, bool adv) {
       e = cudaGraphInstantiate(&exec, graph, 0);
       cudaGraphDestroy(graph);
       if (e != cudaSuccess) return fail(m, zllm_cuda_fail(m->ctx, e, "cudaGraphInstantiate"));
-      m->graphs.push_back({n, want, adv ? 1 : 0, exec});
+      m->graphs.push_back({n, want, adv ? 1 : 0, distinct ? 1 : 0, exec});
     }
     CK(cudaGraphLaunch(exec, s), "cudaGraphLaunch");
   } else {
@@ -580,7 +584,9 @@ static int run(zllm_model *m, const int32_t *seqs, int single_seq, const int32_t
   CK(cudaMemcpyAsync(m->d_pos, hp, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
   CK(cudaMemcpyAsync(m->d_seq, hs, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
   CK(cudaMemcpyAsync(m->d_npos, hn, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
-  int rc0 = launch_shape(m, n, want, false);
+  bool distinct = true;
+  for (int sq = 0; sq < c.n_seq; sq++) distinct = distinct && added[sq] <= 1;
+  int rc0 = launch_shape(m, n, want, false, distinct);
   if (rc0) return rc0;
   const int nl = want == 2 ? n : 1;
   if (want && logits_host)
@@ -651,7 +657,7 @@ extern "C" int zllm_model_generate(zllm_model *m, int seq, const int32_t *seqs, 
   CK(cudaMemcpyAsync(m->d_npos, hn, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s), "ids");
   const int want = n == 1 ? 1 : 2;
   for (int i = 0; i < steps; i++) {
-    int rc = launch_shape(m, n, want, true);
+    int rc = launch_shape(m, n, want, true, true);            // distinct sequences, checked above
     if (rc) return rc;
   }
   CK(cudaMemcpyAsync(out_host, m->d_gen, sizeof(int32_t) * (size_t)steps * n, cudaMemcpyDeviceToHost, s), "tokens");

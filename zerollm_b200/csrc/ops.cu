@@ -211,11 +211,10 @@ static cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, size_t smem, cudaStream_
 cudaError_t launch_rmsnorm_quant(const float *x, const float *w, int n, int ntok, double eps, float *xb, int8_t *xq, float *xd,
                                  int32_t *xs, cudaStream_t s, bool pdl) {
   cudaLaunchAttribute attr[1];
-  // split each token's blocks over CTAs so that about 128 CTAs run (each re-reads the token to get
-  // the same sum of squares)
+  // split each token's blocks over CTAs, one block per warp (each CTA re-reads the token to get the
+  // same sum of squares): the quantization's double divisions are the long chain, not the reads
   const int nblk = n / 32 > 0 ? n / 32 : 1;
-  int split = (128 + ntok - 1) / ntok;
-  if (split > nblk / 8) split = nblk / 8 > 0 ? nblk / 8 : 1;
+  const int split = nblk / 8 > 0 ? nblk / 8 : 1;
   cudaLaunchConfig_t cfg = cfg_of(dim3(ntok, split), dim3(256), 0, s, pdl, attr);
   return cudaLaunchKernelEx(&cfg, rmsnorm_quant_kernel, x, w, n, eps, xb, xq, xd, xs);
 }
