@@ -519,6 +519,8 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
     seqp = None if n_seq == 1 else P(seqs)
     out = np.zeros((TP_STEPS, n_seq), np.int32)
     check(L.zllm_model_generate(h, 0, seqp, P(first), n_seq, 3, P(out)), ctx.h)      # warm-up: record the graphs
+    collective = {0: "none", 1: "NCCL all-reduce",
+                  2: "one-shot all-reduce over NVLink peer memory (CUDA IPC)"}[L.zllm_model_tp_collective(h)]
     cur = np.ascontiguousarray(out[2])
     st = torch.cuda.ExternalStream(L.zllm_model_stream(h), device=f"cuda:{device}")
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -532,7 +534,7 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
     ctx.close()
     wbytes = NL * (2.25 * (Hl * hd * E + 2 * KVl * hd * E + E * Hl * hd + 2 * Fl * E) / 4 + 210 / 256 * E * Fl) + V * E * 2
     return {"seconds": dt, "ms_per_step": round(dt / TP_STEPS * 1e3, 3), "weight_bytes_per_rank": int(wbytes),
-            "last_tokens": same.tolist()}
+            "last_tokens": same.tolist(), "collective": collective}
 
 
 # ------------------------------------------------------------------------------------------ attention (config 2)
@@ -784,6 +786,7 @@ def run_ours(args, world, rank, local):
             barrier()
             r = tp_decode_bench(nseq, world, rank, local)
             slowest = max_over_ranks(r["seconds"])
+            tp["collective_used"] = r["collective"]
             tp[f"b{nseq}"] = {"tok_s": round(nseq * TP_STEPS / slowest, 1), "ms_per_step": round(slowest / TP_STEPS * 1e3, 3),
                               "weight_bytes_per_rank": r["weight_bytes_per_rank"],
                               "hbm_gbs_per_rank_weights": round(r["weight_bytes_per_rank"] / (slowest / TP_STEPS) / 1e9, 1)}
@@ -844,7 +847,7 @@ def run_ours(args, world, rank, local):
             line["tp_decode"] = {"metric": "32B Q4_K_M tensor-parallel decode tok/s (config 4)", "unit": "tok/s",
                                  "model": "Qwen3-32B shapes, random init: Q4_K + Q6_K ffn_down, f16 output head (replicated)",
                                  "tp": world, "kv": f"f16, ctx {TP_CTX}", "prompt": TP_PROMPT, "steps": TP_STEPS,
-                                 "collective": "NCCL all-reduce after attn_output and ffn_down, inside the captured pass",
+                                 "collective": "all-reduce after attn_output and ffn_down, inside the captured pass",
                                  "timing": "CUDA events on the model stream, max over ranks",
                                  "scaling": "strong (one model over all GPUs)", **tp}
         if world == 1 and not args.no_cpu:

@@ -223,6 +223,10 @@ int zllm_tp_unique_id(zllm_ctx *ctx, void *out, size_t bytes);
 /* The model's own stream (a cudaStream_t): every pass runs on it; a caller may record CUDA events
  * on it to time passes on the device (no reference counterpart). */
 void *zllm_model_stream(zllm_model *m);
+/* Which collective sums the row-parallel partials once the model is ready: 0 none (one GPU), 1 NCCL
+ * all-reduce, 2 the library's one-shot all-reduce over NVLink peer memory (every rank its own
+ * process, the peers' buffers mapped by CUDA IPC).  No reference counterpart. */
+int zllm_model_tp_collective(zllm_model *m);
 int zllm_model_set_tp(zllm_model *m, int rank, int size, const void *unique_id);
 
 /* Allocate the KV caches and activations once every tensor is set (called by the first pass). */

@@ -1,7 +1,9 @@
 """Tensor-parallel decode over 2 GPUs (BASELINE config 4 in small): two child processes, one per GPU,
 each holding its shard (zerollm_b200.tp.shard_model) and joining one NCCL group.  Both ranks end
 every pass with the same logits, bit for bit, and those track the single-GPU model within the
-reference's SIMD-vs-JS tolerance (the all-reduce adds the partial sums in another order).  Needs
+reference's SIMD-vs-JS tolerance (the all-reduce adds the partial sums in another order).  Separate
+processes on NVLink-connected GPUs map each other's buffers, so the all-reduce is the library's
+one-shot kernel over peer memory, not NCCL's.  Needs
 two GPUs; NVLS is off for the children (a rank that dies while bound to an NVLink multicast object
 can fault its peers)."""
 import multiprocessing as mp
@@ -43,9 +45,10 @@ def _rank(rank, size, uid_q, out_q):
     m = CudaModel.create(lc, lw, ctx=96, kv="f16", max_batch=64, device=rank, context=ctx, tp=(rank, size, uid))
     step = [m.forward(t).copy() for t in TOKS]
     last = m.forwardBatch(BATCH, logits="last").copy()
+    coll = m.tp_collective()
     m.close()
     ctx.close()
-    out_q.put((rank, np.stack(step), last))
+    out_q.put((rank, np.stack(step), last, coll))
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -59,8 +62,8 @@ def test_tp2_matches_single_gpu():
     res = {}
     try:
         for _ in range(2):
-            r, step, last = out_q.get(timeout=300)
-            res[r] = (step, last)
+            r, step, last, coll = out_q.get(timeout=300)
+            res[r] = (step, last, coll)
     except queue.Empty:
         pass
     for p in procs:
@@ -68,6 +71,7 @@ def test_tp2_matches_single_gpu():
         if p.is_alive():
             p.kill()
     assert sorted(res) == [0, 1], "a rank did not finish"
+    assert res[0][2] == res[1][2] == 2, "expected the one-shot NVLink all-reduce on both ranks"
     assert np.array_equal(res[0][0], res[1][0]) and np.array_equal(res[0][1], res[1][1])
     cfg, w = _model()
     one = CudaModel.create(cfg, w, ctx=96, kv="f16", max_batch=64)

@@ -16,6 +16,7 @@ enum : uint32_t {
   ST_EMPTY_TIMEOUT = 1u << 1,  // producer waited too long for a free stage
   ST_DRAIN_TIMEOUT = 1u << 2,  // copies still in flight at exit did not land in time
   ST_BAD_ARGS = 1u << 3,       // launch geometry rejected inside the kernel
+  ST_PEER_TIMEOUT = 1u << 4,   // a peer GPU's all-reduce slice did not arrive in time
 };
 
 // 2 s: far above any legitimate wait (microseconds), far below a box-level hang.

@@ -147,6 +147,13 @@ int tp_unique_id(void *out, size_t bytes, const char **why);
 int tp_comm_init(void **comm, int rank, int size, const void *unique_id, const char **why);
 void tp_comm_destroy(void *comm);
 cudaError_t tp_allreduce_sum(void *comm, float *buf, size_t count, cudaStream_t s, const char **why);
+// One-shot all-reduce over NVLink peer memory (CUDA IPC between the ranks' processes), for vectors
+// of at most `cap` floats; tp_ar_setup returns -1 (and every rank keeps NCCL) when a peer cannot be
+// mapped.  Collective: every rank calls setup and destroy.
+struct TpAr;
+int tp_ar_setup(void *comm, int rank, int size, int64_t cap, cudaStream_t s, TpAr **out, const char **why);
+cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStream_t s);
+void tp_ar_destroy(TpAr *ar, void *comm, cudaStream_t s);
 
 // An F16 matrix (the output head) pre-tiled once for the same kernel, against f32 activations
 // x [ntok][ldx] split into f16 hi / lo tiles (two MMAs, f32 accumulation): y[t][r] = W[r] . x_t.

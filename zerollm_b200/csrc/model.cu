@@ -64,6 +64,7 @@ struct zllm_model {
   void *gemm_b = nullptr;                                // f16 activation tiles of the tensor-core GEMM (max_batch >= 64)
   void *head_tiles = nullptr, *head_b = nullptr;         // F16 output head tiled for the GEMM, and its activation tiles
   void *tp_comm = nullptr;                               // NCCL communicator when the weights are sharded
+  TpAr *tp_ar = nullptr;                                 // one-shot NVLink all-reduce (NULL: NCCL's)
   int tp_rank = 0, tp_size = 1;
   int8_t *xq = nullptr;
   float *xd = nullptr;
@@ -352,6 +353,11 @@ extern "C" int zllm_model_ready(zllm_model *m) {
   CK(dalloc(&m->part, (size_t)MB * c.n_head_kv * m->nsplit * group * (c.head_dim + 2)), "attention scratch");
   CK(dalloc(&m->counters, (size_t)MB * c.n_head_kv), "attention counters");
   CK(cudaMemsetAsync(m->counters, 0, sizeof(int32_t) * MB * c.n_head_kv, m->stream), "counters");
+  if (m->tp_size > 1) {
+    // the one-shot all-reduce when every peer's buffer maps (collective over the ranks); else NCCL
+    const char *why = "";
+    if (tp_ar_setup(m->tp_comm, m->tp_rank, m->tp_size, (int64_t)MB * E, m->stream, &m->tp_ar, &why)) m->tp_ar = nullptr;
+  }
   CK(cudaStreamSynchronize(m->stream), "model ready");
   m->ready = true;
   return ZLLM_OK;
@@ -392,6 +398,7 @@ static cudaError_t gemv_ex(zllm_model *m, const zllm_weight *w, int n, float *y,
 // Sum the ranks' x (n tokens x n_embd) in place: the all-reduce after a row-parallel projection.
 static cudaError_t tp_reduce(zllm_model *m, int n) {
   if (m->tp_size <= 1) return cudaSuccess;
+  if (m->tp_ar) return tp_ar_sum(m->tp_ar, m->x, (int64_t)n * m->c.n_embd, m->ctx->status_dev, m->stream);
   const char *why = "";
   return tp_allreduce_sum(m->tp_comm, m->x, (size_t)n * m->c.n_embd, m->stream, &why);
 }
@@ -690,6 +697,11 @@ extern "C" int zllm_model_set_graphs(zllm_model *m, int on) {
 
 extern "C" void *zllm_model_logits(zllm_model *m) { return m ? m->logits : nullptr; }
 
+extern "C" int zllm_model_tp_collective(zllm_model *m) {
+  if (!m || m->tp_size <= 1) return 0;
+  return m->tp_ar ? 2 : 1;
+}
+
 static int kv_io(zllm_model *m, int seq, int layer, int is_v, int n, float *host, bool get) {
   if (!m || !host || seq < 0 || seq >= m->c.n_seq || layer < 0 || layer >= m->c.n_layer || (is_v != 0 && is_v != 1) ||
       n < 0 || n > m->c.ctx)
@@ -782,6 +794,7 @@ extern "C" void zllm_model_destroy(zllm_model *m) {
                   (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b, m->head_tiles, m->head_b})
     if (p) cudaFree(p);
   if (m->h_io) cudaFreeHost(m->h_io);
+  if (m->tp_ar) tp_ar_destroy(m->tp_ar, m->tp_comm, m->stream);   // after the graphs that use it
   if (m->tp_comm) tp_comm_destroy(m->tp_comm);          // after the graphs that hold its collectives
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;

@@ -184,6 +184,10 @@ class CudaModel:
             self._tokens[sq].extend(int(v) for v in out[:-1, i])
         return out
 
+    def tp_collective(self) -> int:
+        """0 one GPU, 1 NCCL all-reduce, 2 the one-shot all-reduce over NVLink peer memory."""
+        return int(self.lib.zllm_model_tp_collective(self.h))
+
     def kvGet(self, layer: int, isV: int, n: int, seq: int = 0) -> np.ndarray:
         self._guard()
         out = np.empty(n * self.kv_dim, np.float32)
