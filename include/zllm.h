@@ -60,6 +60,12 @@ const char *zllm_last_error(const zllm_ctx *ctx);
 void *zllm_stream(zllm_ctx *ctx);
 /* Wait for the context stream and report a device-side timeout as ZLLM_E_TIMEOUT. */
 int zllm_sync(zllm_ctx *ctx);
+/* Failure-detection check with no fault: runs the tensor-parallel all-reduce kernel on this GPU
+ * against a phantom second rank that never publishes its slice.  The kernel's bounded wait gives up
+ * after 2 s, the kernel returns, and the call reports ZLLM_E_TIMEOUT (status bit 0x10) like any pass
+ * whose peer died; the context stays usable.  Allocates two small buffers for the call.  No
+ * reference counterpart (the reference runs in one process). */
+int zllm_peer_wait_selftest(zllm_ctx *ctx);
 
 /* ------------------------------------------------------------------------------------ weights */
 /* Upload one matrix of `rows` x `cols` (cols = GGUF ne0, the row length) given as the raw GGUF

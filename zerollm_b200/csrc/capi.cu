@@ -104,11 +104,22 @@ int zllm_check_status(zllm_ctx *c) {
   if (e != cudaSuccess) return zllm_cuda_fail(c, e, "reading the device status word");
   if (st) {
     cudaMemset(c->status_dev, 0, sizeof(unsigned));
-    zllm_set_error(c, "device wait timed out (status 0x%x): a bulk copy or stage hand-off did not complete within 2 s; "
-                      "the kernel drained its copies and returned", st);
+    zllm_set_error(c, "device wait timed out (status 0x%x): a bulk copy, a stage hand-off or a peer GPU's all-reduce "
+                      "slice did not complete within 2 s; the kernel drained its copies and returned", st);
     return ZLLM_E_TIMEOUT;
   }
   return ZLLM_OK;
+}
+
+extern "C" int zllm_peer_wait_selftest(zllm_ctx *c) {
+  if (!c) return ZLLM_E_ARG;
+  cudaSetDevice(c->device);
+  const char *why = "";
+  if (tp_ar_phantom_wait(c->status_dev, c->stream, &why)) {
+    zllm_set_error(c, "zllm_peer_wait_selftest: %s", why);
+    return ZLLM_E_CUDA;
+  }
+  return zllm_check_status(c);
 }
 
 extern "C" int zllm_sync(zllm_ctx *c) {

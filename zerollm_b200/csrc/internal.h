@@ -154,6 +154,8 @@ struct TpAr;
 int tp_ar_setup(void *comm, int rank, int size, int64_t cap, cudaStream_t s, TpAr **out, const char **why);
 cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStream_t s);
 void tp_ar_destroy(TpAr *ar, void *comm, cudaStream_t s);
+// The all-reduce kernel against a phantom peer that never stamps: its bounded wait expires.
+int tp_ar_phantom_wait(unsigned *status, cudaStream_t s, const char **why);
 
 // An F16 matrix (the output head) pre-tiled once for the same kernel, against f32 activations
 // x [ntok][ldx] split into f16 hi / lo tiles (two MMAs, f32 accumulation): y[t][r] = W[r] . x_t.

@@ -272,6 +272,39 @@ cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStrea
   return cudaGetLastError();
 }
 
+// Failure detection without a fault: the all-reduce kernel on this GPU against a phantom second
+// rank whose stamps never come.  The kernel's bounded wait expires (2 s), it sets ST_PEER_TIMEOUT in
+// `status`, finishes and returns; the caller reads the status word as after any pass.
+int tp_ar_phantom_wait(unsigned *status, cudaStream_t s, const char **why) {
+  const int64_t cap = 1024;
+  void *b0 = nullptr, *b1 = nullptr, *x = nullptr;
+  cudaError_t e = cudaMalloc(&b0, ar_bytes(cap));
+  if (e == cudaSuccess) e = cudaMalloc(&b1, ar_bytes(cap));
+  if (e == cudaSuccess) e = cudaMalloc(&x, cap * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemsetAsync(b0, 0, ar_bytes(cap), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b1, 0, ar_bytes(cap), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(x, 0, cap * sizeof(float), s);
+  if (e == cudaSuccess) {
+    ArArgs a{};
+    a.x = reinterpret_cast<float *>(x);
+    a.peer[0] = reinterpret_cast<uint8_t *>(b0);     // this rank
+    a.peer[1] = reinterpret_cast<uint8_t *>(b1);     // the phantom: it never stamps b0's slots
+    a.mine = a.peer[0];
+    a.status = status;
+    a.n = cap;
+    a.cap = cap;
+    a.rank = 0;
+    a.size = 2;
+    tp_ar_kernel<<<1, kArThreads, 0, s>>>(a);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  }
+  for (void *p : {b0, b1, x})
+    if (p) cudaFree(p);
+  if (e != cudaSuccess) { *why = cudaGetErrorString(e); return -1; }
+  return 0;
+}
+
 // Every rank calls this after its last pass; the NCCL all-reduce is the barrier that keeps a rank
 // from freeing its buffer while a peer may still read it.
 void tp_ar_destroy(TpAr *ar, void *comm, cudaStream_t s) {

@@ -35,6 +35,7 @@ SIGNATURES = {
     "zllm_last_error": (C.c_char_p, [vp]),
     "zllm_stream": (vp, [vp]),
     "zllm_sync": (i32, [vp]),
+    "zllm_peer_wait_selftest": (i32, [vp]),
     "zllm_weight_upload": (i32, [vp, i32, i64, i64, vp, sz, PP]),
     "zllm_weight_free": (None, [vp]),
     "zllm_weight_info": (i32, [vp, C.POINTER(i32), C.POINTER(i64), C.POINTER(i64), C.POINTER(sz)]),
