@@ -445,7 +445,8 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
     heads, head_dim 128, vocab 151936), Q4_K everywhere but Q6_K ffn_down, f16 output head, f16 KV
     cache of 8192 positions, tensor-parallel over the `world` GPUs: each rank draws its own shard
     (its 64/world query and 8/world KV heads, its 1/world of the FFN at 256-value blocks), the
-    replicated tensors (embedding, norms, output head) from one shared seed; an NCCL all-reduce
+    replicated tensors (embedding, norms) and the output head (each rank uploading its vocab rows) from
+    one shared seed; an NCCL all-reduce
     follows attn_output and ffn_down.  Prefill TP_PROMPT seeded ids per sequence, then TP_STEPS
     greedy steps through zllm_model_generate, timed with CUDA events on the model's stream."""
     import ctypes as C
@@ -476,18 +477,24 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
                      rope_base=1e6)
     h = C.c_void_p()
     check(L.zllm_model_create(ctx.h, C.byref(mc), C.byref(h)), ctx.h)
+    v0, v1 = ranges(V, world)[rank]                     # this rank's rows of the vocab-split output head
     if world > 1:
         ub = C.create_string_buffer(uid, 128)
         check(L.zllm_model_set_tp(h, rank, world, ub), ctx.h)
+        check(L.zllm_model_set_vocab_shard(h, v0, v1 - v0), ctx.h)
     g_local = torch.Generator(device="cuda")
     g_local.manual_seed(SEED + 1000 * (rank + 1))          # this rank's shards
     g_shared = torch.Generator(device="cuda")
     g_shared.manual_seed(SEED)                            # replicated tensors: the same on every rank
     rng = np.random.default_rng(SEED)
 
-    def mat(kind, layer, t, rows, cols, g):
+    def mat(kind, layer, t, rows, cols, g, keep=None):
         buf = _gen_kquant(t, rows, cols, g) if t != ggml.F16 else \
             (torch.randn(rows, cols, device="cuda", generator=g) * 0.02).half().view(torch.uint8).cpu().numpy().reshape(-1)
+        if keep is not None:                              # rows [keep[0], keep[1]) of the generated matrix
+            rb = buf.size // rows
+            buf = np.ascontiguousarray(buf[keep[0] * rb:keep[1] * rb])
+            rows = keep[1] - keep[0]
         check(L.zllm_model_set_matrix(h, kind, layer, t, rows, cols, buf.ctypes.data_as(C.c_void_p), buf.nbytes), ctx.h)
 
     def vec(kind, layer, n):
@@ -495,7 +502,7 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
         check(L.zllm_model_set_vector(h, kind, layer, a.ctypes.data_as(C.c_void_p), a.size), ctx.h)
 
     mat(T_TOK_EMBD, 0, ggml.Q4_K, V, E, g_shared)
-    mat(T_OUTPUT, 0, ggml.F16, V, E, g_shared)
+    mat(T_OUTPUT, 0, ggml.F16, V, E, g_shared, keep=(v0, v1) if world > 1 else None)
     vec(T_OUTPUT_NORM, 0, E)
     for l in range(NL):
         for k_, n_ in ((T_ATTN_NORM, E), (T_FFN_NORM, E), (T_Q_NORM, hd), (T_K_NORM, hd)):
@@ -532,7 +539,7 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
     same = out[-1].copy()
     L.zllm_model_destroy(h)                               # releases the graphs before the communicator
     ctx.close()
-    wbytes = NL * (2.25 * (Hl * hd * E + 2 * KVl * hd * E + E * Hl * hd + 2 * Fl * E) / 4 + 210 / 256 * E * Fl) + V * E * 2
+    wbytes = NL * (2.25 * (Hl * hd * E + 2 * KVl * hd * E + E * Hl * hd + 2 * Fl * E) / 4 + 210 / 256 * E * Fl) + (v1 - v0) * E * 2
     return {"seconds": dt, "ms_per_step": round(dt / TP_STEPS * 1e3, 3), "weight_bytes_per_rank": int(wbytes),
             "last_tokens": same.tolist(), "collective": collective}
 
@@ -845,7 +852,7 @@ def run_ours(args, world, rank, local):
                 "mix_us": round(us, 1), "per_matrix": parts}
         if tp:
             line["tp_decode"] = {"metric": "32B Q4_K_M tensor-parallel decode tok/s (config 4)", "unit": "tok/s",
-                                 "model": "Qwen3-32B shapes, random init: Q4_K + Q6_K ffn_down, f16 output head (replicated)",
+                                 "model": "Qwen3-32B shapes, random init: Q4_K + Q6_K ffn_down, f16 output head (split by vocab rows, logits gathered)",
                                  "tp": world, "kv": f"f16, ctx {TP_CTX}", "prompt": TP_PROMPT, "steps": TP_STEPS,
                                  "collective": "all-reduce after attn_output and ffn_down, inside the captured pass",
                                  "timing": "CUDA events on the model stream, max over ranks",

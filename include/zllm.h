@@ -234,6 +234,13 @@ void *zllm_model_stream(zllm_model *m);
  * process, the peers' buffers mapped by CUDA IPC).  No reference counterpart. */
 int zllm_model_tp_collective(zllm_model *m);
 int zllm_model_set_tp(zllm_model *m, int rank, int size, const void *unique_id);
+/* Tensor parallel: this rank holds only rows [v0, v0 + n) of the output head, the even split
+ * v0 = rank * vocab / size (call after zllm_model_set_tp, before setting the output matrix, which
+ * then has n rows).  Each pass computes the rank's logits slice and gathers every rank's slice
+ * (NCCL all-gather), so every rank ends with the full logits and the same argmax, while reading
+ * 1/size of the head.  Needs a separate output matrix (not the tied token embedding).  The reference
+ * has one process and no such split (its output head is read by every worker thread). */
+int zllm_model_set_vocab_shard(zllm_model *m, int64_t v0, int64_t n);
 
 /* Allocate the KV caches and activations once every tensor is set (called by the first pass). */
 int zllm_model_ready(zllm_model *m);

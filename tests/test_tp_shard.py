@@ -50,3 +50,24 @@ def test_shard_cuts_whole_blocks():
     with pytest.raises(ValueError):
         shard_cols(t, 100, 356)
     assert shard_rows(t, 2, 5)["data"].size == 3 * ggml.row_bytes(ggml.Q6_K, 1024)
+
+
+@pytest.mark.parametrize("size", [2, 4])
+def test_output_head_splits_by_vocab_rows(size):
+    """The output head goes out by vocab rows, rank r holding [r V / size, (r + 1) V / size): the
+    slices' logits, in rank order, are the full head's logits bit for bit."""
+    cfg = synth.tiny(n_embd=256, n_ff=1024, n_head=16, n_head_kv=4, head_dim=64, vocab=321)
+    w = synth.make_model(cfg, seed=5, quant="q4_k_m", dist="tame", output_type=ggml.F16)
+    V, E = cfg["vocab"], cfg["n_embd"]
+    x = np.random.default_rng(2).standard_normal(E).astype(np.float32)
+    full = O.matvec(w["output"]["type"], w["output"]["data"], V, E, x)
+    parts = []
+    for r in range(size):
+        lc, lw = shard_model(cfg, w, r, size)
+        v0, n = lc["vocab_shard"]
+        assert (v0, v0 + n) == (r * V // size, (r + 1) * V // size) and lc["vocab"] == V
+        parts.append(O.matvec(lw["output"]["type"], lw["output"]["data"], n, E, x))
+    assert np.array_equal(np.concatenate(parts), full)
+    tied = dict(w, output=None)
+    lc, lw = shard_model(cfg, tied, 0, size)
+    assert "vocab_shard" not in lc and lw["output"] is None

@@ -154,6 +154,11 @@ struct TpAr;
 int tp_ar_setup(void *comm, int rank, int size, int64_t cap, cudaStream_t s, TpAr **out, const char **why);
 cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStream_t s);
 void tp_ar_destroy(TpAr *ar, void *comm, cudaStream_t s);
+// Vocab-split output head: every rank's logits slice (padded to vpad columns) to every rank, then
+// the slices in vocab order (rank r holds rows [r V / size, (r + 1) V / size)).
+cudaError_t tp_allgather(void *comm, const float *send, float *recv, size_t count, cudaStream_t s, const char **why);
+cudaError_t launch_vocab_gather(const float *recv, int nl, int64_t vpad, int64_t V, int size, float *logits,
+                                cudaStream_t s);
 // The all-reduce kernel against a phantom peer that never stamps: its bounded wait expires.
 int tp_ar_phantom_wait(unsigned *status, cudaStream_t s, const char **why);
 

@@ -65,6 +65,9 @@ struct zllm_model {
   void *head_tiles = nullptr, *head_b = nullptr;         // F16 output head tiled for the GEMM, and its activation tiles
   void *tp_comm = nullptr;                               // NCCL communicator when the weights are sharded
   TpAr *tp_ar = nullptr;                                 // one-shot NVLink all-reduce (NULL: NCCL's)
+  int64_t vocab0 = 0, vocab_n = 0;                       // vocab-split output head: this rank's rows (n 0: whole)
+  int64_t vpad = 0;                                      // columns of a rank's padded logits slice
+  float *lsend = nullptr, *lrecv = nullptr;              // this rank's slice [LB][vpad], all slices [size][LB][vpad]
   int tp_rank = 0, tp_size = 1;
   int8_t *xq = nullptr;
   float *xd = nullptr;
@@ -142,7 +145,8 @@ extern "C" int zllm_model_set_matrix(zllm_model *m, int kind, int layer, int ggm
   const zllm_model_config &c = m->c;
   int64_t er = 0, ec = 0;
   switch (kind) {
-    case ZLLM_T_TOK_EMBD: case ZLLM_T_OUTPUT: er = c.vocab; ec = c.n_embd; break;
+    case ZLLM_T_TOK_EMBD: er = c.vocab; ec = c.n_embd; break;
+    case ZLLM_T_OUTPUT: er = m->vocab_n ? m->vocab_n : c.vocab; ec = c.n_embd; break;
     case ZLLM_T_WQ: er = m->qdim(); ec = c.n_embd; break;
     case ZLLM_T_WK: case ZLLM_T_WV: er = m->kvdim(); ec = c.n_embd; break;
     case ZLLM_T_WO: er = c.n_embd; ec = m->qdim(); break;
@@ -278,6 +282,23 @@ extern "C" int zllm_model_set_tp(zllm_model *m, int rank, int size, const void *
   return ZLLM_OK;
 }
 
+extern "C" int zllm_model_set_vocab_shard(zllm_model *m, int64_t v0, int64_t n) {
+  if (!m) return ZLLM_E_ARG;
+  if (m->ready || m->out || m->tp_size <= 1) {
+    zllm_set_error(m->ctx, "zllm_model_set_vocab_shard: call it after zllm_model_set_tp, before the output matrix and the first pass");
+    return ZLLM_E_STATE;
+  }
+  const int64_t V = m->c.vocab, a = (int64_t)m->tp_rank * V / m->tp_size, b = (int64_t)(m->tp_rank + 1) * V / m->tp_size;
+  if (v0 != a || n != b - a) {
+    zllm_set_error(m->ctx, "zllm_model_set_vocab_shard: rank %d of %d holds rows [%lld, %lld) of the output head", m->tp_rank,
+                   m->tp_size, (long long)a, (long long)b);
+    return ZLLM_E_ARG;
+  }
+  m->vocab0 = v0;
+  m->vocab_n = n;
+  return ZLLM_OK;
+}
+
 extern "C" int zllm_model_ready(zllm_model *m) {
   if (!m) return ZLLM_E_ARG;
   if (m->ready) return ZLLM_OK;
@@ -331,6 +352,12 @@ extern "C" int zllm_model_ready(zllm_model *m) {
         if (w && kq_type(w->m.type)) zllm_weight_gemm_ok(m->ctx, w);
   }
   CK(dalloc(&m->logits, (size_t)LB * c.vocab), "logits");
+  if (m->vocab_n) {
+    if (!m->out) { zllm_set_error(m->ctx, "model: a vocab-split head needs its own output matrix"); return fail(m, ZLLM_E_ARG); }
+    m->vpad = (c.vocab + m->tp_size - 1) / m->tp_size;
+    CK(dalloc(&m->lsend, (size_t)LB * m->vpad), "logits slice");
+    CK(dalloc(&m->lrecv, (size_t)m->tp_size * LB * m->vpad), "gathered logits");
+  }
   {
     // an F16 output head that passes of kHeadGemmMinRows or more logit rows will use (batched decode,
     // all-position logits) is also kept tiled for the tensor-core GEMM
@@ -506,11 +533,19 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want, bool distinct) {
     const int nl = want == 2 ? n : 1;
     const float *xl = want == 2 ? m->x : m->x + (int64_t)(n - 1) * E;
     RUN(launch_rmsnorm_quant(xl, m->out_norm, (int)E, nl, c.rms_eps, m->xb, m->xq, m->xd, m->xs, s, false));
+    // a vocab-split head writes this rank's slice, and the ranks gather every slice into the logits
+    float *lout = m->vocab_n ? m->lsend : m->logits;
+    const int64_t lstride = m->vocab_n ? m->vpad : c.vocab;
     if (nl >= kHeadGemmMinRows && m->head_tiles) {
       RUN(launch_gemm_prep_f32(m->xb, E, E, nl, m->head_b, s));
-      RUN(launch_gemm_f16_tiled(m->head_tiles, ow->m.rows, E, m->head_b, nl, m->logits, c.vocab, m->ctx->status_dev, s));
+      RUN(launch_gemm_f16_tiled(m->head_tiles, ow->m.rows, E, m->head_b, nl, lout, lstride, m->ctx->status_dev, s));
     } else {
-      RUN(gemv(m, ow, nl, m->logits, c.vocab, nullptr, m->xb, E));
+      RUN(gemv(m, ow, nl, lout, lstride, nullptr, m->xb, E));
+    }
+    if (m->vocab_n) {
+      const char *why = "";
+      RUN(tp_allgather(m->tp_comm, m->lsend, m->lrecv, (size_t)nl * m->vpad, s, &why));
+      RUN(launch_vocab_gather(m->lrecv, nl, m->vpad, c.vocab, m->tp_size, m->logits, s));
     }
     RUN(launch_argmax(m->logits, c.vocab, c.vocab, nl, m->d_arg, s, false));
   }
@@ -792,7 +827,8 @@ extern "C" void zllm_model_destroy(zllm_model *m) {
                   (void *)m->q, (void *)m->k, (void *)m->v, (void *)m->qr, (void *)m->att, (void *)m->g, (void *)m->u,
                   (void *)m->hb, (void *)m->qkv, (void *)m->gu, (void *)m->logits, (void *)m->part, (void *)m->xq, (void *)m->xd, (void *)m->xs,
                   (void *)m->d_tok, (void *)m->d_pos, (void *)m->d_seq, (void *)m->d_npos, (void *)m->d_arg,
-                  (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b, m->head_tiles, m->head_b})
+                  (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b, m->head_tiles, m->head_b,
+                  (void *)m->lsend, (void *)m->lrecv})
     if (p) cudaFree(p);
   if (m->h_io) cudaFreeHost(m->h_io);
   if (m->tp_ar) tp_ar_destroy(m->tp_ar, m->tp_comm, m->stream);   // after the graphs that use it

@@ -104,6 +104,42 @@ cudaError_t tp_allreduce_sum(void *comm, float *buf, size_t count, cudaStream_t 
 
 size_t tp_unique_id_bytes() { return sizeof(ncclUniqueId); }
 
+// every rank's `count` floats, in rank order, on every rank
+cudaError_t tp_allgather(void *comm, const float *send, float *recv, size_t count, cudaStream_t s, const char **why) {
+  const NcclApi &a = nccl();
+  if (!a.ok) { *why = a.why; return cudaErrorUnknown; }
+  const ncclResult_t r = a.all_gather(send, recv, count, ncclFloat32, static_cast<ncclComm_t>(comm), s);
+  if (r != ncclSuccess) { *why = nccl_err(r); return cudaErrorUnknown; }
+  return cudaSuccess;
+}
+
+namespace {
+// rank r's slice of a vocab split evenly over `size` ranks starts at r * V / size
+__device__ __forceinline__ int64_t vocab_start(int r, int64_t V, int size) { return (int64_t)r * V / size; }
+
+// logits [nl][V] from the gathered slices recv [size][nl][vpad]
+__global__ void vocab_gather_kernel(const float *__restrict__ recv, int nl, int64_t vpad, int64_t V, int size,
+                                    float *__restrict__ logits) {
+  const int64_t total = (int64_t)nl * V;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(e / V);
+    const int64_t v = e - (int64_t)t * V;
+    int r = (int)(v * size / V);
+    while (r + 1 < size && vocab_start(r + 1, V, size) <= v) r++;
+    while (r > 0 && vocab_start(r, V, size) > v) r--;
+    logits[e] = recv[((int64_t)r * nl + t) * vpad + (v - vocab_start(r, V, size))];
+  }
+}
+}  // namespace
+
+cudaError_t launch_vocab_gather(const float *recv, int nl, int64_t vpad, int64_t V, int size, float *logits,
+                                cudaStream_t s) {
+  const int64_t total = (int64_t)nl * V;
+  const int64_t grid = (total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096;
+  vocab_gather_kernel<<<(unsigned)grid, 256, 0, s>>>(recv, nl, vpad, V, size, logits);
+  return cudaGetLastError();
+}
+
 // ============================================================================ one-shot all-reduce
 namespace {
 

@@ -45,6 +45,7 @@ SIGNATURES = {
     "zllm_tp_unique_id": (i32, [vp, vp, sz]),
     "zllm_model_stream": (vp, [vp]),
     "zllm_model_tp_collective": (i32, [vp]),
+    "zllm_model_set_vocab_shard": (i32, [vp, i64, i64]),
     "zllm_model_set_tp": (i32, [vp, i32, i32, vp]),
     "zllm_matvec": (i32, [vp, vp, vp, i32, vp]),
     "zllm_rope_tables": (i32, [vp, i32, C.c_double, i32, vp, vp, vp]),

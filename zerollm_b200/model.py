@@ -77,6 +77,9 @@ class CudaModel:
             rank, size, uid = tp
             buf = C.create_string_buffer(bytes(uid), len(uid))
             self._check(self.lib.zllm_model_set_tp(self.h, int(rank), int(size), buf), "zllm_model_set_tp")
+            if cfg.get("vocab_shard") is not None:
+                v0, n = cfg["vocab_shard"]
+                self._check(self.lib.zllm_model_set_vocab_shard(self.h, int(v0), int(n)), "zllm_model_set_vocab_shard")
         self._load(weights)
         self._check(self.lib.zllm_model_ready(self.h), "zllm_model_ready")
         self._logits = np.zeros((self.logitsBatch if self.n_seq == 1 else max(self.logitsBatch, self.n_seq), self.vocab),

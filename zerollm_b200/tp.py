@@ -10,8 +10,10 @@ a model too large for one GPU the Megatron way:
 * attn_output and ffn_down are row-parallel: rank r keeps the matching input columns (cut at whole
   quantization blocks, so every shard is itself a valid GGUF matrix) and produces a partial sum,
   which the ranks add with one NCCL all-reduce after each (zllm_model_set_tp);
-* norms, the token embedding and the output head are replicated, so every rank ends a pass with the
-  same logits and the same greedy token.
+* the output head is split by vocab rows (rank r: rows [r*V/T, (r+1)*V/T)); every pass gathers
+  the ranks' logits slices, so every rank ends a pass with the same full logits and the same greedy
+  token; a head tied to the token embedding stays replicated;
+* norms and the token embedding are replicated.
 """
 from __future__ import annotations
 
@@ -67,6 +69,10 @@ def shard_model(cfg: dict, weights: dict, rank: int, size: int) -> tuple[dict, d
     f0, f1 = ffn_ranges(cfg, weights, size)[rank]
     lc = dict(cfg, n_head=Hl, n_head_kv=KVl, n_ff=f1 - f0)
     lw = {k: v for k, v in weights.items() if k != "layers"}
+    if weights.get("output") is not None:
+        v0, v1 = ranges(weights["output"]["rows"], size)[rank]
+        lw["output"] = shard_rows(weights["output"], v0, v1)
+        lc["vocab_shard"] = (v0, v1 - v0)
     layers = []
     for L in weights["layers"]:
         M = dict(L)
