@@ -219,29 +219,30 @@ __device__ double rms_scale(const float *x, int64_t n, double eps, int warp, int
 }
 
 // Quantize one token's f32 activation into shared memory; bit-exact with quantize_act_kernel
-// (quantizeAct, src/compute/ref-kernels.js:44-62).  Four lanes own a 32-value block, 8 values each,
-// so a 4096-value token keeps all 16 warps busy for one round.  With norm_w the values are first
-// f32(x * s * w) with s the RMSNorm scale (ref-kernels.js:305-310), as rmsnorm_quant_kernel writes them.
-template <int FMT, int NT>
-__device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w, double eps, uint8_t *sxq, float *ssc0,
-                                 float *ssc1, int warp, int lane) {
-  const double rs = norm_w ? rms_scale<NT>(x, k, eps, warp, lane) : 0.0;
-  const int nqb = (int)(k / 8);
+// (quantizeAct, src/compute/ref-kernels.js:44-62).  32 / V lanes own a 32-value block, V values each
+// (V = 8 when the token fits one round of the CTA's threads -- K <= 4096 -- else 16: fewer rounds of
+// the double-precision scale chain).  With norm_w the values are first f32(x * s * w) with s the
+// RMSNorm scale (ref-kernels.js:305-310), as rmsnorm_quant_kernel writes them.
+template <int FMT, int NT, int V>
+__device__ void quantize_rounds(const float *x, int64_t k, const float *norm_w, double rs, uint8_t *sxq, float *ssc0,
+                                float *ssc1, int warp, int lane) {
+  constexpr int LPB = 32 / V;                   // lanes per 32-value block
+  const int nqb = (int)(k / V);
   for (int base = warp * 32; base < nqb; base += NT) {
     const int qb = base + lane;
     const bool act = qb < nqb;
-    float v[8];
+    float v[V];
     if (act) {
-      const float4 *p = reinterpret_cast<const float4 *>(x + (int64_t)qb * 8);
+      const float4 *p = reinterpret_cast<const float4 *>(x + (int64_t)qb * V);
 #pragma unroll
-      for (int i = 0; i < 2; i++) {
+      for (int i = 0; i < V / 4; i++) {
         const float4 f = __ldg(p + i);
         v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
       }
       if (norm_w) {
-        const float4 *wp = reinterpret_cast<const float4 *>(norm_w + (int64_t)qb * 8);
+        const float4 *wp = reinterpret_cast<const float4 *>(norm_w + (int64_t)qb * V);
 #pragma unroll
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < V / 4; i++) {
           const float4 f = __ldg(wp + i);
           const float wv[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
@@ -250,23 +251,25 @@ __device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w,
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; i++) v[i] = 0.f;
+      for (int i = 0; i < V; i++) v[i] = 0.f;
     }
     float a = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
+    for (int i = 0; i < V; i++) {
       const float m = fabsf(v[i]);
       if (m > a) a = m;                         // NaN never raises amax (as `Math.abs(NaN) > amax`)
     }
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+#pragma unroll
+    for (int o = 1; o < LPB; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
     const double scale = __ddiv_rn((double)a, 127.0);
     const double inv = scale != 0.0 ? __ddiv_rn(1.0, scale) : 0.0;
-    uint32_t words[2] = {0, 0};
+    uint32_t words[V / 4];
+#pragma unroll
+    for (int i = 0; i < V / 4; i++) words[i] = 0u;
     int sum = 0;
     bool nan = false;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
+    for (int i = 0; i < V; i++) {
       const double r = round(__dmul_rn((double)v[i], inv));   // half away from zero
       const bool bad = !(r == r);
       const int q = bad ? 0 : (int)r;
@@ -274,17 +277,28 @@ __device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w,
       sum += q;
       words[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
     }
-    const int s16 = sum + __shfl_xor_sync(0xffffffffu, sum, 1);          // the 16-value group of lanes 2m, 2m + 1
-    const int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
-    const bool nan32 = ((__ballot_sync(0xffffffffu, nan) >> (lane & ~3)) & 0xfu) != 0;   // any NaN in the block
+    const int s16 = V == 16 ? sum : sum + __shfl_xor_sync(0xffffffffu, sum, 1);   // the 16-value group
+    int s32 = s16;
+#pragma unroll
+    for (int o = 16 / V; o < LPB; o <<= 1) s32 += __shfl_xor_sync(0xffffffffu, s32, o);
+    const bool nan32 = ((__ballot_sync(0xffffffffu, nan) >> (lane & ~(LPB - 1))) & ((1u << LPB) - 1u)) != 0;
     if (act) {
-      reinterpret_cast<uint2 *>(sxq)[qb] = make_uint2(words[0], words[1]);
+      if constexpr (V == 16) reinterpret_cast<uint4 *>(sxq)[qb] = make_uint4(words[0], words[1], words[2], words[3]);
+      else reinterpret_cast<uint2 *>(sxq)[qb] = make_uint2(words[0], words[1]);
       if constexpr (FMT == T_Q6_K) {
-        if ((lane & 1) == 0) put_group_off(ssc1, qb >> 1, s16);
+        if (V == 16 || (lane & 1) == 0) put_group_off(ssc1, qb * V / 16, s16);
       }
-      if ((lane & 3) == 0) put_block_scales<FMT>(ssc0, qb >> 2, __double2float_rn(scale), nan32 ? 0 : s32);
+      if ((lane & (LPB - 1)) == 0) put_block_scales<FMT>(ssc0, qb / LPB, __double2float_rn(scale), nan32 ? 0 : s32);
     }
   }
+}
+
+template <int FMT, int NT>
+__device__ void quantize_to_smem(const float *x, int64_t k, const float *norm_w, double eps, uint8_t *sxq, float *ssc0,
+                                 float *ssc1, int warp, int lane) {
+  const double rs = norm_w ? rms_scale<NT>(x, k, eps, warp, lane) : 0.0;
+  if (k / 8 <= NT) quantize_rounds<FMT, NT, 8>(x, k, norm_w, rs, sxq, ssc0, ssc1, warp, lane);
+  else quantize_rounds<FMT, NT, 16>(x, k, norm_w, rs, sxq, ssc0, ssc1, warp, lane);
 }
 
 // Stage one token's activation in shared memory (quantized here from f32, or copied when the
