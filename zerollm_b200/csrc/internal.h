@@ -116,7 +116,10 @@ cudaError_t launch_rmsnorm_quant(const float *x, const float *w, int n, int ntok
 cudaError_t launch_swiglu_quant(const float *gate, const float *up, int n, int ntok, int64_t stride, float *hb, int8_t *xq,
                                 float *xd, int32_t *xs, cudaStream_t s, bool pdl);
 cudaError_t launch_embed(const DevMatrix &m, const int32_t *tokens, int ntok, float *x, cudaStream_t s, bool pdl);
-cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, cudaStream_t s, bool pdl);
+// argmax in two stages over kArgmaxChunks chunks per token; pv / pi: [ntok][kArgmaxChunks] scratch
+constexpr int kArgmaxChunks = 64;
+cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, float *pv, int *pi,
+                          cudaStream_t s, bool pdl);
 cudaError_t launch_advance(const int32_t *arg, int n, int32_t *tok, int32_t *pos, int32_t *npos, int32_t *out,
                            int32_t *step, cudaStream_t s, bool pdl);
 

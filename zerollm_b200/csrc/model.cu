@@ -68,6 +68,8 @@ struct zllm_model {
   int64_t vocab0 = 0, vocab_n = 0;                       // vocab-split output head: this rank's rows (n 0: whole)
   int64_t vpad = 0;                                      // columns of a rank's padded logits slice
   float *lsend = nullptr, *lrecv = nullptr;              // this rank's slice [LB][vpad], all slices [size][LB][vpad]
+  float *arg_v = nullptr;                                // argmax chunk results [LB][kArgmaxChunks]
+  int32_t *arg_i = nullptr;
   int tp_rank = 0, tp_size = 1;
   int8_t *xq = nullptr;
   float *xd = nullptr;
@@ -352,6 +354,8 @@ extern "C" int zllm_model_ready(zllm_model *m) {
         if (w && kq_type(w->m.type)) zllm_weight_gemm_ok(m->ctx, w);
   }
   CK(dalloc(&m->logits, (size_t)LB * c.vocab), "logits");
+  CK(dalloc(&m->arg_v, (size_t)LB * kArgmaxChunks), "argmax scratch");
+  CK(dalloc(&m->arg_i, (size_t)LB * kArgmaxChunks), "argmax scratch");
   if (m->vocab_n) {
     if (!m->out) { zllm_set_error(m->ctx, "model: a vocab-split head needs its own output matrix"); return fail(m, ZLLM_E_ARG); }
     m->vpad = (c.vocab + m->tp_size - 1) / m->tp_size;
@@ -547,7 +551,7 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want, bool distinct) {
       RUN(tp_allgather(m->tp_comm, m->lsend, m->lrecv, (size_t)nl * m->vpad, s, &why));
       RUN(launch_vocab_gather(m->lrecv, nl, m->vpad, c.vocab, m->tp_size, m->logits, s));
     }
-    RUN(launch_argmax(m->logits, c.vocab, c.vocab, nl, m->d_arg, s, false));
+    RUN(launch_argmax(m->logits, c.vocab, c.vocab, nl, m->d_arg, m->arg_v, m->arg_i, s, false));
   }
 #undef RUN
   return cudaSuccess;
@@ -828,7 +832,7 @@ extern "C" void zllm_model_destroy(zllm_model *m) {
                   (void *)m->hb, (void *)m->qkv, (void *)m->gu, (void *)m->logits, (void *)m->part, (void *)m->xq, (void *)m->xd, (void *)m->xs,
                   (void *)m->d_tok, (void *)m->d_pos, (void *)m->d_seq, (void *)m->d_npos, (void *)m->d_arg,
                   (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b, m->head_tiles, m->head_b,
-                  (void *)m->lsend, (void *)m->lrecv})
+                  (void *)m->lsend, (void *)m->lrecv, (void *)m->arg_v, (void *)m->arg_i})
     if (p) cudaFree(p);
   if (m->h_io) cudaFreeHost(m->h_io);
   if (m->tp_ar) tp_ar_destroy(m->tp_ar, m->tp_comm, m->stream);   // after the graphs that use it

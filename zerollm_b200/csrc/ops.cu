@@ -148,35 +148,50 @@ __device__ float dequant_at(const DevMatrix &m, int64_t r, int64_t i) {
   return 0.f;
 }
 
+// CTA (t, c): columns [c * kEmbedCols, (c + 1) * kEmbedCols) of token t's row
+constexpr int kEmbedCols = 1024;
 __global__ void embed_kernel(const DevMatrix m, const int32_t *tokens, int ntok, float *x) {
   pdl_launch_dependents();
   pdl_wait();
   const int t = blockIdx.x;
   if (t >= ntok) return;
   const int64_t r = tokens[t];
-  for (int64_t i = threadIdx.x; i < m.cols; i += blockDim.x) x[(int64_t)t * m.cols + i] = dequant_at(m, r, i);
+  const int64_t i1 = min(m.cols, (int64_t)(blockIdx.y + 1) * kEmbedCols);
+  for (int64_t i = (int64_t)blockIdx.y * kEmbedCols + threadIdx.x; i < i1; i += blockDim.x)
+    x[(int64_t)t * m.cols + i] = dequant_at(m, r, i);
 }
 
 // ---------------------------------------------------------------------------- argmax
-__global__ void argmax_kernel(const float *logits, int64_t n, int64_t stride, int32_t *out) {
-  __shared__ float bv[32];
-  __shared__ int bi[32];
-  pdl_launch_dependents();
-  pdl_wait();
-  const float *l = logits + (int64_t)blockIdx.x * stride;
-  float best = -INFINITY;
-  int idx = -1;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = l[i];
-    if (v > best || idx < 0) { best = v; idx = (int)i; }
-  }
-  // first maximum wins: on equal values keep the smaller index
+// The first maximum of each token's logits (src/model/generate.js:4-10), in two stages: CTA (c, t)
+// reduces chunk c of token t's row, then one warp per token combines the chunks with the same rule,
+// which picks the largest value and, among equal ones, the smallest index -- so the answer does not
+// depend on the chunking.
+__device__ __forceinline__ void argmax_merge(float &best, int &idx, float ob, int oi) {
+  if (ob > best || (ob == best && oi >= 0 && (idx < 0 || oi < idx)) || (idx < 0 && oi >= 0)) { best = ob; idx = oi; }
+}
+__device__ __forceinline__ void argmax_warp(float &best, int &idx) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ob = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ob > best || (ob == best && oi < idx) || (idx < 0 && oi >= 0)) { best = ob; idx = oi; }
+    argmax_merge(best, idx, ob, oi);
   }
+}
+__global__ void argmax_part_kernel(const float *logits, int64_t n, int64_t stride, int64_t chunk, float *pv, int *pi) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int c = blockIdx.x, t = blockIdx.y;
+  const float *l = logits + (int64_t)t * stride;
+  const int64_t i1 = min(n, (int64_t)(c + 1) * chunk);
+  float best = -INFINITY;
+  int idx = -1;
+  for (int64_t i = (int64_t)c * chunk + threadIdx.x; i < i1; i += blockDim.x) {
+    const float v = l[i];
+    if (v > best || idx < 0) { best = v; idx = (int)i; }
+  }
+  argmax_warp(best, idx);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
   __syncthreads();
@@ -184,14 +199,19 @@ __global__ void argmax_kernel(const float *logits, int64_t n, int64_t stride, in
     const int nw = blockDim.x >> 5;
     best = lane < nw ? bv[lane] : -INFINITY;
     idx = lane < nw ? bi[lane] : -1;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-      if (ob > best || (ob == best && oi >= 0 && (idx < 0 || oi < idx))) { best = ob; idx = oi; }
-    }
-    if (lane == 0) out[blockIdx.x] = idx;
+    argmax_warp(best, idx);
+    if (lane == 0) { pv[(int64_t)t * gridDim.x + c] = best; pi[(int64_t)t * gridDim.x + c] = idx; }
   }
+}
+__global__ void argmax_final_kernel(const float *pv, const int *pi, int nchunk, int32_t *out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x, lane = threadIdx.x;
+  float best = -INFINITY;
+  int idx = -1;
+  for (int c = lane; c < nchunk; c += 32) argmax_merge(best, idx, pv[(int64_t)t * nchunk + c], pi[(int64_t)t * nchunk + c]);
+  argmax_warp(best, idx);
+  if (lane == 0) out[t] = idx;
 }
 
 // ---------------------------------------------------------------------------- launchers
@@ -231,7 +251,7 @@ cudaError_t launch_swiglu_quant(const float *gate, const float *up, int n, int n
 
 cudaError_t launch_embed(const DevMatrix &m, const int32_t *tokens, int ntok, float *x, cudaStream_t s, bool pdl) {
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = cfg_of(dim3(ntok), dim3(256), 0, s, pdl, attr);
+  cudaLaunchConfig_t cfg = cfg_of(dim3(ntok, (unsigned)((m.cols + kEmbedCols - 1) / kEmbedCols)), dim3(256), 0, s, pdl, attr);
   return cudaLaunchKernelEx(&cfg, embed_kernel, m, tokens, ntok, x);
 }
 
@@ -262,10 +282,15 @@ cudaError_t launch_advance(const int32_t *arg, int n, int32_t *tok, int32_t *pos
   return cudaLaunchKernelEx(&cfg, advance_kernel, arg, n, tok, pos, npos, out, step);
 }
 
-cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, cudaStream_t s, bool pdl) {
+cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, float *pv, int *pi,
+                          cudaStream_t s, bool pdl) {
+  const int64_t chunk = (n + kArgmaxChunks - 1) / kArgmaxChunks;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = cfg_of(dim3(ntok), dim3(1024), 0, s, pdl, attr);
-  return cudaLaunchKernelEx(&cfg, argmax_kernel, logits, n, stride, out);
+  cudaLaunchConfig_t cfg = cfg_of(dim3(kArgmaxChunks, ntok), dim3(256), 0, s, pdl, attr);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, argmax_part_kernel, logits, n, stride, chunk, pv, pi);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg2 = cfg_of(dim3(ntok), dim3(32), 0, s, false, attr);
+  return cudaLaunchKernelEx(&cfg2, argmax_final_kernel, (const float *)pv, (const int *)pi, kArgmaxChunks, out);
 }
 
 }  // namespace zllm
