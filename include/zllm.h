@@ -272,6 +272,20 @@ int zllm_model_kv_get(zllm_model *m, int seq, int layer, int is_v, int n, float 
 int zllm_model_kv_set(zllm_model *m, int seq, int layer, int is_v, int n, const float *in);
 /* After the KV regions were filled (kvSet): the sequence now holds n positions (restorePrefix, pool.js:244-247). */
 int zllm_model_restore_prefix(zllm_model *m, int seq, int n);
+/* Sampling candidates on the device (src/sampling/sampler.js:20-42 topKSelect, after the penalties of
+ * :98-112): the k (<= 256) largest logits of each of the first `rows` rows of the last pass's logits,
+ * sorted by value descending then index ascending, into ids_host / vals_host [rows][k]; entries past
+ * the finite values of a row have id -1.  pen_tok / pen_cnt: the n_pen (<= 4096) distinct recent
+ * tokens and their counts; each gets l/repeat_penalty (l > 0) or l*repeat_penalty, minus
+ * count*frequency + presence, in double, stored as f32.  The softmax, min-p, top-p and the draw
+ * (sampler.js:116-148) run on the k pairs in the caller.  A pass with want 0 and no logits_host
+ * keeps the logits on the device for this call. */
+int zllm_model_topk(zllm_model *m, int rows, int k, const int32_t *pen_tok, const int32_t *pen_cnt, int n_pen,
+                    double repeat_penalty, double frequency, double presence, int32_t *ids_host, float *vals_host);
+/* The same selection on host buffers (kernel-level, for tests): rows x n logits (n <= 327680). */
+int zllm_topk(zllm_ctx *c, const float *logits_host, int rows, int64_t n, int k, const int32_t *pen_tok,
+              const int32_t *pen_cnt, int n_pen, double repeat_penalty, double frequency, double presence,
+              int32_t *ids_host, float *vals_host);
 /* Device-resident prefix slot: save the first n positions of a sequence's KV, restore them (a byte
  * copy) into a sequence, which then holds those n positions. */
 int zllm_model_slot_save(zllm_model *m, int seq, int n);

@@ -298,3 +298,45 @@ class OracleModel:
     def kv_set(self, layer: int, is_v: int, n: int, data: np.ndarray):
         data = np.ascontiguousarray(data, np.float32)
         lib().zo_model_kv_set(self._m, layer, is_v, n, _p(data))
+
+
+# ------------------------------------------------------------------------------------ sampling
+# src/sampling/sampler.js, restated in numpy / Python doubles (the checker of the device top-k).
+def penalize(logits: np.ndarray, history, repeat_penalty=1.0, frequency=0.0, presence=0.0, last_n=64) -> np.ndarray:
+    """sampler.js:98-112: a copy of the f32 logits with each distinct token of the last ``last_n``
+    of ``history`` penalised in double and stored back as f32."""
+    out = np.array(logits, np.float32, copy=True)
+    counts = {}
+    for t in list(history)[max(0, len(history) - last_n):]:
+        counts[int(t)] = counts.get(int(t), 0) + 1
+    for t, c in counts.items():
+        l = float(out[t])
+        v = (l / repeat_penalty if l > 0 else l * repeat_penalty) if repeat_penalty != 1 else l
+        v -= c * frequency + presence
+        out[t] = np.float32(v)
+    return out
+
+
+def topk_select(logits: np.ndarray, k: int):
+    """sampler.js:20-42: the k largest (ids, values), value descending then index ascending
+    (the order the size-k heap plus its final sort produce); NaN values are left out."""
+    l = np.asarray(logits, np.float32)
+    idx = np.nonzero(~np.isnan(l))[0]
+    order = idx[np.lexsort((idx, -l[idx].astype(np.float64)))][:k]
+    return order.astype(np.int32), l[order]
+
+
+def mulberry32(seed: int):
+    """src/util/rng.js:4-13 (a second statement, in numpy uint32, of the published generator)."""
+    a = np.uint32(seed & 0xFFFFFFFF)
+
+    def rand():
+        nonlocal a
+        with np.errstate(over="ignore"):
+            a = np.uint32(a + np.uint32(0x6D2B79F5))
+            t = a
+            t = np.uint32(np.uint32(t ^ (t >> np.uint32(15))) * np.uint32(t | np.uint32(1)))
+            t = np.uint32(t ^ np.uint32(t + np.uint32(np.uint32(t ^ (t >> np.uint32(7))) * np.uint32(t | np.uint32(61)))))
+            return float(np.uint32(t ^ (t >> np.uint32(14)))) / 4294967296.0
+
+    return rand

@@ -120,6 +120,15 @@ cudaError_t launch_embed(const DevMatrix &m, const int32_t *tokens, int ntok, fl
 constexpr int kArgmaxChunks = 64;
 cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, float *pv, int *pi,
                           cudaStream_t s, bool pdl);
+// the k best logits per row (sample.cu): kTopkChunks chunks of at most kTopkSmem bytes each, k <= kTopkMax,
+// at most kTopkMaxPen penalised tokens; pv / pi: [ntok][kTopkChunks][k] scratch; out: [ntok][k]
+constexpr int kTopkChunks = 32;
+constexpr int kTopkMax = 256;
+constexpr int kTopkMaxPen = 4096;
+constexpr int64_t kTopkSmem = 40 * 1024;
+cudaError_t launch_topk(const float *logits, int64_t n, int64_t stride, int ntok, int k, const int32_t *pen_tok,
+                        const int32_t *pen_cnt, int n_pen, double rp, double freq, double pres, float *pv, int *pi,
+                        float *out_v, int32_t *out_i, cudaStream_t s);
 cudaError_t launch_advance(const int32_t *arg, int n, int32_t *tok, int32_t *pos, int32_t *npos, int32_t *out,
                            int32_t *step, cudaStream_t s, bool pdl);
 

@@ -70,6 +70,12 @@ struct zllm_model {
   float *lsend = nullptr, *lrecv = nullptr;              // this rank's slice [LB][vpad], all slices [size][LB][vpad]
   float *arg_v = nullptr;                                // argmax chunk results [LB][kArgmaxChunks]
   int32_t *arg_i = nullptr;
+  int lb = 0;                                            // rows of the logits buffer
+  float *topk_pv = nullptr;                              // top-k chunk candidates [LB][kTopkChunks][kTopkMax]
+  int32_t *topk_pi = nullptr;
+  float *topk_v = nullptr;                               // top-k results [LB][kTopkMax]
+  int32_t *topk_i = nullptr;
+  int32_t *pen = nullptr;                                // penalised tokens and their counts [2][kTopkMaxPen]
   int tp_rank = 0, tp_size = 1;
   int8_t *xq = nullptr;
   float *xd = nullptr;
@@ -356,6 +362,12 @@ extern "C" int zllm_model_ready(zllm_model *m) {
   CK(dalloc(&m->logits, (size_t)LB * c.vocab), "logits");
   CK(dalloc(&m->arg_v, (size_t)LB * kArgmaxChunks), "argmax scratch");
   CK(dalloc(&m->arg_i, (size_t)LB * kArgmaxChunks), "argmax scratch");
+  m->lb = LB;
+  CK(dalloc(&m->topk_pv, (size_t)LB * kTopkChunks * kTopkMax), "top-k scratch");
+  CK(dalloc(&m->topk_pi, (size_t)LB * kTopkChunks * kTopkMax), "top-k scratch");
+  CK(dalloc(&m->topk_v, (size_t)LB * kTopkMax), "top-k scratch");
+  CK(dalloc(&m->topk_i, (size_t)LB * kTopkMax), "top-k scratch");
+  CK(dalloc(&m->pen, (size_t)2 * kTopkMaxPen), "top-k scratch");
   if (m->vocab_n) {
     if (!m->out) { zllm_set_error(m->ctx, "model: a vocab-split head needs its own output matrix"); return fail(m, ZLLM_E_ARG); }
     m->vpad = (c.vocab + m->tp_size - 1) / m->tp_size;
@@ -774,6 +786,38 @@ extern "C" int zllm_model_kv_set(zllm_model *m, int seq, int layer, int is_v, in
   return kv_io(m, seq, layer, is_v, n, const_cast<float *>(in), false);
 }
 
+// The k best logits of each of the last pass's first `rows` rows, sorted (src/sampling/sampler.js:20-42), after the
+// penalties of :98-112 for the n_pen distinct tokens pen_tok with counts pen_cnt; only the k pairs are copied out.
+extern "C" int zllm_model_topk(zllm_model *m, int rows, int k, const int32_t *pen_tok, const int32_t *pen_cnt, int n_pen,
+                               double repeat_penalty, double frequency, double presence, int32_t *ids_host,
+                               float *vals_host) {
+  if (!m || !ids_host || !vals_host || k <= 0 || k > kTopkMax || n_pen < 0 || n_pen > kTopkMaxPen ||
+      (n_pen && (!pen_tok || !pen_cnt)))
+    return ZLLM_E_ARG;
+  if (m->closed) { zllm_set_error(m->ctx, "model is closed"); return ZLLM_E_STATE; }
+  if (m->failed) return ZLLM_E_STATE;
+  if (!m->ready) { int rc = zllm_model_ready(m); if (rc) return rc; }
+  if (rows <= 0 || rows > m->lb || k > m->c.vocab ||
+      ((int64_t)m->c.vocab + kTopkChunks - 1) / kTopkChunks * (int64_t)sizeof(float) > kTopkSmem)
+    return ZLLM_E_ARG;
+  for (int j = 0; j < n_pen; j++)
+    if (pen_tok[j] < 0 || pen_tok[j] >= m->c.vocab) {
+      zllm_set_error(m->ctx, "token id %d out of range", pen_tok[j]);
+      return ZLLM_E_TOKEN;
+    }
+  cudaStream_t s = m->stream;
+  if (n_pen) {
+    CK(cudaMemcpyAsync(m->pen, pen_tok, sizeof(int32_t) * n_pen, cudaMemcpyHostToDevice, s), "penalties");
+    CK(cudaMemcpyAsync(m->pen + kTopkMaxPen, pen_cnt, sizeof(int32_t) * n_pen, cudaMemcpyHostToDevice, s), "penalties");
+  }
+  CK(launch_topk(m->logits, m->c.vocab, m->c.vocab, rows, k, m->pen, m->pen + kTopkMaxPen, n_pen, repeat_penalty, frequency,
+                 presence, m->topk_pv, m->topk_pi, m->topk_v, m->topk_i, s), "top-k");
+  CK(cudaMemcpyAsync(ids_host, m->topk_i, sizeof(int32_t) * rows * k, cudaMemcpyDeviceToHost, s), "top-k");
+  CK(cudaMemcpyAsync(vals_host, m->topk_v, sizeof(float) * rows * k, cudaMemcpyDeviceToHost, s), "top-k");
+  CK(cudaStreamSynchronize(s), "top-k");
+  return ZLLM_OK;
+}
+
 extern "C" int zllm_model_restore_prefix(zllm_model *m, int seq, int n) {
   if (!m || seq < 0 || seq >= m->c.n_seq || n < 0 || n > m->c.ctx) return ZLLM_E_ARG;
   m->pos[seq] = n;                                  // src/compute/pool.js:244-247: the model now holds n positions
@@ -832,7 +876,8 @@ extern "C" void zllm_model_destroy(zllm_model *m) {
                   (void *)m->hb, (void *)m->qkv, (void *)m->gu, (void *)m->logits, (void *)m->part, (void *)m->xq, (void *)m->xd, (void *)m->xs,
                   (void *)m->d_tok, (void *)m->d_pos, (void *)m->d_seq, (void *)m->d_npos, (void *)m->d_arg,
                   (void *)m->counters, (void *)m->d_gen, (void *)m->d_step, m->gemm_b, m->head_tiles, m->head_b,
-                  (void *)m->lsend, (void *)m->lrecv, (void *)m->arg_v, (void *)m->arg_i})
+                  (void *)m->lsend, (void *)m->lrecv, (void *)m->arg_v, (void *)m->arg_i,
+                  (void *)m->topk_pv, (void *)m->topk_pi, (void *)m->topk_v, (void *)m->topk_i, (void *)m->pen})
     if (p) cudaFree(p);
   if (m->h_io) cudaFreeHost(m->h_io);
   if (m->tp_ar) tp_ar_destroy(m->tp_ar, m->tp_comm, m->stream);   // after the graphs that use it

@@ -68,6 +68,8 @@ SIGNATURES = {
     "zllm_model_kv_get": (i32, [vp, i32, i32, i32, i32, vp]),
     "zllm_model_kv_set": (i32, [vp, i32, i32, i32, i32, vp]),
     "zllm_model_restore_prefix": (i32, [vp, i32, i32]),
+    "zllm_model_topk": (i32, [vp, i32, i32, vp, vp, i32, C.c_double, C.c_double, C.c_double, vp, vp]),
+    "zllm_topk": (i32, [vp, vp, i32, C.c_int64, i32, vp, vp, i32, C.c_double, C.c_double, C.c_double, vp, vp]),
     "zllm_model_slot_save": (i32, [vp, i32, i32]),
     "zllm_model_slot_restore": (i32, [vp, i32]),
     "zllm_model_set_graphs": (i32, [vp, i32]),

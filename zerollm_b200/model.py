@@ -143,16 +143,20 @@ class CudaModel:
 
     def forwardBatch(self, tokens, logits=True, seq: int = 0):
         """B tokens at the next positions in one pass; logits True/'last' -> [vocab] of the last token,
-        'all' -> [B][vocab], False/'none' -> None (pool.js:145-160)."""
+        'all' -> [B][vocab], False/'none' -> None (pool.js:145-160).  'device' / 'device-all' compute
+        the same logits but leave them on the GPU (for zerollm_b200.sampler) and return None."""
         self._guard()
         toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64).astype(np.int32))
         B = toks.size
-        want = 0 if logits is False or logits == "none" else 2 if logits == "all" else 1
+        want = 0 if logits is False or logits == "none" else 2 if logits in ("all", "device-all") else 1
+        host = want and logits not in ("device", "device-all")
         rc = self.lib.zllm_model_forward(self.h, seq, toks.ctypes.data_as(C.c_void_p), B, want,
-                                         self._logits.ctypes.data_as(C.c_void_p) if want else None,
-                                         self._argmax.ctypes.data_as(C.c_void_p) if want else None)
+                                         self._logits.ctypes.data_as(C.c_void_p) if host else None,
+                                         self._argmax.ctypes.data_as(C.c_void_p) if host else None)
         self._run(rc, "forward")
         self._tokens[seq].extend(int(t) for t in toks)
+        if not host:
+            return None
         if want == 2:
             return self._logits[:B]
         return self._logits[0] if want else None
