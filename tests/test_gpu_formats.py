@@ -32,7 +32,7 @@ def _file(tmp_path, seed=6):
 def test_model_from_gguf_matches_memory(tmp_path):
     cfg, w, p = _file(tmp_path)
     cfg2, w2 = gguf.load_model(p)
-    a = CudaModel.create(cfg, w, ctx=64, kv="f16")
+    a = CudaModel.create(cfg, w, ctx=64, kv="f16", max_batch=32)
     b = CudaModel.create(cfg2, w2, ctx=64, kv="f16")
     la = a.forwardBatch(PREFIX[:8], logits="all").copy()
     lb = b.forwardBatch(PREFIX[:8], logits="all").copy()
@@ -46,13 +46,13 @@ def test_model_from_gguf_matches_memory(tmp_path):
 def test_prefix_cache_through_the_device(tmp_path):
     cfg, w, p = _file(tmp_path, seed=11)
     cfg, w = gguf.load_model(p)
-    a = CudaModel.create(cfg, w, ctx=64, kv="f16")
+    a = CudaModel.create(cfg, w, ctx=64, kv="f16", max_batch=32)
     cache = PrefixCache(str(tmp_path / "kv"), model_fingerprint(p, kernel_flavour(a)))
     a.forwardBatch(PREFIX, logits=False)
     cache.save(a, PREFIX)
     for t in REST:
         want = a.forward(t).copy()
-    b = CudaModel.create(cfg, w, ctx=64, kv="f16")
+    b = CudaModel.create(cfg, w, ctx=64, kv="f16", max_batch=32)
     assert cache.load(b, PREFIX)
     assert b.pos == len(PREFIX) and b.tokens == PREFIX
     for l in range(cfg["n_layer"]):
@@ -65,10 +65,10 @@ def test_prefix_cache_through_the_device(tmp_path):
     f = cache.file(PREFIX)
     good = open(f, "rb").read()
     open(f, "wb").write(good[:-1])
-    c = CudaModel.create(cfg, w, ctx=64, kv="f16")
+    c = CudaModel.create(cfg, w, ctx=64, kv="f16", max_batch=32)
     assert not cache.load(c, PREFIX)
     assert c.pos == 0
-    fresh = CudaModel.create(cfg, w, ctx=64, kv="f16")
+    fresh = CudaModel.create(cfg, w, ctx=64, kv="f16", max_batch=32)
     assert np.array_equal(c.forward(5), fresh.forward(5))
     for m in (a, b, c, fresh):
         m.close()
