@@ -120,9 +120,9 @@ cudaError_t launch_embed(const DevMatrix &m, const int32_t *tokens, int ntok, fl
 constexpr int kArgmaxChunks = 64;
 cudaError_t launch_argmax(const float *logits, int64_t n, int64_t stride, int ntok, int32_t *out, float *pv, int *pi,
                           cudaStream_t s, bool pdl);
-// the k best logits per row (sample.cu): kTopkChunks chunks of at most kTopkSmem bytes each, k <= kTopkMax,
+// the k best logits per row (sample.cu): kTopkChunks chunks of at most kTopkSmem bytes (value + index) each, k <= kTopkMax,
 // at most kTopkMaxPen penalised tokens; pv / pi: [ntok][kTopkChunks][k] scratch; out: [ntok][k]
-constexpr int kTopkChunks = 32;
+constexpr int kTopkChunks = 64;              // <= 64: the merge warp owns two lists per lane
 constexpr int kTopkMax = 256;
 constexpr int kTopkMaxPen = 4096;
 constexpr int64_t kTopkSmem = 40 * 1024;

@@ -798,7 +798,7 @@ extern "C" int zllm_model_topk(zllm_model *m, int rows, int k, const int32_t *pe
   if (m->failed) return ZLLM_E_STATE;
   if (!m->ready) { int rc = zllm_model_ready(m); if (rc) return rc; }
   if (rows <= 0 || rows > m->lb || k > m->c.vocab ||
-      ((int64_t)m->c.vocab + kTopkChunks - 1) / kTopkChunks * (int64_t)sizeof(float) > kTopkSmem)
+      ((int64_t)m->c.vocab + kTopkChunks - 1) / kTopkChunks * (int64_t)(sizeof(float) + sizeof(int)) > kTopkSmem)
     return ZLLM_E_ARG;
   for (int j = 0; j < n_pen; j++)
     if (pen_tok[j] < 0 || pen_tok[j] >= m->c.vocab) {

@@ -11,9 +11,9 @@
 // and the seeded draw over the k candidates stay with the caller (host doubles).
 //
 // Two stages: CTA (c, t) loads chunk c of row t into shared memory, applies the penalties that
-// fall in the chunk, and extracts its k best in k block-wide rounds (each round takes the best
-// value strictly after the previous one in the order above); one CTA per row then merges the
-// kTopkChunks x k candidates the same way.
+// fall in the chunk, and each thread sorts its own few elements; k block-wide rounds then take the
+// best of the threads' list heads (the winner's owner moves on), giving the chunk's k best in
+// order.  One warp per row merges the kTopkChunks sorted lists the same way, by shuffles alone.
 #include "capi_internal.h"
 #include "common.cuh"
 #include "internal.h"
@@ -68,65 +68,77 @@ __device__ __forceinline__ void block_best(float &bv, int &bi, float *wv, int *w
 __global__ void topk_part_kernel(const float *logits, int64_t n, int64_t stride, int64_t chunk, int k,
                                  const int32_t *pen_tok, const int32_t *pen_cnt, int n_pen, double rp, double freq,
                                  double pres, float *pv, int *pi) {
-  extern __shared__ float sv[];
+  extern __shared__ float sv[];                          // [chunk] values, then [chunk] indices
+  int *si = (int *)(sv + chunk);
   __shared__ float wv[33];
   __shared__ int wi[33];
-  const int c = blockIdx.x, t = blockIdx.y;
+  const int c = blockIdx.x, t = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const float *l = logits + (int64_t)t * stride;
   const int64_t i0 = (int64_t)c * chunk, i1 = min(n, i0 + chunk);
   const int len = i1 > i0 ? (int)(i1 - i0) : 0;
-  for (int j = threadIdx.x; j < len; j += blockDim.x) sv[j] = l[i0 + j];
+  for (int j = tid; j < len; j += nt) sv[j] = l[i0 + j];
   __syncthreads();
-  for (int j = threadIdx.x; j < n_pen; j += blockDim.x) {
+  for (int j = tid; j < n_pen; j += nt) {
     const int tok = pen_tok[j];
     if (tok >= i0 && tok < i1) sv[tok - i0] = penalize(l[tok], pen_cnt[j], rp, freq, pres);
   }
   __syncthreads();
+  // each thread sorts its own elements (positions tid, tid + nt, ...) in the order above, NaN last
+  const int cnt = tid < len ? (len - tid + nt - 1) / nt : 0;
+  for (int q = 0; q < cnt; q++) {
+    const int j = tid + q * nt;
+    const float v = sv[j];
+    const int iv = v != v ? -1 : (int)(i0 + j);
+    int p = q;
+    while (p > 0 && cand_before(v, iv, sv[tid + (p - 1) * nt], si[tid + (p - 1) * nt])) {
+      sv[tid + p * nt] = sv[tid + (p - 1) * nt];
+      si[tid + p * nt] = si[tid + (p - 1) * nt];
+      p--;
+    }
+    sv[tid + p * nt] = v;
+    si[tid + p * nt] = iv;
+  }
   float *ov = pv + ((int64_t)t * gridDim.x + c) * k;
   int *oi = pi + ((int64_t)t * gridDim.x + c) * k;
-  float prev_v = 0.f;
-  int prev_i = -1;
+  // each round the block takes the best of the threads' list heads; the owner (indices are
+  // unique) moves to its next element
+  int p = 0;
   for (int r = 0; r < k; r++) {
-    float bv = -INFINITY;
-    int bi = -1;
-    if (r == 0 || prev_i >= 0)
-      for (int j = threadIdx.x; j < len; j += blockDim.x) {
-        const float v = sv[j];
-        const int i = (int)(i0 + j);
-        if (v != v) continue;
-        if (r > 0 && !cand_before(prev_v, prev_i, v, i)) continue;
-        if (cand_before(v, i, bv, bi)) { bv = v; bi = i; }
-      }
+    float hv = -INFINITY;
+    int hi = -1;
+    if (p < cnt) { hv = sv[tid + p * nt]; hi = si[tid + p * nt]; }
+    float bv = hv;
+    int bi = hi;
     block_best(bv, bi, wv, wi);
-    if (threadIdx.x == 0) { ov[r] = bv; oi[r] = bi; }
-    prev_v = bv;
-    prev_i = bi;
+    if (tid == 0) { ov[r] = bv; oi[r] = bi; }
+    if (bi >= 0 && bi == hi) p++;
   }
 }
 
-__global__ void topk_final_kernel(const float *pv, const int *pi, int m, int k, float *out_v, int32_t *out_i) {
-  __shared__ float wv[33];
-  __shared__ int wi[33];
-  const int t = blockIdx.x;
-  const float *cv = pv + (int64_t)t * m;
-  const int *ci = pi + (int64_t)t * m;
-  float prev_v = 0.f;
-  int prev_i = -1;
+// One warp per row merges the nchunk (<= 64) sorted lists of k: lane L owns lists L and L + 32.
+__global__ void topk_final_kernel(const float *pv, const int *pi, int nchunk, int k, float *out_v, int32_t *out_i) {
+  const int t = blockIdx.x, lane = threadIdx.x;
+  const float *cv = pv + (int64_t)t * nchunk * k;
+  const int *ci = pi + (int64_t)t * nchunk * k;
+  const int la = lane, lb = lane + 32;
+  int pa = 0, pb = 0;
   for (int r = 0; r < k; r++) {
-    float bv = -INFINITY;
-    int bi = -1;
-    if (r == 0 || prev_i >= 0)
-      for (int j = threadIdx.x; j < m; j += blockDim.x) {
-        const int i = ci[j];
-        if (i < 0) continue;
-        const float v = cv[j];
-        if (r > 0 && !cand_before(prev_v, prev_i, v, i)) continue;
-        if (cand_before(v, i, bv, bi)) { bv = v; bi = i; }
-      }
-    block_best(bv, bi, wv, wi);
-    if (threadIdx.x == 0) { out_v[(int64_t)t * k + r] = bv; out_i[(int64_t)t * k + r] = bi; }
-    prev_v = bv;
-    prev_i = bi;
+    float va = -INFINITY, vb = -INFINITY;
+    int ia = -1, ib = -1;
+    if (la < nchunk && pa < k) { va = cv[la * k + pa]; ia = ci[la * k + pa]; }
+    if (lb < nchunk && pb < k) { vb = cv[lb * k + pb]; ib = ci[lb * k + pb]; }
+    const bool from_b = cand_before(vb, ib, va, ia);
+    float bv = from_b ? vb : va;
+    int bi = from_b ? ib : ia;
+    const int mine = bi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (cand_before(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { out_v[(int64_t)t * k + r] = bv; out_i[(int64_t)t * k + r] = bi; }
+    if (bi >= 0 && bi == mine) { if (from_b) pb++; else pa++; }
   }
 }
 
@@ -135,12 +147,12 @@ cudaError_t launch_topk(const float *logits, int64_t n, int64_t stride, int ntok
                         float *out_v, int32_t *out_i, cudaStream_t s) {
   if (ntok <= 0 || k <= 0 || k > kTopkMax || n <= 0) return cudaErrorInvalidValue;
   const int64_t chunk = (n + kTopkChunks - 1) / kTopkChunks;
-  if (chunk * (int64_t)sizeof(float) > kTopkSmem) return cudaErrorInvalidValue;
-  topk_part_kernel<<<dim3(kTopkChunks, ntok), 256, chunk * sizeof(float), s>>>(logits, n, stride, chunk, k, pen_tok, pen_cnt,
-                                                                               n_pen, rp, freq, pres, pv, pi);
+  if (chunk * (int64_t)(sizeof(float) + sizeof(int)) > kTopkSmem) return cudaErrorInvalidValue;
+  topk_part_kernel<<<dim3(kTopkChunks, ntok), 256, chunk * (sizeof(float) + sizeof(int)), s>>>(
+      logits, n, stride, chunk, k, pen_tok, pen_cnt, n_pen, rp, freq, pres, pv, pi);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  topk_final_kernel<<<ntok, 256, 0, s>>>(pv, pi, kTopkChunks * k, k, out_v, out_i);
+  topk_final_kernel<<<ntok, 32, 0, s>>>(pv, pi, kTopkChunks, k, out_v, out_i);
   return cudaGetLastError();
 }
 
@@ -155,7 +167,7 @@ extern "C" int zllm_topk(zllm_ctx *c, const float *logits_host, int rows, int64_
   if (!c) return ZLLM_E_ARG;
   if (!logits_host || !ids_host || !vals_host || rows < 1 || n < 1 || k < 1 || k > kTopkMax || k > n || n_pen < 0 ||
       n_pen > kTopkMaxPen || (n_pen && (!pen_tok || !pen_cnt)) ||
-      (n + kTopkChunks - 1) / kTopkChunks * (int64_t)sizeof(float) > kTopkSmem) {
+      (n + kTopkChunks - 1) / kTopkChunks * (int64_t)(sizeof(float) + sizeof(int)) > kTopkSmem) {
     zllm_set_error(c, "zllm_topk: bad argument");
     return ZLLM_E_ARG;
   }
