@@ -234,3 +234,21 @@ def test_prefix_cache_prune_and_fingerprint(tmp_path):
     mp.write_bytes(b"x" * 10)
     fp = model_fingerprint(str(mp), "cuda/kv-f16")
     assert fp.startswith("model.gguf|10|") and fp.endswith("|cuda/kv-f16")
+
+
+def test_gguf_llama_tied_and_missing_keys(tmp_path):
+    cfg = synth.tiny(arch="llama", qk_norm=False, tied=True)
+    w = synth.make_model(cfg, seed=3, quant="q8_0", dist="tame")
+    p = str(tmp_path / "llama.gguf")
+    gguf.write_gguf(p, cfg, w)
+    c, w2 = gguf.load_model(p)
+    assert c["arch"] == "llama" and c["rope_type"] == "norm"       # config.js: llama -> 'norm', others 'neox'
+    assert c["tied"] and w2["output"] is None and not c["qk_norm"]
+    assert w2["layers"][0]["q_norm"] is None and w2["layers"][0]["wq"]["type"] == ggml.Q8_0
+    g = gguf.read_gguf(p)
+    del g.metadata["llama.block_count"]
+    with pytest.raises(ValueError, match="missing metadata key llama.block_count"):
+        gguf.model_config(g)
+    g.metadata["general.architecture"] = "mamba"
+    with pytest.raises(ValueError, match='architecture "mamba" is not supported'):
+        gguf.model_config(g)
