@@ -155,14 +155,15 @@ int zllm_attn_decode(zllm_ctx *ctx, const zllm_attn_geom *g, const float *q, con
 
 /* zllm_attn_decode with the same arguments and results, but the call allocates no device memory:
  * its scratch (split-context partials and merge counters) is a fixed array compiled into the
- * library, 4 MiB of partials + 4096 counters, held by every GPU that loads the library until the
- * process exits.  For callers that may not allocate during a step (all free HBM already handed to
+ * library, 4 MiB of partials + 4096 counters, held by every GPU on which a context was created
+ * until the process exits.  For callers that may not allocate during a step (all free HBM already handed to
  * a KV pool; device memory owned by another allocator, where a cudaFree would synchronize the
  * device).  A call needing more than 4 MiB of partials (nseq * n_head_kv * splits * group *
  * (head_dim + 2) floats) or more than 4096 (sequence, KV head) pairs returns ZLLM_E_ARG without
  * launching.  All calls on one device share the array: calls that overlap in time race, so order
- * them (one stream, or events).  The first call through a context looks up the array's address
- * (cudaGetSymbolAddress on the context's device).  No counterpart in the reference. */
+ * them (one stream, or events).  zllm_init loads the array on its device and looks up its address
+ * (cudaGetSymbolAddress), so the memory is taken when the first context on a device is created and
+ * no call of this function allocates, the first one included.  No counterpart in the reference. */
 int zllm_attn_decode_noalloc(zllm_ctx *ctx, const zllm_attn_geom *g, const float *q, const void *kcache,
                              const void *vcache, const int32_t *npos, int nseq, int max_pos, float *out, void *stream);
 

@@ -80,10 +80,11 @@ def bench_blocks(rng, name, n_blocks):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ZLLM_REFERENCE"),
+                    help="checkout of the reference repository (its test/data/quant-vectors.json is copied)")
     args = ap.parse_args()
-    src = os.path.join(args.reference, "test", "data", "quant-vectors.json")
-    if os.path.exists(src):
+    src = os.path.join(args.reference, "test", "data", "quant-vectors.json") if args.reference else ""
+    if src and os.path.exists(src):
         shutil.copyfile(src, os.path.join(HERE, "ref_quant_vectors.json"))
         print("copied", src)
     rng = np.random.default_rng(20261201)

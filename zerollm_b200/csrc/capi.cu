@@ -64,11 +64,18 @@ extern "C" int zllm_init(int device, zllm_ctx **out) {
   // the status word lives in device memory: device atomics on mapped host memory are not atomic
   // (and may be lost) on PCIe hosts
   if (e == cudaSuccess) e = cudaMalloc((void **)&c->status_dev, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMallocHost((void **)&c->status_host, sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemsetAsync(c->status_dev, 0, sizeof(unsigned), c->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) {
     fprintf(stderr, "zllm_init: %s\n", cudaGetErrorString(e));
     int rc = e == cudaErrorMemoryAllocation ? ZLLM_E_OOM : ZLLM_E_CUDA;
+    zllm_destroy(c);
+    return rc;
+  }
+  // the fixed scratch of zllm_attn_decode_noalloc comes into being here, not inside a decode step
+  if (int rc = zllm_noalloc_setup(c)) {
+    fprintf(stderr, "zllm_init: %s\n", c->err);
     zllm_destroy(c);
     return rc;
   }
@@ -91,6 +98,7 @@ extern "C" void zllm_destroy(zllm_ctx *c) {
   for (int i = 0; i < kScratchSlots; i++)
     if (c->scratch[i]) cudaFree(c->scratch[i]);
   if (c->status_dev) cudaFree(c->status_dev);
+  if (c->status_host) cudaFreeHost(c->status_host);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
 }
@@ -108,6 +116,15 @@ int zllm_check_status(zllm_ctx *c) {
                       "slice did not complete within 2 s; the kernel drained its copies and returned", st);
     return ZLLM_E_TIMEOUT;
   }
+  return ZLLM_OK;
+}
+
+int zllm_finish(zllm_ctx *c, cudaStream_t s) {
+  *c->status_host = 0;
+  cudaError_t e = cudaMemcpyAsync(c->status_host, c->status_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return zllm_cuda_fail(c, e, "reading the device status word");
+  if (*c->status_host) return zllm_check_status(c);     // rare: clear the word and report, as zllm_sync does
   return ZLLM_OK;
 }
 
@@ -293,5 +310,5 @@ extern "C" int zllm_matvec(zllm_ctx *c, const zllm_weight *w, const float *x_hos
     return rc;
   e = cudaMemcpyAsync(y_host, y_, sizeof(float) * R * ntok, cudaMemcpyDeviceToHost, c->stream);
   if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(y)");
-  return zllm_sync(c);
+  return zllm_finish(c, c->stream);             // status word read back on the stream: one synchronization
 }

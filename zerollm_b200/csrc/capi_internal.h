@@ -16,6 +16,7 @@ struct zllm_ctx {
   int num_sms = 148;
   cudaStream_t stream = nullptr;
   unsigned *status_dev = nullptr;    // device word the kernels report timeouts into (atomicOr)
+  unsigned *status_host = nullptr;   // pinned host copy of it, read back on the stream (zllm_finish)
   void *scratch[kScratchSlots] = {};
   size_t scratch_bytes[kScratchSlots] = {};
   char err[512] = {0};
@@ -38,6 +39,12 @@ void zllm_set_error(zllm_ctx *c, const char *fmt, ...);
 int zllm_cuda_fail(zllm_ctx *c, cudaError_t e, const char *what);
 int zllm_scratch(zllm_ctx *c, int slot, size_t bytes, void **out);
 int zllm_check_status(zllm_ctx *c);
+// Enqueue the status word's copy into pinned host memory on `s`, synchronize `s` once and report a
+// timeout bit: the end of a host-buffer call without a second, blocking copy.
+int zllm_finish(zllm_ctx *c, cudaStream_t s);
+// Loads the fixed attention scratch of zllm_attn_decode_noalloc on the context's device and caches
+// its address (capi_noalloc.cu); zllm_init calls it, so no later call of that entry point allocates.
+int zllm_noalloc_setup(zllm_ctx *c);
 int zllm_attn_splits(const zllm_ctx *c, const zllm_attn_geom *g, int nseq, int max_pos);
 int zllm_attn_launch(zllm_ctx *c, const zllm_attn_geom *g, const float *q, const void *kcache, const void *vcache,
                      const int32_t *npos, int nseq, int nsplit, float *out, float *partial, int32_t *counters,

@@ -12,12 +12,17 @@
 //
 // Limits: the partial results of one call must fit in kPartialBytes (4 MiB) and the call may cover
 // at most kMaxGroups (4096) (sequence, KV head) pairs; larger requests are rejected with ZLLM_E_ARG
-// before anything is launched.  Every GPU that loads this library holds the 4 MiB + 16 KiB array
-// until the process exits.  All calls on one device share the array: two calls that overlap in
+// before anything is launched.  All calls on one device share the array: two calls that overlap in
 // time (different streams, contexts or threads on the same device) race on it, so callers order
-// them (one stream, or events).  The first call through a context looks the array's address up
-// (cudaGetSymbolAddress, with the context's device current; it allocates nothing); later calls
-// reuse the cached address.
+// them (one stream, or events).
+//
+// When the array comes into being: this file is its own CUDA module, and under lazy module loading
+// (the CUDA default) a module's device variables are allocated when the module is first touched.
+// zllm_init touches it -- zllm_noalloc_setup looks the array's address up with cudaGetSymbolAddress,
+// the context's device current -- so the 4 MiB + 16 KiB are taken when the first context on a
+// device is created (an out-of-memory there fails zllm_init, not a decode step), every later call
+// of zllm_attn_decode_noalloc reuses the cached address and allocates nothing, and the device holds
+// the array until the process exits.
 #include <mutex>
 
 #include "../../include/zllm.h"
@@ -36,28 +41,33 @@ __device__ __align__(256) unsigned char g_attn_scratch[kPartialBytes + kMaxGroup
 std::mutex g_addr_mu;
 void *g_addr[kMaxDevices] = {};
 
-// the array's device address on the context's device, looked up once per device
-int scratch_address(zllm_ctx *c, void **out) {
-  if (c->device < 0 || c->device >= kMaxDevices) {
-    zllm_set_error(c, "zllm_attn_decode_noalloc: device %d out of range (max %d)", c->device, kMaxDevices - 1);
+// the array's device address on `device`, looked up once per device with that device current
+int lookup(zllm_ctx *c, int device, void **out) {
+  if (device < 0 || device >= kMaxDevices) {
+    zllm_set_error(c, "fixed attention scratch: device %d out of range (max %d)", device, kMaxDevices - 1);
     return ZLLM_E_ARG;
   }
   std::lock_guard<std::mutex> lock(g_addr_mu);
-  if (!g_addr[c->device]) {
+  if (!g_addr[device]) {
     int prev = 0;
     cudaError_t e = cudaGetDevice(&prev);
-    if (e == cudaSuccess && prev != c->device) e = cudaSetDevice(c->device);
+    if (e == cudaSuccess && prev != device) e = cudaSetDevice(device);
     void *p = nullptr;
     if (e == cudaSuccess) e = cudaGetSymbolAddress(&p, g_attn_scratch);
-    if (prev != c->device) cudaSetDevice(prev);
-    if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaGetSymbolAddress(attention scratch)");
-    g_addr[c->device] = p;
+    if (prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaGetSymbolAddress(fixed attention scratch)");
+    g_addr[device] = p;
   }
-  *out = g_addr[c->device];
+  *out = g_addr[device];
   return ZLLM_OK;
 }
 
 }  // namespace
+
+int zllm_noalloc_setup(zllm_ctx *c) {
+  void *p = nullptr;
+  return lookup(c, c->device, &p);
+}
 
 extern "C" int zllm_attn_decode_noalloc(zllm_ctx *c, const zllm_attn_geom *g, const float *q, const void *kcache,
                                         const void *vcache, const int32_t *npos, int nseq, int max_pos, float *out,
@@ -92,7 +102,7 @@ extern "C" int zllm_attn_decode_noalloc(zllm_ctx *c, const zllm_attn_geom *g, co
     return ZLLM_E_ARG;
   }
   void *base = nullptr;
-  int rc = scratch_address(c, &base);
+  int rc = lookup(c, c->device, &base);        // cached by zllm_init: no allocation, no module load here
   if (rc) return rc;
   float *partial = (float *)base;
   int32_t *counters = (int32_t *)((unsigned char *)base + kPartialBytes);

@@ -16,6 +16,7 @@ weights.  ``model_config`` maps the metadata to the model config (src/model/conf
 """
 from __future__ import annotations
 
+import math
 import os
 import struct
 
@@ -170,7 +171,9 @@ def read_gguf(path: str) -> GGUFFile:
     data_start = -(-c.pos // align) * align
     tensors = []
     for name, dims, t, off in raw:
-        n_el = int(np.prod(dims, dtype=np.int64))
+        n_el = math.prod(int(d) for d in dims)   # Python ints: a corrupt header cannot wrap around
+        if n_el > 1 << 53:
+            raise ValueError(f"GGUF: tensor {name} has an implausible element count {n_el} (dims {dims})")
         n_bytes = None
         if t in ggml.TYPE_INFO:
             _, bs, ts = ggml.TYPE_INFO[t]
