@@ -67,18 +67,9 @@ def measured_tensor_peak():
     return 1590.0, "fallback (1.59 PFLOP/s burst)"
 
 
-def traffic_from_profile():
-    """dram bytes (read + write) per launch from the committed ncu summary of this kernel, if any."""
-    p = os.path.join(ROOT, "profiles", "gemv_q4k_4096x4096.md")
-    if not os.path.exists(p):
-        return None
-    for line in open(p):
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
+# DRAM bytes (read + write) of one kq_stream_kernel<Q4_K> launch of this step, from the ncu capture
+# summarised in profiles/gemv_q4k_4096x4096.md (dram__bytes_read.sum + dram__bytes_write.sum).
+GEMV_TRAFFIC_BYTES = 9494528
 
 
 class Clocks:
@@ -194,7 +185,7 @@ def run_reference(args, world, rank):
               f"plain-JS kernels (the reference is JavaScript; no Node.js runtime on this box)")
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8/f64", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32", "data": "synthetic",
             "config": {"workload": "config0: Q4_K GEMV 4096x4096, batch 1", "rows": ROWS, "cols": COLS, "seed": SEED},
             "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": nthreads, "kind": "port", "sample": sample},
             "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -207,10 +198,8 @@ DEC_WEIGHT_BYTES = 5_618_794_496            # Qwen3-8B Q4_K/Q6_K mix + f16 head:
 DEC_KV_BYTES_PER_POS = 36 * 2 * 8 * 128 * 2  # f16 K and V of every layer, per cached position
 
 
-def _gen_kquant(t, rows, cols, g):
-    """Raw GGUF bytes of a seeded k-quant matrix (config 0/1 distribution: random nibbles / 6-bit
-    scales / high bits, d and dmin = f16(|N(0,1)| * 0.01); Q6_K int8 scales U[-32, 31]), drawn on
-    the GPU and returned as host bytes, as a GGUF reader would hand them over."""
+def _gen_kquant_dev(t, rows, cols, g):
+    """The same seeded k-quant matrix as _gen_kquant, left on the GPU as [rows][row bytes] uint8."""
     import torch
     from zerollm_b200 import ggml
     _, bs, ts = ggml.TYPE_INFO[t]
@@ -223,7 +212,14 @@ def _gen_kquant(t, rows, cols, g):
     else:
         raw[:, 0:2] = d
         raw[:, 2:4] = (torch.randn(nblk, device="cuda", generator=g).abs() * 0.01).half().view(torch.uint8).view(nblk, 2)
-    return raw.cpu().numpy().reshape(-1)
+    return raw.view(rows, (cols // bs) * ts)
+
+
+def _gen_kquant(t, rows, cols, g):
+    """Raw GGUF bytes of a seeded k-quant matrix (config 0/1 distribution: random nibbles / 6-bit
+    scales / high bits, d and dmin = f16(|N(0,1)| * 0.01); Q6_K int8 scales U[-32, 31]), drawn on
+    the GPU and returned as host bytes, as a GGUF reader would hand them over."""
+    return _gen_kquant_dev(t, rows, cols, g).cpu().numpy().reshape(-1)
 
 
 def decode_bench(n_seq: int, device: int, profile: bool = False):
@@ -440,15 +436,20 @@ TP_PROMPT, TP_STEPS, TP_CTX = 512, 128, 8192
 TP_SHAPE = dict(n_embd=5120, n_layer=64, n_ff=25600, n_head=64, n_head_kv=8, head_dim=128, vocab=151936)
 
 
-def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
+def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool = False):
     """Config 4: random-init Qwen3-32B shapes (64 layers, hidden 5120, FFN 25600, 64 query / 8 KV
     heads, head_dim 128, vocab 151936), Q4_K everywhere but Q6_K ffn_down, f16 output head, f16 KV
-    cache of 8192 positions, tensor-parallel over the `world` GPUs: each rank draws its own shard
-    (its 64/world query and 8/world KV heads, its 1/world of the FFN at 256-value blocks), the
-    replicated tensors (embedding, norms) and the output head (each rank uploading its vocab rows) from
-    one shared seed; an NCCL all-reduce
-    follows attn_output and ffn_down.  Prefill TP_PROMPT seeded ids per sequence, then TP_STEPS
-    greedy steps through zllm_model_generate, timed with CUDA events on the model's stream."""
+    cache of 8192 positions, tensor-parallel over the `world` GPUs.  Every rank draws every full
+    matrix from one shared seed (on its GPU) and uploads its cut: its 64/world query and 8/world KV
+    heads of q / k / v, its 1/world of the FFN rows of gate / up, the matching input columns of
+    attn_output and ffn_down (whole 256-value super-blocks), its vocab rows of the output head; the
+    embedding and the norms are replicated.  An all-reduce follows attn_output and ffn_down.
+    Prefill TP_PROMPT seeded ids per sequence, then TP_STEPS greedy steps through
+    zllm_model_generate, timed with CUDA events on the model's stream.
+
+    With `parity` (world > 1), rank 0 also builds the whole model on its own GPU from the same full
+    matrices (TP 1) and runs the same calls on it: the logits of the first decode step of TP `world`
+    against TP 1 (max |diff| / max |logit|) and how many of the greedy tokens agree."""
     import ctypes as C
 
     import torch
@@ -460,10 +461,13 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
     from zerollm_b200.model import tp_unique_id
     from zerollm_b200.tp import ranges
     c = TP_SHAPE
-    E, F, V, NL, hd = c["n_embd"], c["n_ff"], c["vocab"], c["n_layer"], c["head_dim"]
-    Hl, KVl = c["n_head"] // world, c["n_head_kv"] // world
+    E, F, V, NL, hd, H, KV = c["n_embd"], c["n_ff"], c["vocab"], c["n_layer"], c["head_dim"], c["n_head"], c["n_head_kv"]
+    Hl, KVl = H // world, KV // world
     f0, f1 = [(a * 256, b * 256) for a, b in ranges(F // 256, world)][rank]
     Fl = f1 - f0
+    q0, q1, k0, k1 = rank * Hl * hd, (rank + 1) * Hl * hd, rank * KVl * hd, (rank + 1) * KVl * hd
+    v0, v1 = ranges(V, world)[rank]                     # this rank's rows of the vocab-split output head
+    parity = parity and world > 1 and rank == 0 and n_seq == 1
     ctx = Context(device)
     L = ctx.lib
     uid = b"\0" * 128
@@ -472,60 +476,91 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
         obj = [tp_unique_id(ctx) if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         uid = obj[0]
-    mc = ModelConfig(n_embd=E, n_layer=NL, n_ff=Fl, n_head=Hl, n_head_kv=KVl, head_dim=hd, n_rot=hd, vocab=V, neox=1,
-                     kv_f16=1, ctx=TP_CTX, n_seq=n_seq, max_batch=64, logits_batch=16, rms_eps=float(np.float32(1e-6)),
-                     rope_base=1e6)
-    h = C.c_void_p()
-    check(L.zllm_model_create(ctx.h, C.byref(mc), C.byref(h)), ctx.h)
-    v0, v1 = ranges(V, world)[rank]                     # this rank's rows of the vocab-split output head
+
+    def create(heads, kv_heads, ff):
+        mc = ModelConfig(n_embd=E, n_layer=NL, n_ff=ff, n_head=heads, n_head_kv=kv_heads, head_dim=hd, n_rot=hd, vocab=V,
+                         neox=1, kv_f16=1, ctx=TP_CTX, n_seq=n_seq, max_batch=64, logits_batch=16,
+                         rms_eps=float(np.float32(1e-6)), rope_base=1e6)
+        hh = C.c_void_p()
+        check(L.zllm_model_create(ctx.h, C.byref(mc), C.byref(hh)), ctx.h)
+        return hh
+
+    h = create(Hl, KVl, Fl)
+    h1 = create(H, KV, F) if parity else None
     if world > 1:
         ub = C.create_string_buffer(uid, 128)
         check(L.zllm_model_set_tp(h, rank, world, ub), ctx.h)
         check(L.zllm_model_set_vocab_shard(h, v0, v1 - v0), ctx.h)
-    g_local = torch.Generator(device="cuda")
-    g_local.manual_seed(SEED + 1000 * (rank + 1))          # this rank's shards
-    g_shared = torch.Generator(device="cuda")
-    g_shared.manual_seed(SEED)                            # replicated tensors: the same on every rank
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED)                                   # every full matrix: the same on every rank
     rng = np.random.default_rng(SEED)
 
-    def mat(kind, layer, t, rows, cols, g, keep=None):
-        buf = _gen_kquant(t, rows, cols, g) if t != ggml.F16 else \
-            (torch.randn(rows, cols, device="cuda", generator=g) * 0.02).half().view(torch.uint8).cpu().numpy().reshape(-1)
-        if keep is not None:                              # rows [keep[0], keep[1]) of the generated matrix
-            rb = buf.size // rows
-            buf = np.ascontiguousarray(buf[keep[0] * rb:keep[1] * rb])
-            rows = keep[1] - keep[0]
-        check(L.zllm_model_set_matrix(h, kind, layer, t, rows, cols, buf.ctypes.data_as(C.c_void_p), buf.nbytes), ctx.h)
+    def put(hh, kind, layer, t, rows, cols, dev):
+        buf = dev.contiguous().cpu().numpy().reshape(-1)
+        check(L.zllm_model_set_matrix(hh, kind, layer, t, rows, cols, buf.ctypes.data_as(C.c_void_p), buf.nbytes), ctx.h)
+
+    def mat(kind, layer, t, rows, cols, cut=None):
+        """the full matrix from the shared generator; this rank uploads rows [a, b) ("rows", a, b) or
+        input columns [a, b) ("cols", a, b); rank 0 with parity also uploads the whole matrix"""
+        if t == ggml.F16:
+            full = (torch.randn(rows, cols, device="cuda", generator=g) * 0.02).half().view(torch.uint8)
+            blk = 2
+        else:
+            full = _gen_kquant_dev(t, rows, cols, g)
+            blk = ggml.TYPE_INFO[t][2] / ggml.TYPE_INFO[t][1]    # bytes per value
+        if cut is None or world == 1:
+            put(h, kind, layer, t, rows, cols, full)
+        elif cut[0] == "rows":
+            put(h, kind, layer, t, cut[2] - cut[1], cols, full[cut[1]:cut[2]])
+        else:
+            put(h, kind, layer, t, rows, cut[2] - cut[1], full[:, int(cut[1] * blk):int(cut[2] * blk)])
+        if h1 is not None:
+            put(h1, kind, layer, t, rows, cols, full)
+        del full
 
     def vec(kind, layer, n):
         a = (1 + rng.standard_normal(n) * 0.02).astype(np.float32)
-        check(L.zllm_model_set_vector(h, kind, layer, a.ctypes.data_as(C.c_void_p), a.size), ctx.h)
+        for hh in (h, h1):
+            if hh is not None:
+                check(L.zllm_model_set_vector(hh, kind, layer, a.ctypes.data_as(C.c_void_p), a.size), ctx.h)
 
-    mat(T_TOK_EMBD, 0, ggml.Q4_K, V, E, g_shared)
-    mat(T_OUTPUT, 0, ggml.F16, V, E, g_shared, keep=(v0, v1) if world > 1 else None)
+    mat(T_TOK_EMBD, 0, ggml.Q4_K, V, E)
+    mat(T_OUTPUT, 0, ggml.F16, V, E, ("rows", v0, v1))
     vec(T_OUTPUT_NORM, 0, E)
     for l in range(NL):
         for k_, n_ in ((T_ATTN_NORM, E), (T_FFN_NORM, E), (T_Q_NORM, hd), (T_K_NORM, hd)):
             vec(k_, l, n_)
-        for k_, t_, r_, c_ in ((T_WQ, ggml.Q4_K, Hl * hd, E), (T_WK, ggml.Q4_K, KVl * hd, E), (T_WV, ggml.Q4_K, KVl * hd, E),
-                               (T_WO, ggml.Q4_K, E, Hl * hd), (T_GATE, ggml.Q4_K, Fl, E), (T_UP, ggml.Q4_K, Fl, E),
-                               (T_DOWN, ggml.Q6_K, E, Fl)):
-            mat(k_, l, t_, r_, c_, g_local)
+        for k_, t_, r_, c_, cut in ((T_WQ, ggml.Q4_K, H * hd, E, ("rows", q0, q1)), (T_WK, ggml.Q4_K, KV * hd, E, ("rows", k0, k1)),
+                                    (T_WV, ggml.Q4_K, KV * hd, E, ("rows", k0, k1)), (T_WO, ggml.Q4_K, E, H * hd, ("cols", q0, q1)),
+                                    (T_GATE, ggml.Q4_K, F, E, ("rows", f0, f1)), (T_UP, ggml.Q4_K, F, E, ("rows", f0, f1)),
+                                    (T_DOWN, ggml.Q6_K, E, F, ("cols", f0, f1))):
+            mat(k_, l, t_, r_, c_, cut)
     check(L.zllm_model_ready(h), ctx.h)
+    if h1 is not None:
+        check(L.zllm_model_ready(h1), ctx.h)
     P = lambda a: a.ctypes.data_as(C.c_void_p)
     arg = np.zeros(64, np.int32)
     first = np.zeros(n_seq, np.int32)
-    for s_ in range(n_seq):
-        toks = rng.integers(0, V, TP_PROMPT).astype(np.int32)
-        for i in range(0, TP_PROMPT, 64):
-            chunk = np.ascontiguousarray(toks[i:i + 64])
-            want = 1 if i + 64 >= TP_PROMPT else 0
-            check(L.zllm_model_forward(h, s_, P(chunk), chunk.size, want, None, P(arg) if want else None), ctx.h)
-        first[s_] = arg[0]
+    prompts = [rng.integers(0, V, TP_PROMPT).astype(np.int32) for _ in range(n_seq)]
+
+    def prefill(hh):
+        for s_ in range(n_seq):
+            for i in range(0, TP_PROMPT, 64):
+                chunk = np.ascontiguousarray(prompts[s_][i:i + 64])
+                want = 1 if i + 64 >= TP_PROMPT else 0
+                check(L.zllm_model_forward(hh, s_, P(chunk), chunk.size, want, None, P(arg) if want else None), ctx.h)
+            first[s_] = arg[0]
+
+    prefill(h)
+    tok0 = int(first[0])
+    logits = np.zeros(V, np.float32)
+    check(L.zllm_model_forward(h, 0, P(np.array([tok0], np.int32)), 1, 1, P(logits), P(arg)), ctx.h)  # logits out
+    first[0] = arg[0]
     seqs = np.arange(n_seq, dtype=np.int32)
     seqp = None if n_seq == 1 else P(seqs)
     out = np.zeros((TP_STEPS, n_seq), np.int32)
     check(L.zllm_model_generate(h, 0, seqp, P(first), n_seq, 3, P(out)), ctx.h)      # warm-up: record the graphs
+    warm = out[:3, 0].copy()
     collective = {0: "none", 1: "NCCL all-reduce",
                   2: "one-shot all-reduce over NVLink peer memory (CUDA IPC)"}[L.zllm_model_tp_collective(h)]
     cur = np.ascontiguousarray(out[2])
@@ -536,12 +571,30 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int):
     e1.record(st)
     e1.synchronize()
     dt = e0.elapsed_time(e1) / 1e3
-    same = out[-1].copy()
+    res = {}
+    if h1 is not None:                                   # TP 1 on rank 0: the same calls
+        toks = np.concatenate([warm, out[:, 0]])
+        prefill(h1)
+        ref = np.zeros(V, np.float32)
+        check(L.zllm_model_forward(h1, 0, P(np.array([tok0], np.int32)), 1, 1, P(ref), P(arg)), ctx.h)
+        out1 = np.zeros((3 + TP_STEPS, 1), np.int32)
+        check(L.zllm_model_generate(h1, 0, None, P(np.array([arg[0]], np.int32)), 1, 3 + TP_STEPS, P(out1)), ctx.h)
+        agree = 0
+        while agree < toks.size and toks[agree] == out1[agree, 0]:
+            agree += 1
+        srt = np.sort(ref)
+        res["tp_parity"] = {"vs": "the whole model on one GPU (TP 1), same weights and calls",
+                            "max_rel": float(np.abs(logits - ref).max() / np.abs(ref).max()),
+                            "argmax_equal": bool(int(np.argmax(logits)) == int(np.argmax(ref))),
+                            "top1_margin_rel": float((srt[-1] - srt[-2]) / np.abs(ref).max()),
+                            "tokens_equal_steps": int(agree), "steps": int(toks.size)}
     L.zllm_model_destroy(h)                               # releases the graphs before the communicator
+    if h1 is not None:
+        L.zllm_model_destroy(h1)
     ctx.close()
     wbytes = NL * (2.25 * (Hl * hd * E + 2 * KVl * hd * E + E * Hl * hd + 2 * Fl * E) / 4 + 210 / 256 * E * Fl) + (v1 - v0) * E * 2
     return {"seconds": dt, "ms_per_step": round(dt / TP_STEPS * 1e3, 3), "weight_bytes_per_rank": int(wbytes),
-            "last_tokens": same.tolist(), "collective": collective}
+            "collective": collective, **res}
 
 
 # ------------------------------------------------------------------------------------------ attention (config 2)
@@ -774,13 +827,16 @@ def run_ours(args, world, rank, local):
     if not args.no_decode:
         del weights
         torch.cuda.empty_cache()
-        for nseq in (1, 32):
+        # b1 / b32: one model replica and its 1 or 32 sequences per GPU (weak scaling); b32_split:
+        # config 3 as stated, 32 sequences in all spread as 32 / N per GPU (strong scaling)
+        runs = [("b1", 1), ("b32", 32)] + ([("b32_split", 32 // world)] if world > 1 and 32 % world == 0 else [])
+        for key, nseq in runs:
             barrier()
             r = decode_bench(nseq, local)
             slowest = max_over_ranks(r["seconds"])
-            decode[f"b{nseq}"] = {"tok_s": round(world * nseq * DEC_STEPS / slowest, 1), "ms_per_step": r["ms_per_step"],
-                                  "prefill_tok_s_per_gpu": r["prefill_tok_s"], "hbm_gbs_per_gpu": r["hbm_gbs"],
-                                  "step_bytes_per_gpu": r["step_bytes"]}
+            decode[key] = {"tok_s": round(world * nseq * DEC_STEPS / slowest, 1), "seq_per_gpu": nseq,
+                           "ms_per_step": r["ms_per_step"], "prefill_tok_s_per_gpu": r["prefill_tok_s"],
+                           "hbm_gbs_per_gpu": r["hbm_gbs"], "step_bytes_per_gpu": r["step_bytes"]}
 
     gemm = None
     if not args.no_decode:
@@ -791,9 +847,11 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
         for nseq in (1, 16):
             barrier()
-            r = tp_decode_bench(nseq, world, rank, local)
+            r = tp_decode_bench(nseq, world, rank, local, parity=nseq == 1)
             slowest = max_over_ranks(r["seconds"])
             tp["collective_used"] = r["collective"]
+            if "tp_parity" in r:
+                tp["tp_parity"] = r["tp_parity"]
             tp[f"b{nseq}"] = {"tok_s": round(nseq * TP_STEPS / slowest, 1), "ms_per_step": round(slowest / TP_STEPS * 1e3, 3),
                               "weight_bytes_per_rank": r["weight_bytes_per_rank"],
                               "hbm_gbs_per_rank_weights": round(r["weight_bytes_per_rank"] / (slowest / TP_STEPS) / 1e9, 1)}
@@ -803,11 +861,11 @@ def run_ours(args, world, rank, local):
         value = ALGO_BYTES * args.steps * world / (ms / 1e3) / 1e9
         # every launch of the timed region is the one GEMV kernel: its average duration is ms / steps
         achieved = ALGO_BYTES / (ms / args.steps / 1e3) / 1e9
-        traffic = traffic_from_profile()
+        traffic = GEMV_TRAFFIC_BYTES
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8/f64", "data": "synthetic",
+            "vs_baseline": None, "dtype": "int8/f32", "data": "synthetic",
             "config": {"workload": "config0: Q4_K GEMV 4096x4096, batch 1 (quantizeAct fused into the matvec kernel)",
                        "rows": ROWS,
                        "cols": COLS, "weight_copies": NCOPY, "seed": SEED, "parallelism": f"replicas{world}",
@@ -859,6 +917,21 @@ def run_ours(args, world, rank, local):
                                  "scaling": "strong (one model over all GPUs)", **tp}
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds, os.cpu_count() or 1)
+        # the figures a reader needs, last: the driver keeps the end of the line
+        summ = {"config0_gbs": line["value"], "config0_frac": line["roofline"]["frac"], "e2e_gbs": line["e2e"]["value"],
+                "parity_config0": parity}
+        if decode:
+            summ["decode_8b_tok_s"] = {k: v["tok_s"] for k, v in decode.items()}
+        if attn:
+            summ["attn_gbs"] = {k: v.get("hbm_gbs", v.get("hbm_gbs_read_plus_write")) for k, v in attn.items()}
+        if gemm:
+            summ["prefill_gemm_tflops"] = line["prefill_gemm"]["value"]
+            summ["prefill_gemm_frac"] = line["prefill_gemm"]["roofline"]["frac"]
+        if tp:
+            summ["tp_decode_32b_tok_s"] = {k: v["tok_s"] for k, v in tp.items() if k.startswith("b")}
+            if "tp_parity" in tp:
+                summ["tp_parity"] = {k: tp["tp_parity"][k] for k in ("max_rel", "argmax_equal", "tokens_equal_steps", "steps")}
+        line["summary"] = summ
         print(json.dumps(line), flush=True)
     del g_warm, g_main, g_kern
     ctx.close()

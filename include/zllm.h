@@ -112,6 +112,28 @@ int zllm_mm(zllm_ctx *ctx, const zllm_weight *w, const int8_t *xq, const float *
  * context buffer that grows on demand. */
 int zllm_gemm_f16(zllm_ctx *ctx, const void *A, const void *B, int64_t m, int64_t n, int64_t k, float *D, void *stream);
 
+/* One-token k-quant (Q4_K / Q5_K / Q6_K) product with the fusions of the decode pass, on device
+ * buffers: x f32 [cols] is RMSNormed with norm_w first when norm_w is given (src/compute/ref-kernels.js:
+ * 305-310, eps as the model's) and quantized inside the kernel (quantizeAct, :44-62); then
+ *   swiglu == 0: y[r] = (y_add ? y_add[r] : 0) + W[r] . x      (residual: src/compute/worker.js:346, :432)
+ *   swiglu != 0: the rows are (gate, up) pairs 2i, 2i + 1 and y[i] = f32(silu(gate_i) * up_i)
+ *                (worker.js:426, silu ref-kernels.js:322, in double), rows / 2 outputs.
+ * Exposes the fused kernels the model's decode pass launches, for parity tests and hosts that run a
+ * layer op by op. */
+int zllm_mm_fused(zllm_ctx *ctx, const zllm_weight *w, const float *x, const float *norm_w, double eps, int swiglu,
+                  float *y, const float *y_add, void *stream);
+
+/* Layer glue on device buffers, each fused with the quantization its consumer needs (any of xb /
+ * xq+xd+xs may be NULL; quantizing needs n % 32 == 0):
+ *   zllm_rmsnorm_quant: xb[t] = rmsnorm(x[t], w, eps) for ntok vectors of n (src/compute/ref-kernels.js:
+ *     305-310: double sum of squares, s = 1/sqrt(ss/n + eps), f32(x * s * w)), then quantizeAct of xb;
+ *   zllm_swiglu_quant: hb[t][i] = f32(silu(gate[t*stride + i]) * up[t*stride + i]) in double
+ *     (src/compute/worker.js:426, ref-kernels.js:322), then quantizeAct of hb. */
+int zllm_rmsnorm_quant(zllm_ctx *ctx, const float *x, const float *w, int n, int ntok, double eps, float *xb,
+                       int8_t *xq, float *xd, int32_t *xs, void *stream);
+int zllm_swiglu_quant(zllm_ctx *ctx, const float *gate, const float *up, int n, int ntok, int64_t stride, float *hb,
+                      int8_t *xq, float *xd, int32_t *xs, void *stream);
+
 /* Host-buffer convenience: y_host[t][rows] = W . x_host[t][cols] (quantizing x on the device first),
  * blocking.  The CUDA counterpart of `matvec(w, new Act(x), y)` (src/compute/ref-kernels.js:127). */
 int zllm_matvec(zllm_ctx *ctx, const zllm_weight *w, const float *x_host, int ntok, float *y_host);

@@ -56,6 +56,8 @@ def _setup(lib):
     lib.zo_model_pos.restype = i32
     lib.zo_model_pos.argtypes = [vp]
     lib.zo_model_truncate.argtypes = [vp, i32]
+    lib.zo_model_restore_prefix.restype = i32
+    lib.zo_model_restore_prefix.argtypes = [vp, i32]
     lib.zo_model_forward.restype = i32
     lib.zo_model_forward.argtypes = [vp, i32, vp, i32]
     lib.zo_model_kv_get.restype = i32
@@ -280,6 +282,11 @@ class OracleModel:
 
     def truncate(self, n: int):
         lib().zo_model_truncate(self._m, n)
+
+    def restore_prefix(self, n: int):
+        """forward.js:78: after kv_set filled positions [0, n), the model holds n positions."""
+        if lib().zo_model_restore_prefix(self._m, int(n)):
+            raise ValueError(f"prefix of {n} positions does not fit the context ({self._c.ctx})")
 
     def forward(self, token: int, logits: bool = True):
         out = np.zeros(self.vocab, np.float32) if logits else None

@@ -485,6 +485,12 @@ void zo_model_free(zo_model *m) {
 
 int zo_model_pos(const zo_model *m) { return m->pos; }
 void zo_model_truncate(zo_model *m, int n) { if (n < m->pos) m->pos = n < 0 ? 0 : n; }  /* forward.js:86 */
+/* forward.js:78 restorePrefix: after kvSet filled positions [0, n), the model holds n positions */
+int zo_model_restore_prefix(zo_model *m, int n) {
+  if (n < 0 || n > m->c.ctx) return -1;
+  m->pos = n;
+  return 0;
+}
 
 static void mv(const zo_weight *w, const float *x, float *y, int nthreads) {
   zo_matvec(w->type, w->data, w->rows, w->cols, x, y, 0, w->rows, nthreads);

@@ -89,6 +89,7 @@ zo_model *zo_model_new(const zo_config *cfg, const zo_weight *tok_embd, const zo
                        const float *output_norm, const zo_layer *layers, const float *rope_freqs);
 void zo_model_free(zo_model *m);
 int  zo_model_pos(const zo_model *m);
+int  zo_model_restore_prefix(zo_model *m, int n);
 void zo_model_truncate(zo_model *m, int n);
 /* forward.js:94-158.  logits may be NULL (logits:false).  Returns 0, -1 context full, -2 bad token. */
 int  zo_model_forward(zo_model *m, int token, float *logits, int nthreads);

@@ -272,6 +272,47 @@ extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, cons
   return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "gemv launch");
 }
 
+extern "C" int zllm_mm_fused(zllm_ctx *c, const zllm_weight *w, const float *x, const float *norm_w, double eps,
+                             int swiglu, float *y, const float *y_add, void *stream) {
+  if (!c || !w || !x || !y) { zllm_set_error(c, "zllm_mm_fused: bad argument"); return ZLLM_E_ARG; }
+  if (!w->m.data) { zllm_set_error(c, "zllm_mm_fused: the weight's context was destroyed"); return ZLLM_E_STATE; }
+  if (!kq_type(w->m.type)) { zllm_set_error(c, "zllm_mm_fused: Q4_K, Q5_K or Q6_K weights only"); return ZLLM_E_UNSUPPORTED; }
+  GemvFuse fz;
+  fz.norm_w = norm_w;
+  fz.eps = eps;
+  fz.swiglu = swiglu != 0;
+  ActView a{nullptr, nullptr, nullptr, x, w->m.cols};
+  const char *why = "";
+  cudaStream_t st = pick(c, stream);
+  cudaError_t e = launch_gemv_kq_ex(w->m, a, 1, y, w->m.rows, y_add, fz, c->status_dev, c->num_sms, st, pdl_ok(st), &why);
+  if (e == cudaErrorInvalidValue && why[0]) { zllm_set_error(c, "zllm_mm_fused: %s", why); return ZLLM_E_ARG; }
+  return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "zllm_mm_fused launch");
+}
+
+extern "C" int zllm_rmsnorm_quant(zllm_ctx *c, const float *x, const float *w, int n, int ntok, double eps, float *xb,
+                                  int8_t *xq, float *xd, int32_t *xs, void *stream) {
+  const bool q = xq || xd || xs;
+  if (!c || !x || !w || n < 1 || ntok < 1 || (!xb && !q) || (q && (!xq || !xd || !xs || n % 32))) {
+    zllm_set_error(c, "zllm_rmsnorm_quant: bad argument");
+    return ZLLM_E_ARG;
+  }
+  cudaStream_t st = pick(c, stream);
+  cudaError_t e = launch_rmsnorm_quant(x, w, n, ntok, eps, xb, xq, xd, xs, st, pdl_ok(st));
+  return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "zllm_rmsnorm_quant launch");
+}
+
+extern "C" int zllm_swiglu_quant(zllm_ctx *c, const float *gate, const float *up, int n, int ntok, int64_t stride,
+                                 float *hb, int8_t *xq, float *xd, int32_t *xs, void *stream) {
+  const bool q = xq || xd || xs;
+  if (!c || !gate || !up || n < 32 || n % 32 || ntok < 1 || stride < n || (!hb && !q) || (q && (!xq || !xd || !xs))) {
+    zllm_set_error(c, "zllm_swiglu_quant: bad argument (n a positive multiple of 32, stride >= n)");
+    return ZLLM_E_ARG;
+  }
+  cudaStream_t st = pick(c, stream);
+  cudaError_t e = launch_swiglu_quant(gate, up, n, ntok, stride, hb, xq, xd, xs, st, pdl_ok(st));
+  return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "zllm_swiglu_quant launch");
+}
+
 extern "C" int zllm_gemm_f16(zllm_ctx *c, const void *A, const void *B, int64_t m, int64_t n, int64_t k, float *D,
                              void *stream) {
   if (!c || !A || !B || !D || m < 1 || n < 1 || k < 64 || k % 64) {

@@ -42,6 +42,9 @@ SIGNATURES = {
     "zllm_quantize_act": (i32, [vp, vp, i64, i32, vp, vp, vp, vp]),
     "zllm_mm": (i32, [vp, vp, vp, vp, vp, vp, i32, vp, i64, vp, vp]),
     "zllm_gemm_f16": (i32, [vp, vp, vp, i64, i64, i64, vp, vp]),
+    "zllm_mm_fused": (i32, [vp, vp, vp, vp, C.c_double, i32, vp, vp, vp]),
+    "zllm_rmsnorm_quant": (i32, [vp, vp, vp, i32, i32, C.c_double, vp, vp, vp, vp, vp]),
+    "zllm_swiglu_quant": (i32, [vp, vp, vp, i32, i32, i64, vp, vp, vp, vp, vp]),
     "zllm_tp_unique_id": (i32, [vp, vp, sz]),
     "zllm_model_stream": (vp, [vp]),
     "zllm_model_tp_collective": (i32, [vp]),
