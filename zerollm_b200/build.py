@@ -97,9 +97,32 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+NAPI_SRC = os.path.join(PKG, "napi", "zllm_napi.c")
+NAPI_OUT = os.path.join(PKG, "zllm_napi.node")
+
+
+def build_napi(verbose: bool = False) -> str:
+    """The Node-API add-on (zerollm_b200/napi/zllm_napi.c) over libzllm_cuda.so: a plain shared object
+    whose napi_* symbols resolve from the node executable when Node loads it; libzllm_cuda.so is
+    found beside it ($ORIGIN)."""
+    deps = [NAPI_SRC, os.path.join(PKG, "napi", "napi_decl.h"), os.path.join(ROOT, "include", "zllm.h"), LIB]
+    if _stale(NAPI_OUT, deps):
+        cc = os.environ.get("CC") or shutil.which("gcc") or "cc"
+        cmd = [cc, "-O2", "-std=c11", "-Wall", "-Werror", "-fPIC", "-shared", f"-I{os.path.join(ROOT, 'include')}",
+               "-o", NAPI_OUT + ".tmp", NAPI_SRC, f"-L{PKG}", "-lzllm_cuda", "-Wl,-rpath,$ORIGIN"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode:
+            raise RuntimeError(f"N-API add-on build failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(NAPI_OUT + ".tmp", NAPI_OUT)
+    return NAPI_OUT
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
     print(build(a.force, a.verbose))
+    print(build_napi(a.verbose))
