@@ -436,7 +436,8 @@ TP_PROMPT, TP_STEPS, TP_CTX = 512, 128, 8192
 TP_SHAPE = dict(n_embd=5120, n_layer=64, n_ff=25600, n_head=64, n_head_kv=8, head_dim=128, vocab=151936)
 
 
-def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool = False):
+def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool = False, shard_only: bool = False,
+                    profile: bool = False):
     """Config 4: random-init Qwen3-32B shapes (64 layers, hidden 5120, FFN 25600, 64 query / 8 KV
     heads, head_dim 128, vocab 151936), Q4_K everywhere but Q6_K ffn_down, f16 output head, f16 KV
     cache of 8192 positions, tensor-parallel over the `world` GPUs.  Every rank draws every full
@@ -449,7 +450,11 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool
 
     With `parity` (world > 1), rank 0 also builds the whole model on its own GPU from the same full
     matrices (TP 1) and runs the same calls on it: the logits of the first decode step of TP `world`
-    against TP 1 (max |diff| / max |logit|) and how many of the greedy tokens agree."""
+    against TP 1 (max |diff| / max |logit|) and how many of the greedy tokens agree.
+
+    With `shard_only` one process builds rank `rank`'s shard alone, without a group: the same GEMV,
+    attention and head launches as that rank at TP `world` but no collective (its output head is its
+    vocab rows; the logits are meaningless), which separates the collectives' cost from the rest."""
     import ctypes as C
 
     import torch
@@ -467,18 +472,19 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool
     Fl = f1 - f0
     q0, q1, k0, k1 = rank * Hl * hd, (rank + 1) * Hl * hd, rank * KVl * hd, (rank + 1) * KVl * hd
     v0, v1 = ranges(V, world)[rank]                     # this rank's rows of the vocab-split output head
-    parity = parity and world > 1 and rank == 0 and n_seq == 1
+    parity = parity and world > 1 and rank == 0 and n_seq == 1 and not shard_only
     ctx = Context(device)
     L = ctx.lib
     uid = b"\0" * 128
-    if world > 1:
+    if world > 1 and not shard_only:
         import torch.distributed as dist
         obj = [tp_unique_id(ctx) if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         uid = obj[0]
 
     def create(heads, kv_heads, ff):
-        mc = ModelConfig(n_embd=E, n_layer=NL, n_ff=ff, n_head=heads, n_head_kv=kv_heads, head_dim=hd, n_rot=hd, vocab=V,
+        vocab = v1 - v0 if shard_only else V
+        mc = ModelConfig(n_embd=E, n_layer=NL, n_ff=ff, n_head=heads, n_head_kv=kv_heads, head_dim=hd, n_rot=hd, vocab=vocab,
                          neox=1, kv_f16=1, ctx=TP_CTX, n_seq=n_seq, max_batch=64, logits_batch=16,
                          rms_eps=float(np.float32(1e-6)), rope_base=1e6)
         hh = C.c_void_p()
@@ -487,7 +493,7 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool
 
     h = create(Hl, KVl, Fl)
     h1 = create(H, KV, F) if parity else None
-    if world > 1:
+    if world > 1 and not shard_only:
         ub = C.create_string_buffer(uid, 128)
         check(L.zllm_model_set_tp(h, rank, world, ub), ctx.h)
         check(L.zllm_model_set_vocab_shard(h, v0, v1 - v0), ctx.h)
@@ -524,7 +530,10 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool
             if hh is not None:
                 check(L.zllm_model_set_vector(hh, kind, layer, a.ctypes.data_as(C.c_void_p), a.size), ctx.h)
 
-    mat(T_TOK_EMBD, 0, ggml.Q4_K, V, E)
+    if shard_only:                                        # the shard's vocab: its head rows, an embedding of as many
+        mat(T_TOK_EMBD, 0, ggml.Q4_K, v1 - v0, E)
+    else:
+        mat(T_TOK_EMBD, 0, ggml.Q4_K, V, E)
     mat(T_OUTPUT, 0, ggml.F16, V, E, ("rows", v0, v1))
     vec(T_OUTPUT_NORM, 0, E)
     for l in range(NL):
@@ -541,7 +550,7 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool
     P = lambda a: a.ctypes.data_as(C.c_void_p)
     arg = np.zeros(64, np.int32)
     first = np.zeros(n_seq, np.int32)
-    prompts = [rng.integers(0, V, TP_PROMPT).astype(np.int32) for _ in range(n_seq)]
+    prompts = [rng.integers(0, (v1 - v0) if shard_only else V, TP_PROMPT).astype(np.int32) for _ in range(n_seq)]
 
     def prefill(hh):
         for s_ in range(n_seq):
@@ -566,11 +575,16 @@ def tp_decode_bench(n_seq: int, world: int, rank: int, device: int, parity: bool
     cur = np.ascontiguousarray(out[2])
     st = torch.cuda.ExternalStream(L.zllm_model_stream(h), device=f"cuda:{device}")
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = 2 if profile else TP_STEPS
+    if profile:
+        torch.cuda.nvtx.range_push("decode")        # ncu --nvtx --nvtx-include "decode/" captures these steps
     e0.record(st)
-    check(L.zllm_model_generate(h, 0, seqp, P(cur), n_seq, TP_STEPS, P(out)), ctx.h)
+    check(L.zllm_model_generate(h, 0, seqp, P(cur), n_seq, steps, P(out)), ctx.h)
     e1.record(st)
     e1.synchronize()
-    dt = e0.elapsed_time(e1) / 1e3
+    if profile:
+        torch.cuda.nvtx.range_pop()
+    dt = e0.elapsed_time(e1) / 1e3 * TP_STEPS / steps
     res = {}
     if h1 is not None:                                   # TP 1 on rank 0: the same calls
         toks = np.concatenate([warm, out[:, 0]])
@@ -954,11 +968,21 @@ def main():
                     help="plain launches (for ncu): batched GEMV of the Q4_K 24576 x 4096 gate/up matrix at NTOK tokens")
     ap.add_argument("--profile-attn", type=int, nargs=2, default=None, metavar=("CTX", "NSEQ"),
                     help="plain launches (for ncu): config-2 append + attention at CTX positions and NSEQ sequences")
+    ap.add_argument("--tp-shard", type=int, default=0, metavar="T",
+                    help="time rank 0's shard of the 32B tensor-parallel model at TP T alone on one GPU (no collective), "
+                         "decode at one sequence; with --profile, 2 steps inside an NVTX range 'decode' (for ncu)")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="NSEQ",
                     help="only the 8B decode at NSEQ sequences, 2 steps inside an NVTX range 'decode' (for ncu)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args.gpus)
+    if args.tp_shard:
+        import torch
+        torch.cuda.set_device(local)
+        r = tp_decode_bench(1, args.tp_shard, 0, local, shard_only=True, profile=args.profile)
+        print(json.dumps({"tp_shard": args.tp_shard, "ms_per_step": r["ms_per_step"], "tok_s": round(TP_STEPS / r["seconds"], 1),
+                          "weight_bytes_per_rank": r["weight_bytes_per_rank"]}))
+        return
     if args.profile_decode:
         import torch
         torch.cuda.set_device(local)

@@ -189,6 +189,38 @@ int zllm_attn_decode(zllm_ctx *ctx, const zllm_attn_geom *g, const float *q, con
 int zllm_attn_decode_noalloc(zllm_ctx *ctx, const zllm_attn_geom *g, const float *q, const void *kcache,
                              const void *vcache, const int32_t *npos, int nseq, int max_pos, float *out, void *stream);
 
+/* ------------------------------------------------------------------------ paged KV caches
+ * A layer's K cache and V cache as pools of fixed-size pages instead of one contiguous run per
+ * sequence: each pool holds num_pages pages of [n_head_kv][page_size][head_dim] elements (f16 or f32
+ * as g->kv_f16), and row s of block_table lists sequence s's pages in position order, so position p
+ * of sequence s is row p % page_size of page block_table[s * max_pages + p / page_size].  Memory then
+ * follows the positions in use (a server pages 64 sequences of up to 32k positions without reserving
+ * 64 x 32k per layer up front) and sequences that share a prefix can point at the same pages.  The
+ * reference keeps one contiguous cache per worker (src/compute/worker.js:121-125); it has no paging.
+ * page_size is a power of two from 16 to 4096; block_table is device memory.  A position past a row's
+ * max_pages pages, or a table entry outside [0, num_pages), reads page 0 and makes the next
+ * synchronizing call (zllm_sync) return ZLLM_E_ARG. */
+typedef struct {
+  const int32_t *block_table;  /* device [rows][max_pages] page indices */
+  int max_pages;               /* entries per row */
+  int num_pages;               /* pages in each pool */
+  int page_size;               /* positions per page */
+} zllm_kv_pages;
+
+/* zllm_qkv_append into paged pools: token t goes to position pos[t] of sequence seq[t] (table row
+ * seq[t]); the arithmetic and the stored bits are zllm_qkv_append's. */
+int zllm_qkv_append_paged(zllm_ctx *ctx, const zllm_attn_geom *g, const zllm_kv_pages *pages, int ntok, const float *q,
+                          int64_t q_stride, const float *k, const float *v, int64_t kv_stride, const float *bq,
+                          const float *bk, const float *bv, const float *q_norm, const float *k_norm,
+                          const float *rope_cos, const float *rope_sin, const int32_t *pos, const int32_t *seq,
+                          float *q_out, void *kpool, void *vpool, void *stream);
+/* zllm_attn_decode over paged pools: query s attends to positions [0, npos[s]) of table row s
+ * (max_pos <= max_pages * page_size).  The same context split and arithmetic as zllm_attn_decode, so
+ * the outputs are the same bits as over a contiguous cache holding the same rows. */
+int zllm_attn_decode_paged(zllm_ctx *ctx, const zllm_attn_geom *g, const zllm_kv_pages *pages, const float *q,
+                           const void *kpool, const void *vpool, const int32_t *npos, int nseq, int max_pos, float *out,
+                           void *stream);
+
 /* kvSet: n positions of one layer's K or V block of one sequence from f32 [n][n_head_kv*head_dim]
  * (device) -- cast to f16 when kv_f16.  kvGet: the reverse (f16 -> f32 exact).
  * src/compute/worker.js:457-472, src/compute/pool.js:225-238. */

@@ -74,8 +74,8 @@ def test_rmsnorm_quant_bit_exact(ctx, n):
     xq = torch.empty((ntok, n), dtype=torch.int8, device="cuda")
     xd = torch.empty((ntok, n // 32), device="cuda")
     xs = torch.empty((ntok, n // 32), dtype=torch.int32, device="cuda")
-    check(ctx.lib.zllm_rmsnorm_quant(ctx.h, _P(_dev(x)), _P(_dev(w)), n, ntok, EPS, _P(xb), _P(xq), _P(xd), _P(xs), None),
-          ctx.h)
+    xg, wg = _dev(x), _dev(w)                      # held: a freed temporary's memory would be reused
+    check(ctx.lib.zllm_rmsnorm_quant(ctx.h, _P(xg), _P(wg), n, ntok, EPS, _P(xb), _P(xq), _P(xd), _P(xs), None), ctx.h)
     ctx.sync()
     for t in range(ntok):
         want = O.rmsnorm(x[t], w, EPS)
@@ -95,8 +95,8 @@ def test_swiglu_quant_bit_exact(ctx):
     xq = torch.empty((ntok, n), dtype=torch.int8, device="cuda")
     xd = torch.empty((ntok, n // 32), device="cuda")
     xs = torch.empty((ntok, n // 32), dtype=torch.int32, device="cuda")
-    check(ctx.lib.zllm_swiglu_quant(ctx.h, _P(_dev(gate)), _P(_dev(up)), n, ntok, stride, _P(hb), _P(xq), _P(xd),
-                                    _P(xs), None), ctx.h)
+    gg, ug = _dev(gate), _dev(up)
+    check(ctx.lib.zllm_swiglu_quant(ctx.h, _P(gg), _P(ug), n, ntok, stride, _P(hb), _P(xq), _P(xd), _P(xs), None), ctx.h)
     ctx.sync()
     for t in range(ntok):
         want = np.array([np.float32(O.silu(float(g)) * float(u)) for g, u in zip(gate[t, :n], up[t, :n])], np.float32)
@@ -130,7 +130,8 @@ def test_fused_gemv_rmsnorm_staging_bit_exact(ctx, t):
     xn = O.rmsnorm(x, nw, EPS)
     q, d, s = O.quantize_act(xn)
     y = torch.empty((1, rows), device="cuda")
-    check(ctx.lib.zllm_mm(ctx.h, w.h, _P(_dev(q)), _P(_dev(d)), _P(_dev(s)), None, 1, _P(y), rows, None, None), ctx.h)
+    qg, dg, sg = _dev(q), _dev(d), _dev(s)
+    check(ctx.lib.zllm_mm(ctx.h, w.h, _P(qg), _P(dg), _P(sg), None, 1, _P(y), rows, None, None), ctx.h)
     ctx.sync()
     assert np.array_equal(got, y[0].cpu().numpy())
     assert _rel(got, O.matvec(t, wt["data"], rows, cols, xn, nthreads=NTHREADS)) <= 1e-3

@@ -10,7 +10,7 @@ from __future__ import annotations
 import ctypes as C
 
 from .kernels import _ptr, _stream
-from .lib import AttnGeom, check
+from .lib import AttnGeom, KvPages, check
 
 
 def _torch():
@@ -116,3 +116,58 @@ def kv_copy(ctx, geom: AttnGeom, dst, dst_head_stride: int, src, src_head_stride
     st = _cur_stream(dst.device, stream)
     check(ctx.lib.zllm_kv_copy(ctx.h, C.byref(geom), _ptr(dst), dst_head_stride, _ptr(src), src_head_stride, n,
                                _stream(st)), ctx.h, "zllm_kv_copy")
+
+
+class PagedKV:
+    """Paged K and V pools of one layer: [num_pages][n_kv][page_size][hd] each (f16 bits as int16 or
+    f32), and a block table [rows][max_pages] int32 of page indices (zllm_kv_pages)."""
+
+    def __init__(self, ctx, n_kv: int, head_dim: int, num_pages: int, page_size: int, kv_f16: bool, table):
+        torch = _torch()
+        self.ctx, self.n_kv, self.head_dim, self.num_pages, self.page_size, self.kv_f16 = \
+            ctx, n_kv, head_dim, num_pages, page_size, kv_f16
+        dt = torch.int16 if kv_f16 else torch.float32
+        shape = (num_pages, n_kv, page_size, head_dim)
+        self.k = torch.zeros(shape, dtype=dt, device=f"cuda:{ctx.device}")
+        self.v = torch.zeros(shape, dtype=dt, device=f"cuda:{ctx.device}")
+        self.table = torch.as_tensor(table, dtype=torch.int32).to(f"cuda:{ctx.device}").contiguous()
+        self.max_pages = self.table.shape[1]
+
+    def desc(self) -> KvPages:
+        return KvPages(block_table=self.table.data_ptr(), max_pages=self.max_pages, num_pages=self.num_pages,
+                       page_size=self.page_size)
+
+    def geom(self, n_head: int, n_rot: int | None = None, neox: bool = True, eps: float = 1e-6) -> AttnGeom:
+        return AttnGeom(n_head=n_head, n_head_kv=self.n_kv, head_dim=self.head_dim,
+                        n_rot=self.head_dim if n_rot is None else n_rot, neox=1 if neox else 0,
+                        kv_f16=1 if self.kv_f16 else 0, ctx=self.max_pages * self.page_size, rms_eps=float(eps),
+                        seq_stride=0, head_stride=0)
+
+
+def qkv_append_paged(ctx, geom: AttnGeom, kv: PagedKV, q, k, v, pos, seq, rope, q_norm=None, k_norm=None, bq=None,
+                     bk=None, bv=None, q_out=None, stream=None):
+    """qkv_append into the paged pools (token t at position pos[t] of table row seq[t])."""
+    torch = _torch()
+    ntok = q.shape[0]
+    if q_out is None:
+        q_out = torch.empty((ntok, geom.n_head * geom.head_dim), dtype=torch.float32, device=q.device)
+    pg = kv.desc()
+    st = _cur_stream(q.device, stream)
+    check(ctx.lib.zllm_qkv_append_paged(ctx.h, C.byref(geom), C.byref(pg), ntok, _ptr(q), q.stride(0), _ptr(k), _ptr(v),
+                                        k.stride(0), _ptr(bq), _ptr(bk), _ptr(bv), _ptr(q_norm), _ptr(k_norm),
+                                        _ptr(rope[0]), _ptr(rope[1]), _ptr(pos), _ptr(seq), _ptr(q_out), _ptr(kv.k),
+                                        _ptr(kv.v), _stream(st)), ctx.h, "zllm_qkv_append_paged")
+    return q_out
+
+
+def attn_decode_paged(ctx, geom: AttnGeom, kv: PagedKV, q, npos, max_pos: int, out=None, stream=None):
+    """Decode attention over the paged pools: query s reads table row s."""
+    torch = _torch()
+    nseq = q.shape[0]
+    if out is None:
+        out = torch.empty_like(q)
+    pg = kv.desc()
+    st = _cur_stream(q.device, stream)
+    check(ctx.lib.zllm_attn_decode_paged(ctx.h, C.byref(geom), C.byref(pg), _ptr(q), _ptr(kv.k), _ptr(kv.v), _ptr(npos),
+                                         nseq, int(max_pos), _ptr(out), _stream(st)), ctx.h, "zllm_attn_decode_paged")
+    return out

@@ -112,6 +112,11 @@ int zllm_check_status(zllm_ctx *c) {
   if (e != cudaSuccess) return zllm_cuda_fail(c, e, "reading the device status word");
   if (st) {
     cudaMemset(c->status_dev, 0, sizeof(unsigned));
+    if (st == ST_BAD_ARGS) {
+      zllm_set_error(c, "a kernel found an index out of range in device data (status 0x%x: a paged-KV table entry or a "
+                        "position past its table row) and read page 0 instead", st);
+      return ZLLM_E_ARG;
+    }
     zllm_set_error(c, "device wait timed out (status 0x%x): a bulk copy, a stage hand-off or a peer GPU's all-reduce "
                       "slice did not complete within 2 s; the kernel drained its copies and returned", st);
     return ZLLM_E_TIMEOUT;

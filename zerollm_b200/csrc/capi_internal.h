@@ -48,4 +48,4 @@ int zllm_noalloc_setup(zllm_ctx *c);
 int zllm_attn_splits(const zllm_ctx *c, const zllm_attn_geom *g, int nseq, int max_pos);
 int zllm_attn_launch(zllm_ctx *c, const zllm_attn_geom *g, const float *q, const void *kcache, const void *vcache,
                      const int32_t *npos, int nseq, int nsplit, float *out, float *partial, int32_t *counters,
-                     cudaStream_t s, const int32_t *seq);
+                     cudaStream_t s, const int32_t *seq, const zllm::KvPages *pages);

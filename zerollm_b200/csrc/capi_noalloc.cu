@@ -110,5 +110,5 @@ extern "C" int zllm_attn_decode_noalloc(zllm_ctx *c, const zllm_attn_geom *g, co
   // the merge counters must start at zero; clear the ones this launch uses
   cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)groups * sizeof(int32_t), s);
   if (e != cudaSuccess) return zllm_cuda_fail(c, e, "zllm_attn_decode_noalloc: counter clear");
-  return zllm_attn_launch(c, g, q, kcache, vcache, npos, nseq, nsplit, out, partial, counters, s, nullptr);
+  return zllm_attn_launch(c, g, q, kcache, vcache, npos, nseq, nsplit, out, partial, counters, s, nullptr, nullptr);
 }

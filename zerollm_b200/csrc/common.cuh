@@ -81,6 +81,17 @@ __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, u
       : "memory");
 }
 
+// ---------------------------------------------------------------------------- cp.async (16 bytes)
+// global -> shared through L2 only; per-thread groups: commit closes the thread's group of copies
+// issued since the last commit, wait<N> returns once at most N of the thread's groups are pending
+// (hardware-tracked: no spin loop of ours).  Both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void *src_gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src_gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // ---------------------------------------------------------------------------- PDL
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

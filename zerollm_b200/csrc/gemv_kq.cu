@@ -14,14 +14,16 @@
 // The weights are stored as units of (16-row tile, super-block) (kq_layout.h); a CTA owns a
 // contiguous range of tiles.  The integer dots are warp-level MMAs (mma.sync m16n8k32 / m16n8k16,
 // uint8 or int8 x int8 -> int32, exact) on a unit, whose A operand is the unit itself:
-//   * one token (kq_stream_kernel): the B operand is block-diagonal -- column j carries the
+//   * one token (kq_ring_kernel): the B operand is block-diagonal -- column j carries the
 //     activation of sub-block (group) j and is zero elsewhere -- so the 8 MMAs of a unit leave the
-//     16 rows x 8 sub-blocks of integer dots in one accumulator.  Every warp streams its share of
-//     the CTA's units straight from HBM into registers (coalesced 16-byte loads, a few units in
-//     flight), with no shared-memory staging of the weights;
+//     16 rows x 8 sub-blocks of integer dots in one accumulator.  Every warp stages its share of
+//     the CTA's units through a shared-memory ring with 16-byte cp.async (coalesced 512-byte warp
+//     copies, several units in flight);
 //   * 2..16 tokens per launch (kq_batch_kernel): B column j carries token j, one MMA per sub-block
 //     (group) and group of 8 tokens.  The CTA's units are walked super-block by super-block, so a
-//     warp loads a super-block's activation fragments once and reuses them for every tile.
+//     warp loads a super-block's activation fragments once and reuses them for every tile; the
+//     block terms of a token pair are computed with packed f32x2 arithmetic, element for element
+//     the same rounding as the one-token kernel's scalar formula.
 // Block terms are f32 with a fixed formula shared by both kernels (k45_pair / q6_pair below); an
 // integer dot leaves the MMA already biased by 1.5 * 2^23 (the accumulator starts there), so one
 // subtraction turns it into the exact float.  The order of the additions is fixed as well: each
@@ -145,7 +147,7 @@ struct KqArgs {
   float *y;
   const float *y_add;
   int64_t y_stride;
-  int x_off, part_off;  // shared-memory regions
+  int x_off, part_off, ring_off;  // shared-memory regions
 };
 
 // tiles [T0, T1) of a CTA: an even split of the launch's tiles
@@ -218,6 +220,48 @@ __device__ double rms_scale(const float *x, int64_t n, double eps, int warp, int
   return __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(tot, (double)n), eps)));
 }
 
+// ---------------------------------------------------------------------------- exact quantizeAct, f32 fast path
+// quantizeAct (src/compute/ref-kernels.js:44-62) computes, per 32-value block with maximum |x| amax,
+//   scale = amax / 127, d = f32(scale), inv = 1 / scale, q = round-half-away(x * inv)   (doubles).
+// The same integers come out of f32 arithmetic almost always:
+//   * d: for every float amax, f32(amax / 127 in double) equals the f32 quotient amax / 127.f --
+//     127's binary expansion repeats with period 7, so the double quotient can never sit on an
+//     f32 rounding midpoint (checked exhaustively over all positive floats);
+//   * q: r = x * f32(127 / amax) is within |r| * 2^-23 <= 1.6e-5 of the double product, so it rounds
+//     the same way unless its fraction is within 2^-12 of one half; those values (about 5 in 10^4
+//     of random inputs) and every value of a block whose amax is below 2^-96 (where 127 / amax
+//     leaves f32's range) take the double formula itself.
+// amax == 0 and amax == inf both give inv == 0 in the reference (1 / inf), hence invf = 0.
+struct QuantBlock { float d, invf; bool dbl; };
+__device__ __forceinline__ QuantBlock quant_block(float amax) {
+  QuantBlock b;
+  b.d = __fdiv_rn(amax, 127.f);
+  b.dbl = amax > 0.f && amax < 0x1p-96f;
+  b.invf = (amax == 0.f || isinf(amax) || b.dbl) ? 0.f : __fdiv_rn(127.f, amax);
+  return b;
+}
+// q of one value from the f32 estimate; `slow` is set (and q is meaningless) when the value must take
+// the double formula (quant_value_dbl): a fraction within 2^-12 of one half, a NaN, or a block whose
+// amax is below 2^-96.  The rounding adds 1.5 * 2^23, which leaves r rounded to the nearest integer
+// (ties to even) in the low mantissa bits; away from the ties that is round-half-away, and the ties
+// are among the slow values.
+__device__ __forceinline__ int quant_value_fast(float x, const QuantBlock &b, bool &slow) {
+  const float r = __fmul_rn(x, b.invf);
+  const float t = __fadd_rn(r, kBiasF);
+  const float e = __fsub_rn(r, __fsub_rn(t, kBiasF));   // r minus its rounded value, exactly
+  slow = b.dbl || !(fabsf(e) < 0.5f - 0x1p-12f);          // NaN lands here too
+  return __float_as_int(t) - kBias;
+}
+// the reference's double formula itself (bad: the value is NaN or NaN after scaling -- q is 0 and the
+// block sum becomes 0)
+__device__ __noinline__ int quant_value_dbl(float x, float amax, bool &bad) {
+  const double scale = __ddiv_rn((double)amax, 127.0);
+  const double inv = scale != 0.0 ? __ddiv_rn(1.0, scale) : 0.0;
+  const double rd = round(__dmul_rn((double)x, inv));       // half away from zero
+  bad = !(rd == rd);
+  return bad ? 0 : (int)rd;
+}
+
 // Quantize one token's f32 activation into shared memory; bit-exact with quantize_act_kernel
 // (quantizeAct, src/compute/ref-kernels.js:44-62).  32 / V lanes own a 32-value block, V values each
 // (V = 8 when the token fits one round of the CTA's threads -- K <= 4096 -- else 16: fewer rounds of
@@ -255,27 +299,38 @@ __device__ void quantize_rounds(const float *x, int64_t k, const float *norm_w, 
     }
     float a = 0.f;
 #pragma unroll
-    for (int i = 0; i < V; i++) {
-      const float m = fabsf(v[i]);
-      if (m > a) a = m;                         // NaN never raises amax (as `Math.abs(NaN) > amax`)
-    }
+    for (int i = 0; i < V; i++) a = fmaxf(a, fabsf(v[i]));   // NaN never raises amax (as `Math.abs(NaN) > amax`)
 #pragma unroll
     for (int o = 1; o < LPB; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    const double scale = __ddiv_rn((double)a, 127.0);
-    const double inv = scale != 0.0 ? __ddiv_rn(1.0, scale) : 0.0;
-    uint32_t words[V / 4];
-#pragma unroll
-    for (int i = 0; i < V / 4; i++) words[i] = 0u;
-    int sum = 0;
-    bool nan = false;
+    const QuantBlock qb_ = quant_block(a);
+    int qv[V];
+    uint32_t slow = 0u;
 #pragma unroll
     for (int i = 0; i < V; i++) {
-      const double r = round(__dmul_rn((double)v[i], inv));   // half away from zero
-      const bool bad = !(r == r);
-      const int q = bad ? 0 : (int)r;
+      bool sl;
+      qv[i] = quant_value_fast(v[i], qb_, sl);
+      slow |= (uint32_t)sl << i;
+    }
+    bool nan = false;
+    while (slow) {                              // rare: the values the f32 estimate cannot settle
+      const int i = __ffs(slow) - 1;
+      slow &= slow - 1u;
+      bool bad;
+      float xi = v[0];
+#pragma unroll
+      for (int j = 1; j < V; j++) xi = j == i ? v[j] : xi;
+      const int q = quant_value_dbl(xi, a, bad);
       nan |= bad;
-      sum += q;
-      words[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
+#pragma unroll
+      for (int j = 0; j < V; j++) qv[j] = j == i ? q : qv[j];
+    }
+    uint32_t words[V / 4];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < V / 4; i++) {           // the low bytes of four q, then their sum
+      words[i] = __byte_perm(__byte_perm(qv[4 * i], qv[4 * i + 1], 0x0040), __byte_perm(qv[4 * i + 2], qv[4 * i + 3], 0x0040),
+                             0x5410);
+      sum = __dp4a((int)words[i], 0x01010101, sum);
     }
     const int s16 = V == 16 ? sum : sum + __shfl_xor_sync(0xffffffffu, sum, 1);   // the 16-value group
     int s32 = s16;
@@ -288,7 +343,7 @@ __device__ void quantize_rounds(const float *x, int64_t k, const float *norm_w, 
       if constexpr (FMT == T_Q6_K) {
         if (V == 16 || (lane & 1) == 0) put_group_off(ssc1, qb * V / 16, s16);
       }
-      if ((lane & (LPB - 1)) == 0) put_block_scales<FMT>(ssc0, qb / LPB, __double2float_rn(scale), nan32 ? 0 : s32);
+      if ((lane & (LPB - 1)) == 0) put_block_scales<FMT>(ssc0, qb / LPB, qb_.d, nan32 ? 0 : s32);
     }
   }
 }
@@ -337,26 +392,6 @@ template <int FMT> struct PairRegs;
 template <> struct PairRegs<T_Q4_K> { uint4 q[2][2]; uint4 h[2]; };             // quants [row][half], header [row]
 template <> struct PairRegs<T_Q5_K> { uint4 q[2][2]; uint4 h[2]; uint2 e[2]; }; // + high bits [row]
 template <> struct PairRegs<T_Q6_K> { uint4 l[2][2]; uint4 qh[2]; uint32_t sc[2]; uint4 sc16[2]; uint32_t d[2]; };
-
-template <int FMT, bool ALL_SC = false>
-__device__ __forceinline__ void load_unit(PairRegs<FMT> &R, const uint8_t *u, int lane, int g) {
-#pragma unroll
-  for (int r = 0; r < 2; r++) {
-    if constexpr (FMT == T_Q6_K) {
-      R.l[r][0] = ldg128(u + ((2 * r) * 32 + lane) * 16);
-      R.l[r][1] = ldg128(u + ((2 * r + 1) * 32 + lane) * 16);
-      R.qh[r] = ldg128(u + kQ6H + (r * 32 + lane) * 16);
-      if constexpr (ALL_SC) R.sc16[r] = ldg128(u + kQ6S + 16 * (8 * r + g));
-      else R.sc[r] = __ldg(reinterpret_cast<const uint32_t *>(u + kQ6S + (r * 32 + lane) * 4));
-      R.d[r] = __ldg(reinterpret_cast<const unsigned short *>(u + kQ6D + 2 * (8 * r + g)));
-    } else {
-      R.q[r][0] = ldg128(u + ((2 * r) * 32 + lane) * 16);
-      R.q[r][1] = ldg128(u + ((2 * r + 1) * 32 + lane) * 16);
-      R.h[r] = ldg128(u + hdr_off<FMT>() + 16 * (8 * r + g));
-      if constexpr (FMT == T_Q5_K) R.e[r] = __ldg(reinterpret_cast<const uint2 *>(u + kE5 + (r * 32 + lane) * 8));
-    }
-  }
-}
 
 // The A operands of chunk c (sub-blocks 2c and 2c + 1) of a Q4_K / Q5_K unit: lo = {row g k 0-3,
 // row g+8 k 0-3, row g k 16-19, row g+8 k 16-19} of sub-block 2c, hi the same of sub-block 2c + 1.
@@ -443,53 +478,90 @@ __device__ __forceinline__ void pair_sums(const PairRegs<FMT> &R, int g, int t, 
   }
 }
 
-// One token.  A CTA owns tiles [T0, T1); their units, (tile, super-block) in order, are one
-// contiguous range, cut into 16 equal runs, one per warp.  A warp keeps D units of loads in flight
-// in registers -- the first ones issued before griddepcontrol.wait -- and writes each unit's two
-// super-block sums to shared memory.  After one CTA barrier a thread per row adds its super-block
-// sums in super-block order and applies the epilogue.  No waits on other warps or copies: nothing
-// to bound.
-constexpr int kStreamWarps = 16;
-constexpr int kStreamDepth = 2;
+// ---------------------------------------------------------------------------- one token, shared-memory ring
+// Every warp stages its share of the CTA's units through its own ring of S unit slots in shared
+// memory with 16-byte cp.async (lane l copies the unit's 16-byte pieces l, l + 32, ..., the pieces it
+// reads back itself, except for the row headers): S units per warp -- for a 4096-row matrix the
+// SM's whole share -- are in flight before griddepcontrol.wait, and the registers only ever hold the
+// unit being computed.  Sixteen warps (one CTA per SM) keep enough independent work in flight to
+// cover the MMA, shared-memory and shuffle latencies of the unit arithmetic; measured on a B200
+// against eight warps with two CTAs per SM (the next launch's CTA resident and loading under
+// programmatic dependent launch), which was 20-30 % slower.  Waits are cp.async.wait_group (tracked
+// by the hardware, no spin loop) and warp / CTA barriers: nothing to bound.
+template <int FMT> constexpr int ring_slots() { return FMT == T_Q4_K ? 4 : 3; }
+constexpr int kRingWarps = 16;
 
 template <int FMT>
-__global__ void __launch_bounds__(kStreamWarps * 32, 1) kq_stream_kernel(const KqArgs p) {
-  constexpr int NT = kStreamWarps * 32, D = kStreamDepth, US = unit_bytes<FMT>();
+__device__ __forceinline__ void copy_unit(uint32_t dst, const uint8_t *src, int lane) {
+  constexpr int CH = unit_bytes<FMT>() / 16;
+#pragma unroll
+  for (int c = lane; c < CH; c += 32) cp_async16(dst + 16 * c, src + 16 * c);
+}
+
+// load_unit's registers from a unit staged in shared memory (same offsets)
+template <int FMT>
+__device__ __forceinline__ void load_unit_smem(PairRegs<FMT> &R, uint32_t u, int lane, int g) {
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    if constexpr (FMT == T_Q6_K) {
+      R.l[r][0] = lds128(u + ((2 * r) * 32 + lane) * 16);
+      R.l[r][1] = lds128(u + ((2 * r + 1) * 32 + lane) * 16);
+      R.qh[r] = lds128(u + kQ6H + (r * 32 + lane) * 16);
+      R.sc[r] = lds32(u + kQ6S + (r * 32 + lane) * 4);
+      R.d[r] = lds16(u + kQ6D + 2 * (8 * r + g));
+    } else {
+      R.q[r][0] = lds128(u + ((2 * r) * 32 + lane) * 16);
+      R.q[r][1] = lds128(u + ((2 * r + 1) * 32 + lane) * 16);
+      R.h[r] = lds128(u + hdr_off<FMT>() + 16 * (8 * r + g));
+      if constexpr (FMT == T_Q5_K) R.e[r] = lds64(u + kE5 + (r * 32 + lane) * 8);
+    }
+  }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kRingWarps * 32, 1) kq_ring_kernel(const KqArgs p) {
+  constexpr int NT = kRingWarps * 32, S = ring_slots<FMT>(), US = unit_bytes<FMT>();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   int T0, T1;
   cta_tiles(p.rows, T0, T1);
   const int nb = p.nb;
   const int npair = (T1 - T0) * nb;
-  const int i0 = (int)((int64_t)warp * npair / kStreamWarps), i1 = (int)((int64_t)(warp + 1) * npair / kStreamWarps);
+  const int i0 = (int)((int64_t)warp * npair / kRingWarps), i1 = (int)((int64_t)(warp + 1) * npair / kRingWarps);
   const int64_t row0 = (int64_t)T0 * kTile;
   const int nrows = (int)(min((int64_t)T1 * kTile, p.rows) - row0);
   float *sums = reinterpret_cast<float *>(smem + p.part_off);      // [pair][16 rows]
+  const uint32_t ring = smem_u32(smem + p.ring_off) + (uint32_t)(warp * S * US);
   const uint8_t *base = p.w + (int64_t)T0 * nb * US;
 
-  PairRegs<FMT> R[D];
+  // the first S units of the warp (the weights are not the previous kernel's output)
 #pragma unroll
-  for (int d = 0; d < D; d++)
-    if (i0 + d < i1) load_unit<FMT>(R[d], base + (int64_t)(i0 + d) * US, lane, g);   // not the previous kernel's output
+  for (int d = 0; d < S; d++) {
+    if (i0 + d < i1) copy_unit<FMT>(ring + d * US, base + (int64_t)(i0 + d) * US, lane);
+    cp_async_commit();
+  }
   pdl_launch_dependents();
   pdl_wait();                                   // the activation is
   const SAct sa = stage_token<FMT, NT>(p, smem + p.x_off, warp, lane, g);
   __syncthreads();
 
   int sb = nb > 0 ? i0 % nb : 0;                // super-block of unit i
-  for (int i = i0; i < i1; i += D) {
-#pragma unroll
-    for (int d = 0; d < D; d++) {
-      const int ii = i + d;
-      if (ii < i1) {
-        float S0, S1;
-        pair_sums<FMT>(R[d], g, t, sa, sb, S0, S1);
-        if (ii + D < i1) load_unit<FMT>(R[d], base + (int64_t)(ii + D) * US, lane, g);
-        if (t == 0) { sums[ii * kTile + g] = S0; sums[ii * kTile + g + 8] = S1; }
-        if (++sb == nb) sb = 0;
-      }
-    }
+  int slot = 0;
+  for (int i = i0; i < i1; i++) {
+    cp_async_wait<S - 1>();                     // unit i (the oldest pending group) has landed
+    __syncwarp();                               // ... and every lane's pieces of it are visible
+    PairRegs<FMT> R;
+    load_unit_smem<FMT>(R, ring + slot * US, lane, g);
+    float S0, S1;
+    pair_sums<FMT>(R, g, t, sa, sb, S0, S1);
+    __syncwarp();                               // every lane is done with the slot
+    if (i + S < i1) copy_unit<FMT>(ring + slot * US, base + (int64_t)(i + S) * US, lane);
+    cp_async_commit();                          // one group per iteration, empty or not
+    if (t == 0) { sums[i * kTile + g] = S0; sums[i * kTile + g + 8] = S1; }
+    if (++sb == nb) sb = 0;
+    if (++slot == S) slot = 0;
   }
+  cp_async_wait<0>();
   __syncthreads();
 
   // one thread per row (per (gate, up) pair with swiglu): the super-block sums in order
@@ -508,33 +580,81 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 1) kq_stream_kernel(const K
 }
 
 // ---------------------------------------------------------------------------- 2..16 tokens
-// Per-warp scale staging of one super-block for the batch kernel:
-//   Q4_K / Q5_K: [token][pair c] float4 (xd, xd, xd*xs, xd*xs of 32-blocks 2c, 2c + 1);
-//   Q6_K:        [token][32-block] float xd.
+// Packed pairs of f32 (Blackwell's f32x2 arithmetic): element x in the low word, y in the high word.
+// Each element is rounded exactly as the scalar instruction rounds it, so a packed term is the same
+// bits as the scalar formula (k45_pair / q6_pair) of each of its two tokens.
+typedef unsigned long long f2v;
+__device__ __forceinline__ f2v f2pack(float x, float y) {
+  f2v r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ f2v f2bits(uint32_t x, uint32_t y) {
+  f2v r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(x), "r"(y));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(f2v v, float &x, float &y) { asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v)); }
+__device__ __forceinline__ f2v f2fma(f2v a, f2v b, f2v c) {
+  f2v d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f2v f2mul(f2v a, f2v b) {
+  f2v d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2v f2add(f2v a, f2v b) {
+  f2v d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2v f2sub(f2v a, f2v b) {
+  f2v d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+constexpr f2v kBias2 = ((f2v)0x4B400000u << 32) | 0x4B400000u;    // (kBiasF, kBiasF)
+// two biased MMA accumulators -> their exact integer values as a pair
+__device__ __forceinline__ f2v biased_f2(int a, int b) { return f2sub(f2bits((uint32_t)a, (uint32_t)b), kBias2); }
+
+// Per-warp scale staging of one super-block, token pairs (2u, 2u + 1) packed:
+//   Q4_K / Q5_K: [pair u][chunk c] 32 bytes: (xd0, xd0'), (xd1, xd1'), (xm0, xm0'), (xm1, xm1') with
+//                xd0 / xd1 the scales of 32-blocks 2c, 2c + 1 and xm = xd * xs (unprimed: token 2u);
+//   Q6_K:        [pair u][32-block b] (xd, xd').
 template <int FMT, int NTOK> constexpr int batch_sc_bytes() { return FMT == T_Q6_K ? NTOK * 8 * 4 : NTOK * 4 * 16; }
 
 template <int FMT, int NTOK>
 __device__ __forceinline__ void stage_batch_scales(const KqArgs &p, int sb, uint8_t *wsc, int lane) {
   const int64_t kb = p.k / 32;
   if constexpr (FMT == T_Q6_K) {
-    float *o = reinterpret_cast<float *>(wsc);
+    float2 *o = reinterpret_cast<float2 *>(wsc);
 #pragma unroll
-    for (int e = lane; e < NTOK * 8; e += 32) {
-      const int tok = e >> 3, b = e & 7;
-      o[e] = tok < p.ntok ? __ldg(p.xd + tok * kb + sb * 8 + b) : 0.f;
+    for (int e = lane; e < NTOK / 2 * 8; e += 32) {
+      const int u = e >> 3, b = e & 7, t0 = 2 * u, t1 = 2 * u + 1;
+      o[e] = make_float2(t0 < p.ntok ? __ldg(p.xd + t0 * kb + sb * 8 + b) : 0.f,
+                         t1 < p.ntok ? __ldg(p.xd + t1 * kb + sb * 8 + b) : 0.f);
     }
   } else {
     float4 *o = reinterpret_cast<float4 *>(wsc);
 #pragma unroll
-    for (int e = lane; e < NTOK * 4; e += 32) {
-      const int tok = e >> 2, c = e & 3;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (tok < p.ntok) {
-        const float2 xd = __ldg(reinterpret_cast<const float2 *>(p.xd + tok * kb + sb * 8 + 2 * c));
-        const int2 xs = __ldg(reinterpret_cast<const int2 *>(p.xs + tok * kb + sb * 8 + 2 * c));
-        v = make_float4(xd.x, xd.y, __fmul_rn(xd.x, __int2float_rn(xs.x)), __fmul_rn(xd.y, __int2float_rn(xs.y)));
+    for (int e = lane; e < NTOK / 2 * 4; e += 32) {
+      const int u = e >> 2, c = e & 3;
+      float v[2][4];
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const int tok = 2 * u + j;
+        v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
+        if (tok < p.ntok) {
+          const float2 xd = __ldg(reinterpret_cast<const float2 *>(p.xd + tok * kb + sb * 8 + 2 * c));
+          const int2 xs = __ldg(reinterpret_cast<const int2 *>(p.xs + tok * kb + sb * 8 + 2 * c));
+          v[j][0] = xd.x; v[j][1] = xd.y;
+          v[j][2] = __fmul_rn(xd.x, __int2float_rn(xs.x)); v[j][3] = __fmul_rn(xd.y, __int2float_rn(xs.y));
+        }
       }
-      o[e] = v;
+      o[2 * e] = make_float4(v[0][0], v[1][0], v[0][1], v[1][1]);
+      o[2 * e + 1] = make_float4(v[0][2], v[1][2], v[0][3], v[1][3]);
     }
   }
 }
@@ -554,47 +674,61 @@ __device__ __forceinline__ void load_batch_b(const KqArgs &p, int sb, int g, int
   }
 }
 
-// One Q4_K / Q5_K unit for NG token groups: S[G][e] = the super-block sum of row g + 8 (e >> 1),
-// token 8G + 2t + (e & 1), in the canonical order.
+// One Q4_K / Q5_K unit for NG token groups: S[G][r] = the super-block sums of row g + 8r for tokens
+// 8G + 2t and 8G + 2t + 1 (packed), in the canonical order: k45_pair per chunk, ((P0 + P1) + (P2 + P3)).
 template <int FMT, int NG>
 __device__ __forceinline__ void unit_k45_batch(const PairRegs<FMT> &R, const uint32_t (&B)[NG][16], uint32_t wsc, int t,
-                                               float (&S)[NG][4]) {
+                                               f2v (&S)[NG][2]) {
   constexpr bool FIVE = FMT == T_Q5_K;
   uint2 eg = make_uint2(0, 0), eh = make_uint2(0, 0);
   if constexpr (FIVE) { eg = R.e[0]; eh = R.e[1]; }
   const float d[2] = {h2f(R.h[0].x & 0xffffu), h2f(R.h[1].x & 0xffffu)};
   const float dm[2] = {h2f(R.h[0].x >> 16), h2f(R.h[1].x >> 16)};
-  float q01[NG][4];
+  f2v q01[NG][2];
 #pragma unroll
   for (int c = 0; c < 4; c++) {
     uint32_t lo[4], hi[4];
     k45_operands<FIVE>(R.q, eg, eh, c, lo, hi);
-    const K45Sc s[2] = {k45_sc(d[0], dm[0], k45_field(R.h[0], c)), k45_sc(d[1], dm[1], k45_field(R.h[1], c))};
+    // per row: (d*sc) of both sub-blocks and -(dmin*mn), broadcast to both tokens of a pair
+    f2v ds0[2], ds1[2], ndm0[2], ndm1[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const K45Sc s = k45_sc(d[r], dm[r], k45_field(R.h[r], c));
+      ds0[r] = f2pack(s.ds0, s.ds0); ds1[r] = f2pack(s.ds1, s.ds1);
+      ndm0[r] = f2pack(-s.dm0, -s.dm0); ndm1[r] = f2pack(-s.dm1, -s.dm1);
+    }
 #pragma unroll
     for (int G = 0; G < NG; G++) {
       int L[4] = {kBias, kBias, kBias, kBias}, U[4] = {kBias, kBias, kBias, kBias};
       mma_k32(L, lo[0], lo[1], lo[2], lo[3], B[G][4 * c], B[G][4 * c + 1]);
       mma_k32(U, hi[0], hi[1], hi[2], hi[3], B[G][4 * c + 2], B[G][4 * c + 3]);
-      const uint4 w0 = lds128(wsc + 16 * ((8 * G + 2 * t) * 4 + c)), w1 = lds128(wsc + 16 * ((8 * G + 2 * t + 1) * 4 + c));
-      const float4 xdm[2] = {make_float4(__uint_as_float(w0.x), __uint_as_float(w0.y), __uint_as_float(w0.z), __uint_as_float(w0.w)),
-                             make_float4(__uint_as_float(w1.x), __uint_as_float(w1.y), __uint_as_float(w1.z), __uint_as_float(w1.w))};
+      const uint32_t a = wsc + 32 * ((4 * G + t) * 4 + c);
+      const uint4 w0 = lds128(a), w1 = lds128(a + 16);
+      const f2v xd0 = f2bits(w0.x, w0.y), xd1 = f2bits(w0.z, w0.w), xm0 = f2bits(w1.x, w1.y), xm1 = f2bits(w1.z, w1.w);
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float P = k45_pair(s[e >> 1], biased_f(L[e]), biased_f(U[e]), xdm[e & 1]);
-        if (c == 0 || c == 2) q01[G][e] = P;
-        else if (c == 1) S[G][e] = __fadd_rn(q01[G][e], P);
-        else S[G][e] = __fadd_rn(S[G][e], __fadd_rn(q01[G][e], P));
+      for (int r = 0; r < 2; r++) {
+        // k45_pair for both tokens: fma(xd1*ds1, lo1, fma(xd0*ds0, lo0, -(fma(dm1, xm1, dm0*xm0))))
+        const f2v nm = f2fma(ndm1[r], xm1, f2mul(ndm0[r], xm0));
+        const f2v P = f2fma(f2mul(xd1, ds1[r]), biased_f2(U[2 * r], U[2 * r + 1]),
+                            f2fma(f2mul(xd0, ds0[r]), biased_f2(L[2 * r], L[2 * r + 1]), nm));
+        if (c == 0 || c == 2) q01[G][r] = P;
+        else if (c == 1) S[G][r] = f2add(q01[G][r], P);
+        else S[G][r] = f2add(S[G][r], f2add(q01[G][r], P));
       }
     }
   }
 }
 
-// One Q6_K unit for NG token groups (same output convention).
+// One Q6_K unit for NG token groups (same output convention): q6_pair per group pair, the pairs of
+// each 128-value half as ((P0 + P1) + (P2 + P3)), then half 0 + half 1.  The terms are scalar here:
+// a packed (f32x2) statement of the same formula gave results a few ulps off the one-token kernel's
+// on a B200 (measured; the Q4_K / Q5_K packed terms match bit for bit), so Q6_K keeps the scalar
+// arithmetic and packs only its sums.
 template <int NG>
 __device__ __forceinline__ void unit_q6_batch(const PairRegs<T_Q6_K> &R, const uint32_t (&B)[NG][16], uint32_t wsc,
-                                              int t, float (&S)[NG][4]) {
+                                              int t, f2v (&Sx)[NG][2]) {
   const float d[2] = {h2f(R.d[0]), h2f(R.d[1])};
-  float part[NG][4];                            // the running (P0 + P1) of a half; S holds half 0's tree
+  float S[NG][4], part[NG][4];                  // part: the running (P0 + P1) of a half; S holds half 0's tree
 #pragma unroll
   for (int h = 0; h < 2; h++) {
     const uint32_t lgw[4] = {R.l[0][h].x, R.l[0][h].y, R.l[0][h].z, R.l[0][h].w};
@@ -621,8 +755,8 @@ __device__ __forceinline__ void unit_q6_batch(const PairRegs<T_Q6_K> &R, const u
         int C0[4] = {kBias, kBias, kBias, kBias}, C1[4] = {kBias, kBias, kBias, kBias};
         mma_k16s(C0, A[0][0], A[0][1], B[G][8 * h + 2 * k]);
         mma_k16s(C1, A[1][0], A[1][1], B[G][8 * h + 2 * k + 1]);
-        const float xd[2] = {lds_f(wsc + 4 * ((8 * G + 2 * t) * 8 + 4 * h + k)),
-                             lds_f(wsc + 4 * ((8 * G + 2 * t + 1) * 8 + 4 * h + k))};
+        const uint2 xw = lds64(wsc + 8 * ((4 * G + t) * 8 + 4 * h + k));
+        const float xd[2] = {__uint_as_float(xw.x), __uint_as_float(xw.y)};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
           const int ri = e >> 1;
@@ -637,24 +771,27 @@ __device__ __forceinline__ void unit_q6_batch(const PairRegs<T_Q6_K> &R, const u
       }
     }
   }
+#pragma unroll
+  for (int G = 0; G < NG; G++) {
+    Sx[G][0] = f2pack(S[G][0], S[G][1]);
+    Sx[G][1] = f2pack(S[G][2], S[G][3]);
+  }
 }
 
 // 2..16 tokens.  A CTA owns tiles [T0, T1); its units are taken super-block-major (unit i = tile
 // i % nt of super-block i / nt) and cut into equal runs, one per warp, so a warp loads the
-// activation fragments of a super-block once for all the tiles it takes of it.  Weights stream
-// from HBM into registers (D units in flight, the first before griddepcontrol.wait); each unit's
-// super-block sums go to shared memory [tile][super-block][row][token], and after one CTA barrier
-// a thread per (row, token) adds them in super-block order.  No waits: nothing to bound.
-// Two token groups hold twice the activation fragments: 12 warps leave each thread 168 registers.
-template <int NG> constexpr int batch_warps() { return NG == 2 ? 12 : 16; }
-constexpr int kBatchDepth = 2;
-constexpr int64_t kBatchBudget = 210 * 1024;
+// activation fragments of a super-block once for all the tiles it takes of it.  Each warp stages its
+// units through a ring of kBatchSlots shared-memory slots with 16-byte cp.async (as kq_ring_kernel),
+// the first before griddepcontrol.wait; each unit's super-block sums go to shared memory
+// [tile][super-block][row][token], and after one CTA barrier a thread per (row, token) adds them in
+// super-block order.  The waits are cp.async.wait_group and warp / CTA barriers: nothing to bound.
+constexpr int kBatchWarps = 8;
+constexpr int kBatchSlots = 2;
+constexpr int64_t kBatchBudget = 220 * 1024;
 
 template <int FMT, int NG>
-__global__ void __launch_bounds__(batch_warps<NG>() * 32, 1) kq_batch_kernel(const KqArgs p) {
-  constexpr int NW = batch_warps<NG>();
-  // Q6_K units (34 registers a lane) keep one in flight with two token groups
-  constexpr int NT = NW * 32, NTOK = 8 * NG, D = FMT == T_Q6_K && NG == 2 ? 1 : kBatchDepth, US = unit_bytes<FMT>();
+__global__ void __launch_bounds__(kBatchWarps * 32, 1) kq_batch_kernel(const KqArgs p) {
+  constexpr int NW = kBatchWarps, NT = NW * 32, NTOK = 8 * NG, S = kBatchSlots, US = unit_bytes<FMT>();
   constexpr int SCB = batch_sc_bytes<FMT, NTOK>();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -662,50 +799,68 @@ __global__ void __launch_bounds__(batch_warps<NG>() * 32, 1) kq_batch_kernel(con
   cta_tiles(p.rows, T0, T1);
   const int nb = p.nb, nt = T1 - T0, N = nt * nb;
   const int i0 = (int)((int64_t)warp * N / NW), i1 = (int)((int64_t)(warp + 1) * N / NW);
-  float *sums = reinterpret_cast<float *>(smem + p.part_off);      // [tile][sb][16 rows][NTOK]
-  uint8_t *wsc = smem + warp * SCB;
+  const uint32_t ring = smem_u32(smem + p.ring_off) + (uint32_t)(warp * S * US);
+  uint8_t *wsc = smem + p.x_off + warp * SCB;
   const uint32_t wsc_a = smem_u32(wsc);
+  float *sums = reinterpret_cast<float *>(smem + p.part_off);      // [tile][sb][16 rows][NTOK]
   const uint8_t *base = p.w + (int64_t)T0 * nb * US;
   auto unit_ptr = [&](int i) {
     const int sb = i / nt, tl = i - sb * nt;
     return base + ((int64_t)tl * nb + sb) * US;
   };
 
-  PairRegs<FMT> R[D];
 #pragma unroll
-  for (int d = 0; d < D; d++)
-    if (i0 + d < i1) load_unit<FMT, true>(R[d], unit_ptr(i0 + d), lane, g);   // not the previous kernel's output
+  for (int d = 0; d < S; d++) {                 // not the previous kernel's output
+    if (i0 + d < i1) copy_unit<FMT>(ring + d * US, unit_ptr(i0 + d), lane);
+    cp_async_commit();
+  }
   pdl_launch_dependents();
   pdl_wait();                                   // the activation is
 
   uint32_t B[NG][16];
-  int cur = -1;
-  for (int i = i0; i < i1; i += D) {
-#pragma unroll
-    for (int d = 0; d < D; d++) {
-      const int ii = i + d;
-      if (ii < i1) {
-        const int sb = ii / nt, tl = ii - sb * nt;
-        if (sb != cur) {
-          load_batch_b<NG>(p, sb, g, t, B);
-          __syncwarp();
-          stage_batch_scales<FMT, NTOK>(p, sb, wsc, lane);
-          __syncwarp();
-          cur = sb;
-        }
-        float S[NG][4];
-        if constexpr (FMT == T_Q6_K) unit_q6_batch<NG>(R[d], B, wsc_a, t, S);
-        else unit_k45_batch<FMT, NG>(R[d], B, wsc_a, t, S);
-        if (ii + D < i1) load_unit<FMT, true>(R[d], unit_ptr(ii + D), lane, g);
-        float *su = sums + ((int64_t)tl * nb + sb) * kTile * NTOK;
-#pragma unroll
-        for (int G = 0; G < NG; G++)
-#pragma unroll
-          for (int ri = 0; ri < 2; ri++)
-            *reinterpret_cast<float2 *>(su + (g + 8 * ri) * NTOK + 8 * G + 2 * t) = make_float2(S[G][2 * ri], S[G][2 * ri + 1]);
-      }
+  int cur = -1, slot = 0;
+  for (int i = i0; i < i1; i++) {
+    const int sb = i / nt, tl = i - sb * nt;
+    if (sb != cur) {
+      load_batch_b<NG>(p, sb, g, t, B);
+      __syncwarp();
+      stage_batch_scales<FMT, NTOK>(p, sb, wsc, lane);
+      cur = sb;
     }
+    cp_async_wait<S - 1>();                     // unit i has landed
+    __syncwarp();                               // ... every lane's pieces of it, and the staged scales, are visible
+    PairRegs<FMT> R;
+    if constexpr (FMT == T_Q6_K) {
+      const uint32_t u = ring + slot * US;
+#pragma unroll
+      for (int r = 0; r < 2; r++) {
+        R.l[r][0] = lds128(u + ((2 * r) * 32 + lane) * 16);
+        R.l[r][1] = lds128(u + ((2 * r + 1) * 32 + lane) * 16);
+        R.qh[r] = lds128(u + kQ6H + (r * 32 + lane) * 16);
+        R.sc16[r] = lds128(u + kQ6S + 16 * (8 * r + g));
+        R.d[r] = lds16(u + kQ6D + 2 * (8 * r + g));
+      }
+    } else {
+      load_unit_smem<FMT>(R, ring + slot * US, lane, g);
+    }
+    f2v Sx[NG][2];
+    if constexpr (FMT == T_Q6_K) unit_q6_batch<NG>(R, B, wsc_a, t, Sx);
+    else unit_k45_batch<FMT, NG>(R, B, wsc_a, t, Sx);
+    __syncwarp();                               // every lane is done with the slot and the scales
+    if (i + S < i1) copy_unit<FMT>(ring + slot * US, unit_ptr(i + S), lane);
+    cp_async_commit();
+    float *su = sums + ((int64_t)tl * nb + sb) * kTile * NTOK;
+#pragma unroll
+    for (int G = 0; G < NG; G++)
+#pragma unroll
+      for (int r = 0; r < 2; r++) {
+        float a, b;
+        f2unpack(Sx[G][r], a, b);
+        *reinterpret_cast<float2 *>(su + (g + 8 * r) * NTOK + 8 * G + 2 * t) = make_float2(a, b);
+      }
+    if (++slot == S) slot = 0;
   }
+  cp_async_wait<0>();
   __syncthreads();
 
   // one thread per (row, token) (per (gate, up) pair and token with swiglu): sums in super-block order
@@ -760,39 +915,50 @@ cudaError_t launch_ex(int64_t max_smem, const KqArgs &a, int grid, int block, in
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-// The one-token launches over a matrix: each takes whole tiles, at most as many per CTA as leave
-// the CTA's super-block sums room in shared memory next to the staged activation.
-constexpr int64_t kStreamBudget = 200 * 1024;
+// The one-token launches over a matrix (kq_ring_kernel): a CTA per SM, each over whole tiles, at
+// most as many per CTA as leave its super-block sums room in shared memory next to the staged
+// activation and the weight rings.
+constexpr int64_t kRingBudget = 220 * 1024;
+
+int64_t ring_bytes(int type) {
+  switch (type) {
+    case T_Q4_K: return (int64_t)kRingWarps * ring_slots<T_Q4_K>() * unit_bytes<T_Q4_K>();
+    case T_Q5_K: return (int64_t)kRingWarps * ring_slots<T_Q5_K>() * unit_bytes<T_Q5_K>();
+    default: return (int64_t)kRingWarps * ring_slots<T_Q6_K>() * unit_bytes<T_Q6_K>();
+  }
+}
 
 cudaError_t launch_stream(const DevMatrix &m, const ActView &act, float *y, const float *y_add, const GemvFuse &fz,
                           int num_sms, cudaStream_t s, bool pdl, const char **why) {
   const int64_t nb = m.cols / 256;
-  const int64_t x_bytes = kq_x_bytes(m);
-  const int64_t cap = (kStreamBudget - x_bytes) / (nb * kTile * 4);       // tiles per CTA
+  const int64_t x_bytes = kq_x_bytes(m), rb = ring_bytes(m.type);
+  const int64_t tiles_all = (m.rows + kTile - 1) / kTile;
+  const int64_t per_tile = nb * kTile * 4;                                 // super-block sums of one tile
+  const int64_t cap = (kRingBudget - rb - x_bytes) / per_tile;              // tiles per CTA
   if (cap < 1) { *why = "k-quant rows too long for the one-token GEMV"; return cudaErrorInvalidValue; }
-  const int64_t tiles_all = (m.rows + kTile - 1) / kTile, per_launch = cap * num_sms;
+  const int64_t per_launch = cap * num_sms;
   const int us = kq_unit_bytes(m.type);
   for (int64_t tb = 0; tb < tiles_all; tb += per_launch) {
     const int64_t nt = tiles_all - tb < per_launch ? tiles_all - tb : per_launch;
-    const int64_t rb = tb * kTile;
+    const int64_t r0 = tb * kTile;
     const int grid = (int)(nt < num_sms ? nt : num_sms);
     const int64_t tiles_cta = (nt + grid - 1) / grid;
     KqArgs a{};
     a.w = m.data + tb * nb * us;
-    a.rows = m.rows - rb < nt * kTile ? m.rows - rb : nt * kTile;
+    a.rows = m.rows - r0 < nt * kTile ? m.rows - r0 : nt * kTile;
     a.nb = (int)nb; a.ntok = 1; a.k = m.cols;
     a.xq = act.xq; a.xd = act.xd; a.xs = act.xs; a.x = act.x;
-    a.y = y + (fz.swiglu ? rb / 2 : rb);
-    a.y_add = y_add ? y_add + rb : nullptr;
+    a.y = y + (fz.swiglu ? r0 / 2 : r0);
+    a.y_add = y_add ? y_add + r0 : nullptr;
     a.norm_w = fz.norm_w; a.norm_eps = fz.eps; a.swiglu = fz.swiglu ? 1 : 0;
-    a.x_off = 0; a.part_off = (int)x_bytes;
-    const int smem = (int)(x_bytes + tiles_cta * nb * kTile * 4);
-    const int block = kStreamWarps * 32;
+    a.ring_off = 0; a.x_off = (int)rb; a.part_off = (int)(rb + x_bytes);
+    const int smem = (int)(rb + x_bytes + tiles_cta * per_tile);
+    const int block = kRingWarps * 32;
     cudaError_t e;
     switch (m.type) {
-      case T_Q4_K: e = launch_ex<kq_stream_kernel<T_Q4_K>>(kStreamBudget, a, grid, block, smem, s, pdl); break;
-      case T_Q5_K: e = launch_ex<kq_stream_kernel<T_Q5_K>>(kStreamBudget, a, grid, block, smem, s, pdl); break;
-      default: e = launch_ex<kq_stream_kernel<T_Q6_K>>(kStreamBudget, a, grid, block, smem, s, pdl); break;
+      case T_Q4_K: e = launch_ex<kq_ring_kernel<T_Q4_K>>(kRingBudget, a, grid, block, smem, s, pdl); break;
+      case T_Q5_K: e = launch_ex<kq_ring_kernel<T_Q5_K>>(kRingBudget, a, grid, block, smem, s, pdl); break;
+      default: e = launch_ex<kq_ring_kernel<T_Q6_K>>(kRingBudget, a, grid, block, smem, s, pdl); break;
     }
     if (e != cudaSuccess) return e;
   }
@@ -801,7 +967,7 @@ cudaError_t launch_stream(const DevMatrix &m, const ActView &act, float *y, cons
 
 template <int NG>
 cudaError_t launch_batch_ng(const KqArgs &a, int type, int grid, int smem, cudaStream_t s, bool pdl) {
-  const int block = batch_warps<NG>() * 32;
+  const int block = kBatchWarps * 32;
   switch (type) {
     case T_Q4_K: return launch_ex<kq_batch_kernel<T_Q4_K, NG>>(kBatchBudget, a, grid, block, smem, s, pdl);
     case T_Q5_K: return launch_ex<kq_batch_kernel<T_Q5_K, NG>>(kBatchBudget, a, grid, block, smem, s, pdl);
@@ -809,8 +975,9 @@ cudaError_t launch_batch_ng(const KqArgs &a, int type, int grid, int smem, cudaS
   }
 }
 
-// 2..n tokens: launches of up to 16 tokens (8 with one MMA group), each over as many tiles per CTA
-// as leave the super-block sums room in shared memory.
+// 2..n tokens: launches of up to kBatchTok tokens (one or two MMA groups of 8), each over as
+// many tiles per CTA as leave the super-block sums room in shared memory beside the weight rings and
+// the scale staging.
 cudaError_t launch_batch(const DevMatrix &m, const ActView &act, int ntok, float *y, int64_t y_stride,
                          const float *y_add, const GemvFuse &fz, int num_sms, cudaStream_t s, bool pdl,
                          const char **why) {
@@ -818,34 +985,34 @@ cudaError_t launch_batch(const DevMatrix &m, const ActView &act, int ntok, float
   const int64_t nb = m.cols / 256;
   const int64_t tiles_all = (m.rows + kTile - 1) / kTile;
   const int us = kq_unit_bytes(m.type);
+  const int64_t rb = (int64_t)kBatchWarps * kBatchSlots * us;
   for (int t0 = 0; t0 < ntok; t0 += kBatchTok) {
     const int nt_tok = ntok - t0 < kBatchTok ? ntok - t0 : kBatchTok;
     const int ng = nt_tok > 8 ? 2 : 1;
     const int ntokp = 8 * ng;
-    const int64_t sc_bytes = (int64_t)(ng == 2 ? batch_warps<2>() : batch_warps<1>()) *
-                             (m.type == T_Q6_K ? ntokp * 8 * 4 : ntokp * 4 * 16);
+    const int64_t sc_bytes = (int64_t)kBatchWarps * (m.type == T_Q6_K ? ntokp * 8 * 4 : ntokp * 4 * 16);
     const int64_t per_tile = nb * kTile * ntokp * 4;
-    const int64_t cap = (kBatchBudget - sc_bytes) / per_tile;              // tiles per CTA
+    const int64_t cap = (kBatchBudget - rb - sc_bytes) / per_tile;        // tiles per CTA
     if (cap < 1) { *why = "k-quant rows too long for the batched GEMV"; return cudaErrorInvalidValue; }
     const int64_t per_launch = cap * num_sms;
     for (int64_t tb = 0; tb < tiles_all; tb += per_launch) {
       const int64_t nt = tiles_all - tb < per_launch ? tiles_all - tb : per_launch;
-      const int64_t rb = tb * kTile;
+      const int64_t r0 = tb * kTile;
       const int grid = (int)(nt < num_sms ? nt : num_sms);
       const int64_t tiles_cta = (nt + grid - 1) / grid;
       KqArgs a{};
       a.w = m.data + tb * nb * us;
-      a.rows = m.rows - rb < nt * kTile ? m.rows - rb : nt * kTile;
+      a.rows = m.rows - r0 < nt * kTile ? m.rows - r0 : nt * kTile;
       a.nb = (int)nb; a.ntok = nt_tok; a.k = m.cols;
       a.xq = act.xq + (int64_t)t0 * m.cols;
       a.xd = act.xd + (int64_t)t0 * (m.cols / 32);
       a.xs = act.xs + (int64_t)t0 * (m.cols / 32);
-      a.y = y + (int64_t)t0 * y_stride + (fz.swiglu ? rb / 2 : rb);
-      a.y_add = y_add ? y_add + (int64_t)t0 * y_stride + rb : nullptr;
+      a.y = y + (int64_t)t0 * y_stride + (fz.swiglu ? r0 / 2 : r0);
+      a.y_add = y_add ? y_add + (int64_t)t0 * y_stride + r0 : nullptr;
       a.y_stride = y_stride;
       a.swiglu = fz.swiglu ? 1 : 0;
-      a.part_off = (int)sc_bytes;
-      const int smem = (int)(sc_bytes + tiles_cta * per_tile);
+      a.ring_off = 0; a.x_off = (int)rb; a.part_off = (int)(rb + sc_bytes);
+      const int smem = (int)(rb + sc_bytes + tiles_cta * per_tile);
       const cudaError_t e = ng == 2 ? launch_batch_ng<2>(a, m.type, grid, smem, s, pdl)
                                     : launch_batch_ng<1>(a, m.type, grid, smem, s, pdl);
       if (e != cudaSuccess) return e;

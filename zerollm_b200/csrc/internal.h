@@ -44,6 +44,27 @@ struct GemvPlan {
   int units, g, uw, upt, cr, nsg, stage_bytes, grid, smem_bytes, max_rows;
 };
 
+// Paged KV caches: a layer's K (and V) pool holds num_pages pages of [n_kv][1 << page_log2][head_dim]
+// elements; row s of table lists sequence s's pages in position order (max_pages entries), so
+// position p of sequence s lives at row p & (page size - 1) of page table[s * max_pages + (p >> page_log2)].
+struct KvPages {
+  const int32_t *table;            // device [nseq][max_pages]; NULL: contiguous caches
+  int max_pages, num_pages, page_log2;
+};
+// element offset of position p's row of KV head kh of sequence row `srow` in a page pool; a position
+// past the row's max_pages pages or an entry outside [0, num_pages) reads page 0 and reports
+// ST_BAD_ARGS (the table lives on the device, where the host does not look)
+__device__ __forceinline__ int64_t kv_page_row(const KvPages &pg, int64_t srow, int n_kv, int kh, int p, int hd,
+                                               unsigned *status) {
+  const int slot = p >> pg.page_log2;
+  int page = slot < pg.max_pages ? __ldg(pg.table + srow * pg.max_pages + slot) : -1;
+  if (page < 0 || page >= pg.num_pages) {
+    if (status) atomicOr(status, 8u);   // ST_BAD_ARGS (common.cuh)
+    page = 0;
+  }
+  return ((((int64_t)page * n_kv + kh) << pg.page_log2) + (p & ((1 << pg.page_log2) - 1))) * hd;
+}
+
 // q/k/v post-processing of `ntok` tokens (biases, q/k RMSNorm, RoPE) and the K/V append.
 struct QkvPostArgs {
   const float *q, *k, *v;          // [ntok][q_stride] / [ntok][kv_stride] f32 projections
@@ -58,6 +79,8 @@ struct QkvPostArgs {
   int64_t seq_stride, head_stride; // elements between sequences / KV heads (positions are head_dim apart)
   int n_head, n_kv, head_dim, n_rot, neox, kv_f16, ntok;
   double eps;
+  KvPages pages;                   // paged caches (pages.table != NULL): kcache / vcache are page pools
+  unsigned *status;                // device status word (a bad page index), may be NULL
 };
 
 // decode attention: a sequence of n positions is cut into context splits whose number and length
@@ -100,6 +123,7 @@ struct AttnArgs {
   // memory and the last context split appends the key / value row before reading it
   int fused;
   QkvPostArgs post;
+  KvPages pages;                   // paged caches (pages.table != NULL; not with `fused`): row b of the table is query b's
 };
 
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t s, bool pdl);

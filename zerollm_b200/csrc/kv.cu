@@ -75,7 +75,8 @@ __device__ void post_head(const QkvPostArgs &a, int t, int h, float *row, float 
   }
   // append k and v at `pos` of this sequence's cache (worker.js:303-308)
   const int kh = h - a.n_head;
-  const int64_t base = (int64_t)a.seq[t] * a.seq_stride + (int64_t)kh * a.head_stride + (int64_t)pos * hd;
+  const int64_t base = a.pages.table ? kv_page_row(a.pages, a.seq[t], a.n_kv, kh, pos, hd, a.status)
+                                     : (int64_t)a.seq[t] * a.seq_stride + (int64_t)kh * a.head_stride + (int64_t)pos * hd;
   const float *vsrc = a.v + (int64_t)t * a.kv_stride + kh * hd;
   const float *bv = a.bv ? a.bv + kh * hd : nullptr;
   if (a.kv_f16) {
@@ -166,7 +167,7 @@ struct KvRow {
   }
 };
 
-template <typename T, int HD, int G>
+template <typename T, int HD, int G, bool PAGED>
 __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const AttnArgs a) {
   constexpr int DPL = HD / 32;
   // batch: 32 / G positions, fewer where K and V of two batches would not fit in registers
@@ -193,8 +194,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
   const int t0 = min(npos, split * slen), t1 = min(npos, t0 + slen);
   const int w0 = min(t1, t0 + warp * ppw), w1 = min(t1, w0 + ppw);
   const int64_t cs = a.seq ? a.seq[b] : b;            // cache sequence of this query
-  const T *kbase = reinterpret_cast<const T *>(a.kcache) + cs * a.seq_stride + (int64_t)kh * a.head_stride;
-  const T *vbase = reinterpret_cast<const T *>(a.vcache) + cs * a.seq_stride + (int64_t)kh * a.head_stride;
+  const T *kpool = reinterpret_cast<const T *>(a.kcache), *vpool = reinterpret_cast<const T *>(a.vcache);
+  const int64_t cbase = PAGED ? 0 : cs * a.seq_stride + (int64_t)kh * a.head_stride;
+  // element offset of position p's K (and V) row: contiguous, or through query b's page-table row
+  auto row = [&](int p) -> int64_t {
+    if constexpr (PAGED) return kv_page_row(a.pages, b, a.n_kv, kh, p, HD, a.status);
+    else return cbase + (int64_t)p * HD;
+  };
   // fused decode: this launch appends the query's own position npos - 1 (the last split's CTA does)
   const int newp = a.fused ? npos - 1 : -1;
 
@@ -203,8 +209,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
 #pragma unroll
     for (int j = 0; j < NB; j++) {
       const int p = min(p0 + j, w1 - 1);               // past the end: repeat the last row (masked below)
-      k[j].load(kbase + (int64_t)p * HD, lane, p == newp);
-      v[j].load(vbase + (int64_t)p * HD, lane, p == newp);
+      const int64_t o = row(p);
+      k[j].load(kpool + o, lane, p == newp);
+      v[j].load(vpool + o, lane, p == newp);
     }
   };
   // the first batch streams in during the fused prologue unless it holds the row being appended
@@ -401,7 +408,7 @@ size_t attn_smem_bytes(int head_dim, int group, bool f16) {
 
 template <typename T, int HD, int G>
 static cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s, bool pdl) {
-  auto kern = attn_decode_kernel<T, HD, G>;
+  auto kern = a.pages.table ? attn_decode_kernel<T, HD, G, true> : attn_decode_kernel<T, HD, G, false>;
   const size_t smem = 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nsplit, a.n_kv, a.nseq);

@@ -651,8 +651,7 @@ static int run(zllm_model *m, const int32_t *seqs, int single_seq, const int32_t
   if (want && logits_host)
     CK(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * nl * c.vocab, cudaMemcpyDeviceToHost, s), "logits");
   if (want && argmax_host) CK(cudaMemcpyAsync(argmax_host, m->d_arg, sizeof(int32_t) * nl, cudaMemcpyDeviceToHost, s), "argmax");
-  CK(cudaStreamSynchronize(s), "pass");
-  int rc = zllm_check_status(m->ctx);
+  int rc = zllm_finish(m->ctx, s);             // one synchronization; the status word comes back on the stream
   if (rc) return fail(m, rc);
   for (int sq = 0; sq < c.n_seq; sq++) m->pos[sq] += added[sq];
   return ZLLM_OK;
@@ -720,8 +719,7 @@ extern "C" int zllm_model_generate(zllm_model *m, int seq, const int32_t *seqs, 
     if (rc) return rc;
   }
   CK(cudaMemcpyAsync(out_host, m->d_gen, sizeof(int32_t) * (size_t)steps * n, cudaMemcpyDeviceToHost, s), "tokens");
-  CK(cudaStreamSynchronize(s), "generate");
-  int rc = zllm_check_status(m->ctx);
+  int rc = zllm_finish(m->ctx, s);
   if (rc) return fail(m, rc);
   for (int i = 0; i < n; i++) m->pos[seqs ? seqs[i] : seq] += steps;
   return ZLLM_OK;

@@ -55,6 +55,9 @@ SIGNATURES = {
     "zllm_qkv_append": (i32, [vp, vp, i32, vp, i64, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "zllm_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, vp, vp]),
     "zllm_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, vp, vp]),
+    "zllm_qkv_append_paged": (i32, [vp, vp, vp, i32, vp, i64, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                    vp]),
+    "zllm_attn_decode_paged": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, vp, vp]),
     "zllm_kv_import": (i32, [vp, vp, vp, i32, vp, vp]),
     "zllm_kv_export": (i32, [vp, vp, vp, i32, vp, vp]),
     "zllm_kv_copy": (i32, [vp, vp, vp, i64, vp, i64, i32, vp]),
@@ -98,6 +101,11 @@ class AttnGeom(C.Structure):
     _fields_ = [("n_head", C.c_int), ("n_head_kv", C.c_int), ("head_dim", C.c_int), ("n_rot", C.c_int),
                 ("neox", C.c_int), ("kv_f16", C.c_int), ("ctx", C.c_int), ("rms_eps", C.c_double),
                 ("seq_stride", C.c_int64), ("head_stride", C.c_int64)]
+
+class KvPages(C.Structure):
+    """zllm_kv_pages (include/zllm.h)"""
+    _fields_ = [("block_table", C.c_void_p), ("max_pages", C.c_int), ("num_pages", C.c_int), ("page_size", C.c_int)]
+
 
 _lib = None
 
