@@ -2,9 +2,11 @@
 
 * the f16 x f16 core (zllm_gemm_f16) against torch's f32 product of the same f16 operands;
 * k-quant weights x quantized activations (zllm_mm with >= 64 tokens) against the oracle's matvec
-  per token (ref-kernels.js:196-277): the compensated f16 products (hi / lo pairs, three MMAs)
-  stay within 1.5e-4 of the largest output (measured 2e-6 to 6e-5, growing with K; the contract
-  is 1e-3; a single f16 product measured 3e-4 to 6e-4);
+  per token (ref-kernels.js:196-277) within 1.5e-4 of the largest output (the contract is 1e-3; a
+  single f16 product measured 3e-4 to 6e-4).  Q4_K, Q5_K and Q6_K with |scale| <= 64 take the
+  exact-A kernel (sub-block scale x quant exact in f16, activation as an f16 hi / lo pair, super-
+  block scales applied in f32); Q6_K with larger scales (the quantizer's usual +-128) the hi / lo
+  kernel (three MMAs);
 * partial row / token tiles, the residual add, block scales far outside f16's range (a per-matrix
   power of two), and a NaN scale, which keeps the exact per-token kernel (same bits as single
   tokens).
@@ -73,6 +75,21 @@ def test_kquant_gemm_matches_oracle(ctx, t, rows, cols, ntok):
     # every token against the exact per-token path
     single = np.stack([matvec(w, Act(ctx, X[i])).cpu().numpy().ravel() for i in range(ntok)])
     assert max(_rel(got[i], single[i]) for i in range(ntok)) <= 1.5e-4
+
+
+def test_q6k_full_scale_range(ctx):
+    """Q6_K sub-block scales over the quantizer's full int8 range: (q - 32) * scale reaches 4096 and
+    is not exact in f16, so these matrices take the hi / lo kernel, within the same bound."""
+    rng = np.random.default_rng(11)
+    rows, cols, ntok = 256, 2048, 70
+    raw = synth.quant_blocks(ggml.Q6_K, rows, cols, rng, "bench").reshape(rows, -1, 210).copy()
+    raw[:, :, 192:208] = rng.integers(-128, 128, (rows, cols // 256, 16)).astype(np.int8).view(np.uint8)
+    w = Weight(ctx, ggml.Q6_K, rows, cols, raw.reshape(-1))
+    X = rng.standard_normal((ntok, cols)).astype(np.float32)
+    got = matvec(w, Act(ctx, X)).cpu().numpy()
+    assert np.isfinite(got).all()
+    for i in (0, ntok - 1):
+        assert _rel(got[i], O.matvec(ggml.Q6_K, raw.reshape(-1), rows, cols, X[i])) <= 1.5e-4
 
 
 def test_gemm_residual(ctx):

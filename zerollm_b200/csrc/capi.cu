@@ -234,16 +234,37 @@ int zllm_weight_gemm_ok(zllm_ctx *c, zllm_weight *w) {
   if (w->gemm_ok >= 0) return w->gemm_ok;
   if (!gemm_kq_supported(w->m)) return w->gemm_ok = 0;
   void *buf = nullptr;
-  if (zllm_scratch(c, 13, 4, &buf)) return 0;
-  unsigned bits = 0;
-  cudaError_t e = launch_kq_bound(w->m, reinterpret_cast<unsigned *>(buf), c->stream);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(&bits, buf, 4, cudaMemcpyDeviceToHost, c->stream);
+  if (zllm_scratch(c, 13, 16, &buf)) return 0;
+  unsigned bits[3] = {0, 0, 0};
+  unsigned *d = reinterpret_cast<unsigned *>(buf);
+  cudaError_t e = launch_kq_bound(w->m, d, c->stream);
+  if (e == cudaSuccess) e = launch_kx_info(w->m, d + 1, c->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(bits, buf, 12, cudaMemcpyDeviceToHost, c->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   if (e != cudaSuccess) { cudaGetLastError(); return 0; }
-  float bound;
-  memcpy(&bound, &bits, 4);
+  float bound, mbound;
+  memcpy(&bound, &bits[0], 4);
+  memcpy(&mbound, &bits[1], 4);
   w->gemm_wscale = gemm_weight_scale(bound);
+  w->gemm_mscale = gemm_weight_scale(mbound);
+  // exact A: Q4_K / Q5_K always (sc * q <= 63 * 31), Q6_K while (q - 32) * scale stays within 2048
+  w->gemm_kx = w->m.type == zllm::T_Q6_K ? bits[2] <= 64 : true;
   return w->gemm_ok = bound < 3.0e38f ? 1 : 0;          // NaN or infinite scales: the exact kernel
+}
+
+// The tensor-core GEMM of a qualifying weight on ntok >= kGemmMinTokens tokens of (xq, xd, xs):
+// activation tiles in bbuf (gemm_act_bytes), then the product.
+size_t gemm_act_bytes(const zllm_weight *w, int ntok) {
+  return w->gemm_kx ? gemm_bx_bytes(w->m.cols, ntok, w->m.type) : gemm_b_bytes(w->m.cols, ntok);
+}
+cudaError_t gemm_run(const zllm_weight *w, const ActView &a, int ntok, void *bbuf, float *y, int64_t y_stride,
+                     const float *y_add, unsigned *status, cudaStream_t st, bool swiglu) {
+  if (w->gemm_kx) {
+    cudaError_t e = launch_gemm_prep_kx(a, ntok, w->m.type, bbuf, st);
+    return e == cudaSuccess ? launch_gemm_kx(w->m, bbuf, ntok, y, y_stride, y_add, w->gemm_mscale, status, st, swiglu) : e;
+  }
+  cudaError_t e = launch_gemm_prep(a, ntok, bbuf, st);
+  return e == cudaSuccess ? launch_gemm_kq(w->m, bbuf, ntok, y, y_stride, y_add, w->gemm_wscale, status, st, swiglu) : e;
 }
 
 extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, const float *xd, const int32_t *xs,
@@ -266,10 +287,9 @@ extern "C" int zllm_mm(zllm_ctx *c, const zllm_weight *w, const int8_t *xq, cons
       zllm_weight_gemm_ok(c, const_cast<zllm_weight *>(w))) {
     // kGemmMinTokens or more tokens: the tensor-core GEMM on f16 tiles of the activation
     void *bbuf = nullptr;
-    int rc = zllm_scratch(c, 14, gemm_b_bytes(w->m.cols, ntok), &bbuf);
+    int rc = zllm_scratch(c, 14, gemm_act_bytes(w, ntok), &bbuf);
     if (rc) return rc;
-    cudaError_t e = launch_gemm_prep(a, ntok, bbuf, st);
-    if (e == cudaSuccess) e = launch_gemm_kq(w->m, bbuf, ntok, y, y_stride, y_add, w->gemm_wscale, c->status_dev, st);
+    cudaError_t e = gemm_run(w, a, ntok, bbuf, y, y_stride, y_add, c->status_dev, st, false);
     return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "gemm launch");
   }
   cudaError_t e = launch_gemv(w->m, a, ntok, y, y_stride, y_add, c->status_dev, c->num_sms, st, pdl_ok(st), &why);

@@ -30,10 +30,15 @@ struct zllm_weight {
   bool owns = true;
   int gemm_ok = -1;      // k-quant: the tensor-core GEMM may take it (1), not (0), not yet known (-1)
   float gemm_wscale = 1.f;   // power of two applied to its dequantized values in f16
+  bool gemm_kx = false;      // it takes the exact-A GEMM (launch_gemm_kx) rather than the hi / lo one
+  float gemm_mscale = 1.f;   // the exact-A GEMM's power of two for the min values
 };
 
 // Whether the tensor-core GEMM may take this k-quant weight (computed once, synchronously).
 int zllm_weight_gemm_ok(zllm_ctx *c, zllm_weight *w);
+size_t gemm_act_bytes(const zllm_weight *w, int ntok);
+cudaError_t gemm_run(const zllm_weight *w, const zllm::ActView &a, int ntok, void *bbuf, float *y, int64_t y_stride,
+                     const float *y_add, unsigned *status, cudaStream_t st, bool swiglu);
 
 void zllm_set_error(zllm_ctx *c, const char *fmt, ...);
 int zllm_cuda_fail(zllm_ctx *c, cudaError_t e, const char *what);

@@ -142,6 +142,13 @@ __device__ __forceinline__ float2 lds_f2(uint32_t a) {
   return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
 }
 __device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+// The same load issued where it stands in the program: a prefetch the compiler may not sink to the
+// first use of its result (volatile asm keeps its place among the other volatile statements).
+__device__ __forceinline__ uint4 ldg128_now(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
 // int32 -> double without the conversion pipe: (2^52 + 2^31 + v) - (2^52 + 2^31) is exact in double.
 // i2d_biased takes v + 2^31 (mod 2^32), which an integer multiply-add produces for free.
 __device__ __forceinline__ double i2d_biased(uint32_t v_plus_2p31) {

@@ -31,6 +31,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kq_layout.h"
+#include "tc05.cuh"
 
 namespace zllm {
 
@@ -51,121 +52,8 @@ constexpr int kPairBytes = 2 * kTileBytes;   // a hi tile and its lo tile
 constexpr int kQ6HOff = 2048, kQ6SOff = 3072, kQ6DOff = 3328;   // Q6_K unit regions (kq_layout.h)
 static_assert(GM == GN, "A and B tiles share one size");
 
-// ---------------------------------------------------------------------------- tcgen05 wrappers
-__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// 16-byte global -> shared copy through L2 (LDGSTS); completion tracked per thread
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-// arrive on `bar` once this thread's earlier cp.async copies have landed (no pending-count increment:
-// the barrier's expected count includes these arrivals)
-__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// D[tmem] (+)= A[smem] . B[smem]^T, both K-major f16, f32 accumulation
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc)
-      : "memory");
-}
-// arrive on `bar` once every tcgen05 operation this thread issued before has completed
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-// 32 lanes x 32 consecutive f32 columns: thread i gets lane (base lane + i), columns col..col+31
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu)      // start address
-         | ((uint64_t)1 << 16)                   // leading byte offset (unused for swizzled K-major)
-         | ((uint64_t)(1024 >> 4) << 32)         // stride byte offset: 8 rows x 128 B
-         | ((uint64_t)1 << 46)                   // descriptor version
-         | ((uint64_t)2 << 61);                  // 128-byte swizzle
-}
-// Instruction descriptor of kind::f16: f16 A and B, f32 D, both K-major, M x N.
-// instruction descriptor of kind::f16 with f32 accumulation, M = GM; N (a multiple of 16, at most
-// GN) goes in bits 17..22 as N / 8
-constexpr uint32_t kIdescM = (1u << 4) | ((uint32_t)(GM >> 4) << 24);
-__device__ __forceinline__ uint32_t idesc_n(int n) { return kIdescM | ((uint32_t)(n >> 3) << 17); }
-
-// byte offset of element (row, k) of a [rows][64] f16 tile in the 128-byte-swizzled layout
-__host__ __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
-  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
-}
-
-// ---------------------------------------------------------------------------- bounded waits
-// try_wait without a suspend-time hint: the thread polls instead of sleeping between tries, which
-// keeps the reaction to a completed phase short in these tightly coupled pipelines
-__device__ __forceinline__ bool try_wait_spin(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-struct Ctl {
-  volatile int *abort;
-  unsigned *status;
-};
-// one thread; false after a give-up (sets the status bit and the abort flag) or when aborted
-__device__ __forceinline__ bool wait1(uint64_t *bar, uint32_t parity, const Ctl &c, uint32_t bit) {
-  if (*c.abort) return false;
-  for (int i = 0; i < 64; i++)
-    if (try_wait_spin(bar, parity)) return true;
-  const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
-  uint32_t n = 0;
-  while (!try_wait_spin(bar, parity)) {
-    if (*c.abort) return false;
-    if ((++n & 63u) == 0 && globaltimer_ns() > deadline) {
-      atomicOr(c.status, bit);
-      *c.abort = 1;
-      return false;
-    }
-  }
-  return true;
-}
-// a warp: lane 0 waits, the verdict is broadcast
-__device__ __forceinline__ bool waitw(uint64_t *bar, uint32_t parity, const Ctl &c, uint32_t bit, int lane) {
-  bool ok = true;
-  if (lane == 0) ok = wait1(bar, parity, c, bit);
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok;
-}
+constexpr uint32_t kIdescM = idesc_f16(GM, 0);
+__device__ __forceinline__ uint32_t idesc_n(int n) { return idesc_f16(GM, n); }
 
 // ---------------------------------------------------------------------------- dequantization
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -204,9 +92,9 @@ template <int FMT> struct Raw {      // Q4_K, Q5_K
 #pragma unroll
     for (int cp = 0; cp < 2; cp++)
 #pragma unroll
-      for (int tt = 0; tt < 2; tt++) q[cp][tt] = ldg128(u + ((2 * r + cp) * 32 + 4 * g + 2 * tp + tt) * 16);
-    if constexpr (FMT == T_Q5_K) e = ldg128(u + 2048 + 32 * m + 16 * tp);
-    hd = ldg128(u + (FMT == T_Q4_K ? 2048 : 2560) + 16 * m);
+      for (int tt = 0; tt < 2; tt++) q[cp][tt] = ldg128_now(u + ((2 * r + cp) * 32 + 4 * g + 2 * tp + tt) * 16);
+    if constexpr (FMT == T_Q5_K) e = ldg128_now(u + 2048 + 32 * m + 16 * tp);
+    hd = ldg128_now(u + (FMT == T_Q4_K ? 2048 : 2560) + 16 * m);
   }
 };
 template <> struct Raw<T_Q6_K> {
@@ -217,10 +105,10 @@ template <> struct Raw<T_Q6_K> {
 #pragma unroll
     for (int h = 0; h < 2; h++)
 #pragma unroll
-      for (int tt = 0; tt < 2; tt++) ql[h][tt] = ldg128(u + ((2 * r + h) * 32 + 4 * g + 2 * tp + tt) * 16);
-    qh[0] = ldg128(u + kQ6HOff + 64 * m + 32 * tp);
-    qh[1] = ldg128(u + kQ6HOff + 64 * m + 32 * tp + 16);
-    sc = ldg128(u + kQ6SOff + 16 * m);
+      for (int tt = 0; tt < 2; tt++) ql[h][tt] = ldg128_now(u + ((2 * r + h) * 32 + 4 * g + 2 * tp + tt) * 16);
+    qh[0] = ldg128_now(u + kQ6HOff + 64 * m + 32 * tp);
+    qh[1] = ldg128_now(u + kQ6HOff + 64 * m + 32 * tp + 16);
+    sc = ldg128_now(u + kQ6SOff + 16 * m);
     d = __ldg(reinterpret_cast<const unsigned short *>(u + kQ6DOff + 2 * m));
   }
 };
@@ -688,6 +576,490 @@ __global__ void kq_bound_kernel(const uint8_t *w, int64_t nunits, unsigned *out)
   atomicMax(out, __float_as_uint(b));
 }
 
+// ============================================================================ exact-A GEMM (kx)
+// The same contraction with the weights dequantized EXACTLY into f16, so only the activation needs a
+// hi / lo pair: two MMAs per 16-value K slice (A . B_hi + A . B_lo) instead of three.
+//   * A of a super-block is sc * q per sub-block -- Q4_K / Q5_K: 6-bit scale times a 4- or 5-bit
+//     quant, at most 63 * 31 = 1953; Q6_K: int8 scale times (q - 32), exact while every |scale| of
+//     the matrix is at most 64 (checked once per matrix) -- all integers f16 holds exactly.  The
+//     dequantization is byte work: nibbles spread into f16 lanes with prmt, then one f16x2 FMA
+//     (1024 + q) * sc - 1024 * sc, whose single rounding is of an exact small integer.
+//   * The super-block scale d cannot join an exact f16 operand, so each super-block's MMAs
+//     accumulate into one of two TMEM buffers, and four epilogue warps fold d * buffer into a running
+//     total in TMEM (tcgen05.ld / st) while the next super-block's MMAs fill the other buffer.
+//   * Q4_K / Q5_K's min term -dmin * mn * (sum of the sub-block's activation) rides as one more
+//     64-value K step per super-block: A row [-dmin mn hi x8 | same x8 | -dmin mn lo x8 | 0],
+//     B row [xsum hi x8 | xsum lo x8 | xsum hi x8 | 0], one MMA over the first 32 columns giving
+//     hi.hi + hi.lo + lo.hi, accumulated across super-blocks in a third TMEM region (no d scaling).
+//     The min values carry a per-matrix power of two (the mscale argument) and xsum 2^-5 (a 32-value
+//     sum of activations each below 2^15) to stay inside f16's range.
+// TMEM: buffers [0, 128) and [128, 256), total [256, 384), min term [384, 512).  Roles (448
+// threads): lane 0 of warp 0 streams each step's activation tiles with one bulk copy, warp 1 owns
+// TMEM and its lane 0 issues the MMAs, warps 2..9 dequantize (each lane holds the next super-block's
+// words in registers), warps 10..13 fold the buffers and write y.  Every wait is bounded; the roles
+// off the critical path wait with suspending tries.
+constexpr int kXAStages = 4, kXBStages = 4;
+constexpr int kXProdWarp = 0, kXMmaWarp = 1, kXDqWarp0 = 2, kXEpiWarp0 = kXDqWarp0 + kDqWarps, kXEpiWarps = 4;
+constexpr int kXThreads = (kXEpiWarp0 + kXEpiWarps) * 32;
+constexpr uint32_t kXTmemCols = 512, kXTot = 256, kXMin = 384;
+template <int FMT> constexpr int kx_steps_per_sb() { return FMT == T_Q6_K ? 4 : 5; }
+constexpr size_t kx_smem_bytes() {
+  return 1024 + (size_t)kXAStages * kTileBytes + (size_t)kXBStages * kPairBytes + (2 * kXAStages + 2 * kXBStages + 5) * 8 + 16;
+}
+static_assert(kx_smem_bytes() <= 232448, "shared memory");
+
+// f16x2 of the low bytes of a word's bytes 0, 1 (sel 0x5140) or 2, 3 (sel 0x7362) as 1024 + b
+__device__ __forceinline__ uint32_t bytes_h2(uint32_t t4, uint32_t sel) { return __byte_perm(t4, 0x64646464u, sel); }
+__device__ __forceinline__ uint32_t h2fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t h2sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// f16 bits of a small integer |v| <= 2048, twice (exact)
+__device__ __forceinline__ uint32_t int_h2(int v) {
+  const uint32_t h = __half_as_ushort(__int2half_rn(v));
+  return h | (h << 16);
+}
+
+template <int FMT> struct DqX {      // Q4_K, Q5_K: one super-block of one thread's row half
+  uint4 q[2][2], e;
+  uint32_t F[4];                     // the 24-bit scale / min field of each chunk
+  uint32_t hdx;                      // d | dmin << 16 (f16 bits)
+  __device__ __forceinline__ void set(const Raw<FMT> &R) {
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+#pragma unroll
+      for (int j = 0; j < 2; j++) q[i][j] = R.q[i][j];
+    e = R.e;
+    hdx = R.hd.x;
+#pragma unroll
+    for (int c = 0; c < 4; c++) F[c] = k45_field(R.hd, c);
+  }
+  // chunk c (sub-blocks 2c, 2c + 1): out[j] = positions 16j + 8tp .. + 7 of the step, exact sc * q
+  template <int c>
+  __device__ __forceinline__ void emit(uint4 (&out)[4]) const {
+#pragma unroll
+    for (int nib = 0; nib < 2; nib++) {
+      const int sc = (int)((F[c] >> (6 * nib)) & 63u);
+      const uint32_t s2 = int_h2(sc), nb2 = int_h2(-1024 * sc);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        uint32_t o[4];
+#pragma unroll
+        for (int tt = 0; tt < 2; tt++) {
+          const uint32_t w = word4(q[c >> 1][tt], 2 * (c & 1) + h);
+          uint32_t t4 = (w >> (4 * nib)) & 0x0f0f0f0fu;
+          if constexpr (FMT == T_Q5_K) t4 |= ((word4(e, 2 * tt + h) >> (2 * c + nib)) & 0x01010101u) << 4;
+          o[2 * tt] = h2fma(bytes_h2(t4, 0x5140), s2, nb2);
+          o[2 * tt + 1] = h2fma(bytes_h2(t4, 0x7362), s2, nb2);
+        }
+        out[2 * nib + h] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  // the min step: position chunk tp + 2j; chunk 0: -dmin*mn hi of sub-blocks 0..7, chunk 1: the same
+  // hi, chunk 2: the lo parts, the rest zero
+  __device__ __forceinline__ void emit_min(int tp, float mscale, uint4 (&out)[4]) const {
+    const float dmin = h2f(hdx >> 16) * mscale;
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float v[2];
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const int j = 2 * i + u;               // sub-block j: chunk j >> 1, min field j & 1
+        v[u] = -(dmin * (float)((F[j >> 1] >> (12 + 6 * (j & 1))) & 63u));
+      }
+      split2(v[0], v[1], hi[i], lo[i]);
+    }
+    const uint4 H = make_uint4(hi[0], hi[1], hi[2], hi[3]), Lo = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    const uint4 Z = make_uint4(0, 0, 0, 0);
+    out[0] = H;                                // chunk tp: 0 (hi) or 1 (hi again)
+    out[1] = tp == 0 ? Lo : Z;                 // chunk tp + 2: 2 (lo) or 3
+    out[2] = Z;
+    out[3] = Z;
+  }
+};
+template <> struct DqX<T_Q6_K> {
+  uint4 ql[2][2], qh[2], sc;
+  __device__ __forceinline__ void set(const Raw<T_Q6_K> &R) {
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      qh[i] = R.qh[i];
+#pragma unroll
+      for (int j = 0; j < 2; j++) ql[i][j] = R.ql[i][j];
+    }
+    sc = R.sc;
+  }
+  // chunk c (half c >> 1, 32-value run c & 1): out[j] = positions 16j + 8tp .. + 7, (q - 32) * scale
+  template <int c>
+  __device__ __forceinline__ void emit(uint4 (&out)[4]) const {
+    constexpr int half = c >> 1, hb = c & 1;
+    const uint32_t k1056 = int_h2(1056);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int p = j >> 1, uu = j & 1, k = 2 * hb + p, G = 8 * half + 2 * k + uu;
+      const int o = G < 8 ? 4 * (G >> 1) + (G & 1) : 4 * ((G - 8) >> 1) + 2 + (G & 1);
+      const uint32_t s2 = int_h2((int)(int8_t)((word4(sc, o >> 2) >> (8 * (o & 3))) & 0xffu));
+      uint32_t r[4];
+#pragma unroll
+      for (int tt = 0; tt < 2; tt++) {
+        const uint32_t w = word4(ql[half][tt], 2 * uu + p), eh = word4(qh[tt], 2 * half + uu);
+        const uint32_t t4 = ((w >> (4 * hb)) & 0x0f0f0f0fu) | (((eh >> (2 * k)) & 0x03030303u) << 4);
+        r[2 * tt] = h2mul(h2sub(bytes_h2(t4, 0x5140), k1056), s2);
+        r[2 * tt + 1] = h2mul(h2sub(bytes_h2(t4, 0x7362), k1056), s2);
+      }
+      out[j] = make_uint4(r[0], r[1], r[2], r[3]);
+    }
+  }
+};
+
+template <int FMT>
+__global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p) {
+  constexpr int US = FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360;
+  constexpr int AS = kXAStages, BS = kXBStages, SPS = kx_steps_per_sb<FMT>();
+  constexpr bool MINS = FMT != T_Q6_K;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t *a_ring = smem, *b_ring = smem + AS * kTileBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(b_ring + BS * kPairBytes);
+  uint64_t *full_a = bars, *empty_a = bars + AS, *full_b = bars + 2 * AS, *empty_b = full_b + BS;
+  uint64_t *buf_full = empty_b + BS, *buf_free = buf_full + 2, *acc_full = buf_free + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tile = blockIdx.x, n_tile = blockIdx.y;
+  const int nb = p.nb, nsteps = nb * SPS;
+  const int64_t tiles16 = (p.rows + 15) / 16;
+  const int tile0 = m_tile * 8;
+  const int ntile = (int)min((int64_t)8, tiles16 - tile0);
+  const Ctl ctl{abort_flag, p.status};
+  // each M tile starts at its own super-block (spreads the CTAs of one token tile over the activation);
+  // the order of the super-block sums then depends on the tile alone
+  const int koff_sb = nb > 0 ? (m_tile * 7) % nb : 0;
+  const int ntok_tile = min(GN, p.ntok - n_tile * GN);
+  const int nmma = (ntok_tile + 15) / 16 * 16;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < AS; s++) { mbar_init(&full_a[s], kDqWarps); mbar_init(&empty_a[s], 1); }
+    for (int s = 0; s < BS; s++) { mbar_init(&full_b[s], 1); mbar_init(&empty_b[s], 1); }
+    for (int b = 0; b < 2; b++) { mbar_init(&buf_full[b], 1); mbar_init(&buf_free[b], kXEpiWarps); }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kXMmaWarp) tmem_alloc(tmem_slot, kXTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kXProdWarp) {
+    // ---- activation producer: one lane, one bulk copy per step (the min step: its hi tile alone);
+    // step s of the walk is step (sb + koff) * SPS + kk of the tiles
+    if (lane == 0) {
+      const uint32_t part = (uint32_t)nmma * 128;      // the first nmma rows of a 128-row tile
+      int kk = 0, sbg = koff_sb, issued = 0;
+      for (int s = 0; s < nsteps; s++) {
+        const int st = s % BS;
+        if (s >= BS && !wait1(&empty_b[st], (uint32_t)(s / BS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
+        const uint8_t *src = p.b + ((int64_t)n_tile * nsteps + sbg * SPS + kk) * 2 * kTileBytes;
+        uint8_t *dst = b_ring + (size_t)st * kPairBytes;
+        const bool hi_only = MINS && kk == 4;
+        mbar_arrive_expect_tx(&full_b[st], hi_only ? part : 2 * part);
+        if (!hi_only && part == (uint32_t)kTileBytes) {
+          bulk_g2s(dst, src, 2 * kTileBytes, &full_b[st]);
+        } else {
+          bulk_g2s(dst, src, part, &full_b[st]);
+          if (!hi_only) bulk_g2s(dst + kTileBytes, src + kTileBytes, part, &full_b[st]);
+        }
+        issued++;
+        if (++kk == SPS) {
+          kk = 0;
+          if (++sbg == nb) sbg = 0;
+        }
+      }
+      // copies still landing in shared memory (an abort) are waited for before the CTA exits
+      const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
+      for (int s = issued > BS ? issued - BS : 0; s < issued; s++)
+        if (!mbar_wait_bounded(&full_b[s % BS], (uint32_t)(s / BS) & 1u, deadline)) atomicOr(p.status, ST_DRAIN_TIMEOUT);
+    }
+  } else if (warp == kXMmaWarp) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_n(nmma);
+      const uint64_t adesc0 = sw128_desc(smem_u32(a_ring)), bdesc0 = sw128_desc(smem_u32(b_ring));
+      int issued = 0, kk = 0, sbi = 0;
+      for (int s = 0; s < nsteps; s++) {
+        const int sa = s % AS, sbs = s % BS;
+        if (kk == 0 && sbi >= 2 && !wait1(&buf_free[sbi & 1], (uint32_t)((sbi >> 1) - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
+        if (!wait1(&full_b[sbs], (uint32_t)(s / BS) & 1u, ctl, ST_FULL_TIMEOUT) ||
+            !wait1(&full_a[sa], (uint32_t)(s / AS) & 1u, ctl, ST_FULL_TIMEOUT))
+          break;
+        fence_async_smem();
+        tc_fence_after();
+        // descriptor start addresses are in 16-byte units: a byte offset o adds o >> 4
+        const uint64_t ad = adesc0 + (uint64_t)(sa * (kTileBytes >> 4));
+        const uint64_t bh = bdesc0 + (uint64_t)(sbs * (kPairBytes >> 4)), bl = bh + (kTileBytes >> 4);
+        if (!MINS || kk < 4) {
+          const uint32_t d = tmem + (uint32_t)((sbi & 1) * GN);
+#pragma unroll
+          for (int sl = 0; sl < GK / 16; sl++) {
+            mma_f16(d, ad + 2 * sl, bh + 2 * sl, idesc, (kk | sl) != 0);
+            mma_f16(d, ad + 2 * sl, bl + 2 * sl, idesc, 1u);
+          }
+        } else {
+#pragma unroll
+          for (int sl = 0; sl < 2; sl++)             // columns 0..31 carry the min term
+            mma_f16(tmem + kXMin, ad + 2 * sl, bh + 2 * sl, idesc, (sbi | sl) != 0);
+        }
+        mma_commit(&empty_a[sa]);
+        mma_commit(&empty_b[sbs]);
+        if (kk == 3) mma_commit(&buf_full[sbi & 1]);
+        issued++;
+        if (++kk == SPS) {
+          kk = 0;
+          sbi++;
+        }
+      }
+      mma_commit(acc_full);
+      if (issued < nsteps) *abort_flag = 1;
+      if (!mbar_wait_bounded(acc_full, 0u, globaltimer_ns() + WAIT_DEADLINE_NS)) atomicOr(p.status, ST_DRAIN_TIMEOUT);
+    }
+  } else if (warp < kXEpiWarp0) {
+    // ---- dequantizing warps: warp dw owns unit dw of the tile; lane -> row m, half tp (as gemm_kq_kernel)
+    const int dw = warp - kXDqWarp0;
+    const int m = (lane & 7) + 8 * (lane >> 4), tp = (lane >> 3) & 1, row = 16 * dw + m;
+    const bool present = dw < ntile;
+    const uint8_t *ubase = p.w + (int64_t)(tile0 + (present ? dw : 0)) * nb * US;
+    uint32_t aoff[4];                              // this lane's 16-byte pieces of a swizzled A tile
+#pragma unroll
+    for (int j = 0; j < 4; j++) aoff[j] = sw128_off(row, 16 * j + 8 * tp);
+    // the next super-block's words are loaded into registers while this one is dequantized
+    Raw<FMT> nxt;
+    DqX<FMT> cur;
+    if (present) nxt.load(ubase + (int64_t)koff_sb * US, m, tp);
+    int kk = 0, sbi = 0, snext = koff_sb + 1 < nb ? koff_sb + 1 : 0;
+    for (int s = 0; s < nsteps; s++) {
+      const int st = s % AS;
+      if (kk == 0) {
+        if (present) {
+          cur.set(nxt);
+          if (sbi + 1 < nb) nxt.load(ubase + (int64_t)snext * US, m, tp);
+        }
+        if (++snext == nb) snext = 0;
+      }
+      if (s >= AS && !waitw(&empty_a[st], (uint32_t)(s / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
+      uint4 out[4];
+      if (present) {
+        switch (kk) {
+          case 0: cur.template emit<0>(out); break;
+          case 1: cur.template emit<1>(out); break;
+          case 2: cur.template emit<2>(out); break;
+          case 3: cur.template emit<3>(out); break;
+          default:
+            if constexpr (MINS) cur.emit_min(tp, p.wscale, out);
+            break;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++) out[j] = make_uint4(0, 0, 0, 0);
+      }
+      uint8_t *at = a_ring + (size_t)st * kTileBytes;
+#pragma unroll
+      for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at + aoff[j]) = out[j];
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_a[st]);
+      if (++kk == SPS) {
+        kk = 0;
+        sbi++;
+      }
+    }
+  } else {
+    // ---- epilogue: warp w owns TMEM lanes 32 (w % 4) ..; per super-block total += d * buffer
+    const int quarter = warp & 3;
+    const int64_t row = (int64_t)m_tile * GM + quarter * 32 + lane;
+    const int64_t t16 = row / 16;
+    const bool rv = row < p.rows && t16 < tiles16;
+    const uint8_t *urow = p.w + t16 * nb * US;
+    const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    const int nch = (nmma + 31) / 32;
+    const int mrow = (int)(row & 15);
+    const unsigned short *dptr = reinterpret_cast<const unsigned short *>(
+        urow + (FMT == T_Q6_K ? kQ6DOff + 2 * mrow : (FMT == T_Q4_K ? 2048 : 2560) + 16 * mrow));
+    bool ok = true;
+    int sbg = koff_sb;
+    for (int sbi = 0; sbi < nb && ok; sbi++) {
+      const float d = rv ? h2f(__ldg(dptr + (int64_t)sbg * (US / 2))) : 0.f;
+      if (++sbg == nb) sbg = 0;
+      ok = waitw<true>(&buf_full[sbi & 1], (uint32_t)(sbi >> 1) & 1u, ctl, ST_FULL_TIMEOUT, lane);
+      ok = __shfl_sync(0xffffffffu, ok && !*abort_flag, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t buf = tmem + lanes + (uint32_t)((sbi & 1) * GN);
+      for (int c = 0; c < nch; c++) {
+        float v[32], t[32];
+        tmem_ld32(buf + c * 32, v);
+        if (sbi > 0) {
+          tmem_ld32(tmem + lanes + kXTot + c * 32, t);
+#pragma unroll
+          for (int i = 0; i < 32; i++) t[i] = __fmaf_rn(d, v[i], t[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i++) t[i] = __fmul_rn(d, v[i]);
+        }
+        tmem_st32(tmem + lanes + kXTot + c * 32, t);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&buf_free[sbi & 1]);
+    }
+    if (ok) ok = waitw<true>(acc_full, 0u, ctl, ST_FULL_TIMEOUT, lane);
+    ok = __shfl_sync(0xffffffffu, ok && !*abort_flag, 0);
+    tc_fence_after();
+    if (ok) {
+      for (int c = 0; c < nch; c++) {
+        const int col0 = c * 32;
+        if (col0 >= ntok_tile) break;
+        float t[32], mv[32];
+        tmem_ld32(tmem + lanes + kXTot + col0, t);
+        if constexpr (MINS) {
+          tmem_ld32(tmem + lanes + kXMin + col0, mv);
+#pragma unroll
+          for (int i = 0; i < 32; i++) t[i] = __fmaf_rn(mv[i], p.wscale_inv, t[i]);
+        }
+        if (p.swiglu) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            const int tok = n_tile * GN + col0 + i;
+            if (tok < p.ntok) {
+              const float o = t[i] * p.bscale[tok];
+              const float up = __shfl_xor_sync(0xffffffffu, o, 1);
+              if (row < p.rows && (row & 1) == 0) {
+                const double z = o;
+                const double sl = __ddiv_rn(z, __dadd_rn(1.0, exp(-z)));
+                p.y[(int64_t)tok * p.y_stride + row / 2] = __double2float_rn(__dmul_rn(sl, (double)up));
+              }
+            }
+          }
+        } else if (row < p.rows) {
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            const int tok = n_tile * GN + col0 + i;
+            if (tok < p.ntok) {
+              float o = t[i] * p.bscale[tok];
+              const int64_t at = (int64_t)tok * p.y_stride + row;
+              if (p.y_add) o = __fadd_rn(p.y_add[at], o);
+              p.y[at] = o;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kXMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kXTmemCols);
+  }
+}
+
+// Activation tiles of the kx walk: [n_tile][step][hi, lo][128][64] f16, steps kk < 4 of super-block
+// sb are values 256 sb + 64 kk .. as gemm_bfill_kernel writes them; Q4_K / Q5_K's step 4 is the min
+// step: xsum of sub-block j (xd * xs, the sum of its dequantized activation) * 2^-5 / bscale as
+// [hi x8 | lo x8 | hi x8 | 0] in the hi tile.
+__global__ void gemm_bfill_kx_kernel(const int8_t *xq, const float *xd, int64_t k, int ntok, int npad,
+                                     const float *bscale, int sps, uint8_t *bt) {
+  const int64_t groups = k / 8, total = (int64_t)npad * groups;
+  const int nsteps = (int)(k / 256) * sps;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int n = (int)(e / groups);
+    const int64_t g8 = e % groups, k0 = g8 * 8;
+    uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+    if (n < ntok) {
+      const float sc = xd[(int64_t)n * (k / 32) + k0 / 32] / bscale[n];
+      const uint2 q = *reinterpret_cast<const uint2 *>(xq + (int64_t)n * k + k0);
+      const int8_t *qb = reinterpret_cast<const int8_t *>(&q);
+#pragma unroll
+      for (int i = 0; i < 4; i++) split2(sc * (float)qb[2 * i], sc * (float)qb[2 * i + 1], h[i], l[i]);
+    }
+    const int nt = n / GN, nr = n % GN, c = (int)(k0 / 64), kk = (int)(k0 % 64);
+    const int step = (c >> 2) * sps + (c & 3);
+    uint8_t *base = bt + ((int64_t)nt * nsteps + step) * 2 * kTileBytes + sw128_off(nr, kk);
+    *reinterpret_cast<uint4 *>(base) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4 *>(base + kTileBytes) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+__global__ void gemm_bfill_kx_min_kernel(const float *xd, const int32_t *xs, int64_t k, int ntok, int npad,
+                                         const float *bscale, uint8_t *bt) {
+  const int nb = (int)(k / 256), nsteps = nb * 5;
+  const int64_t total = (int64_t)npad * nb * 8;         // (token, super-block, 16-byte chunk)
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int n = (int)(e / (nb * 8)), sb = (int)((e / 8) % nb), ch = (int)(e % 8);
+    uint32_t hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
+    if (n < ntok && ch < 3) {
+      const float inv = 0.03125f / bscale[n];          // 2^-5 / 2^e: exact
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        float v[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+          const int64_t b = (int64_t)n * (k / 32) + sb * 8 + 2 * i + u;
+          v[u] = __fmul_rn(xd[b], (float)xs[b]) * inv;
+        }
+        split2(v[0], v[1], hi[i], lo[i]);
+      }
+    }
+    const int nt = n / GN, nr = n % GN;
+    uint8_t *base = bt + ((int64_t)nt * nsteps + sb * 5 + 4) * 2 * kTileBytes;
+    const uint4 val = ch == 0 || ch == 2 ? make_uint4(hi[0], hi[1], hi[2], hi[3])
+                      : ch == 1           ? make_uint4(lo[0], lo[1], lo[2], lo[3])
+                                          : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4 *>(base + sw128_off(nr, 8 * ch)) = val;
+    *reinterpret_cast<uint4 *>(base + kTileBytes + sw128_off(nr, 8 * ch)) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Per matrix, for the kx path: bits of max |dmin| * 63 (Q4_K / Q5_K: the min values' range) and, for
+// Q6_K, the largest |scale| (exact only up to 64).
+template <int FMT>
+__global__ void kx_info_kernel(const uint8_t *w, int64_t nunits, unsigned *out) {
+  constexpr int US = FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360;
+  float b = 0.f;
+  unsigned scmax = 0;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nunits * 16; e += (int64_t)gridDim.x * blockDim.x) {
+    const uint8_t *u = w + (e / 16) * US;
+    const int m = (int)(e % 16);
+    if constexpr (FMT == T_Q6_K) {
+      for (int i = 0; i < 16; i++) {
+        const int v = (int)(int8_t)u[kQ6SOff + 16 * m + i];
+        scmax = max(scmax, (unsigned)(v < 0 ? -v : v));
+      }
+    } else {
+      const uint32_t h = *reinterpret_cast<const uint32_t *>(u + (FMT == T_Q4_K ? 2048 : 2560) + 16 * m);
+      float v = fabsf(h2f(h >> 16)) * 63.f;
+      if (!(v <= 3.0e38f)) v = __int_as_float(0x7f800000);
+      b = fmaxf(b, v);
+    }
+  }
+  atomicMax(out, __float_as_uint(b));
+  atomicMax(out + 1, scmax);
+}
+
 }  // namespace
 
 cudaError_t launch_kq_bound(const DevMatrix &m, unsigned *out, cudaStream_t s) {
@@ -818,6 +1190,86 @@ cudaError_t launch_gemm_f16_tiled(const void *tiles, int64_t rows, int64_t k, co
   a.wscale = 1.f; a.wscale_inv = 1.f;
   a.nb = (int)(k / 256); a.kc = (int)(k / 64); a.status = status;
   return launch_t<T_F16>(a, dim3((unsigned)(mpad / GM), (unsigned)(npad / GN)), smem_bytes<T_F16>(), s);
+}
+
+// ---------------------------------------------------------------------------- exact-A GEMM host side
+cudaError_t launch_kx_info(const DevMatrix &m, unsigned *out, cudaStream_t s) {
+  const int64_t nunits = (m.rows + 15) / 16 * (m.cols / 256);
+  const int64_t grid = (nunits * 16 + 255) / 256 < 1024 ? (nunits * 16 + 255) / 256 : 1024;
+  cudaError_t e = cudaMemsetAsync(out, 0, 8, s);
+  if (e != cudaSuccess) return e;
+  switch (m.type) {
+    case T_Q4_K: kx_info_kernel<T_Q4_K><<<(unsigned)grid, 256, 0, s>>>(m.data, nunits, out); break;
+    case T_Q5_K: kx_info_kernel<T_Q5_K><<<(unsigned)grid, 256, 0, s>>>(m.data, nunits, out); break;
+    case T_Q6_K: kx_info_kernel<T_Q6_K><<<(unsigned)grid, 256, 0, s>>>(m.data, nunits, out); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+int kx_steps(int type) { return type == T_Q6_K ? kx_steps_per_sb<T_Q6_K>() : kx_steps_per_sb<T_Q4_K>(); }
+
+size_t gemm_bx_bytes(int64_t k, int ntok, int type) {
+  const int64_t npad = gemm_tokens_pad(ntok);
+  return (size_t)(npad / GN) * (size_t)(k / 256) * kx_steps(type) * kPairBytes + (size_t)npad * 4;
+}
+
+cudaError_t launch_gemm_prep_kx(const ActView &act, int ntok, int type, void *bbuf, cudaStream_t s) {
+  const int64_t npad = gemm_tokens_pad(ntok), k = act.k;
+  const int sps = kx_steps(type);
+  uint8_t *bt = reinterpret_cast<uint8_t *>(bbuf);
+  float *bscale = reinterpret_cast<float *>(bt + (npad / GN) * (k / 256) * sps * kPairBytes);
+  const int threads = 256;
+  gemm_bscale_kernel<<<(unsigned)((npad * 32 + threads - 1) / threads), threads, 0, s>>>(act.xd, k / 32, ntok, (int)npad,
+                                                                                         bscale);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  int64_t total = npad * (k / 8);
+  int64_t grid = (total + threads - 1) / threads < 148 * 16 ? (total + threads - 1) / threads : 148 * 16;
+  gemm_bfill_kx_kernel<<<(unsigned)grid, threads, 0, s>>>(act.xq, act.xd, k, ntok, (int)npad, bscale, sps, bt);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || sps == 4) return e;
+  total = npad * (k / 256) * 8;
+  grid = (total + threads - 1) / threads < 148 * 8 ? (total + threads - 1) / threads : 148 * 8;
+  gemm_bfill_kx_min_kernel<<<(unsigned)grid, threads, 0, s>>>(act.xd, act.xs, k, ntok, (int)npad, bscale, bt);
+  return cudaGetLastError();
+}
+
+template <int FMT>
+static cudaError_t launch_kx_t(const GemmArgs &a, dim3 grid, cudaStream_t s) {
+  static bool granted[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!granted[dev]) {
+    e = cudaFuncSetAttribute(gemm_kx_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kx_smem_bytes());
+    if (e != cudaSuccess) return e;
+    granted[dev] = true;
+  }
+  gemm_kx_kernel<FMT><<<grid, kXThreads, kx_smem_bytes(), s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_kx(const DevMatrix &m, const void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
+                           float mscale, unsigned *status, cudaStream_t s, bool swiglu) {
+  if (!gemm_kq_supported(m) || (swiglu && (m.rows % 2 || y_add))) return cudaErrorInvalidValue;
+  const int64_t npad = gemm_tokens_pad(ntok);
+  GemmArgs a{};
+  a.w = m.data;
+  a.b = reinterpret_cast<const uint8_t *>(bbuf);
+  a.bscale = reinterpret_cast<const float *>(a.b + (npad / GN) * (m.cols / 256) * kx_steps(m.type) * kPairBytes);
+  a.y = y; a.y_add = y_add; a.y_stride = y_stride;
+  // the min values carry mscale and xsum 2^-5: their accumulator comes back with 2^5 / mscale
+  a.wscale = mscale; a.wscale_inv = 32.f / mscale; a.swiglu = swiglu ? 1 : 0;
+  a.rows = m.rows; a.ntok = ntok; a.nb = (int)(m.cols / 256); a.kc = (int)(m.cols / 64);
+  a.status = status;
+  const dim3 grid((unsigned)((m.rows + GM - 1) / GM), (unsigned)(npad / GN));
+  switch (m.type) {
+    case T_Q4_K: return launch_kx_t<T_Q4_K>(a, grid, s);
+    case T_Q5_K: return launch_kx_t<T_Q5_K>(a, grid, s);
+    default: return launch_kx_t<T_Q6_K>(a, grid, s);
+  }
 }
 
 }  // namespace zllm

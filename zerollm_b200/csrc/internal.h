@@ -177,6 +177,16 @@ cudaError_t launch_kq_bound(const DevMatrix &m, unsigned *out, cudaStream_t s);
 cudaError_t launch_gemm_prep(const ActView &act, int ntok, void *bbuf, cudaStream_t s);
 cudaError_t launch_gemm_kq(const DevMatrix &m, const void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
                            float wscale, unsigned *status, cudaStream_t s, bool swiglu = false);
+// The exact-A variant of the same GEMM (weights dequantized exactly into f16, two MMAs per slice,
+// per-super-block scaling in TMEM): launch_kx_info writes (bits of max |dmin| * 63, max |Q6_K scale|)
+// of a matrix; Q4_K / Q5_K with finite scales always qualify, Q6_K when every |scale| <= 64.  The
+// activation goes through launch_gemm_prep_kx (gemm_bx_bytes of scratch); mscale is the power of
+// two gemm_weight_scale gives for the dmin bound.
+cudaError_t launch_kx_info(const DevMatrix &m, unsigned *out, cudaStream_t s);
+size_t gemm_bx_bytes(int64_t k, int ntok, int type);
+cudaError_t launch_gemm_prep_kx(const ActView &act, int ntok, int type, void *bbuf, cudaStream_t s);
+cudaError_t launch_gemm_kx(const DevMatrix &m, const void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
+                           float mscale, unsigned *status, cudaStream_t s, bool swiglu = false);
 // Tensor-parallel collectives (tp.cu): NCCL opened at run time.  Return 0 / cudaSuccess, else set *why.
 size_t tp_unique_id_bytes();
 int tp_unique_id(void *out, size_t bytes, const char **why);
@@ -188,7 +198,7 @@ cudaError_t tp_allreduce_sum(void *comm, float *buf, size_t count, cudaStream_t 
 // mapped.  Collective: every rank calls setup and destroy.
 struct TpAr;
 int tp_ar_setup(void *comm, int rank, int size, int64_t cap, cudaStream_t s, TpAr **out, const char **why);
-cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStream_t s);
+cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStream_t s, bool pdl = false);
 void tp_ar_destroy(TpAr *ar, void *comm, cudaStream_t s);
 // Vocab-split output head: every rank's logits slice (padded to vpad columns) to every rank, then
 // the slices in vocab order (rank r holds rows [r V / size, (r + 1) V / size)).

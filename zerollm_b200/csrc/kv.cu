@@ -45,12 +45,14 @@ __device__ void post_head(const QkvPostArgs &a, int t, int h, float *row, float 
   }
   __syncwarp();
   if (norm) {
-    // rmsnorm (ref-kernels.js:305-310): ss summed in double in element order (as the JS loop), then
-    // s = 1 / sqrt(ss / n + eps) and out = f32(x * s * w)
+    // rmsnorm (ref-kernels.js:305-310): ss summed in double, then s = 1 / sqrt(ss / n + eps) and
+    // out = f32(x * s * w).  The sum is a fixed tree (each lane its elements in order, then a
+    // butterfly over the lanes) rather than the JS loop's left-to-right order: the double can differ
+    // in its last bits, and the f32 outputs then only when that crosses an f32 rounding boundary
+    // (as rmsnorm_quant_kernel's tree)
     double ss = 0.0;
-    if (lane == 0)
-      for (int i = 0; i < hd; i++) ss = __dadd_rn(ss, __dmul_rn((double)row[i], (double)row[i]));
-    ss = __shfl_sync(0xffffffffu, ss, 0);
+    for (int i = lane; i < hd; i += 32) ss = __dadd_rn(ss, __dmul_rn((double)row[i], (double)row[i]));
+    ss = warp_sum_f64(ss);
     const double s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)hd), a.eps)));
     for (int i = lane; i < hd; i += 32) row[i] = __double2float_rn(__dmul_rn(__dmul_rn((double)row[i], s), (double)norm[i]));
   }
@@ -181,8 +183,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
   __shared__ float sq[G][HD];                           // fused: this KV head's roped queries
   __shared__ int last_flag;
 
+  // Under programmatic dependent launch this runs while the q/k/v projection finishes: in a fused
+  // decode pass the cache rows of earlier positions and the lengths are not that kernel's output, so
+  // the first K/V batch streams in before griddepcontrol.wait; q and the newest row are read after.
   pdl_launch_dependents();
-  pdl_wait();                                         // q and the newest K/V row come from the previous kernel
+  if (!a.fused) pdl_wait();                           // unfused: every input may be the previous kernel's
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   // the partition depends on the sequence's own length only, so a query gets the same bits alone
@@ -214,9 +219,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
       v[j].load(vpool + o, lane, p == newp);
     }
   };
-  // the first batch streams in during the fused prologue unless it holds the row being appended
-  const bool early = !(w0 <= newp && newp < w0 + NB);
+  // fused: the first batch streams in during the wait and the prologue unless it holds the row this
+  // kernel appends; unfused, the previous kernel may have appended any of the rows (zllm_qkv_append
+  // just before), so every load waits
+  const bool early = a.fused && !(w0 <= newp && newp < w0 + NB);
   if (w0 < w1 && early) load_batch(w0, kr, vr);
+  if (a.fused) pdl_wait();                            // q / k / v come from the previous kernel
   if (a.fused) {
     // q/k/v post-processing of this query (qkv_post_kernel's arithmetic): warps take the KV head's
     // G query heads, and in the last split also the key / value head, which is appended before any

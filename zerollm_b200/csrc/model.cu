@@ -354,10 +354,11 @@ extern "C" int zllm_model_ready(zllm_model *m) {
   CK(dalloc(&m->hb, MB * F), "act");
   if (MB >= kGemmMinTokens) {
     // passes of kGemmMinTokens or more tokens run the k-quant projections as tensor-core GEMMs
-    CK(cudaMalloc(&m->gemm_b, gemm_b_bytes(KX, MB)), "GEMM activation tiles");
+    size_t gb = gemm_b_bytes(KX, MB);
     for (auto &L : m->L)
       for (zllm_weight *w : {L.w[0], L.w[1], L.w[2], L.w[3], L.w[4], L.w[5], L.w[6], L.qkv, L.gu})
-        if (w && kq_type(w->m.type)) zllm_weight_gemm_ok(m->ctx, w);
+        if (w && kq_type(w->m.type) && zllm_weight_gemm_ok(m->ctx, w)) gb = std::max(gb, gemm_act_bytes(w, MB));
+    CK(cudaMalloc(&m->gemm_b, gb), "GEMM activation tiles");
   }
   CK(dalloc(&m->logits, (size_t)LB * c.vocab), "logits");
   CK(dalloc(&m->arg_v, (size_t)LB * kArgmaxChunks), "argmax scratch");
@@ -417,9 +418,7 @@ static bool use_gemm(const zllm_model *m, const zllm_weight *w, int n) {
 static cudaError_t gemm(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add, int64_t k,
                         bool swiglu) {
   const ActView a{m->xq, m->xd, m->xs, nullptr, k};
-  cudaError_t e = launch_gemm_prep(a, n, m->gemm_b, m->stream);
-  if (e != cudaSuccess) return e;
-  return launch_gemm_kq(w->m, m->gemm_b, n, y, ys, y_add, w->gemm_wscale, m->ctx->status_dev, m->stream, swiglu);
+  return gemm_run(w, a, n, m->gemm_b, y, ys, y_add, m->ctx->status_dev, m->stream, swiglu);
 }
 
 static cudaError_t gemv(zllm_model *m, const zllm_weight *w, int n, float *y, int64_t ys, const float *y_add, const float *xf,
@@ -441,7 +440,9 @@ static cudaError_t gemv_ex(zllm_model *m, const zllm_weight *w, int n, float *y,
 // Sum the ranks' x (n tokens x n_embd) in place: the all-reduce after a row-parallel projection.
 static cudaError_t tp_reduce(zllm_model *m, int n) {
   if (m->tp_size <= 1) return cudaSuccess;
-  if (m->tp_ar) return tp_ar_sum(m->tp_ar, m->x, (int64_t)n * m->c.n_embd, m->ctx->status_dev, m->stream);
+  // chained with programmatic dependent launch: the all-reduce waits for the GEMV in hardware and the
+  // next GEMV streams its weights in while the ranks exchange their partial sums
+  if (m->tp_ar) return tp_ar_sum(m->tp_ar, m->x, (int64_t)n * m->c.n_embd, m->ctx->status_dev, m->stream, true);
   const char *why = "";
   return tp_allreduce_sum(m->tp_comm, m->x, (size_t)n * m->c.n_embd, m->stream, &why);
 }
@@ -455,10 +456,9 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want, bool distinct) {
   const int64_t E = c.n_embd, F = c.n_ff, Q = m->qdim(), KV = m->kvdim();
   cudaStream_t s = m->stream;
   cudaError_t e;
-  // Programmatic dependent launch for the GEMVs only (each streams its first weights in before it
-  // waits for its activation): in single-token passes where a GEMV follows a GEMV -- ahead of the
-  // attention and the small kernels the early-resident CTAs cost more than they save -- and for
-  // every k-quant GEMV of a multi-token pass (measured: +2 % at 32 sequences, batch 1 unchanged).
+  // Programmatic dependent launch (a kernel streams its weights or cache rows in before it waits
+  // for its input): in single-token passes for the GEMVs, the attention and the o projection after
+  // it; and for every k-quant GEMV of a multi-token pass (measured: +2 % at 32 sequences).
 #define RUN(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
   RUN(launch_embed(m->tok->m, m->d_tok, n, m->x, s, false));
   const zllm_attn_geom g = m->geom();
@@ -504,13 +504,16 @@ static cudaError_t enqueue_pass(zllm_model *m, int n, int want, bool distinct) {
     // one split count for every pass: a query's context partition (and so its rounding) does not
     // depend on how many tokens share the pass, so batched passes equal token-by-token ones bit for bit
     aa.n_head = c.n_head; aa.n_kv = c.n_head_kv; aa.head_dim = c.head_dim; aa.nseq = n; aa.nsplit = m->nsplit;
-    RUN(launch_attn(aa, c.kv_f16 != 0, s, false));
+    // single-token passes chain the attention and the o projection with programmatic dependent
+    // launch: the attention streams its first K/V rows while the q/k/v GEMV finishes, and the o
+    // GEMV's CTAs land on the SMs the attention leaves free and stream their weights meanwhile
+    RUN(launch_attn(aa, c.kv_f16 != 0, s, one));
     // tensor parallel: attn_output and ffn_down are row-parallel, so each rank holds a partial sum;
     // rank 0 adds the residual, the others overwrite x, and one all-reduce gives every rank
     // x + sum of the partials
     const float *res = m->tp_size > 1 && m->tp_rank != 0 ? nullptr : m->x;
     if (one && kq_type(L.w[WO]->m.type)) {
-      RUN(gemv_ex(m, L.w[WO], 1, m->x, E, res, ActView{nullptr, nullptr, nullptr, m->att, Q}, GemvFuse{}));
+      RUN(gemv_ex(m, L.w[WO], 1, m->x, E, res, ActView{nullptr, nullptr, nullptr, m->att, Q}, GemvFuse{}, true));
     } else {
       RUN(launch_quantize(m->att, Q, n, m->xq, m->xd, m->xs, m->ctx->status_dev, s, false));
       RUN(gemv(m, L.w[WO], n, m->x, E, res, m->att, Q, true));                      // x += wo . att

@@ -180,6 +180,11 @@ __device__ __forceinline__ int ld_acquire_sys(const int *p) {
 // seen this rank's stamp of the epoch in between, which this rank writes after its reads of p.
 __global__ void __launch_bounds__(kArThreads) tp_ar_kernel(const ArArgs a) {
   const int c = blockIdx.x, tid = threadIdx.x;
+  // under programmatic dependent launch the next GEMV may become resident now and stream its
+  // weights; x (and the epoch, which the previous all-reduce advanced before any later kernel ran)
+  // are read only after the producing kernel has completed
+  pdl_launch_dependents();
+  pdl_wait();
   int *myflags = reinterpret_cast<int *>(a.mine + ar_flag_off(a.cap));
   int *epoch = myflags + kArMaxRanks * kArMaxCtas, *done = epoch + 1;
   const int e = *reinterpret_cast<volatile int *>(epoch) + 1;
@@ -290,7 +295,7 @@ int tp_ar_setup(void *comm, int rank, int size, int64_t cap, cudaStream_t s, TpA
   return -1;
 }
 
-cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStream_t s) {
+cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStream_t s, bool pdl) {
   if (n > ar->cap) return cudaErrorInvalidValue;
   ArArgs a{};
   a.x = x;
@@ -301,11 +306,21 @@ cudaError_t tp_ar_sum(TpAr *ar, float *x, int64_t n, unsigned *status, cudaStrea
   a.cap = ar->cap;
   a.rank = ar->rank;
   a.size = ar->size;
-  int64_t ctas = (n + 1023) / 1024;
+  // slices of 256 values: a one-token hidden state (5120) spreads over 20 CTAs, each with its own
+  // peer stores and stamp polls in flight
+  int64_t ctas = (n + kArThreads - 1) / kArThreads;
   if (ctas > kArMaxCtas) ctas = kArMaxCtas;
   if (ctas < 1) ctas = 1;
-  tp_ar_kernel<<<(unsigned)ctas, kArThreads, 0, s>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(kArThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, tp_ar_kernel, a);
 }
 
 // Failure detection without a fault: the all-reduce kernel on this GPU against a phantom second
