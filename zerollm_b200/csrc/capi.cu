@@ -255,12 +255,12 @@ int zllm_weight_gemm_ok(zllm_ctx *c, zllm_weight *w) {
 // The tensor-core GEMM of a qualifying weight on ntok >= kGemmMinTokens tokens of (xq, xd, xs):
 // activation tiles in bbuf (gemm_act_bytes), then the product.
 size_t gemm_act_bytes(const zllm_weight *w, int ntok) {
-  return w->gemm_kx ? gemm_bx_bytes(w->m.cols, ntok, w->m.type) : gemm_b_bytes(w->m.cols, ntok);
+  return w->gemm_kx ? gemm_bx_bytes(w->m.cols, ntok, w->m.type, w->m.rows) : gemm_b_bytes(w->m.cols, ntok);
 }
 cudaError_t gemm_run(const zllm_weight *w, const ActView &a, int ntok, void *bbuf, float *y, int64_t y_stride,
                      const float *y_add, unsigned *status, cudaStream_t st, bool swiglu) {
   if (w->gemm_kx) {
-    cudaError_t e = launch_gemm_prep_kx(a, ntok, w->m.type, bbuf, st);
+    cudaError_t e = launch_gemm_prep_kx(a, ntok, w->m.type, w->m.rows, bbuf, st);
     return e == cudaSuccess ? launch_gemm_kx(w->m, bbuf, ntok, y, y_stride, y_add, w->gemm_mscale, status, st, swiglu) : e;
   }
   cudaError_t e = launch_gemm_prep(a, ntok, bbuf, st);

@@ -228,6 +228,12 @@ struct GemmArgs {
   int ntok, nb, kc;       // tokens, super-blocks per row, 64-value chunks per row
   int swiglu;             // rows are (gate, up) pairs: y[t][r / 2] = silu(gate) * up
   unsigned *status;
+  // exact-A kernel only: bytes of one activation tile (128 x 64 f16, or fewer rows for a single
+  // short token tile), and split-K: nsplit CTAs per output tile, sbps super-blocks each, partial
+  // sums in ws [split][token][row], tile_cnt counting the splits that are done
+  int btile, nsplit, sbps;
+  float *ws;
+  unsigned *tile_cnt;
 };
 
 // A CTA computes a 128-row x 128-token tile; its MMAs use N = the tile's tokens rounded up to 16,
@@ -445,8 +451,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
 // ---------------------------------------------------------------------------- activation tiles
 // Per token t: the power of two 2^e_t with every |xd * xq| * 2^-e_t below 2^15 (f16 keeps 11 bits
 // down to 2^-14 of it); bscale[t] = 2^e_t multiplies the accumulators back.  Padding tokens get 1.
-__global__ void gemm_bscale_kernel(const float *xd, int64_t nblk, int ntok, int npad, float *bscale) {
+__global__ void gemm_bscale_kernel(const float *xd, int64_t nblk, int ntok, int npad, float *bscale, unsigned *zero = nullptr,
+                                   int nzero = 0) {
   const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  for (int i = (int)(blockIdx.x * blockDim.x + threadIdx.x); i < nzero; i += (int)(gridDim.x * blockDim.x)) zero[i] = 0;
   if (warp >= npad) return;
   float amax = 0.f;
   if (warp < ntok)
@@ -724,6 +732,41 @@ template <> struct DqX<T_Q6_K> {
   }
 };
 
+// y for 32 tokens from tok0 of one row (a lane): t = output / bscale (kx_store) or the output itself
+// (kx_store_scaled); SwiGLU pairs rows 2i, 2i + 1 across neighbouring lanes
+__device__ __forceinline__ void kx_store_scaled(const GemmArgs &p, const float (&t)[32], int tok0, int64_t row) {
+  if (p.swiglu) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      const int tok = tok0 + i;
+      const float o = t[i];
+      const float up = __shfl_xor_sync(0xffffffffu, o, 1);
+      if (tok < p.ntok && row < p.rows && (row & 1) == 0) {
+        const double z = o;
+        const double sl = __ddiv_rn(z, __dadd_rn(1.0, exp(-z)));
+        p.y[(int64_t)tok * p.y_stride + row / 2] = __double2float_rn(__dmul_rn(sl, (double)up));
+      }
+    }
+  } else if (row < p.rows) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      const int tok = tok0 + i;
+      if (tok < p.ntok) {
+        float o = t[i];
+        const int64_t at = (int64_t)tok * p.y_stride + row;
+        if (p.y_add) o = __fadd_rn(p.y_add[at], o);
+        p.y[at] = o;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void kx_store(const GemmArgs &p, const float (&t)[32], int tok0, int64_t row) {
+  float o[32];
+#pragma unroll
+  for (int i = 0; i < 32; i++) o[i] = tok0 + i < p.ntok ? t[i] * p.bscale[tok0 + i] : 0.f;
+  kx_store_scaled(p, o, tok0, row);
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p) {
   constexpr int US = FMT == T_Q4_K ? 2304 : FMT == T_Q5_K ? 2816 : 3360;
@@ -737,17 +780,20 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   uint64_t *buf_full = empty_b + BS, *buf_free = buf_full + 2, *acc_full = buf_free + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile int *last_flag = reinterpret_cast<volatile int *>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tile = blockIdx.x, n_tile = blockIdx.y;
-  const int nb = p.nb, nsteps = nb * SPS;
+  const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
+  const int nb = p.nb, nsteps_all = nb * SPS;
+  // this CTA's super-blocks: [sb0, sb0 + nsb) of the row (split-K), walked from local index koff_sb
+  const int sb0 = split * p.sbps, nsb = min(nb, sb0 + p.sbps) - sb0, nsteps = nsb * SPS;
   const int64_t tiles16 = (p.rows + 15) / 16;
   const int tile0 = m_tile * 8;
   const int ntile = (int)min((int64_t)8, tiles16 - tile0);
   const Ctl ctl{abort_flag, p.status};
-  // each M tile starts at its own super-block (spreads the CTAs of one token tile over the activation);
-  // the order of the super-block sums then depends on the tile alone
-  const int koff_sb = nb > 0 ? (m_tile * 7) % nb : 0;
+  // each M tile starts at its own super-block of the range (spreads the CTAs of one token tile over
+  // the activation); the order of the super-block sums then depends on the tile alone
+  const int koff_sb = nsb > 0 ? (m_tile * 7) % nsb : 0;
   const int ntok_tile = min(GN, p.ntok - n_tile * GN);
   const int nmma = (ntok_tile + 15) / 16 * 16;
 
@@ -769,12 +815,12 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
     // ---- activation producer: one lane, one bulk copy per step (the min step: its hi tile alone);
     // step s of the walk is step (sb + koff) * SPS + kk of the tiles
     if (lane == 0) {
-      const uint32_t part = (uint32_t)nmma * 128;      // the first nmma rows of a 128-row tile
-      int kk = 0, sbg = koff_sb, issued = 0;
+      const uint32_t part = (uint32_t)nmma * 128;      // the first nmma rows of a tile
+      int kk = 0, sbl = koff_sb, issued = 0;
       for (int s = 0; s < nsteps; s++) {
         const int st = s % BS;
         if (s >= BS && !wait1(&empty_b[st], (uint32_t)(s / BS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
-        const uint8_t *src = p.b + ((int64_t)n_tile * nsteps + sbg * SPS + kk) * 2 * kTileBytes;
+        const uint8_t *src = p.b + ((int64_t)n_tile * nsteps_all + (int64_t)(sb0 + sbl) * SPS + kk) * 2 * p.btile;
         uint8_t *dst = b_ring + (size_t)st * kPairBytes;
         const bool hi_only = MINS && kk == 4;
         mbar_arrive_expect_tx(&full_b[st], hi_only ? part : 2 * part);
@@ -782,12 +828,12 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
           bulk_g2s(dst, src, 2 * kTileBytes, &full_b[st]);
         } else {
           bulk_g2s(dst, src, part, &full_b[st]);
-          if (!hi_only) bulk_g2s(dst + kTileBytes, src + kTileBytes, part, &full_b[st]);
+          if (!hi_only) bulk_g2s(dst + kTileBytes, src + p.btile, part, &full_b[st]);
         }
         issued++;
         if (++kk == SPS) {
           kk = 0;
-          if (++sbg == nb) sbg = 0;
+          if (++sbl == nsb) sbl = 0;
         }
       }
       // copies still landing in shared memory (an abort) are waited for before the CTA exits
@@ -849,16 +895,16 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
     // the next super-block's words are loaded into registers while this one is dequantized
     Raw<FMT> nxt;
     DqX<FMT> cur;
-    if (present) nxt.load(ubase + (int64_t)koff_sb * US, m, tp);
-    int kk = 0, sbi = 0, snext = koff_sb + 1 < nb ? koff_sb + 1 : 0;
+    if (present && nsb > 0) nxt.load(ubase + (int64_t)(sb0 + koff_sb) * US, m, tp);
+    int kk = 0, sbi = 0, snext = koff_sb + 1 < nsb ? koff_sb + 1 : 0;
     for (int s = 0; s < nsteps; s++) {
       const int st = s % AS;
       if (kk == 0) {
         if (present) {
           cur.set(nxt);
-          if (sbi + 1 < nb) nxt.load(ubase + (int64_t)snext * US, m, tp);
+          if (sbi + 1 < nsb) nxt.load(ubase + (int64_t)(sb0 + snext) * US, m, tp);
         }
-        if (++snext == nb) snext = 0;
+        if (++snext == nsb) snext = 0;
       }
       if (s >= AS && !waitw(&empty_a[st], (uint32_t)(s / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
       uint4 out[4];
@@ -900,10 +946,10 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
     const unsigned short *dptr = reinterpret_cast<const unsigned short *>(
         urow + (FMT == T_Q6_K ? kQ6DOff + 2 * mrow : (FMT == T_Q4_K ? 2048 : 2560) + 16 * mrow));
     bool ok = true;
-    int sbg = koff_sb;
-    for (int sbi = 0; sbi < nb && ok; sbi++) {
-      const float d = rv ? h2f(__ldg(dptr + (int64_t)sbg * (US / 2))) : 0.f;
-      if (++sbg == nb) sbg = 0;
+    int sbl = koff_sb;
+    for (int sbi = 0; sbi < nsb && ok; sbi++) {
+      const float d = rv ? h2f(__ldg(dptr + (int64_t)(sb0 + sbl) * (US / 2))) : 0.f;
+      if (++sbl == nsb) sbl = 0;
       ok = waitw<true>(&buf_full[sbi & 1], (uint32_t)(sbi >> 1) & 1u, ctl, ST_FULL_TIMEOUT, lane);
       ok = __shfl_sync(0xffffffffu, ok && !*abort_flag, 0);
       if (!ok) break;
@@ -941,32 +987,47 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
 #pragma unroll
           for (int i = 0; i < 32; i++) t[i] = __fmaf_rn(mv[i], p.wscale_inv, t[i]);
         }
-        if (p.swiglu) {
+        if (p.nsplit > 1) {
+          // this split's partial sums; the last split to finish adds them up below
+          if (row < p.rows) {
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            const int tok = n_tile * GN + col0 + i;
-            if (tok < p.ntok) {
-              const float o = t[i] * p.bscale[tok];
-              const float up = __shfl_xor_sync(0xffffffffu, o, 1);
-              if (row < p.rows && (row & 1) == 0) {
-                const double z = o;
-                const double sl = __ddiv_rn(z, __dadd_rn(1.0, exp(-z)));
-                p.y[(int64_t)tok * p.y_stride + row / 2] = __double2float_rn(__dmul_rn(sl, (double)up));
-              }
+            for (int i = 0; i < 32; i++) {
+              const int tok = n_tile * GN + col0 + i;
+              if (tok < p.ntok) p.ws[((int64_t)split * p.ntok + tok) * p.rows + row] = t[i] * p.bscale[tok];
             }
           }
-        } else if (row < p.rows) {
-#pragma unroll
-          for (int i = 0; i < 32; i++) {
-            const int tok = n_tile * GN + col0 + i;
-            if (tok < p.ntok) {
-              float o = t[i] * p.bscale[tok];
-              const int64_t at = (int64_t)tok * p.y_stride + row;
-              if (p.y_add) o = __fadd_rn(p.y_add[at], o);
-              p.y[at] = o;
-            }
-          }
+        } else {
+          kx_store(p, t, n_tile * GN + col0, row);
         }
+      }
+    }
+    if (p.nsplit > 1) {
+      // one arrival per CTA on the tile's counter (aborted CTAs too: the status word carries the
+      // error); the last one sums the splits in split order, so the bits do not depend on timing
+      __threadfence();
+      named_sync(1, kXEpiWarps * 32);
+      unsigned *cnt = p.tile_cnt + (int64_t)n_tile * gridDim.x + m_tile;
+      if (warp == kXEpiWarp0 && lane == 0) *last_flag = atomicAdd(cnt, 1u) == (unsigned)(p.nsplit - 1);
+      named_sync(1, kXEpiWarps * 32);
+      if (*last_flag) {
+        __threadfence();
+        for (int c = 0; c * 32 < ntok_tile; c++) {
+          const int tok0 = n_tile * GN + c * 32;
+          float t[32];
+#pragma unroll
+          for (int i = 0; i < 32; i++) t[i] = 0.f;
+          // split by split, 32 independent loads in flight; the sums in split order
+          for (int z = 0; z < p.nsplit; z++) {
+            const float *wz = p.ws + ((int64_t)z * p.ntok + tok0) * p.rows + row;
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = tok0 + i < p.ntok && row < p.rows ? __ldcg(wz + (int64_t)i * p.rows) : 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i++) t[i] = __fadd_rn(t[i], v[i]);
+          }
+          kx_store_scaled(p, t, tok0, row);
+        }
+        if (warp == kXEpiWarp0 && lane == 0) *cnt = 0;
       }
     }
   }
@@ -978,13 +1039,14 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   }
 }
 
-// Activation tiles of the kx walk: [n_tile][step][hi, lo][128][64] f16, steps kk < 4 of super-block
-// sb are values 256 sb + 64 kk .. as gemm_bfill_kernel writes them; Q4_K / Q5_K's step 4 is the min
-// step: xsum of sub-block j (xd * xs, the sum of its dequantized activation) * 2^-5 / bscale as
-// [hi x8 | lo x8 | hi x8 | 0] in the hi tile.
-__global__ void gemm_bfill_kx_kernel(const int8_t *xq, const float *xd, int64_t k, int ntok, int npad,
-                                     const float *bscale, int sps, uint8_t *bt) {
-  const int64_t groups = k / 8, total = (int64_t)npad * groups;
+// Activation tiles of the kx walk: [n_tile][step][hi, lo][rows][64] f16 (rows = 128, or the 16-row
+// rounding of the tokens when there is one short tile; btile = rows * 128 bytes), steps kk < 4 of
+// super-block sb are values 256 sb + 64 kk .. as gemm_bfill_kernel writes them; Q4_K / Q5_K's step 4
+// is the min step: xsum of sub-block j (xd * xs, the sum of its dequantized activation) * 2^-5 /
+// bscale as [hi x8 | lo x8 | hi x8 | 0] in the hi tile.  nrows tokens are filled (zeros past ntok).
+__global__ void gemm_bfill_kx_kernel(const int8_t *xq, const float *xd, int64_t k, int ntok, int nrows,
+                                     const float *bscale, int sps, int btile, uint8_t *bt) {
+  const int64_t groups = k / 8, total = (int64_t)nrows * groups;
   const int nsteps = (int)(k / 256) * sps;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int n = (int)(e / groups);
@@ -999,15 +1061,15 @@ __global__ void gemm_bfill_kx_kernel(const int8_t *xq, const float *xd, int64_t 
     }
     const int nt = n / GN, nr = n % GN, c = (int)(k0 / 64), kk = (int)(k0 % 64);
     const int step = (c >> 2) * sps + (c & 3);
-    uint8_t *base = bt + ((int64_t)nt * nsteps + step) * 2 * kTileBytes + sw128_off(nr, kk);
+    uint8_t *base = bt + ((int64_t)nt * nsteps + step) * 2 * btile + sw128_off(nr, kk);
     *reinterpret_cast<uint4 *>(base) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4 *>(base + kTileBytes) = make_uint4(l[0], l[1], l[2], l[3]);
+    *reinterpret_cast<uint4 *>(base + btile) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
-__global__ void gemm_bfill_kx_min_kernel(const float *xd, const int32_t *xs, int64_t k, int ntok, int npad,
-                                         const float *bscale, uint8_t *bt) {
+__global__ void gemm_bfill_kx_min_kernel(const float *xd, const int32_t *xs, int64_t k, int ntok, int nrows,
+                                         const float *bscale, int btile, uint8_t *bt) {
   const int nb = (int)(k / 256), nsteps = nb * 5;
-  const int64_t total = (int64_t)npad * nb * 8;         // (token, super-block, 16-byte chunk)
+  const int64_t total = (int64_t)nrows * nb * 8;        // (token, super-block, 16-byte chunk)
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int n = (int)(e / (nb * 8)), sb = (int)((e / 8) % nb), ch = (int)(e % 8);
     uint32_t hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
@@ -1025,12 +1087,11 @@ __global__ void gemm_bfill_kx_min_kernel(const float *xd, const int32_t *xs, int
       }
     }
     const int nt = n / GN, nr = n % GN;
-    uint8_t *base = bt + ((int64_t)nt * nsteps + sb * 5 + 4) * 2 * kTileBytes;
+    uint8_t *base = bt + ((int64_t)nt * nsteps + sb * 5 + 4) * 2 * btile;
     const uint4 val = ch == 0 || ch == 2 ? make_uint4(hi[0], hi[1], hi[2], hi[3])
                       : ch == 1           ? make_uint4(lo[0], lo[1], lo[2], lo[3])
                                           : make_uint4(0, 0, 0, 0);
     *reinterpret_cast<uint4 *>(base + sw128_off(nr, 8 * ch)) = val;
-    *reinterpret_cast<uint4 *>(base + kTileBytes + sw128_off(nr, 8 * ch)) = make_uint4(0, 0, 0, 0);
   }
 }
 
@@ -1209,29 +1270,60 @@ cudaError_t launch_kx_info(const DevMatrix &m, unsigned *out, cudaStream_t s) {
 
 int kx_steps(int type) { return type == T_Q6_K ? kx_steps_per_sb<T_Q6_K>() : kx_steps_per_sb<T_Q4_K>(); }
 
-size_t gemm_bx_bytes(int64_t k, int ntok, int type) {
-  const int64_t npad = gemm_tokens_pad(ntok);
-  return (size_t)(npad / GN) * (size_t)(k / 256) * kx_steps(type) * kPairBytes + (size_t)npad * 4;
+// Token tiles: 128 rows each; a single short tile keeps the 16-row rounding of its tokens.
+static int kx_tile_rows(int ntok) { return ntok < GN ? (ntok + 15) / 16 * 16 : GN; }
+static int kx_sms() {
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms[dev] = 148;
+  return sms[dev];
+}
+// Split-K, only where the output tiles alone would leave more than half of the SMs idle (a split
+// CTA pays a pipeline fill, its partial sums and a share of the reduction): as many splits as fit
+// one wave, at least 4 super-blocks each.
+int kx_splits(int64_t rows, int ntok, int64_t k) {
+  const int64_t tiles = (rows + GM - 1) / GM * (gemm_tokens_pad(ntok) / GN);
+  const int nb = (int)(k / 256), sms = kx_sms();
+  if (tiles * 2 > sms || nb < 8) return 1;
+  int sp = (int)(sms / tiles);
+  if (sp > nb / 4) sp = nb / 4;
+  const int sbps = (nb + sp - 1) / sp;
+  return (nb + sbps - 1) / sbps;
 }
 
-cudaError_t launch_gemm_prep_kx(const ActView &act, int ntok, int type, void *bbuf, cudaStream_t s) {
+// [activation tiles][bscale: npad floats][tile counters][split partials]
+static size_t kx_tiles_bytes(int64_t k, int ntok, int type) {
+  return (size_t)(gemm_tokens_pad(ntok) / GN) * (size_t)(k / 256) * kx_steps(type) * 2 * kx_tile_rows(ntok) * 128;
+}
+size_t gemm_bx_bytes(int64_t k, int ntok, int type, int64_t rows) {
+  const int64_t npad = gemm_tokens_pad(ntok), tiles = (rows + GM - 1) / GM * (npad / GN);
+  const int sp = kx_splits(rows, ntok, k);
+  size_t b = kx_tiles_bytes(k, ntok, type) + (size_t)npad * 4 + (size_t)tiles * 4;
+  b = (b + 255) / 256 * 256;
+  return sp > 1 ? b + (size_t)sp * ntok * rows * 4 : b;
+}
+
+cudaError_t launch_gemm_prep_kx(const ActView &act, int ntok, int type, int64_t rows, void *bbuf, cudaStream_t s) {
   const int64_t npad = gemm_tokens_pad(ntok), k = act.k;
-  const int sps = kx_steps(type);
+  const int sps = kx_steps(type), tr = kx_tile_rows(ntok), nrows = ntok < GN ? tr : (int)npad;
+  const int64_t tiles = (rows + GM - 1) / GM * (npad / GN);
   uint8_t *bt = reinterpret_cast<uint8_t *>(bbuf);
-  float *bscale = reinterpret_cast<float *>(bt + (npad / GN) * (k / 256) * sps * kPairBytes);
+  float *bscale = reinterpret_cast<float *>(bt + kx_tiles_bytes(k, ntok, type));
+  unsigned *cnt = reinterpret_cast<unsigned *>(bscale + npad);
   const int threads = 256;
   gemm_bscale_kernel<<<(unsigned)((npad * 32 + threads - 1) / threads), threads, 0, s>>>(act.xd, k / 32, ntok, (int)npad,
-                                                                                         bscale);
+                                                                                         bscale, cnt, (int)tiles);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  int64_t total = npad * (k / 8);
+  int64_t total = (int64_t)nrows * (k / 8);
   int64_t grid = (total + threads - 1) / threads < 148 * 16 ? (total + threads - 1) / threads : 148 * 16;
-  gemm_bfill_kx_kernel<<<(unsigned)grid, threads, 0, s>>>(act.xq, act.xd, k, ntok, (int)npad, bscale, sps, bt);
+  gemm_bfill_kx_kernel<<<(unsigned)grid, threads, 0, s>>>(act.xq, act.xd, k, ntok, nrows, bscale, sps, tr * 128, bt);
   e = cudaGetLastError();
   if (e != cudaSuccess || sps == 4) return e;
-  total = npad * (k / 256) * 8;
+  total = (int64_t)nrows * (k / 256) * 8;
   grid = (total + threads - 1) / threads < 148 * 8 ? (total + threads - 1) / threads : 148 * 8;
-  gemm_bfill_kx_min_kernel<<<(unsigned)grid, threads, 0, s>>>(act.xd, act.xs, k, ntok, (int)npad, bscale, bt);
+  gemm_bfill_kx_min_kernel<<<(unsigned)grid, threads, 0, s>>>(act.xd, act.xs, k, ntok, nrows, bscale, tr * 128, bt);
   return cudaGetLastError();
 }
 
@@ -1251,20 +1343,28 @@ static cudaError_t launch_kx_t(const GemmArgs &a, dim3 grid, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_kx(const DevMatrix &m, const void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
+cudaError_t launch_gemm_kx(const DevMatrix &m, void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
                            float mscale, unsigned *status, cudaStream_t s, bool swiglu) {
   if (!gemm_kq_supported(m) || (swiglu && (m.rows % 2 || y_add))) return cudaErrorInvalidValue;
-  const int64_t npad = gemm_tokens_pad(ntok);
+  const int64_t npad = gemm_tokens_pad(ntok), tiles = (m.rows + GM - 1) / GM * (npad / GN);
+  const int nb = (int)(m.cols / 256), sp = kx_splits(m.rows, ntok, m.cols);
+  uint8_t *base = reinterpret_cast<uint8_t *>(bbuf);
+  const size_t tb = kx_tiles_bytes(m.cols, ntok, m.type);
   GemmArgs a{};
   a.w = m.data;
-  a.b = reinterpret_cast<const uint8_t *>(bbuf);
-  a.bscale = reinterpret_cast<const float *>(a.b + (npad / GN) * (m.cols / 256) * kx_steps(m.type) * kPairBytes);
+  a.b = base;
+  a.bscale = reinterpret_cast<const float *>(base + tb);
+  a.tile_cnt = reinterpret_cast<unsigned *>(base + tb + (size_t)npad * 4);
+  a.ws = reinterpret_cast<float *>(base + (tb + (size_t)npad * 4 + (size_t)tiles * 4 + 255) / 256 * 256);
   a.y = y; a.y_add = y_add; a.y_stride = y_stride;
   // the min values carry mscale and xsum 2^-5: their accumulator comes back with 2^5 / mscale
   a.wscale = mscale; a.wscale_inv = 32.f / mscale; a.swiglu = swiglu ? 1 : 0;
-  a.rows = m.rows; a.ntok = ntok; a.nb = (int)(m.cols / 256); a.kc = (int)(m.cols / 64);
+  a.rows = m.rows; a.ntok = ntok; a.nb = nb; a.kc = (int)(m.cols / 64);
+  a.btile = kx_tile_rows(ntok) * 128;
+  a.nsplit = sp;
+  a.sbps = (nb + sp - 1) / sp;
   a.status = status;
-  const dim3 grid((unsigned)((m.rows + GM - 1) / GM), (unsigned)(npad / GN));
+  const dim3 grid((unsigned)((m.rows + GM - 1) / GM), (unsigned)(npad / GN), (unsigned)sp);
   switch (m.type) {
     case T_Q4_K: return launch_kx_t<T_Q4_K>(a, grid, s);
     case T_Q5_K: return launch_kx_t<T_Q5_K>(a, grid, s);

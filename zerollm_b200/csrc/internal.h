@@ -180,12 +180,14 @@ cudaError_t launch_gemm_kq(const DevMatrix &m, const void *bbuf, int ntok, float
 // The exact-A variant of the same GEMM (weights dequantized exactly into f16, two MMAs per slice,
 // per-super-block scaling in TMEM): launch_kx_info writes (bits of max |dmin| * 63, max |Q6_K scale|)
 // of a matrix; Q4_K / Q5_K with finite scales always qualify, Q6_K when every |scale| <= 64.  The
-// activation goes through launch_gemm_prep_kx (gemm_bx_bytes of scratch); mscale is the power of
-// two gemm_weight_scale gives for the dmin bound.
+// activation goes through launch_gemm_prep_kx (gemm_bx_bytes of scratch, which also holds the
+// split-K partial sums: kx_splits CTAs share an output tile when the tiles alone would leave SMs
+// idle); mscale is the power of two gemm_weight_scale gives for the dmin bound.
 cudaError_t launch_kx_info(const DevMatrix &m, unsigned *out, cudaStream_t s);
-size_t gemm_bx_bytes(int64_t k, int ntok, int type);
-cudaError_t launch_gemm_prep_kx(const ActView &act, int ntok, int type, void *bbuf, cudaStream_t s);
-cudaError_t launch_gemm_kx(const DevMatrix &m, const void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
+int kx_splits(int64_t rows, int ntok, int64_t k);
+size_t gemm_bx_bytes(int64_t k, int ntok, int type, int64_t rows);
+cudaError_t launch_gemm_prep_kx(const ActView &act, int ntok, int type, int64_t rows, void *bbuf, cudaStream_t s);
+cudaError_t launch_gemm_kx(const DevMatrix &m, void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
                            float mscale, unsigned *status, cudaStream_t s, bool swiglu = false);
 // Tensor-parallel collectives (tp.cu): NCCL opened at run time.  Return 0 / cudaSuccess, else set *why.
 size_t tp_unique_id_bytes();

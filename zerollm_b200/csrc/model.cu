@@ -357,7 +357,8 @@ extern "C" int zllm_model_ready(zllm_model *m) {
     size_t gb = gemm_b_bytes(KX, MB);
     for (auto &L : m->L)
       for (zllm_weight *w : {L.w[0], L.w[1], L.w[2], L.w[3], L.w[4], L.w[5], L.w[6], L.qkv, L.gu})
-        if (w && kq_type(w->m.type) && zllm_weight_gemm_ok(m->ctx, w)) gb = std::max(gb, gemm_act_bytes(w, MB));
+        if (w && kq_type(w->m.type) && zllm_weight_gemm_ok(m->ctx, w))
+          for (int n = kGemmMinTokens; n <= MB; n++) gb = std::max(gb, gemm_act_bytes(w, n));   // split-K varies with n
     CK(cudaMalloc(&m->gemm_b, gb), "GEMM activation tiles");
   }
   CK(dalloc(&m->logits, (size_t)LB * c.vocab), "logits");
