@@ -304,6 +304,9 @@ def decode_bench(n_seq: int, device: int, profile: bool = False):
 
 # ------------------------------------------------------------------------------------------ prefill GEMM (config 1)
 GEMM_TOKENS = 512
+# MMAs executed per useful MMA over the config-1 mix: 34 / 16 per Q4_K super-block (two per slice
+# plus the min step), 32 / 16 for Q6_K, weighted by the matrices' sizes
+GEMM_EXEC_FACTOR = 2.09
 GEMM_MIX = (("attn_q", "Q4_K", 4096, 4096), ("attn_k", "Q4_K", 1024, 4096), ("attn_v", "Q4_K", 1024, 4096),
             ("attn_output", "Q4_K", 4096, 4096), ("ffn_gate", "Q4_K", 12288, 4096), ("ffn_up", "Q4_K", 12288, 4096),
             ("ffn_down", "Q6_K", 4096, 12288))
@@ -370,7 +373,7 @@ def gemm_bench(device: int, reps: int = 20):
 
 def profile_run(args, device: int):
     """Plain launches without graphs or timing, for ncu: --profile-gemm (config 1's attn_q at 512
-    tokens: gemm_bscale / gemm_bfill / gemm_kq_kernel per step), --profile-batch NTOK (config 3's
+    tokens: gemm_bscale / gemm_bfill_kx / gemm_bfill_kx_min / gemm_kx_kernel per step), --profile-batch NTOK (config 3's
     interleaved gate/up, Q4_K 24576 x 4096, at NTOK tokens: kq_batch_kernel launches) or
     --profile-attn CTX NSEQ (config 2: qkv_post_kernel + attn_decode_kernel per step);
     args.warmup + args.steps steps."""
@@ -914,13 +917,15 @@ def run_ours(args, world, rank, local):
             line["prefill_gemm"] = {
                 "metric": "prefill GEMM mix TFLOP/s (config 1)", "unit": "TFLOP/s", "tokens": GEMM_TOKENS,
                 "model": "one Qwen3-8B layer: Q4_K q/k/v/o/gate/up, Q6_K down", "api": "zllm_mm (512 tokens)",
-                "kernel": "gemm_kq_kernel: tcgen05.mma kind::f16, f32 accumulation in TMEM, weights dequantized into "
-                          "f16 hi/lo tiles in shared memory, activations as f16 hi/lo tiles",
+                "kernel": "gemm_kx_kernel: tcgen05.mma kind::f16, sub-block scale x quant dequantized exactly into f16, "
+                          "activation as an f16 hi/lo pair, per-super-block TMEM buffers folded with d in f32; split-K "
+                          "for the 1024-row k/v projections",
                 "value": round(useful, 1),
                 "roofline": {"bound": "tensor", "achieved": round(useful, 1), "peak": pk, "unit": "TFLOP/s",
                              "frac": round(useful / pk, 4), "peak_source": pk_kind,
-                             "executed_tflops": round(3 * useful, 1),
-                             "note": "three MMAs (hi.hi, hi.lo, lo.hi) per useful one keep ~1e-5 of the exact result"},
+                             "executed_tflops": round(GEMM_EXEC_FACTOR * useful, 1),
+                             "note": "two MMAs (A.B_hi, A.B_lo) per useful one, plus Q4_K's min step (2 of 34 MMAs per "
+                                     "super-block): 2.09x over this mix; within 1e-6 of the exact result"},
                 "mix_us": round(us, 1), "per_matrix": parts}
         if tp:
             line["tp_decode"] = {"metric": "32B Q4_K_M tensor-parallel decode tok/s (config 4)", "unit": "tok/s",

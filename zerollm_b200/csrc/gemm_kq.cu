@@ -606,7 +606,7 @@ __global__ void kq_bound_kernel(const uint8_t *w, int64_t nunits, unsigned *out)
 // TMEM and its lane 0 issues the MMAs, warps 2..9 dequantize (each lane holds the next super-block's
 // words in registers), warps 10..13 fold the buffers and write y.  Every wait is bounded; the roles
 // off the critical path wait with suspending tries.
-constexpr int kXAStages = 4, kXBStages = 4;
+constexpr int kXAStages = 4, kXBStages = 5;
 constexpr int kXProdWarp = 0, kXMmaWarp = 1, kXDqWarp0 = 2, kXEpiWarp0 = kXDqWarp0 + kDqWarps, kXEpiWarps = 4;
 constexpr int kXThreads = (kXEpiWarp0 + kXEpiWarps) * 32;
 constexpr uint32_t kXTmemCols = 512, kXTot = 256, kXMin = 384;
@@ -847,34 +847,49 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
       const uint32_t idesc = idesc_n(nmma);
       const uint64_t adesc0 = sw128_desc(smem_u32(a_ring)), bdesc0 = sw128_desc(smem_u32(b_ring));
       int issued = 0, kk = 0, sbi = 0;
-      for (int s = 0; s < nsteps; s++) {
-        const int sa = s % AS, sbs = s % BS;
-        if (kk == 0 && sbi >= 2 && !wait1(&buf_free[sbi & 1], (uint32_t)((sbi >> 1) - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
-        if (!wait1(&full_b[sbs], (uint32_t)(s / BS) & 1u, ctl, ST_FULL_TIMEOUT) ||
-            !wait1(&full_a[sa], (uint32_t)(s / AS) & 1u, ctl, ST_FULL_TIMEOUT))
-          break;
-        fence_async_smem();
-        tc_fence_after();
-        // descriptor start addresses are in 16-byte units: a byte offset o adds o >> 4
-        const uint64_t ad = adesc0 + (uint64_t)(sa * (kTileBytes >> 4));
-        const uint64_t bh = bdesc0 + (uint64_t)(sbs * (kPairBytes >> 4)), bl = bh + (kTileBytes >> 4);
-        if (!MINS || kk < 4) {
-          const uint32_t d = tmem + (uint32_t)((sbi & 1) * GN);
-#pragma unroll
-          for (int sl = 0; sl < GK / 16; sl++) {
-            mma_f16(d, ad + 2 * sl, bh + 2 * sl, idesc, (kk | sl) != 0);
-            mma_f16(d, ad + 2 * sl, bl + 2 * sl, idesc, 1u);
-          }
-        } else {
-#pragma unroll
-          for (int sl = 0; sl < 2; sl++)             // columns 0..31 carry the min term
-            mma_f16(tmem + kXMin, ad + 2 * sl, bh + 2 * sl, idesc, (sbi | sl) != 0);
+      // two K steps per round (the dequantizing warps' pairs: 0 + 1, 2 + 3, then the min step
+      // alone): one round of waits and commits per 16 MMAs
+      for (int s = 0; s < nsteps;) {
+        const int n2 = (!MINS || kk < 4) ? 2 : 1;
+        if (kk == 0 && sbi >= 2) {
+          // the epilogue's tcgen05.ld / st of this buffer come before the MMAs that overwrite it
+          if (!wait1(&buf_free[sbi & 1], (uint32_t)((sbi >> 1) - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
+          tc_fence_after();
         }
-        mma_commit(&empty_a[sa]);
-        mma_commit(&empty_b[sbs]);
-        if (kk == 3) mma_commit(&buf_full[sbi & 1]);
-        issued++;
-        if (++kk == SPS) {
+        // the tiles' writers fenced their stores into the async proxy before arriving (dequantized
+        // tiles) or wrote them through it (bulk copies); the MMAs only read them
+        bool ok = true;
+        for (int j = 0; j < n2 && ok; j++)
+          ok = wait1(&full_b[(s + j) % BS], (uint32_t)((s + j) / BS) & 1u, ctl, ST_FULL_TIMEOUT) &&
+               wait1(&full_a[(s + j) % AS], (uint32_t)((s + j) / AS) & 1u, ctl, ST_FULL_TIMEOUT);
+        if (!ok) break;
+        for (int j = 0; j < n2; j++) {
+          const int t = s + j, sa = t % AS, sbs = t % BS, kkj = kk + j;
+          // descriptor start addresses are in 16-byte units: a byte offset o adds o >> 4
+          const uint64_t ad = adesc0 + (uint64_t)(sa * (kTileBytes >> 4));
+          const uint64_t bh = bdesc0 + (uint64_t)(sbs * (kPairBytes >> 4)), bl = bh + (kTileBytes >> 4);
+          if (!MINS || kkj < 4) {
+            const uint32_t d = tmem + (uint32_t)((sbi & 1) * GN);
+#pragma unroll
+            for (int sl = 0; sl < GK / 16; sl++) {
+              mma_f16(d, ad + 2 * sl, bh + 2 * sl, idesc, (kkj | sl) != 0);
+              mma_f16(d, ad + 2 * sl, bl + 2 * sl, idesc, 1u);
+            }
+          } else {
+#pragma unroll
+            for (int sl = 0; sl < 2; sl++)             // columns 0..31 carry the min term
+              mma_f16(tmem + kXMin, ad + 2 * sl, bh + 2 * sl, idesc, (sbi | sl) != 0);
+          }
+        }
+        for (int j = 0; j < n2; j++) {
+          mma_commit(&empty_a[(s + j) % AS]);
+          mma_commit(&empty_b[(s + j) % BS]);
+        }
+        if (kk + n2 - 1 == 3) mma_commit(&buf_full[sbi & 1]);
+        issued += n2;
+        s += n2;
+        kk += n2;
+        if (kk == SPS) {
           kk = 0;
           sbi++;
         }
@@ -897,8 +912,10 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
     DqX<FMT> cur;
     if (present && nsb > 0) nxt.load(ubase + (int64_t)(sb0 + koff_sb) * US, m, tp);
     int kk = 0, sbi = 0, snext = koff_sb + 1 < nsb ? koff_sb + 1 : 0;
-    for (int s = 0; s < nsteps; s++) {
-      const int st = s % AS;
+    // two K steps per round (chunks 0 + 1, 2 + 3, then Q4_K / Q5_K's min step alone): twice the
+    // independent work between the barrier handshakes
+    for (int s = 0; s < nsteps;) {
+      const int n2 = kk < 4 ? 2 : 1;
       if (kk == 0) {
         if (present) {
           cur.set(nxt);
@@ -906,29 +923,40 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
         }
         if (++snext == nsb) snext = 0;
       }
-      if (s >= AS && !waitw(&empty_a[st], (uint32_t)(s / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
-      uint4 out[4];
+      const int st0 = s % AS, st1 = (s + 1) % AS;
+      if (s >= AS && !waitw(&empty_a[st0], (uint32_t)(s / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
+      if (n2 == 2 && s + 1 >= AS && !waitw(&empty_a[st1], (uint32_t)((s + 1) / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
+      uint4 o0[4], o1[4];
       if (present) {
-        switch (kk) {
-          case 0: cur.template emit<0>(out); break;
-          case 1: cur.template emit<1>(out); break;
-          case 2: cur.template emit<2>(out); break;
-          case 3: cur.template emit<3>(out); break;
-          default:
-            if constexpr (MINS) cur.emit_min(tp, p.wscale, out);
-            break;
+        if (kk == 0) {
+          cur.template emit<0>(o0);
+          cur.template emit<1>(o1);
+        } else if (kk == 2) {
+          cur.template emit<2>(o0);
+          cur.template emit<3>(o1);
+        } else {
+          if constexpr (MINS) cur.emit_min(tp, p.wscale, o0);
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 4; j++) out[j] = make_uint4(0, 0, 0, 0);
+        for (int j = 0; j < 4; j++) o0[j] = o1[j] = make_uint4(0, 0, 0, 0);
       }
-      uint8_t *at = a_ring + (size_t)st * kTileBytes;
+      uint8_t *at0 = a_ring + (size_t)st0 * kTileBytes, *at1 = a_ring + (size_t)st1 * kTileBytes;
 #pragma unroll
-      for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at + aoff[j]) = out[j];
+      for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at0 + aoff[j]) = o0[j];
+      if (n2 == 2) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at1 + aoff[j]) = o1[j];
+      }
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full_a[st]);
-      if (++kk == SPS) {
+      if (lane == 0) {
+        mbar_arrive(&full_a[st0]);
+        if (n2 == 2) mbar_arrive(&full_a[st1]);
+      }
+      s += n2;
+      kk += n2;
+      if (kk == SPS) {
         kk = 0;
         sbi++;
       }

@@ -90,6 +90,18 @@ __device__ __forceinline__ bool try_wait_spin(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// test_wait: never suspends -- the cheap check when the phase has most likely completed already
+__device__ __forceinline__ bool test_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 struct Ctl {
   volatile int *abort;
   unsigned *status;
@@ -99,6 +111,7 @@ struct Ctl {
 // roles off the critical path, whose polling would take issue slots from the others.
 template <bool Sleep = false>
 __device__ __forceinline__ bool wait1(uint64_t *bar, uint32_t parity, const Ctl &c, uint32_t bit) {
+  if (test_wait(bar, parity)) return true;           // the common case: no abort check needed
   if (*c.abort) return false;
   for (int i = 0; i < (Sleep ? 1 : 64); i++)
     if (Sleep ? mbar_try_wait(bar, parity) : try_wait_spin(bar, parity)) return true;
