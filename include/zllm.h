@@ -135,7 +135,11 @@ int zllm_swiglu_quant(zllm_ctx *ctx, const float *gate, const float *up, int n, 
                       int8_t *xq, float *xd, int32_t *xs, void *stream);
 
 /* Host-buffer convenience: y_host[t][rows] = W . x_host[t][cols] (quantizing x on the device first),
- * blocking.  The CUDA counterpart of `matvec(w, new Act(x), y)` (src/compute/ref-kernels.js:127). */
+ * blocking.  The CUDA counterpart of `matvec(w, new Act(x), y)` (src/compute/ref-kernels.js:127).
+ * With pinned (page-locked) host buffers, a call repeated on the same weight and buffers is recorded
+ * once as a CUDA graph (copy in, product, copies out) and replayed: one launch and one
+ * synchronization per call.  Below the GEMM's 64 tokens only; the recording is dropped with the
+ * weight. */
 int zllm_matvec(zllm_ctx *ctx, const zllm_weight *w, const float *x_host, int ntok, float *y_host);
 
 /* ------------------------------------------------------------------------------------ attention

@@ -164,6 +164,32 @@ def test_host_entry_point_equals_device_path(ctx):
             assert np.array_equal(a, b)
 
 
+def test_host_entry_point_pinned_replay(ctx):
+    """zllm_matvec on pinned host buffers: a call repeated with the same buffers is recorded as a CUDA
+    graph and replayed.  New inputs every call, a second weight, and a larger call that regrows the
+    context's scratch in between: each result equals the device path's bits."""
+    import ctypes as C
+    from zerollm_b200.lib import check
+    rng = np.random.default_rng(21)
+    rows, cols = 512, 4096
+    w1 = Weight.from_tensor(ctx, synth.tensor(ggml.Q4_K, rows, cols, rng, "bench"))
+    w2 = Weight.from_tensor(ctx, synth.tensor(ggml.Q6_K, rows, cols, rng, "bench"))
+    big = Weight.from_tensor(ctx, synth.tensor(ggml.Q4_K, 2048, 8192, rng, "bench"))
+    xh = torch.empty(cols, dtype=torch.float32).pin_memory()
+    yh = torch.empty(rows, dtype=torch.float32).pin_memory()
+    P = lambda t: C.c_void_p(t.data_ptr())
+    for it in range(9):
+        w = w2 if it in (4, 5) else w1
+        X = rng.standard_normal(cols).astype(np.float32)
+        xh.copy_(torch.from_numpy(X))
+        check(ctx.lib.zllm_matvec(ctx.h, w.h, P(xh), 1, P(yh)), ctx.h)
+        want = matvec(w, Act(ctx, X), fused_quant=True).cpu().numpy().ravel()
+        ctx.sync()
+        assert np.array_equal(yh.numpy().view(np.uint32), want.view(np.uint32)), it
+        if it == 6:                                             # regrows the scratch slots
+            matvec_host(big, rng.standard_normal((3, 8192)).astype(np.float32))
+
+
 def test_rejects_bad_shapes(ctx):
     from zerollm_b200.lib import ZllmError
     with pytest.raises(ZllmError):

@@ -83,6 +83,8 @@ extern "C" int zllm_init(int device, zllm_ctx **out) {
   return ZLLM_OK;
 }
 
+static void mv_forget(zllm_weight *w);
+
 extern "C" void zllm_destroy(zllm_ctx *c) {
   if (!c) return;
   cudaSetDevice(c->device);
@@ -90,6 +92,7 @@ extern "C" void zllm_destroy(zllm_ctx *c) {
   // weights may outlive their context: free their device memory now and detach them, so a later
   // zllm_weight_free only releases the handle
   for (zllm_weight *w : c->weights) {
+    mv_forget(w);
     if (w->m.data && w->owns) cudaFree(w->m.data);
     w->m.data = nullptr;
     w->ctx = nullptr;
@@ -198,11 +201,20 @@ extern "C" int zllm_weight_upload(zllm_ctx *c, int type, int64_t rows, int64_t c
   return ZLLM_OK;
 }
 
+// Drop zllm_matvec's recorded call on this weight (the weight or its context is going away).
+static void mv_forget(zllm_weight *w) {
+  if (w->mv_exec) cudaGraphExecDestroy(w->mv_exec);
+  w->mv_exec = nullptr;
+  memset(w->mv_key, 0, sizeof w->mv_key);
+  memset(w->mv_seen, 0, sizeof w->mv_seen);
+}
+
 extern "C" void zllm_weight_free(zllm_weight *w) {
   if (!w) return;
   if (w->ctx) {
     cudaSetDevice(w->ctx->device);
     cudaStreamSynchronize(w->ctx->stream);
+    mv_forget(w);
     if (w->m.data && w->owns) cudaFree(w->m.data);
     w->ctx->weights.erase(w);
   }
@@ -364,17 +376,70 @@ extern "C" int zllm_matvec(zllm_ctx *c, const zllm_weight *w, const float *x_hos
   if ((rc = zllm_scratch(c, 2, sizeof(float) * (K / 32 + 1) * ntok, &xd_))) return rc;
   if ((rc = zllm_scratch(c, 3, sizeof(int32_t) * (K / 32 + 1) * ntok, &xsum_))) return rc;
   if ((rc = zllm_scratch(c, 4, sizeof(float) * R * ntok, &y_))) return rc;
-  cudaError_t e = cudaMemcpyAsync(xs_, x_host, sizeof(float) * K * ntok, cudaMemcpyHostToDevice, c->stream);
-  if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(x)");
   // one token on a k-quant: the GEMV quantizes x itself
   const bool q = type_quantized(w->m.type), fused = q && ntok == 1 && kq_type(w->m.type);
-  if (q && !fused &&
-      (rc = zllm_quantize_act(c, (const float *)xs_, K, ntok, (int8_t *)xq_, (float *)xd_, (int32_t *)xsum_, c->stream)))
+  // the whole call: x in, (quantization,) the product, y and the status word out
+  auto enqueue = [&]() -> int {
+    cudaError_t e = cudaMemcpyAsync(xs_, x_host, sizeof(float) * K * ntok, cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(x)");
+    int r;
+    if (q && !fused &&
+        (r = zllm_quantize_act(c, (const float *)xs_, K, ntok, (int8_t *)xq_, (float *)xd_, (int32_t *)xsum_, c->stream)))
+      return r;
+    if ((r = zllm_mm(c, w, fused ? nullptr : (const int8_t *)xq_, (const float *)xd_, (const int32_t *)xsum_,
+                     (const float *)xs_, ntok, (float *)y_, R, nullptr, c->stream)))
+      return r;
+    e = cudaMemcpyAsync(y_host, y_, sizeof(float) * R * ntok, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->status_host, c->status_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "cudaMemcpyAsync(y)");
+  };
+  // Below the GEMM's token count nothing in the call allocates or synchronizes, so it is recorded
+  // once as a CUDA graph and replayed: one launch and one synchronization per call.
+  // Pinned host buffers only (a pageable copy cannot be recorded), and only for a call seen twice in
+  // a row, so one-off buffers do not pay for a recording.
+  auto pinned = [](const void *p) {
+    cudaPointerAttributes at;
+    const bool ok = cudaPointerGetAttributes(&at, p) == cudaSuccess && at.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    return ok;
+  };
+  // every address the recording holds: host buffers or a scratch slot regrown (zllm_topk shares
+  // slots 0-4) record the call again
+  const void *key[9] = {w->m.data, x_host, y_host, xs_, xq_, xd_, xsum_, y_, reinterpret_cast<const void *>((intptr_t)ntok)};
+  zllm_weight *wm = const_cast<zllm_weight *>(w);
+  const bool hit = wm->mv_exec && memcmp(key, wm->mv_key, sizeof key) == 0;
+  const bool graph = hit || (!(ntok >= kGemmMinTokens && kq_type(w->m.type)) && memcmp(key, wm->mv_seen, sizeof key) == 0 &&
+                             pinned(x_host) && pinned(y_host));
+  memcpy(wm->mv_seen, key, sizeof key);
+  if (graph && !hit) {
+    if (wm->mv_exec) cudaGraphExecDestroy(wm->mv_exec);
+    wm->mv_exec = nullptr;
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return zllm_cuda_fail(c, e, "zllm_matvec: begin capture");
+    rc = enqueue();
+    e = cudaStreamEndCapture(c->stream, &g);
+    if (rc == ZLLM_OK && e != cudaSuccess) rc = zllm_cuda_fail(c, e, "zllm_matvec: end capture");
+    if (rc == ZLLM_OK) {
+      e = cudaGraphInstantiate(&wm->mv_exec, g, 0);
+      if (e != cudaSuccess) {
+        wm->mv_exec = nullptr;
+        rc = zllm_cuda_fail(c, e, "zllm_matvec: graph instantiate");
+      }
+    }
+    if (g) cudaGraphDestroy(g);
+    if (rc) return rc;
+    memcpy(wm->mv_key, key, sizeof key);
+  }
+  *c->status_host = 0;
+  if (graph) {
+    cudaError_t e = cudaGraphLaunch(wm->mv_exec, c->stream);
+    if (e != cudaSuccess) return zllm_cuda_fail(c, e, "zllm_matvec: graph launch");
+  } else if ((rc = enqueue())) {
     return rc;
-  if ((rc = zllm_mm(c, w, fused ? nullptr : (const int8_t *)xq_, (const float *)xd_, (const int32_t *)xsum_,
-                    (const float *)xs_, ntok, (float *)y_, R, nullptr, c->stream)))
-    return rc;
-  e = cudaMemcpyAsync(y_host, y_, sizeof(float) * R * ntok, cudaMemcpyDeviceToHost, c->stream);
-  if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(y)");
-  return zllm_finish(c, c->stream);             // status word read back on the stream: one synchronization
+  }
+  cudaError_t e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) return zllm_cuda_fail(c, e, "zllm_matvec: synchronize");
+  if (*c->status_host) return zllm_check_status(c);     // rare: clear the word and report, as zllm_sync does
+  return ZLLM_OK;
 }

@@ -32,6 +32,11 @@ struct zllm_weight {
   float gemm_wscale = 1.f;   // power of two applied to its dequantized values in f16
   bool gemm_kx = false;      // it takes the exact-A GEMM (launch_gemm_kx) rather than the hi / lo one
   float gemm_mscale = 1.f;   // the exact-A GEMM's power of two for the min values
+  // zllm_matvec's call on this weight recorded as a CUDA graph (copy in, GEMV, copies out), replayed
+  // while the host buffers and the context scratch it used stay the same
+  cudaGraphExec_t mv_exec = nullptr;
+  const void *mv_key[9] = {};
+  const void *mv_seen[9] = {};    // the previous call's addresses
 };
 
 // Whether the tensor-core GEMM may take this k-quant weight (computed once, synchronously).
