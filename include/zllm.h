@@ -136,10 +136,10 @@ int zllm_swiglu_quant(zllm_ctx *ctx, const float *gate, const float *up, int n, 
 
 /* Host-buffer convenience: y_host[t][rows] = W . x_host[t][cols] (quantizing x on the device first),
  * blocking.  The CUDA counterpart of `matvec(w, new Act(x), y)` (src/compute/ref-kernels.js:127).
- * With pinned (page-locked) host buffers, a call repeated on the same weight and buffers is recorded
- * once as a CUDA graph (copy in, product, copies out) and replayed: one launch and one
- * synchronization per call.  Below the GEMM's 64 tokens only; the recording is dropped with the
- * weight. */
+ * With pinned (page-locked, device-mapped) host buffers, a call repeated on the same weight and
+ * buffers is recorded once as a CUDA graph and replayed: one launch and one synchronization per call,
+ * x read and y written by the GPU through the mapped buffers.  Below the GEMM's 64 tokens only; the
+ * recording is dropped with the weight, and the buffers are re-checked on every call. */
 int zllm_matvec(zllm_ctx *ctx, const zllm_weight *w, const float *x_host, int ntok, float *y_host);
 
 /* ------------------------------------------------------------------------------------ attention

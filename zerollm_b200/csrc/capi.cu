@@ -1,4 +1,5 @@
 // extern "C" entry points of libzllm_cuda.so (declared in include/zllm.h).
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -48,6 +49,27 @@ static cudaStream_t pick(zllm_ctx *c, void *stream) { return stream ? (cudaStrea
 // Programmatic dependent launch is used on real streams only: the legacy default stream (handle 0,
 // passed through `zllm_stream`-less callers) keeps plain stream ordering.
 static bool pdl_ok(cudaStream_t s) { return s != nullptr && s != cudaStreamLegacy && s != cudaStreamPerThread; }
+
+namespace {
+// zllm_matvec's recorded call on mapped pinned buffers: the GPU fetches x itself (the product is
+// launched programmatically behind it and prefetches its weights meanwhile), and the status word is
+// stored into the mapped pinned host word once the product has finished
+__global__ void mv_fetch_kernel(const float *__restrict__ src, float *__restrict__ dst, int64_t n) {
+  zllm::pdl_launch_dependents();
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, step = (int64_t)gridDim.x * blockDim.x;
+  if (((uintptr_t)src | (uintptr_t)dst) % 16 == 0) {
+    for (int64_t i = t; i < n / 4; i += step)
+      reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(src)[i];
+    for (int64_t i = n / 4 * 4 + t; i < n; i += step) dst[i] = src[i];
+  } else {
+    for (int64_t i = t; i < n; i += step) dst[i] = src[i];
+  }
+}
+__global__ void mv_status_kernel(const unsigned *st, unsigned *out) {
+  zllm::pdl_wait();
+  *out = *reinterpret_cast<const volatile unsigned *>(st);
+}
+}  // namespace
 
 // ------------------------------------------------------------------------------------ context
 extern "C" const char *zllm_version(void) { return "zllm-b200 0.1 (sm_100a)"; }
@@ -378,40 +400,79 @@ extern "C" int zllm_matvec(zllm_ctx *c, const zllm_weight *w, const float *x_hos
   if ((rc = zllm_scratch(c, 4, sizeof(float) * R * ntok, &y_))) return rc;
   // one token on a k-quant: the GEMV quantizes x itself
   const bool q = type_quantized(w->m.type), fused = q && ntok == 1 && kq_type(w->m.type);
-  // the whole call: x in, (quantization,) the product, y and the status word out
+  // the whole call: x in, (quantization,) the product, y and the status word out; y_dev: y_host's
+  // device address when the recorded call writes it straight into the mapped pinned buffer
+  float *y_dev = nullptr;
+  const float *x_dev = nullptr;
+  unsigned *status_map = nullptr;
   auto enqueue = [&]() -> int {
-    cudaError_t e = cudaMemcpyAsync(xs_, x_host, sizeof(float) * K * ntok, cudaMemcpyHostToDevice, c->stream);
-    if (e != cudaSuccess) return zllm_cuda_fail(c, e, "cudaMemcpyAsync(x)");
+    cudaError_t e;
+    if (x_dev) {
+      const int64_t n = K * ntok;
+      mv_fetch_kernel<<<(unsigned)std::min<int64_t>((n / 4 + 255) / 256 + 1, 64), 256, 0, c->stream>>>(x_dev, (float *)xs_, n);
+      e = cudaGetLastError();
+    } else {
+      e = cudaMemcpyAsync(xs_, x_host, sizeof(float) * K * ntok, cudaMemcpyHostToDevice, c->stream);
+    }
+    if (e != cudaSuccess) return zllm_cuda_fail(c, e, "zllm_matvec: x in");
     int r;
     if (q && !fused &&
         (r = zllm_quantize_act(c, (const float *)xs_, K, ntok, (int8_t *)xq_, (float *)xd_, (int32_t *)xsum_, c->stream)))
       return r;
     if ((r = zllm_mm(c, w, fused ? nullptr : (const int8_t *)xq_, (const float *)xd_, (const int32_t *)xsum_,
-                     (const float *)xs_, ntok, (float *)y_, R, nullptr, c->stream)))
+                     (const float *)xs_, ntok, y_dev ? y_dev : (float *)y_, R, nullptr, c->stream)))
       return r;
-    e = cudaMemcpyAsync(y_host, y_, sizeof(float) * R * ntok, cudaMemcpyDeviceToHost, c->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(c->status_host, c->status_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
-    return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "cudaMemcpyAsync(y)");
+    if (!y_dev) e = cudaMemcpyAsync(y_host, y_, sizeof(float) * R * ntok, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess && status_map) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1);
+      cfg.blockDim = dim3(1);
+      cfg.stream = c->stream;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      at[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelEx(&cfg, mv_status_kernel, (const unsigned *)c->status_dev, status_map);
+    } else if (e == cudaSuccess) {
+      e = cudaMemcpyAsync(c->status_host, c->status_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    }
+    return e == cudaSuccess ? ZLLM_OK : zllm_cuda_fail(c, e, "zllm_matvec: y / status out");
   };
   // Below the GEMM's token count nothing in the call allocates or synchronizes, so it is recorded
   // once as a CUDA graph and replayed: one launch and one synchronization per call.
   // Pinned host buffers only (a pageable copy cannot be recorded), and only for a call seen twice in
   // a row, so one-off buffers do not pay for a recording.
-  auto pinned = [](const void *p) {
+  auto pinned = [](const void *p, void **dev) {
     cudaPointerAttributes at;
     const bool ok = cudaPointerGetAttributes(&at, p) == cudaSuccess && at.type == cudaMemoryTypeHost;
     cudaGetLastError();
+    if (dev) *dev = ok ? at.devicePointer : nullptr;
     return ok;
   };
   // every address the recording holds: host buffers or a scratch slot regrown (zllm_topk shares
   // slots 0-4) record the call again
-  const void *key[9] = {w->m.data, x_host, y_host, xs_, xq_, xd_, xsum_, y_, reinterpret_cast<const void *>((intptr_t)ntok)};
+  const void *key[11] = {w->m.data, x_host, y_host, xs_, xq_, xd_, xsum_, y_, reinterpret_cast<const void *>((intptr_t)ntok),
+                         nullptr, nullptr};
   zllm_weight *wm = const_cast<zllm_weight *>(w);
-  const bool hit = wm->mv_exec && memcmp(key, wm->mv_key, sizeof key) == 0;
-  const bool graph = hit || (!(ntok >= kGemmMinTokens && kq_type(w->m.type)) && memcmp(key, wm->mv_seen, sizeof key) == 0 &&
-                             pinned(x_host) && pinned(y_host));
+  // the buffers are checked on every call, replays included: a recording must never run on a
+  // buffer that was unpinned since, even at the same address
+  void *xmap = nullptr, *ymap = nullptr;
+  const bool eligible = !(ntok >= kGemmMinTokens && kq_type(w->m.type)) && pinned(x_host, &xmap) && pinned(y_host, &ymap);
+  key[9] = xmap;
+  key[10] = ymap;
+  const bool hit = eligible && wm->mv_exec && memcmp(key, wm->mv_key, sizeof key) == 0;
+  const bool graph = hit || (eligible && memcmp(key, wm->mv_seen, sizeof key) == 0);
   memcpy(wm->mv_seen, key, sizeof key);
   if (graph && !hit) {
+    // the recorded call reads x and writes y and the status word over PCIe through the mapped
+    // buffers: no copy nodes, and the product's launch overlaps the fetch of x
+    void *smap = nullptr;
+    if (xmap && ymap && pinned(c->status_host, &smap) && smap) {
+      y_dev = static_cast<float *>(ymap);
+      x_dev = static_cast<const float *>(xmap);
+      status_map = static_cast<unsigned *>(smap);
+    }
     if (wm->mv_exec) cudaGraphExecDestroy(wm->mv_exec);
     wm->mv_exec = nullptr;
     cudaGraph_t g = nullptr;

@@ -35,8 +35,8 @@ struct zllm_weight {
   // zllm_matvec's call on this weight recorded as a CUDA graph (copy in, GEMV, copies out), replayed
   // while the host buffers and the context scratch it used stay the same
   cudaGraphExec_t mv_exec = nullptr;
-  const void *mv_key[9] = {};
-  const void *mv_seen[9] = {};    // the previous call's addresses
+  const void *mv_key[11] = {};
+  const void *mv_seen[11] = {};   // the previous call's addresses
 };
 
 // Whether the tensor-core GEMM may take this k-quant weight (computed once, synchronously).
