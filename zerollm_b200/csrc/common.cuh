@@ -141,6 +141,42 @@ __device__ __forceinline__ float2 lds_f2(uint32_t a) {
   const uint2 v = lds64(a);
   return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
 }
+// ---------------------------------------------------------------------------- packed f32 pairs
+// Blackwell's f32x2 arithmetic: element x in the low word, y in the high word; each element rounds
+// exactly as the scalar instruction would.
+typedef unsigned long long f2v;
+__device__ __forceinline__ f2v f2pack(float x, float y) {
+  f2v r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ f2v f2bits(uint32_t x, uint32_t y) {
+  f2v r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(x), "r"(y));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(f2v v, float &x, float &y) { asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v)); }
+__device__ __forceinline__ f2v f2fma(f2v a, f2v b, f2v c) {
+  f2v d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f2v f2mul(f2v a, f2v b) {
+  f2v d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2v f2add(f2v a, f2v b) {
+  f2v d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2v f2sub(f2v a, f2v b) {
+  f2v d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ uint4 ldg128(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 // The same load issued where it stands in the program: a prefetch the compiler may not sink to the
 // first use of its result (volatile asm keeps its place among the other volatile statements).

@@ -583,38 +583,6 @@ __global__ void __launch_bounds__(kRingWarps * 32, 1) kq_ring_kernel(const KqArg
 // Packed pairs of f32 (Blackwell's f32x2 arithmetic): element x in the low word, y in the high word.
 // Each element is rounded exactly as the scalar instruction rounds it, so a packed term is the same
 // bits as the scalar formula (k45_pair / q6_pair) of each of its two tokens.
-typedef unsigned long long f2v;
-__device__ __forceinline__ f2v f2pack(float x, float y) {
-  f2v r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
-  return r;
-}
-__device__ __forceinline__ f2v f2bits(uint32_t x, uint32_t y) {
-  f2v r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(x), "r"(y));
-  return r;
-}
-__device__ __forceinline__ void f2unpack(f2v v, float &x, float &y) { asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(v)); }
-__device__ __forceinline__ f2v f2fma(f2v a, f2v b, f2v c) {
-  f2v d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ f2v f2mul(f2v a, f2v b) {
-  f2v d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ f2v f2add(f2v a, f2v b) {
-  f2v d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ f2v f2sub(f2v a, f2v b) {
-  f2v d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 constexpr f2v kBias2 = ((f2v)0x4B400000u << 32) | 0x4B400000u;    // (kBiasF, kBiasF)
 // two biased MMA accumulators -> their exact integer values as a pair
 __device__ __forceinline__ f2v biased_f2(int a, int b) { return f2sub(f2bits((uint32_t)a, (uint32_t)b), kBias2); }

@@ -167,6 +167,15 @@ struct KvRow {
     if constexpr (sizeof(T) == 2) return h2f((w[i >> 1] >> (16 * (i & 1))) & 0xffffu);
     else return __uint_as_float(w[i]);
   }
+  // dims 2 ip and 2 ip + 1 as a packed pair (the same values get() gives)
+  __device__ __forceinline__ f2v get2(int ip) const {
+    if constexpr (sizeof(T) == 2) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[ip]));
+      return f2pack(f.x, f.y);
+    } else {
+      return f2bits(w[2 * ip], w[2 * ip + 1]);
+    }
+  }
 };
 
 template <typename T, int HD, int G, bool PAGED>
@@ -236,13 +245,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
   }
   if (w0 < w1 && !early) load_batch(w0, kr, vr);
 
-  float q[G][DPL], acc[G][DPL];
+  // packed pairs (f32x2): the query as pairs of heads (GP of them; a lone head stays scalar), the
+  // accumulators as pairs of dims -- every element still takes the scalar code's roundings in the
+  // scalar code's order
+  constexpr int GP = G / 2, DP = DPL / 2;
+  float q[G][DPL];
+  f2v qh[GP > 0 ? GP : 1][DPL], acc[G][DP];
 #pragma unroll
   for (int g = 0; g < G; g++) {
     const float *qs = a.fused ? &sq[g][lane * DPL] : a.q + ((int64_t)b * a.n_head + kh * G + g) * HD + lane * DPL;
 #pragma unroll
-    for (int i = 0; i < DPL; i++) { q[g][i] = qs[i]; acc[g][i] = 0.f; }
+    for (int i = 0; i < DPL; i++) q[g][i] = qs[i];
+#pragma unroll
+    for (int ip = 0; ip < DP; ip++) acc[g][ip] = 0ull;
   }
+#pragma unroll
+  for (int gp = 0; gp < GP; gp++)
+#pragma unroll
+    for (int i = 0; i < DPL; i++) qh[gp][i] = f2pack(q[2 * gp][i], q[2 * gp + 1][i]);
   // running max / sum of head (lane % G), kept identically by every lane of that head
   float m_run = -INFINITY, l_run = 0.f;
   const int my_i = lane / R, my_h = my_i % G, my_p = my_i / G;
@@ -254,14 +274,25 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
     // partial scores, index j * G + g
     float v32[NI];
 #pragma unroll
-    for (int j = 0; j < NB; j++)
+    for (int j = 0; j < NB; j++) {
+      float kf[DPL];
 #pragma unroll
-      for (int g = 0; g < G; g++) {
+      for (int ip = 0; ip < DP; ip++) f2unpack(kc[j].get2(ip), kf[2 * ip], kf[2 * ip + 1]);
+      if constexpr (GP > 0) {
+#pragma unroll
+        for (int gp = 0; gp < GP; gp++) {
+          f2v d = 0ull;
+#pragma unroll
+          for (int i = 0; i < DPL; i++) d = f2fma(qh[gp][i], f2pack(kf[i], kf[i]), d);
+          f2unpack(d, v32[j * G + 2 * gp], v32[j * G + 2 * gp + 1]);
+        }
+      } else {
         float d = 0.f;
 #pragma unroll
-        for (int i = 0; i < DPL; i++) d = __fmaf_rn(q[g][i], kc[j].get(i), d);
-        v32[j * G + g] = d;
+        for (int i = 0; i < DPL; i++) d = __fmaf_rn(q[0][i], kf[i], d);
+        v32[j * G] = d;
       }
+    }
     // butterfly reduce-scatter: lane l ends with the full sum of index l / R (the R lanes of an
     // index add the same two values at each step, so they hold the same bits)
 #pragma unroll
@@ -301,19 +332,23 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
 #pragma unroll
     for (int g = 0; g < G; g++) {
       const float al = sa[warp][g];
+      const f2v al2 = f2pack(al, al);
 #pragma unroll
-      for (int i = 0; i < DPL; i++) acc[g][i] *= al;
+      for (int ip = 0; ip < DP; ip++) acc[g][ip] = f2mul(acc[g][ip], al2);
     }
 #pragma unroll
     for (int j = 0; j < NB; j++) {
-      float pj[G];
+      f2v pj[G];
 #pragma unroll
-      for (int g = 0; g < G; g++) pj[g] = sp[warp][j][g];
+      for (int g = 0; g < G; g++) {
+        const float pg = sp[warp][j][g];
+        pj[g] = f2pack(pg, pg);
+      }
 #pragma unroll
-      for (int i = 0; i < DPL; i++) {
-        const float vv = vc[j].get(i);
+      for (int ip = 0; ip < DP; ip++) {
+        const f2v vv = vc[j].get2(ip);
 #pragma unroll
-        for (int g = 0; g < G; g++) acc[g][i] = __fmaf_rn(pj[g], vv, acc[g][i]);
+        for (int g = 0; g < G; g++) acc[g][ip] = f2fma(pj[g], vv, acc[g][ip]);
       }
     }
     __syncwarp();                                      // sp / sa are rewritten by the next batch
@@ -328,7 +363,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
 #pragma unroll
   for (int g = 0; g < G; g++)
 #pragma unroll
-    for (int i = 0; i < DPL; i++) sacc[warp][g][lane * DPL + i] = acc[g][i];
+    for (int ip = 0; ip < DP; ip++) f2unpack(acc[g][ip], sacc[warp][g][lane * DPL + 2 * ip], sacc[warp][g][lane * DPL + 2 * ip + 1]);
   __syncthreads();
   const int64_t grp = (int64_t)b * a.n_kv + kh;
   float *part = a.partial + (grp * a.nsplit + split) * (size_t)(G * (HD + 2));
