@@ -67,9 +67,9 @@ def measured_tensor_peak():
     return 1590.0, "fallback (1.59 PFLOP/s burst)"
 
 
-# DRAM bytes (read + write) of one kq_stream_kernel<Q4_K> launch of this step, from the ncu capture
+# DRAM bytes (read + write) of one kq_ring_kernel<Q4_K> launch of this step, from the ncu capture
 # summarised in profiles/gemv_q4k_4096x4096.md (dram__bytes_read.sum + dram__bytes_write.sum).
-GEMV_TRAFFIC_BYTES = 9494528
+GEMV_TRAFFIC_BYTES = 9536768
 
 
 class Clocks:
@@ -896,7 +896,7 @@ def run_ours(args, world, rank, local):
                     "steps": e_steps, "api": "zllm_matvec (host buffers, pinned)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "kq_stream_kernel<Q4_K> (one token, in-kernel activation quantization)",
+                         "kernel": "kq_ring_kernel<Q4_K> (one token, in-kernel activation quantization)",
                          "kernel_us": round(ms / args.steps * 1e3, 3),
                          "prequantized_kernel_us": round(kern_ms * 1e3, 3),
                          "algorithmic_bytes_per_launch": ALGO_BYTES},
