@@ -77,9 +77,10 @@ def _filled_cache(ctx, rng, n_layer, nkv, hd, max_ctx, kv_f16, nseq):
     return cache
 
 
+# (2 KV heads or fewer take 16-warp CTAs: a tensor-parallel rank's share of a GQA model)
 CASES = [(128, 32, 8, True, (1,)), (128, 32, 8, True, (2100, 63, 64)), (128, 32, 8, False, (700,)),
          (64, 8, 8, True, (65, 300)), (64, 16, 2, True, (129,)), (128, 64, 8, True, (1500,)),
-         (128, 8, 8, False, (1, 2, 3)), (64, 4, 4, False, (257,))]
+         (128, 8, 8, False, (1, 2, 3)), (64, 4, 4, False, (257,)), (128, 8, 1, True, (580, 1, 2100, 257))]
 
 
 @pytest.mark.parametrize("hd,nh,nkv,kv_f16,npos", CASES)
@@ -107,6 +108,32 @@ def test_decode_attention_matches_oracle(ctx, hd, nh, nkv, kv_f16, npos):
             rel = np.abs(got - want).max() / max(np.abs(want).max(), 1e-30)
             assert rel <= (2e-3 if kv_f16 else 1e-3)
             assert rel <= 1e-5, (b, h, rel)
+
+
+def _one_seq_view(cache, b):
+    """The cache seen as holding sequence b alone (a view of the same rows)."""
+    import copy
+    v = copy.copy(cache)
+    v.t = cache.t[b:b + 1]
+    v.nseq = 1
+    return v
+
+
+@pytest.mark.parametrize("nh,nkv", [(32, 8), (8, 1), (16, 2)])
+def test_attention_batch_invariant(ctx, nh, nkv):
+    """A sequence's output is the same bits alone and in a batch of others (8- and 16-warp CTAs)."""
+    rng = np.random.default_rng(nh + nkv)
+    lens = (580, 33, 2100, 1)
+    cache = _filled_cache(ctx, rng, 1, nkv, 128, 2112, True, len(lens))
+    g = cache.geom(nh, eps=EPS)
+    q = torch.as_tensor(rng.standard_normal((len(lens), nh * 128)).astype(np.float32)).cuda()
+    npos = torch.as_tensor(np.array(lens, np.int32)).cuda()
+    batch = attn_decode(ctx, g, cache, 0, q, npos, max(lens)).clone()
+    for b in range(len(lens)):
+        # the same cache rows seen as a batch of one: query b, sequence b's block
+        one = attn_decode(ctx, g, _one_seq_view(cache, b), 0, q[b:b + 1].contiguous(), npos[b:b + 1], lens[b])
+        ctx.sync()
+        assert torch.equal(one[0], batch[b]), b
 
 
 def test_attention_repeated_launches_leave_counters_clean(ctx):

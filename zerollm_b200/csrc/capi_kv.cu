@@ -70,8 +70,8 @@ extern "C" int zllm_qkv_append(zllm_ctx *c, const zllm_attn_geom *g, int ntok, c
 // context splits of a decode attention launch: those of the longest sequence (attn_nsplit is
 // non-decreasing in the length)
 int zllm_attn_splits(const zllm_ctx *c, const zllm_attn_geom *g, int nseq, int max_pos) {
-  (void)c; (void)g; (void)nseq;
-  return attn_nsplit(max_pos);
+  (void)c; (void)nseq;
+  return attn_nsplit(max_pos, attn_warps(g->n_head_kv));
 }
 
 // the paging descriptor as the kernels take it; ZLLM_OK or ZLLM_E_ARG with the message set

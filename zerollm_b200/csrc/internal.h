@@ -84,26 +84,32 @@ struct QkvPostArgs {
 };
 
 // decode attention: a sequence of n positions is cut into context splits whose number and length
-// depend on n alone (so a query's partition, and its bits, do not depend on the batch around it).
-// At least kAttnMinSplit positions per split, at most kAttnSplitCap splits until the splits reach
-// kAttnMaxSplit positions: 37 splits x 8 KV heads = 296 CTAs = two per SM of the 148.  Measured on
-// B200 (config 2 and the 8B decode), 256 positions per split beat 128 (more work per warp, fewer
-// partials to merge: +30 % at 2048 x 64 sequences and 8192 x 1, +5 % at 32-sequence decode) and
-// 512 (which starves one short sequence of CTAs: -26 % at 2048 x 1).
+// depend on n and the layer's geometry alone (so a query's partition, and its bits, do not depend on
+// the batch around it).  A split is processed by attn_warps(n_kv) warps: 8, or 16 when a layer has at
+// most 2 KV heads (a tensor-parallel rank's share of a GQA model), where the few (KV head, split)
+// CTAs of a short batch would otherwise each walk long chains of positions.  At least kAttnMinSplit
+// positions per split, at most a cap of splits (37 CTAs of 8 warps per KV head: two per SM over 8 KV
+// heads; 18 of 16 warps: one per SM) until the splits reach a maximum length.  Measured on B200
+// (config 2 and the 8B decode), 256 positions per split beat 128 (more work per warp, fewer partials
+// to merge: +30 % at 2048 x 64 sequences and 8192 x 1, +5 % at 32-sequence decode) and 512 (which
+// starves one short sequence of CTAs: -26 % at 2048 x 1); 16 warps everywhere gained 23-26 % at one
+// sequence but lost 4-28 % at 64 (one CTA per SM idles at CTA boundaries), hence only for few KV heads.
 // attn_nsplit is non-decreasing in n, so a launch sized for the longest sequence fits every other.
-constexpr int kAttnWarps = 8, kAttnMinSplit = 256, kAttnMaxSplit = 1024, kAttnSplitCap = 37;
-__host__ __device__ inline int attn_nsplit(int n) {
+constexpr int kAttnMinSplit = 256;
+__host__ __device__ constexpr int attn_warps(int n_kv) { return n_kv <= 2 ? 16 : 8; }
+__host__ __device__ inline int attn_nsplit(int n, int warps) {
+  const int cap = warps == 16 ? 18 : 37, max_len = warps == 16 ? 2048 : 1024;
   int ns = (n + kAttnMinSplit - 1) / kAttnMinSplit;
-  if (ns > kAttnSplitCap) ns = kAttnSplitCap;
-  const int big = (n + kAttnMaxSplit - 1) / kAttnMaxSplit;
+  if (ns > cap) ns = cap;
+  const int big = (n + max_len - 1) / max_len;
   if (ns < big) ns = big;
   return ns < 1 ? 1 : ns;
 }
-// positions per warp of a split (the split is kAttnWarps times that)
-__host__ __device__ inline int attn_warp_len(int n) {
-  const int ns = attn_nsplit(n);
+// positions per warp of a split (the split is `warps` times that)
+__host__ __device__ inline int attn_warp_len(int n, int warps) {
+  const int ns = attn_nsplit(n, warps);
   const int per = (n + ns - 1) / ns;
-  return (per + kAttnWarps - 1) / kAttnWarps;
+  return (per + warps - 1) / warps;
 }
 
 struct AttnArgs {

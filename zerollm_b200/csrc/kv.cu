@@ -132,9 +132,10 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t s, bool pdl) {
 }
 
 // ============================================================================ decode attention
-// CTA = 8 warps, one (sequence, KV head, context split); the splits of a sequence of n positions
-// are attn_nsplit(n) runs of 8 x attn_warp_len(n) positions, and each warp streams its own
-// attn_warp_len(n) positions with no CTA barrier until the end.  Lane l holds dims
+// CTA = W warps (attn_warps(n_kv): 8, or 16 with at most 2 KV heads), one (sequence, KV head,
+// context split); the splits of a sequence of n positions are attn_nsplit(n, W) runs of
+// W x attn_warp_len(n, W) positions, and each warp streams its own
+// attn_warp_len(n, W) positions with no CTA barrier until the end.  Lane l holds dims
 // [l*DPL, (l+1)*DPL) of the G query heads and of their output accumulators.  Positions go in
 // batches of NB: K and V rows are read straight from HBM (coalesced, the next batch in flight
 // while the current one is used); a batch's NI = NB x G partial dot products are added across the
@@ -178,8 +179,9 @@ struct KvRow {
   }
 };
 
-template <typename T, int HD, int G, bool PAGED>
-__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const AttnArgs a) {
+template <typename T, int HD, int G, bool PAGED, int W>
+__global__ void __launch_bounds__(W * 32, 16 / W) attn_decode_kernel(const AttnArgs a) {
+  constexpr int kAttnWarps = W;
   constexpr int DPL = HD / 32;
   // batch: 32 / G positions, fewer where K and V of two batches would not fit in registers
   constexpr int NBMAX = 16 / KvRow<T, HD>::WORDS;
@@ -188,7 +190,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
   __shared__ float sp[kAttnWarps][NB][G];               // a batch's probabilities
   __shared__ float sa[kAttnWarps][G];                   // a batch's rescale factors
   __shared__ float sm[kAttnWarps][G], sl[kAttnWarps][G];
-  __shared__ float sacc[kAttnWarps][G][HD];
+  extern __shared__ __align__(16) float attn_dyn[];
+  float(*sacc)[G][HD] = reinterpret_cast<float(*)[G][HD]>(attn_dyn);   // [W][G][HD], dynamic
   __shared__ float sq[G][HD];                           // fused: this KV head's roped queries
   __shared__ int last_flag;
 
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const A
   // the partition depends on the sequence's own length only, so a query gets the same bits alone
   // or in any batch
   const int npos = a.npos[b];
-  const int ppw = attn_warp_len(npos), slen = ppw * kAttnWarps;
+  const int ppw = attn_warp_len(npos, W), slen = ppw * kAttnWarps;
   const int active = npos > 0 ? (npos + slen - 1) / slen : 1;
   if (split >= active) return;                        // nothing of this sequence here (no partial, no count)
   const int t0 = min(npos, split * slen), t1 = min(npos, t0 + slen);
@@ -444,18 +447,30 @@ cudaError_t launch_kv_block_copy(void *dst, int64_t dst_row, int64_t dst_blk, co
   return cudaGetLastError();
 }
 
+// dynamic shared memory of a launch: the warps' accumulators [warps][group][head_dim] f32 (the
+// larger warp count's)
 size_t attn_smem_bytes(int head_dim, int group, bool f16) {
-  (void)head_dim; (void)group; (void)f16;
-  return 0;                                           // static shared memory only
+  (void)f16;
+  return (size_t)16 * group * head_dim * sizeof(float);
 }
 
-template <typename T, int HD, int G>
-static cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s, bool pdl) {
-  auto kern = a.pages.table ? attn_decode_kernel<T, HD, G, true> : attn_decode_kernel<T, HD, G, false>;
-  const size_t smem = 0;
+template <typename T, int HD, int G, int W>
+static cudaError_t launch_attn_w(const AttnArgs &a, cudaStream_t s, bool pdl) {
+  auto kern = a.pages.table ? attn_decode_kernel<T, HD, G, true, W> : attn_decode_kernel<T, HD, G, false, W>;
+  const size_t smem = (size_t)W * G * HD * sizeof(float);
+  // above 48 KB of dynamic shared memory a kernel must be granted it (once per kernel and device)
+  static bool granted[2][64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  bool &gr = granted[a.pages.table ? 1 : 0][dev];
+  if (!gr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    gr = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nsplit, a.n_kv, a.nseq);
-  cfg.blockDim = dim3(kAttnWarps * 32);
+  cfg.blockDim = dim3(W * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -464,6 +479,11 @@ static cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s, bool pdl) {
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <typename T, int HD, int G>
+static cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s, bool pdl) {
+  return attn_warps(a.n_kv) == 16 ? launch_attn_w<T, HD, G, 16>(a, s, pdl) : launch_attn_w<T, HD, G, 8>(a, s, pdl);
 }
 
 template <typename T, int HD>
