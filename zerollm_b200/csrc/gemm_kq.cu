@@ -606,7 +606,11 @@ __global__ void kq_bound_kernel(const uint8_t *w, int64_t nunits, unsigned *out)
 // TMEM and its lane 0 issues the MMAs, warps 2..9 dequantize (each lane holds the next super-block's
 // words in registers), warps 10..13 fold the buffers and write y.  Every wait is bounded; the roles
 // off the critical path wait with suspending tries.
-constexpr int kXAStages = 4, kXBStages = 5;
+// One ring depth for the dequantized and the activation tiles: stage i of both is filled and
+// released together, so a stage has one "full" barrier (the bulk copy's bytes and the 8
+// dequantizing warps' arrivals) and one "empty" barrier (one MMA commit) -- a single check and a
+// single commit per K step on the MMA lane, whose barrier operations are the pipeline's bottleneck.
+constexpr int kXAStages = 4, kXBStages = kXAStages;
 constexpr int kXProdWarp = 0, kXMmaWarp = 1, kXDqWarp0 = 2, kXEpiWarp0 = kXDqWarp0 + kDqWarps, kXEpiWarps = 4;
 constexpr int kXThreads = (kXEpiWarp0 + kXEpiWarps) * 32;
 constexpr uint32_t kXTmemCols = 512, kXTot = 256, kXMin = 384;
@@ -776,8 +780,8 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t *a_ring = smem, *b_ring = smem + AS * kTileBytes;
   uint64_t *bars = reinterpret_cast<uint64_t *>(b_ring + BS * kPairBytes);
-  uint64_t *full_a = bars, *empty_a = bars + AS, *full_b = bars + 2 * AS, *empty_b = full_b + BS;
-  uint64_t *buf_full = empty_b + BS, *buf_free = buf_full + 2, *acc_full = buf_free + 2;
+  uint64_t *full_a = bars, *empty_a = bars + AS, *full_b = full_a, *empty_b = empty_a;   // shared by both rings
+  uint64_t *buf_full = bars + 2 * AS + 2 * BS, *buf_free = buf_full + 2, *acc_full = buf_free + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile int *last_flag = reinterpret_cast<volatile int *>(tmem_slot + 2);
@@ -798,8 +802,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   const int nmma = (ntok_tile + 15) / 16 * 16;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < AS; s++) { mbar_init(&full_a[s], kDqWarps); mbar_init(&empty_a[s], 1); }
-    for (int s = 0; s < BS; s++) { mbar_init(&full_b[s], 1); mbar_init(&empty_b[s], 1); }
+    for (int s = 0; s < AS; s++) { mbar_init(&full_a[s], kDqWarps + 1); mbar_init(&empty_a[s], 1); }
     for (int b = 0; b < 2; b++) { mbar_init(&buf_full[b], 1); mbar_init(&buf_free[b], kXEpiWarps); }
     mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -860,8 +863,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
         // tiles) or wrote them through it (bulk copies); the MMAs only read them
         bool ok = true;
         for (int j = 0; j < n2 && ok; j++)
-          ok = wait1(&full_b[(s + j) % BS], (uint32_t)((s + j) / BS) & 1u, ctl, ST_FULL_TIMEOUT) &&
-               wait1(&full_a[(s + j) % AS], (uint32_t)((s + j) / AS) & 1u, ctl, ST_FULL_TIMEOUT);
+          ok = wait1(&full_a[(s + j) % AS], (uint32_t)((s + j) / AS) & 1u, ctl, ST_FULL_TIMEOUT);
         if (!ok) break;
         for (int j = 0; j < n2; j++) {
           const int t = s + j, sa = t % AS, sbs = t % BS, kkj = kk + j;
@@ -883,7 +885,6 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
         }
         for (int j = 0; j < n2; j++) {
           mma_commit(&empty_a[(s + j) % AS]);
-          mma_commit(&empty_b[(s + j) % BS]);
         }
         if (kk + n2 - 1 == 3) mma_commit(&buf_full[sbi & 1]);
         issued += n2;
