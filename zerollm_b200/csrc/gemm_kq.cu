@@ -606,11 +606,12 @@ __global__ void kq_bound_kernel(const uint8_t *w, int64_t nunits, unsigned *out)
 // TMEM and its lane 0 issues the MMAs, warps 2..9 dequantize (each lane holds the next super-block's
 // words in registers), warps 10..13 fold the buffers and write y.  Every wait is bounded; the roles
 // off the critical path wait with suspending tries.
-// One ring depth for the dequantized and the activation tiles: stage i of both is filled and
-// released together, so a stage has one "full" barrier (the bulk copy's bytes and the 8
-// dequantizing warps' arrivals) and one "empty" barrier (one MMA commit) -- a single check and a
-// single commit per K step on the MMA lane, whose barrier operations are the pipeline's bottleneck.
-constexpr int kXAStages = 4, kXBStages = kXAStages;
+// The rings move in rounds: a round is two K steps (chunks 0 + 1, 2 + 3; Q4_K / Q5_K's min step
+// alone), and a stage holds a round's dequantized tiles and activation tiles (two slots each).  A
+// stage has one "full" barrier (the round's bulk-copy bytes and the 8 dequantizing warps' arrivals)
+// and one "empty" barrier (one MMA commit): one check and one commit per 16 MMAs on the MMA lane,
+// whose barrier operations bound the pipeline.  kXRounds stages of 2 slots.
+constexpr int kXRounds = 2, kXAStages = 2 * kXRounds, kXBStages = kXAStages;
 constexpr int kXProdWarp = 0, kXMmaWarp = 1, kXDqWarp0 = 2, kXEpiWarp0 = kXDqWarp0 + kDqWarps, kXEpiWarps = 4;
 constexpr int kXThreads = (kXEpiWarp0 + kXEpiWarps) * 32;
 constexpr uint32_t kXTmemCols = 512, kXTot = 256, kXMin = 384;
@@ -780,7 +781,8 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t *a_ring = smem, *b_ring = smem + AS * kTileBytes;
   uint64_t *bars = reinterpret_cast<uint64_t *>(b_ring + BS * kPairBytes);
-  uint64_t *full_a = bars, *empty_a = bars + AS, *full_b = full_a, *empty_b = empty_a;   // shared by both rings
+  constexpr int RS = kXRounds;
+  uint64_t *full_r = bars, *empty_r = bars + RS;                                    // per round stage
   uint64_t *buf_full = bars + 2 * AS + 2 * BS, *buf_free = buf_full + 2, *acc_full = buf_free + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -802,7 +804,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   const int nmma = (ntok_tile + 15) / 16 * 16;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < AS; s++) { mbar_init(&full_a[s], kDqWarps + 1); mbar_init(&empty_a[s], 1); }
+    for (int s = 0; s < RS; s++) { mbar_init(&full_r[s], kDqWarps + 1); mbar_init(&empty_r[s], 1); }
     for (int b = 0; b < 2; b++) { mbar_init(&buf_full[b], 1); mbar_init(&buf_free[b], kXEpiWarps); }
     mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -815,45 +817,50 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == kXProdWarp) {
-    // ---- activation producer: one lane, one bulk copy per step (the min step: its hi tile alone);
-    // step s of the walk is step (sb + koff) * SPS + kk of the tiles
+    // ---- activation producer: one lane, one bulk copy per step (the min step: its hi tile alone),
+    // a round's copies into its stage's two slots; step s of the walk is step (sb + koff) * SPS + kk
+    // of the tiles
     if (lane == 0) {
       const uint32_t part = (uint32_t)nmma * 128;      // the first nmma rows of a tile
-      int kk = 0, sbl = koff_sb, issued = 0;
-      for (int s = 0; s < nsteps; s++) {
-        const int st = s % BS;
-        if (s >= BS && !wait1(&empty_b[st], (uint32_t)(s / BS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
-        const uint8_t *src = p.b + ((int64_t)n_tile * nsteps_all + (int64_t)(sb0 + sbl) * SPS + kk) * 2 * p.btile;
-        uint8_t *dst = b_ring + (size_t)st * kPairBytes;
-        const bool hi_only = MINS && kk == 4;
-        mbar_arrive_expect_tx(&full_b[st], hi_only ? part : 2 * part);
-        if (!hi_only && part == (uint32_t)kTileBytes) {
-          bulk_g2s(dst, src, 2 * kTileBytes, &full_b[st]);
-        } else {
-          bulk_g2s(dst, src, part, &full_b[st]);
-          if (!hi_only) bulk_g2s(dst + kTileBytes, src + p.btile, part, &full_b[st]);
+      int kk = 0, sbl = koff_sb, r = 0;
+      for (int s = 0; s < nsteps; r++) {
+        const int n2 = (!MINS || kk < 4) ? 2 : 1, st = r % RS;
+        if (r >= RS && !wait1(&empty_r[st], (uint32_t)(r / RS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
+        uint32_t bytes = 0;
+        for (int j = 0; j < n2; j++) bytes += MINS && kk + j == 4 ? part : 2 * part;
+        mbar_arrive_expect_tx(&full_r[st], bytes);
+        for (int j = 0; j < n2; j++) {
+          const uint8_t *src = p.b + ((int64_t)n_tile * nsteps_all + (int64_t)(sb0 + sbl) * SPS + kk + j) * 2 * p.btile;
+          uint8_t *dst = b_ring + (size_t)(st * 2 + j) * kPairBytes;
+          const bool hi_only = MINS && kk + j == 4;
+          if (!hi_only && part == (uint32_t)kTileBytes) {
+            bulk_g2s(dst, src, 2 * kTileBytes, &full_r[st]);
+          } else {
+            bulk_g2s(dst, src, part, &full_r[st]);
+            if (!hi_only) bulk_g2s(dst + kTileBytes, src + p.btile, part, &full_r[st]);
+          }
         }
-        issued++;
-        if (++kk == SPS) {
+        s += n2;
+        kk += n2;
+        if (kk == SPS) {
           kk = 0;
           if (++sbl == nsb) sbl = 0;
         }
       }
       // copies still landing in shared memory (an abort) are waited for before the CTA exits
       const uint64_t deadline = globaltimer_ns() + WAIT_DEADLINE_NS;
-      for (int s = issued > BS ? issued - BS : 0; s < issued; s++)
-        if (!mbar_wait_bounded(&full_b[s % BS], (uint32_t)(s / BS) & 1u, deadline)) atomicOr(p.status, ST_DRAIN_TIMEOUT);
+      for (int q = r > RS ? r - RS : 0; q < r; q++)
+        if (!mbar_wait_bounded(&full_r[q % RS], (uint32_t)(q / RS) & 1u, deadline)) atomicOr(p.status, ST_DRAIN_TIMEOUT);
     }
   } else if (warp == kXMmaWarp) {
     // ---- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_n(nmma);
       const uint64_t adesc0 = sw128_desc(smem_u32(a_ring)), bdesc0 = sw128_desc(smem_u32(b_ring));
-      int issued = 0, kk = 0, sbi = 0;
-      // two K steps per round (the dequantizing warps' pairs: 0 + 1, 2 + 3, then the min step
-      // alone): one round of waits and commits per 16 MMAs
-      for (int s = 0; s < nsteps;) {
-        const int n2 = (!MINS || kk < 4) ? 2 : 1;
+      int issued = 0, kk = 0, sbi = 0, r = 0;
+      // a round: one check of its stage, its 16 (min step: 2) MMAs, one commit
+      for (int s = 0; s < nsteps; r++) {
+        const int n2 = (!MINS || kk < 4) ? 2 : 1, st = r % RS;
         if (kk == 0 && sbi >= 2) {
           // the epilogue's tcgen05.ld / st of this buffer come before the MMAs that overwrite it
           if (!wait1(&buf_free[sbi & 1], (uint32_t)((sbi >> 1) - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
@@ -861,15 +868,12 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
         }
         // the tiles' writers fenced their stores into the async proxy before arriving (dequantized
         // tiles) or wrote them through it (bulk copies); the MMAs only read them
-        bool ok = true;
-        for (int j = 0; j < n2 && ok; j++)
-          ok = wait1(&full_a[(s + j) % AS], (uint32_t)((s + j) / AS) & 1u, ctl, ST_FULL_TIMEOUT);
-        if (!ok) break;
+        if (!wait1(&full_r[st], (uint32_t)(r / RS) & 1u, ctl, ST_FULL_TIMEOUT)) break;
         for (int j = 0; j < n2; j++) {
-          const int t = s + j, sa = t % AS, sbs = t % BS, kkj = kk + j;
+          const int slot = st * 2 + j, kkj = kk + j;
           // descriptor start addresses are in 16-byte units: a byte offset o adds o >> 4
-          const uint64_t ad = adesc0 + (uint64_t)(sa * (kTileBytes >> 4));
-          const uint64_t bh = bdesc0 + (uint64_t)(sbs * (kPairBytes >> 4)), bl = bh + (kTileBytes >> 4);
+          const uint64_t ad = adesc0 + (uint64_t)(slot * (kTileBytes >> 4));
+          const uint64_t bh = bdesc0 + (uint64_t)(slot * (kPairBytes >> 4)), bl = bh + (kTileBytes >> 4);
           if (!MINS || kkj < 4) {
             const uint32_t d = tmem + (uint32_t)((sbi & 1) * GN);
 #pragma unroll
@@ -883,9 +887,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
               mma_f16(tmem + kXMin, ad + 2 * sl, bh + 2 * sl, idesc, (sbi | sl) != 0);
           }
         }
-        for (int j = 0; j < n2; j++) {
-          mma_commit(&empty_a[(s + j) % AS]);
-        }
+        mma_commit(&empty_r[st]);
         if (kk + n2 - 1 == 3) mma_commit(&buf_full[sbi & 1]);
         issued += n2;
         s += n2;
@@ -915,8 +917,8 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
     int kk = 0, sbi = 0, snext = koff_sb + 1 < nsb ? koff_sb + 1 : 0;
     // two K steps per round (chunks 0 + 1, 2 + 3, then Q4_K / Q5_K's min step alone): twice the
     // independent work between the barrier handshakes
-    for (int s = 0; s < nsteps;) {
-      const int n2 = kk < 4 ? 2 : 1;
+    for (int s = 0, r = 0; s < nsteps; r++) {
+      const int n2 = kk < 4 ? 2 : 1, st = r % RS;
       if (kk == 0) {
         if (present) {
           cur.set(nxt);
@@ -924,9 +926,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
         }
         if (++snext == nsb) snext = 0;
       }
-      const int st0 = s % AS, st1 = (s + 1) % AS;
-      if (s >= AS && !waitw(&empty_a[st0], (uint32_t)(s / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
-      if (n2 == 2 && s + 1 >= AS && !waitw(&empty_a[st1], (uint32_t)((s + 1) / AS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
+      if (r >= RS && !waitw(&empty_r[st], (uint32_t)(r / RS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT, lane)) break;
       uint4 o0[4], o1[4];
       if (present) {
         if (kk == 0) {
@@ -942,7 +942,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
 #pragma unroll
         for (int j = 0; j < 4; j++) o0[j] = o1[j] = make_uint4(0, 0, 0, 0);
       }
-      uint8_t *at0 = a_ring + (size_t)st0 * kTileBytes, *at1 = a_ring + (size_t)st1 * kTileBytes;
+      uint8_t *at0 = a_ring + (size_t)(st * 2) * kTileBytes, *at1 = at0 + kTileBytes;
 #pragma unroll
       for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at0 + aoff[j]) = o0[j];
       if (n2 == 2) {
@@ -951,10 +951,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
       }
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&full_a[st0]);
-        if (n2 == 2) mbar_arrive(&full_a[st1]);
-      }
+      if (lane == 0) mbar_arrive(&full_r[st]);
       s += n2;
       kk += n2;
       if (kk == SPS) {
