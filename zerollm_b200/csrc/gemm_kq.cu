@@ -606,18 +606,22 @@ __global__ void kq_bound_kernel(const uint8_t *w, int64_t nunits, unsigned *out)
 // TMEM and its lane 0 issues the MMAs, warps 2..9 dequantize (each lane holds the next super-block's
 // words in registers), warps 10..13 fold the buffers and write y.  Every wait is bounded; the roles
 // off the critical path wait with suspending tries.
-// The rings move in rounds: a round is two K steps (chunks 0 + 1, 2 + 3; Q4_K / Q5_K's min step
-// alone), and a stage holds a round's dequantized tiles and activation tiles (two slots each).  A
-// stage has one "full" barrier (the round's bulk-copy bytes and the 8 dequantizing warps' arrivals)
-// and one "empty" barrier (one MMA commit): one check and one commit per 16 MMAs on the MMA lane,
-// whose barrier operations bound the pipeline.  kXRounds stages of 2 slots.
+// The rings move in rounds: a super-block is two rounds, chunks 0 + 1 and chunks 2 + 3 (with Q4_K /
+// Q5_K's min step as a third step of the second round), and a stage holds a round's dequantized and
+// activation tiles.  A stage has one "full" barrier (the round's bulk-copy bytes and the 8
+// dequantizing warps' arrivals) and one "empty" barrier (one MMA commit): one check and one commit
+// per round on the MMA lane, whose barrier operations bound the pipeline.  Two stages, so the first
+// round of every super-block uses stage 0 (2 slots) and the second stage 1 (2 slots and the min
+// step's: a third dequantized tile and one activation hi tile).
 constexpr int kXRounds = 2, kXAStages = 2 * kXRounds, kXBStages = kXAStages;
+constexpr int kXASlots = kXAStages + 1;                        // + the min step's dequantized tile
+constexpr size_t kXBRing = (size_t)kXBStages * kPairBytes + kTileBytes;   // + its activation hi tile
 constexpr int kXProdWarp = 0, kXMmaWarp = 1, kXDqWarp0 = 2, kXEpiWarp0 = kXDqWarp0 + kDqWarps, kXEpiWarps = 4;
 constexpr int kXThreads = (kXEpiWarp0 + kXEpiWarps) * 32;
 constexpr uint32_t kXTmemCols = 512, kXTot = 256, kXMin = 384;
 template <int FMT> constexpr int kx_steps_per_sb() { return FMT == T_Q6_K ? 4 : 5; }
 constexpr size_t kx_smem_bytes() {
-  return 1024 + (size_t)kXAStages * kTileBytes + (size_t)kXBStages * kPairBytes + (2 * kXAStages + 2 * kXBStages + 5) * 8 + 16;
+  return 1024 + (size_t)kXASlots * kTileBytes + kXBRing + (2 * kXAStages + 2 * kXBStages + 5) * 8 + 16;
 }
 static_assert(kx_smem_bytes() <= 232448, "shared memory");
 
@@ -779,9 +783,13 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   constexpr bool MINS = FMT != T_Q6_K;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t *a_ring = smem, *b_ring = smem + AS * kTileBytes;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(b_ring + BS * kPairBytes);
+  uint8_t *a_ring = smem, *b_ring = smem + kXASlots * kTileBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(b_ring + kXBRing);
   constexpr int RS = kXRounds;
+  // steps in the round that starts at step kk of a super-block (0: chunks 0, 1; 2: chunks 2, 3 and,
+  // with MINS, the min step); the min step's tiles are dequantized slot AS and the hi tile after the
+  // BS activation pairs
+  auto round_steps = [](int kk) { return kk == 0 ? 2 : (MINS ? 3 : 2); };
   uint64_t *full_r = bars, *empty_r = bars + RS;                                    // per round stage
   uint64_t *buf_full = bars + 2 * AS + 2 * BS, *buf_free = buf_full + 2, *acc_full = buf_free + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
@@ -818,21 +826,21 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
 
   if (warp == kXProdWarp) {
     // ---- activation producer: one lane, one bulk copy per step (the min step: its hi tile alone),
-    // a round's copies into its stage's two slots; step s of the walk is step (sb + koff) * SPS + kk
+    // a round's copies into its stage's slots (the min step's into the hi tile after them); step s of the walk is step (sb + koff) * SPS + kk
     // of the tiles
     if (lane == 0) {
       const uint32_t part = (uint32_t)nmma * 128;      // the first nmma rows of a tile
       int kk = 0, sbl = koff_sb, r = 0;
       for (int s = 0; s < nsteps; r++) {
-        const int n2 = (!MINS || kk < 4) ? 2 : 1, st = r % RS;
+        const int n2 = round_steps(kk), st = r % RS;
         if (r >= RS && !wait1(&empty_r[st], (uint32_t)(r / RS - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
         uint32_t bytes = 0;
         for (int j = 0; j < n2; j++) bytes += MINS && kk + j == 4 ? part : 2 * part;
         mbar_arrive_expect_tx(&full_r[st], bytes);
         for (int j = 0; j < n2; j++) {
           const uint8_t *src = p.b + ((int64_t)n_tile * nsteps_all + (int64_t)(sb0 + sbl) * SPS + kk + j) * 2 * p.btile;
-          uint8_t *dst = b_ring + (size_t)(st * 2 + j) * kPairBytes;
           const bool hi_only = MINS && kk + j == 4;
+          uint8_t *dst = hi_only ? b_ring + (size_t)BS * kPairBytes : b_ring + (size_t)(st * 2 + j) * kPairBytes;
           if (!hi_only && part == (uint32_t)kTileBytes) {
             bulk_g2s(dst, src, 2 * kTileBytes, &full_r[st]);
           } else {
@@ -858,9 +866,9 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
       const uint32_t idesc = idesc_n(nmma);
       const uint64_t adesc0 = sw128_desc(smem_u32(a_ring)), bdesc0 = sw128_desc(smem_u32(b_ring));
       int issued = 0, kk = 0, sbi = 0, r = 0;
-      // a round: one check of its stage, its 16 (min step: 2) MMAs, one commit
+      // a round: one check of its stage, its 16 MMAs (+ 2 for a min step), one commit
       for (int s = 0; s < nsteps; r++) {
-        const int n2 = (!MINS || kk < 4) ? 2 : 1, st = r % RS;
+        const int n2 = round_steps(kk), st = r % RS;
         if (kk == 0 && sbi >= 2) {
           // the epilogue's tcgen05.ld / st of this buffer come before the MMAs that overwrite it
           if (!wait1(&buf_free[sbi & 1], (uint32_t)((sbi >> 1) - 1) & 1u, ctl, ST_EMPTY_TIMEOUT)) break;
@@ -870,8 +878,9 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
         // tiles) or wrote them through it (bulk copies); the MMAs only read them
         if (!wait1(&full_r[st], (uint32_t)(r / RS) & 1u, ctl, ST_FULL_TIMEOUT)) break;
         for (int j = 0; j < n2; j++) {
-          const int slot = st * 2 + j, kkj = kk + j;
-          // descriptor start addresses are in 16-byte units: a byte offset o adds o >> 4
+          const int kkj = kk + j, slot = MINS && kkj == 4 ? AS : st * 2 + j;
+          // descriptor start addresses are in 16-byte units: a byte offset o adds o >> 4 (the min
+          // step's activation hi tile follows the BS pairs)
           const uint64_t ad = adesc0 + (uint64_t)(slot * (kTileBytes >> 4));
           const uint64_t bh = bdesc0 + (uint64_t)(slot * (kPairBytes >> 4)), bl = bh + (kTileBytes >> 4);
           if (!MINS || kkj < 4) {
@@ -888,7 +897,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
           }
         }
         mma_commit(&empty_r[st]);
-        if (kk + n2 - 1 == 3) mma_commit(&buf_full[sbi & 1]);
+        if (kk <= 3 && kk + n2 - 1 >= 3) mma_commit(&buf_full[sbi & 1]);
         issued += n2;
         s += n2;
         kk += n2;
@@ -915,10 +924,10 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
     DqX<FMT> cur;
     if (present && nsb > 0) nxt.load(ubase + (int64_t)(sb0 + koff_sb) * US, m, tp);
     int kk = 0, sbi = 0, snext = koff_sb + 1 < nsb ? koff_sb + 1 : 0;
-    // two K steps per round (chunks 0 + 1, 2 + 3, then Q4_K / Q5_K's min step alone): twice the
-    // independent work between the barrier handshakes
+    // two K steps per round (chunks 0 + 1, then 2 + 3 with Q4_K / Q5_K's min step): two or three
+    // tiles of independent work between the barrier handshakes
     for (int s = 0, r = 0; s < nsteps; r++) {
-      const int n2 = kk < 4 ? 2 : 1, st = r % RS;
+      const int n2 = round_steps(kk), st = r % RS;
       if (kk == 0) {
         if (present) {
           cur.set(nxt);
@@ -932,11 +941,9 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
         if (kk == 0) {
           cur.template emit<0>(o0);
           cur.template emit<1>(o1);
-        } else if (kk == 2) {
+        } else {
           cur.template emit<2>(o0);
           cur.template emit<3>(o1);
-        } else {
-          if constexpr (MINS) cur.emit_min(tp, p.wscale, o0);
         }
       } else {
 #pragma unroll
@@ -945,9 +952,18 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
       uint8_t *at0 = a_ring + (size_t)(st * 2) * kTileBytes, *at1 = at0 + kTileBytes;
 #pragma unroll
       for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at0 + aoff[j]) = o0[j];
-      if (n2 == 2) {
 #pragma unroll
-        for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at1 + aoff[j]) = o1[j];
+      for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at1 + aoff[j]) = o1[j];
+      if (n2 == 3) {                               // the min step: dequantized slot AS
+        if constexpr (MINS) {
+          if (present) cur.emit_min(tp, p.wscale, o0);
+          else
+#pragma unroll
+            for (int j = 0; j < 4; j++) o0[j] = make_uint4(0, 0, 0, 0);
+          uint8_t *at2 = a_ring + (size_t)AS * kTileBytes;
+#pragma unroll
+          for (int j = 0; j < 4; j++) *reinterpret_cast<uint4 *>(at2 + aoff[j]) = o0[j];
+        }
       }
       fence_async_smem();
       __syncwarp();
