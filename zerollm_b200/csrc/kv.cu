@@ -179,6 +179,66 @@ struct KvRow {
   }
 };
 
+// The end of a decode-attention CTA, after its warps stored their running max / sum (sm, sl) and
+// accumulators (sacc(w): warp w's [G][HD] f32) and the CTA synchronised: the W warps merged in warp
+// order, then the output (one split) or this split's partial, which the last CTA of the (sequence,
+// KV head) merges in split order.
+template <int G, int HD, int W, typename Sacc>
+__device__ __forceinline__ void attn_finish(const AttnArgs &a, const float (*sm)[G], const float (*sl)[G], Sacc sacc,
+                                            int active, int split, int b, int kh, int &last_flag) {
+  const int64_t grp = (int64_t)b * a.n_kv + kh;
+  float *part = a.partial + (grp * a.nsplit + split) * (size_t)(G * (HD + 2));
+  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+    const int g = e / HD, d = e % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < W; w++) M = fmaxf(M, sm[w][g]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; w++) {
+      if (sm[w][g] == -INFINITY) continue;
+      const float f = expf(sm[w][g] - M);
+      L = __fmaf_rn(sl[w][g], f, L);
+      O = __fmaf_rn(sacc(w)[g * HD + d], f, O);
+    }
+    if (active == 1) {
+      a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
+    } else {
+      part[2 * G + e] = O;
+      if (d == 0) { part[g] = M; part[G + g] = L; }
+    }
+  }
+  if (active == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int done = atomicAdd(a.counters + grp, 1);
+    last_flag = done == active - 1;
+  }
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+  // merge the active splits in split order (deterministic)
+  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+    const int g = e / HD;
+    float M = -INFINITY;
+#pragma unroll 8
+    for (int j = 0; j < active; j++) M = fmaxf(M, __ldcg(a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2)) + g));
+    float L = 0.f, O = 0.f;
+#pragma unroll 8
+    for (int j = 0; j < active; j++) {
+      const float *pj = a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2));
+      const float mj = __ldcg(pj + g);
+      if (mj == -INFINITY) continue;
+      const float f = expf(mj - M);
+      L = __fmaf_rn(__ldcg(pj + G + g), f, L);
+      O = __fmaf_rn(__ldcg(pj + 2 * G + e), f, O);
+    }
+    a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
+  }
+  if (threadIdx.x == 0) a.counters[grp] = 0;            // ready for the next launch
+}
+
 template <typename T, int HD, int G, bool PAGED, int W>
 __global__ void __launch_bounds__(W * 32, 16 / W) attn_decode_kernel(const AttnArgs a) {
   constexpr int kAttnWarps = W;
@@ -368,57 +428,202 @@ __global__ void __launch_bounds__(W * 32, 16 / W) attn_decode_kernel(const AttnA
 #pragma unroll
     for (int ip = 0; ip < DP; ip++) f2unpack(acc[g][ip], sacc[warp][g][lane * DPL + 2 * ip], sacc[warp][g][lane * DPL + 2 * ip + 1]);
   __syncthreads();
-  const int64_t grp = (int64_t)b * a.n_kv + kh;
-  float *part = a.partial + (grp * a.nsplit + split) * (size_t)(G * (HD + 2));
-  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
-    const int g = e / HD, d = e % HD;
-    float M = -INFINITY;
+  attn_finish<G, HD, W>(a, sm, sl, [&](int w) { return &sacc[w][0][0]; }, active, split, b, kh, last_flag);
+}
+
+// ============================================================================ decode attention on the tensor cores (f16 KV)
+// The same grid, context partition, fused prologue and merges as attn_decode_kernel, for f16
+// caches.  A warp streams its positions in chunks of 16 K and V rows through its own shared-memory
+// stage (16-byte cp.async, each row's 16-byte pieces XOR-swizzled by row so ldmatrix is free of bank
+// conflicts; the next chunk's K rows load during this chunk's softmax and P.V, its V rows during the
+// next chunk's Q.K) and does both products with mma.sync m16n8k16 (f16 operands, f32 accumulators):
+//   S^T (16 positions x 8 heads) = K (16 x HD) . Q^T       Q as an f16 pair hi + lo: two MMAs per step
+//   O^T (HD x 8 heads)          += V^T (HD x 16) . P^T      P = exp(S - max) as an f16 pair hi + lo
+// K and V are f16 already, every f16 x f16 product is exact in f32, and the pairs carry q and p to
+// ~22 bits, so the result stays within ~1e-6 of the CUDA-core kernel's f32 arithmetic (the f16-KV
+// contract is 2e-3).  The online softmax per head is the same running-max form (per chunk of 16
+// positions).  P goes from the score layout (positions x heads) to the operand layout (heads x
+// positions) in registers with movmatrix.  Heads beyond G are zero queries and never stored.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+               "{%0, %1, %2, %3};"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+// (x0, x1) as f16 hi and lo pairs: hi = f16(x), lo = f16(x - hi), element 0 in the low half
+__device__ __forceinline__ void f16_pair(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
+  hi = *reinterpret_cast<const uint32_t *>(&h);
+  lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+constexpr int kAttnChunk = 16;
+template <int HD> constexpr int attn_stage_bytes() { return 2 * kAttnChunk * HD * 2; }   // K then V rows
+
+template <int HD, int G, bool PAGED, int W>
+__global__ void __launch_bounds__(W * 32, 16 / W) attn_mma_kernel(const AttnArgs a) {
+  constexpr int ROWB = HD * 2, CH = ROWB / 16, KS = HD / 16, STAGE = attn_stage_bytes<HD>();
+  constexpr int PIECES = kAttnChunk * CH / 32;          // 16-byte pieces per lane per tensor
+  static_assert(G <= 8 && G * HD * 4 <= STAGE, "a warp's accumulators fit its stage");
+  extern __shared__ __align__(128) uint8_t attn_stage[];  // [W][STAGE]; after the loop warp w's [G][HD] f32
+  __shared__ float sm[W][G], sl[W][G];
+  __shared__ float sq[G][HD];                           // fused: this KV head's roped queries
+  __shared__ float srow[HD];                            // fused: the appended key row's staging
+  __shared__ int last_flag;
+
+  pdl_launch_dependents();
+  if (!a.fused) pdl_wait();                           // unfused: every input may be the previous kernel's
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  const int npos = a.npos[b];
+  const int ppw = attn_warp_len(npos, W), slen = ppw * W;
+  const int active = npos > 0 ? (npos + slen - 1) / slen : 1;
+  if (split >= active) return;                        // nothing of this sequence here (no partial, no count)
+  const int t0 = min(npos, split * slen), t1 = min(npos, t0 + slen);
+  const int w0 = min(t1, t0 + warp * ppw), w1 = min(t1, w0 + ppw);
+  const int64_t cs = a.seq ? a.seq[b] : b;
+  const uint16_t *kpool = reinterpret_cast<const uint16_t *>(a.kcache), *vpool = reinterpret_cast<const uint16_t *>(a.vcache);
+  const int64_t cbase = PAGED ? 0 : cs * a.seq_stride + (int64_t)kh * a.head_stride;
+  auto row = [&](int p) -> int64_t {
+    if constexpr (PAGED) return kv_page_row(a.pages, b, a.n_kv, kh, p, HD, a.status);
+    else return cbase + (int64_t)p * HD;
+  };
+  const int newp = a.fused ? npos - 1 : -1;
+  uint8_t *stage = attn_stage + (size_t)warp * STAGE;
+  const uint32_t kst = smem_u32(stage), vst = kst + kAttnChunk * ROWB;
+  // one commit group: the 16 K (or V) rows from position p0 (past w1: the last row again, masked)
+  auto issue = [&](const uint16_t *pool, uint32_t dst0, int p0) {
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm[w][g]);
-    float L = 0.f, O = 0.f;
+    for (int k = 0; k < PIECES; k++) {
+      const int q = lane + 32 * k, r = q / CH, c = q % CH;
+      const int64_t o = row(min(p0 + r, w1 - 1));
+      cp_async16(dst0 + r * ROWB + ((c ^ (r & 7)) << 4), pool + o + c * 8);
+    }
+    cp_async_commit();
+  };
+  const bool early = a.fused && !(w0 <= newp && newp < w0 + kAttnChunk);
+  if (w0 < w1 && early) { issue(kpool, kst, w0); issue(vpool, vst, w0); }
+  if (a.fused) pdl_wait();                            // q / k / v come from the previous kernel
+  if (a.fused) {
+    const int nh = G + (split == active - 1 ? 1 : 0);
+    for (int hh = warp; hh < nh; hh += W)
+      post_head(a.post, b, hh < G ? kh * G + hh : a.n_head + kh, hh < G ? &sq[hh][0] : srow, nullptr, lane);
+    __threadfence();                                  // the appended row reaches L2 before any cp.async reads it
+    __syncthreads();
+  }
+  if (w0 < w1 && !early) { issue(kpool, kst, w0); issue(vpool, vst, w0); }
+
+  // Q^T as B operands: step j, lane (g, t): head g, dims 16 j + 2 t (+1) and 16 j + 2 t + 8 (+9)
+  uint32_t qh[KS][2], ql[KS][2];
+  {
+    const float *qs = a.fused ? &sq[g < G ? g : 0][0] : a.q + ((int64_t)b * a.n_head + kh * G + (g < G ? g : 0)) * HD;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; w++) {
-      if (sm[w][g] == -INFINITY) continue;
-      const float f = expf(sm[w][g] - M);
-      L = __fmaf_rn(sl[w][g], f, L);
-      O = __fmaf_rn(sacc[w][g][d], f, O);
-    }
-    if (active == 1) {
-      a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
-    } else {
-      part[2 * G + e] = O;
-      if (d == 0) { part[g] = M; part[G + g] = L; }
-    }
+    for (int j = 0; j < KS; j++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int d = 16 * j + 2 * t + 8 * e;
+        const float x0 = g < G ? qs[d] : 0.f, x1 = g < G ? qs[d + 1] : 0.f;
+        f16_pair(x0, x1, qh[j][e], ql[j][e]);
+      }
   }
-  if (active == 1) return;
-  __threadfence();
+  // running max / sum of heads 2t and 2t + 1, and O^T: m-tile i, lane (g, t) holds dims 16 i + g
+  // (c0: head 2t, c1: 2t + 1) and 16 i + g + 8 (c2, c3)
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float acc[KS][4];
+#pragma unroll
+  for (int i = 0; i < KS; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  const int lq = lane >> 3, lr = lane & 7;            // ldmatrix: this lane's matrix and row in it
+  for (int p0 = w0; p0 < w1; p0 += kAttnChunk) {
+    const bool more = p0 + kAttnChunk < w1;
+    cp_async_wait<1>();                               // this chunk's K rows (its V rows may still load)
+    __syncwarp();
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < KS; j++) {
+      uint32_t ka[4];
+      const int r = (lq & 1) * 8 + lr, c = 2 * j + (lq >> 1);
+      ldsm_x4(kst + r * ROWB + ((c ^ (r & 7)) << 4), ka);
+      mma_16816(sc, ka, qh[j][0], qh[j][1]);
+      mma_16816(sc, ka, ql[j][0], ql[j][1]);
+    }
+    __syncwarp();                                     // every lane's K reads are done
+    if (more) issue(kpool, kst, p0 + kAttnChunk); else cp_async_commit();
+    // online softmax over the chunk: rows g (position p0 + g) and g + 8
+    const bool v0 = p0 + g < w1, v1 = p0 + g + 8 < w1;
+    const float x0 = v0 ? sc[0] * a.scale : -INFINITY, x1 = v0 ? sc[1] * a.scale : -INFINITY;
+    const float x2 = v1 ? sc[2] * a.scale : -INFINITY, x3 = v1 ? sc[3] * a.scale : -INFINITY;
+    float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float al0 = m0 == -INFINITY ? 0.f : expf(m0 - mn0), al1 = m1 == -INFINITY ? 0.f : expf(m1 - mn1);
+    const float p_0 = v0 ? expf(x0 - mn0) : 0.f, p_1 = v0 ? expf(x1 - mn1) : 0.f;
+    const float p_2 = v1 ? expf(x2 - mn0) : 0.f, p_3 = v1 ? expf(x3 - mn1) : 0.f;
+    float ps0 = p_0 + p_2, ps1 = p_1 + p_3;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      ps0 += __shfl_xor_sync(0xffffffffu, ps0, o);
+      ps1 += __shfl_xor_sync(0xffffffffu, ps1, o);
+    }
+    l0 = __fmaf_rn(l0, al0, ps0);
+    l1 = __fmaf_rn(l1, al1, ps1);
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int i = 0; i < KS; i++) {
+      acc[i][0] *= al0; acc[i][1] *= al1; acc[i][2] *= al0; acc[i][3] *= al1;
+    }
+    // P^T operands: rows g / g + 8 of the score layout, transposed
+    uint32_t h01, l01, h23, l23;
+    f16_pair(p_0, p_1, h01, l01);
+    f16_pair(p_2, p_3, h23, l23);
+    const uint32_t bh0 = movm_t(h01), bh1 = movm_t(h23), bl0 = movm_t(l01), bl1 = movm_t(l23);
+    cp_async_wait<1>();                               // this chunk's V rows
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < KS; i++) {
+      uint32_t va[4];
+      const int r = (lq >> 1) * 8 + lr, c = 2 * i + (lq & 1);
+      ldsm_x4_t(vst + r * ROWB + ((c ^ (r & 7)) << 4), va);
+      mma_16816(acc[i], va, bh0, bh1);
+      mma_16816(acc[i], va, bl0, bl1);
+    }
+    __syncwarp();                                     // every lane's V reads are done
+    if (more) issue(vpool, vst, p0 + kAttnChunk); else cp_async_commit();
+  }
+  cp_async_wait<0>();
+  __syncwarp();
+  // this warp's state into its own stage (no other warp reads a stage) and the CTA's max / sum table
+  float *sw = reinterpret_cast<float *>(stage);
+#pragma unroll
+  for (int i = 0; i < KS; i++) {
+    if (2 * t < G) { sw[(2 * t) * HD + 16 * i + g] = acc[i][0]; sw[(2 * t) * HD + 16 * i + g + 8] = acc[i][2]; }
+    if (2 * t + 1 < G) { sw[(2 * t + 1) * HD + 16 * i + g] = acc[i][1]; sw[(2 * t + 1) * HD + 16 * i + g + 8] = acc[i][3]; }
+  }
+  if (g == 0) {
+    if (2 * t < G) { sm[warp][2 * t] = m0; sl[warp][2 * t] = l0; }
+    if (2 * t + 1 < G) { sm[warp][2 * t + 1] = m1; sl[warp][2 * t + 1] = l1; }
+  }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int done = atomicAdd(a.counters + grp, 1);
-    last_flag = done == active - 1;
-  }
-  __syncthreads();
-  if (!last_flag) return;
-  __threadfence();
-  // merge the active splits in split order (deterministic)
-  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
-    const int g = e / HD;
-    float M = -INFINITY;
-#pragma unroll 8
-    for (int j = 0; j < active; j++) M = fmaxf(M, __ldcg(a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2)) + g));
-    float L = 0.f, O = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < active; j++) {
-      const float *pj = a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2));
-      const float mj = __ldcg(pj + g);
-      if (mj == -INFINITY) continue;
-      const float f = expf(mj - M);
-      L = __fmaf_rn(__ldcg(pj + G + g), f, L);
-      O = __fmaf_rn(__ldcg(pj + 2 * G + e), f, O);
-    }
-    a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
-  }
-  if (threadIdx.x == 0) a.counters[grp] = 0;            // ready for the next launch
+  attn_finish<G, HD, W>(a, sm, sl, [&](int w) { return reinterpret_cast<const float *>(attn_stage + (size_t)w * STAGE); },
+                        active, split, b, kh, last_flag);
 }
 
 // ============================================================================ KV block copy
@@ -456,8 +661,10 @@ size_t attn_smem_bytes(int head_dim, int group, bool f16) {
 
 template <typename T, int HD, int G, int W>
 static cudaError_t launch_attn_w(const AttnArgs &a, cudaStream_t s, bool pdl) {
-  auto kern = a.pages.table ? attn_decode_kernel<T, HD, G, true, W> : attn_decode_kernel<T, HD, G, false, W>;
-  const size_t smem = (size_t)W * G * HD * sizeof(float);
+  constexpr bool MMA = sizeof(T) == 2;                // f16 caches: the tensor-core kernel
+  auto kern = MMA ? (a.pages.table ? attn_mma_kernel<HD, G, true, W> : attn_mma_kernel<HD, G, false, W>)
+                  : (a.pages.table ? attn_decode_kernel<T, HD, G, true, W> : attn_decode_kernel<T, HD, G, false, W>);
+  const size_t smem = MMA ? (size_t)W * attn_stage_bytes<HD>() : (size_t)W * G * HD * sizeof(float);
   // above 48 KB of dynamic shared memory a kernel must be granted it (once per kernel and device)
   static bool granted[2][64] = {};
   int dev = 0;
