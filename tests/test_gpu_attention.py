@@ -110,6 +110,31 @@ def test_decode_attention_matches_oracle(ctx, hd, nh, nkv, kv_f16, npos):
             assert rel <= 1e-5, (b, h, rel)
 
 
+@pytest.mark.parametrize("nkv,npos", [(8, 60000), (2, 140000)])
+def test_decode_attention_many_splits(ctx, nkv, npos):
+    """Contexts long enough for more than 64 context splits (the last CTA then merges the splits one
+    at a time) next to one just below (eight loads in flight per element): both against the oracle,
+    within 5e-5 of the largest output (f32 sums over 60k-140k positions in a different order than
+    the oracle's; the f16-KV contract is 2e-3)."""
+    hd, group = 64, 2
+    nh = nkv * group
+    rng = np.random.default_rng(npos)
+    cache = _filled_cache(ctx, rng, 1, nkv, hd, npos, True, 1)
+    g = cache.geom(nh, eps=EPS)
+    q = (rng.standard_normal((1, nh * hd)) * 2).astype(np.float32)
+    out = attn_decode(ctx, g, cache, 0, torch.as_tensor(q).cuda(), torch.as_tensor(np.array([npos], np.int32)).cuda(),
+                      npos)
+    ctx.sync()
+    out = out.cpu().numpy()
+    host = cache.t.cpu().numpy()
+    for h in range(nh):
+        kh = h // group
+        want = O.attn_head(q[0, h * hd:(h + 1) * hd], host[0, 0, 0, kh, :npos].view(np.uint16),
+                           host[0, 0, 1, kh, :npos].view(np.uint16), True)
+        got = out[0, h * hd:(h + 1) * hd]
+        assert np.abs(got - want).max() / max(np.abs(want).max(), 1e-30) <= 5e-5, h
+
+
 def _one_seq_view(cache, b):
     """The cache seen as holding sequence b alone (a view of the same rows)."""
     import copy

@@ -218,23 +218,78 @@ __device__ __forceinline__ void attn_finish(const AttnArgs &a, const float (*sm)
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
-  // merge the active splits in split order (deterministic)
-  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
-    const int g = e / HD;
-    float M = -INFINITY;
-#pragma unroll 8
-    for (int j = 0; j < active; j++) M = fmaxf(M, __ldcg(a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2)) + g));
-    float L = 0.f, O = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < active; j++) {
-      const float *pj = a.partial + (grp * a.nsplit + j) * (size_t)(G * (HD + 2));
-      const float mj = __ldcg(pj + g);
-      if (mj == -INFINITY) continue;
-      const float f = expf(mj - M);
-      L = __fmaf_rn(__ldcg(pj + G + g), f, L);
-      O = __fmaf_rn(__ldcg(pj + 2 * G + e), f, O);
+  // merge the active splits in split order (deterministic).  Up to kMergeFast splits: first warp
+  // g (< G <= W) finds head g's maximum M, every split's factor exp(m_j - M) (0 for a split without
+  // a finite maximum, which then adds nothing) and the sum L; then every element adds its splits'
+  // accumulators in split order with eight loads in flight at a time (a load-compare-load chain per
+  // split measured ~15 us at 37 splits).  More splits (contexts beyond ~64k positions) take the
+  // same arithmetic one split at a time.
+  constexpr int kMergeFast = 64;
+  constexpr size_t PS = (size_t)G * (HD + 2);
+  const float *pbase = a.partial + grp * a.nsplit * PS;
+  __shared__ float sf[G][kMergeFast];
+  __shared__ float sL[G];
+  if (active <= kMergeFast) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < G) {
+      const int g = warp;
+      float M = -INFINITY;
+      for (int j = lane; j < active; j += 32) M = fmaxf(M, __ldcg(pbase + j * PS + g));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      for (int j = lane; j < active; j += 32) {
+        const float mj = __ldcg(pbase + j * PS + g);
+        sf[g][j] = mj == -INFINITY ? 0.f : expf(mj - M);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        float L = 0.f;
+        for (int j0 = 0; j0 < active; j0 += 8) {
+          float l[8];
+#pragma unroll
+          for (int k = 0; k < 8; k++) l[k] = j0 + k < active ? __ldcg(pbase + (j0 + k) * PS + G + g) : 0.f;
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const float f = j0 + k < active ? sf[g][j0 + k] : 0.f;
+            if (f != 0.f) L = __fmaf_rn(l[k], f, L);
+          }
+        }
+        sL[g] = L;
+      }
     }
-    a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
+    __syncthreads();
+    for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+      const int g = e / HD;
+      float O = 0.f;
+      for (int j0 = 0; j0 < active; j0 += 8) {
+        float o[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) o[k] = j0 + k < active ? __ldcg(pbase + (j0 + k) * PS + 2 * G + e) : 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          const float f = j0 + k < active ? sf[g][j0 + k] : 0.f;
+          if (f != 0.f) O = __fmaf_rn(o[k], f, O);
+        }
+      }
+      const float L = sL[g];
+      a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
+    }
+  } else {
+    for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+      const int g = e / HD;
+      float M = -INFINITY;
+      for (int j = 0; j < active; j++) M = fmaxf(M, __ldcg(pbase + j * PS + g));
+      float L = 0.f, O = 0.f;
+      for (int j = 0; j < active; j++) {
+        const float *pj = pbase + j * PS;
+        const float mj = __ldcg(pj + g);
+        if (mj == -INFINITY) continue;
+        const float f = expf(mj - M);
+        L = __fmaf_rn(__ldcg(pj + G + g), f, L);
+        O = __fmaf_rn(__ldcg(pj + 2 * G + e), f, O);
+      }
+      a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
+    }
   }
   if (threadIdx.x == 0) a.counters[grp] = 0;            // ready for the next launch
 }
