@@ -218,12 +218,14 @@ __device__ __forceinline__ void attn_finish(const AttnArgs &a, const float (*sm)
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
-  // merge the active splits in split order (deterministic).  Up to kMergeFast splits: first warp
-  // g (< G <= W) finds head g's maximum M, every split's factor exp(m_j - M) (0 for a split without
-  // a finite maximum, which then adds nothing) and the sum L; then every element adds its splits'
-  // accumulators in split order with eight loads in flight at a time (a load-compare-load chain per
-  // split measured ~15 us at 37 splits).  More splits (contexts beyond ~64k positions) take the
-  // same arithmetic one split at a time.
+  // merge the active splits in split order (deterministic).  Up to kMergeFast splits: warp g
+  // (< G <= W) reads every split's maximum and sum of head g at once (lane l: splits l, l + 32),
+  // finds the maximum M, the factors exp(m_j - M) (0 for a split without a finite maximum, which
+  // then adds nothing) and L = sum of l_j f_j (a fixed butterfly); then each thread adds its
+  // elements' accumulators over the splits in split order, up to 32 loads in flight.  (Rounds of
+  // dependent L2 reads are what this costs: a load-compare-load chain per split measured ~15 us at
+  // 37 splits.)  More splits (contexts beyond ~64k positions) take the same arithmetic one split at
+  // a time.
   constexpr int kMergeFast = 64;
   constexpr size_t PS = (size_t)G * (HD + 2);
   const float *pbase = a.partial + grp * a.nsplit * PS;
@@ -233,46 +235,52 @@ __device__ __forceinline__ void attn_finish(const AttnArgs &a, const float (*sm)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < G) {
       const int g = warp;
-      float M = -INFINITY;
-      for (int j = lane; j < active; j += 32) M = fmaxf(M, __ldcg(pbase + j * PS + g));
+      const bool ha = lane < active, hb = lane + 32 < active;
+      const float ma = ha ? __ldcg(pbase + lane * PS + g) : -INFINITY, la = ha ? __ldcg(pbase + lane * PS + G + g) : 0.f;
+      const float mb = hb ? __ldcg(pbase + (lane + 32) * PS + g) : -INFINITY;
+      const float lb = hb ? __ldcg(pbase + (lane + 32) * PS + G + g) : 0.f;
+      float M = fmaxf(ma, mb);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      for (int j = lane; j < active; j += 32) {
-        const float mj = __ldcg(pbase + j * PS + g);
-        sf[g][j] = mj == -INFINITY ? 0.f : expf(mj - M);
-      }
-      __syncwarp();
-      if (lane == 0) {
-        float L = 0.f;
-        for (int j0 = 0; j0 < active; j0 += 8) {
-          float l[8];
+      const float fa = ma == -INFINITY ? 0.f : expf(ma - M), fb = mb == -INFINITY ? 0.f : expf(mb - M);
+      if (ha) sf[g][lane] = fa;
+      if (hb) sf[g][lane + 32] = fb;
+      float L = (fa != 0.f ? la * fa : 0.f) + (fb != 0.f ? lb * fb : 0.f);
 #pragma unroll
-          for (int k = 0; k < 8; k++) l[k] = j0 + k < active ? __ldcg(pbase + (j0 + k) * PS + G + g) : 0.f;
-#pragma unroll
-          for (int k = 0; k < 8; k++) {
-            const float f = j0 + k < active ? sf[g][j0 + k] : 0.f;
-            if (f != 0.f) L = __fmaf_rn(l[k], f, L);
-          }
-        }
-        sL[g] = L;
-      }
+      for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+      if (lane == 0) sL[g] = L;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
-      const int g = e / HD;
-      float O = 0.f;
-      for (int j0 = 0; j0 < active; j0 += 8) {
-        float o[8];
+    constexpr int NT = W * 32, EPT = (G * HD + NT - 1) / NT, RND = EPT >= 4 ? 8 : 32 / EPT;
+    float O[EPT];
 #pragma unroll
-        for (int k = 0; k < 8; k++) o[k] = j0 + k < active ? __ldcg(pbase + (j0 + k) * PS + 2 * G + e) : 0.f;
+    for (int k = 0; k < EPT; k++) O[k] = 0.f;
+    for (int j0 = 0; j0 < active; j0 += RND) {
+      float o[EPT][RND];
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-          const float f = j0 + k < active ? sf[g][j0 + k] : 0.f;
-          if (f != 0.f) O = __fmaf_rn(o[k], f, O);
+      for (int k = 0; k < EPT; k++) {
+        const int e = threadIdx.x + k * NT;
+#pragma unroll
+        for (int jj = 0; jj < RND; jj++)
+          o[k][jj] = e < G * HD && j0 + jj < active ? __ldcg(pbase + (j0 + jj) * PS + 2 * G + e) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < EPT; k++) {
+        const int e = threadIdx.x + k * NT, g = (e < G * HD ? e : 0) / HD;
+#pragma unroll
+        for (int jj = 0; jj < RND; jj++) {
+          const float f = j0 + jj < active ? sf[g][j0 + jj] : 0.f;
+          if (f != 0.f) O[k] = __fmaf_rn(o[k][jj], f, O[k]);
         }
       }
-      const float L = sL[g];
-      a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O / L : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < EPT; k++) {
+      const int e = threadIdx.x + k * NT;
+      if (e < G * HD) {
+        const float L = sL[e / HD];
+        a.out[((int64_t)b * a.n_head + kh * G) * HD + e] = L > 0.f ? O[k] / L : 0.f;
+      }
     }
   } else {
     for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
@@ -570,21 +578,11 @@ __global__ void __launch_bounds__(W * 32, 16 / W) attn_mma_kernel(const AttnArgs
     }
     cp_async_commit();
   };
-  const bool early = a.fused && !(w0 <= newp && newp < w0 + kAttnChunk);
-  if (w0 < w1 && early) { issue(kpool, kst, w0); issue(vpool, vst, w0); }
-  if (a.fused) pdl_wait();                            // q / k / v come from the previous kernel
-  if (a.fused) {
-    const int nh = G + (split == active - 1 ? 1 : 0);
-    for (int hh = warp; hh < nh; hh += W)
-      post_head(a.post, b, hh < G ? kh * G + hh : a.n_head + kh, hh < G ? &sq[hh][0] : srow, nullptr, lane);
-    __threadfence();                                  // the appended row reaches L2 before any cp.async reads it
-    __syncthreads();
-  }
-  if (w0 < w1 && !early) { issue(kpool, kst, w0); issue(vpool, vst, w0); }
-
-  // Q^T as B operands: step j, lane (g, t): head g, dims 16 j + 2 t (+1) and 16 j + 2 t + 8 (+9)
+  // Q^T as B operands: step j, lane (g, t): head g, dims 16 j + 2 t (+1) and 16 j + 2 t + 8 (+9).
+  // Unfused, the query is read before the first copies are issued: loads issued behind a warp's
+  // burst of cp.async wait for it to drain (measured ~4 us at 32k positions x 1 sequence).
   uint32_t qh[KS][2], ql[KS][2];
-  {
+  auto load_q = [&]() {
     const float *qs = a.fused ? &sq[g < G ? g : 0][0] : a.q + ((int64_t)b * a.n_head + kh * G + (g < G ? g : 0)) * HD;
 #pragma unroll
     for (int j = 0; j < KS; j++)
@@ -594,6 +592,19 @@ __global__ void __launch_bounds__(W * 32, 16 / W) attn_mma_kernel(const AttnArgs
         const float x0 = g < G ? qs[d] : 0.f, x1 = g < G ? qs[d + 1] : 0.f;
         f16_pair(x0, x1, qh[j][e], ql[j][e]);
       }
+  };
+  const bool early = a.fused && !(w0 <= newp && newp < w0 + kAttnChunk);
+  if (!a.fused) load_q();
+  if (w0 < w1 && (early || !a.fused)) { issue(kpool, kst, w0); issue(vpool, vst, w0); }
+  if (a.fused) {
+    pdl_wait();                                       // q / k / v come from the previous kernel
+    const int nh = G + (split == active - 1 ? 1 : 0);
+    for (int hh = warp; hh < nh; hh += W)
+      post_head(a.post, b, hh < G ? kh * G + hh : a.n_head + kh, hh < G ? &sq[hh][0] : srow, nullptr, lane);
+    __threadfence();                                  // the appended row reaches L2 before any cp.async reads it
+    __syncthreads();
+    if (w0 < w1 && !early) { issue(kpool, kst, w0); issue(vpool, vst, w0); }
+    load_q();
   }
   // running max / sum of heads 2t and 2t + 1, and O^T: m-tile i, lane (g, t) holds dims 16 i + g
   // (c0: head 2t, c1: 2t + 1) and 16 i + g + 8 (c2, c3)
@@ -717,8 +728,9 @@ size_t attn_smem_bytes(int head_dim, int group, bool f16) {
 template <typename T, int HD, int G, int W>
 static cudaError_t launch_attn_w(const AttnArgs &a, cudaStream_t s, bool pdl) {
   constexpr bool MMA = sizeof(T) == 2;                // f16 caches: the tensor-core kernel
-  auto kern = MMA ? (a.pages.table ? attn_mma_kernel<HD, G, true, W> : attn_mma_kernel<HD, G, false, W>)
-                  : (a.pages.table ? attn_decode_kernel<T, HD, G, true, W> : attn_decode_kernel<T, HD, G, false, W>);
+  void (*kern)(AttnArgs);
+  if constexpr (MMA) kern = a.pages.table ? attn_mma_kernel<HD, G, true, W> : attn_mma_kernel<HD, G, false, W>;
+  else kern = a.pages.table ? attn_decode_kernel<T, HD, G, true, W> : attn_decode_kernel<T, HD, G, false, W>;
   const size_t smem = MMA ? (size_t)W * attn_stage_bytes<HD>() : (size_t)W * G * HD * sizeof(float);
   // above 48 KB of dynamic shared memory a kernel must be granted it (once per kernel and device)
   static bool granted[2][64] = {};
