@@ -375,7 +375,7 @@ def profile_run(args, device: int):
     """Plain launches without graphs or timing, for ncu: --profile-gemm (config 1's attn_q at 512
     tokens: gemm_bscale / gemm_bfill_kx / gemm_bfill_kx_min / gemm_kx_kernel per step), --profile-batch NTOK (config 3's
     interleaved gate/up, Q4_K 24576 x 4096, at NTOK tokens: kq_batch_kernel launches) or
-    --profile-attn CTX NSEQ (config 2: qkv_post_kernel + attn_decode_kernel per step);
+    --profile-attn CTX NSEQ (config 2: qkv_post_kernel + attn_mma_kernel per step);
     args.warmup + args.steps steps."""
     import ctypes as C
 

@@ -5,9 +5,10 @@
 //    (round to nearest even, NaN as the reference encodes it) or stored as f32.
 //    Replaces src/compute/worker.js:296-309 (k-norm :301, RoPE :302, f32ToF16 :305 / f32 copy
 //    :307-308) and the q side :313-315; RefModel: src/model/forward.js:113-121.
-//  * attn_decode_kernel -- softmax(q K^T / sqrt(hd)) V for the query heads of one KV head over
-//    positions [0, npos), split over the context (flash decoding): each CTA streams a range of K/V
-//    rows through shared memory with 1D bulk copies, keeps an online softmax, and the last CTA of a
+//  * attn_mma_kernel (f16 caches) / attn_decode_kernel (f32 caches) -- softmax(q K^T / sqrt(hd)) V
+//    for the query heads of one KV head over positions [0, npos), split over the context (flash
+//    decoding): each warp of a CTA streams its own run of K/V rows (through a shared-memory stage and
+//    the tensor cores, or straight into registers), keeps an online softmax, and the last CTA of a
 //    (sequence, KV head) merges the partial results.  Replaces the per-head attention of
 //    src/compute/worker.js:310-337 (JS loop :320-333, WASM attn_scores / attn_av
 //    src/compute/wasm/attn-kernels.js:26-194) and src/model/forward.js:123-140.
