@@ -829,6 +829,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
     // a round's copies into its stage's slots (the min step's into the hi tile after them); step s of the walk is step (sb + koff) * SPS + kk
     // of the tiles
     if (lane == 0) {
+      pdl_wait();                                      // the activation tiles are the previous kernel's
       const uint32_t part = (uint32_t)nmma * 128;      // the first nmma rows of a tile
       int kk = 0, sbl = koff_sb, r = 0;
       for (int s = 0; s < nsteps; r++) {
@@ -977,6 +978,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
     }
   } else {
     // ---- epilogue: warp w owns TMEM lanes 32 (w % 4) ..; per super-block total += d * buffer
+    pdl_wait();                                        // bscale, the tile counters and y_add
     const int quarter = warp & 3;
     const int64_t row = (int64_t)m_tile * GM + quarter * 32 + lane;
     const int64_t t16 = row / 16;
@@ -1088,6 +1090,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
 // bscale as [hi x8 | lo x8 | hi x8 | 0] in the hi tile.  nrows tokens are filled (zeros past ntok).
 __global__ void gemm_bfill_kx_kernel(const int8_t *xq, const float *xd, int64_t k, int ntok, int nrows,
                                      const float *bscale, int sps, int btile, uint8_t *bt) {
+  pdl_launch_dependents();                      // the GEMM after it may start its weight work
   const int64_t groups = k / 8, total = (int64_t)nrows * groups;
   const int nsteps = (int)(k / 256) * sps;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -1110,6 +1113,7 @@ __global__ void gemm_bfill_kx_kernel(const int8_t *xq, const float *xd, int64_t 
 }
 __global__ void gemm_bfill_kx_min_kernel(const float *xd, const int32_t *xs, int64_t k, int ntok, int nrows,
                                          const float *bscale, int btile, uint8_t *bt) {
+  pdl_launch_dependents();                      // the GEMM after it may start its weight work
   const int nb = (int)(k / 256), nsteps = nb * 5;
   const int64_t total = (int64_t)nrows * nb * 8;        // (token, super-block, 16-byte chunk)
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -1381,8 +1385,20 @@ static cudaError_t launch_kx_t(const GemmArgs &a, dim3 grid, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     granted[dev] = true;
   }
-  gemm_kx_kernel<FMT><<<grid, kXThreads, kx_smem_bytes(), s>>>(a);
-  return cudaGetLastError();
+  // chained to the activation preparation with programmatic dependent launch: the dequantizing
+  // warps and the MMA lane start on the weights while the preparation finishes; the activation
+  // producer and the epilogue warps wait for it (griddepcontrol.wait) before touching its output
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kXThreads);
+  cfg.dynamicSmemBytes = kx_smem_bytes();
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = s != nullptr && s != cudaStreamLegacy && s != cudaStreamPerThread ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemm_kx_kernel<FMT>, a);
 }
 
 cudaError_t launch_gemm_kx(const DevMatrix &m, void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
