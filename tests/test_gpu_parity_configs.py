@@ -8,8 +8,9 @@ wherever the oracle's top-1 margin exceeds 1e-3.  Each test states its bar in th
   kernels (src/compute/ref-kernels.js:44-62, :305-322; src/compute/worker.js:426) and the fused
   GEMV forms the decode pass launches -- RMSNorm in the activation staging, the SwiGLU epilogue and
   the residual epilogue (worker.js:346, :432);
-* config 1: the 512-token prefill GEMM on attn_q (Q4_K 4096 x 4096) and ffn_down (Q6_K
-  4096 x 12288), every 37th token row against the oracle's matvec;
+* config 1: the 512-token prefill GEMM on attn_q (Q4_K 4096 x 4096), ffn_down (Q6_K
+  4096 x 12288) and attn_k (Q4_K 1024 x 4096: split-K, the splits of a tile one cluster), every
+  37th token row against the oracle's matvec;
 * config 2: decode attention over f16 caches of 8192 and 32768 positions (the 37-split regime,
   more than 256 positions per split) with two sequences, and 64 sequences at 8192;
 * config 3 widths: a 2-layer model with the Qwen3-8B shapes (hidden 4096, FFN 12288, 32 / 8 heads,
@@ -173,8 +174,8 @@ def test_fused_gemv_residual_epilogue_bit_exact(ctx, t, rows, cols):
 
 
 # --------------------------------------------------------------------------------- config 1
-@pytest.mark.parametrize("t,rows,cols", [(ggml.Q4_K, 4096, 4096), (ggml.Q6_K, 4096, 12288)],
-                         ids=["attn_q-Q4_K-4096x4096", "ffn_down-Q6_K-4096x12288"])
+@pytest.mark.parametrize("t,rows,cols", [(ggml.Q4_K, 4096, 4096), (ggml.Q6_K, 4096, 12288), (ggml.Q4_K, 1024, 4096)],
+                         ids=["attn_q-Q4_K-4096x4096", "ffn_down-Q6_K-4096x12288", "attn_k-Q4_K-1024x4096-splitK"])
 def test_prefill_gemm_512_tokens(ctx, t, rows, cols):
     rng = np.random.default_rng(512 + t)
     wt = synth.tensor(t, rows, cols, rng, "bench")

@@ -72,6 +72,21 @@ __device__ __forceinline__ bool mbar_wait_lazy(uint64_t *bar, uint32_t parity) {
   return mbar_wait_bounded(bar, parity, deadline);
 }
 
+// ---------------------------------------------------------------------------- thread-block clusters
+// every thread of every CTA of the cluster arrives, then waits (release / acquire: shared-memory
+// writes before the barrier are visible to the cluster's reads after it)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// a float at the same shared-memory offset as `local` in the cluster's CTA of rank `rank`
+__device__ __forceinline__ float ld_dsmem_f32(const float *local, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
 // ---------------------------------------------------------------------------- 1D bulk copy
 // global -> shared, completion counted on `bar` (bytes and both addresses 16-byte aligned).
 __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar) {

@@ -1032,48 +1032,45 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
           for (int i = 0; i < 32; i++) t[i] = __fmaf_rn(mv[i], p.wscale_inv, t[i]);
         }
         if (p.nsplit > 1) {
-          // this split's partial sums; the last split to finish adds them up below
-          if (row < p.rows) {
+          // this split's partial sums, [token][row] in its own shared memory (the A ring: every MMA
+          // that read it has completed); the cluster adds them up after the kernel's roles end
+          float *ps = reinterpret_cast<float *>(smem);
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
-              const int tok = n_tile * GN + col0 + i;
-              if (tok < p.ntok) p.ws[((int64_t)split * p.ntok + tok) * p.rows + row] = t[i] * p.bscale[tok];
-            }
+          for (int i = 0; i < 32; i++) {
+            const int tok = n_tile * GN + col0 + i;
+            ps[(col0 + i) * GM + quarter * 32 + lane] = tok < p.ntok ? t[i] * p.bscale[tok] : 0.f;
           }
         } else {
           kx_store(p, t, n_tile * GN + col0, row);
         }
       }
     }
-    if (p.nsplit > 1) {
-      // one arrival per CTA on the tile's counter (aborted CTAs too: the status word carries the
-      // error); the last one sums the splits in split order, so the bits do not depend on timing
-      __threadfence();
-      named_sync(1, kXEpiWarps * 32);
-      unsigned *cnt = p.tile_cnt + (int64_t)n_tile * gridDim.x + m_tile;
-      if (warp == kXEpiWarp0 && lane == 0) *last_flag = atomicAdd(cnt, 1u) == (unsigned)(p.nsplit - 1);
-      named_sync(1, kXEpiWarps * 32);
-      if (*last_flag) {
-        __threadfence();
-        for (int c = 0; c * 32 < ntok_tile; c++) {
-          const int tok0 = n_tile * GN + c * 32;
-          float t[32];
+  }
+  if (p.nsplit > 1) {
+    // split-K: the nsplit CTAs of an output tile form a cluster; after every partial is in its CTA's
+    // shared memory, CTA z adds the partials of token chunks z, z + nsplit, .. in split order
+    // through distributed shared memory (the bits of a one-CTA sum of the same order) and writes
+    // them; the second barrier keeps every CTA's shared memory alive until the others have read it
+    cluster_sync_all();
+    if (warp >= kXEpiWarp0) {
+      const int quarter = warp & 3, rowl = quarter * 32 + lane;
+      const int64_t row = (int64_t)m_tile * GM + rowl;
+      const float *ps = reinterpret_cast<const float *>(smem);
+      for (int c = split; c * 32 < ntok_tile; c += p.nsplit) {
+        float t[32];
 #pragma unroll
-          for (int i = 0; i < 32; i++) t[i] = 0.f;
-          // split by split, 32 independent loads in flight; the sums in split order
-          for (int z = 0; z < p.nsplit; z++) {
-            const float *wz = p.ws + ((int64_t)z * p.ntok + tok0) * p.rows + row;
-            float v[32];
+        for (int i = 0; i < 32; i++) t[i] = 0.f;
+        for (int z = 0; z < p.nsplit; z++) {
+          float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = tok0 + i < p.ntok && row < p.rows ? __ldcg(wz + (int64_t)i * p.rows) : 0.f;
+          for (int i = 0; i < 32; i++) v[i] = ld_dsmem_f32(ps + (c * 32 + i) * GM + rowl, (uint32_t)z);
 #pragma unroll
-            for (int i = 0; i < 32; i++) t[i] = __fadd_rn(t[i], v[i]);
-          }
-          kx_store_scaled(p, t, tok0, row);
+          for (int i = 0; i < 32; i++) t[i] = __fadd_rn(t[i], v[i]);
         }
-        if (warp == kXEpiWarp0 && lane == 0) *cnt = 0;
+        kx_store_scaled(p, t, n_tile * GN + c * 32, row);
       }
     }
+    cluster_sync_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -1334,6 +1331,7 @@ int kx_splits(int64_t rows, int ntok, int64_t k) {
   if (tiles * 2 > sms || nb < 8) return 1;
   int sp = (int)(sms / tiles);
   if (sp > nb / 4) sp = nb / 4;
+  if (sp > 8) sp = 8;                                  // the splits of a tile are one (portable) cluster
   const int sbps = (nb + sp - 1) / sp;
   return (nb + sbps - 1) / sbps;
 }
@@ -1393,11 +1391,20 @@ static cudaError_t launch_kx_t(const GemmArgs &a, dim3 grid, cudaStream_t s) {
   cfg.blockDim = dim3(kXThreads);
   cfg.dynamicSmemBytes = kx_smem_bytes();
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (s != nullptr && s != cudaStreamLegacy && s != cudaStreamPerThread) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na++].val.programmaticStreamSerializationAllowed = 1;
+  }
+  if (grid.z > 1) {                                 // split-K: a tile's splits are one cluster
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na++].val.clusterDim.z = grid.z;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = s != nullptr && s != cudaStreamLegacy && s != cudaStreamPerThread ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, gemm_kx_kernel<FMT>, a);
 }
 
