@@ -134,7 +134,6 @@ struct AttnArgs {
 
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t s, bool pdl);
 bool attn_supported(int head_dim, int group);
-size_t attn_smem_bytes(int head_dim, int group, bool f16);
 cudaError_t launch_attn(const AttnArgs &a, bool f16, cudaStream_t s, bool pdl);
 cudaError_t launch_kv_block_copy(void *dst, int64_t dst_row, int64_t dst_blk, const void *src, int64_t src_row,
                                  int64_t src_blk, int64_t row_bytes, int rows, int nblk, int num_sms, cudaStream_t s);

@@ -719,13 +719,6 @@ cudaError_t launch_kv_block_copy(void *dst, int64_t dst_row, int64_t dst_blk, co
   return cudaGetLastError();
 }
 
-// dynamic shared memory of a launch: the warps' accumulators [warps][group][head_dim] f32 (the
-// larger warp count's)
-size_t attn_smem_bytes(int head_dim, int group, bool f16) {
-  (void)f16;
-  return (size_t)16 * group * head_dim * sizeof(float);
-}
-
 template <typename T, int HD, int G, int W>
 static cudaError_t launch_attn_w(const AttnArgs &a, cudaStream_t s, bool pdl) {
   constexpr bool MMA = sizeof(T) == 2;                // f16 caches: the tensor-core kernel
