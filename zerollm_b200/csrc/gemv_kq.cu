@@ -534,20 +534,29 @@ __global__ void __launch_bounds__(kRingWarps * 32, 1) kq_ring_kernel(const KqArg
   const uint32_t ring = smem_u32(smem + p.ring_off) + (uint32_t)(warp * S * US);
   const uint8_t *base = p.w + (int64_t)T0 * nb * US;
 
-  // The warp's first unit streams in before griddepcontrol.wait (the weights are not the previous
-  // kernel's output), the rest of its first S only after the activation's loads: loads issued behind
-  // a burst of cp.async wait for the burst to drain, and staging the activation behind all S units
-  // cost ~8 % of a 4096 x 4096 launch (measured on a B200: 4.61 -> 4.22 us; issuing every unit after
-  // the staging instead, 4.92 us).
-  if (i0 < i1) copy_unit<FMT>(ring, base + (int64_t)i0 * US, lane);
-  cp_async_commit();
+  // The warp's first unit (two when its run is longer than its ring) streams in before
+  // griddepcontrol.wait (the weights are not the previous kernel's output), the rest of its first S
+  // only after the activation's loads: loads issued behind a burst of cp.async wait for the burst to
+  // drain, and staging the activation behind all S units cost ~8 % of a 4096 x 4096 launch (measured
+  // on a B200: 4.61 -> 4.22 us; every unit after the staging 4.92 us; two units before it 4.95 us
+  // there, but faster on the long runs of the 8B gate/up and down matrices).
+  const int pre = i1 - i0 > S ? 2 : 1;
+#pragma unroll
+  for (int d = 0; d < 2; d++) {
+    if (d < pre) {
+      if (i0 + d < i1) copy_unit<FMT>(ring + d * US, base + (int64_t)(i0 + d) * US, lane);
+      cp_async_commit();
+    }
+  }
   pdl_launch_dependents();
   pdl_wait();                                   // the activation is
   const SAct sa = stage_token<FMT, NT>(p, smem + p.x_off, warp, lane, g);
 #pragma unroll
   for (int d = 1; d < S; d++) {
-    if (i0 + d < i1) copy_unit<FMT>(ring + d * US, base + (int64_t)(i0 + d) * US, lane);
-    cp_async_commit();
+    if (d >= pre) {
+      if (i0 + d < i1) copy_unit<FMT>(ring + d * US, base + (int64_t)(i0 + d) * US, lane);
+      cp_async_commit();
+    }
   }
   __syncthreads();
 
