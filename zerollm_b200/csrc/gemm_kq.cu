@@ -52,7 +52,6 @@ constexpr int kPairBytes = 2 * kTileBytes;   // a hi tile and its lo tile
 constexpr int kQ6HOff = 2048, kQ6SOff = 3072, kQ6DOff = 3328;   // Q6_K unit regions (kq_layout.h)
 static_assert(GM == GN, "A and B tiles share one size");
 
-constexpr uint32_t kIdescM = idesc_f16(GM, 0);
 __device__ __forceinline__ uint32_t idesc_n(int n) { return idesc_f16(GM, n); }
 
 // ---------------------------------------------------------------------------- dequantization
@@ -229,11 +228,8 @@ struct GemmArgs {
   int swiglu;             // rows are (gate, up) pairs: y[t][r / 2] = silu(gate) * up
   unsigned *status;
   // exact-A kernel only: bytes of one activation tile (128 x 64 f16, or fewer rows for a single
-  // short token tile), and split-K: nsplit CTAs per output tile, sbps super-blocks each, partial
-  // sums in ws [split][token][row], tile_cnt counting the splits that are done
+  // short token tile), and split-K: nsplit CTAs per output tile (one cluster), sbps super-blocks each
   int btile, nsplit, sbps;
-  float *ws;
-  unsigned *tile_cnt;
 };
 
 // A CTA computes a 128-row x 128-token tile; its MMAs use N = the tile's tokens rounded up to 16,
@@ -451,10 +447,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kq_kernel(const GemmArgs p) 
 // ---------------------------------------------------------------------------- activation tiles
 // Per token t: the power of two 2^e_t with every |xd * xq| * 2^-e_t below 2^15 (f16 keeps 11 bits
 // down to 2^-14 of it); bscale[t] = 2^e_t multiplies the accumulators back.  Padding tokens get 1.
-__global__ void gemm_bscale_kernel(const float *xd, int64_t nblk, int ntok, int npad, float *bscale, unsigned *zero = nullptr,
-                                   int nzero = 0) {
+__global__ void gemm_bscale_kernel(const float *xd, int64_t nblk, int ntok, int npad, float *bscale) {
   const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-  for (int i = (int)(blockIdx.x * blockDim.x + threadIdx.x); i < nzero; i += (int)(gridDim.x * blockDim.x)) zero[i] = 0;
   if (warp >= npad) return;
   float amax = 0.f;
   if (warp < ntok)
@@ -794,7 +788,6 @@ __global__ void __launch_bounds__(kXThreads, 1) gemm_kx_kernel(const GemmArgs p)
   uint64_t *buf_full = bars + 2 * AS + 2 * BS, *buf_free = buf_full + 2, *acc_full = buf_free + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  volatile int *last_flag = reinterpret_cast<volatile int *>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
@@ -1336,28 +1329,25 @@ int kx_splits(int64_t rows, int ntok, int64_t k) {
   return (nb + sbps - 1) / sbps;
 }
 
-// [activation tiles][bscale: npad floats][tile counters][split partials]
+// [activation tiles][bscale: npad floats]
 static size_t kx_tiles_bytes(int64_t k, int ntok, int type) {
   return (size_t)(gemm_tokens_pad(ntok) / GN) * (size_t)(k / 256) * kx_steps(type) * 2 * kx_tile_rows(ntok) * 128;
 }
 size_t gemm_bx_bytes(int64_t k, int ntok, int type, int64_t rows) {
-  const int64_t npad = gemm_tokens_pad(ntok), tiles = (rows + GM - 1) / GM * (npad / GN);
-  const int sp = kx_splits(rows, ntok, k);
-  size_t b = kx_tiles_bytes(k, ntok, type) + (size_t)npad * 4 + (size_t)tiles * 4;
-  b = (b + 255) / 256 * 256;
-  return sp > 1 ? b + (size_t)sp * ntok * rows * 4 : b;
+  (void)rows;                                          // split-K partials stay in the clusters' shared memory
+  const size_t b = kx_tiles_bytes(k, ntok, type) + (size_t)gemm_tokens_pad(ntok) * 4;
+  return (b + 255) / 256 * 256;
 }
 
 cudaError_t launch_gemm_prep_kx(const ActView &act, int ntok, int type, int64_t rows, void *bbuf, cudaStream_t s) {
   const int64_t npad = gemm_tokens_pad(ntok), k = act.k;
   const int sps = kx_steps(type), tr = kx_tile_rows(ntok), nrows = ntok < GN ? tr : (int)npad;
-  const int64_t tiles = (rows + GM - 1) / GM * (npad / GN);
+  (void)rows;
   uint8_t *bt = reinterpret_cast<uint8_t *>(bbuf);
   float *bscale = reinterpret_cast<float *>(bt + kx_tiles_bytes(k, ntok, type));
-  unsigned *cnt = reinterpret_cast<unsigned *>(bscale + npad);
   const int threads = 256;
   gemm_bscale_kernel<<<(unsigned)((npad * 32 + threads - 1) / threads), threads, 0, s>>>(act.xd, k / 32, ntok, (int)npad,
-                                                                                         bscale, cnt, (int)tiles);
+                                                                                         bscale);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   int64_t total = (int64_t)nrows * (k / 8);
@@ -1411,7 +1401,7 @@ static cudaError_t launch_kx_t(const GemmArgs &a, dim3 grid, cudaStream_t s) {
 cudaError_t launch_gemm_kx(const DevMatrix &m, void *bbuf, int ntok, float *y, int64_t y_stride, const float *y_add,
                            float mscale, unsigned *status, cudaStream_t s, bool swiglu) {
   if (!gemm_kq_supported(m) || (swiglu && (m.rows % 2 || y_add))) return cudaErrorInvalidValue;
-  const int64_t npad = gemm_tokens_pad(ntok), tiles = (m.rows + GM - 1) / GM * (npad / GN);
+  const int64_t npad = gemm_tokens_pad(ntok);
   const int nb = (int)(m.cols / 256), sp = kx_splits(m.rows, ntok, m.cols);
   uint8_t *base = reinterpret_cast<uint8_t *>(bbuf);
   const size_t tb = kx_tiles_bytes(m.cols, ntok, m.type);
@@ -1419,8 +1409,6 @@ cudaError_t launch_gemm_kx(const DevMatrix &m, void *bbuf, int ntok, float *y, i
   a.w = m.data;
   a.b = base;
   a.bscale = reinterpret_cast<const float *>(base + tb);
-  a.tile_cnt = reinterpret_cast<unsigned *>(base + tb + (size_t)npad * 4);
-  a.ws = reinterpret_cast<float *>(base + (tb + (size_t)npad * 4 + (size_t)tiles * 4 + 255) / 256 * 256);
   a.y = y; a.y_add = y_add; a.y_stride = y_stride;
   // the min values carry mscale and xsum 2^-5: their accumulator comes back with 2^5 / mscale
   a.wscale = mscale; a.wscale_inv = 32.f / mscale; a.swiglu = swiglu ? 1 : 0;
