@@ -96,9 +96,11 @@ int zllm_quantize_act(zllm_ctx *ctx, const float *x, int64_t k, int ntok, int8_t
  * Replaces the per-type kernels matvec_* / mm_* (src/compute/wasm/kernels.js:30-240,
  * src/compute/wasm/kquant-kernels.js:337-504) and the dispatch in src/compute/worker.js:251-270.
  * y_add == y gives the in-place residual add of worker.js:346 / :432.
- * 64 or more tokens on a k-quant W run the tensor-core GEMM (weights and the quantized activation
- * each split into an f16 hi/lo pair, three MMAs, f32 accumulation: within ~1e-5 of the largest
- * output of the per-token arithmetic, not bit-identical to it); 1..63 tokens keep the per-token
+ * 64 or more tokens on a k-quant W run the tensor-core GEMM (sub-block scale x quant dequantized
+ * exactly into f16, the quantized activation as an f16 hi/lo pair, two MMAs per K slice, f32
+ * accumulation with the super-block scales applied in f32: within ~1e-6 of the largest output of the
+ * per-token arithmetic, not bit-identical to it; Q6_K matrices with a sub-block scale above 64 split
+ * the weights into hi/lo too, three MMAs, ~1e-5); 1..63 tokens keep the per-token
  * arithmetic, so batches below 64 reproduce single tokens bit for bit
  * (test/kquant-kernels.test.js:65-97).  The GEMM's activation tiles live in a context scratch
  * buffer that grows on demand (a cudaMalloc on first use). */
